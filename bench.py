@@ -1,0 +1,306 @@
+"""Throughput benchmark of the forecast path (one JSON line on rank 0).
+
+Workload (BASELINE.json metric / configs[2]): Chronos-2-shaped random-init checkpoint (768-d,
+12 layers, 12 heads, d_ff 3072, patch 16, 21 quantiles), 256 seeded series per GPU of 8192 steps
+(5 % NaN), horizon 1024. One step = one forecast of the batch. Synthetic data (seeded sine +
+random walk + noise, lognormal scale); random-init weights; no hub access.
+
+  value  series/s with inputs resident in HBM (tsfm_forecast_chronos2_device), device time from
+         CUDA events on the launching stream, L2 flushed between steps, max over ranks.
+  e2e    series/s through the host entry point tsfm_forecast_chronos2 with pinned host buffers:
+         H2D of the inputs and D2H of the quantiles inside the timed region.
+  roofline  of the dominant kernel (the tcgen05 linear kernel): algorithmic FLOPs / summed
+         CUDA-event launch time, against the measured sustained BF16 peak.
+  cpu_baseline  the CPU restatement (oracle) on a bounded sample of the same workload.
+
+`--impl reference` times the reference algorithm's CPU implementation instead (the oracle port,
+all host threads; the Zig reference cannot be built on these hosts) on rank 0 only.
+
+Multi-GPU: `python -m torch.distributed.run --nproc-per-node N bench.py --gpus N`: each rank
+forecasts its own 256 series (weak scaling, no collective on the data path).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "tsfm-zig_b200"), ROOT]
+
+METRIC = "forecast series/sec at 1/2/4/8 B200 (Chronos-2-shaped ctx8192 H1024); % TC peak"
+SERIES_PER_GPU = 256
+CONTEXT = 8192
+HORIZON = 1024
+GF_PER_SERIES = 130.02  # algorithmic GFLOP per series at ctx 8192, H 1024 (2 FLOPs per MAC)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--series", type=int, default=SERIES_PER_GPU)
+    ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p["bf16_tflops_sustained"], p["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class Clocks:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) >= 9:
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_model(device):
+    from tsfm_b200 import Model, synthetic as syn
+    cfg = syn.chronos2_config(context_length=CONTEXT, max_output_patches=64)
+    w = syn.random_checkpoint(cfg, seed=20261201)
+    return cfg, w, Model(cfg, w, devices=(device,))
+
+
+def traffic_from_profile():
+    """DRAM bytes per launch of the linear kernel from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "linear_tc_chronos2.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_gemm_step:"):
+                return float(line.split(":")[1])
+    except Exception:
+        pass
+    return None
+
+
+def cpu_baseline(sample):
+    """The oracle (CPU restatement of the reference path) on `sample` series of the workload."""
+    from oracle import binding as ob
+    from tsfm_b200 import config as cm, synthetic as syn, tensor_table
+    cfg = syn.chronos2_config(context_length=CONTEXT, max_output_patches=64)
+    w = syn.random_checkpoint(cfg, seed=20261201)
+    m = ob.OracleModel(cm.parse(cfg), w, tensor_table)
+    x = syn.seeded_series(sample, CONTEXT, seed=1000)
+    t0 = time.perf_counter()
+    m.forecast_chronos2(x, HORIZON)
+    dt = time.perf_counter() - t0
+    return sample / dt, ob.get_threads(), dt
+
+
+def run_reference(a, rank):
+    if rank != 0:
+        return
+    from oracle import binding as ob
+    from tsfm_b200 import config as cm, synthetic as syn, tensor_table
+    ob.set_threads(os.cpu_count() or 1)
+    cfg = syn.chronos2_config(context_length=CONTEXT, max_output_patches=64)
+    w = syn.random_checkpoint(cfg, seed=20261201)
+    m = ob.OracleModel(cm.parse(cfg), w, tensor_table)
+    n = max(1, a.cpu_sample)
+    x = syn.seeded_series(n, CONTEXT, seed=1000)
+    for _ in range(max(0, min(a.warmup, 1))):
+        m.forecast_chronos2(x[:1], HORIZON)
+    times = []
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        m.forecast_chronos2(x, HORIZON)
+        times.append(time.perf_counter() - t0)
+    ms = float(np.mean(times)) * 1e3
+    v = n / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "series/s", "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "chronos2-ctx8192-h1024", "series_per_step": n, "context": CONTEXT,
+                   "horizon": HORIZON, "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": v, "unit": "series/s", "cores": ob.get_threads(), "kind": "port",
+                         "sample": f"{n} series x 8192 steps, horizon 1024, per step"},
+        "e2e": {"value": v, "unit": "series/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        return run_reference(a, rank)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from tsfm_b200 import synthetic as syn
+    cfg, w, model = build_model(local)
+    del w
+    b, q = a.series, 21
+    x = syn.seeded_series(b, CONTEXT, seed=1000 + rank * b)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty((b, HORIZON, q), device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        model.forecast_chronos2_device(xd.data_ptr(), b, CONTEXT, HORIZON, out.data_ptr(), sp)
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    launches = model.last_launch_count()
+
+    # Device-resident throughput: events per step on the launching stream, L2 flushed in between.
+    barrier()
+    torch.cuda.synchronize()
+    total_ms = 0.0
+    with Clocks(local) as clk:
+        for _ in range(a.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            e1.synchronize()
+            total_ms += e0.elapsed_time(e1)
+    torch.cuda.synchronize()
+    barrier()
+    t = torch.tensor([total_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = t.item() / a.steps
+    value = b * world / (ms_step / 1e3)
+
+    # End to end through the host entry point: pinned inputs in, quantiles out.
+    xp = torch.from_numpy(x).pin_memory()
+    op = torch.empty((b, HORIZON, q), dtype=torch.float32).pin_memory()
+    xnp, onp = xp.numpy(), op.numpy()
+    model.forecast_chronos2(xnp, HORIZON, out=onp)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        model.forecast_chronos2(xnp, HORIZON, out=onp)
+    e2e_s = (time.perf_counter() - t0) / a.steps
+    barrier()
+    te = torch.tensor([e2e_s], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = b * world / te.item()
+
+    # Per-kernel-class timing (events around every launch) on separate, untimed steps.
+    model.profile(True)
+    model.profile_reset()
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    cls = {c: model.profile_read(c) for c in ("gemm", "attention", "rmsnorm", "patch", "head", "other")}
+    model.profile(False)
+    burst, sustained, hbm, src = peaks()
+    g = cls["gemm"]
+    achieved = g["work"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else None
+    traffic = traffic_from_profile()
+    kernels = {c: {"launches_per_step": v["launches"] / 2, "ms_per_step": v["ms"] / 2,
+                   "share": v["ms"] / max(1e-9, sum(u["ms"] for u in cls.values()))} for c, v in cls.items()}
+    if cls["attention"]["ms"] > 0:
+        kernels["attention"]["tflops"] = cls["attention"]["work"] / (cls["attention"]["ms"] / 1e3) / 1e12
+
+    if rank == 0:
+        cpu = None
+        try:
+            v, cores, dt = cpu_baseline(a.cpu_sample)
+            cpu = {"value": v, "unit": "series/s", "cores": cores, "kind": "port",
+                   "sample": f"{a.cpu_sample} series x 8192 steps, horizon 1024 ({dt:.1f} s)"}
+        except Exception as ex:  # the baseline leg must not hide the GPU number
+            cpu = {"value": None, "unit": "series/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "series/s", "n_gpus": world, "steps": a.steps,
+            "warmup": max(3, a.warmup), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded sine + random walk + noise, 5% NaN; "
+                                                             "random-init N(0,0.02) weights)",
+            "config": {"workload": "chronos2-ctx8192-h1024", "d_model": 768, "layers": 12, "heads": 12, "d_ff": 3072,
+                       "patch": 16, "quantiles": 21, "series_per_gpu": b, "global_batch": b * world,
+                       "context": CONTEXT, "horizon": HORIZON, "parallelism": f"series-sharded x{world}",
+                       "l2": "flushed between steps (256 MB write)"},
+            "tc_peak_frac": (GF_PER_SERIES * 1e9 * b / (ms_step / 1e3)) / (burst * 1e12),
+            "roofline": {"bound": "tensor", "kernel": "linear_tc_kernel (tcgen05 GEMM)", "achieved": achieved,
+                         "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained if achieved else None,
+                         "peak_source": f"{src} bf16_tflops_sustained", "traffic": traffic},
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e, "unit": "series/s", "h2d_bytes_per_step": b * CONTEXT * 4,
+                    "d2h_bytes_per_step": b * HORIZON * q * 4},
+            "gpu_launches": launches * a.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

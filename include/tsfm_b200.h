@@ -1,0 +1,276 @@
+/*
+ * tsfm_b200.h — C ABI of the B200 forecast backend.
+ *
+ * One shared library (libtsfm_b200.so) replaces the forward pass of tsfm-zig's three model
+ * families with sm_100a CUDA kernels. Every entry point takes plain pointers and sizes, returns a
+ * tsfm_status (0 = success) and never throws; the message of the last failure on the calling
+ * thread is tsfm_last_error(). There is no CPU fallback: an unusable device is an error.
+ *
+ * Two seams of the reference are replaced:
+ *
+ *  1. The family seam. Each family's `forecaster.forecast` becomes one call:
+ *       chronos2/forecaster.zig:14-22      -> tsfm_forecast_chronos2
+ *       chronos_bolt/forecaster.zig:22     -> tsfm_forecast_bolt
+ *       timestral/forecaster.zig:57-69     -> tsfm_forecast_timestral
+ *     The weights come from the caller's safetensors mapping (core/safetensors.zig:59-97) through
+ *     a table of named tensors; the tensor names and element counts are those the reference's
+ *     `Model.load` functions ask for (chronos2/model.zig:77-125, chronos_bolt/model.zig:101-172,
+ *     timestral/model.zig:136-200), and a missing tensor, a wrong element count or an unsupported
+ *     dtype is reported like `Weights.get` reports it.
+ *
+ *  2. The GEMM offload seam of the CUDA backend (platform/cuda/gemm.c:232-330): the four
+ *     functions cuda_weight_register / cuda_weight_release / cuda_sgemm_nt / cuda_sgemm_nn keep
+ *     their signatures and meaning as tsfm_weight_register ... tsfm_sgemm_nn.
+ *
+ * Layouts are row-major. Host-pointer entry points copy inputs to the device and results back and
+ * return when the results are written; *_device entry points take device pointers and a CUDA
+ * stream (cudaStream_t passed as void*) and return after enqueueing.
+ */
+#ifndef TSFM_B200_H
+#define TSFM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------------------------------------
+ * Status codes. The reference returns Zig error unions; each code below names the error it
+ * stands for (e.g. error.MissingTensor in core/safetensors.zig:62).
+ */
+typedef enum tsfm_status {
+    TSFM_OK = 0,
+    TSFM_ERR_INVALID_ARGUMENT = 1,   /* null pointer, zero size, bad option */
+    TSFM_ERR_INVALID_CONFIG = 2,     /* error.InvalidConfig (config.zig validate) */
+    TSFM_ERR_MISSING_TENSOR = 3,     /* error.MissingTensor */
+    TSFM_ERR_SHAPE_MISMATCH = 4,     /* error.ShapeMismatch */
+    TSFM_ERR_UNSUPPORTED_DTYPE = 5,  /* error.UnsupportedDtype */
+    TSFM_ERR_CUDA = 6,               /* a CUDA runtime or driver call failed */
+    TSFM_ERR_OUT_OF_MEMORY = 7,      /* device or host allocation failed */
+    TSFM_ERR_DEVICE_TIMEOUT = 8,     /* a kernel's bounded wait gave up (see tsfm_last_error) */
+    TSFM_ERR_EMPTY_INPUT = 9,        /* error.EmptyInput */
+    TSFM_ERR_HORIZON_TOO_LONG = 10,  /* error.HorizonTooLong */
+    TSFM_ERR_UNSUPPORTED = 11,       /* a configuration the backend does not implement */
+    TSFM_ERR_DEGENERATE_INPUT = 12,  /* error.DegenerateInput (timestral/forecaster.zig:419) */
+    TSFM_ERR_ASYMMETRIC_QUANTILES = 13, /* error.AsymmetricQuantiles (timestral/forecaster.zig:110) */
+    TSFM_ERR_COVARIATES_UNSUPPORTED = 14, /* error.CovariatesUnsupported / KnownCovariatesUnsupported */
+    TSFM_ERR_NO_DEVICE = 15          /* no CUDA device, or the device ordinal is out of range */
+} tsfm_status;
+
+typedef enum tsfm_family {
+    TSFM_CHRONOS2 = 1,
+    TSFM_CHRONOS_BOLT = 2,
+    TSFM_TIMESTRAL = 3
+} tsfm_family;
+
+/* Checkpoint dtypes accepted by the weight table (core/safetensors.zig:66: F32, F16, BF16). */
+typedef enum tsfm_dtype {
+    TSFM_DTYPE_F32 = 0,
+    TSFM_DTYPE_F16 = 1,
+    TSFM_DTYPE_BF16 = 2
+} tsfm_dtype;
+
+/* Operand type of the tensor-core contractions; accumulation is always FP32. */
+typedef enum tsfm_compute {
+    TSFM_COMPUTE_BF16 = 0,
+    TSFM_COMPUTE_TF32 = 1
+} tsfm_compute;
+
+/* Timestral layer kinds, the entries of `block_schedule` (timestral/config.zig:94-100). */
+typedef enum tsfm_layer_kind {
+    TSFM_LAYER_TIME = 0,
+    TSFM_LAYER_VARIATE = 1,
+    TSFM_LAYER_TIME_VARIATE = 2,
+    TSFM_LAYER_VARIATE_TIME = 3
+} tsfm_layer_kind;
+
+/* One named checkpoint tensor: `data` points at `numel` elements of `dtype` (host memory, e.g.
+ * the safetensors mapping). The table is read during tsfm_model_create only. */
+typedef struct tsfm_tensor {
+    const char *name;
+    const void *data;
+    int32_t dtype;   /* tsfm_dtype */
+    uint64_t numel;
+} tsfm_tensor;
+
+/* The inference configuration of one checkpoint. The fields mirror the reference's Config
+ * structs (chronos2/config.zig:9-30, chronos_bolt/config.zig:10-32, timestral/config.zig:6-28);
+ * fields a family does not use are ignored. `validate()` of each family is applied by
+ * tsfm_model_create. */
+typedef struct tsfm_config {
+    int32_t family;              /* tsfm_family */
+    /* shared transformer shape */
+    int32_t d_model;
+    int32_t d_ff;                /* Chronos d_ff; Timestral mlp_hidden_dim */
+    int32_t num_heads;
+    int32_t d_kv;                /* Chronos head width; Timestral uses d_model / num_heads */
+    int32_t num_layers;          /* Chronos encoder layers (Timestral: n_layer_kinds) */
+    int32_t num_decoder_layers;  /* Chronos-Bolt */
+    int32_t patch_size;          /* input_patch_size (== stride, == output_patch_size) */
+    int32_t context_length;
+    int32_t max_output_patches;  /* Chronos-2 */
+    int32_t prediction_length;   /* Chronos-Bolt */
+    int32_t num_quantiles;
+    const double *quantiles;     /* Chronos quantiles / Timestral quantile_knots */
+    double layer_norm_epsilon;   /* Timestral norm_eps */
+    double rope_theta;
+    double time_encoding_scale;  /* Chronos-2 */
+    int32_t use_arcsinh;         /* Chronos-2 use_arcsinh; Timestral use_asinh */
+    int32_t use_reg_token;
+    /* Chronos-Bolt T5 specifics */
+    int32_t relative_attention_num_buckets;
+    int32_t relative_attention_max_distance;
+    int32_t decoder_start_token_id;
+    int32_t reg_token_id;
+    /* Timestral */
+    int32_t block_size;
+    int32_t n_layer_kinds;
+    const int32_t *layer_kinds;  /* tsfm_layer_kind per layer */
+    double rope_partial_factor;
+    double minimum_scale;
+    double quantile_width_factor;
+    int32_t covariate_enabled;
+    int32_t attend_missing_patches;
+    int32_t time_attn_gate;      /* 1 = "sdpa_sigmoid" gate present */
+    int32_t variate_attn_gate;
+} tsfm_config;
+
+typedef struct tsfm_model tsfm_model;
+
+/* Timestral covariates (timestral/forecaster.zig:37-46): numeric arrays are (B, C, len) f32 with
+ * NaN for missing, categorical ones (B, C, len) f64 codes; past arrays have len T, known ones
+ * T + horizon. A null pointer means "none". */
+typedef struct tsfm_covariates {
+    const float *past;      size_t n_past;
+    const float *known;     size_t n_known;
+    const double *cat_past; size_t n_cat_past;
+    const double *cat_known; size_t n_cat_known;
+} tsfm_covariates;
+
+/* Timestral forecaster options (timestral/forecaster.zig:21-32). */
+typedef struct tsfm_timestral_options {
+    size_t max_context;               /* 0 = the trained context length */
+    size_t per_shot_horizon_patches;  /* default 32, capped at block_size */
+    float quantile_real_cap_k;        /* default 1e4; 0 disables */
+    float extreme_value_threshold;    /* default 1e30 */
+    int32_t symmetric_averaging;      /* default 1 */
+    int32_t clip_nonnegative;         /* default 1 */
+} tsfm_timestral_options;
+
+/* ---------------------------------------------------------------------------------------------
+ * Library */
+
+/* Message of the last failure on the calling thread ("" if none). Never null. */
+const char *tsfm_last_error(void);
+/* Name of a status code. */
+const char *tsfm_status_string(int32_t status);
+/* Number of visible CUDA devices. */
+int32_t tsfm_device_count(int32_t *count);
+/* Library version string. */
+const char *tsfm_version(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * Models. A model holds one weight replica per device in `devices` (n_devices >= 1). Forecasts
+ * shard series across the replicas (contiguous ranges, one host thread per device, no
+ * collective); the output does not depend on the number of devices. Replaces `Model.load` of
+ * each family plus nn.Weight.initWith's upload (core/nn.zig:35-38). */
+int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors, size_t n_tensors,
+                          int32_t compute, const int32_t *devices, int32_t n_devices,
+                          tsfm_model **out);
+void tsfm_model_destroy(tsfm_model *model);
+/* Device bytes held by the weights of one replica. */
+int32_t tsfm_model_weight_bytes(const tsfm_model *model, uint64_t *bytes);
+
+/* ---------------------------------------------------------------------------------------------
+ * Forecasts (host pointers). */
+
+/* chronos2/forecaster.zig:14-22: `inputs` (b, t) f32 with NaN = missing; writes (b, horizon, Q)
+ * quantiles in the config's quantile order. horizon <= max_output_patches * patch_size. */
+int32_t tsfm_forecast_chronos2(tsfm_model *model, const float *inputs, size_t b, size_t t,
+                               size_t horizon, float *out);
+
+/* chronos_bolt/forecaster.zig:22: as above; horizons beyond prediction_length feed every quantile
+ * path back (chronos_bolt/forecaster.zig:45-78). */
+int32_t tsfm_forecast_bolt(tsfm_model *model, const float *inputs, size_t b, size_t t,
+                           size_t horizon, float *out);
+
+/* timestral/forecaster.zig:57-69: `inputs` (b, v, t) f32, zero where unobserved, `observed`
+ * (b, v, t) 0/1 bytes; writes (b, v, horizon, Q). `cov` and `opts` may be null (none / defaults). */
+int32_t tsfm_forecast_timestral(tsfm_model *model, const float *inputs, const uint8_t *observed,
+                                size_t b, size_t v, size_t t, size_t horizon,
+                                const tsfm_covariates *cov, const tsfm_timestral_options *opts,
+                                float *out);
+
+/* Default Timestral options (timestral/forecaster.zig:21-32). */
+void tsfm_timestral_default_options(tsfm_timestral_options *opts);
+
+/* ---------------------------------------------------------------------------------------------
+ * Forecasts on device-resident data (first replica's device only): `inputs` and `out` are device
+ * pointers, `stream` a cudaStream_t or null for the legacy default stream. */
+int32_t tsfm_forecast_chronos2_device(tsfm_model *model, const float *inputs, size_t b, size_t t,
+                                      size_t horizon, float *out, void *stream);
+int32_t tsfm_forecast_bolt_device(tsfm_model *model, const float *inputs, size_t b, size_t t,
+                                  size_t horizon, float *out, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Per-kernel timing of the device forward. When enabled, every kernel launch of a forecast is
+ * bracketed by CUDA events on the launching stream; tsfm_profile_read returns, per kernel class,
+ * the launch count, the summed device time (ms) and the algorithmic work (FLOPs for contractions,
+ * bytes for memory-bound kernels). Class names: "gemm", "attention", "rmsnorm", "patch", "head",
+ * "other". */
+int32_t tsfm_profile_enable(tsfm_model *model, int32_t enable);
+int32_t tsfm_profile_reset(tsfm_model *model);
+int32_t tsfm_profile_read(tsfm_model *model, const char *kernel_class, uint64_t *launches,
+                          double *ms, double *work);
+/* Kernel launches made by the most recent forecast on the first replica. */
+int32_t tsfm_last_launch_count(tsfm_model *model, uint64_t *launches);
+
+/* ---------------------------------------------------------------------------------------------
+ * The reference's CUDA GEMM seam (platform/cuda/gemm.c:232-330), same signatures and semantics:
+ * host pointers, row-major, 0 = success. The device is the current CUDA device (gemm.c uses
+ * device 0). Products run on the tensor cores with 3xTF32 splitting, which keeps them within
+ * FP32 SGEMM accuracy (the reference's own test uses tolerance 1e-4). */
+void *tsfm_weight_register(const float *data, size_t len);                    /* gemm.c:232 */
+void tsfm_weight_release(void *handle);                                      /* gemm.c:244 */
+int tsfm_sgemm_nt(int m, int n, int k, float alpha, const float *A, int lda,  /* gemm.c:316 */
+                  const float *B, int ldb, float *C, int ldc, void *b_buf);
+int tsfm_sgemm_nn(int m, int n, int k, const float *A, int lda,               /* gemm.c:323 */
+                  const float *B, int ldb, float *C, int ldc, void *b_buf);
+
+/* ---------------------------------------------------------------------------------------------
+ * Kernel-level entry points on device pointers (what the family forwards are built from; used by
+ * the kernel parity tests). All return after enqueueing on `stream`.
+ *
+ * tsfm_kernel_linear: y[M, N] (+)= act(x[M, K] · W[N, K]^T + bias) on the tensor cores.
+ *   x_dtype/w_dtype: TSFM_DTYPE_BF16 (kind::f16) or TSFM_DTYPE_F32 (kind::tf32); both equal.
+ *   out_mode: 0 = store bf16, 1 = store f32, 2 = accumulate into f32 (y += result).
+ *   act: 0 none, 1 relu. bias may be null. Replaces nn.linear (core/nn.zig:270-293). */
+int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_t w_dtype,
+                           const float *bias, void *y, int32_t out_mode, int32_t act,
+                           int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldy,
+                           void *stream);
+
+/* tsfm_kernel_attention: o = softmax(mask(scale · q k^T + bias)) v per (group, head) over `n`
+ * tokens of head width 64, q/k/v bf16 with row stride ld_qkv (elements), o bf16 with row stride
+ * ld_o; group g's tokens are rows [g*n, (g+1)*n). key_valid: (groups, n) bytes, or null = all
+ * valid. mask_mode: 0 = T5 additive (invalid keys excluded; a row with no valid key averages all
+ * keys, as -floatMax addition does), 1 = causal over valid keys with the diagonal open,
+ * 2 = bidirectional over valid keys with the diagonal open. rel_bias: (heads, 2n-1) f32 added
+ * at [h][j - i + n - 1], or null. Replaces attn.selfAttend (core/attn.zig:72-96). */
+int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64_t ld_qkv,
+                              void *o, int64_t ld_o, const uint8_t *key_valid,
+                              const float *rel_bias, int32_t groups, int32_t heads, int32_t n,
+                              float scale, int32_t mask_mode, void *stream);
+
+/* tsfm_kernel_rmsnorm: out[r, :] = x[r, :] / sqrt(mean(x^2) + eps) * scale, x f32, out bf16 or
+ * f32 (out_dtype). Replaces nn.rmsNorm (core/nn.zig:367-396). */
+int32_t tsfm_kernel_rmsnorm(const float *x, const float *scale, void *out, int32_t out_dtype,
+                            int64_t rows, int64_t dim, float eps, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TSFM_B200_H */

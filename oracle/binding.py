@@ -1,0 +1,103 @@
+"""ORACLE binding — test infrastructure only (see oracle.h).
+
+ctypes over oracle/liboracle.so, the CPU restatement of the reference forecast path. Only the
+tests, __graft_entry__.smoke() and bench.py's CPU-baseline / reference legs may import this, and
+only as the checker or the timed CPU baseline.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} missing: run `make -C oracle`")
+    lib = ctypes.CDLL(LIB_PATH)
+    P, SZ, I32, F = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_float
+    sig = {
+        "oracle_set_threads": (I32, [I32]),
+        "oracle_get_threads": (I32, []),
+        "oracle_last_error": (ctypes.c_char_p, []),
+        "oracle_model_create": (I32, [P, P, SZ, ctypes.POINTER(P)]),
+        "oracle_model_destroy": (None, [P]),
+        "oracle_forecast_chronos2": (I32, [P, P, SZ, SZ, SZ, P]),
+        "oracle_forecast_bolt": (I32, [P, P, SZ, SZ, SZ, P]),
+        "oracle_forecast_timestral": (I32, [P, P, P, SZ, SZ, SZ, SZ, P, P, P]),
+        "oracle_relative_bucket": (I32, [ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint32]),
+        "oracle_quantile_linear": (F, [P, SZ, F]),
+        "oracle_self_attend": (I32, [I32, P, P, P, P, SZ, SZ, SZ, SZ, SZ, SZ, F, P, P]),
+        "oracle_mask_pick": (I32, [I32, I32, I32]),
+        "oracle_parse_blocks": (I32, [ctypes.c_char_p, P, SZ, ctypes.POINTER(SZ), ctypes.POINTER(SZ),
+                                      ctypes.POINTER(SZ)]),
+        "oracle_linear": (I32, [P, P, P, P, SZ, SZ, SZ]),
+        "oracle_rmsnorm": (I32, [P, P, P, SZ, SZ, F]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+    return lib
+
+
+lib = _load()
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def check(st):
+    if st != 0:
+        raise RuntimeError(f"oracle status {st}: {lib.oracle_last_error().decode()}")
+
+
+class OracleModel:
+    """A checkpoint loaded into the CPU restatement. `parsed` is a tsfm_b200.config.ParsedConfig."""
+
+    def __init__(self, parsed, tensors, table_fn):
+        table, keep = table_fn(tensors)
+        h = ctypes.c_void_p()
+        check(lib.oracle_model_create(ctypes.addressof(parsed.struct), ctypes.addressof(table), len(tensors),
+                                      ctypes.byref(h)))
+        del keep
+        self.h = h
+        self.parsed = parsed
+        self.q = parsed.struct.num_quantiles
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.oracle_model_destroy(self.h)
+            self.h = None
+
+    def forecast_chronos2(self, x, horizon):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty((x.shape[0], horizon, self.q), np.float32)
+        check(lib.oracle_forecast_chronos2(self.h, _ptr(x), x.shape[0], x.shape[1], horizon, _ptr(out)))
+        return out
+
+    def forecast_bolt(self, x, horizon):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty((x.shape[0], horizon, self.q), np.float32)
+        check(lib.oracle_forecast_bolt(self.h, _ptr(x), x.shape[0], x.shape[1], horizon, _ptr(out)))
+        return out
+
+    def forecast_timestral(self, inputs, observed, horizon, cov=None, opts=None):
+        x = np.ascontiguousarray(inputs, np.float32)
+        o = np.ascontiguousarray(observed, np.uint8)
+        b, v, t = x.shape
+        out = np.empty((b, v, horizon, self.q), np.float32)
+        check(lib.oracle_forecast_timestral(self.h, _ptr(x), _ptr(o), b, v, t, horizon,
+                                            None if cov is None else ctypes.addressof(cov),
+                                            None if opts is None else ctypes.addressof(opts), _ptr(out)))
+        return out
+
+
+def set_threads(n):
+    lib.oracle_set_threads(int(n))
+
+
+def get_threads():
+    return lib.oracle_get_threads()

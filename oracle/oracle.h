@@ -1,0 +1,72 @@
+/*
+ * ORACLE — test infrastructure only. Not part of the product.
+ *
+ * A CPU restatement of tsfm-zig's forecast path (the reference is Zig 0.17.1 and cannot be built
+ * here). Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may load it, and
+ * only as the checker or the timed CPU baseline; the CUDA library never links or calls it.
+ *
+ * Parity status: pinned to the reference's own known-answer tests (the T5 bucket table of
+ * chronos_bolt/model.zig:695-703, quantileLinear of chronos_bolt/forecaster.zig:222-228, the
+ * mask-vs-float64 attention property of core/attn.zig:156-189, the CSV cases of
+ * core/series.zig:95-112). The reference publishes no forecast-level golden outputs, so
+ * forecast-level parity of this restatement is unpinned beyond those pieces.
+ *
+ * Arithmetic follows the reference: FP32 compute, FP64 for instance-norm and Welford statistics,
+ * the same operation order per element; matrix products use a fixed per-element reduction order,
+ * so results do not depend on the thread count (the reference's core/nn.zig:285-288 property).
+ */
+#ifndef TSFM_ORACLE_H
+#define TSFM_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../include/tsfm_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct oracle_model oracle_model;
+
+int32_t oracle_set_threads(int32_t n);
+int32_t oracle_get_threads(void);
+const char *oracle_last_error(void);
+
+int32_t oracle_model_create(const tsfm_config *cfg, const tsfm_tensor *tensors, size_t n_tensors,
+                            oracle_model **out);
+void oracle_model_destroy(oracle_model *m);
+
+int32_t oracle_forecast_chronos2(oracle_model *m, const float *inputs, size_t b, size_t t,
+                                 size_t horizon, float *out);
+int32_t oracle_forecast_bolt(oracle_model *m, const float *inputs, size_t b, size_t t,
+                             size_t horizon, float *out);
+int32_t oracle_forecast_timestral(oracle_model *m, const float *inputs, const uint8_t *observed,
+                                  size_t b, size_t v, size_t t, size_t horizon,
+                                  const tsfm_covariates *cov, const tsfm_timestral_options *opts,
+                                  float *out);
+
+/* Known-answer pieces, exposed so the tests can pin them against the reference's own vectors. */
+int32_t oracle_relative_bucket(int64_t rel, uint32_t num_buckets, uint32_t max_distance);
+float oracle_quantile_linear(const float *sorted, size_t n, float level);
+/* attn.selfAttend for one head; mask: 0 full, 1 keys_additive, 2 causal, 3 causal_keys,
+ * 4 full_keys (the order of core/attn.zig:10-21). */
+int32_t oracle_self_attend(int32_t mask, const float *q, const float *k, const float *v, float *o,
+                           size_t ldq, size_t ldk, size_t ldv, size_t ldo, size_t n, size_t hd,
+                           float scale, const uint8_t *key_valid, const float *bias);
+int32_t oracle_mask_pick(int32_t causal, int32_t all_keys_valid, int32_t additive);
+/* core/series.zig parseBlocks: returns 0 and fills blocks/rows/len, writing up to cap values;
+ * nonzero error codes: 1 RaggedInput, 2 RaggedBlocks, 3 EmptyInput, 4 capacity. */
+int32_t oracle_parse_blocks(const char *text, double *values, size_t cap, size_t *blocks,
+                            size_t *rows, size_t *len);
+/* nn.linear (y = x W^T + b) and nn.rmsNorm, for kernel-level parity tests. */
+int32_t oracle_linear(const float *x, const float *w, const float *bias, float *y, size_t rows,
+                      size_t out, size_t in);
+int32_t oracle_rmsnorm(const float *x, const float *scale, float *out, size_t rows, size_t dim,
+                       float eps);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

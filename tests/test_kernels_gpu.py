@@ -1,0 +1,183 @@
+"""Kernel-level parity on the GPU, through the C ABI: the tcgen05 linear kernel against a torch
+fp32 reference of the same product (BF16 and TF32 operands, partial tiles, every epilogue), the
+flash-attention kernel against a float64 reference of the reference's masks, RMSNorm against the
+oracle, and the reference's own padded-stride GEMM-seam test (core/gpu_test.zig:56-101)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import tsfm_b200 as tb  # noqa: E402
+from oracle import binding as ob  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+BF16, F32 = 2, 0
+
+
+def dev():
+    return torch.device("cuda:0")
+
+
+def stream_ptr():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def linear(x, w, bias, y, out_mode, act, M, N, K):
+    tb.check(tb.lib.tsfm_kernel_linear(x.data_ptr(), BF16 if x.dtype == torch.bfloat16 else F32, w.data_ptr(),
+                                       BF16 if w.dtype == torch.bfloat16 else F32,
+                                       None if bias is None else bias.data_ptr(), y.data_ptr(), out_mode, act,
+                                       M, N, K, x.stride(0), w.stride(0), y.stride(0), stream_ptr()))
+    torch.cuda.synchronize()
+
+
+SHAPES = [(128, 256, 64), (300, 336, 48), (1000, 768, 768), (257, 128, 3072), (7, 64, 200), (4096, 2304, 768)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("dtype", ["bf16", "tf32"])
+def test_linear_matches_torch_fp32(M, N, K, dtype):
+    g = torch.Generator(device="cpu").manual_seed(M * 7 + N * 3 + K)
+    x = torch.randn(M, K, generator=g)
+    w = torch.randn(N, K, generator=g) * 0.05
+    bias = torch.randn(N, generator=g)
+    if dtype == "bf16":
+        xd, wd = x.to(dev(), torch.bfloat16), w.to(dev(), torch.bfloat16)
+    else:
+        # TF32 operands: round to the 10-bit mantissa first so the product is exact in fp32
+        xd = x.to(dev()).view(torch.int32).add(0x1000).bitwise_and(~0x1FFF).view(torch.float32)
+        wd = w.to(dev()).view(torch.int32).add(0x1000).bitwise_and(~0x1FFF).view(torch.float32)
+    ref = xd.double() @ wd.double().T + bias.to(dev()).double()
+    tol = 2e-5 * K ** 0.5 * ref.abs().max().item() + 1e-5
+    # f32 store with bias
+    y = torch.full((M, N), float("nan"), device=dev())
+    linear(xd, wd, bias.to(dev()), y, 1, 0, M, N, K)
+    assert (y.double() - ref).abs().max().item() <= tol
+    # relu + bf16 store
+    yb = torch.zeros((M, N), device=dev(), dtype=torch.bfloat16)
+    linear(xd, wd, bias.to(dev()), yb, 0, 1, M, N, K)
+    assert (yb.double() - ref.clamp_min(0)).abs().max().item() <= tol + 2 ** -8 * ref.abs().max().item()
+    # accumulate into an existing residual
+    base = torch.randn(M, N, generator=g).to(dev())
+    y2 = base.clone()
+    linear(xd, wd, None, y2, 2, 0, M, N, K)
+    ref2 = base.double() + xd.double() @ wd.double().T
+    assert (y2.double() - ref2).abs().max().item() <= tol
+
+
+def test_linear_padded_output_stride_keeps_padding():
+    M, N, K = 200, 96, 64
+    x = torch.randn(M, K, device=dev()).to(torch.bfloat16)
+    w = torch.randn(N, K, device=dev()).to(torch.bfloat16)
+    y = torch.full((M, N + 40), -12345.0, device=dev())
+    tb.check(tb.lib.tsfm_kernel_linear(x.data_ptr(), BF16, w.data_ptr(), BF16, None, y.data_ptr(), 1, 0, M, N, K,
+                                       K, K, N + 40, stream_ptr()))
+    torch.cuda.synchronize()
+    assert torch.all(y[:, N:] == -12345.0)
+    ref = x.double() @ w.double().T
+    assert (y[:, :N].double() - ref).abs().max().item() < 1e-3
+
+
+def attention_ref(q, k, v, kv, rel, n, heads, scale, mode):
+    """float64 restatement of the reference masks (core/attn.zig:35-67 + T5 -floatMax addition)."""
+    G = q.shape[0] // n
+    out = torch.zeros(q.shape[0], heads * 64, dtype=torch.float64)
+    qd, kd, vd = q.double().cpu(), k.double().cpu(), v.double().cpu()
+    for g in range(G):
+        valid = kv[g].bool() if kv is not None else torch.ones(n, dtype=torch.bool)
+        for h in range(heads):
+            sl = slice(h * 64, (h + 1) * 64)
+            s = qd[g * n:(g + 1) * n, sl] @ kd[g * n:(g + 1) * n, sl].T * scale
+            if rel is not None:
+                i = torch.arange(n)
+                s = s + rel[h][(i[None, :] - i[:, None]) + n - 1].double()
+            i = torch.arange(n)
+            if mode == 0:
+                allowed = valid[None, :].expand(n, n).clone()
+                if not valid.any():
+                    allowed[:] = True
+                    s = torch.zeros_like(s)
+            elif mode == 1:
+                allowed = (i[None, :] == i[:, None]) | (valid[None, :] & (i[None, :] <= i[:, None]))
+            else:
+                allowed = (i[None, :] == i[:, None]) | valid[None, :]
+            s = s.masked_fill(~allowed, float("-inf"))
+            p = torch.softmax(s, dim=1)
+            out[g * n:(g + 1) * n, sl] = p @ vd[g * n:(g + 1) * n, sl]
+    return out
+
+
+@pytest.mark.parametrize("n,mode,with_rel", [(129, 0, True), (577, 0, False), (11, 0, True), (160, 1, False),
+                                             (70, 2, False), (64, 1, False)])
+def test_attention_matches_float64_reference(n, mode, with_rel):
+    heads, G = 3, 4
+    g = torch.Generator().manual_seed(n + mode)
+    ld = 3 * heads * 64 + 8
+    qkv = (torch.randn(G * n, ld, generator=g) * 0.7).to(torch.bfloat16).to(dev())
+    q, k, v = qkv[:, :heads * 64], qkv[:, heads * 64:2 * heads * 64], qkv[:, 2 * heads * 64:3 * heads * 64]
+    kv = (torch.rand(G, n, generator=g) > 0.3).to(torch.uint8)
+    kv[1, :] = 0  # a group with no valid key
+    kv[2, :] = 1
+    rel = torch.randn(heads, 2 * n - 1, generator=g) if with_rel else None
+    o = torch.zeros(G * n, heads * 64, device=dev(), dtype=torch.bfloat16)
+    kvd = kv.to(dev())
+    reld = rel.to(dev()) if rel is not None else None
+    scale = 1.0 if mode == 0 else 0.125
+    tb.check(tb.lib.tsfm_kernel_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, o.data_ptr(), heads * 64,
+                                          kvd.data_ptr(), None if reld is None else reld.data_ptr(), G, heads, n,
+                                          scale, mode, stream_ptr()))
+    torch.cuda.synchronize()
+    ref = attention_ref(q, k, v, kv, rel, n, heads, scale, mode)
+    err = (o.double().cpu() - ref).abs().max().item()
+    assert err < 3e-2, err
+
+
+def test_rmsnorm_matches_oracle():
+    rows, dim = 1000, 768
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((rows, dim)).astype(np.float32) * 3
+    s = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    want = np.zeros_like(x)
+    ob.lib.oracle_rmsnorm(x.ctypes.data, s.ctypes.data, want.ctypes.data, rows, dim, 1e-6)
+    xd, sd = torch.from_numpy(x).to(dev()), torch.from_numpy(s).to(dev())
+    out = torch.zeros(rows, dim, device=dev())
+    tb.check(tb.lib.tsfm_kernel_rmsnorm(xd.data_ptr(), sd.data_ptr(), out.data_ptr(), F32, rows, dim, 1e-6,
+                                        stream_ptr()))
+    outb = torch.zeros(rows, dim, device=dev(), dtype=torch.bfloat16)
+    tb.check(tb.lib.tsfm_kernel_rmsnorm(xd.data_ptr(), sd.data_ptr(), outb.data_ptr(), BF16, rows, dim, 1e-6,
+                                        stream_ptr()))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(outb.float().cpu().numpy(), want, rtol=2 ** -7, atol=1e-2)
+
+
+def test_gemm_seam_padded_strides_like_reference_gpu_test():
+    # core/gpu_test.zig:56-101: m, n, k = 37, 29, 23; lda, ldb, ldc = 31, 41, 47; sentinel -12345
+    # must survive in the padding; tolerance 1e-4; registered-weight NT and activation NN paths.
+    m, n, k, lda, ldb, ldc = 37, 29, 23, 31, 41, 47
+    rng = np.random.default_rng(0x5EED)
+    a = (rng.random(lda * m, dtype=np.float32) * 2 - 1)
+    bnt = (rng.random(ldb * n, dtype=np.float32) * 2 - 1)
+    bnn = (rng.random(ldb * k, dtype=np.float32) * 2 - 1)
+    A = a.reshape(m, lda)[:, :k].astype(np.float64)
+    BNT = bnt.reshape(n, ldb)[:, :k].astype(np.float64)
+    BNN = bnn.reshape(k, ldb)[:, :n].astype(np.float64)
+    out = np.full(ldc * m, -12345.0, np.float32)
+    assert tb.lib.tsfm_sgemm_nt(m, n, k, 0.7, a.ctypes.data, lda, bnt.ctypes.data, ldb, out.ctypes.data, ldc, None) == 0
+    o = out.reshape(m, ldc)
+    np.testing.assert_allclose(o[:, :n], 0.7 * A @ BNT.T, atol=1e-4)
+    assert np.all(o[:, n:] == -12345.0)
+    wd = np.ascontiguousarray(BNT.astype(np.float32))
+    h = tb.lib.tsfm_weight_register(wd.ctypes.data, wd.size)
+    assert h
+    out[:] = -12345.0
+    assert tb.lib.tsfm_sgemm_nt(m, n, k, 0.7, a.ctypes.data, lda, wd.ctypes.data, k, out.ctypes.data, ldc, h) == 0
+    np.testing.assert_allclose(o[:, :n], 0.7 * A @ BNT.T, atol=1e-4)
+    assert np.all(o[:, n:] == -12345.0)
+    tb.lib.tsfm_weight_release(h)
+    out[:] = -12345.0
+    assert tb.lib.tsfm_sgemm_nn(m, n, k, a.ctypes.data, lda, bnn.ctypes.data, ldb, out.ctypes.data, ldc, None) == 0
+    np.testing.assert_allclose(o[:, :n], A @ BNN, atol=1e-4)
+    assert np.all(o[:, n:] == -12345.0)

@@ -1,0 +1,477 @@
+// The C ABI (include/tsfm_b200.h): argument checks, error reporting, model creation with one
+// replica per device, series sharding across replicas (one host thread per device, no
+// collective), host<->device staging, and the reference's GEMM seam.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <thread>
+
+#include "model.h"
+
+using namespace tsfm;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t report(const Status &s) {
+    g_last_error = s.code ? s.msg : std::string();
+    return s.code;
+}
+
+template <class F>
+int32_t guarded(F &&f) {
+    try {
+        return report(f());
+    } catch (const std::bad_alloc &) {
+        return report(Status::fail(TSFM_ERR_OUT_OF_MEMORY, "host allocation failed"));
+    } catch (const std::exception &e) {
+        return report(Status::fail(TSFM_ERR_INVALID_ARGUMENT, e.what()));
+    } catch (...) {
+        return report(Status::fail(TSFM_ERR_INVALID_ARGUMENT, "unknown exception"));
+    }
+}
+
+Status device_count(int *n) {
+    *n = 0;
+    cudaError_t e = cudaGetDeviceCount(n);
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) {
+        cudaGetLastError();
+        *n = 0;
+        return Status::fail(TSFM_ERR_NO_DEVICE, std::string("no CUDA device: ") + cudaGetErrorString(e));
+    }
+    if (e != cudaSuccess) return Status::cuda(e, "cudaGetDeviceCount");
+    if (*n == 0) return Status::fail(TSFM_ERR_NO_DEVICE, "no CUDA device");
+    return Status::ok();
+}
+
+// Device error words for the kernel-level entry points (one per device, allocated once).
+int *kernel_err_word() {
+    static std::mutex mu;
+    static int *words[64] = {nullptr};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!words[dev]) {
+        void *p = nullptr;
+        if (cudaMalloc(&p, 16) == cudaSuccess) {
+            cudaMemset(p, 0, 16);
+            words[dev] = static_cast<int *>(p);
+        }
+    }
+    return words[dev];
+}
+
+bool is_pinned(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+// Runs fn(i) for every replica, one host thread per replica beyond the first; returns the first
+// failure in replica order after all threads joined.
+template <class F>
+Status for_replicas(size_t n, F &&fn) {
+    if (n == 1) return fn(0);
+    std::vector<Status> st(n);
+    std::vector<std::thread> th;
+    for (size_t i = 1; i < n; ++i) th.emplace_back([&, i] {
+        try {
+            st[i] = fn(i);
+        } catch (const std::bad_alloc &) {
+            st[i] = Status::fail(TSFM_ERR_OUT_OF_MEMORY, "host allocation failed");
+        } catch (...) {
+            st[i] = Status::fail(TSFM_ERR_INVALID_ARGUMENT, "worker thread failed");
+        }
+    });
+    st[0] = fn(0);
+    for (auto &t : th) t.join();
+    for (auto &s : st)
+        if (!s) return s;
+    return Status::ok();
+}
+
+// Forecast `nb` series of one replica from host memory, in chunks that fit the workspace.
+template <class Fwd, class Ws>
+Status replica_forecast(Replica &r, const float *in, int64_t nb, int64_t t, int64_t out_per_series, float *out,
+                        Fwd &&fwd, Ws &&ws_bytes) {
+    std::lock_guard<std::mutex> lk(r.mu);
+    TSFM_CUDA(cudaSetDevice(r.device), "cudaSetDevice");
+    r.prof.cur_launches = 0;
+    size_t free_b = 0, total_b = 0;
+    TSFM_CUDA(cudaMemGetInfo(&free_b, &total_b), "cudaMemGetInfo");
+    const double budget = 0.6 * (double)(free_b + r.ws.buf.bytes);
+    const double per = (double)ws_bytes(1) + (double)(t + out_per_series) * 4.0;
+    int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(nb, (int64_t)(budget / std::max(per, 1.0))));
+    // Keep chunks balanced: equal sizes rather than a long tail.
+    const int64_t nchunks = (nb + chunk - 1) / chunk;
+    chunk = (nb + nchunks - 1) / nchunks;
+    const size_t in_bytes = (size_t)chunk * t * 4, out_bytes = (size_t)chunk * out_per_series * 4;
+    TSFM_TRY(r.ws.reserve(ws_bytes(chunk) + Arena::span(in_bytes) + Arena::span(out_bytes) + 4096));
+    const bool pin_in = is_pinned(in), pin_out = is_pinned(out);
+    if (!pin_in) TSFM_TRY(r.pin_in.ensure(in_bytes));
+    if (!pin_out) TSFM_TRY(r.pin_out.ensure(out_bytes));
+    // The I/O buffers sit at the top of the arena, above what the forward takes.
+    char *top = static_cast<char *>(r.ws.buf.p) + r.ws.buf.bytes;
+    float *d_out = reinterpret_cast<float *>(top - Arena::span(out_bytes));
+    float *d_in = reinterpret_cast<float *>(reinterpret_cast<char *>(d_out) - Arena::span(in_bytes));
+    for (int64_t s0 = 0; s0 < nb; s0 += chunk) {
+        const int64_t n = std::min(chunk, nb - s0);
+        const float *src = in + s0 * t;
+        if (!pin_in) {
+            std::memcpy(r.pin_in.p, src, (size_t)n * t * 4);
+            src = static_cast<const float *>(r.pin_in.p);
+        }
+        TSFM_CUDA(cudaMemcpyAsync(d_in, src, (size_t)n * t * 4, cudaMemcpyHostToDevice, r.stream), "copy inputs");
+        TSFM_TRY(fwd(d_in, n, d_out, r.stream));
+        if (r.ws.used > (size_t)(reinterpret_cast<char *>(d_in) - static_cast<char *>(r.ws.buf.p)))
+            return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "workspace overlaps the I/O buffers");
+        float *dst = out + s0 * out_per_series;
+        void *stage = pin_out ? static_cast<void *>(dst) : r.pin_out.p;
+        TSFM_CUDA(cudaMemcpyAsync(stage, d_out, (size_t)n * out_per_series * 4, cudaMemcpyDeviceToHost, r.stream),
+                  "copy results");
+        TSFM_CUDA(cudaStreamSynchronize(r.stream), "forecast");
+        if (!pin_out) std::memcpy(dst, r.pin_out.p, (size_t)n * out_per_series * 4);
+    }
+    TSFM_TRY(check_device_error(r));
+    r.prof.collect();
+    r.prof.last_forecast_launches = r.prof.cur_launches;
+    return Status::ok();
+}
+
+Status check_model(tsfm_model *m, int family) {
+    if (!m) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null model");
+    if (m->cfg.family != family) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "model is of another family");
+    return Status::ok();
+}
+
+Status c2_args(const tsfm_model *m, const void *in, size_t b, size_t t, size_t horizon, const void *out) {
+    if (!in || !out) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null inputs or outputs");
+    if (b == 0 || t == 0) return Status::fail(TSFM_ERR_EMPTY_INPUT, "EmptyInput");
+    if (horizon == 0 || horizon > (size_t)m->cfg.max_output_patches * m->cfg.patch_size)
+        return Status::fail(TSFM_ERR_HORIZON_TOO_LONG, strf("HorizonTooLong: Chronos-2 supports horizons up to %d steps",
+                                                            m->cfg.max_output_patches * m->cfg.patch_size));
+    return Status::ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *tsfm_last_error(void) { return g_last_error.c_str(); }
+
+const char *tsfm_version(void) { return "tsfm-b200 0.1.0 (sm_100a)"; }
+
+const char *tsfm_status_string(int32_t s) {
+    switch (s) {
+        case TSFM_OK: return "ok";
+        case TSFM_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case TSFM_ERR_INVALID_CONFIG: return "invalid config";
+        case TSFM_ERR_MISSING_TENSOR: return "missing tensor";
+        case TSFM_ERR_SHAPE_MISMATCH: return "shape mismatch";
+        case TSFM_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
+        case TSFM_ERR_CUDA: return "CUDA error";
+        case TSFM_ERR_OUT_OF_MEMORY: return "out of memory";
+        case TSFM_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+        case TSFM_ERR_EMPTY_INPUT: return "empty input";
+        case TSFM_ERR_HORIZON_TOO_LONG: return "horizon too long";
+        case TSFM_ERR_UNSUPPORTED: return "unsupported";
+        case TSFM_ERR_DEGENERATE_INPUT: return "degenerate input";
+        case TSFM_ERR_ASYMMETRIC_QUANTILES: return "asymmetric quantiles";
+        case TSFM_ERR_COVARIATES_UNSUPPORTED: return "covariates unsupported";
+        case TSFM_ERR_NO_DEVICE: return "no device";
+        default: return "unknown status";
+    }
+}
+
+int32_t tsfm_device_count(int32_t *count) {
+    return guarded([&] {
+        if (!count) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null count");
+        int n = 0;
+        Status s = device_count(&n);
+        *count = n;
+        return s;
+    });
+}
+
+int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors, size_t n_tensors, int32_t compute,
+                          const int32_t *devices, int32_t n_devices, tsfm_model **out) {
+    return guarded([&]() -> Status {
+        if (!config || !out || (!tensors && n_tensors)) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null argument");
+        *out = nullptr;
+        if (compute != TSFM_COMPUTE_BF16)
+            return Status::fail(TSFM_ERR_UNSUPPORTED, "compute type: only TSFM_COMPUTE_BF16 is implemented");
+        std::unique_ptr<tsfm_model> m(new tsfm_model());
+        m->cfg = *config;
+        if (config->num_quantiles > 0 && config->quantiles)
+            m->quantiles.assign(config->quantiles, config->quantiles + config->num_quantiles);
+        m->cfg.quantiles = m->quantiles.data();
+        if (config->n_layer_kinds > 0 && config->layer_kinds)
+            m->kinds.assign(config->layer_kinds, config->layer_kinds + config->n_layer_kinds);
+        m->cfg.layer_kinds = m->kinds.data();
+        m->compute = compute;
+        const tsfm_config &c = m->cfg;
+        if (c.family == TSFM_CHRONOS2) {
+            TSFM_TRY(c2_validate(c));
+        } else {
+            return Status::fail(TSFM_ERR_UNSUPPORTED, "family not implemented in this build");
+        }
+        TensorTable table(tensors, n_tensors);
+        if (c.family == TSFM_CHRONOS2) TSFM_TRY(c2_check_tensors(c, table));
+        int ndev = 0;
+        TSFM_TRY(device_count(&ndev));
+        std::vector<int> devs;
+        if (!devices || n_devices <= 0) {
+            devs.push_back(0);
+        } else {
+            for (int i = 0; i < n_devices; ++i) {
+                if (devices[i] < 0 || devices[i] >= ndev)
+                    return Status::fail(TSFM_ERR_NO_DEVICE, strf("device %d out of range (%d visible)", devices[i], ndev));
+                devs.push_back(devices[i]);
+            }
+        }
+        for (size_t i = 0; i < devs.size(); ++i) {
+            auto r = std::make_unique<Replica>();
+            r->device = devs[i];
+            TSFM_CUDA(cudaSetDevice(r->device), "cudaSetDevice");
+            TSFM_CUDA(cudaStreamCreateWithFlags(&r->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+            TSFM_TRY(r->err.alloc(16));
+            TSFM_CUDA(cudaMemset(r->err.p, 0, 16), "clear error word");
+            if (c.family == TSFM_CHRONOS2) {
+                auto w = std::make_unique<C2Dev>();
+                TSFM_TRY(c2_load(*r, c, table, *w));
+                m->c2.push_back(std::move(w));
+            }
+            if (i == 0)
+                for (auto &b : r->weights) m->weight_bytes += b.bytes;
+            m->reps.push_back(std::move(r));
+        }
+        *out = m.release();
+        return Status::ok();
+    });
+}
+
+void tsfm_model_destroy(tsfm_model *model) {
+    if (!model) return;
+    for (auto &r : model->reps) {
+        cudaSetDevice(r->device);
+        if (r->stream) cudaStreamSynchronize(r->stream);
+    }
+    delete model;
+}
+
+int32_t tsfm_model_weight_bytes(const tsfm_model *model, uint64_t *bytes) {
+    return guarded([&] {
+        if (!model || !bytes) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null argument");
+        *bytes = model->weight_bytes;
+        return Status::ok();
+    });
+}
+
+int32_t tsfm_forecast_chronos2(tsfm_model *model, const float *inputs, size_t b, size_t t, size_t horizon, float *out) {
+    return guarded([&]() -> Status {
+        TSFM_TRY(check_model(model, TSFM_CHRONOS2));
+        TSFM_TRY(c2_args(model, inputs, b, t, horizon, out));
+        const size_t n = model->reps.size();
+        const int64_t q = model->cfg.num_quantiles;
+        return for_replicas(n, [&](size_t i) -> Status {
+            const int64_t s0 = (int64_t)(b * i / n), s1 = (int64_t)(b * (i + 1) / n);
+            if (s1 <= s0) return Status::ok();
+            Replica &r = *model->reps[i];
+            const C2Dev &w = *model->c2[i];
+            const tsfm_config &c = model->cfg;
+            return replica_forecast(
+                r, inputs + s0 * t, s1 - s0, (int64_t)t, (int64_t)horizon * q, out + s0 * horizon * q,
+                [&](const float *d_in, int64_t nb, float *d_out, cudaStream_t s) {
+                    return c2_forward(r, c, w, d_in, nb, (int64_t)t, (int64_t)horizon, d_out, s);
+                },
+                [&](int64_t nb) { return c2_workspace(c, nb, (int64_t)t, (int64_t)horizon); });
+        });
+    });
+}
+
+int32_t tsfm_forecast_chronos2_device(tsfm_model *model, const float *inputs, size_t b, size_t t, size_t horizon,
+                                      float *out, void *stream) {
+    return guarded([&]() -> Status {
+        TSFM_TRY(check_model(model, TSFM_CHRONOS2));
+        TSFM_TRY(c2_args(model, inputs, b, t, horizon, out));
+        Replica &r = *model->reps[0];
+        const C2Dev &w = *model->c2[0];
+        std::lock_guard<std::mutex> lk(r.mu);
+        TSFM_CUDA(cudaSetDevice(r.device), "cudaSetDevice");
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : r.stream;
+        r.prof.cur_launches = 0;
+        size_t free_b = 0, total_b = 0;
+        TSFM_CUDA(cudaMemGetInfo(&free_b, &total_b), "cudaMemGetInfo");
+        const double budget = 0.6 * (double)(free_b + r.ws.buf.bytes);
+        const int64_t q = model->cfg.num_quantiles;
+        int64_t chunk = std::max<int64_t>(
+            1, std::min<int64_t>((int64_t)b, (int64_t)(budget / (double)c2_workspace(model->cfg, 1, t, horizon))));
+        const int64_t nchunks = ((int64_t)b + chunk - 1) / chunk;
+        chunk = ((int64_t)b + nchunks - 1) / nchunks;
+        TSFM_TRY(r.ws.reserve(c2_workspace(model->cfg, chunk, t, horizon)));
+        for (int64_t s0 = 0; s0 < (int64_t)b; s0 += chunk) {
+            const int64_t n = std::min<int64_t>(chunk, (int64_t)b - s0);
+            TSFM_TRY(c2_forward(r, model->cfg, w, inputs + s0 * t, n, (int64_t)t, (int64_t)horizon,
+                                out + s0 * (int64_t)horizon * q, s));
+        }
+        TSFM_CUDA(cudaStreamSynchronize(s), "forecast");
+        TSFM_TRY(check_device_error(r));
+        r.prof.collect();
+        r.prof.last_forecast_launches = r.prof.cur_launches;
+        return Status::ok();
+    });
+}
+
+int32_t tsfm_forecast_bolt(tsfm_model *model, const float *, size_t, size_t, size_t, float *) {
+    return guarded([&] { return check_model(model, TSFM_CHRONOS_BOLT); });
+}
+
+int32_t tsfm_forecast_bolt_device(tsfm_model *model, const float *, size_t, size_t, size_t, float *, void *) {
+    return guarded([&] { return check_model(model, TSFM_CHRONOS_BOLT); });
+}
+
+void tsfm_timestral_default_options(tsfm_timestral_options *o) {
+    if (!o) return;
+    o->max_context = 0;
+    o->per_shot_horizon_patches = 32;
+    o->quantile_real_cap_k = 1e4f;
+    o->extreme_value_threshold = 1e30f;
+    o->symmetric_averaging = 1;
+    o->clip_nonnegative = 1;
+}
+
+int32_t tsfm_forecast_timestral(tsfm_model *model, const float *, const uint8_t *, size_t, size_t, size_t, size_t,
+                                const tsfm_covariates *, const tsfm_timestral_options *, float *) {
+    return guarded([&] { return check_model(model, TSFM_TIMESTRAL); });
+}
+
+int32_t tsfm_profile_enable(tsfm_model *model, int32_t enable) {
+    return guarded([&] {
+        if (!model) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null model");
+        for (auto &r : model->reps) r->prof.enabled = enable != 0;
+        return Status::ok();
+    });
+}
+
+int32_t tsfm_profile_reset(tsfm_model *model) {
+    return guarded([&] {
+        if (!model) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null model");
+        for (auto &r : model->reps) {
+            std::fill(std::begin(r->prof.launches), std::end(r->prof.launches), 0);
+            std::fill(std::begin(r->prof.ms), std::end(r->prof.ms), 0.0);
+            std::fill(std::begin(r->prof.work), std::end(r->prof.work), 0.0);
+        }
+        return Status::ok();
+    });
+}
+
+int32_t tsfm_profile_read(tsfm_model *model, const char *kernel_class, uint64_t *launches, double *ms, double *work) {
+    return guarded([&] {
+        if (!model || !kernel_class) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null argument");
+        int cls = -1;
+        for (int i = 0; i < 6; ++i)
+            if (std::strcmp(kernel_class, kclass_name(i)) == 0) cls = i;
+        if (cls < 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, std::string("unknown kernel class ") + kernel_class);
+        uint64_t l = 0;
+        double t = 0, wk = 0;
+        for (auto &r : model->reps) {
+            l += r->prof.launches[cls];
+            t += r->prof.ms[cls];
+            wk += r->prof.work[cls];
+        }
+        if (launches) *launches = l;
+        if (ms) *ms = t;
+        if (work) *work = wk;
+        return Status::ok();
+    });
+}
+
+int32_t tsfm_last_launch_count(tsfm_model *model, uint64_t *launches) {
+    return guarded([&] {
+        if (!model || !launches) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null argument");
+        *launches = model->reps[0]->prof.last_forecast_launches;
+        return Status::ok();
+    });
+}
+
+// ---- kernel-level entry points ------------------------------------------------------------
+
+int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_t w_dtype, const float *bias, void *y,
+                           int32_t out_mode, int32_t act, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                           int64_t ldy, void *stream) {
+    return guarded([&]() -> Status {
+        if (!x || !w || !y) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        if (x_dtype != w_dtype || (x_dtype != TSFM_DTYPE_BF16 && x_dtype != TSFM_DTYPE_F32))
+            return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "linear: x and w must both be BF16 or both F32");
+        if (out_mode < 0 || out_mode > 2 || act < 0 || act > 1)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode / act");
+        LinearCall c;
+        c.x = x;
+        c.w = w;
+        c.f32 = x_dtype == TSFM_DTYPE_F32;
+        c.M = M;
+        c.N = N;
+        c.K = K;
+        c.ldx = ldx;
+        c.ldw = ldw;
+        c.y = y;
+        c.ldy = ldy;
+        c.out_mode = out_mode;
+        c.bias = bias;
+        c.act = act;
+        c.err = kernel_err_word();
+        return launch_linear(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64_t ld_qkv, void *o, int64_t ld_o,
+                              const uint8_t *key_valid, const float *rel_bias, int32_t groups, int32_t heads, int32_t n,
+                              float scale, int32_t mask_mode, void *stream) {
+    return guarded([&]() -> Status {
+        if (!q || !k || !v || !o) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        if (mask_mode < 0 || mask_mode > 2) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "bad mask_mode");
+        AttentionCall c;
+        c.q = static_cast<const __nv_bfloat16 *>(q);
+        c.k = static_cast<const __nv_bfloat16 *>(k);
+        c.v = static_cast<const __nv_bfloat16 *>(v);
+        c.ld_qkv = ld_qkv;
+        c.o = static_cast<__nv_bfloat16 *>(o);
+        c.ld_o = ld_o;
+        c.key_valid = key_valid;
+        c.kv_stride = n;
+        c.rel_bias = rel_bias;
+        c.groups = groups;
+        c.heads = heads;
+        c.n = n;
+        c.scale = scale;
+        c.mask_mode = mask_mode;
+        c.ne = n;
+        c.l = n;
+        return launch_attention(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t tsfm_kernel_rmsnorm(const float *x, const float *scale, void *out, int32_t out_dtype, int64_t rows, int64_t dim,
+                            float eps, void *stream) {
+    return guarded([&]() -> Status {
+        if (!x || !scale || !out) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        RmsNormCall c;
+        c.x = x;
+        c.scale = scale;
+        c.out = out;
+        c.out_mode = out_dtype == TSFM_DTYPE_BF16 ? 0 : 1;
+        c.rows = rows;
+        c.dim = dim;
+        c.eps = eps;
+        return launch_rmsnorm(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
+}  // extern "C"

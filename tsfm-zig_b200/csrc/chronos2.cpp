@@ -1,0 +1,371 @@
+// Chronos-2 on the device: the encoder-only patched transformer of chronos2/model.zig and the
+// forecaster of chronos2/forecaster.zig, as one stream of kernels per chunk of series.
+//
+// Per layer (chronos2/model.zig:189-203):
+//   rmsnorm(x) -> xn;  [q|k|v] = xn Wqkv^T with rotate-half RoPE fused in the epilogue;
+//   flash attention (scale 1, T5 key mask);  x += o Wo^T (accumulate epilogue);
+//   rmsnorm(x) -> xn;  v = xn Wv^T;  x += v Wo^T  (singleton-group attention, model.zig:265-269);
+//   rmsnorm(x) -> xn;  h = relu(xn Wi^T);  x += h Wo^T.
+// The residual stream x stays FP32 in HBM; GEMM operands are BF16 with FP32 accumulation.
+// The patch embedding writes straight into each series' sequence rows (row-remapped epilogue);
+// the REG token and the future-patch embeddings, identical for every series, are computed once
+// at load and broadcast. The head runs only on the future-patch rows.
+#include <cmath>
+#include <cstring>
+
+#include "model.h"
+
+namespace tsfm {
+
+namespace {
+
+std::string layer_name(const char *fmt, int a, int b = 0) { return strf(fmt, a, b); }
+
+Status load_resblock(Replica &r, const TensorTable &t, const std::string &prefix, int64_t in, int64_t hid,
+                     int64_t out, bool bias, bool f32_in, bool f32_hidden, DResBlock &dst) {
+    std::vector<float> w;
+    TSFM_TRY(t.get(prefix + ".hidden_layer.weight", hid * in, w));
+    TSFM_TRY(upload_lin(r, w, hid, in, f32_in, dst.hidden));
+    TSFM_TRY(t.get(prefix + ".output_layer.weight", out * hid, w));
+    TSFM_TRY(upload_lin(r, w, out, hid, f32_hidden, dst.output));
+    TSFM_TRY(t.get(prefix + ".residual_layer.weight", out * in, w));
+    TSFM_TRY(upload_lin(r, w, out, in, f32_in, dst.residual));
+    if (bias) {
+        TSFM_TRY(t.get(prefix + ".hidden_layer.bias", hid, w));
+        TSFM_TRY(upload_bias(r, w, dst.hidden));
+        TSFM_TRY(t.get(prefix + ".output_layer.bias", out, w));
+        TSFM_TRY(upload_bias(r, w, dst.output));
+        TSFM_TRY(t.get(prefix + ".residual_layer.bias", out, w));
+        TSFM_TRY(upload_bias(r, w, dst.residual));
+    }
+    return Status::ok();
+}
+
+Status linear(Replica &r, cudaStream_t s, const DLin &L, const void *x, int64_t M, int64_t ldx, void *y, int64_t ldy,
+              int out_mode, int act, const LinearCall *extra = nullptr) {
+    LinearCall c;
+    if (extra) c = *extra;
+    c.x = x;
+    c.w = L.w;
+    c.f32 = L.f32;
+    c.M = M;
+    c.N = L.out;
+    c.K = L.in;
+    c.ldx = ldx;
+    c.ldw = L.in;
+    c.y = y;
+    c.ldy = ldy;
+    c.out_mode = out_mode;
+    c.bias = L.b;
+    c.act = act;
+    c.err = static_cast<int *>(r.err.p);
+    LaunchScope ls(r, s, K_GEMM, 2.0 * (double)M * (double)L.out * (double)L.in);
+    return launch_linear(c, s);
+}
+
+Status rmsnorm(Replica &r, cudaStream_t s, const float *x, const float *scale, void *out, int out_mode, int64_t rows,
+               int64_t dim, float eps, int64_t g = 0, int64_t G = 0, int64_t off = 0) {
+    RmsNormCall c;
+    c.x = x;
+    c.scale = scale;
+    c.out = out;
+    c.out_mode = out_mode;
+    c.rows = rows;
+    c.dim = dim;
+    c.eps = eps;
+    c.g = g;
+    c.G = G;
+    c.off = off;
+    LaunchScope ls(r, s, K_NORM, (double)rows * dim * (4.0 + (out_mode == 0 ? 2.0 : 4.0)));
+    return launch_rmsnorm(c, s);
+}
+
+}  // namespace
+
+Status c2_validate(const tsfm_config &c) {
+    // chronos2/config.zig:44-55
+    if (c.num_heads <= 0 || c.d_model != c.num_heads * c.d_kv) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: d_model != num_heads * d_kv");
+    if (c.d_ff <= 0 || c.num_layers <= 0) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: d_ff / num_layers");
+    if (c.patch_size <= 0) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: patch size");
+    if (c.context_length <= 0 || c.max_output_patches <= 0) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: context_length / max_output_patches");
+    if (c.num_quantiles <= 0 || !c.quantiles) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: quantiles");
+    if (!c.use_reg_token) return Status::fail(TSFM_ERR_INVALID_CONFIG, "UnsupportedConfig: use_reg_token = false");
+    if (!(c.time_encoding_scale > 0) || !(c.layer_norm_epsilon > 0)) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: time_encoding_scale / eps");
+    // Kernel constraints of this backend.
+    if (c.d_kv != 64) return Status::fail(TSFM_ERR_UNSUPPORTED, "Chronos-2: head width must be 64");
+    if (c.d_model % 64 || c.d_ff % 8) return Status::fail(TSFM_ERR_UNSUPPORTED, "Chronos-2: d_model % 64 and d_ff % 8 must be 0");
+    if ((3 * c.patch_size) % 4 || (c.num_quantiles * c.patch_size) % 4)
+        return Status::fail(TSFM_ERR_UNSUPPORTED, "Chronos-2: patch feature rows must be 16-byte multiples");
+    return Status::ok();
+}
+
+Status c2_check_tensors(const tsfm_config &c, const TensorTable &t) {
+    const int64_t d = c.d_model, ps = c.patch_size, hid = c.d_ff, q = c.num_quantiles;
+    struct Blk {
+        const char *prefix;
+        int64_t in, out;
+    };
+    for (const Blk &b : {Blk{"input_patch_embedding", 3 * ps, d}, Blk{"output_patch_embedding", d, q * ps}}) {
+        const std::string p = b.prefix;
+        TSFM_TRY(t.check(p + ".hidden_layer.weight", hid * b.in));
+        TSFM_TRY(t.check(p + ".hidden_layer.bias", hid));
+        TSFM_TRY(t.check(p + ".output_layer.weight", b.out * hid));
+        TSFM_TRY(t.check(p + ".output_layer.bias", b.out));
+        TSFM_TRY(t.check(p + ".residual_layer.weight", b.out * b.in));
+        TSFM_TRY(t.check(p + ".residual_layer.bias", b.out));
+    }
+    TSFM_TRY(t.check("encoder.final_layer_norm.weight", d));
+    TSFM_TRY(t.check("shared.weight", 2 * d));
+    for (int li = 0; li < c.num_layers; ++li) {
+        for (int which = 0; which < 2; ++which) {
+            const std::string p = layer_name("encoder.block.%d.layer.%d.", li, which);
+            TSFM_TRY(t.check(p + "layer_norm.weight", d));
+            for (const char *nm : {"q", "k", "v", "o"}) TSFM_TRY(t.check(p + "self_attention." + nm + ".weight", d * d));
+        }
+        TSFM_TRY(t.check(layer_name("encoder.block.%d.layer.2.layer_norm.weight", li), d));
+        TSFM_TRY(t.check(layer_name("encoder.block.%d.layer.2.mlp.wi.weight", li), hid * d));
+        TSFM_TRY(t.check(layer_name("encoder.block.%d.layer.2.mlp.wo.weight", li), d * hid));
+    }
+    return Status::ok();
+}
+
+Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, C2Dev &w) {
+    const int64_t d = c.d_model, ps = c.patch_size, hid = c.d_ff, q = c.num_quantiles;
+    // The patch features enter a TF32 product (K = 3 * patch); everything else is BF16.
+    TSFM_TRY(load_resblock(r, t, "input_patch_embedding", 3 * ps, hid, d, true, true, false, w.in_embed));
+    TSFM_TRY(load_resblock(r, t, "output_patch_embedding", d, hid, q * ps, true, false, false, w.out_embed));
+    std::vector<float> v;
+    TSFM_TRY(t.get("encoder.final_layer_norm.weight", d, v));
+    TSFM_TRY(upload_f32(r, v, &w.final_norm));
+    TSFM_TRY(t.get("shared.weight", 2 * d, v));
+    std::vector<float> reg(v.begin() + d, v.begin() + 2 * d);
+    TSFM_TRY(upload_f32(r, reg, &w.reg));
+    for (int li = 0; li < c.num_layers; ++li) {
+        C2Dev::Layer L;
+        std::vector<float> qkv;
+        for (int which = 0; which < 2; ++which) {
+            const std::string p = layer_name("encoder.block.%d.layer.%d.", li, which);
+            TSFM_TRY(t.get(p + "layer_norm.weight", d, v));
+            TSFM_TRY(upload_f32(r, v, which == 0 ? &L.time_norm : &L.group_norm));
+            if (which == 0) {
+                qkv.clear();
+                for (const char *nm : {"q", "k", "v"}) {
+                    TSFM_TRY(t.get(p + "self_attention." + nm + ".weight", d * d, v));
+                    qkv.insert(qkv.end(), v.begin(), v.end());
+                }
+                TSFM_TRY(upload_lin(r, qkv, 3 * d, d, false, L.qkv));
+                TSFM_TRY(t.get(p + "self_attention.o.weight", d * d, v));
+                TSFM_TRY(upload_lin(r, v, d, d, false, L.o));
+            } else {
+                // Singleton groups: only v and o take part (chronos2/model.zig:265-269); q and k are
+                // still required to exist, as the reference loads them.
+                TSFM_TRY(t.get(p + "self_attention.q.weight", d * d, v));
+                TSFM_TRY(t.get(p + "self_attention.k.weight", d * d, v));
+                TSFM_TRY(t.get(p + "self_attention.v.weight", d * d, v));
+                TSFM_TRY(upload_lin(r, v, d, d, false, L.gv));
+                TSFM_TRY(t.get(p + "self_attention.o.weight", d * d, v));
+                TSFM_TRY(upload_lin(r, v, d, d, false, L.go));
+            }
+        }
+        TSFM_TRY(t.get(layer_name("encoder.block.%d.layer.2.layer_norm.weight", li), d, v));
+        TSFM_TRY(upload_f32(r, v, &L.mlp_norm));
+        TSFM_TRY(t.get(layer_name("encoder.block.%d.layer.2.mlp.wi.weight", li), hid * d, v));
+        TSFM_TRY(upload_lin(r, v, hid, d, false, L.wi));
+        TSFM_TRY(t.get(layer_name("encoder.block.%d.layer.2.mlp.wo.weight", li), d * hid, v));
+        TSFM_TRY(upload_lin(r, v, d, hid, false, L.wo));
+        w.layers.push_back(L);
+    }
+    // RoPE tables for every position a sequence can have (chronos2/model.zig:107-113, 178-187).
+    const int64_t hd = c.d_kv, half = hd / 2;
+    const int64_t max_ctx_patches = (c.context_length + ps - 1) / ps;
+    w.max_seq = max_ctx_patches + 1 + c.max_output_patches;
+    std::vector<float> inv(half), cs(w.max_seq * half), sn(w.max_seq * half);
+    const float base = (float)c.rope_theta;
+    for (int64_t i = 0; i < half; ++i) inv[i] = 1.0f / std::pow(base, (float)(2 * i) / (float)hd);
+    for (int64_t tok = 0; tok < w.max_seq; ++tok)
+        for (int64_t i = 0; i < half; ++i) {
+            const float ang = inv[i] * (float)tok;
+            cs[tok * half + i] = std::cos(ang);
+            sn[tok * half + i] = std::sin(ang);
+        }
+    TSFM_TRY(upload_f32(r, cs, &w.rope_cos));
+    TSFM_TRY(upload_f32(r, sn, &w.rope_sin));
+
+    // Future patches carry only their time encoding (chronos2/forecaster.zig:146-154), the same for
+    // every series: embed them once for the longest horizon.
+    const int64_t nf = c.max_output_patches;
+    std::vector<float> ff(nf * 3 * ps, 0.0f);
+    for (int64_t p = 0; p < nf; ++p)
+        for (int64_t i = 0; i < ps; ++i) {
+            const float tv = (float)(p * ps + i) / (float)c.time_encoding_scale;
+            uint32_t u;
+            std::memcpy(&u, &tv, 4);
+            if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & ~0x1fffu;  // TF32 operand
+            float tr;
+            std::memcpy(&tr, &u, 4);
+            ff[p * 3 * ps + i] = tr;
+        }
+    float *d_ff = nullptr;
+    TSFM_TRY(upload_f32(r, ff, &d_ff));
+    TSFM_TRY(upload_f32(r, std::vector<float>(nf * d, 0.0f), &w.fut_emb));
+    DevBuf tmp;
+    TSFM_TRY(tmp.alloc(nf * hid * 2));
+    cudaStream_t s = r.stream;
+    TSFM_TRY(linear(r, s, w.in_embed.hidden, d_ff, nf, 3 * ps, tmp.p, hid, 0, 1));
+    TSFM_TRY(linear(r, s, w.in_embed.residual, d_ff, nf, 3 * ps, w.fut_emb, d, 1, 0));
+    TSFM_TRY(linear(r, s, w.in_embed.output, tmp.p, nf, hid, w.fut_emb, d, 2, 0));
+    TSFM_CUDA(cudaStreamSynchronize(s), "Chronos-2 future embeddings");
+    TSFM_TRY(check_device_error(r));
+    return Status::ok();
+}
+
+static void c2_geometry(const tsfm_config &c, int64_t t_in, int64_t horizon, int64_t &t, int64_t &start, int64_t &pad,
+                        int64_t &n_ctx, int64_t &n_out, int64_t &seq) {
+    const int64_t ps = c.patch_size;
+    t = std::min<int64_t>(t_in, c.context_length);
+    start = t_in - t;
+    pad = (ps - t % ps) % ps;
+    n_ctx = (t + pad) / ps;
+    n_out = (horizon + ps - 1) / ps;
+    seq = n_ctx + 1 + n_out;
+}
+
+size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64_t horizon) {
+    int64_t t, start, pad, n_ctx, n_out, seq;
+    c2_geometry(c, t_in, horizon, t, start, pad, n_ctx, n_out, seq);
+    const int64_t d = c.d_model, ff = c.d_ff, ps = c.patch_size, q = c.num_quantiles, rows = nb * seq;
+    size_t b = 0;
+    b += Arena::span(nb * 4) * 2;
+    b += Arena::span(nb * n_ctx * 3 * ps * 4);
+    b += Arena::span(nb * seq);
+    b += Arena::span(rows * d * 4);
+    b += Arena::span(rows * d * 2);
+    b += Arena::span(rows * 3 * d * 2);
+    b += Arena::span(rows * d * 2);
+    b += Arena::span(rows * ff * 2);
+    b += Arena::span(nb * n_out * q * ps * 4);
+    return b;
+}
+
+Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float *d_in, int64_t b, int64_t t_in,
+                  int64_t horizon, float *d_out, cudaStream_t s) {
+    int64_t t, start, pad, n_ctx, n_out, seq;
+    c2_geometry(c, t_in, horizon, t, start, pad, n_ctx, n_out, seq);
+    const int64_t d = c.d_model, ff = c.d_ff, ps = c.patch_size, q = c.num_quantiles, nh = c.num_heads;
+    const float eps = (float)c.layer_norm_epsilon;
+    const int64_t rows = b * seq;
+    if (seq > w.max_seq) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "Chronos-2: sequence longer than the RoPE table");
+
+    Arena &ws = r.ws;
+    ws.reset();
+    float *loc = ws.take<float>(b), *scl = ws.take<float>(b);
+    float *feats = ws.take<float>(b * n_ctx * 3 * ps);
+    uint8_t *kv = ws.take<uint8_t>(b * seq);
+    float *x = ws.take<float>(rows * d);
+    __nv_bfloat16 *xn = ws.take<__nv_bfloat16>(rows * d);
+    __nv_bfloat16 *qkv = ws.take<__nv_bfloat16>(rows * 3 * d);
+    __nv_bfloat16 *ao = ws.take<__nv_bfloat16>(rows * d);
+    __nv_bfloat16 *h = ws.take<__nv_bfloat16>(rows * ff);
+    float *raw = ws.take<float>(b * n_out * q * ps);
+    if (ws.used > ws.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Chronos-2: workspace too small");
+
+    // 1. instance norm + patch features (TF32-rounded FP32) + key validity.
+    {
+        PatchCall pc;
+        pc.inputs = d_in;
+        pc.stride = t_in;
+        pc.start = start;
+        pc.t = t;
+        pc.b = b;
+        pc.ps = (int)ps;
+        pc.pad = (int)pad;
+        pc.n_ctx = (int)n_ctx;
+        pc.feat_kind = 0;
+        pc.tscale = (float)c.time_encoding_scale;
+        pc.arcsinh = c.use_arcsinh;
+        pc.feat_mode = 3;
+        pc.feats = feats;
+        pc.loc = loc;
+        pc.scale = scl;
+        pc.key_valid = kv;
+        pc.seq = seq;
+        pc.extra_valid = (int)(1 + n_out);
+        LaunchScope ls(r, s, K_PATCH, (double)b * t * 4 + (double)b * n_ctx * 3 * ps * 4);
+        TSFM_TRY(launch_patch(pc, s));
+    }
+    // 2. patch embedding ResBlock straight into the sequence rows: x = res(f) + out(relu(hid(f))).
+    {
+        const int64_t m = b * n_ctx;
+        TSFM_TRY(linear(r, s, w.in_embed.hidden, feats, m, 3 * ps, h, ff, 0, 1));
+        LinearCall remap;
+        remap.rm_g = n_ctx;
+        remap.rm_G = seq;
+        remap.rm_off = 0;
+        TSFM_TRY(linear(r, s, w.in_embed.residual, feats, m, 3 * ps, x, d, 1, 0, &remap));
+        TSFM_TRY(linear(r, s, w.in_embed.output, h, m, ff, x, d, 2, 0, &remap));
+        LaunchScope ls(r, s, K_OTHER, (double)b * (1 + n_out) * d * 8);
+        TSFM_TRY(launch_broadcast_rows(x, b, seq, n_ctx, w.reg, 1, d, s));
+        TSFM_TRY(launch_broadcast_rows(x, b, seq, n_ctx + 1, w.fut_emb, n_out, d, s));
+    }
+    // 3. encoder layers.
+    for (const C2Dev::Layer &L : w.layers) {
+        TSFM_TRY(rmsnorm(r, s, x, L.time_norm, xn, 0, rows, d, eps));
+        LinearCall rope;
+        rope.rope_cos = w.rope_cos;
+        rope.rope_sin = w.rope_sin;
+        rope.rope_cols = (int)(2 * d);
+        rope.rope_p1 = 0;
+        rope.rope_p2 = seq;
+        TSFM_TRY(linear(r, s, L.qkv, xn, rows, d, qkv, 3 * d, 0, 0, &rope));
+        {
+            AttentionCall ac;
+            ac.q = qkv;
+            ac.k = qkv + d;
+            ac.v = qkv + 2 * d;
+            ac.ld_qkv = 3 * d;
+            ac.o = ao;
+            ac.ld_o = d;
+            ac.key_valid = kv;
+            ac.kv_stride = seq;
+            ac.groups = (int)b;
+            ac.heads = (int)nh;
+            ac.n = (int)seq;
+            ac.scale = 1.0f;
+            ac.mask_mode = 0;
+            LaunchScope ls(r, s, K_ATTN, 4.0 * (double)b * nh * seq * seq * 64);
+            TSFM_TRY(launch_attention(ac, s));
+        }
+        TSFM_TRY(linear(r, s, L.o, ao, rows, d, x, d, 2, 0));
+        TSFM_TRY(rmsnorm(r, s, x, L.group_norm, xn, 0, rows, d, eps));
+        TSFM_TRY(linear(r, s, L.gv, xn, rows, d, ao, d, 0, 0));
+        TSFM_TRY(linear(r, s, L.go, ao, rows, d, x, d, 2, 0));
+        TSFM_TRY(rmsnorm(r, s, x, L.mlp_norm, xn, 0, rows, d, eps));
+        TSFM_TRY(linear(r, s, L.wi, xn, rows, d, h, ff, 0, 1));
+        TSFM_TRY(linear(r, s, L.wo, h, rows, ff, x, d, 2, 0));
+    }
+    // 4. final norm on the future-patch rows only, then the quantile head.
+    const int64_t m = b * n_out;
+    TSFM_TRY(rmsnorm(r, s, x, w.final_norm, xn, 0, m, d, eps, n_out, seq, n_ctx + 1));
+    TSFM_TRY(linear(r, s, w.out_embed.hidden, xn, m, d, h, ff, 0, 1));
+    TSFM_TRY(linear(r, s, w.out_embed.residual, xn, m, d, raw, q * ps, 1, 0));
+    TSFM_TRY(linear(r, s, w.out_embed.output, h, m, ff, raw, q * ps, 2, 0));
+    {
+        HeadPostCall hc;
+        hc.raw = raw;
+        hc.loc = loc;
+        hc.scale = scl;
+        hc.out = d_out;
+        hc.b = b;
+        hc.horizon = horizon;
+        hc.q = (int)q;
+        hc.ps = (int)ps;
+        hc.n_out = (int)n_out;
+        hc.arcsinh = c.use_arcsinh;
+        hc.layout = 0;
+        LaunchScope ls(r, s, K_HEAD, (double)b * horizon * q * 8);
+        TSFM_TRY(launch_head_post(hc, s));
+    }
+    return Status::ok();
+}
+
+}  // namespace tsfm

@@ -1,0 +1,148 @@
+// Internal API between the host runtime (C++) and the CUDA kernels. No torch types anywhere.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/tsfm_b200.h"
+
+namespace tsfm {
+
+struct Status {
+    int code = 0;
+    std::string msg;
+    static Status ok() { return Status{}; }
+    static Status fail(int c, std::string m) {
+        Status s;
+        s.code = c;
+        s.msg = std::move(m);
+        return s;
+    }
+    static Status cuda(cudaError_t e, const std::string &where) {
+        return fail(e == cudaErrorMemoryAllocation ? TSFM_ERR_OUT_OF_MEMORY : TSFM_ERR_CUDA,
+                    where + ": " + cudaGetErrorString(e));
+    }
+    explicit operator bool() const { return code == 0; }
+};
+
+#define TSFM_TRY(expr)                  \
+    do {                                \
+        ::tsfm::Status _s = (expr);     \
+        if (!_s) return _s;             \
+    } while (0)
+
+#define TSFM_CUDA(expr, where)                                   \
+    do {                                                         \
+        cudaError_t _e = (expr);                                 \
+        if (_e != cudaSuccess) return ::tsfm::Status::cuda(_e, where); \
+    } while (0)
+
+// y = epilogue(x[M, K] · w[N, K]^T). x and w are both BF16 (f32 = false) or both FP32 read as
+// TF32 (f32 = true).
+struct LinearCall {
+    const void *x = nullptr;
+    const void *w = nullptr;
+    bool f32 = false;
+    int64_t M = 0, N = 0, K = 0, ldx = 0, ldw = 0;
+    void *y = nullptr;
+    int64_t ldy = 0;
+    int out_mode = 0;  // 0 bf16, 1 f32, 2 f32 accumulate (y += ...), 3 f32 rounded to tf32
+    const float *bias = nullptr;
+    int act = 0;       // 0 none, 1 relu
+    // output row remap: y row = (r / rm_g) * rm_G + r % rm_g + rm_off when rm_g > 0
+    int64_t rm_g = 0, rm_G = 0, rm_off = 0;
+    // rotate-half RoPE on columns [0, rope_cols), 64-wide heads; tables [positions, 32]
+    const float *rope_cos = nullptr, *rope_sin = nullptr;
+    int rope_cols = 0;
+    int64_t rope_p1 = 0, rope_p2 = 1;  // position index = (r / p1) * p2 + r % p2 (p1 == 0: r % p2)
+    int *err = nullptr;                // device error word
+};
+Status launch_linear(const LinearCall &c, cudaStream_t stream);
+
+// Flash attention over groups of n tokens, head width 64, BF16 q/k/v/o.
+struct AttentionCall {
+    const __nv_bfloat16 *q = nullptr, *k = nullptr, *v = nullptr;
+    int64_t ld_qkv = 0;
+    __nv_bfloat16 *o = nullptr;
+    int64_t ld_o = 0;
+    const uint8_t *key_valid = nullptr;  // (groups, kv_len) or null
+    int64_t kv_stride = 0;               // stride of key_valid between groups (default n)
+    const float *rel_bias = nullptr;     // (heads, 2n - 1) or null
+    int groups = 0, heads = 0, n = 0;
+    float scale = 1.0f;
+    // 0: T5 additive (keys_additive / full); 1: causal over valid keys, diagonal open;
+    // 2: bidirectional over valid keys, diagonal open. For modes 1-2, queries i >= ne are
+    // decoder queries reading keys [0, l) that are valid plus [ne, i].
+    int mask_mode = 0;
+    int ne = 0, l = 0;
+    const uint8_t *group_bidir = nullptr;  // per group: 1 = bidirectional encoder rows (mode 1 only)
+};
+Status launch_attention(const AttentionCall &c, cudaStream_t stream);
+
+// RMSNorm: out[r] = x[in_row(r)] * (1 / sqrt(mean(x^2) + eps)) * scale.
+// in_row(r) = (r / g) * G + r % g + off when g > 0. out_mode: 0 bf16, 1 f32, 3 f32 rounded to tf32.
+struct RmsNormCall {
+    const float *x = nullptr;
+    const float *scale = nullptr;
+    void *out = nullptr;
+    int out_mode = 0;
+    int64_t rows = 0, dim = 0;
+    float eps = 1e-6f;
+    int64_t g = 0, G = 0, off = 0;
+};
+Status launch_rmsnorm(const RmsNormCall &c, cudaStream_t stream);
+
+// Chronos-2 / Chronos-Bolt instance normalisation and patch features (chronos2/forecaster.zig:94-154,
+// chronos_bolt/forecaster.zig:150-197), one CTA per series.
+struct PatchCall {
+    const float *inputs = nullptr;  // row s at inputs + s * stride + start, length t
+    int64_t stride = 0, start = 0, t = 0;
+    int64_t b = 0;
+    int ps = 16, pad = 0, n_ctx = 0;
+    int feat_kind = 0;      // 0 Chronos-2 [time, value, mask], 1 Chronos-Bolt [value, mask]
+    float tscale = 1.0f;
+    int arcsinh = 1;
+    int feat_mode = 1;      // features dtype: 0 bf16, 1 f32, 3 f32 rounded to tf32
+    void *feats = nullptr;  // (b * n_ctx, feat_width)
+    float *loc = nullptr, *scale = nullptr;  // (b)
+    uint8_t *key_valid = nullptr;            // (b, seq): [0, n_ctx) written, then `extra_valid` ones
+    int64_t seq = 0;
+    int extra_valid = 0;
+};
+Status launch_patch(const PatchCall &c, cudaStream_t stream);
+
+// Copies `n_rows` rows of `src` (d floats) into every series' sequence at rows
+// s * seq + row0 .. + n_rows (the shared REG and future-patch embeddings).
+Status launch_broadcast_rows(float *x, int64_t b, int64_t seq, int64_t row0, const float *src,
+                             int64_t n_rows, int64_t d, cudaStream_t stream);
+
+// Chronos-2 head post-processing (chronos2/forecaster.zig:186-203): out[(s*H + step)*Q + qi] =
+// sinh(raw[(s*n_out + p)*Q*ps + qi*ps + i]) * scale[s] + loc[s] for step = p*ps + i < H.
+struct HeadPostCall {
+    const float *raw = nullptr;
+    const float *loc = nullptr, *scale = nullptr;
+    float *out = nullptr;
+    int64_t b = 0, horizon = 0;
+    int q = 0, ps = 0, n_out = 0;
+    int arcsinh = 1;
+    int layout = 0;  // 0 Chronos-2 (patch, q, ps) rows; 1 Chronos-Bolt (q, P) rows -> (b, q, P) store
+};
+Status launch_head_post(const HeadPostCall &c, cudaStream_t stream);
+
+// FP32 -> BF16 / TF32 conversion of a device buffer (weights at load).
+Status launch_convert(const float *src, void *dst, int64_t n, int mode, cudaStream_t stream);
+
+int num_sms();
+
+}  // namespace tsfm
+
+namespace tsfm {
+// 3xTF32 operand split for FP32-accurate products: hi = tf32(alpha * x), lo = tf32(alpha * x - hi)
+// for a [rows, cols] matrix with row stride ld_src; outputs have row stride ld_dst, padding columns
+// [cols, ld_dst) are zeroed.
+Status launch_split_tf32(const float *src, int64_t rows, int64_t cols, int64_t ld_src, float alpha, float *hi,
+                         float *lo, int64_t ld_dst, cudaStream_t stream);
+}  // namespace tsfm

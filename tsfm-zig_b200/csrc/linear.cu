@@ -1,0 +1,451 @@
+// The linear-layer kernel: y = epilogue(x[M, K] · W[N, K]^T) on the sm_100a tensor cores.
+//
+// Replaces nn.linear / gemmNTFallback (core/nn.zig:68-162, 270-293) and the cuBLAS SGEMM the
+// reference offloads to (platform/cuda/gemm.c:252-314).
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0       TMA producer: 128-byte-swizzled K-major tiles of x (128 rows) and W (BN rows)
+//                into a STAGES-deep shared-memory ring, one mbarrier pair per stage.
+//   warp 1       tensor-memory allocator + MMA issuer (one elected thread): tcgen05.mma
+//                M=128 x N=BN x K=16 (BF16, kind::f16) or K=8 (TF32, kind::tf32), FP32
+//                accumulators in TMEM, double-buffered so the epilogue of tile i overlaps the
+//                main loop of tile i+1.
+//   warps 2..5   epilogue: tcgen05.ld 32 lanes x 32 columns, fused bias / ReLU / rotate-half RoPE
+//                / residual accumulation, vectorised stores (BF16 or FP32), optional row remap
+//                so embeddings land directly in their sequence slots.
+// Tiles are walked m-major with the BN-wide column tiles of one row block adjacent, so CTAs
+// working on the same 128 rows of x run together and share them through L2; W stays L2-resident.
+// Every output element is reduced over K by one CTA in a fixed order (no split-K, no atomics),
+// so results do not depend on the grid size or the number of GPUs.
+#include "kernels.h"
+#include "ptx.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace tsfm {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct TileCfg {
+    static constexpr int STAGES = BN >= 256 ? 4 : 6;
+    static constexpr int A_BYTES = kBM * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+    static constexpr int SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+};
+
+struct Epi {
+    int64_t M, N, K;
+    void *out;
+    int64_t ldo;
+    const float *bias;
+    int act;           // 0 none, 1 relu
+    int out_mode;      // 0 bf16 store, 1 f32 store, 2 f32 accumulate, 3 f32 store rounded to tf32
+    int64_t rm_g, rm_G, rm_off;  // output row = (r / rm_g) * rm_G + r % rm_g + rm_off (rm_g > 0)
+    const float *rope_cos;       // [positions, 32]; null = no rotation
+    const float *rope_sin;
+    int rope_cols;               // columns [0, rope_cols) are rotated per 64-wide head
+    int64_t rope_p1, rope_p2;    // position index = (r / p1) * p2 + r % p2 (p1 == 0: r % p2)
+    int *err;
+};
+
+__device__ __forceinline__ void store_chunk(const Epi &e, int64_t orow, int64_t col0, int nvalid, float (&v)[32]) {
+    if (e.out_mode == 0) {
+        __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(e.out) + orow * e.ldo + col0;
+        if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 pk;
+                uint32_t *w = reinterpret_cast<uint32_t *>(&pk);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    __nv_bfloat162 b2 = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+                    w[j] = *reinterpret_cast<uint32_t *>(&b2);
+                }
+                reinterpret_cast<uint4 *>(o)[q] = pk;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nvalid) o[j] = __float2bfloat16_rn(v[j]);
+        }
+    } else {
+        float *o = reinterpret_cast<float *>(e.out) + orow * e.ldo + col0;
+        if (e.out_mode == 3) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = to_tf32(v[j]);
+        }
+        const bool vec = nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
+        if (e.out_mode == 2) {
+            if (vec) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    float4 a = reinterpret_cast<float4 *>(o)[q];
+                    a.x += v[4 * q];
+                    a.y += v[4 * q + 1];
+                    a.z += v[4 * q + 2];
+                    a.w += v[4 * q + 3];
+                    reinterpret_cast<float4 *>(o)[q] = a;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (j < nvalid) o[j] += v[j];
+            }
+        } else {
+            if (vec) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    reinterpret_cast<float4 *>(o)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (j < nvalid) o[j] = v[j];
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void bias_act(const Epi &e, int64_t col0, int nvalid, float (&v)[32]) {
+    if (e.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < nvalid) v[j] += __ldg(e.bias + col0 + j);
+    }
+    if (e.act == 1) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+    }
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Epi e) {
+    using C = TileCfg<BN>;
+    constexpr int STAGES = C::STAGES;
+    constexpr int BK = 128 / (int)sizeof(T);
+    constexpr uint32_t FMT = sizeof(T) == 2 ? 1u : 2u;
+    constexpr uint32_t IDESC = idesc_f32acc(FMT, kBM, BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * C::A_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sB + STAGES * C::B_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t m_tiles = (e.M + kBM - 1) / kBM, n_tiles = (e.N + BN - 1) / BN;
+    const int64_t tiles = m_tiles * n_tiles;
+    const int num_k = (int)((e.K + BK - 1) / BK);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], 4 * 32);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            uint32_t issued = 0, issued_ph = 0;  // per-stage bit: loaded at least once / parity of last load
+            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int32_t m0 = (int32_t)((t / n_tiles) * kBM), n0 = (int32_t)((t % n_tiles) * BN);
+                for (int kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
+                    tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * BK, m0);
+                    tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * BK, n0);
+                    issued |= 1u << s;
+                    issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // Let loads already in flight land before the CTA can exit: the last load issued
+                // into stage i completes phase issued_ph[i] of full[i]; bounded grace period.
+                const unsigned long long t0 = globaltimer_ns();
+                for (int i = 0; i < STAGES; ++i) {
+                    if (!((issued >> i) & 1u)) continue;
+                    while (!mbar_try_wait(&full[i], (issued_ph >> i) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int acc = 0;
+            uint32_t aph = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_MMA_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag, e.err, ERR_SITE_GEMM_MMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = sdesc_k128(sA + s * C::A_BYTES);
+                    const uint64_t bd = sdesc_k128(sB + s * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        // advance 32 bytes along K inside the 128-byte swizzle atom
+                        if constexpr (sizeof(T) == 2)
+                            mma_bf16(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
+                        else
+                            mma_tf32(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
+                    }
+                    mma_commit(&empty[s]);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(&tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    aph ^= 1u;
+                }
+            }
+            // All MMAs issued by this thread have completed once `drain` fires; the tensor
+            // memory can then be released safely even on the abort path.
+            mma_commit(drain);
+            const unsigned long long t0 = globaltimer_ns();
+            while (!mbar_try_wait(drain, 0)) {
+                if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                    if (e.err) atomicCAS(e.err, 0, ERR_SITE_GEMM_DRAIN);
+                    break;
+                }
+            }
+        }
+    } else {
+        // Epilogue warps 2..5 own TMEM lane groups (warp % 4) * 32.
+        const int eg = warp & 3;
+        const int r_in_tile = eg * 32 + lane;
+        int acc = 0;
+        uint32_t aph = 0;
+        for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+            // Warp-uniform wait: every lane polls the barrier, and the warp leaves together if any
+            // lane gave up, so the .sync.aligned TMEM loads below always run converged.
+            const bool got = mbar_wait(&tfull[acc], aph, abort_flag, e.err, ERR_SITE_GEMM_EPILOGUE);
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
+            const int64_t row = (t / n_tiles) * kBM + r_in_tile;
+            const int64_t ncol0 = (t % n_tiles) * BN;
+            const bool row_ok = row < e.M;
+            const int64_t orow = e.rm_g > 0 ? (row / e.rm_g) * e.rm_G + row % e.rm_g + e.rm_off : row;
+            const uint32_t tbase = tmem_base + ((uint32_t)(eg * 32) << 16) + (uint32_t)(acc * BN);
+            if (e.rope_cos != nullptr) {
+                // 64-column chunks: one head; rotate-half pairs (i, i + 32) of columns < rope_cols.
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 64) {
+                    const int64_t col0 = ncol0 + c;
+                    if (col0 >= e.N) break;
+                    float lo[32], hi[32];
+                    tmem_ld32(tbase + c, lo);
+                    tmem_ld32(tbase + c + 32, hi);
+                    tmem_wait_ld();
+                    if (col0 < e.rope_cols && row_ok) {
+                        const int64_t pidx = e.rope_p1 > 0 ? (row / e.rope_p1) * e.rope_p2 + row % e.rope_p2 : row % e.rope_p2;
+                        const float4 *cs = reinterpret_cast<const float4 *>(e.rope_cos + pidx * 32);
+                        const float4 *sn = reinterpret_cast<const float4 *>(e.rope_sin + pidx * 32);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 c4 = __ldg(cs + q), s4 = __ldg(sn + q);
+                            const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float x1 = lo[4 * q + j], x2 = hi[4 * q + j];
+                                lo[4 * q + j] = x1 * cc[j] - x2 * ss[j];
+                                hi[4 * q + j] = x2 * cc[j] + x1 * ss[j];
+                            }
+                        }
+                    }
+                    const int64_t rem0 = e.N - col0;
+                    const int nv0 = rem0 < 32 ? (int)rem0 : 32;
+                    const int64_t rem1 = e.N - col0 - 32;
+                    const int nv1 = rem1 <= 0 ? 0 : (rem1 < 32 ? (int)rem1 : 32);
+                    bias_act(e, col0, nv0, lo);
+                    if (nv1 > 0) bias_act(e, col0 + 32, nv1, hi);
+                    if (row_ok) {
+                        store_chunk(e, orow, col0, nv0, lo);
+                        if (nv1 > 0) store_chunk(e, orow, col0 + 32, nv1, hi);
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    const int64_t col0 = ncol0 + c;
+                    if (col0 >= e.N) break;
+                    float v[32];
+                    tmem_ld32(tbase + c, v);
+                    tmem_wait_ld();
+                    const int64_t rem = e.N - col0;
+                    const int nv = rem < 32 ? (int)rem : 32;
+                    bias_act(e, col0, nv, v);
+                    if (row_ok) store_chunk(e, orow, col0, nv, v);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                aph ^= 1u;
+            }
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// ---- host side ------------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+int g_num_sms[64] = {0};
+
+bool load_encode() {
+    std::call_once(g_encode_once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode != nullptr;
+}
+
+Status make_tmap(CUtensorMap *map, const void *base, bool f32, int64_t inner, int64_t outer, int64_t ld,
+                 uint32_t box_inner, uint32_t box_outer) {
+    if (!load_encode()) return Status::fail(TSFM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const int esz = f32 ? 4 : 2;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * esz) & 15))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: operand base and row stride must be 16-byte aligned");
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                          const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return Status::fail(TSFM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return Status::ok();
+}
+
+int sm_count() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (g_num_sms[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        g_num_sms[dev] = n > 0 ? n : 148;
+    }
+    return g_num_sms[dev];
+}
+
+template <typename T, int BN>
+Status launch_t(const LinearCall &c, cudaStream_t stream) {
+    using C = TileCfg<BN>;
+    constexpr bool F32 = sizeof(T) == 4;
+    constexpr int BK = 128 / (int)sizeof(T);
+    CUtensorMap ta, tb;
+    Status s = make_tmap(&ta, c.x, F32, c.K, c.M, c.ldx, BK, kBM);
+    if (!s) return s;
+    s = make_tmap(&tb, c.w, F32, c.K, c.N, c.ldw, BK, BN);
+    if (!s) return s;
+    cudaError_t ce = cudaFuncSetAttribute(linear_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (ce != cudaSuccess) return Status::cuda(ce, "linear: set shared memory");
+    Epi e;
+    e.M = c.M;
+    e.N = c.N;
+    e.K = c.K;
+    e.out = c.y;
+    e.ldo = c.ldy;
+    e.bias = c.bias;
+    e.act = c.act;
+    e.out_mode = c.out_mode;
+    e.rm_g = c.rm_g;
+    e.rm_G = c.rm_G;
+    e.rm_off = c.rm_off;
+    e.rope_cos = c.rope_cos;
+    e.rope_sin = c.rope_sin;
+    e.rope_cols = c.rope_cols;
+    e.rope_p1 = c.rope_p1;
+    e.rope_p2 = c.rope_p2;
+    e.err = c.err;
+    const int64_t tiles = ((c.M + kBM - 1) / kBM) * ((c.N + BN - 1) / BN);
+    const int grid = (int)std::min<int64_t>(tiles, sm_count());
+    linear_tc_kernel<T, BN><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, e);
+    ce = cudaGetLastError();
+    if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch");
+    return Status::ok();
+}
+
+}  // namespace
+
+int num_sms() { return sm_count(); }
+
+Status launch_linear(const LinearCall &c, cudaStream_t stream) {
+    if (c.M <= 0 || c.N <= 0 || c.K <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: empty product");
+    if (c.M > INT32_MAX || c.N > INT32_MAX || c.K > INT32_MAX)
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: dimension exceeds the TMA coordinate range");
+    if (c.out_mode < 0 || c.out_mode > 3) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode");
+    if (c.rope_cos && (c.out_mode == 2 || c.rope_cols % 64)) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad rope");
+    const bool small_n = c.N <= 128;
+    if (c.f32) return small_n ? launch_t<float, 128>(c, stream) : launch_t<float, 256>(c, stream);
+    return small_n ? launch_t<__nv_bfloat16, 128>(c, stream) : launch_t<__nv_bfloat16, 256>(c, stream);
+}
+
+}  // namespace tsfm

@@ -1,0 +1,242 @@
+#include "runtime.h"
+
+#include <cstdarg>
+#include <cstring>
+
+namespace tsfm {
+
+std::string strf(const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    return buf;
+}
+
+Status DevBuf::alloc(size_t n) {
+    reset();
+    if (n == 0) return Status::ok();
+    cudaError_t e = cudaMalloc(&p, n);
+    if (e != cudaSuccess) {
+        p = nullptr;
+        return Status::cuda(e, strf("cudaMalloc(%zu)", n));
+    }
+    bytes = n;
+    return Status::ok();
+}
+
+Status PinnedBuf::ensure(size_t n) {
+    if (n <= bytes) return Status::ok();
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    bytes = 0;
+    cudaError_t e = cudaMallocHost(&p, n);
+    if (e != cudaSuccess) {
+        p = nullptr;
+        return Status::cuda(e, strf("cudaMallocHost(%zu)", n));
+    }
+    bytes = n;
+    return Status::ok();
+}
+
+Status Arena::reserve(size_t bytes) {
+    used = 0;
+    if (bytes <= buf.bytes) return Status::ok();
+    return buf.alloc(bytes);
+}
+
+const char *kclass_name(int c) {
+    static const char *names[6] = {"gemm", "attention", "rmsnorm", "patch", "head", "other"};
+    return c >= 0 && c < 6 ? names[c] : "other";
+}
+
+Profiler::~Profiler() {
+    for (auto &r : pending) {
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    for (auto e : pool) cudaEventDestroy(e);
+}
+
+cudaEvent_t Profiler::take() {
+    if (!pool.empty()) {
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+void Profiler::collect() {
+    for (auto &r : pending) {
+        float t = 0.0f;
+        if (cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess) ms[r.cls] += t;
+        pool.push_back(r.a);
+        pool.push_back(r.b);
+    }
+    pending.clear();
+}
+
+LaunchScope::LaunchScope(Replica &rep, cudaStream_t st, int c, double w) : r(rep), cls(c), work(w), s(st) {
+    r.prof.launches[cls] += 1;
+    r.prof.work[cls] += w;
+    r.prof.cur_launches += 1;
+    if (r.prof.enabled) {
+        a = r.prof.take();
+        b = r.prof.take();
+        cudaEventRecord(a, s);
+    }
+}
+
+LaunchScope::~LaunchScope() {
+    if (a) {
+        cudaEventRecord(b, s);
+        r.prof.pending.push_back({cls, work, a, b});
+    }
+}
+
+Replica::~Replica() {
+    if (stream) {
+        cudaSetDevice(device);
+        cudaStreamDestroy(stream);
+    }
+}
+
+TensorTable::TensorTable(const tsfm_tensor *t, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        if (t[i].name) by_name[t[i].name] = &t[i];
+}
+
+static float half_bits_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000) << 16;
+    uint32_t exp = (h >> 10) & 0x1f, mant = h & 0x3ff, bits;
+    if (exp == 0) {
+        if (mant == 0) {
+            bits = sign;
+        } else {
+            int e = -1;
+            do {
+                ++e;
+                mant <<= 1;
+            } while ((mant & 0x400) == 0);
+            mant &= 0x3ff;
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | (mant << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7f800000u | (mant << 13);
+    } else {
+        bits = sign | ((exp + 112) << 23) | (mant << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+Status TensorTable::check(const std::string &name, size_t numel) const {
+    auto it = by_name.find(name);
+    if (it == by_name.end()) return Status::fail(TSFM_ERR_MISSING_TENSOR, "missing tensor: " + name);
+    const tsfm_tensor *t = it->second;
+    if (t->dtype != TSFM_DTYPE_F32 && t->dtype != TSFM_DTYPE_F16 && t->dtype != TSFM_DTYPE_BF16)
+        return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "tensor " + name + " has unsupported dtype");
+    if (t->numel != numel)
+        return Status::fail(TSFM_ERR_SHAPE_MISMATCH, strf("tensor %s: expected %zu elements, file has %llu",
+                                                          name.c_str(), numel, (unsigned long long)t->numel));
+    if (!t->data && numel) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "tensor " + name + " has no data");
+    return Status::ok();
+}
+
+Status TensorTable::get(const std::string &name, size_t numel, std::vector<float> &out) const {
+    auto it = by_name.find(name);
+    if (it == by_name.end()) return Status::fail(TSFM_ERR_MISSING_TENSOR, "missing tensor: " + name);
+    const tsfm_tensor *t = it->second;
+    if (t->dtype != TSFM_DTYPE_F32 && t->dtype != TSFM_DTYPE_F16 && t->dtype != TSFM_DTYPE_BF16)
+        return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "tensor " + name + " has unsupported dtype");
+    if (t->numel != numel)
+        return Status::fail(TSFM_ERR_SHAPE_MISMATCH, strf("tensor %s: expected %zu elements, file has %llu",
+                                                          name.c_str(), numel, (unsigned long long)t->numel));
+    if (!t->data && numel) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "tensor " + name + " has no data");
+    out.resize(numel);
+    if (t->dtype == TSFM_DTYPE_F32) {
+        std::memcpy(out.data(), t->data, numel * 4);
+    } else {
+        const uint16_t *s = static_cast<const uint16_t *>(t->data);
+        for (size_t i = 0; i < numel; ++i) {
+            if (t->dtype == TSFM_DTYPE_BF16) {
+                const uint32_t bits = (uint32_t)s[i] << 16;
+                std::memcpy(&out[i], &bits, 4);
+            } else {
+                out[i] = half_bits_to_float(s[i]);
+            }
+        }
+    }
+    return Status::ok();
+}
+
+static uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);  // quiet NaN
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+static float f32_to_tf32_rna(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7f800000u) != 0x7f800000u) {
+        u += 0x1000u;
+        u &= ~0x1fffu;
+    }
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
+Status upload_f32(Replica &r, const std::vector<float> &h, float **out) {
+    DevBuf b;
+    TSFM_TRY(b.alloc(h.size() * 4));
+    TSFM_CUDA(cudaMemcpy(b.p, h.data(), h.size() * 4, cudaMemcpyHostToDevice), "upload");
+    *out = static_cast<float *>(b.p);
+    r.weights.push_back(std::move(b));
+    return Status::ok();
+}
+
+Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, bool f32, DLin &dst) {
+    DevBuf b;
+    dst.out = out;
+    dst.in = in;
+    dst.f32 = f32;
+    if (f32) {
+        std::vector<float> t(w.size());
+        for (size_t i = 0; i < w.size(); ++i) t[i] = f32_to_tf32_rna(w[i]);
+        TSFM_TRY(b.alloc(t.size() * 4));
+        TSFM_CUDA(cudaMemcpy(b.p, t.data(), t.size() * 4, cudaMemcpyHostToDevice), "upload weight");
+    } else {
+        std::vector<uint16_t> t(w.size());
+        for (size_t i = 0; i < w.size(); ++i) t[i] = f32_to_bf16_rne(w[i]);
+        TSFM_TRY(b.alloc(t.size() * 2));
+        TSFM_CUDA(cudaMemcpy(b.p, t.data(), t.size() * 2, cudaMemcpyHostToDevice), "upload weight");
+    }
+    dst.w = b.p;
+    r.weights.push_back(std::move(b));
+    return Status::ok();
+}
+
+Status upload_bias(Replica &r, const std::vector<float> &b, DLin &dst) { return upload_f32(r, b, &dst.b); }
+
+Status check_device_error(Replica &r) {
+    int code = 0;
+    TSFM_CUDA(cudaMemcpy(&code, r.err.p, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+    if (code != 0) {
+        const int zero = 0;
+        cudaMemcpy(r.err.p, &zero, sizeof(int), cudaMemcpyHostToDevice);
+        return Status::fail(TSFM_ERR_DEVICE_TIMEOUT,
+                            strf("a kernel's bounded wait gave up (site 0x%04x) on device %d", code, r.device));
+    }
+    return Status::ok();
+}
+
+}  // namespace tsfm

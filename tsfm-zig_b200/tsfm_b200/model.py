@@ -1,0 +1,116 @@
+"""Model: a loaded checkpoint on one or more GPUs, driven through the C ABI.
+
+Mirrors the reference's per-family entry points: `forecast_chronos2` is
+chronos2/forecaster.zig:14-22, `forecast_bolt` chronos_bolt/forecaster.zig:22,
+`forecast_timestral` timestral/forecaster.zig:57-69. Inputs and outputs are numpy arrays in host
+memory (pinned or pageable); the *_device variants take raw device pointers.
+"""
+import ctypes
+
+import numpy as np
+
+from . import config as config_mod
+from ._native import COMPUTE, DTYPE, Tensor, check, lib
+
+_NP_DTYPE = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16", np.dtype(np.uint16): "BF16"}
+
+
+def tensor_table(tensors):
+    """(ctypes array of tsfm_tensor, keep-alive list) over a name -> numpy array mapping.
+    uint16 arrays are read as raw bfloat16 bits."""
+    keep = []
+    arr = (Tensor * len(tensors))()
+    for i, name in enumerate(sorted(tensors)):
+        a = np.ascontiguousarray(tensors[name])
+        if a.dtype not in _NP_DTYPE:
+            raise TypeError(f"tensor {name}: unsupported dtype {a.dtype}")
+        nb = name.encode()
+        keep += [a, nb]
+        arr[i].name = nb
+        arr[i].data = a.ctypes.data
+        arr[i].dtype = DTYPE[_NP_DTYPE[a.dtype]]
+        arr[i].numel = a.size
+    return arr, keep
+
+
+class Model:
+    def __init__(self, cfg, tensors, devices=(0,), compute="bf16"):
+        self.parsed = config_mod.parse(cfg)
+        self.family = self.parsed.family
+        self.cfg = cfg
+        table, keep = tensor_table(tensors)
+        devs = (ctypes.c_int32 * len(devices))(*devices)
+        h = ctypes.c_void_p()
+        check(lib.tsfm_model_create(ctypes.byref(self.parsed.struct), table, len(tensors), COMPUTE[compute], devs,
+                                    len(devices), ctypes.byref(h)))
+        del keep
+        self._h = h
+        self.devices = tuple(devices)
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def num_quantiles(self):
+        return self.parsed.struct.num_quantiles
+
+    @property
+    def quantiles(self):
+        return self.parsed.quantiles
+
+    def close(self):
+        if self._h:
+            lib.tsfm_model_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def weight_bytes(self):
+        v = ctypes.c_uint64()
+        check(lib.tsfm_model_weight_bytes(self._h, ctypes.byref(v)))
+        return v.value
+
+    # -- Chronos-2 / Chronos-Bolt ---------------------------------------------------------------
+    def _univariate(self, fn, inputs, horizon, out=None):
+        x = np.ascontiguousarray(inputs, dtype=np.float32)
+        if x.ndim != 2:
+            raise ValueError("inputs must be (series, steps)")
+        b, t = x.shape
+        if out is None:
+            out = np.empty((b, horizon, self.num_quantiles), np.float32)
+        check(fn(self._h, x.ctypes.data, b, t, horizon, out.ctypes.data))
+        return out
+
+    def forecast_chronos2(self, inputs, horizon, out=None):
+        return self._univariate(lib.tsfm_forecast_chronos2, inputs, horizon, out)
+
+    def forecast_bolt(self, inputs, horizon, out=None):
+        return self._univariate(lib.tsfm_forecast_bolt, inputs, horizon, out)
+
+    def forecast_chronos2_device(self, in_ptr, b, t, horizon, out_ptr, stream=0):
+        check(lib.tsfm_forecast_chronos2_device(self._h, in_ptr, b, t, horizon, out_ptr, stream or None))
+
+    def forecast_bolt_device(self, in_ptr, b, t, horizon, out_ptr, stream=0):
+        check(lib.tsfm_forecast_bolt_device(self._h, in_ptr, b, t, horizon, out_ptr, stream or None))
+
+    # -- profiling ------------------------------------------------------------------------------
+    def profile(self, enable=True):
+        check(lib.tsfm_profile_enable(self._h, int(enable)))
+
+    def profile_reset(self):
+        check(lib.tsfm_profile_reset(self._h))
+
+    def profile_read(self, cls):
+        n, ms, work = ctypes.c_uint64(), ctypes.c_double(), ctypes.c_double()
+        check(lib.tsfm_profile_read(self._h, cls.encode(), ctypes.byref(n), ctypes.byref(ms), ctypes.byref(work)))
+        return {"launches": n.value, "ms": ms.value, "work": work.value}
+
+    def last_launch_count(self):
+        n = ctypes.c_uint64()
+        check(lib.tsfm_last_launch_count(self._h, ctypes.byref(n)))
+        return n.value
