@@ -278,7 +278,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "series/s", "n_gpus": world, "steps": a.steps,
             "warmup": max(3, a.warmup), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded sine + random walk + noise, 5% NaN; "
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded sine + random walk + noise, 5% NaN; "
                                                              "random-init N(0,0.02) weights)",
             "config": {"workload": "chronos2-ctx8192-h1024", "d_model": 768, "layers": 12, "heads": 12, "d_ff": 3072,
                        "patch": 16, "quantiles": 21, "series_per_gpu": b, "global_batch": b * world,

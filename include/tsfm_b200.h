@@ -72,10 +72,13 @@ typedef enum tsfm_dtype {
     TSFM_DTYPE_BF16 = 2
 } tsfm_dtype;
 
-/* Operand type of the tensor-core contractions; accumulation is always FP32. */
+/* Operand type of the tensor-core contractions; accumulation and the residual stream are always
+ * FP32. F16 and BF16 run at the same tensor-core rate; F16 keeps 3 more mantissa bits (the
+ * precision of TF32), BF16 the FP32 exponent range. TF32 is reserved. */
 typedef enum tsfm_compute {
     TSFM_COMPUTE_BF16 = 0,
-    TSFM_COMPUTE_TF32 = 1
+    TSFM_COMPUTE_TF32 = 1,
+    TSFM_COMPUTE_F16 = 2
 } tsfm_compute;
 
 /* Timestral layer kinds, the entries of `block_schedule` (timestral/config.zig:94-100). */
@@ -244,8 +247,9 @@ int tsfm_sgemm_nn(int m, int n, int k, const float *A, int lda,               /*
  * the kernel parity tests). All return after enqueueing on `stream`.
  *
  * tsfm_kernel_linear: y[M, N] (+)= act(x[M, K] · W[N, K]^T + bias) on the tensor cores.
- *   x_dtype/w_dtype: TSFM_DTYPE_BF16 (kind::f16) or TSFM_DTYPE_F32 (kind::tf32); both equal.
- *   out_mode: 0 = store bf16, 1 = store f32, 2 = accumulate into f32 (y += result).
+ *   x_dtype/w_dtype: TSFM_DTYPE_BF16 or TSFM_DTYPE_F16 (kind::f16), or TSFM_DTYPE_F32 (read as
+ *   TF32, kind::tf32); both equal.
+ *   out_mode: 0 = store in the 16-bit operand type, 1 = store f32, 2 = accumulate into f32.
  *   act: 0 none, 1 relu. bias may be null. Replaces nn.linear (core/nn.zig:270-293). */
 int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_t w_dtype,
                            const float *bias, void *y, int32_t out_mode, int32_t act,
@@ -262,7 +266,7 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
 int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64_t ld_qkv,
                               void *o, int64_t ld_o, const uint8_t *key_valid,
                               const float *rel_bias, int32_t groups, int32_t heads, int32_t n,
-                              float scale, int32_t mask_mode, void *stream);
+                              float scale, int32_t mask_mode, int32_t dtype, void *stream);
 
 /* tsfm_kernel_rmsnorm: out[r, :] = x[r, :] / sqrt(mean(x^2) + eps) * scale, x f32, out bf16 or
  * f32 (out_dtype). Replaces nn.rmsNorm (core/nn.zig:367-396). */

@@ -17,6 +17,8 @@
 #include "kernels.h"
 #include "ptx.cuh"
 
+#include <cuda_fp16.h>
+
 namespace tsfm {
 
 namespace {
@@ -25,13 +27,14 @@ constexpr int BQ = 64, BKV = 64, HD = 64;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnP {
-    const __nv_bfloat16 *q, *k, *v;
+    const uint16_t *q, *k, *v;  // 16-bit elements (BF16 or FP16)
     int64_t ld;
-    __nv_bfloat16 *o;
+    uint16_t *o;
     int64_t ldo;
     const uint8_t *key_valid;
     int64_t kvs;
     const float *rel;
+    int64_t rel_stride, rel_center;
     int n, heads;
     float scale_log2;
     int ne, l;
@@ -62,24 +65,39 @@ __device__ __forceinline__ void ldsm_x4_t(const void *p, uint32_t &r0, uint32_t 
                  : "r"(smem_u32(p)));
 }
 
+template <bool F16>
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    if constexpr (F16) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t *>(&v);
+template <bool F16>
+__device__ __forceinline__ uint32_t pack16(float lo, float hi) {
+    if constexpr (F16) {
+        __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&v);
+    } else {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&v);
+    }
 }
 
-template <int MODE>
+template <int MODE, bool F16>
 __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
-    __shared__ __align__(128) __nv_bfloat16 sQ[BQ * HD];
-    __shared__ __align__(128) __nv_bfloat16 sK[2][BKV * HD];
-    __shared__ __align__(128) __nv_bfloat16 sV[2][BKV * HD];
+    __shared__ __align__(128) uint16_t sQ[BQ * HD];
+    __shared__ __align__(128) uint16_t sK[2][BKV * HD];
+    __shared__ __align__(128) uint16_t sV[2][BKV * HD];
     __shared__ uint8_t sValid[2][BKV];
 
     const int qb = blockIdx.x, h = blockIdx.y, g = blockIdx.z;
@@ -106,7 +124,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
     for (int c = tid; c < BQ * 8; c += 128) {
         const int r = c >> 3, ch = c & 7;
         const int tok = q0 + r;
-        const __nv_bfloat16 *src = p.q + (row0 + min(tok, n - 1)) * p.ld + h * HD + ch * 8;
+        const uint16_t *src = p.q + (row0 + min(tok, n - 1)) * p.ld + h * HD + ch * 8;
         cp_async16(&sQ[swz(r, ch * 8)], src, tok < n);
     }
     auto load_kv = [&](int kt, int buf) {
@@ -166,8 +184,8 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
                 const int dim = kk * 16 + ((lane >> 3) & 1) * 8;
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(&sK[buf][swz(key, dim)], b0, b1, b2, b3);
-                mma16816(s[2 * np], qf[kk], b0, b1);
-                mma16816(s[2 * np + 1], qf[kk], b2, b3);
+                mma16816<F16>(s[2 * np], qf[kk], b0, b1);
+                mma16816<F16>(s[2 * np + 1], qf[kk], b2, b3);
             }
         }
         // Scale, bias, mask.
@@ -188,7 +206,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
                         x = 0.0f;
                     } else {
                         allowed = valid;
-                        if (p.rel && allowed && i < n) x += __ldg(p.rel + (int64_t)h * (2 * n - 1) + (j - i) + n - 1) * kLog2e;
+                        if (p.rel && allowed && i < n) x += __ldg(p.rel + (int64_t)h * p.rel_stride + (j - i) + p.rel_center) * kLog2e;
                     }
                 } else {
                     if (i < p.ne)
@@ -229,18 +247,18 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             uint32_t a[4];
-            a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-            a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-            a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-            a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+            a[0] = pack16<F16>(s[2 * kk][0], s[2 * kk][1]);
+            a[1] = pack16<F16>(s[2 * kk][2], s[2 * kk][3]);
+            a[2] = pack16<F16>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            a[3] = pack16<F16>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
             for (int dp = 0; dp < 4; ++dp) {
                 const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
                 const int dim = dp * 16 + (lane >> 4) * 8;
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_t(&sV[buf][swz(key, dim)], b0, b1, b2, b3);
-                mma16816(o[2 * dp], a, b0, b1);
-                mma16816(o[2 * dp + 1], a, b2, b3);
+                mma16816<F16>(o[2 * dp], a, b0, b1);
+                mma16816<F16>(o[2 * dp + 1], a, b2, b3);
             }
         }
         __syncthreads();
@@ -257,9 +275,9 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
     for (int nt = 0; nt < 8; ++nt) {
         const int col = h * HD + nt * 8 + (lane & 3) * 2;
         if (qi0 < n)
-            *reinterpret_cast<uint32_t *>(p.o + (row0 + qi0) * p.ldo + col) = pack_bf16(o[nt][0] * inv0, o[nt][1] * inv0);
+            *reinterpret_cast<uint32_t *>(p.o + (row0 + qi0) * p.ldo + col) = pack16<F16>(o[nt][0] * inv0, o[nt][1] * inv0);
         if (qi1 < n)
-            *reinterpret_cast<uint32_t *>(p.o + (row0 + qi1) * p.ldo + col) = pack_bf16(o[nt][2] * inv1, o[nt][3] * inv1);
+            *reinterpret_cast<uint32_t *>(p.o + (row0 + qi1) * p.ldo + col) = pack16<F16>(o[nt][2] * inv1, o[nt][3] * inv1);
     }
 }
 
@@ -273,15 +291,17 @@ Status launch_attention(const AttentionCall &c, cudaStream_t stream) {
     if (c.groups > 65535 || c.heads > 65535)
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: too many groups for one launch");
     AttnP p;
-    p.q = c.q;
-    p.k = c.k;
-    p.v = c.v;
+    p.q = static_cast<const uint16_t *>(c.q);
+    p.k = static_cast<const uint16_t *>(c.k);
+    p.v = static_cast<const uint16_t *>(c.v);
     p.ld = c.ld_qkv;
-    p.o = c.o;
+    p.o = static_cast<uint16_t *>(c.o);
     p.ldo = c.ld_o;
     p.key_valid = c.key_valid;
     p.kvs = c.kv_stride > 0 ? c.kv_stride : c.n;
     p.rel = c.rel_bias;
+    p.rel_stride = c.rel_stride > 0 ? c.rel_stride : 2 * (int64_t)c.n - 1;
+    p.rel_center = c.rel_center >= 0 ? c.rel_center : (int64_t)c.n - 1;
     p.n = c.n;
     p.heads = c.heads;
     p.scale_log2 = c.scale * kLog2e;
@@ -290,10 +310,12 @@ Status launch_attention(const AttentionCall &c, cudaStream_t stream) {
     p.bidir = c.group_bidir;
     p.bidir_all = c.mask_mode == 2;
     dim3 grid((c.n + BQ - 1) / BQ, c.heads, c.groups);
+    const bool f16 = c.dtype == E_F16;
+    if (c.dtype != E_F16 && c.dtype != E_BF16) return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "attention: dtype");
     if (c.mask_mode == 0)
-        attn_kernel<0><<<grid, 128, 0, stream>>>(p);
+        f16 ? attn_kernel<0, true><<<grid, 128, 0, stream>>>(p) : attn_kernel<0, false><<<grid, 128, 0, stream>>>(p);
     else
-        attn_kernel<1><<<grid, 128, 0, stream>>>(p);
+        f16 ? attn_kernel<1, true><<<grid, 128, 0, stream>>>(p) : attn_kernel<1, false><<<grid, 128, 0, stream>>>(p);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return Status::cuda(e, "attention: launch");
     return Status::ok();

@@ -97,48 +97,49 @@ Status for_replicas(size_t n, F &&fn) {
     return Status::ok();
 }
 
-// Forecast `nb` series of one replica from host memory, in chunks that fit the workspace.
-template <class Fwd, class Ws>
-Status replica_forecast(Replica &r, const float *in, int64_t nb, int64_t t, int64_t out_per_series, float *out,
-                        Fwd &&fwd, Ws &&ws_bytes) {
+// Forecast `nb` series of one replica from host memory: inputs staged through pinned memory
+// (unless the caller's buffer is pinned already), the family's device forecast, results back.
+template <class Fwd>
+Status replica_forecast(Replica &r, const void *in, size_t in_bytes, size_t out_bytes, void *out, Fwd &&fwd) {
     std::lock_guard<std::mutex> lk(r.mu);
     TSFM_CUDA(cudaSetDevice(r.device), "cudaSetDevice");
     r.prof.cur_launches = 0;
-    size_t free_b = 0, total_b = 0;
-    TSFM_CUDA(cudaMemGetInfo(&free_b, &total_b), "cudaMemGetInfo");
-    const double budget = 0.6 * (double)(free_b + r.ws.buf.bytes);
-    const double per = (double)ws_bytes(1) + (double)(t + out_per_series) * 4.0;
-    int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(nb, (int64_t)(budget / std::max(per, 1.0))));
-    // Keep chunks balanced: equal sizes rather than a long tail.
-    const int64_t nchunks = (nb + chunk - 1) / chunk;
-    chunk = (nb + nchunks - 1) / nchunks;
-    const size_t in_bytes = (size_t)chunk * t * 4, out_bytes = (size_t)chunk * out_per_series * 4;
-    TSFM_TRY(r.ws.reserve(ws_bytes(chunk) + Arena::span(in_bytes) + Arena::span(out_bytes) + 4096));
+    const size_t in_span = Arena::span(in_bytes);
+    if (r.io.bytes < in_span + out_bytes) TSFM_TRY(r.io.alloc(in_span + out_bytes));
+    float *d_in = static_cast<float *>(r.io.p);
+    float *d_out = reinterpret_cast<float *>(static_cast<char *>(r.io.p) + in_span);
     const bool pin_in = is_pinned(in), pin_out = is_pinned(out);
-    if (!pin_in) TSFM_TRY(r.pin_in.ensure(in_bytes));
-    if (!pin_out) TSFM_TRY(r.pin_out.ensure(out_bytes));
-    // The I/O buffers sit at the top of the arena, above what the forward takes.
-    char *top = static_cast<char *>(r.ws.buf.p) + r.ws.buf.bytes;
-    float *d_out = reinterpret_cast<float *>(top - Arena::span(out_bytes));
-    float *d_in = reinterpret_cast<float *>(reinterpret_cast<char *>(d_out) - Arena::span(in_bytes));
-    for (int64_t s0 = 0; s0 < nb; s0 += chunk) {
-        const int64_t n = std::min(chunk, nb - s0);
-        const float *src = in + s0 * t;
-        if (!pin_in) {
-            std::memcpy(r.pin_in.p, src, (size_t)n * t * 4);
-            src = static_cast<const float *>(r.pin_in.p);
-        }
-        TSFM_CUDA(cudaMemcpyAsync(d_in, src, (size_t)n * t * 4, cudaMemcpyHostToDevice, r.stream), "copy inputs");
-        TSFM_TRY(fwd(d_in, n, d_out, r.stream));
-        if (r.ws.used > (size_t)(reinterpret_cast<char *>(d_in) - static_cast<char *>(r.ws.buf.p)))
-            return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "workspace overlaps the I/O buffers");
-        float *dst = out + s0 * out_per_series;
-        void *stage = pin_out ? static_cast<void *>(dst) : r.pin_out.p;
-        TSFM_CUDA(cudaMemcpyAsync(stage, d_out, (size_t)n * out_per_series * 4, cudaMemcpyDeviceToHost, r.stream),
-                  "copy results");
-        TSFM_CUDA(cudaStreamSynchronize(r.stream), "forecast");
-        if (!pin_out) std::memcpy(dst, r.pin_out.p, (size_t)n * out_per_series * 4);
+    const void *src = in;
+    if (!pin_in) {
+        TSFM_TRY(r.pin_in.ensure(in_bytes));
+        std::memcpy(r.pin_in.p, in, in_bytes);
+        src = r.pin_in.p;
     }
+    TSFM_CUDA(cudaMemcpyAsync(d_in, src, in_bytes, cudaMemcpyHostToDevice, r.stream), "copy inputs");
+    TSFM_TRY(fwd(d_in, d_out, r.stream));
+    void *stage = out;
+    if (!pin_out) {
+        TSFM_TRY(r.pin_out.ensure(out_bytes));
+        stage = r.pin_out.p;
+    }
+    TSFM_CUDA(cudaMemcpyAsync(stage, d_out, out_bytes, cudaMemcpyDeviceToHost, r.stream), "copy results");
+    TSFM_CUDA(cudaStreamSynchronize(r.stream), "forecast");
+    if (!pin_out) std::memcpy(out, r.pin_out.p, out_bytes);
+    TSFM_TRY(check_device_error(r));
+    r.prof.collect();
+    r.prof.last_forecast_launches = r.prof.cur_launches;
+    return Status::ok();
+}
+
+// The same on device pointers (first replica, caller's stream).
+template <class Fwd>
+Status replica_forecast_device(Replica &r, cudaStream_t stream, Fwd &&fwd) {
+    std::lock_guard<std::mutex> lk(r.mu);
+    TSFM_CUDA(cudaSetDevice(r.device), "cudaSetDevice");
+    cudaStream_t s = stream ? stream : r.stream;
+    r.prof.cur_launches = 0;
+    TSFM_TRY(fwd(s));
+    TSFM_CUDA(cudaStreamSynchronize(s), "forecast");
     TSFM_TRY(check_device_error(r));
     r.prof.collect();
     r.prof.last_forecast_launches = r.prof.cur_launches;
@@ -205,8 +206,9 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
     return guarded([&]() -> Status {
         if (!config || !out || (!tensors && n_tensors)) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null argument");
         *out = nullptr;
-        if (compute != TSFM_COMPUTE_BF16)
-            return Status::fail(TSFM_ERR_UNSUPPORTED, "compute type: only TSFM_COMPUTE_BF16 is implemented");
+        if (compute != TSFM_COMPUTE_BF16 && compute != TSFM_COMPUTE_F16)
+            return Status::fail(TSFM_ERR_UNSUPPORTED, "compute type: TSFM_COMPUTE_BF16 and TSFM_COMPUTE_F16 are implemented");
+        const int act = compute == TSFM_COMPUTE_F16 ? E_F16 : E_BF16;
         std::unique_ptr<tsfm_model> m(new tsfm_model());
         m->cfg = *config;
         if (config->num_quantiles > 0 && config->quantiles)
@@ -245,7 +247,7 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
             TSFM_CUDA(cudaMemset(r->err.p, 0, 16), "clear error word");
             if (c.family == TSFM_CHRONOS2) {
                 auto w = std::make_unique<C2Dev>();
-                TSFM_TRY(c2_load(*r, c, table, *w));
+                TSFM_TRY(c2_load(*r, c, table, act, *w));
                 m->c2.push_back(std::move(w));
             }
             if (i == 0)
@@ -285,13 +287,12 @@ int32_t tsfm_forecast_chronos2(tsfm_model *model, const float *inputs, size_t b,
             if (s1 <= s0) return Status::ok();
             Replica &r = *model->reps[i];
             const C2Dev &w = *model->c2[i];
-            const tsfm_config &c = model->cfg;
-            return replica_forecast(
-                r, inputs + s0 * t, s1 - s0, (int64_t)t, (int64_t)horizon * q, out + s0 * horizon * q,
-                [&](const float *d_in, int64_t nb, float *d_out, cudaStream_t s) {
-                    return c2_forward(r, c, w, d_in, nb, (int64_t)t, (int64_t)horizon, d_out, s);
-                },
-                [&](int64_t nb) { return c2_workspace(c, nb, (int64_t)t, (int64_t)horizon); });
+            const int64_t nb = s1 - s0;
+            return replica_forecast(r, inputs + s0 * t, (size_t)nb * t * 4, (size_t)nb * horizon * q * 4,
+                                    out + s0 * horizon * q, [&](const float *d_in, float *d_out, cudaStream_t s) {
+                                        return c2_forecast(r, model->cfg, w, d_in, nb, (int64_t)t, (int64_t)horizon,
+                                                           d_out, s);
+                                    });
         });
     });
 }
@@ -302,30 +303,9 @@ int32_t tsfm_forecast_chronos2_device(tsfm_model *model, const float *inputs, si
         TSFM_TRY(check_model(model, TSFM_CHRONOS2));
         TSFM_TRY(c2_args(model, inputs, b, t, horizon, out));
         Replica &r = *model->reps[0];
-        const C2Dev &w = *model->c2[0];
-        std::lock_guard<std::mutex> lk(r.mu);
-        TSFM_CUDA(cudaSetDevice(r.device), "cudaSetDevice");
-        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : r.stream;
-        r.prof.cur_launches = 0;
-        size_t free_b = 0, total_b = 0;
-        TSFM_CUDA(cudaMemGetInfo(&free_b, &total_b), "cudaMemGetInfo");
-        const double budget = 0.6 * (double)(free_b + r.ws.buf.bytes);
-        const int64_t q = model->cfg.num_quantiles;
-        int64_t chunk = std::max<int64_t>(
-            1, std::min<int64_t>((int64_t)b, (int64_t)(budget / (double)c2_workspace(model->cfg, 1, t, horizon))));
-        const int64_t nchunks = ((int64_t)b + chunk - 1) / chunk;
-        chunk = ((int64_t)b + nchunks - 1) / nchunks;
-        TSFM_TRY(r.ws.reserve(c2_workspace(model->cfg, chunk, t, horizon)));
-        for (int64_t s0 = 0; s0 < (int64_t)b; s0 += chunk) {
-            const int64_t n = std::min<int64_t>(chunk, (int64_t)b - s0);
-            TSFM_TRY(c2_forward(r, model->cfg, w, inputs + s0 * t, n, (int64_t)t, (int64_t)horizon,
-                                out + s0 * (int64_t)horizon * q, s));
-        }
-        TSFM_CUDA(cudaStreamSynchronize(s), "forecast");
-        TSFM_TRY(check_device_error(r));
-        r.prof.collect();
-        r.prof.last_forecast_launches = r.prof.cur_launches;
-        return Status::ok();
+        return replica_forecast_device(r, static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
+            return c2_forecast(r, model->cfg, *model->c2[0], inputs, (int64_t)b, (int64_t)t, (int64_t)horizon, out, s);
+        });
     });
 }
 
@@ -408,14 +388,18 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
                            int64_t ldy, void *stream) {
     return guarded([&]() -> Status {
         if (!x || !w || !y) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
-        if (x_dtype != w_dtype || (x_dtype != TSFM_DTYPE_BF16 && x_dtype != TSFM_DTYPE_F32))
-            return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "linear: x and w must both be BF16 or both F32");
+        if (x_dtype != w_dtype ||
+            (x_dtype != TSFM_DTYPE_BF16 && x_dtype != TSFM_DTYPE_F16 && x_dtype != TSFM_DTYPE_F32))
+            return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "linear: x and w must both be BF16, F16 or F32");
+        const int elem = x_dtype == TSFM_DTYPE_F32 ? E_F32 : x_dtype == TSFM_DTYPE_F16 ? E_F16 : E_BF16;
+        if (out_mode == 0 && elem == E_F32)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: out_mode 0 stores the 16-bit operand type");
         if (out_mode < 0 || out_mode > 2 || act < 0 || act > 1)
             return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode / act");
         LinearCall c;
         c.x = x;
         c.w = w;
-        c.f32 = x_dtype == TSFM_DTYPE_F32;
+        c.dtype = elem;
         c.M = M;
         c.N = N;
         c.K = K;
@@ -423,7 +407,7 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
         c.ldw = ldw;
         c.y = y;
         c.ldy = ldy;
-        c.out_mode = out_mode;
+        c.out_mode = out_mode == 0 ? out_mode_for(elem) : out_mode == 1 ? OUT_F32 : OUT_F32_ACC;
         c.bias = bias;
         c.act = act;
         c.err = kernel_err_word();
@@ -433,16 +417,16 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
 
 int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64_t ld_qkv, void *o, int64_t ld_o,
                               const uint8_t *key_valid, const float *rel_bias, int32_t groups, int32_t heads, int32_t n,
-                              float scale, int32_t mask_mode, void *stream) {
+                              float scale, int32_t mask_mode, int32_t dtype, void *stream) {
     return guarded([&]() -> Status {
         if (!q || !k || !v || !o) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
         if (mask_mode < 0 || mask_mode > 2) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "bad mask_mode");
         AttentionCall c;
-        c.q = static_cast<const __nv_bfloat16 *>(q);
-        c.k = static_cast<const __nv_bfloat16 *>(k);
-        c.v = static_cast<const __nv_bfloat16 *>(v);
+        c.q = q;
+        c.k = k;
+        c.v = v;
         c.ld_qkv = ld_qkv;
-        c.o = static_cast<__nv_bfloat16 *>(o);
+        c.o = o;
         c.ld_o = ld_o;
         c.key_valid = key_valid;
         c.kv_stride = n;
@@ -452,6 +436,9 @@ int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64
         c.n = n;
         c.scale = scale;
         c.mask_mode = mask_mode;
+        if (dtype != TSFM_DTYPE_BF16 && dtype != TSFM_DTYPE_F16)
+            return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "attention: q/k/v must be BF16 or F16");
+        c.dtype = dtype == TSFM_DTYPE_F16 ? E_F16 : E_BF16;
         c.ne = n;
         c.l = n;
         return launch_attention(c, static_cast<cudaStream_t>(stream));
@@ -466,7 +453,7 @@ int32_t tsfm_kernel_rmsnorm(const float *x, const float *scale, void *out, int32
         c.x = x;
         c.scale = scale;
         c.out = out;
-        c.out_mode = out_dtype == TSFM_DTYPE_BF16 ? 0 : 1;
+        c.out_mode = out_dtype == TSFM_DTYPE_BF16 ? OUT_BF16 : out_dtype == TSFM_DTYPE_F16 ? OUT_F16 : OUT_F32;
         c.rows = rows;
         c.dim = dim;
         c.eps = eps;

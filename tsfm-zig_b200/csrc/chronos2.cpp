@@ -14,73 +14,12 @@
 #include <cstring>
 
 #include "model.h"
+#include "ops.h"
+
+#include <algorithm>
 
 namespace tsfm {
 
-namespace {
-
-std::string layer_name(const char *fmt, int a, int b = 0) { return strf(fmt, a, b); }
-
-Status load_resblock(Replica &r, const TensorTable &t, const std::string &prefix, int64_t in, int64_t hid,
-                     int64_t out, bool bias, bool f32_in, bool f32_hidden, DResBlock &dst) {
-    std::vector<float> w;
-    TSFM_TRY(t.get(prefix + ".hidden_layer.weight", hid * in, w));
-    TSFM_TRY(upload_lin(r, w, hid, in, f32_in, dst.hidden));
-    TSFM_TRY(t.get(prefix + ".output_layer.weight", out * hid, w));
-    TSFM_TRY(upload_lin(r, w, out, hid, f32_hidden, dst.output));
-    TSFM_TRY(t.get(prefix + ".residual_layer.weight", out * in, w));
-    TSFM_TRY(upload_lin(r, w, out, in, f32_in, dst.residual));
-    if (bias) {
-        TSFM_TRY(t.get(prefix + ".hidden_layer.bias", hid, w));
-        TSFM_TRY(upload_bias(r, w, dst.hidden));
-        TSFM_TRY(t.get(prefix + ".output_layer.bias", out, w));
-        TSFM_TRY(upload_bias(r, w, dst.output));
-        TSFM_TRY(t.get(prefix + ".residual_layer.bias", out, w));
-        TSFM_TRY(upload_bias(r, w, dst.residual));
-    }
-    return Status::ok();
-}
-
-Status linear(Replica &r, cudaStream_t s, const DLin &L, const void *x, int64_t M, int64_t ldx, void *y, int64_t ldy,
-              int out_mode, int act, const LinearCall *extra = nullptr) {
-    LinearCall c;
-    if (extra) c = *extra;
-    c.x = x;
-    c.w = L.w;
-    c.f32 = L.f32;
-    c.M = M;
-    c.N = L.out;
-    c.K = L.in;
-    c.ldx = ldx;
-    c.ldw = L.in;
-    c.y = y;
-    c.ldy = ldy;
-    c.out_mode = out_mode;
-    c.bias = L.b;
-    c.act = act;
-    c.err = static_cast<int *>(r.err.p);
-    LaunchScope ls(r, s, K_GEMM, 2.0 * (double)M * (double)L.out * (double)L.in);
-    return launch_linear(c, s);
-}
-
-Status rmsnorm(Replica &r, cudaStream_t s, const float *x, const float *scale, void *out, int out_mode, int64_t rows,
-               int64_t dim, float eps, int64_t g = 0, int64_t G = 0, int64_t off = 0) {
-    RmsNormCall c;
-    c.x = x;
-    c.scale = scale;
-    c.out = out;
-    c.out_mode = out_mode;
-    c.rows = rows;
-    c.dim = dim;
-    c.eps = eps;
-    c.g = g;
-    c.G = G;
-    c.off = off;
-    LaunchScope ls(r, s, K_NORM, (double)rows * dim * (4.0 + (out_mode == 0 ? 2.0 : 4.0)));
-    return launch_rmsnorm(c, s);
-}
-
-}  // namespace
 
 Status c2_validate(const tsfm_config &c) {
     // chronos2/config.zig:44-55
@@ -118,22 +57,39 @@ Status c2_check_tensors(const tsfm_config &c, const TensorTable &t) {
     TSFM_TRY(t.check("shared.weight", 2 * d));
     for (int li = 0; li < c.num_layers; ++li) {
         for (int which = 0; which < 2; ++which) {
-            const std::string p = layer_name("encoder.block.%d.layer.%d.", li, which);
+            const std::string p = strf("encoder.block.%d.layer.%d.", li, which);
             TSFM_TRY(t.check(p + "layer_norm.weight", d));
             for (const char *nm : {"q", "k", "v", "o"}) TSFM_TRY(t.check(p + "self_attention." + nm + ".weight", d * d));
         }
-        TSFM_TRY(t.check(layer_name("encoder.block.%d.layer.2.layer_norm.weight", li), d));
-        TSFM_TRY(t.check(layer_name("encoder.block.%d.layer.2.mlp.wi.weight", li), hid * d));
-        TSFM_TRY(t.check(layer_name("encoder.block.%d.layer.2.mlp.wo.weight", li), d * hid));
+        TSFM_TRY(t.check(strf("encoder.block.%d.layer.2.layer_norm.weight", li), d));
+        TSFM_TRY(t.check(strf("encoder.block.%d.layer.2.mlp.wi.weight", li), hid * d));
+        TSFM_TRY(t.check(strf("encoder.block.%d.layer.2.mlp.wo.weight", li), d * hid));
     }
     return Status::ok();
 }
 
-Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, C2Dev &w) {
+Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, C2Dev &w) {
     const int64_t d = c.d_model, ps = c.patch_size, hid = c.d_ff, q = c.num_quantiles;
-    // The patch features enter a TF32 product (K = 3 * patch); everything else is BF16.
-    TSFM_TRY(load_resblock(r, t, "input_patch_embedding", 3 * ps, hid, d, true, true, false, w.in_embed));
-    TSFM_TRY(load_resblock(r, t, "output_patch_embedding", d, hid, q * ps, true, false, false, w.out_embed));
+    w.act = act;
+    // The patch features enter a TF32 product (K = 3 * patch); every other product takes 16-bit
+    // operands of type `act`.
+    TSFM_TRY(load_resblock(r, t, "input_patch_embedding", 3 * ps, hid, d, true, E_F32, act, w.in_embed));
+    {
+        const std::string p = "output_patch_embedding";
+        std::vector<float> m;
+        TSFM_TRY(t.get(p + ".hidden_layer.weight", hid * d, m));
+        TSFM_TRY(upload_lin3(r, m, hid, d, w.head_hidden));
+        TSFM_TRY(t.get(p + ".hidden_layer.bias", hid, m));
+        TSFM_TRY(upload_bias(r, m, w.head_hidden.hi));
+        TSFM_TRY(t.get(p + ".output_layer.weight", q * ps * hid, m));
+        TSFM_TRY(upload_lin3(r, m, q * ps, hid, w.head_output));
+        TSFM_TRY(t.get(p + ".output_layer.bias", q * ps, m));
+        TSFM_TRY(upload_bias(r, m, w.head_output.hi));
+        TSFM_TRY(t.get(p + ".residual_layer.weight", q * ps * d, m));
+        TSFM_TRY(upload_lin3(r, m, q * ps, d, w.head_residual));
+        TSFM_TRY(t.get(p + ".residual_layer.bias", q * ps, m));
+        TSFM_TRY(upload_bias(r, m, w.head_residual.hi));
+    }
     std::vector<float> v;
     TSFM_TRY(t.get("encoder.final_layer_norm.weight", d, v));
     TSFM_TRY(upload_f32(r, v, &w.final_norm));
@@ -144,7 +100,7 @@ Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, C2Dev &w)
         C2Dev::Layer L;
         std::vector<float> qkv;
         for (int which = 0; which < 2; ++which) {
-            const std::string p = layer_name("encoder.block.%d.layer.%d.", li, which);
+            const std::string p = strf("encoder.block.%d.layer.%d.", li, which);
             TSFM_TRY(t.get(p + "layer_norm.weight", d, v));
             TSFM_TRY(upload_f32(r, v, which == 0 ? &L.time_norm : &L.group_norm));
             if (which == 0) {
@@ -153,26 +109,26 @@ Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, C2Dev &w)
                     TSFM_TRY(t.get(p + "self_attention." + nm + ".weight", d * d, v));
                     qkv.insert(qkv.end(), v.begin(), v.end());
                 }
-                TSFM_TRY(upload_lin(r, qkv, 3 * d, d, false, L.qkv));
+                TSFM_TRY(upload_lin(r, qkv, 3 * d, d, act, L.qkv));
                 TSFM_TRY(t.get(p + "self_attention.o.weight", d * d, v));
-                TSFM_TRY(upload_lin(r, v, d, d, false, L.o));
+                TSFM_TRY(upload_lin(r, v, d, d, act, L.o));
             } else {
                 // Singleton groups: only v and o take part (chronos2/model.zig:265-269); q and k are
                 // still required to exist, as the reference loads them.
                 TSFM_TRY(t.get(p + "self_attention.q.weight", d * d, v));
                 TSFM_TRY(t.get(p + "self_attention.k.weight", d * d, v));
                 TSFM_TRY(t.get(p + "self_attention.v.weight", d * d, v));
-                TSFM_TRY(upload_lin(r, v, d, d, false, L.gv));
+                TSFM_TRY(upload_lin(r, v, d, d, act, L.gv));
                 TSFM_TRY(t.get(p + "self_attention.o.weight", d * d, v));
-                TSFM_TRY(upload_lin(r, v, d, d, false, L.go));
+                TSFM_TRY(upload_lin(r, v, d, d, act, L.go));
             }
         }
-        TSFM_TRY(t.get(layer_name("encoder.block.%d.layer.2.layer_norm.weight", li), d, v));
+        TSFM_TRY(t.get(strf("encoder.block.%d.layer.2.layer_norm.weight", li), d, v));
         TSFM_TRY(upload_f32(r, v, &L.mlp_norm));
-        TSFM_TRY(t.get(layer_name("encoder.block.%d.layer.2.mlp.wi.weight", li), hid * d, v));
-        TSFM_TRY(upload_lin(r, v, hid, d, false, L.wi));
-        TSFM_TRY(t.get(layer_name("encoder.block.%d.layer.2.mlp.wo.weight", li), d * hid, v));
-        TSFM_TRY(upload_lin(r, v, d, hid, false, L.wo));
+        TSFM_TRY(t.get(strf("encoder.block.%d.layer.2.mlp.wi.weight", li), hid * d, v));
+        TSFM_TRY(upload_lin(r, v, hid, d, act, L.wi));
+        TSFM_TRY(t.get(strf("encoder.block.%d.layer.2.mlp.wo.weight", li), d * hid, v));
+        TSFM_TRY(upload_lin(r, v, d, hid, act, L.wo));
         w.layers.push_back(L);
     }
     // RoPE tables for every position a sequence can have (chronos2/model.zig:107-113, 178-187).
@@ -209,11 +165,11 @@ Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, C2Dev &w)
     TSFM_TRY(upload_f32(r, ff, &d_ff));
     TSFM_TRY(upload_f32(r, std::vector<float>(nf * d, 0.0f), &w.fut_emb));
     DevBuf tmp;
-    TSFM_TRY(tmp.alloc(nf * hid * 2));
+    TSFM_TRY(tmp.alloc(nf * hid * 2));  // 16-bit hidden activations
     cudaStream_t s = r.stream;
-    TSFM_TRY(linear(r, s, w.in_embed.hidden, d_ff, nf, 3 * ps, tmp.p, hid, 0, 1));
-    TSFM_TRY(linear(r, s, w.in_embed.residual, d_ff, nf, 3 * ps, w.fut_emb, d, 1, 0));
-    TSFM_TRY(linear(r, s, w.in_embed.output, tmp.p, nf, hid, w.fut_emb, d, 2, 0));
+    TSFM_TRY(op_linear(r, s, w.in_embed.hidden, d_ff, nf, 3 * ps, tmp.p, hid, out_mode_for(act), 1));
+    TSFM_TRY(op_linear(r, s, w.in_embed.residual, d_ff, nf, 3 * ps, w.fut_emb, d, OUT_F32, 0));
+    TSFM_TRY(op_linear(r, s, w.in_embed.output, tmp.p, nf, hid, w.fut_emb, d, OUT_F32_ACC, 0));
     TSFM_CUDA(cudaStreamSynchronize(s), "Chronos-2 future embeddings");
     TSFM_TRY(check_device_error(r));
     return Status::ok();
@@ -230,7 +186,7 @@ static void c2_geometry(const tsfm_config &c, int64_t t_in, int64_t horizon, int
     seq = n_ctx + 1 + n_out;
 }
 
-size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64_t horizon) {
+static size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64_t horizon) {
     int64_t t, start, pad, n_ctx, n_out, seq;
     c2_geometry(c, t_in, horizon, t, start, pad, n_ctx, n_out, seq);
     const int64_t d = c.d_model, ff = c.d_ff, ps = c.patch_size, q = c.num_quantiles, rows = nb * seq;
@@ -244,11 +200,13 @@ size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64_t hori
     b += Arena::span(rows * d * 2);
     b += Arena::span(rows * ff * 2);
     b += Arena::span(nb * n_out * q * ps * 4);
+    b += Arena::span(nb * n_out * d * 4) * 2;   // head input, hi / lo
+    b += Arena::span(nb * n_out * ff * 4) * 2;  // head hidden, hi / lo
     return b;
 }
 
-Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float *d_in, int64_t b, int64_t t_in,
-                  int64_t horizon, float *d_out, cudaStream_t s) {
+static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float *d_in, int64_t b,
+                         int64_t t_in, int64_t horizon, float *d_out, cudaStream_t s) {
     int64_t t, start, pad, n_ctx, n_out, seq;
     c2_geometry(c, t_in, horizon, t, start, pad, n_ctx, n_out, seq);
     const int64_t d = c.d_model, ff = c.d_ff, ps = c.patch_size, q = c.num_quantiles, nh = c.num_heads;
@@ -262,11 +220,15 @@ Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float 
     float *feats = ws.take<float>(b * n_ctx * 3 * ps);
     uint8_t *kv = ws.take<uint8_t>(b * seq);
     float *x = ws.take<float>(rows * d);
-    __nv_bfloat16 *xn = ws.take<__nv_bfloat16>(rows * d);
-    __nv_bfloat16 *qkv = ws.take<__nv_bfloat16>(rows * 3 * d);
-    __nv_bfloat16 *ao = ws.take<__nv_bfloat16>(rows * d);
-    __nv_bfloat16 *h = ws.take<__nv_bfloat16>(rows * ff);
+    // 16-bit activations (element type w.act)
+    uint16_t *xn = ws.take<uint16_t>(rows * d);
+    uint16_t *qkv = ws.take<uint16_t>(rows * 3 * d);
+    uint16_t *ao = ws.take<uint16_t>(rows * d);
+    uint16_t *h = ws.take<uint16_t>(rows * ff);
+    const int A16 = out_mode_for(w.act);
     float *raw = ws.take<float>(b * n_out * q * ps);
+    float *hid_hi = ws.take<float>(b * n_out * d), *hid_lo = ws.take<float>(b * n_out * d);
+    float *hh_hi = ws.take<float>(b * n_out * ff), *hh_lo = ws.take<float>(b * n_out * ff);
     if (ws.used > ws.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Chronos-2: workspace too small");
 
     // 1. instance norm + patch features (TF32-rounded FP32) + key validity.
@@ -283,7 +245,7 @@ Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float 
         pc.feat_kind = 0;
         pc.tscale = (float)c.time_encoding_scale;
         pc.arcsinh = c.use_arcsinh;
-        pc.feat_mode = 3;
+        pc.feat_mode = OUT_TF32;
         pc.feats = feats;
         pc.loc = loc;
         pc.scale = scl;
@@ -296,32 +258,33 @@ Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float 
     // 2. patch embedding ResBlock straight into the sequence rows: x = res(f) + out(relu(hid(f))).
     {
         const int64_t m = b * n_ctx;
-        TSFM_TRY(linear(r, s, w.in_embed.hidden, feats, m, 3 * ps, h, ff, 0, 1));
+        TSFM_TRY(op_linear(r, s, w.in_embed.hidden, feats, m, 3 * ps, h, ff, A16, 1));
         LinearCall remap;
         remap.rm_g = n_ctx;
         remap.rm_G = seq;
         remap.rm_off = 0;
-        TSFM_TRY(linear(r, s, w.in_embed.residual, feats, m, 3 * ps, x, d, 1, 0, &remap));
-        TSFM_TRY(linear(r, s, w.in_embed.output, h, m, ff, x, d, 2, 0, &remap));
+        TSFM_TRY(op_linear(r, s, w.in_embed.residual, feats, m, 3 * ps, x, d, OUT_F32, 0, &remap));
+        TSFM_TRY(op_linear(r, s, w.in_embed.output, h, m, ff, x, d, OUT_F32_ACC, 0, &remap));
         LaunchScope ls(r, s, K_OTHER, (double)b * (1 + n_out) * d * 8);
         TSFM_TRY(launch_broadcast_rows(x, b, seq, n_ctx, w.reg, 1, d, s));
         TSFM_TRY(launch_broadcast_rows(x, b, seq, n_ctx + 1, w.fut_emb, n_out, d, s));
     }
     // 3. encoder layers.
     for (const C2Dev::Layer &L : w.layers) {
-        TSFM_TRY(rmsnorm(r, s, x, L.time_norm, xn, 0, rows, d, eps));
+        TSFM_TRY(op_rmsnorm(r, s, x, L.time_norm, xn, A16, rows, d, eps));
         LinearCall rope;
         rope.rope_cos = w.rope_cos;
         rope.rope_sin = w.rope_sin;
         rope.rope_cols = (int)(2 * d);
         rope.rope_p1 = 0;
         rope.rope_p2 = seq;
-        TSFM_TRY(linear(r, s, L.qkv, xn, rows, d, qkv, 3 * d, 0, 0, &rope));
+        TSFM_TRY(op_linear(r, s, L.qkv, xn, rows, d, qkv, 3 * d, A16, 0, &rope));
         {
             AttentionCall ac;
             ac.q = qkv;
             ac.k = qkv + d;
             ac.v = qkv + 2 * d;
+            ac.dtype = w.act;
             ac.ld_qkv = 3 * d;
             ac.o = ao;
             ac.ld_o = d;
@@ -335,20 +298,23 @@ Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float 
             LaunchScope ls(r, s, K_ATTN, 4.0 * (double)b * nh * seq * seq * 64);
             TSFM_TRY(launch_attention(ac, s));
         }
-        TSFM_TRY(linear(r, s, L.o, ao, rows, d, x, d, 2, 0));
-        TSFM_TRY(rmsnorm(r, s, x, L.group_norm, xn, 0, rows, d, eps));
-        TSFM_TRY(linear(r, s, L.gv, xn, rows, d, ao, d, 0, 0));
-        TSFM_TRY(linear(r, s, L.go, ao, rows, d, x, d, 2, 0));
-        TSFM_TRY(rmsnorm(r, s, x, L.mlp_norm, xn, 0, rows, d, eps));
-        TSFM_TRY(linear(r, s, L.wi, xn, rows, d, h, ff, 0, 1));
-        TSFM_TRY(linear(r, s, L.wo, h, rows, ff, x, d, 2, 0));
+        TSFM_TRY(op_linear(r, s, L.o, ao, rows, d, x, d, OUT_F32_ACC, 0));
+        TSFM_TRY(op_rmsnorm(r, s, x, L.group_norm, xn, A16, rows, d, eps));
+        TSFM_TRY(op_linear(r, s, L.gv, xn, rows, d, ao, d, A16, 0));
+        TSFM_TRY(op_linear(r, s, L.go, ao, rows, d, x, d, OUT_F32_ACC, 0));
+        TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps));
+        TSFM_TRY(op_linear(r, s, L.wi, xn, rows, d, h, ff, A16, 1));
+        TSFM_TRY(op_linear(r, s, L.wo, h, rows, ff, x, d, OUT_F32_ACC, 0));
     }
     // 4. final norm on the future-patch rows only, then the quantile head.
     const int64_t m = b * n_out;
-    TSFM_TRY(rmsnorm(r, s, x, w.final_norm, xn, 0, m, d, eps, n_out, seq, n_ctx + 1));
-    TSFM_TRY(linear(r, s, w.out_embed.hidden, xn, m, d, h, ff, 0, 1));
-    TSFM_TRY(linear(r, s, w.out_embed.residual, xn, m, d, raw, q * ps, 1, 0));
-    TSFM_TRY(linear(r, s, w.out_embed.output, h, m, ff, raw, q * ps, 2, 0));
+    TSFM_TRY(op_rmsnorm(r, s, x, w.final_norm, hid_hi, OUT_F32, m, d, eps, n_out, seq, n_ctx + 1));
+    // FP32-accurate head: out(relu(hidden(x))) + residual(x) with split-TF32 products.
+    TSFM_TRY(op_split(r, s, hid_hi, hid_lo, m, d, d));
+    TSFM_TRY(op_linear3(r, s, w.head_hidden, hid_hi, hid_lo, m, d, hh_hi, ff, false, 1));
+    TSFM_TRY(op_split(r, s, hh_hi, hh_lo, m, ff, ff));
+    TSFM_TRY(op_linear3(r, s, w.head_residual, hid_hi, hid_lo, m, d, raw, q * ps, false, 0));
+    TSFM_TRY(op_linear3(r, s, w.head_output, hh_hi, hh_lo, m, ff, raw, q * ps, true, 0));
     {
         HeadPostCall hc;
         hc.raw = raw;
@@ -364,6 +330,23 @@ Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float 
         hc.layout = 0;
         LaunchScope ls(r, s, K_HEAD, (double)b * horizon * q * 8);
         TSFM_TRY(launch_head_post(hc, s));
+    }
+    return Status::ok();
+}
+
+// Chunks of series sized so the workspace stays within the budget (the reference bounds its
+// scratch the same way: chronos2/forecaster.zig:42-57).
+Status c2_forecast(Replica &r, const tsfm_config &c, const C2Dev &w, const float *d_in, int64_t b, int64_t t_in,
+                   int64_t horizon, float *d_out, cudaStream_t s) {
+    const size_t per = c2_workspace(c, 1, t_in, horizon);
+    int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(b, (int64_t)(workspace_budget(r) / std::max<size_t>(per, 1))));
+    const int64_t nchunks = (b + chunk - 1) / chunk;
+    chunk = (b + nchunks - 1) / nchunks;
+    TSFM_TRY(r.ws.reserve(c2_workspace(c, chunk, t_in, horizon)));
+    const int64_t q = c.num_quantiles;
+    for (int64_t s0 = 0; s0 < b; s0 += chunk) {
+        const int64_t n = std::min(chunk, b - s0);
+        TSFM_TRY(c2_forward(r, c, w, d_in + s0 * t_in, n, t_in, horizon, d_out + s0 * horizon * q, s));
     }
     return Status::ok();
 }

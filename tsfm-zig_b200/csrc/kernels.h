@@ -11,6 +11,12 @@
 
 namespace tsfm {
 
+// Element types of tensor-core operands and 16-bit activations.
+enum ElemType { E_BF16 = 0, E_F16 = 1, E_F32 = 2 };
+// Output modes of the kernels that write activations.
+enum OutMode { OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ACC = 2, OUT_TF32 = 3, OUT_F16 = 4 };
+inline int out_mode_for(int elem) { return elem == E_F16 ? OUT_F16 : elem == E_BF16 ? OUT_BF16 : OUT_TF32; }
+
 struct Status {
     int code = 0;
     std::string msg;
@@ -40,16 +46,16 @@ struct Status {
         if (_e != cudaSuccess) return ::tsfm::Status::cuda(_e, where); \
     } while (0)
 
-// y = epilogue(x[M, K] · w[N, K]^T). x and w are both BF16 (f32 = false) or both FP32 read as
-// TF32 (f32 = true).
+// y = epilogue(x[M, K] · w[N, K]^T). x and w share one element type: BF16 or FP16 (kind::f16) or
+// FP32 read as TF32 (kind::tf32).
 struct LinearCall {
     const void *x = nullptr;
     const void *w = nullptr;
-    bool f32 = false;
+    int dtype = E_BF16;
     int64_t M = 0, N = 0, K = 0, ldx = 0, ldw = 0;
     void *y = nullptr;
     int64_t ldy = 0;
-    int out_mode = 0;  // 0 bf16, 1 f32, 2 f32 accumulate (y += ...), 3 f32 rounded to tf32
+    int out_mode = OUT_BF16;  // OutMode; OUT_F32_ACC: y += result
     const float *bias = nullptr;
     int act = 0;       // 0 none, 1 relu
     // output row remap: y row = (r / rm_g) * rm_G + r % rm_g + rm_off when rm_g > 0
@@ -62,15 +68,18 @@ struct LinearCall {
 };
 Status launch_linear(const LinearCall &c, cudaStream_t stream);
 
-// Flash attention over groups of n tokens, head width 64, BF16 q/k/v/o.
+// Flash attention over groups of n tokens, head width 64, 16-bit q/k/v/o (dtype E_BF16 / E_F16).
 struct AttentionCall {
-    const __nv_bfloat16 *q = nullptr, *k = nullptr, *v = nullptr;
+    const void *q = nullptr, *k = nullptr, *v = nullptr;
+    int dtype = E_BF16;
     int64_t ld_qkv = 0;
-    __nv_bfloat16 *o = nullptr;
+    void *o = nullptr;
     int64_t ld_o = 0;
     const uint8_t *key_valid = nullptr;  // (groups, kv_len) or null
     int64_t kv_stride = 0;               // stride of key_valid between groups (default n)
-    const float *rel_bias = nullptr;     // (heads, 2n - 1) or null
+    const float *rel_bias = nullptr;     // per head, indexed by key - query offset, or null
+    int64_t rel_stride = 0;              // floats per head (0: 2n - 1)
+    int64_t rel_center = -1;             // index of offset 0 (-1: n - 1)
     int groups = 0, heads = 0, n = 0;
     float scale = 1.0f;
     // 0: T5 additive (keys_additive / full); 1: causal over valid keys, diagonal open;
@@ -83,7 +92,7 @@ struct AttentionCall {
 Status launch_attention(const AttentionCall &c, cudaStream_t stream);
 
 // RMSNorm: out[r] = x[in_row(r)] * (1 / sqrt(mean(x^2) + eps)) * scale.
-// in_row(r) = (r / g) * G + r % g + off when g > 0. out_mode: 0 bf16, 1 f32, 3 f32 rounded to tf32.
+// in_row(r) = (r / g) * G + r % g + off when g > 0. out_mode: OUT_BF16, OUT_F32, OUT_TF32, OUT_F16.
 struct RmsNormCall {
     const float *x = nullptr;
     const float *scale = nullptr;
@@ -105,7 +114,7 @@ struct PatchCall {
     int feat_kind = 0;      // 0 Chronos-2 [time, value, mask], 1 Chronos-Bolt [value, mask]
     float tscale = 1.0f;
     int arcsinh = 1;
-    int feat_mode = 1;      // features dtype: 0 bf16, 1 f32, 3 f32 rounded to tf32
+    int feat_mode = OUT_TF32;  // features: OUT_BF16, OUT_F32, OUT_TF32 or OUT_F16
     void *feats = nullptr;  // (b * n_ctx, feat_width)
     float *loc = nullptr, *scale = nullptr;  // (b)
     uint8_t *key_valid = nullptr;            // (b, seq): [0, n_ctx) written, then `extra_valid` ones
@@ -132,7 +141,7 @@ struct HeadPostCall {
 };
 Status launch_head_post(const HeadPostCall &c, cudaStream_t stream);
 
-// FP32 -> BF16 / TF32 conversion of a device buffer (weights at load).
+// FP32 -> OutMode conversion of a device buffer.
 Status launch_convert(const float *src, void *dst, int64_t n, int mode, cudaStream_t stream);
 
 int num_sms();
@@ -145,4 +154,45 @@ namespace tsfm {
 // [cols, ld_dst) are zeroed.
 Status launch_split_tf32(const float *src, int64_t rows, int64_t cols, int64_t ld_src, float alpha, float *hi,
                          float *lo, int64_t ld_dst, cudaStream_t stream);
+}  // namespace tsfm
+
+namespace tsfm {
+// One-query cross-attention (chronos_bolt/model.zig:360-381): per (series, head) softmax over the
+// series' `seq` keys of q · k_j with the T5 additive -floatMax mask (a series with no valid key
+// averages uniformly), o = sum_j p_j v_j. q: [b, ld_q] (head h at h*64), k/v rows s*seq + j with
+// row stride ld_kv, o: [b, ld_o]; all 16-bit of `dtype`; head width 64.
+struct CrossAttnCall {
+    const void *q = nullptr, *k = nullptr, *v = nullptr;
+    int dtype = E_BF16;
+    int64_t ld_q = 0, ld_kv = 0, ld_o = 0;
+    void *o = nullptr;
+    const uint8_t *key_valid = nullptr;  // (b, seq)
+    int64_t b = 0;
+    int heads = 0, seq = 0;
+};
+Status launch_cross_attention(const CrossAttnCall &c, cudaStream_t stream);
+
+// storeBlock (chronos_bolt/forecaster.zig:97-105): out[(s*H + start + p)*q + qi] =
+// pred[(s*q + qi)*P + p] for start + p < H.
+Status launch_bolt_store(const float *pred, float *out, int64_t b, int q, int P, int64_t horizon, int64_t start,
+                         cudaStream_t stream);
+
+// Context rows of the next Bolt block (chronos_bolt/forecaster.zig:56-64): next[row, i] =
+// (skip + i < len ? cur[row, skip + i] : pred[row, skip + i - len]) for rows of `rows` with
+// new_len columns; cur is [rows, len], pred [rows, P].
+Status launch_bolt_extend(const float *cur, int64_t len, const float *pred, int P, float *next, int64_t new_len,
+                          int64_t skip, int64_t rows, cudaStream_t stream);
+
+// Empirical quantiles of the q*q path samples per (series, step) (chronos_bolt/forecaster.zig:66-75):
+// samples k = raw[(s*q*q + k)*P + p], sorted ascending, quantile_linear at each level ->
+// pred[(s*q + qi)*P + p].
+Status launch_bolt_quantiles(const float *raw, const float *levels, float *pred, int64_t b, int q, int P,
+                             cudaStream_t stream);
+}  // namespace tsfm
+
+namespace tsfm {
+// dst[(r*rep + k) * len + i] = src[r * stride + offset + i]: every series' context copied once per
+// quantile path (chronos_bolt/forecaster.zig:47-48).
+Status launch_bolt_replicate(const float *src, int64_t stride, int64_t offset, int64_t len, int rep, float *dst,
+                             int64_t rows, cudaStream_t stream);
 }  // namespace tsfm

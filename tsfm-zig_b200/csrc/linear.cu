@@ -20,9 +20,11 @@
 #include "kernels.h"
 #include "ptx.cuh"
 
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <type_traits>
 
 namespace tsfm {
 
@@ -46,7 +48,7 @@ struct Epi {
     int64_t ldo;
     const float *bias;
     int act;           // 0 none, 1 relu
-    int out_mode;      // 0 bf16 store, 1 f32 store, 2 f32 accumulate, 3 f32 store rounded to tf32
+    int out_mode;      // OutMode
     int64_t rm_g, rm_G, rm_off;  // output row = (r / rm_g) * rm_G + r % rm_g + rm_off (rm_g > 0)
     const float *rope_cos;       // [positions, 32]; null = no rotation
     const float *rope_sin;
@@ -55,34 +57,55 @@ struct Epi {
     int *err;
 };
 
-__device__ __forceinline__ void store_chunk(const Epi &e, int64_t orow, int64_t col0, int nvalid, float (&v)[32]) {
-    if (e.out_mode == 0) {
-        __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(e.out) + orow * e.ldo + col0;
-        if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+template <typename H>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+template <typename H>
+__device__ __forceinline__ void store16(const Epi &e, int64_t orow, int64_t col0, int nvalid, const float (&v)[32]) {
+    H *o = reinterpret_cast<H *>(e.out) + orow * e.ldo + col0;
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint4 pk;
-                uint32_t *w = reinterpret_cast<uint32_t *>(&pk);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    __nv_bfloat162 b2 = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
-                    w[j] = *reinterpret_cast<uint32_t *>(&b2);
-                }
-                reinterpret_cast<uint4 *>(o)[q] = pk;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (j < nvalid) o[j] = __float2bfloat16_rn(v[j]);
+        for (int q = 0; q < 4; ++q) {
+            uint4 pk;
+            pk.x = pack2<H>(v[q * 8 + 0], v[q * 8 + 1]);
+            pk.y = pack2<H>(v[q * 8 + 2], v[q * 8 + 3]);
+            pk.z = pack2<H>(v[q * 8 + 4], v[q * 8 + 5]);
+            pk.w = pack2<H>(v[q * 8 + 6], v[q * 8 + 7]);
+            reinterpret_cast<uint4 *>(o)[q] = pk;
         }
     } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < nvalid) {
+                const uint32_t w = pack2<H>(v[j], 0.0f);
+                *reinterpret_cast<uint16_t *>(o + j) = (uint16_t)(w & 0xffffu);
+            }
+    }
+}
+
+__device__ __forceinline__ void store_chunk(const Epi &e, int64_t orow, int64_t col0, int nvalid, float (&v)[32]) {
+    if (e.out_mode == OUT_BF16) {
+        store16<__nv_bfloat16>(e, orow, col0, nvalid, v);
+    } else if (e.out_mode == OUT_F16) {
+        store16<__half>(e, orow, col0, nvalid, v);
+    } else {
         float *o = reinterpret_cast<float *>(e.out) + orow * e.ldo + col0;
-        if (e.out_mode == 3) {
+        if (e.out_mode == OUT_TF32) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = to_tf32(v[j]);
         }
         const bool vec = nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
-        if (e.out_mode == 2) {
+        if (e.out_mode == OUT_F32_ACC) {
             if (vec) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
@@ -91,12 +114,18 @@ __device__ __forceinline__ void store_chunk(const Epi &e, int64_t orow, int64_t 
                     a.y += v[4 * q + 1];
                     a.z += v[4 * q + 2];
                     a.w += v[4 * q + 3];
+                    if (e.act == 1) {
+                        a.x = fmaxf(a.x, 0.0f);
+                        a.y = fmaxf(a.y, 0.0f);
+                        a.z = fmaxf(a.z, 0.0f);
+                        a.w = fmaxf(a.w, 0.0f);
+                    }
                     reinterpret_cast<float4 *>(o)[q] = a;
                 }
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    if (j < nvalid) o[j] += v[j];
+                    if (j < nvalid) o[j] = e.act == 1 ? fmaxf(o[j] + v[j], 0.0f) : o[j] + v[j];
             }
         } else {
             if (vec) {
@@ -118,7 +147,8 @@ __device__ __forceinline__ void bias_act(const Epi &e, int64_t col0, int nvalid,
         for (int j = 0; j < 32; ++j)
             if (j < nvalid) v[j] += __ldg(e.bias + col0 + j);
     }
-    if (e.act == 1) {
+    // In accumulate mode the activation applies to the accumulated sum (store_chunk).
+    if (e.act == 1 && e.out_mode != OUT_F32_ACC) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
     }
@@ -130,7 +160,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     using C = TileCfg<BN>;
     constexpr int STAGES = C::STAGES;
     constexpr int BK = 128 / (int)sizeof(T);
-    constexpr uint32_t FMT = sizeof(T) == 2 ? 1u : 2u;
+    // operand format: BF16 = 1, F16 = 0 (kind::f16); TF32 = 2 (kind::tf32)
+    constexpr uint32_t FMT = std::is_same<T, float>::value ? 2u : std::is_same<T, __half>::value ? 0u : 1u;
     constexpr uint32_t IDESC = idesc_f32acc(FMT, kBM, BN);
 
     extern __shared__ uint8_t smem_raw[];
@@ -235,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < 4; ++kk) {
                         // advance 32 bytes along K inside the 128-byte swizzle atom
                         if constexpr (sizeof(T) == 2)
-                            mma_bf16(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
+                            mma_f16kind(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
                         else
                             mma_tf32(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
                     }
@@ -365,17 +396,20 @@ bool load_encode() {
     return g_encode != nullptr;
 }
 
-Status make_tmap(CUtensorMap *map, const void *base, bool f32, int64_t inner, int64_t outer, int64_t ld,
+Status make_tmap(CUtensorMap *map, const void *base, int dtype, int64_t inner, int64_t outer, int64_t ld,
                  uint32_t box_inner, uint32_t box_outer) {
     if (!load_encode()) return Status::fail(TSFM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const bool f32 = dtype == E_F32;
     const int esz = f32 ? 4 : 2;
+    const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                       : dtype == E_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * esz) & 15))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: operand base and row stride must be 16-byte aligned");
     cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+    CUresult r = g_encode(map, dt, 2,
                           const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -398,12 +432,11 @@ int sm_count() {
 template <typename T, int BN>
 Status launch_t(const LinearCall &c, cudaStream_t stream) {
     using C = TileCfg<BN>;
-    constexpr bool F32 = sizeof(T) == 4;
     constexpr int BK = 128 / (int)sizeof(T);
     CUtensorMap ta, tb;
-    Status s = make_tmap(&ta, c.x, F32, c.K, c.M, c.ldx, BK, kBM);
+    Status s = make_tmap(&ta, c.x, c.dtype, c.K, c.M, c.ldx, BK, kBM);
     if (!s) return s;
-    s = make_tmap(&tb, c.w, F32, c.K, c.N, c.ldw, BK, BN);
+    s = make_tmap(&tb, c.w, c.dtype, c.K, c.N, c.ldw, BK, BN);
     if (!s) return s;
     cudaError_t ce = cudaFuncSetAttribute(linear_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (ce != cudaSuccess) return Status::cuda(ce, "linear: set shared memory");
@@ -441,11 +474,16 @@ Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     if (c.M <= 0 || c.N <= 0 || c.K <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: empty product");
     if (c.M > INT32_MAX || c.N > INT32_MAX || c.K > INT32_MAX)
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: dimension exceeds the TMA coordinate range");
-    if (c.out_mode < 0 || c.out_mode > 3) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode");
-    if (c.rope_cos && (c.out_mode == 2 || c.rope_cols % 64)) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad rope");
+    if (c.out_mode < OUT_BF16 || c.out_mode > OUT_F16) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode");
+    if (c.rope_cos && (c.out_mode == OUT_F32_ACC || c.rope_cols % 64))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad rope");
     const bool small_n = c.N <= 128;
-    if (c.f32) return small_n ? launch_t<float, 128>(c, stream) : launch_t<float, 256>(c, stream);
-    return small_n ? launch_t<__nv_bfloat16, 128>(c, stream) : launch_t<__nv_bfloat16, 256>(c, stream);
+    switch (c.dtype) {
+        case E_F32: return small_n ? launch_t<float, 128>(c, stream) : launch_t<float, 256>(c, stream);
+        case E_F16: return small_n ? launch_t<__half, 128>(c, stream) : launch_t<__half, 256>(c, stream);
+        case E_BF16: return small_n ? launch_t<__nv_bfloat16, 128>(c, stream) : launch_t<__nv_bfloat16, 256>(c, stream);
+        default: return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "linear: operand type");
+    }
 }
 
 }  // namespace tsfm

@@ -10,7 +10,10 @@ namespace tsfm {
 
 // Chronos-2 weights on one device (chronos2/model.zig:77-125).
 struct C2Dev {
-    DResBlock in_embed, out_embed;
+    DResBlock in_embed;
+    // The quantile head runs FP32-accurate (split TF32): its output passes through sinh, which
+    // amplifies errors by cosh(v) at the tails.
+    DLin3 head_hidden, head_output, head_residual;
     struct Layer {
         float *time_norm = nullptr, *group_norm = nullptr, *mlp_norm = nullptr;
         DLin qkv, o, gv, go, wi, wo;
@@ -20,6 +23,7 @@ struct C2Dev {
     float *rope_cos = nullptr, *rope_sin = nullptr;  // [max_seq, 32]
     float *fut_emb = nullptr;                        // [max_output_patches, d]: shared future-patch embeddings
     int64_t max_seq = 0;
+    int act = E_F16;  // element type of GEMM operands / 16-bit activations
 };
 
 // Chronos-Bolt weights on one device (chronos_bolt/model.zig:101-172).
@@ -31,14 +35,15 @@ struct BoltDev {
     };
     struct Dec {
         float *self_norm = nullptr, *cross_norm = nullptr, *ffn_norm = nullptr;
-        DLin self_vo, cross_q, cross_kv, cross_o, wi, wo;  // self_vo = o·v folded (one key)
-        float *x_after_self = nullptr;  // decoder state after the token-only self-attention of layer 0
+        DLin self_v, self_o, cross_q, cross_kv, cross_o, wi, wo;
     };
     std::vector<Enc> enc;
     std::vector<Dec> dec;
     float *enc_final = nullptr, *dec_final = nullptr, *reg = nullptr, *start = nullptr;
-    float *rel_bias = nullptr;  // [heads, 2 * max_seq - 1] by relative offset
+    float *rel = nullptr;  // [heads, 2 * max_seq - 1]: bias by key - query offset (offset 0 at max_seq - 1)
     int64_t max_seq = 0;
+    float *levels = nullptr;  // quantile levels (f32) for the long-horizon loop
+    int act = E_F16;
 };
 
 struct tsfm_model_impl {
@@ -54,12 +59,20 @@ struct tsfm_model_impl {
 
 Status c2_validate(const tsfm_config &c);
 Status c2_check_tensors(const tsfm_config &c, const TensorTable &t);
-Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, C2Dev &w);
-// Forecast b series of length t_in (device pointers) into out (b, horizon, Q).
-Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const float *d_in, int64_t b, int64_t t_in,
-                  int64_t horizon, float *d_out, cudaStream_t s);
-// Workspace bytes for a chunk of nb series.
-size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64_t horizon);
+Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, C2Dev &w);
+// Device forecast of b series (inputs/out on the device), chunked to fit the workspace budget.
+Status c2_forecast(Replica &r, const tsfm_config &c, const C2Dev &w, const float *d_in, int64_t b, int64_t t_in,
+                   int64_t horizon, float *d_out, cudaStream_t s);
+
+Status bolt_validate(const tsfm_config &c);
+Status bolt_check_tensors(const tsfm_config &c, const TensorTable &t);
+Status bolt_load(Replica &r, const tsfm_config &c, const TensorTable &t, BoltDev &w);
+Status bolt_forecast(Replica &r, const tsfm_config &c, const BoltDev &w, const float *d_in, int64_t b, int64_t t_in,
+                     int64_t horizon, float *d_out, cudaStream_t s);
+
+// Bytes of device memory a forward may use for workspace (60 % of what is free plus the
+// workspace already held).
+size_t workspace_budget(Replica &r);
 
 }  // namespace tsfm
 

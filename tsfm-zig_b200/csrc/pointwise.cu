@@ -5,6 +5,8 @@
 #include "kernels.h"
 #include "ptx.cuh"
 
+#include <cuda_fp16.h>
+
 namespace tsfm {
 
 namespace {
@@ -16,10 +18,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 __device__ __forceinline__ void put(void *out, int mode, int64_t idx, float v) {
-    if (mode == 0)
+    if (mode == OUT_BF16)
         reinterpret_cast<__nv_bfloat16 *>(out)[idx] = __float2bfloat16_rn(v);
+    else if (mode == OUT_F16)
+        reinterpret_cast<__half *>(out)[idx] = __float2half_rn(v);
     else
-        reinterpret_cast<float *>(out)[idx] = mode == 3 ? to_tf32(v) : v;
+        reinterpret_cast<float *>(out)[idx] = mode == OUT_TF32 ? to_tf32(v) : v;
 }
 
 // nn.rmsNorm (core/nn.zig:374-396): one warp per row.
@@ -47,14 +51,20 @@ __global__ void rmsnorm_kernel(RmsNormCall c) {
             const float4 v = *reinterpret_cast<const float4 *>(x + i);
             const float4 s = __ldg(reinterpret_cast<const float4 *>(c.scale + i));
             const float o0 = v.x * inv * s.x, o1 = v.y * inv * s.y, o2 = v.z * inv * s.z, o3 = v.w * inv * s.w;
-            if (c.out_mode == 0) {
+            if (c.out_mode == OUT_BF16) {
                 __nv_bfloat162 a = __floats2bfloat162_rn(o0, o1), b = __floats2bfloat162_rn(o2, o3);
                 uint2 pk;
                 pk.x = *reinterpret_cast<uint32_t *>(&a);
                 pk.y = *reinterpret_cast<uint32_t *>(&b);
                 *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(c.out) + ob + i) = pk;
+            } else if (c.out_mode == OUT_F16) {
+                __half2 a = __floats2half2_rn(o0, o1), b = __floats2half2_rn(o2, o3);
+                uint2 pk;
+                pk.x = *reinterpret_cast<uint32_t *>(&a);
+                pk.y = *reinterpret_cast<uint32_t *>(&b);
+                *reinterpret_cast<uint2 *>(reinterpret_cast<__half *>(c.out) + ob + i) = pk;
             } else {
-                float4 w = c.out_mode == 3 ? make_float4(to_tf32(o0), to_tf32(o1), to_tf32(o2), to_tf32(o3))
+                float4 w = c.out_mode == OUT_TF32 ? make_float4(to_tf32(o0), to_tf32(o1), to_tf32(o2), to_tf32(o3))
                                            : make_float4(o0, o1, o2, o3);
                 *reinterpret_cast<float4 *>(reinterpret_cast<float *>(c.out) + ob + i) = w;
             }

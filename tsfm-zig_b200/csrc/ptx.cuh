@@ -143,7 +143,7 @@ __device__ __forceinline__ uint64_t sdesc_k128(const void *smem_tile) {
 }
 
 // Instruction descriptor: FP32 accumulator, K-major A and B, M = 128, N = n.
-// a_fmt/b_fmt: 1 = BF16 (kind::f16), 2 = TF32 (kind::tf32).
+// fmt: 0 = F16, 1 = BF16 (kind::f16), 2 = TF32 (kind::tf32).
 __host__ __device__ constexpr uint32_t idesc_f32acc(uint32_t fmt, uint32_t m, uint32_t n) {
     return (1u << 4)             // D format F32
            | (fmt << 7)          // A format
@@ -152,7 +152,8 @@ __host__ __device__ constexpr uint32_t idesc_f32acc(uint32_t fmt, uint32_t m, ui
            | ((m >> 4) << 24);   // M >> 4
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+// kind::f16 covers both BF16 and FP16 operands (the format is in the instruction descriptor).
+__device__ __forceinline__ void mma_f16kind(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"

@@ -3,6 +3,8 @@
 #include <cstdarg>
 #include <cstring>
 
+#include <cuda_fp16.h>
+
 namespace tsfm {
 
 std::string strf(const char *fmt, ...) {
@@ -204,12 +206,17 @@ Status upload_f32(Replica &r, const std::vector<float> &h, float **out) {
     return Status::ok();
 }
 
-Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, bool f32, DLin &dst) {
+Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, int dtype, DLin &dst) {
     DevBuf b;
     dst.out = out;
     dst.in = in;
-    dst.f32 = f32;
-    if (f32) {
+    dst.dtype = dtype;
+    if (dtype == E_F16) {
+        std::vector<__half> t(w.size());
+        for (size_t i = 0; i < w.size(); ++i) t[i] = __float2half_rn(w[i]);
+        TSFM_TRY(b.alloc(t.size() * 2));
+        TSFM_CUDA(cudaMemcpy(b.p, t.data(), t.size() * 2, cudaMemcpyHostToDevice), "upload weight");
+    } else if (dtype == E_F32) {
         std::vector<float> t(w.size());
         for (size_t i = 0; i < w.size(); ++i) t[i] = f32_to_tf32_rna(w[i]);
         TSFM_TRY(b.alloc(t.size() * 4));
@@ -226,6 +233,18 @@ Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t 
 }
 
 Status upload_bias(Replica &r, const std::vector<float> &b, DLin &dst) { return upload_f32(r, b, &dst.b); }
+
+Status upload_lin3(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, DLin3 &dst) {
+    std::vector<float> hi(w.size()), lo(w.size());
+    for (size_t i = 0; i < w.size(); ++i) {
+        hi[i] = f32_to_tf32_rna(w[i]);
+        lo[i] = f32_to_tf32_rna(w[i] - hi[i]);
+    }
+    // upload_lin with E_F32 rounds to TF32 again, which leaves these values unchanged.
+    TSFM_TRY(upload_lin(r, hi, out, in, E_F32, dst.hi));
+    TSFM_TRY(upload_lin(r, lo, out, in, E_F32, dst.lo));
+    return Status::ok();
+}
 
 Status check_device_error(Replica &r) {
     int code = 0;

@@ -54,16 +54,22 @@ struct PinnedBuf {
     Status ensure(size_t n);
 };
 
-// A linear layer's device weight: W [out, in] in the operand dtype of its GEMM, FP32 bias.
+// A linear layer's device weight: W [out, in] in the operand type of its GEMM, FP32 bias.
 struct DLin {
     void *w = nullptr;
-    bool f32 = false;  // FP32 storage read as TF32 (rounded at upload); else BF16
+    int dtype = E_BF16;  // E_BF16, E_F16, or E_F32 (stored TF32-rounded, read as TF32)
     int64_t out = 0, in = 0;
     float *b = nullptr;
 };
 
 struct DResBlock {
     DLin hidden, output, residual;
+};
+
+// A weight split into two TF32 parts, w = hi + lo (hi = tf32(w), lo = tf32(w - hi)), for products
+// that must keep FP32 accuracy: x w^T ~= x_hi w_hi + x_hi w_lo + x_lo w_hi. The bias rides on hi.
+struct DLin3 {
+    DLin hi, lo;
 };
 
 // Per-kernel-class launch accounting (optionally timed with CUDA events).
@@ -124,7 +130,9 @@ struct Replica {
     cudaStream_t stream = nullptr;
     DevBuf err;  // device error word(s)
     std::vector<DevBuf> weights;
-    Arena ws;
+    Arena ws;   // per-chunk model workspace
+    Arena fc;   // forecaster buffers that live across chunks (Bolt quantile paths)
+    DevBuf io;  // device copies of host inputs / outputs
     PinnedBuf pin_in, pin_out;
     Profiler prof;
     std::mutex mu;
@@ -143,8 +151,9 @@ struct TensorTable {
 
 // Upload helpers (run with the replica's device current).
 Status upload_f32(Replica &r, const std::vector<float> &h, float **out);
-Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, bool f32, DLin &dst);
+Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, int dtype, DLin &dst);
 Status upload_bias(Replica &r, const std::vector<float> &b, DLin &dst);
+Status upload_lin3(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, DLin3 &dst);
 
 // Checks the device error word after a stream sync.
 Status check_device_error(Replica &r);

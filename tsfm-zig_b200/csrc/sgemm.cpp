@@ -75,7 +75,7 @@ Status sgemm_nt_impl(int m, int n, int k, float alpha, const float *A, int lda, 
     TSFM_TRY(launch_split_tf32(static_cast<const float *>(x->raw_a.p), m, k, k, alpha, ahi, alo, kp, s));
     TSFM_TRY(launch_split_tf32(static_cast<const float *>(x->raw_b.p), n, k, k, 1.0f, bhi, blo, kp, s));
     LinearCall lc;
-    lc.f32 = true;
+    lc.dtype = E_F32;
     lc.M = m;
     lc.N = n;
     lc.K = kp;
@@ -86,11 +86,11 @@ Status sgemm_nt_impl(int m, int n, int k, float alpha, const float *A, int lda, 
     lc.err = static_cast<int *>(x->err.p);
     lc.x = alo;
     lc.w = bhi;
-    lc.out_mode = 1;
+    lc.out_mode = OUT_F32;
     TSFM_TRY(launch_linear(lc, s));
     lc.x = ahi;
     lc.w = blo;
-    lc.out_mode = 2;
+    lc.out_mode = OUT_F32_ACC;
     TSFM_TRY(launch_linear(lc, s));
     lc.x = ahi;
     lc.w = bhi;

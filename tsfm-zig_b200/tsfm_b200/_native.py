@@ -19,7 +19,7 @@ STATUS_NAMES = {
 }
 FAMILY = {"chronos2": 1, "chronos_bolt": 2, "timestral": 3}
 DTYPE = {"F32": 0, "F16": 1, "BF16": 2}
-COMPUTE = {"bf16": 0, "tf32": 1}
+COMPUTE = {"bf16": 0, "tf32": 1, "f16": 2}
 LAYER_KIND = {"time": 0, "variate": 1, "time_variate": 2, "variate_time": 3}
 
 
@@ -106,7 +106,7 @@ SIGNATURES = {
                                      ctypes.c_int, _P, ctypes.c_int, _P]),
     "tsfm_kernel_linear": (_I32, [_P, _I32, _P, _I32, _P, _P, _I32, _I32, _I64, _I64, _I64, _I64, _I64,
                                   _I64, _P]),
-    "tsfm_kernel_attention": (_I32, [_P, _P, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _F, _I32, _P]),
+    "tsfm_kernel_attention": (_I32, [_P, _P, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _F, _I32, _I32, _P]),
     "tsfm_kernel_rmsnorm": (_I32, [_P, _P, _P, _I32, _I64, _I64, _F, _P]),
 }
 

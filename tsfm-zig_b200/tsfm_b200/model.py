@@ -34,7 +34,7 @@ def tensor_table(tensors):
 
 
 class Model:
-    def __init__(self, cfg, tensors, devices=(0,), compute="bf16"):
+    def __init__(self, cfg, tensors, devices=(0,), compute="f16"):
         self.parsed = config_mod.parse(cfg)
         self.family = self.parsed.family
         self.cfg = cfg
