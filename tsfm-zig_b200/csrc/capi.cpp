@@ -21,6 +21,14 @@ int32_t report(const Status &s) {
     return s.code;
 }
 
+}  // namespace
+
+namespace tsfm {
+int32_t set_last_error(const Status &s) { return report(s); }
+}  // namespace tsfm
+
+namespace {
+
 template <class F>
 int32_t guarded(F &&f) {
     try {

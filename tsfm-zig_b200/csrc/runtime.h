@@ -160,4 +160,7 @@ Status check_device_error(Replica &r);
 
 std::string strf(const char *fmt, ...);
 
+// Records `s` as the calling thread's last error (read by tsfm_last_error) and returns its code.
+int32_t set_last_error(const Status &s);
+
 }  // namespace tsfm

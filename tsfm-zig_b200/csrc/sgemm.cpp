@@ -13,8 +13,6 @@ using namespace tsfm;
 
 namespace {
 
-thread_local std::string g_seam_error;
-
 struct SeamCtx {
     int device = -1;
     cudaStream_t stream = nullptr;
@@ -107,10 +105,8 @@ Status sgemm_nt_impl(int m, int n, int k, float alpha, const float *A, int lda, 
     return Status::ok();
 }
 
-int seam_status(const Status &st) {
-    g_seam_error = st.msg;
-    return st.code;
-}
+// The seam keeps gemm.c's int return (0 = success); the message goes to tsfm_last_error().
+int seam_status(const Status &st) { return set_last_error(st); }
 
 }  // namespace
 
