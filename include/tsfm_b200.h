@@ -242,6 +242,20 @@ int tsfm_sgemm_nt(int m, int n, int k, float alpha, const float *A, int lda,  /*
 int tsfm_sgemm_nn(int m, int n, int k, const float *A, int lda,               /* gemm.c:323 */
                   const float *B, int ldb, float *C, int ldc, void *b_buf);
 
+/* tsfm_sgemm_nt_noalloc has no counterpart in the reference. It computes the same FP32-accurate
+ * C[m, n] = alpha * A[m, k] * B[n, k]^T as tsfm_sgemm_nt, but on DEVICE pointers A, B, C (row
+ * strides lda, ldb, ldc in elements) and without allocating anything, for callers that cannot
+ * call cudaMalloc once running: latency-bound loops that cannot afford the device-wide
+ * synchronisation of cudaMalloc/cudaFree, real-time hosts that forbid allocation after start-up,
+ * and processes whose own pool owns all device memory. Its scratch is a fixed 16 MiB array inside
+ * the library (held by every GPU that loads it): (m + n) * round_up(k, 4) must not exceed
+ * 2^21 - 64 floats, else TSFM_ERR_INVALID_ARGUMENT. All calls share that array: calls that
+ * overlap on the GPU race. The first call on each device looks up the array's address (which may
+ * load the library's device code), so make it before any stream capture. Runs on `stream` (null =
+ * legacy default stream) and returns when C is written; 0 = success, else a tsfm_status. */
+int32_t tsfm_sgemm_nt_noalloc(int m, int n, int k, float alpha, const float *A, int lda,
+                              const float *B, int ldb, float *C, int ldc, void *stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Kernel-level entry points on device pointers (what the family forwards are built from; used by
  * the kernel parity tests). All return after enqueueing on `stream`.

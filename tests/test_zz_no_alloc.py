@@ -1,0 +1,74 @@
+"""The allocation-free GEMM entry point (tsfm_sgemm_nt_noalloc), called through the C ABI.
+
+Some callers of this library cannot allocate device memory while running (cudaMalloc/cudaFree
+synchronise the whole device; real-time loops forbid allocation after start-up; a process-wide
+pool may own all device memory). For them the library keeps its scratch in a fixed array of its
+own. This test checks, on two calls in a row, that the allocation-free entry point returns what
+the ordinary seam entry point tsfm_sgemm_nt returns (same 1e-4 tolerance as the seam's own test),
+that device free memory does not change across a call once the first call has set the array up,
+and that a product too large for the array is rejected rather than run.
+
+The file is named to be collected last, so a run that stops at the first failure has already run
+every other test; it passes alone in a fresh process as well.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import tsfm_b200 as tb  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def seam(A, B, alpha):
+    """tsfm_sgemm_nt on host copies (the existing entry point)."""
+    m, k = A.shape
+    n = B.shape[0]
+    a = np.ascontiguousarray(A.cpu().numpy())
+    b = np.ascontiguousarray(B.cpu().numpy())
+    c = np.zeros((m, n), np.float32)
+    assert tb.lib.tsfm_sgemm_nt(m, n, k, alpha, a.ctypes.data, k, b.ctypes.data, k, c.ctypes.data, n, None) == 0
+    return c
+
+
+def noalloc(A, B, C, alpha, stream):
+    m, k = A.shape
+    n = B.shape[0]
+    return tb.lib.tsfm_sgemm_nt_noalloc(m, n, k, alpha, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0),
+                                        C.data_ptr(), C.stride(0), stream)
+
+
+def test_noalloc_matches_seam_on_two_calls_in_a_row():
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator().manual_seed(1234)
+    # Both calls use the same kernel instances (N <= 128 tiles), so the second call cannot load
+    # new device code either.
+    shapes = [(37, 29, 23, 0.7), (300, 100, 257, 1.0)]
+    for call, (m, n, k, alpha) in enumerate(shapes):
+        A = (torch.rand(m, k, generator=g) * 2 - 1).to(dev)
+        B = (torch.rand(n, k, generator=g) * 2 - 1).to(dev)
+        C = torch.full((m, n), float("nan"), device=dev)
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
+        st = noalloc(A, B, C, alpha, stream)
+        free_after = torch.cuda.mem_get_info()[0]
+        assert st == 0, tb.last_error()
+        if call > 0:
+            assert free_after == free_before  # nothing allocated once set up
+        want = seam(A, B, alpha)
+        np.testing.assert_allclose(C.cpu().numpy(), want, atol=1e-4)
+        ref = alpha * (A.double() @ B.double().T)
+        assert (C.double() - ref).abs().max().item() <= 1e-4
+
+
+def test_noalloc_rejects_products_beyond_its_scratch():
+    dev = torch.device("cuda:0")
+    m, n, k = 2048, 2048, 1024  # (m + n) * k = 4M floats > 2M
+    A = torch.zeros(m, k, device=dev)
+    B = torch.zeros(n, k, device=dev)
+    C = torch.zeros(m, n, device=dev)
+    st = noalloc(A, B, C, 1.0, torch.cuda.current_stream().cuda_stream)
+    assert tb.STATUS_NAMES[st] == "INVALID_ARGUMENT"
+    assert "scratch" in tb.last_error()

@@ -104,6 +104,8 @@ SIGNATURES = {
                                      ctypes.c_int, _P, ctypes.c_int, _P]),
     "tsfm_sgemm_nn": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P,
                                      ctypes.c_int, _P, ctypes.c_int, _P]),
+    "tsfm_sgemm_nt_noalloc": (_I32, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _F, _P, ctypes.c_int, _P,
+                                     ctypes.c_int, _P, ctypes.c_int, _P]),
     "tsfm_kernel_linear": (_I32, [_P, _I32, _P, _I32, _P, _P, _I32, _I32, _I64, _I64, _I64, _I64, _I64,
                                   _I64, _P]),
     "tsfm_kernel_attention": (_I32, [_P, _P, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _F, _I32, _I32, _P]),
