@@ -1,0 +1,187 @@
+"""Timestral forecasts on the GPU against the oracle (the CPU restatement of
+timestral/forecaster.zig + timestral/model.zig): univariate and multivariate targets, past and
+known-future covariates (numeric and target-encoded categorical), the block-autoregressive loop
+with its refine frame and feedback, context truncation, the quantile cap, the symmetric pass and
+the non-negative clip, plus the reference's error cases.
+
+Tolerance: max |dq| <= TOL * sigma_eff per target row, sigma_eff = the population std of the
+row's observed context (1 for an all-missing row, 1e-5 for a constant one), times
+max(1, cosh(v) / cosh(2)) where v = asinh of the oracle quantile in that frame: the head's output
+passes through sinh, whose slope cosh(v) amplifies a small encoder difference at the tails (the
+same bound as the Chronos-2 tests). 4 float32 ulps of max(|q|, |loc|) are discounted for the
+float32 storage of q = sinh(v) * scale + loc."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import tsfm_b200 as tb  # noqa: E402
+from oracle import binding as ob  # noqa: E402
+from tsfm_b200 import synthetic as syn  # noqa: E402
+
+from helpers import instance_scale  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+EPS32 = float(np.finfo(np.float32).eps)
+
+
+def tiny_cfg(**kw):
+    base = dict(d_model=128, num_heads=2, mlp_hidden_dim=256, num_layers=2, patch=16, context_length=512,
+                block_size=8)
+    extra = {k: kw.pop(k) for k in list(kw) if k not in ("schedule", "quantiles")}
+    cfg = syn.timestral_config(**base, **kw)
+    cfg.update(extra)
+    return cfg
+
+
+def models(cfg, seed=7):
+    w = syn.random_checkpoint(cfg, seed=seed, norm_jitter=0.1)
+    gpu = tb.Model(cfg, w)
+    return gpu, ob.OracleModel(gpu.parsed, w, tb.tensor_table), w
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    return models(tiny_cfg())
+
+
+def rel_err(got, want, x):
+    """got/want (b, v, h, q); x (b, v, t) with NaN where unobserved."""
+    b, v, t = x.shape
+    flat = x.reshape(b * v, t)
+    sig = instance_scale(flat).reshape(b, v, 1, 1)
+    loc = np.array([np.nanmean(r) if np.isfinite(r).any() else 0.0 for r in flat]).reshape(b, v, 1, 1)
+    vv = np.arcsinh((want.astype(np.float64) - loc) / sig)
+    amp = np.maximum(1.0, np.cosh(np.clip(vv, -30, 30)) / np.cosh(2.0))
+    floor = 4 * EPS32 * np.maximum(np.abs(want), np.abs(loc))
+    excess = np.maximum(np.abs(got.astype(np.float64) - want) - floor, 0.0)
+    return float(np.max(excess / (sig * amp)))
+
+
+def split(x):
+    obs = np.isfinite(x)
+    z = np.where(obs, x, 0.0).astype(np.float32)
+    return z, obs.astype(np.uint8)
+
+
+def edge_inputs(b, v, t, seed=5):
+    x = syn.seeded_series(b * v, t, seed=seed).reshape(b, v, t)
+    x[1, 0, :] = np.nan                 # all missing
+    x[2 % b, 0, :] = 3.25               # constant
+    x[3 % b, 0, : t // 2] = np.nan      # long leading gap
+    if t > 64:
+        x[0, 0, 16:48] = np.nan         # whole missing patches
+    return x
+
+
+def run_both(gpu, ora, x, horizon, cov=None, opts=None, ocov=None):
+    z, o = split(x)
+    got = gpu.forecast_timestral(z, horizon, observed=o, cov=cov, opts=opts)
+    want = ora.forecast_timestral(z, o, horizon, None if ocov is None else ocov, opts)
+    return got, want
+
+
+@pytest.mark.parametrize("t,horizon", [(300, 24), (512, 130), (40, 16), (1000, 64), (17, 5)])
+def test_univariate_matches_oracle(tiny, t, horizon):
+    gpu, ora, _ = tiny
+    x = edge_inputs(5, 1, t)
+    got, want = run_both(gpu, ora, x, horizon)
+    assert got.shape == want.shape == (5, 1, horizon, 9)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want, x[:, :, -512:]) <= TOL
+
+
+def test_multivariate_matches_oracle(tiny):
+    gpu, ora, _ = tiny
+    x = edge_inputs(4, 3, 260, seed=8)
+    got, want = run_both(gpu, ora, x, 40)
+    assert got.shape == (4, 3, 40, 9)
+    assert rel_err(got, want, x) <= TOL
+
+
+def covariate_arrays(b, t, horizon, seed=21):
+    rng = np.random.default_rng(seed)
+    past = syn.ar1_covariates(b, 2, t, seed=seed)
+    known = syn.ar1_covariates(b, 1, t + horizon, seed=seed + 1)
+    known[:, :, 5:9] = np.nan
+    cat_past = rng.integers(0, 4, (b, 1, t)).astype(np.float64)
+    cat_past[:, :, :3] = np.nan
+    cat_known = rng.integers(0, 3, (b, 1, t + horizon)).astype(np.float64)
+    cat_known[:, :, -2:] = 7.0  # a code never seen in the context
+    return past, known, cat_past, cat_known
+
+
+@pytest.mark.parametrize("per_shot", [8, 2])
+def test_covariates_match_oracle(tiny, per_shot):
+    gpu, ora, _ = tiny
+    b, t, horizon = 3, 200, 56
+    x = edge_inputs(b, 1, t, seed=12)
+    past, known, cat_past, cat_known = covariate_arrays(b, t, horizon)
+    cov = tb.covariates(past=past, known=known, cat_past=cat_past, cat_known=cat_known)
+    opts = tb.timestral_options(per_shot_horizon_patches=per_shot)
+    got, want = run_both(gpu, ora, x, horizon, cov=cov, opts=opts, ocov=cov[0])
+    assert got.shape == (b, 1, horizon, 9)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want, x) <= TOL
+
+
+def test_past_only_covariates_multivariate(tiny):
+    gpu, ora, _ = tiny
+    b, t, horizon = 2, 150, 20
+    x = edge_inputs(b, 2, t, seed=30)
+    past = syn.ar1_covariates(b, 3, t, seed=31)
+    cov = tb.covariates(past=past)
+    got, want = run_both(gpu, ora, x, horizon, cov=cov, ocov=cov[0])
+    assert rel_err(got, want, x) <= TOL
+
+
+@pytest.mark.parametrize("kw", [dict(symmetric_averaging=False), dict(clip_nonnegative=False),
+                                dict(max_context=256, per_shot_horizon_patches=3), dict(quantile_real_cap_k=0.0),
+                                dict(quantile_real_cap_k=0.5)])
+def test_options_match_oracle(tiny, kw):
+    gpu, ora, _ = tiny
+    x = edge_inputs(4, 1, 600, seed=40)
+    x[0] = np.abs(x[0])  # a non-negative row: the clip applies to it
+    opts = tb.timestral_options(**kw)
+    got, want = run_both(gpu, ora, x, 100, opts=opts)
+    assert rel_err(got, want, x[:, :, -512:]) <= TOL
+
+
+def test_replicas_are_bit_identical(tiny):
+    gpu, _, w = tiny
+    two = tb.Model(tiny_cfg(), w, devices=(0, 0))
+    x = edge_inputs(6, 1, 300, seed=50)
+    z, o = split(x)
+    assert np.array_equal(gpu.forecast_timestral(z, 48, observed=o), two.forecast_timestral(z, 48, observed=o))
+
+
+def test_covariates_unsupported_errors():
+    cfg = tiny_cfg(covariate_enabled=False)
+    gpu, _, _ = models(cfg)
+    x = edge_inputs(2, 1, 100)
+    cov = tb.covariates(past=syn.ar1_covariates(2, 1, 100))
+    with pytest.raises(tb.TsfmError) as e:
+        gpu.forecast_timestral(x, 16, cov=cov)
+    assert e.value.name == "COVARIATES_UNSUPPORTED"
+
+
+def test_known_covariates_need_a_time_then_mixed_schedule():
+    # Only variate-then-time layers: no time layer is followed by both axes.
+    gpu, _, _ = models(tiny_cfg(schedule=["variate_time", "time"]))
+    x = edge_inputs(2, 1, 100)
+    cov = tb.covariates(known=syn.ar1_covariates(2, 1, 116))
+    with pytest.raises(tb.TsfmError) as e:
+        gpu.forecast_timestral(x, 16, cov=cov)
+    assert e.value.name == "COVARIATES_UNSUPPORTED"
+
+
+def test_asymmetric_quantiles_error():
+    q = [0.1, 0.2, 0.5, 0.7, 0.95]
+    gpu, _, _ = models(tiny_cfg(quantiles=q))
+    x = edge_inputs(2, 1, 100)
+    with pytest.raises(tb.TsfmError) as e:
+        gpu.forecast_timestral(x, 16)
+    assert e.value.name == "ASYMMETRIC_QUANTILES"
+    out = gpu.forecast_timestral(x, 16, opts=tb.timestral_options(symmetric_averaging=False))
+    assert out.shape == (2, 1, 16, 5) and np.isfinite(out).all()

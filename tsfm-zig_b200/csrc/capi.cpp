@@ -227,13 +227,19 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
         m->cfg.layer_kinds = m->kinds.data();
         m->compute = compute;
         const tsfm_config &c = m->cfg;
+        TensorTable table(tensors, n_tensors);
         if (c.family == TSFM_CHRONOS2) {
             TSFM_TRY(c2_validate(c));
+            TSFM_TRY(c2_check_tensors(c, table));
+        } else if (c.family == TSFM_CHRONOS_BOLT) {
+            TSFM_TRY(bolt_validate(c));
+            TSFM_TRY(bolt_check_tensors(c, table));
+        } else if (c.family == TSFM_TIMESTRAL) {
+            TSFM_TRY(ts_validate(c));
+            TSFM_TRY(ts_check_tensors(c, table));
         } else {
             return Status::fail(TSFM_ERR_UNSUPPORTED, "family not implemented in this build");
         }
-        TensorTable table(tensors, n_tensors);
-        if (c.family == TSFM_CHRONOS2) TSFM_TRY(c2_check_tensors(c, table));
         int ndev = 0;
         TSFM_TRY(device_count(&ndev));
         std::vector<int> devs;
@@ -257,6 +263,14 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
                 auto w = std::make_unique<C2Dev>();
                 TSFM_TRY(c2_load(*r, c, table, act, *w));
                 m->c2.push_back(std::move(w));
+            } else if (c.family == TSFM_CHRONOS_BOLT) {
+                auto w = std::make_unique<BoltDev>();
+                TSFM_TRY(bolt_load(*r, c, table, act, *w));
+                m->bolt.push_back(std::move(w));
+            } else {
+                auto w = std::make_unique<TsDev>();
+                TSFM_TRY(ts_load(*r, c, table, act, *w));
+                m->ts.push_back(std::move(w));
             }
             if (i == 0)
                 for (auto &b : r->weights) m->weight_bytes += b.bytes;
@@ -317,12 +331,43 @@ int32_t tsfm_forecast_chronos2_device(tsfm_model *model, const float *inputs, si
     });
 }
 
-int32_t tsfm_forecast_bolt(tsfm_model *model, const float *, size_t, size_t, size_t, float *) {
-    return guarded([&] { return check_model(model, TSFM_CHRONOS_BOLT); });
+static Status bolt_args(const void *in, size_t b, size_t t, size_t horizon, const void *out) {
+    if (!in || !out) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null inputs or outputs");
+    if (b == 0 || t == 0 || horizon == 0) return Status::fail(TSFM_ERR_EMPTY_INPUT, "EmptyInput");
+    return Status::ok();
 }
 
-int32_t tsfm_forecast_bolt_device(tsfm_model *model, const float *, size_t, size_t, size_t, float *, void *) {
-    return guarded([&] { return check_model(model, TSFM_CHRONOS_BOLT); });
+int32_t tsfm_forecast_bolt(tsfm_model *model, const float *inputs, size_t b, size_t t, size_t horizon, float *out) {
+    return guarded([&]() -> Status {
+        TSFM_TRY(check_model(model, TSFM_CHRONOS_BOLT));
+        TSFM_TRY(bolt_args(inputs, b, t, horizon, out));
+        const size_t n = model->reps.size();
+        const int64_t q = model->cfg.num_quantiles;
+        return for_replicas(n, [&](size_t i) -> Status {
+            const int64_t s0 = (int64_t)(b * i / n), s1 = (int64_t)(b * (i + 1) / n);
+            if (s1 <= s0) return Status::ok();
+            Replica &r = *model->reps[i];
+            const BoltDev &w = *model->bolt[i];
+            const int64_t nb = s1 - s0;
+            return replica_forecast(r, inputs + s0 * t, (size_t)nb * t * 4, (size_t)nb * horizon * q * 4,
+                                    out + s0 * horizon * q, [&](const float *d_in, float *d_out, cudaStream_t s) {
+                                        return bolt_forecast(r, model->cfg, w, d_in, nb, (int64_t)t, (int64_t)horizon,
+                                                             d_out, s);
+                                    });
+        });
+    });
+}
+
+int32_t tsfm_forecast_bolt_device(tsfm_model *model, const float *inputs, size_t b, size_t t, size_t horizon, float *out,
+                                  void *stream) {
+    return guarded([&]() -> Status {
+        TSFM_TRY(check_model(model, TSFM_CHRONOS_BOLT));
+        TSFM_TRY(bolt_args(inputs, b, t, horizon, out));
+        Replica &r = *model->reps[0];
+        return replica_forecast_device(r, static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
+            return bolt_forecast(r, model->cfg, *model->bolt[0], inputs, (int64_t)b, (int64_t)t, (int64_t)horizon, out, s);
+        });
+    });
 }
 
 void tsfm_timestral_default_options(tsfm_timestral_options *o) {
@@ -335,9 +380,45 @@ void tsfm_timestral_default_options(tsfm_timestral_options *o) {
     o->clip_nonnegative = 1;
 }
 
-int32_t tsfm_forecast_timestral(tsfm_model *model, const float *, const uint8_t *, size_t, size_t, size_t, size_t,
-                                const tsfm_covariates *, const tsfm_timestral_options *, float *) {
-    return guarded([&] { return check_model(model, TSFM_TIMESTRAL); });
+int32_t tsfm_forecast_timestral(tsfm_model *model, const float *inputs, const uint8_t *observed, size_t b, size_t v,
+                                size_t t, size_t horizon, const tsfm_covariates *cov, const tsfm_timestral_options *opts,
+                                float *out) {
+    return guarded([&]() -> Status {
+        TSFM_TRY(check_model(model, TSFM_TIMESTRAL));
+        if (!inputs || !observed || !out) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null inputs or outputs");
+        if (b == 0 || v == 0 || t == 0 || horizon == 0) return Status::fail(TSFM_ERR_EMPTY_INPUT, "EmptyInput");
+        tsfm_timestral_options o;
+        tsfm_timestral_default_options(&o);
+        if (opts) o = *opts;
+        tsfm_covariates cv{};
+        if (cov) cv = *cov;
+        if ((cv.past && !cv.n_past) || (cv.known && !cv.n_known) || (cv.cat_past && !cv.n_cat_past) ||
+            (cv.cat_known && !cv.n_cat_known))
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "covariate array without channels");
+        const size_t n = model->reps.size();
+        const size_t q = (size_t)model->cfg.num_quantiles;
+        // Series shard across replicas; every array is (b, channels, len), so a shard is a
+        // contiguous slice of each.
+        return for_replicas(n, [&](size_t i) -> Status {
+            const size_t s0 = b * i / n, s1 = b * (i + 1) / n;
+            if (s1 <= s0) return Status::ok();
+            Replica &r = *model->reps[i];
+            std::lock_guard<std::mutex> lk(r.mu);
+            TSFM_CUDA(cudaSetDevice(r.device), "cudaSetDevice");
+            r.prof.cur_launches = 0;
+            tsfm_covariates sh = cv;
+            if (cv.past) sh.past = cv.past + s0 * cv.n_past * t;
+            if (cv.known) sh.known = cv.known + s0 * cv.n_known * (t + horizon);
+            if (cv.cat_past) sh.cat_past = cv.cat_past + s0 * cv.n_cat_past * t;
+            if (cv.cat_known) sh.cat_known = cv.cat_known + s0 * cv.n_cat_known * (t + horizon);
+            TSFM_TRY(ts_forecast(r, model->cfg, *model->ts[i], inputs + s0 * v * t, observed + s0 * v * t, s1 - s0, v, t,
+                                 horizon, cov ? &sh : nullptr, o, out + s0 * v * horizon * q));
+            TSFM_TRY(check_device_error(r));
+            r.prof.collect();
+            r.prof.last_forecast_launches = r.prof.cur_launches;
+            return Status::ok();
+        });
+    });
 }
 
 int32_t tsfm_profile_enable(tsfm_model *model, int32_t enable) {

@@ -57,7 +57,7 @@ struct LinearCall {
     int64_t ldy = 0;
     int out_mode = OUT_BF16;  // OutMode; OUT_F32_ACC: y += result
     const float *bias = nullptr;
-    int act = 0;       // 0 none, 1 relu
+    int act = 0;       // 0 none, 1 relu, 2 silu
     // output row remap: y row = (r / rm_g) * rm_G + r % rm_g + rm_off when rm_g > 0
     int64_t rm_g = 0, rm_G = 0, rm_off = 0;
     // rotate-half RoPE on columns [0, rope_cols), 64-wide heads; tables [positions, 32]
@@ -101,6 +101,7 @@ struct RmsNormCall {
     int64_t rows = 0, dim = 0;
     float eps = 1e-6f;
     int64_t g = 0, G = 0, off = 0;
+    const int64_t *rows_idx = nullptr;  // when set: in_row(r) = rows_idx[r]
 };
 Status launch_rmsnorm(const RmsNormCall &c, cudaStream_t stream);
 

@@ -47,7 +47,7 @@ struct Epi {
     void *out;
     int64_t ldo;
     const float *bias;
-    int act;           // 0 none, 1 relu
+    int act;           // 0 none, 1 relu, 2 silu
     int out_mode;      // OutMode
     int64_t rm_g, rm_G, rm_off;  // output row = (r / rm_g) * rm_G + r % rm_g + rm_off (rm_g > 0)
     const float *rope_cos;       // [positions, 32]; null = no rotation
@@ -56,6 +56,11 @@ struct Epi {
     int64_t rope_p1, rope_p2;    // position index = (r / p1) * p2 + r % p2 (p1 == 0: r % p2)
     int *err;
 };
+
+// 0 none, 1 relu, 2 silu
+__device__ __forceinline__ float apply_act(int act, float v) {
+    return act == 1 ? fmaxf(v, 0.0f) : act == 2 ? v / (1.0f + expf(-v)) : v;
+}
 
 template <typename H>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -114,18 +119,16 @@ __device__ __forceinline__ void store_chunk(const Epi &e, int64_t orow, int64_t 
                     a.y += v[4 * q + 1];
                     a.z += v[4 * q + 2];
                     a.w += v[4 * q + 3];
-                    if (e.act == 1) {
-                        a.x = fmaxf(a.x, 0.0f);
-                        a.y = fmaxf(a.y, 0.0f);
-                        a.z = fmaxf(a.z, 0.0f);
-                        a.w = fmaxf(a.w, 0.0f);
-                    }
+                    a.x = apply_act(e.act, a.x);
+                    a.y = apply_act(e.act, a.y);
+                    a.z = apply_act(e.act, a.z);
+                    a.w = apply_act(e.act, a.w);
                     reinterpret_cast<float4 *>(o)[q] = a;
                 }
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    if (j < nvalid) o[j] = e.act == 1 ? fmaxf(o[j] + v[j], 0.0f) : o[j] + v[j];
+                    if (j < nvalid) o[j] = apply_act(e.act, o[j] + v[j]);
             }
         } else {
             if (vec) {
@@ -151,6 +154,10 @@ __device__ __forceinline__ void bias_act(const Epi &e, int64_t col0, int nvalid,
     if (e.act == 1 && e.out_mode != OUT_F32_ACC) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+    }
+    if (e.act == 2 && e.out_mode != OUT_F32_ACC) {  // silu (nn.siluInPlace, core/nn.zig:399-407)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = v[j] / (1.0f + expf(-v[j]));
     }
 }
 

@@ -28,7 +28,8 @@ struct C2Dev {
 
 // Chronos-Bolt weights on one device (chronos_bolt/model.zig:101-172).
 struct BoltDev {
-    DResBlock in_embed, out_embed;
+    DResBlock in_embed;
+    DLin3 head_hidden, head_output, head_residual;  // FP32-accurate quantile head
     struct Enc {
         float *attn_norm = nullptr, *ffn_norm = nullptr;
         DLin qkv, o, wi, wo;
@@ -46,6 +47,32 @@ struct BoltDev {
     int act = E_F16;
 };
 
+// Timestral weights on one device (timestral/model.zig:26-70).
+struct TsDev {
+    DResBlock patch_proj;                           // 2P -> 4d (SiLU) -> d, with bias
+    DLin3 head_hidden, head_output, head_residual;  // FP32-accurate quantile head, no bias
+    float *fq_rep = nullptr;                        // forecast query replicated block_size times
+    float *out_norm = nullptr, *inv_freq = nullptr, *widths = nullptr;
+    struct Attn {
+        bool is_time = true, gate = false;
+        float *norm = nullptr;
+        DLin qkvg;  // rows [q | k | v | gate]: q, k, v permuted to head-major; gate when enabled
+        DLin o;
+    };
+    struct Layer {
+        int n_attn = 1;
+        Attn attns[2];
+        float *mlp_norm = nullptr;
+        DLin w12, w3;
+    };
+    std::vector<Layer> layers;
+    int64_t max_qkv_cols = 0;
+    int act = E_F16;
+    // Per-forecast roles of one series' rows (0 target, 1 past covariate, 2 known covariate).
+    const int8_t *roles = nullptr;
+    std::vector<int8_t> roles_host;
+};
+
 struct tsfm_model_impl {
     tsfm_config cfg{};
     std::vector<double> quantiles;
@@ -54,6 +81,7 @@ struct tsfm_model_impl {
     std::vector<std::unique_ptr<Replica>> reps;
     std::vector<std::unique_ptr<C2Dev>> c2;
     std::vector<std::unique_ptr<BoltDev>> bolt;
+    std::vector<std::unique_ptr<TsDev>> ts;
     uint64_t weight_bytes = 0;
 };
 
@@ -66,9 +94,17 @@ Status c2_forecast(Replica &r, const tsfm_config &c, const C2Dev &w, const float
 
 Status bolt_validate(const tsfm_config &c);
 Status bolt_check_tensors(const tsfm_config &c, const TensorTable &t);
-Status bolt_load(Replica &r, const tsfm_config &c, const TensorTable &t, BoltDev &w);
+Status bolt_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, BoltDev &w);
 Status bolt_forecast(Replica &r, const tsfm_config &c, const BoltDev &w, const float *d_in, int64_t b, int64_t t_in,
                      int64_t horizon, float *d_out, cudaStream_t s);
+
+Status ts_validate(const tsfm_config &c);
+Status ts_check_tensors(const tsfm_config &c, const TensorTable &t);
+Status ts_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, TsDev &w);
+// Host-memory forecast of b series with v target variates each: out is (b, v, horizon, q).
+Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inputs, const uint8_t *observed, size_t b,
+                   size_t v, size_t t0, size_t horizon, const tsfm_covariates *cov, const tsfm_timestral_options &opts,
+                   float *out);
 
 // Bytes of device memory a forward may use for workspace (60 % of what is free plus the
 // workspace already held).

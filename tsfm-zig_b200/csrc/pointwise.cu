@@ -31,7 +31,7 @@ __global__ void rmsnorm_kernel(RmsNormCall c) {
     const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (r >= c.rows) return;
-    const int64_t in_row = c.g > 0 ? (r / c.g) * c.G + r % c.g + c.off : r;
+    const int64_t in_row = c.rows_idx ? c.rows_idx[r] : c.g > 0 ? (r / c.g) * c.G + r % c.g + c.off : r;
     const float *x = c.x + in_row * c.dim;
     const bool vec = (c.dim % 4) == 0;
     float ss = 0.0f;

@@ -1,0 +1,798 @@
+// Timestral on the device: the decoder-only time/variate transformer of timestral/model.zig and
+// the block-autoregressive forecaster of timestral/forecaster.zig.
+//
+// Host side (C++, per series; timestral/forecaster.zig:57-141, 201-421): options, categorical
+// target encoding, covariate channels, the mirrored inputs of the symmetric pass, forward-fill and
+// left padding to a patch multiple. Both passes of the symmetric average are batched as one
+// device run over twice the series (series are independent).
+// Device side: per block, statistics + features, patch embedding, the transformer over
+// [Enc ; Dec] tokens (fused QKV|gate GEMM with partial RoPE in its epilogue, flash attention with
+// the encoder causal_keys / decoder-chain masks, 11x11 variate attention, gated output, SwiGLU
+// MLP), the FP32-accurate head with the monotone quantile construction, the refine frame, the
+// feedback of medians / known futures / blanks; then the quantile cap, the NaN check, the
+// symmetric average and the non-negative clip.
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstring>
+
+#include "model.h"
+#include "ops.h"
+#include "timestral_kernels.h"
+
+namespace tsfm {
+
+namespace {
+
+int64_t hd_of(const tsfm_config &c) { return c.d_model / c.num_heads; }
+int64_t rope_dim(const tsfm_config &c) { return (int64_t)((double)hd_of(c) * c.rope_partial_factor); }
+
+// The (attention, is_time) list of a layer kind (timestral/config.zig:94-100).
+int layer_axes(int kind, bool *is_time) {
+    switch (kind) {
+        case TSFM_LAYER_TIME: is_time[0] = true; return 1;
+        case TSFM_LAYER_VARIATE: is_time[0] = false; return 1;
+        case TSFM_LAYER_TIME_VARIATE: is_time[0] = true; is_time[1] = false; return 2;
+        default: is_time[0] = false; is_time[1] = true; return 2;
+    }
+}
+
+// Config.supportsKnownCovariates (timestral/config.zig:49-72).
+bool supports_known(const tsfm_config &c) {
+    if (!c.covariate_enabled) return false;
+    std::vector<bool> ops;
+    for (int i = 0; i < c.n_layer_kinds; ++i) {
+        bool it[2];
+        const int na = layer_axes(c.layer_kinds[i], it);
+        for (int a = 0; a < na; ++a) ops.push_back(it[a]);
+    }
+    for (size_t i = 0; i < ops.size(); ++i) {
+        if (!ops[i]) continue;
+        bool any_time = false, any_var = false;
+        for (size_t j = i + 1; j < ops.size(); ++j) {
+            any_time = any_time || ops[j];
+            any_var = any_var || !ops[j];
+        }
+        if (any_time && any_var) return true;
+    }
+    return false;
+}
+
+int median_index(const tsfm_config &c) {
+    for (int i = 0; i < c.num_quantiles; ++i)
+        if (c.quantiles[i] == 0.5) return i;
+    return 0;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host preprocessing (timestral/forecaster.zig)
+
+long slot_of(const std::vector<double> &cats, double code) {
+    if (std::isnan(code)) return -1;
+    auto it = std::lower_bound(cats.begin(), cats.end(), code);
+    return it != cats.end() && *it == code ? it - cats.begin() : -1;
+}
+
+// targetEncode (forecaster.zig:243-289), smooth = 1.
+void target_encode(const double *target, const double *past, size_t t, const double *future, size_t nf, float *out_past,
+                   float *out_future) {
+    double item_count = 0, item_sum = 0;
+    for (size_t i = 0; i < t; ++i)
+        if (std::isfinite(target[i])) {
+            item_count += 1;
+            item_sum += target[i];
+        }
+    const double mean = item_count > 0 ? item_sum / item_count : 0.0;
+    std::vector<double> cats;
+    for (size_t i = 0; i < t; ++i)
+        if (std::isfinite(past[i])) cats.push_back(past[i]);
+    std::sort(cats.begin(), cats.end());
+    cats.erase(std::unique(cats.begin(), cats.end()), cats.end());
+    const size_t nc = cats.size();
+    std::vector<double> sums(nc + 1, 0.0), counts(nc + 1, 0.0);
+    for (size_t i = 0; i < t; ++i) {
+        if (!std::isfinite(target[i])) continue;
+        const long s = slot_of(cats, past[i]);
+        const size_t slot = s < 0 ? nc : (size_t)s;
+        sums[slot] += target[i];
+        counts[slot] += 1;
+    }
+    for (size_t i = 0; i < t; ++i) {
+        const long s = slot_of(cats, past[i]);
+        const size_t slot = s < 0 ? nc : (size_t)s;
+        out_past[i] = (float)((mean + sums[slot]) / (1.0 + counts[slot]));
+    }
+    if (future)
+        for (size_t i = 0; i < nf; ++i) {
+            double v;
+            if (std::isnan(future[i])) {
+                v = (mean + sums[nc]) / (1.0 + counts[nc]);
+            } else {
+                const long s = slot_of(cats, future[i]);
+                v = s >= 0 ? (mean + sums[s]) / (1.0 + counts[s]) : mean;
+            }
+            out_future[i] = (float)v;
+        }
+}
+
+struct HostRows {
+    std::vector<float> rows;   // (b * vall, t)
+    std::vector<uint8_t> mask;
+    std::vector<float> kf;     // (b * vall, hpad)
+    std::vector<uint8_t> kfm;
+};
+
+// forecastRaw's input preparation (forecaster.zig:319-388): forward-filled targets, covariate
+// rows, the last `keep` steps left-padded to a patch multiple, and the known futures.
+void prepare_rows(const float *inputs, const uint8_t *observed, size_t b, size_t v, size_t t0, size_t horizon,
+                  const float *past, size_t n_past, const float *known, size_t n_known, size_t keep, size_t t,
+                  size_t hpad, HostRows &h) {
+    const size_t vall = v + n_past + n_known, nrows = b * vall;
+    h.rows.assign(nrows * t, 0.0f);
+    h.mask.assign(nrows * t, 0);
+    h.kf.assign(nrows * hpad, 0.0f);
+    h.kfm.assign(nrows * hpad, 0);
+    for (size_t s = 0; s < b; ++s)
+        for (size_t i = 0; i < vall; ++i) {
+            const size_t r = s * vall + i;
+            float last = 0.0f;
+            bool seen = false;
+            for (size_t j = 0; j < t0; ++j) {
+                float val;
+                bool ob;
+                if (i < v) {
+                    const size_t idx = (s * v + i) * t0 + j;
+                    if (observed[idx]) {
+                        last = inputs[idx];
+                        seen = true;
+                    }
+                    val = seen ? last : 0.0f;
+                    ob = observed[idx] != 0;
+                } else if (i < v + n_past) {
+                    const float x = past[(s * n_past + (i - v)) * t0 + j];
+                    ob = !std::isnan(x);
+                    val = ob ? x : 0.0f;
+                } else {
+                    const float x = known[(s * n_known + (i - v - n_past)) * (t0 + horizon) + j];
+                    ob = !std::isnan(x);
+                    val = ob ? x : 0.0f;
+                }
+                if (j >= t0 - keep) {
+                    const size_t dst = r * t + (t - keep) + (j - (t0 - keep));
+                    h.rows[dst] = val;
+                    h.mask[dst] = ob;
+                }
+            }
+            if (i >= v + n_past)
+                for (size_t j = 0; j < horizon; ++j) {
+                    const float x = known[(s * n_known + (i - v - n_past)) * (t0 + horizon) + t0 + j];
+                    h.kfm[r * hpad + j] = !std::isnan(x);
+                    h.kf[r * hpad + j] = h.kfm[r * hpad + j] ? x : 0.0f;
+                }
+        }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Device forward
+
+struct Block {
+    int64_t groups, vall, v, t, h, ps;
+    bool cov;
+};
+
+size_t block_workspace(const tsfm_config &c, const TsDev &w, const Block &k) {
+    const int64_t d = c.d_model, hid = c.d_ff, q = c.num_quantiles, ps = k.ps;
+    const int64_t R = k.groups * k.vall, hl = k.h * ps, wlen = k.cov ? k.t + hl : k.t, n = wlen / ps;
+    const int64_t sl = n + k.h, rows = R * sl, nt = k.groups * k.v;
+    const int64_t cols = w.max_qkv_cols;
+    size_t b = 0;
+    b += Arena::span(R * n * 4) * 2 + Arena::span(R * 4) * 2 + Arena::span(R) * 2 + Arena::span(R * n);
+    b += Arena::span(k.groups * 4) + Arena::span(R * n * 2 * ps * 4);
+    b += Arena::span(k.groups * sl * 32 * 4) * 2;
+    b += Arena::span(rows * d * 4) + Arena::span(rows * d * 2) + Arena::span(rows * cols * 2) + Arena::span(rows * d * 2);
+    b += Arena::span(rows * std::max<int64_t>(2 * hid, 4 * d) * 2) + Arena::span(rows * hid * 2);
+    b += Arena::span(nt * k.h * 8) + Arena::span(nt * 8);
+    b += Arena::span(nt * k.h * d * 4) * 2 + Arena::span(nt * k.h * 4 * d * 4) * 2 + Arena::span(nt * hl * q * 4) * 2;
+    return b;
+}
+
+// Model.predictBlock (timestral/model.zig:220-432) for `groups` series at context length t:
+// writes qs (groups * v, h * ps, q).
+Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Block &k, const float *ctx,
+                     const uint8_t *obs, const float *kf, const uint8_t *kfm, int64_t kf_ld, float *qs, cudaStream_t s) {
+    const int64_t d = c.d_model, hid = c.d_ff, q = c.num_quantiles, ps = k.ps, nh = c.num_heads;
+    const int64_t R = k.groups * k.vall, hl = k.h * ps, wlen = k.cov ? k.t + hl : k.t, n = wlen / ps;
+    const int64_t ne = n, sl = ne + k.h, rows = R * sl, l = k.t / ps, nt = k.groups * k.v;
+    const float eps = (float)c.layer_norm_epsilon;
+    const int A16 = out_mode_for(w.act);
+    Arena &ws = r.ws;
+    ws.reset();
+    float *loc = ws.take<float>(R * n), *scl = ws.take<float>(R * n);
+    float *kloc = ws.take<float>(R), *kscl = ws.take<float>(R);
+    uint8_t *binary = ws.take<uint8_t>(R), *bidir = ws.take<uint8_t>(R);
+    uint8_t *kv = ws.take<uint8_t>(R * n);
+    int *first_obs = ws.take<int>(k.groups);
+    float *feats = ws.take<float>(R * n * 2 * ps);
+    float *cs = ws.take<float>(k.groups * sl * 32), *sn = ws.take<float>(k.groups * sl * 32);
+    float *x = ws.take<float>(rows * d);
+    uint16_t *xn = ws.take<uint16_t>(rows * d);
+    uint16_t *qkvg = ws.take<uint16_t>(rows * w.max_qkv_cols);
+    uint16_t *o16 = ws.take<uint16_t>(rows * d);
+    uint16_t *h16 = ws.take<uint16_t>(rows * std::max<int64_t>(2 * hid, 4 * d));
+    uint16_t *a16 = ws.take<uint16_t>(rows * hid);
+    int64_t *head_rows = ws.take<int64_t>(nt * k.h);
+    int64_t *target_row = ws.take<int64_t>(nt);
+    float *hid_hi = ws.take<float>(nt * k.h * d), *hid_lo = ws.take<float>(nt * k.h * d);
+    float *hh_hi = ws.take<float>(nt * k.h * 4 * d), *hh_lo = ws.take<float>(nt * k.h * 4 * d);
+    float *raw = ws.take<float>(nt * hl * q);
+    if (ws.used > ws.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Timestral: workspace too small");
+
+    // 1. statistics, features, key validity, first observed patch.
+    TSFM_CUDA(cudaMemsetAsync(first_obs, 0x7f, k.groups * sizeof(int), s), "timestral: first_obs");
+    {
+        TsStatsCall sc;
+        sc.ctx = ctx;
+        sc.obs = obs;
+        sc.t = k.t;
+        sc.kf = kf;
+        sc.kfm = kfm;
+        sc.kf_ld = kf_ld;
+        sc.hl = hl;
+        sc.cov = k.cov;
+        sc.rows = R;
+        sc.ps = (int)ps;
+        sc.vall = (int)k.vall;
+        sc.roles = w.roles;
+        sc.min_scale = c.minimum_scale;
+        sc.use_asinh = c.use_arcsinh;
+        sc.attend_missing = c.attend_missing_patches;
+        sc.loc = loc;
+        sc.scale = scl;
+        sc.kloc = kloc;
+        sc.kscale = kscl;
+        sc.binary = binary;
+        sc.key_valid = kv;
+        sc.first_obs = first_obs;
+        LaunchScope ls(r, s, K_PATCH, (double)R * wlen * 5 * 2);
+        TSFM_TRY(launch_ts_stats(sc, feats, s));
+    }
+    // 2. patch embedding into the encoder rows; forecast queries into the decoder rows.
+    {
+        const int64_t m = R * n;
+        TSFM_TRY(op_linear(r, s, w.patch_proj.hidden, feats, m, 2 * ps, h16, 4 * d, A16, 2));
+        LinearCall remap;
+        remap.rm_g = n;
+        remap.rm_G = sl;
+        TSFM_TRY(op_linear(r, s, w.patch_proj.residual, feats, m, 2 * ps, x, d, OUT_F32, 0, &remap));
+        TSFM_TRY(op_linear(r, s, w.patch_proj.output, h16, m, 4 * d, x, d, OUT_F32_ACC, 0, &remap));
+        LaunchScope ls(r, s, K_OTHER, (double)R * k.h * d * 8);
+        TSFM_TRY(launch_broadcast_rows(x, R, sl, ne, w.fq_rep, k.h, d, s));
+    }
+    // 3. RoPE tables relative to each group's first observed patch; per-row attention flags;
+    //    head row indices.
+    {
+        LaunchScope ls(r, s, K_OTHER, (double)k.groups * sl * 32 * 8);
+        TSFM_TRY(launch_ts_rope(first_obs, k.groups, sl, ne, l, w.inv_freq, 32, cs, sn, s));
+    }
+    {
+        std::vector<uint8_t> bd(R);
+        std::vector<int64_t> hr(nt * k.h), tr(nt);
+        int64_t oi = 0;
+        for (int64_t row = 0; row < R; ++row) {
+            const int role = w.roles_host[row % k.vall];
+            bd[row] = k.cov && role == 2;
+            if (role != 0) continue;
+            tr[oi] = row;
+            for (int64_t j = 0; j < k.h; ++j) hr[oi * k.h + j] = row * sl + ne + j;
+            ++oi;
+        }
+        TSFM_CUDA(cudaMemcpyAsync(bidir, bd.data(), R, cudaMemcpyHostToDevice, s), "timestral: flags");
+        TSFM_CUDA(cudaMemcpyAsync(head_rows, hr.data(), hr.size() * 8, cudaMemcpyHostToDevice, s), "timestral: rows");
+        TSFM_CUDA(cudaMemcpyAsync(target_row, tr.data(), tr.size() * 8, cudaMemcpyHostToDevice, s), "timestral: rows");
+        TSFM_CUDA(cudaStreamSynchronize(s), "timestral: flags");  // the host vectors go out of scope
+    }
+    // 4. transformer (runTransformer, timestral/model.zig:434-482).
+    for (const TsDev::Layer &L : w.layers) {
+        for (int ai = 0; ai < L.n_attn; ++ai) {
+            const TsDev::Attn &a = L.attns[ai];
+            const int64_t cols = a.qkvg.out;
+            TSFM_TRY(op_rmsnorm(r, s, x, a.norm, xn, A16, rows, d, eps));
+            LinearCall rope;
+            if (a.is_time) {
+                rope.rope_cos = cs;
+                rope.rope_sin = sn;
+                rope.rope_cols = (int)(2 * d);
+                rope.rope_p1 = sl * k.vall;
+                rope.rope_p2 = sl;
+            }
+            TSFM_TRY(op_linear(r, s, a.qkvg, xn, rows, d, qkvg, cols, A16, 0, a.is_time ? &rope : nullptr));
+            if (a.is_time) {
+                AttentionCall ac;
+                ac.q = qkvg;
+                ac.k = qkvg + d;
+                ac.v = qkvg + 2 * d;
+                ac.dtype = w.act;
+                ac.ld_qkv = cols;
+                ac.o = o16;
+                ac.ld_o = d;
+                ac.key_valid = kv;
+                ac.kv_stride = ne;
+                ac.groups = (int)R;
+                ac.heads = (int)nh;
+                ac.n = (int)sl;
+                ac.scale = 1.0f / std::sqrt((float)hd_of(c));
+                ac.mask_mode = 1;
+                ac.ne = (int)ne;
+                ac.l = (int)l;
+                ac.group_bidir = bidir;
+                LaunchScope ls(r, s, K_ATTN, 2.0 * (double)R * nh * sl * sl * 64);
+                TSFM_TRY(launch_attention(ac, s));
+            } else {
+                TsVariateCall vc;
+                vc.qkv = qkvg;
+                vc.ld = cols;
+                vc.d = d;
+                vc.o = o16;
+                vc.ldo = d;
+                vc.dtype = w.act;
+                vc.groups = k.groups;
+                vc.sl = sl;
+                vc.ne = ne;
+                vc.vall = (int)k.vall;
+                vc.heads = (int)nh;
+                vc.key_valid = kv;
+                vc.roles = w.roles;
+                vc.cov = k.cov;
+                vc.scale = 1.0f / std::sqrt((float)hd_of(c));
+                LaunchScope ls(r, s, K_ATTN, 4.0 * (double)k.groups * sl * nh * k.vall * k.vall * 64);
+                TSFM_TRY(launch_ts_variate(vc, s));
+            }
+            if (a.gate) {
+                LaunchScope ls(r, s, K_OTHER, (double)rows * d * 6);
+                TSFM_TRY(launch_ts_gate(o16, d, qkvg + 3 * d, cols, rows, d, w.act, s));
+            }
+            TSFM_TRY(op_linear(r, s, a.o, o16, rows, d, x, d, OUT_F32_ACC, 0));
+        }
+        TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps));
+        TSFM_TRY(op_linear(r, s, L.w12, xn, rows, d, h16, 2 * hid, A16, 0));
+        {
+            LaunchScope ls(r, s, K_OTHER, (double)rows * hid * 6);
+            TSFM_TRY(launch_ts_swiglu(h16, a16, rows, hid, w.act, s));
+        }
+        TSFM_TRY(op_linear(r, s, L.w3, a16, rows, hid, x, d, OUT_F32_ACC, 0));
+    }
+    // 5. out_norm on the target rows' decoder tokens, FP32-accurate head, monotone quantiles.
+    const int64_t mh = nt * k.h;
+    {
+        RmsNormCall rc;
+        rc.x = x;
+        rc.scale = w.out_norm;
+        rc.out = hid_hi;
+        rc.out_mode = OUT_F32;
+        rc.rows = mh;
+        rc.dim = d;
+        rc.eps = eps;
+        rc.rows_idx = head_rows;
+        LaunchScope ls(r, s, K_NORM, (double)mh * d * 8);
+        TSFM_TRY(launch_rmsnorm(rc, s));
+    }
+    TSFM_TRY(op_split(r, s, hid_hi, hid_lo, mh, d, d));
+    TSFM_TRY(op_linear3(r, s, w.head_hidden, hid_hi, hid_lo, mh, d, hh_hi, 4 * d, false, 2));
+    TSFM_TRY(op_split(r, s, hh_hi, hh_lo, mh, 4 * d, 4 * d));
+    TSFM_TRY(op_linear3(r, s, w.head_residual, hid_hi, hid_lo, mh, d, raw, ps * q, false, 0));
+    TSFM_TRY(op_linear3(r, s, w.head_output, hh_hi, hh_lo, mh, 4 * d, raw, ps * q, true, 0));
+    TsHeadCall hc;
+    hc.raw = raw;
+    hc.out = qs;
+    hc.loc = loc;
+    hc.scale = scl;
+    hc.target_row = target_row;
+    hc.nt = nt;
+    hc.hl = hl;
+    hc.n = n;
+    hc.l = l;
+    hc.q = (int)q;
+    hc.m = median_index(c);
+    hc.widths = w.widths;
+    hc.wf = (float)c.quantile_width_factor;
+    hc.use_asinh = c.use_arcsinh;
+    LaunchScope ls(r, s, K_HEAD, (double)nt * hl * q * 8);
+    return launch_ts_head(hc, s);
+}
+
+Status load_norm(Replica &r, const TensorTable &t, const std::string &name, int64_t d, float **dst) {
+    std::vector<float> v;
+    TSFM_TRY(t.get(name, d, v));
+    return upload_f32(r, v, dst);
+}
+
+}  // namespace
+
+Status ts_validate(const tsfm_config &c) {
+    // timestral/config.zig:74-85
+    if (c.num_heads <= 0 || c.d_model % c.num_heads) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: d_model % num_heads");
+    const int64_t rd = rope_dim(c);
+    if (rd == 0 || rd % 2) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: rope dim");
+    if (c.n_layer_kinds <= 0 || !c.layer_kinds) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: block_schedule");
+    for (int i = 0; i < c.n_layer_kinds; ++i)
+        if (c.layer_kinds[i] < 0 || c.layer_kinds[i] > 3) return Status::fail(TSFM_ERR_INVALID_CONFIG, "UnknownLayerKind");
+    if (c.num_quantiles <= 0 || !c.quantiles) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: quantile knots");
+    bool median = false;
+    for (int i = 0; i < c.num_quantiles; ++i) {
+        median = median || c.quantiles[i] == 0.5;
+        if (i > 0 && !(c.quantiles[i - 1] < c.quantiles[i])) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: quantile knots");
+    }
+    if (!median) return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: no 0.5 knot");
+    if (c.patch_size <= 0 || c.block_size <= 0 || c.context_length <= 0 || c.d_ff <= 0)
+        return Status::fail(TSFM_ERR_INVALID_CONFIG, "InvalidConfig: sizes");
+    // Kernel constraints of this backend.
+    if (hd_of(c) != 64) return Status::fail(TSFM_ERR_UNSUPPORTED, "Timestral: head width must be 64");
+    if (c.d_model % 64 || c.d_ff % 8 || (2 * c.patch_size) % 4 || ((int64_t)c.patch_size * c.num_quantiles) % 4)
+        return Status::fail(TSFM_ERR_UNSUPPORTED, "Timestral: dimensions must keep 16-byte rows");
+    if (c.num_quantiles > 32) return Status::fail(TSFM_ERR_UNSUPPORTED, "Timestral: at most 32 quantiles");
+    return Status::ok();
+}
+
+Status ts_check_tensors(const tsfm_config &c, const TensorTable &t) {
+    const int64_t d = c.d_model, ps = c.patch_size, hid = c.d_ff, q = c.num_quantiles;
+    TSFM_TRY(check_resblock(t, "representation.patch_proj", 2 * ps, 4 * d, d, true));
+    TSFM_TRY(t.check("representation.forecast_query", d));
+    TSFM_TRY(check_resblock(t, "head.projection", d, 4 * d, ps * q, false));
+    TSFM_TRY(t.check("transformer.out_norm.scale", d));
+    for (int li = 0; li < c.n_layer_kinds; ++li) {
+        bool it[2];
+        const int na = layer_axes(c.layer_kinds[li], it);
+        for (int ai = 0; ai < na; ++ai) {
+            TSFM_TRY(t.check(strf("transformer.layers.%d.attn_norms.%d.scale", li, ai), d));
+            TSFM_TRY(t.check(strf("transformer.layers.%d.attns.%d.wQKV.weight", li, ai), 3 * d * d));
+            TSFM_TRY(t.check(strf("transformer.layers.%d.attns.%d.wO.weight", li, ai), d * d));
+            if (it[ai] ? c.time_attn_gate : c.variate_attn_gate)
+                TSFM_TRY(t.check(strf("transformer.layers.%d.attns.%d._gate.weight", li, ai), d * d));
+        }
+        TSFM_TRY(t.check(strf("transformer.layers.%d.mlp_norm.scale", li), d));
+        TSFM_TRY(t.check(strf("transformer.layers.%d.mlp.w12.weight", li), 2 * hid * d));
+        TSFM_TRY(t.check(strf("transformer.layers.%d.mlp.w3.weight", li), d * hid));
+    }
+    return Status::ok();
+}
+
+Status ts_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, TsDev &w) {
+    const int64_t d = c.d_model, ps = c.patch_size, hid = c.d_ff, q = c.num_quantiles, nh = c.num_heads, hd = hd_of(c);
+    w.act = act;
+    TSFM_TRY(load_resblock(r, t, "representation.patch_proj", 2 * ps, 4 * d, d, true, E_F32, act, w.patch_proj));
+    std::vector<float> v;
+    TSFM_TRY(t.get("representation.forecast_query", d, v));
+    std::vector<float> rep;
+    for (int i = 0; i < c.block_size; ++i) rep.insert(rep.end(), v.begin(), v.end());
+    TSFM_TRY(upload_f32(r, rep, &w.fq_rep));
+    TSFM_TRY(t.get("head.projection.hidden_layer.weight", 4 * d * d, v));
+    TSFM_TRY(upload_lin3(r, v, 4 * d, d, w.head_hidden));
+    TSFM_TRY(t.get("head.projection.output_layer.weight", ps * q * 4 * d, v));
+    TSFM_TRY(upload_lin3(r, v, ps * q, 4 * d, w.head_output));
+    TSFM_TRY(t.get("head.projection.residual_layer.weight", ps * q * d, v));
+    TSFM_TRY(upload_lin3(r, v, ps * q, d, w.head_residual));
+    TSFM_TRY(load_norm(r, t, "transformer.out_norm.scale", d, &w.out_norm));
+    w.max_qkv_cols = 3 * d;
+    for (int li = 0; li < c.n_layer_kinds; ++li) {
+        TsDev::Layer L;
+        bool it[2];
+        L.n_attn = layer_axes(c.layer_kinds[li], it);
+        for (int ai = 0; ai < L.n_attn; ++ai) {
+            TsDev::Attn &a = L.attns[ai];
+            a.is_time = it[ai];
+            a.gate = (it[ai] ? c.time_attn_gate : c.variate_attn_gate) != 0;
+            TSFM_TRY(load_norm(r, t, strf("transformer.layers.%d.attn_norms.%d.scale", li, ai), d, &a.norm));
+            std::vector<float> src;
+            TSFM_TRY(t.get(strf("transformer.layers.%d.attns.%d.wQKV.weight", li, ai), 3 * d * d, src));
+            // permuteQkv (timestral/model.zig:72-85): rows (qkv, head_dim, heads) -> (qkv, head, head_dim).
+            std::vector<float> fused(3 * d * d);
+            for (int64_t sel = 0; sel < 3; ++sel)
+                for (int64_t h = 0; h < nh; ++h)
+                    for (int64_t dd = 0; dd < hd; ++dd)
+                        std::memcpy(&fused[((sel * nh + h) * hd + dd) * d], &src[(sel * d + dd * nh + h) * d], d * 4);
+            if (a.gate) {
+                TSFM_TRY(t.get(strf("transformer.layers.%d.attns.%d._gate.weight", li, ai), d * d, v));
+                fused.insert(fused.end(), v.begin(), v.end());  // one GEMM yields [q | k | v | gate]
+            }
+            const int64_t cols = (int64_t)fused.size() / d;
+            w.max_qkv_cols = std::max(w.max_qkv_cols, cols);
+            TSFM_TRY(upload_lin(r, fused, cols, d, act, a.qkvg));
+            TSFM_TRY(t.get(strf("transformer.layers.%d.attns.%d.wO.weight", li, ai), d * d, v));
+            TSFM_TRY(upload_lin(r, v, d, d, act, a.o));
+        }
+        TSFM_TRY(load_norm(r, t, strf("transformer.layers.%d.mlp_norm.scale", li), d, &L.mlp_norm));
+        TSFM_TRY(t.get(strf("transformer.layers.%d.mlp.w12.weight", li), 2 * hid * d, v));
+        TSFM_TRY(upload_lin(r, v, 2 * hid, d, act, L.w12));
+        TSFM_TRY(t.get(strf("transformer.layers.%d.mlp.w3.weight", li), d * hid, v));
+        TSFM_TRY(upload_lin(r, v, d, hid, act, L.w3));
+        w.layers.push_back(L);
+    }
+    // inv_freq with zeros past rope_dim / 2 (identity rotation) (timestral/model.zig:180-188).
+    const int64_t rd = rope_dim(c);
+    std::vector<float> inv(hd / 2, 0.0f);
+    const float base = (float)c.rope_theta;
+    for (int64_t i = 0; i < rd / 2; ++i) inv[i] = 1.0f / std::pow(base, (float)(2 * i) / (float)rd);
+    TSFM_TRY(upload_f32(r, inv, &w.inv_freq));
+    // Quantile widths of the monotone head (timestral/model.zig:510-514).
+    const int m = median_index(c);
+    std::vector<float> widths(q, 0.0f);
+    for (int i = m + 1; i < q; ++i) widths[i] = (float)(c.quantiles[i] - c.quantiles[i - 1]);
+    for (int i = 0; i < m; ++i) widths[i] = (float)(c.quantiles[i + 1] - c.quantiles[i]);
+    TSFM_TRY(upload_f32(r, widths, &w.widths));
+    return Status::ok();
+}
+
+// forecaster.forecast (timestral/forecaster.zig:57-180) for b series on one replica; all arrays
+// are host memory, `out` is (b, v, horizon, q).
+Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inputs, const uint8_t *observed, size_t b,
+                   size_t v, size_t t0, size_t horizon, const tsfm_covariates *covp, const tsfm_timestral_options &opts,
+                   float *out) {
+    const int64_t q = c.num_quantiles, ps = c.patch_size;
+    tsfm_timestral_options o = opts;
+    if (o.max_context == 0) o.max_context = (size_t)c.context_length;
+    o.per_shot_horizon_patches = std::min<size_t>(std::max<size_t>(o.per_shot_horizon_patches, 1), (size_t)c.block_size);
+    tsfm_covariates cov{};
+    if (covp) cov = *covp;
+    const bool any_cov = cov.past || cov.known || cov.cat_past || cov.cat_known;
+    if (any_cov && !c.covariate_enabled) return Status::fail(TSFM_ERR_COVARIATES_UNSUPPORTED, "CovariatesUnsupported");
+    if ((cov.known || cov.cat_known) && !supports_known(c))
+        return Status::fail(TSFM_ERR_COVARIATES_UNSUPPORTED, "KnownCovariatesUnsupported");
+
+    // Categorical codes: target-encoded against a univariate target, else raw (forecaster.zig:92-103).
+    std::vector<double> target;
+    const bool have_target = (cov.cat_past || cov.cat_known) && v == 1;
+    if (have_target) {
+        target.resize(b * t0);
+        for (size_t s = 0; s < b; ++s) {
+            bool started = false;
+            float last = 0.0f;
+            for (size_t i = 0; i < t0; ++i) {
+                if (observed[s * t0 + i]) {
+                    started = true;
+                    last = inputs[s * t0 + i];
+                }
+                const bool in_window = t0 <= o.max_context || i >= t0 - o.max_context;
+                target[s * t0 + i] = started && in_window ? (double)last : std::nan("");
+            }
+        }
+    }
+    auto encode_cat = [&](const double *codes, size_t nc, size_t len) {
+        std::vector<float> outv(b * nc * len);
+        for (size_t s = 0; s < b; ++s)
+            for (size_t j = 0; j < nc; ++j) {
+                const double *row = codes + (s * nc + j) * len;
+                float *dst = &outv[(s * nc + j) * len];
+                if (!have_target) {
+                    for (size_t i = 0; i < len; ++i) dst[i] = (float)row[i];
+                    continue;
+                }
+                target_encode(&target[s * t0], row, t0, len > t0 ? row + t0 : nullptr, len - t0, dst,
+                              len > t0 ? dst + t0 : nullptr);
+                for (size_t i = 0; i < t0; ++i)
+                    if (std::isnan(target[s * t0 + i]) && std::isnan(row[i])) dst[i] = std::nanf("");
+            }
+        return outv;
+    };
+    std::vector<float> enc_past, enc_known;
+    if (cov.cat_past) enc_past = encode_cat(cov.cat_past, cov.n_cat_past, t0);
+    if (cov.cat_known) enc_known = encode_cat(cov.cat_known, cov.n_cat_known, t0 + horizon);
+    auto cat_channels = [&](const float *a, size_t ca, const std::vector<float> &bb, size_t cb, size_t len) {
+        std::vector<float> outv;
+        if (ca + cb == 0) return outv;
+        outv.resize(b * (ca + cb) * len);
+        for (size_t i = 0; i < b; ++i) {
+            if (a) std::memcpy(&outv[i * (ca + cb) * len], a + i * ca * len, ca * len * 4);
+            if (!bb.empty()) std::memcpy(&outv[(i * (ca + cb) + ca) * len], &bb[i * cb * len], cb * len * 4);
+        }
+        return outv;
+    };
+    const size_t np = cov.past ? cov.n_past : 0, nk = cov.known ? cov.n_known : 0;
+    const size_t ncp = cov.cat_past ? cov.n_cat_past : 0, nck = cov.cat_known ? cov.n_cat_known : 0;
+    std::vector<float> past_rows = cat_channels(cov.past, np, enc_past, ncp, t0);
+    std::vector<float> known_rows = cat_channels(cov.known, nk, enc_known, nck, t0 + horizon);
+    const size_t n_past = np + ncp, n_known = nk + nck;
+    if (n_past == 0 && n_known == 0 && any_cov) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "InvalidInput");
+    if (o.symmetric_averaging)
+        for (int64_t i = 0; i < q; ++i)
+            if (std::fabs(c.quantiles[i] + c.quantiles[q - 1 - i] - 1.0) > 1e-9)
+                return Status::fail(TSFM_ERR_ASYMMETRIC_QUANTILES, "AsymmetricQuantiles");
+
+    // forecastRaw input preparation for the forward pass and, batched after it, the mirrored pass.
+    const size_t vall = v + n_past + n_known;
+    const size_t keep = std::min(t0, o.max_context);
+    const size_t t = (keep + ps - 1) / ps * ps;
+    const size_t hpad = (horizon + ps - 1) / ps * ps;
+    const int passes = o.symmetric_averaging ? 2 : 1;
+    HostRows fwd, mir;
+    prepare_rows(inputs, observed, b, v, t0, horizon, past_rows.data(), n_past, known_rows.data(), n_known, keep, t,
+                 hpad, fwd);
+    if (passes == 2) {
+        std::vector<float> neg(b * v * t0), npast(past_rows.size()), nknown(known_rows.size());
+        for (size_t i = 0; i < neg.size(); ++i) neg[i] = -inputs[i];
+        for (size_t i = 0; i < npast.size(); ++i) npast[i] = -past_rows[i];
+        for (size_t i = 0; i < nknown.size(); ++i) nknown[i] = -known_rows[i];
+        prepare_rows(neg.data(), observed, b, v, t0, horizon, npast.data(), n_past, nknown.data(), n_known, keep, t,
+                     hpad, mir);
+    }
+    const int64_t groups = (int64_t)b * passes, R = groups * (int64_t)vall;
+    std::vector<float> rows0(R * t), kf(R * hpad);
+    std::vector<uint8_t> mask0(R * t), kfm(R * hpad);
+    std::memcpy(rows0.data(), fwd.rows.data(), fwd.rows.size() * 4);
+    std::memcpy(mask0.data(), fwd.mask.data(), fwd.mask.size());
+    std::memcpy(kf.data(), fwd.kf.data(), fwd.kf.size() * 4);
+    std::memcpy(kfm.data(), fwd.kfm.data(), fwd.kfm.size());
+    if (passes == 2) {
+        std::memcpy(rows0.data() + fwd.rows.size(), mir.rows.data(), mir.rows.size() * 4);
+        std::memcpy(mask0.data() + fwd.mask.size(), mir.mask.data(), mir.mask.size());
+        std::memcpy(kf.data() + fwd.kf.size(), mir.kf.data(), mir.kf.size() * 4);
+        std::memcpy(kfm.data() + fwd.kfm.size(), mir.kfm.data(), mir.kfm.size());
+    }
+    // Non-negative clip flags per (series, variate) (forecaster.zig:163-180).
+    std::vector<uint8_t> clip_row(b * v, 0);
+    if (o.clip_nonnegative)
+        for (size_t rr = 0; rr < b * v; ++rr) {
+            bool any = false, nonneg = true;
+            for (size_t i = 0; i < t0; ++i)
+                if (observed[rr * t0 + i] && std::isfinite(inputs[rr * t0 + i])) {
+                    any = true;
+                    nonneg = nonneg && inputs[rr * t0 + i] >= 0;
+                }
+            clip_row[rr] = any && nonneg;
+        }
+
+    // Roles of one series' rows: targets, past-only, known-future.
+    std::vector<int8_t> roles(vall);
+    for (size_t i = 0; i < vall; ++i) roles[i] = i < v ? 0 : (i < v + n_past ? 1 : 2);
+    w.roles_host.assign(roles.begin(), roles.end());
+    const bool covw = vall > v;
+    const int64_t nt = groups * (int64_t)v;
+    const int med = median_index(c);
+
+    // Device buffers that live across blocks.
+    const int64_t max_t = std::max<int64_t>((int64_t)t, (int64_t)std::max<size_t>(ps, o.max_context / ps * ps)) + hpad;
+    size_t fc_bytes = Arena::span(R * t * 4) + Arena::span(R * t) + 2 * Arena::span(R * max_t * 4) +
+                      2 * Arena::span(R * max_t) + Arena::span(R * hpad * 4) + Arena::span(R * hpad) +
+                      Arena::span(nt * horizon * q * 4) * 2 + Arena::span(nt * o.per_shot_horizon_patches * ps * q * 4) +
+                      Arena::span(b * v) + Arena::span(vall) + Arena::span(16);
+    TSFM_TRY(r.fc.reserve(fc_bytes));
+    Arena &fc = r.fc;
+    fc.reset();
+    float *d_rows0 = fc.take<float>(R * t);
+    uint8_t *d_mask0 = fc.take<uint8_t>(R * t);
+    float *ctx_a = fc.take<float>(R * max_t), *ctx_b = fc.take<float>(R * max_t);
+    uint8_t *msk_a = fc.take<uint8_t>(R * max_t), *msk_b = fc.take<uint8_t>(R * max_t);
+    float *d_kf = fc.take<float>(R * hpad);
+    uint8_t *d_kfm = fc.take<uint8_t>(R * hpad);
+    float *d_raw = fc.take<float>(nt * horizon * q);
+    float *d_out = fc.take<float>(nt * horizon * q);
+    float *d_qs = fc.take<float>(nt * (int64_t)o.per_shot_horizon_patches * ps * q);
+    uint8_t *d_clip = fc.take<uint8_t>(b * v);
+    int8_t *d_roles = fc.take<int8_t>(vall);
+    int *d_nan = fc.take<int>(4);
+    if (fc.used > fc.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Timestral: forecaster buffers too small");
+    cudaStream_t s = r.stream;
+    TSFM_CUDA(cudaMemcpyAsync(d_rows0, rows0.data(), rows0.size() * 4, cudaMemcpyHostToDevice, s), "timestral: rows");
+    TSFM_CUDA(cudaMemcpyAsync(d_mask0, mask0.data(), mask0.size(), cudaMemcpyHostToDevice, s), "timestral: mask");
+    TSFM_CUDA(cudaMemcpyAsync(ctx_a, rows0.data(), rows0.size() * 4, cudaMemcpyHostToDevice, s), "timestral: rows");
+    TSFM_CUDA(cudaMemcpyAsync(msk_a, mask0.data(), mask0.size(), cudaMemcpyHostToDevice, s), "timestral: mask");
+    TSFM_CUDA(cudaMemcpyAsync(d_kf, kf.data(), kf.size() * 4, cudaMemcpyHostToDevice, s), "timestral: known");
+    TSFM_CUDA(cudaMemcpyAsync(d_kfm, kfm.data(), kfm.size(), cudaMemcpyHostToDevice, s), "timestral: known");
+    TSFM_CUDA(cudaMemcpyAsync(d_clip, clip_row.data(), clip_row.size(), cudaMemcpyHostToDevice, s), "timestral: clip");
+    TSFM_CUDA(cudaMemcpyAsync(d_roles, roles.data(), vall, cudaMemcpyHostToDevice, s), "timestral: roles");
+    TSFM_CUDA(cudaMemsetAsync(d_nan, 0, 16, s), "timestral: nan flag");
+    w.roles = d_roles;
+
+    // blockDecode (timestral/forecaster.zig:423-563), groups chunked by the workspace budget.
+    int64_t tcur = (int64_t)t;
+    float *ctx = ctx_a, *nctx = ctx_b;
+    uint8_t *cm = msk_a, *nm = msk_b;
+    int64_t remaining = (int64_t)(horizon + ps - 1) / ps, done = 0;
+    const bool known_any = n_known > 0;
+    while (remaining > 0) {
+        const int64_t block = std::min<int64_t>((int64_t)o.per_shot_horizon_patches, remaining), blen = block * ps;
+        Block k{groups, (int64_t)vall, (int64_t)v, tcur, block, ps, covw};
+        const size_t per_group = block_workspace(c, w, Block{1, (int64_t)vall, (int64_t)v, tcur, block, ps, covw});
+        int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(groups, (int64_t)(workspace_budget(r) / std::max<size_t>(per_group, 1))));
+        const int64_t nchunks = (groups + chunk - 1) / chunk;
+        chunk = (groups + nchunks - 1) / nchunks;
+        Block kc = k;
+        kc.groups = chunk;
+        TSFM_TRY(r.ws.reserve(block_workspace(c, w, kc)));
+        for (int64_t g0 = 0; g0 < groups; g0 += chunk) {
+            Block kk = k;
+            kk.groups = std::min(chunk, groups - g0);
+            const int64_t r0 = g0 * (int64_t)vall;
+            TSFM_TRY(predict_block(r, c, w, kk, ctx + r0 * tcur, cm + r0 * tcur, known_any ? d_kf + r0 * hpad + done : nullptr,
+                                   known_any ? d_kfm + r0 * hpad + done : nullptr, (int64_t)hpad,
+                                   d_qs + g0 * (int64_t)v * blen * q, s));
+        }
+        if (block > 1) {
+            TsRefineCall rc;
+            rc.qs = d_qs;
+            rc.ctx = ctx;
+            rc.mask = cm;
+            rc.t = tcur;
+            rc.groups = groups;
+            rc.vall = (int)vall;
+            rc.v = (int)v;
+            rc.ps = (int)ps;
+            rc.h = (int)block;
+            rc.q = (int)q;
+            rc.med = med;
+            rc.min_scale = c.minimum_scale;
+            LaunchScope ls(r, s, K_HEAD, (double)nt * tcur * 8);
+            TSFM_TRY(launch_ts_refine(rc, s));
+        }
+        {
+            LaunchScope ls(r, s, K_OTHER, (double)nt * blen * q * 8);
+            TSFM_TRY(launch_ts_store(d_qs, d_raw, nt, blen, (int)q, (int64_t)horizon, done, s));
+        }
+        remaining -= block;
+        done += blen;
+        if (remaining == 0) break;
+        const int64_t nt_len = tcur + blen;
+        const int64_t keep_t = nt_len > (int64_t)o.max_context
+                                   ? std::max<int64_t>(ps, (int64_t)o.max_context / ps * ps)
+                                   : nt_len;
+        if (keep_t > max_t) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "Timestral: context buffer too small");
+        TsFeedbackCall fb;
+        fb.ctx = ctx;
+        fb.mask = cm;
+        fb.t = tcur;
+        fb.rows = R;
+        fb.keep_t = keep_t;
+        fb.blen = blen;
+        fb.qs = d_qs;
+        fb.q = (int)q;
+        fb.med = med;
+        fb.vall = (int)vall;
+        fb.v = (int)v;
+        fb.roles = d_roles;
+        fb.kf = d_kf;
+        fb.kfm = d_kfm;
+        fb.hpad = (int64_t)hpad;
+        fb.done = done - blen;
+        fb.extreme = o.extreme_value_threshold;
+        fb.nctx = nctx;
+        fb.nmask = nm;
+        {
+            LaunchScope ls(r, s, K_OTHER, (double)R * keep_t * 10);
+            TSFM_TRY(launch_ts_feedback(fb, s));
+        }
+        std::swap(ctx, nctx);
+        std::swap(cm, nm);
+        tcur = keep_t;
+    }
+    // Quantile cap + NaN check (forecaster.zig:396-419), then the symmetric average and clip.
+    {
+        TsCapCall cc;
+        cc.out = d_raw;
+        cc.rows_ctx = d_rows0;
+        cc.mask = d_mask0;
+        cc.t = (int64_t)t;
+        cc.groups = groups;
+        cc.horizon = (int64_t)horizon;
+        cc.vall = (int)vall;
+        cc.v = (int)v;
+        cc.q = (int)q;
+        cc.cap_k = o.quantile_real_cap_k;
+        cc.min_scale = c.minimum_scale;
+        cc.nan_flag = d_nan;
+        LaunchScope ls(r, s, K_OTHER, (double)nt * (t * 5 + horizon * q * 8));
+        TSFM_TRY(launch_ts_cap(cc, s));
+    }
+    {
+        const int64_t rows_out = (int64_t)(b * v);
+        LaunchScope ls(r, s, K_OTHER, (double)rows_out * horizon * q * 12);
+        TSFM_TRY(launch_ts_finish(d_raw, passes == 2 ? d_raw + rows_out * horizon * q : nullptr,
+                                  o.clip_nonnegative ? d_clip : nullptr, d_out, rows_out, (int64_t)horizon, (int)q, s));
+    }
+    int nan_flag = 0;
+    TSFM_CUDA(cudaMemcpyAsync(&nan_flag, d_nan, 4, cudaMemcpyDeviceToHost, s), "timestral: nan flag");
+    TSFM_CUDA(cudaMemcpyAsync(out, d_out, b * v * horizon * q * 4, cudaMemcpyDeviceToHost, s), "timestral: results");
+    TSFM_CUDA(cudaStreamSynchronize(s), "timestral");
+    if (nan_flag) return Status::fail(TSFM_ERR_DEGENERATE_INPUT, "DegenerateInput: a forecast is NaN");
+    return Status::ok();
+}
+
+}  // namespace tsfm

@@ -1,0 +1,552 @@
+// Kernels specific to Timestral (timestral/model.zig, timestral/forecaster.zig): per-row causal
+// statistics and patch features, per-group RoPE tables, the attention gate and SwiGLU
+// activations, the 11x11 variate attention, the monotone quantile head, the refine frame, the
+// block feedback, the quantile cap and the symmetric average. Rows of one series are
+// contiguous and ordered targets, past-only covariates, known-future covariates.
+#include <cfloat>
+#include <climits>
+
+#include "kernels.h"
+#include "ptx.cuh"
+#include "timestral_kernels.h"
+
+#include <cuda_fp16.h>
+
+namespace tsfm {
+
+namespace {
+
+__device__ __forceinline__ float load16(const void *p, int64_t i, int dtype) {
+    if (dtype == E_F16) return __half2float(static_cast<const __half *>(p)[i]);
+    return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+}
+__device__ __forceinline__ void store16(void *p, int64_t i, int dtype, float v) {
+    if (dtype == E_F16)
+        static_cast<__half *>(p)[i] = __float2half_rn(v);
+    else
+        static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+}
+
+int grid_for(int64_t total, int block) {
+    const int64_t g = (total + block - 1) / block;
+    const int64_t cap = (int64_t)num_sms() * 16;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(g, cap));
+}
+
+// Window value / observation at step i of row r: the context, then (with covariates) the known
+// futures or blanks (timestral/model.zig:253-274).
+struct Win {
+    const TsStatsCall &c;
+    __device__ float x(int64_t r, int64_t i) const {
+        if (i < c.t) return c.ctx[r * c.t + i];
+        return c.kf ? c.kf[r * c.kf_ld + (i - c.t)] : 0.0f;
+    }
+    __device__ bool o(int64_t r, int64_t i) const {
+        if (i < c.t) return c.obs[r * c.t + i] != 0;
+        return c.kfm ? c.kfm[r * c.kf_ld + (i - c.t)] != 0 : false;
+    }
+};
+
+// One thread per row: causal per-patch Welford statistics (StatsJob.run,
+// timestral/model.zig:712-750), whole-row statistics of known-future rows (model.zig:285-305),
+// key validity and the group's first observed patch (model.zig:344-362).
+__global__ void ts_stats_kernel(TsStatsCall c) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= c.rows) return;
+    const Win W{c};
+    const int64_t w = c.cov ? c.t + c.hl : c.t, n = w / c.ps;
+    const bool known = c.cov && c.roles[r % c.vall] == 2;
+    double cum_w = 0, cum_x = 0, m2 = 0, prev = 0;
+    bool started = false;
+    int first = INT_MAX;
+    for (int64_t p = 0; p < n; ++p) {
+        bool any = false;
+        for (int k = 0; k < c.ps; ++k) {
+            const int64_t i = p * c.ps + k;
+            const bool ob = W.o(r, i);
+            const double wg = ob ? 1.0 : 0.0, x = (double)W.x(r, i);
+            cum_w += wg;
+            cum_x += wg * x;
+            const double den = fmax(cum_w, 1.0);
+            const double mean = cum_x / den;
+            m2 += (x - prev) * (x - mean) * wg;
+            prev = mean;
+            any = any || ob;
+        }
+        const double den = fmax(cum_w, 1.0);
+        const double var = m2 / fmax(den - 1.0, 1.0);
+        c.loc[r * n + p] = (float)prev;
+        c.scale[r * n + p] = (float)fmax(sqrt(var), c.min_scale);
+        if (any && first == INT_MAX) first = (int)p;
+        started = started || any;
+        c.key_valid[r * n + p] = c.attend_missing ? (any || started) : any;
+    }
+    if (first != INT_MAX) atomicMin(&c.first_obs[r / c.vall], first);
+    float kl = 0.0f, ks = 1.0f;
+    uint8_t bin = 0;
+    if (known) {
+        float cnt = 0.0f, sum = 0.0f;
+        bool zero_one = true, anyo = false;
+        for (int64_t i = 0; i < w; ++i)
+            if (W.o(r, i)) {
+                const float x = W.x(r, i);
+                cnt += 1.0f;
+                sum += x;
+                zero_one = zero_one && (x == 0.0f || x == 1.0f);
+                anyo = true;
+            }
+        kl = sum / fmaxf(cnt, 1.0f);
+        float ss = 0.0f;
+        for (int64_t i = 0; i < w; ++i)
+            if (W.o(r, i)) {
+                const float dv = W.x(r, i) - kl;
+                ss += dv * dv;
+            }
+        ks = fmaxf(sqrtf(ss / fmaxf(cnt, 1.0f)), (float)c.min_scale);
+        bin = zero_one && anyo;
+        if (bin) {
+            kl = 0.0f;
+            ks = 1.0f;
+        }
+    }
+    c.kloc[r] = kl;
+    c.kscale[r] = ks;
+    c.binary[r] = bin;
+}
+
+// Patch features [asinh((x - loc_p) / scale_p), missing] per step (timestral/model.zig:306-327).
+__global__ void ts_feat_kernel(TsStatsCall c, float *feats) {
+    const Win W{c};
+    const int64_t w = c.cov ? c.t + c.hl : c.t, n = w / c.ps;
+    const int64_t total = c.rows * w;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = idx / w, j = idx % w, p = j / c.ps;
+        const int i = (int)(j % c.ps);
+        const bool known = c.cov && c.roles[r % c.vall] == 2;
+        const float lo = known ? c.kloc[r] : c.loc[r * n + p];
+        const float sc = fmaxf(known ? c.kscale[r] : c.scale[r * n + p], FLT_EPSILON);
+        const bool ob = W.o(r, j);
+        float v = 0.0f;
+        if (ob) {
+            v = (W.x(r, j) - lo) / sc;
+            if (c.use_asinh && !(known && c.binary[r])) v = asinhf(v);
+        }
+        float *dst = feats + (r * n + p) * 2 * c.ps;
+        dst[i] = to_tf32(v);
+        dst[c.ps + i] = ob ? 0.0f : 1.0f;
+    }
+}
+
+// cos / sin of rotate-half RoPE per (group, token): encoder token p sits at time p, decoder
+// token j at l + j, both relative to the group's first observed patch (model.zig:449-463).
+__global__ void ts_rope_kernel(const int *first_obs, int64_t groups, int64_t sl, int64_t ne, int64_t l,
+                               const float *inv_freq, int half, float *cs, float *sn) {
+    const int64_t total = groups * sl * half;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(idx % half);
+        const int64_t tok = (idx / half) % sl, g = idx / (half * sl);
+        int64_t fo = first_obs[g];
+        if (fo >= ne) fo = 0;
+        const int64_t time = tok < ne ? tok : l + tok - ne;
+        const float ang = inv_freq[i] * (float)(time - fo);
+        cs[idx] = cosf(ang);
+        sn[idx] = sinf(ang);
+    }
+}
+
+// o = o * sigmoid(g) (nn.mulSigmoid, core/nn.zig:423-433).
+__global__ void ts_gate_kernel(void *o, int64_t ldo, const void *g, int64_t ldg, int64_t rows, int64_t d, int dtype) {
+    const int64_t total = rows * d;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = idx / d, j = idx % d;
+        const float x = load16(o, r * ldo + j, dtype), gv = load16(g, r * ldg + j, dtype);
+        store16(o, r * ldo + j, dtype, x / (1.0f + expf(-gv)));
+    }
+}
+
+// a = gate * silu(up) with [gate | up] per row (MlpAct.run, timestral/model.zig:159-165).
+__global__ void ts_swiglu_kernel(const void *h, void *a, int64_t rows, int64_t hid, int dtype) {
+    const int64_t total = rows * hid;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = idx / hid, j = idx % hid;
+        const float gt = load16(h, r * 2 * hid + j, dtype), up = load16(h, r * 2 * hid + hid + j, dtype);
+        store16(a, idx, dtype, gt * (up / (1.0f + expf(-up))));
+    }
+}
+
+// Variate attention (VariateJob.run, timestral/model.zig:648-709): at each (group, token) the
+// group's rows attend to each other per head. One warp per (group, token, head); each lane owns
+// head dims (2 lane, 2 lane + 1).
+constexpr int kMaxRows = 16;
+__global__ void ts_variate_kernel(TsVariateCall c) {
+    const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t total = c.groups * c.sl * c.heads;
+    if (wid >= total) return;
+    const int h = (int)(wid % c.heads);
+    const int64_t tok = (wid / c.heads) % c.sl, g = wid / (c.heads * c.sl);
+    const int64_t r0 = g * c.vall;
+    float q0[kMaxRows], q1[kMaxRows], k0[kMaxRows], k1[kMaxRows];
+    for (int i = 0; i < c.vall; ++i) {
+        const int64_t row = (r0 + i) * c.sl + tok;
+        const int64_t base = row * c.ld + h * 64 + 2 * lane;
+        q0[i] = load16(c.qkv, base, c.dtype);
+        q1[i] = load16(c.qkv, base + 1, c.dtype);
+        k0[i] = load16(c.qkv, base + c.d, c.dtype);
+        k1[i] = load16(c.qkv, base + c.d + 1, c.dtype);
+    }
+    for (int iq = 0; iq < c.vall; ++iq) {
+        float s[kMaxRows];
+        float mx = -INFINITY;
+        for (int ik = 0; ik < c.vall; ++ik) {
+            bool ok = ik == iq;
+            if (!ok) {
+                const bool valid = tok >= c.ne || c.key_valid[(r0 + ik) * c.ne + tok] != 0;
+                bool forbidden = false;
+                if (c.cov) {
+                    const int rq = c.roles[iq], rk = c.roles[ik];
+                    forbidden = (rq != 0 && rk == 0) || (rq == 2 && rk != 2);
+                }
+                ok = valid && !forbidden;
+            }
+            float dot = q0[iq] * k0[ik] + q1[iq] * k1[ik];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            s[ik] = ok ? dot * c.scale : -INFINITY;
+            mx = fmaxf(mx, s[ik]);
+        }
+        float sum = 0.0f;
+        for (int ik = 0; ik < c.vall; ++ik) {
+            s[ik] = s[ik] == -INFINITY ? 0.0f : expf(s[ik] - mx);
+            sum += s[ik];
+        }
+        const float inv = 1.0f / sum;
+        float o0 = 0.0f, o1 = 0.0f;
+        for (int ik = 0; ik < c.vall; ++ik) {
+            const float p = s[ik] * inv;
+            if (p == 0.0f) continue;
+            const int64_t base = ((r0 + ik) * c.sl + tok) * c.ld + 2 * c.d + h * 64 + 2 * lane;
+            o0 += p * load16(c.qkv, base, c.dtype);
+            o1 += p * load16(c.qkv, base + 1, c.dtype);
+        }
+        const int64_t ob = ((r0 + iq) * c.sl + tok) * c.ldo + h * 64 + 2 * lane;
+        store16(c.o, ob, c.dtype, o0);
+        store16(c.o, ob + 1, c.dtype, o1);
+    }
+}
+
+__device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// nn.clampNonfinite (core/nn.zig:522-563) over q values.
+__device__ void clamp_nonfinite(float *v, int q) {
+    float hi = -INFINITY, lo = INFINITY;
+    bool any_inf = false;
+    for (int i = 0; i < q; ++i) {
+        if (isfinite(v[i])) {
+            hi = fmaxf(hi, v[i]);
+            lo = fminf(lo, v[i]);
+        } else if (isinf(v[i])) {
+            any_inf = true;
+        }
+    }
+    if (!any_inf) return;
+    for (int i = 0; i < q; ++i) {
+        if (v[i] == INFINITY) v[i] = hi;
+        if (v[i] == -INFINITY) v[i] = lo;
+        if (isinf(v[i])) v[i] = 0.0f;
+    }
+}
+
+// Monotone quantile head and back-transform (timestral/model.zig:379-431): median free, the
+// others at cumulative softplus offsets, then sinh(.) * scale + loc of the anchor frame (the
+// last context patch), then clampNonfinite. One thread per (target row, step).
+constexpr int kMaxQ = 32;
+__global__ void ts_head_kernel(TsHeadCall c) {
+    const int64_t total = c.nt * c.hl;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t oi = idx / c.hl;
+        const int64_t r = c.target_row[oi];
+        const float lo = c.loc[r * c.n + c.l - 1], sc = c.scale[r * c.n + c.l - 1];
+        const float *rv = c.raw + idx * c.q;
+        float ov[kMaxQ];
+        const float med = rv[c.m];
+        float acc = 0.0f;
+        for (int i = c.m + 1; i < c.q; ++i) {
+            acc += c.wf * c.widths[i] * softplus(rv[i]);
+            ov[i] = fminf(fmaxf(med + acc, -FLT_MAX), FLT_MAX);
+        }
+        acc = 0.0f;
+        for (int i = c.m - 1; i >= 0; --i) {
+            acc += c.wf * c.widths[i] * softplus(rv[i]);
+            ov[i] = fminf(fmaxf(med - acc, -FLT_MAX), FLT_MAX);
+        }
+        ov[c.m] = med;
+        for (int i = 0; i < c.q; ++i) {
+            const float y = c.use_asinh ? sinhf(ov[i]) : ov[i];
+            ov[i] = y * sc + lo;
+        }
+        clamp_nonfinite(ov, c.q);
+        for (int i = 0; i < c.q; ++i) c.out[idx * c.q + i] = ov[i];
+    }
+}
+
+struct Welford {
+    double w, mean, m2;
+};
+__device__ Welford combine(Welford a, Welford b) {  // timestral/forecaster.zig:567-577
+    const double w = a.w + b.w;
+    if (w == 0) return {0, 0, 0};
+    const double w_safe = fmax(w, DBL_MIN);
+    const double delta = b.mean - a.mean;
+    return {w, a.mean + delta * b.w / w_safe, a.m2 + b.m2 + delta * delta * a.w * b.w / w_safe};
+}
+
+// refineBlock (timestral/forecaster.zig:582-662): one thread per target row moves the block
+// from the anchor frame to the advancing refine frame.
+constexpr int kMaxBlock = 64;
+__global__ void ts_refine_kernel(TsRefineCall c) {
+    const int64_t tr = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (tr >= c.groups * c.v) return;
+    const int64_t g = tr / c.v, i = tr % c.v, r = g * c.vall + i;
+    const float *row = c.ctx + r * c.t;
+    const uint8_t *msk = c.mask + r * c.t;
+    const int64_t l = c.t / c.ps;
+    // Causal statistics at the last context patch (the anchor frame).
+    double cum_w = 0, cum_x = 0, m2 = 0, prev = 0;
+    for (int64_t j = 0; j < c.t; ++j) {
+        const double wg = msk[j] ? 1.0 : 0.0, x = (double)row[j];
+        cum_w += wg;
+        cum_x += wg * x;
+        const double mean = cum_x / fmax(cum_w, 1.0);
+        m2 += (x - prev) * (x - mean) * wg;
+        prev = mean;
+    }
+    const float loc0 = (float)prev;
+    const float scale0 = (float)fmax(sqrt(m2 / fmax(fmax(cum_w, 1.0) - 1.0, 1.0)), c.min_scale);
+    float *block = c.qs + tr * c.h * c.ps * c.q;
+    Welford st{0, 0, 0};
+    for (int64_t p = 0; p < l; ++p) {
+        double cnt = 0, sum = 0;
+        for (int k = 0; k < c.ps; ++k)
+            if (msk[p * c.ps + k]) {
+                cnt += 1;
+                sum += row[p * c.ps + k];
+            }
+        Welford pm{cnt, 0, 0};
+        if (cnt > 0) {
+            pm.mean = sum / fmax(cnt, 1.0);
+            for (int k = 0; k < c.ps; ++k)
+                if (msk[p * c.ps + k]) {
+                    const double dv = (double)row[p * c.ps + k] - pm.mean;
+                    pm.m2 += dv * dv;
+                }
+        }
+        st = combine(st, pm);
+    }
+    const double clip = sqrt((double)FLT_MAX) / 1e3;
+    const double offset = st.mean;
+    float loc_j[kMaxBlock], scale_j[kMaxBlock];
+    for (int j = 0; j < c.h; ++j) {
+        const double var = fmax(st.m2 / fmax(st.w - 1.0, 1.0), 0.0);
+        const double sc = fmax(sqrt(var), c.min_scale);
+        loc_j[j] = (float)st.mean;
+        scale_j[j] = (float)sc;
+        double bsum = 0;
+        for (int k = 0; k < c.ps; ++k) {
+            const double sm = ((double)block[(j * c.ps + k) * c.q + c.med] - (double)loc0) / (double)scale0;
+            bsum += fmin(fmax(sm * sc + st.mean - offset, -clip), clip) + offset;
+        }
+        const double bmean = bsum / (double)c.ps;
+        double bm2 = 0;
+        for (int k = 0; k < c.ps; ++k) {
+            const double sm = ((double)block[(j * c.ps + k) * c.q + c.med] - (double)loc0) / (double)scale0;
+            const double f = fmin(fmax(sm * sc + st.mean - offset, -clip), clip) + offset;
+            bm2 += (f - bmean) * (f - bmean);
+        }
+        st = combine(st, {(double)c.ps, bmean, bm2});
+    }
+    loc_j[0] = loc0;
+    scale_j[0] = scale0;
+    for (int64_t s = 0; s < (int64_t)c.h * c.ps; ++s) {
+        float *rowq = block + s * c.q;
+        const float lj = loc_j[s / c.ps], sj = scale_j[s / c.ps];
+        for (int k = 0; k < c.q; ++k) rowq[k] = (rowq[k] - loc0) / scale0 * sj + lj;
+        clamp_nonfinite(rowq, c.q);
+    }
+}
+
+// Store a decoded block into the (targets, horizon, q) output and build the next context
+// (timestral/forecaster.zig:502-560).
+__global__ void ts_store_kernel(const float *qs, float *out, int64_t nt, int64_t blen, int q, int64_t horizon,
+                                int64_t done) {
+    const int64_t total = nt * blen * q;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t rt = idx / (blen * q), s = (idx / q) % blen;
+        if (done + s < horizon) out[(rt * horizon + done + s) * q + idx % q] = qs[idx];
+    }
+}
+
+__global__ void ts_feedback_kernel(TsFeedbackCall c) {
+    const int64_t total = c.rows * c.keep_t;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = idx / c.keep_t, j = idx % c.keep_t;
+        const int64_t nt_len = c.t + c.blen, start = nt_len - c.keep_t;
+        const int64_t ncopy = start < c.t ? c.t - start : 0;
+        float val;
+        uint8_t ob;
+        if (j < ncopy) {
+            val = c.ctx[r * c.t + start + j];
+            ob = c.mask[r * c.t + start + j];
+        } else {
+            const int64_t s = (start < c.t ? 0 : start - c.t) + (j - ncopy);
+            const int role = c.roles[r % c.vall];
+            if (role == 0) {
+                const int64_t trow = (r / c.vall) * c.v + (r % c.vall);
+                float m = c.qs[(trow * c.blen + s) * c.q + c.med];
+                if (!isfinite(m) || fabsf(m) >= c.extreme) m = 0.0f;
+                val = m;
+                ob = 1;
+            } else if (role == 2) {
+                val = c.kf[r * c.hpad + c.done + s];
+                ob = c.kfm[r * c.hpad + c.done + s];
+            } else {
+                val = 0.0f;
+                ob = 0;
+            }
+        }
+        c.nctx[idx] = val;
+        c.nmask[idx] = ob;
+    }
+}
+
+// Quantile cap (timestral/forecaster.zig:396-418) and the NaN check (:419): one thread per target
+// row computes the statistics of its initial context, then clamps its (horizon, q) block.
+__global__ void ts_cap_kernel(TsCapCall c) {
+    const int64_t tr = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (tr >= c.groups * c.v) return;
+    const int64_t r = (tr / c.v) * c.vall + tr % c.v;
+    const float *row = c.rows_ctx + r * c.t;
+    const uint8_t *msk = c.mask + r * c.t;
+    float *o = c.out + tr * c.horizon * c.q;
+    if (c.cap_k > 0.0f) {
+        double cum_w = 0, cum_x = 0, m2 = 0, prev = 0;
+        float mx = -INFINITY, mn = INFINITY;
+        for (int64_t j = 0; j < c.t; ++j) {
+            const double wg = msk[j] ? 1.0 : 0.0, x = (double)row[j];
+            cum_w += wg;
+            cum_x += wg * x;
+            const double mean = cum_x / fmax(cum_w, 1.0);
+            m2 += (x - prev) * (x - mean) * wg;
+            prev = mean;
+            if (msk[j]) {
+                mx = fmaxf(mx, row[j]);
+                mn = fminf(mn, row[j]);
+            }
+        }
+        const float scale_last = (float)fmax(sqrt(m2 / fmax(fmax(cum_w, 1.0) - 1.0, 1.0)), c.min_scale);
+        if (isinf(mx)) mx = 0.0f;
+        if (isinf(mn)) mn = 0.0f;
+        const float a = scale_last * c.cap_k;
+        for (int64_t k = 0; k < c.horizon * c.q; ++k) o[k] = fminf(fmaxf(o[k], mn - a), mx + a);
+    }
+    for (int64_t k = 0; k < c.horizon * c.q; ++k)
+        if (isnan(o[k])) atomicOr(c.nan_flag, 1);
+}
+
+// Symmetric averaging 0.5 * (a_j - m_{q-1-j}) and the non-negative clip
+// (timestral/forecaster.zig:132-136, 163-180).
+__global__ void ts_finish_kernel(const float *fwd, const float *mir, const uint8_t *clip_row, float *out, int64_t rows,
+                                 int64_t horizon, int q) {
+    const int64_t total = rows * horizon * q;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        const int j = (int)(idx % q);
+        const int64_t base = idx - j, r = idx / (horizon * q);
+        float v = fwd[idx];
+        if (mir) v = 0.5f * (v + -mir[base + (q - 1 - j)]);
+        if (clip_row && clip_row[r]) v = fmaxf(v, 0.0f);
+        out[idx] = v;
+    }
+}
+
+}  // namespace
+
+Status launch_ts_stats(const TsStatsCall &c, float *feats, cudaStream_t s) {
+    if (c.rows <= 0) return Status::ok();
+    ts_stats_kernel<<<(unsigned)((c.rows + 127) / 128), 128, 0, s>>>(c);
+    TSFM_CUDA(cudaGetLastError(), "timestral stats: launch");
+    const int64_t w = c.cov ? c.t + c.hl : c.t;
+    ts_feat_kernel<<<grid_for(c.rows * w, 256), 256, 0, s>>>(c, feats);
+    TSFM_CUDA(cudaGetLastError(), "timestral features: launch");
+    return Status::ok();
+}
+
+Status launch_ts_rope(const int *first_obs, int64_t groups, int64_t sl, int64_t ne, int64_t l, const float *inv_freq,
+                      int half, float *cs, float *sn, cudaStream_t s) {
+    ts_rope_kernel<<<grid_for(groups * sl * half, 256), 256, 0, s>>>(first_obs, groups, sl, ne, l, inv_freq, half, cs, sn);
+    TSFM_CUDA(cudaGetLastError(), "timestral rope: launch");
+    return Status::ok();
+}
+
+Status launch_ts_gate(void *o, int64_t ldo, const void *g, int64_t ldg, int64_t rows, int64_t d, int dtype, cudaStream_t s) {
+    ts_gate_kernel<<<grid_for(rows * d, 256), 256, 0, s>>>(o, ldo, g, ldg, rows, d, dtype);
+    TSFM_CUDA(cudaGetLastError(), "timestral gate: launch");
+    return Status::ok();
+}
+
+Status launch_ts_swiglu(const void *h, void *a, int64_t rows, int64_t hid, int dtype, cudaStream_t s) {
+    ts_swiglu_kernel<<<grid_for(rows * hid, 256), 256, 0, s>>>(h, a, rows, hid, dtype);
+    TSFM_CUDA(cudaGetLastError(), "timestral swiglu: launch");
+    return Status::ok();
+}
+
+Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s) {
+    if (c.vall > kMaxRows) return Status::fail(TSFM_ERR_UNSUPPORTED, "Timestral: more than 16 rows per series");
+    const int64_t warps = c.groups * c.sl * c.heads;
+    ts_variate_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(c);
+    TSFM_CUDA(cudaGetLastError(), "timestral variate attention: launch");
+    return Status::ok();
+}
+
+Status launch_ts_head(const TsHeadCall &c, cudaStream_t s) {
+    if (c.q > kMaxQ) return Status::fail(TSFM_ERR_UNSUPPORTED, "Timestral: more than 32 quantiles");
+    ts_head_kernel<<<grid_for(c.nt * c.hl, 128), 128, 0, s>>>(c);
+    TSFM_CUDA(cudaGetLastError(), "timestral head: launch");
+    return Status::ok();
+}
+
+Status launch_ts_refine(const TsRefineCall &c, cudaStream_t s) {
+    if (c.h > kMaxBlock) return Status::fail(TSFM_ERR_UNSUPPORTED, "Timestral: block longer than 64 patches");
+    const int64_t n = c.groups * c.v;
+    ts_refine_kernel<<<(unsigned)((n + 63) / 64), 64, 0, s>>>(c);
+    TSFM_CUDA(cudaGetLastError(), "timestral refine: launch");
+    return Status::ok();
+}
+
+Status launch_ts_store(const float *qs, float *out, int64_t nt, int64_t blen, int q, int64_t horizon, int64_t done,
+                       cudaStream_t s) {
+    ts_store_kernel<<<grid_for(nt * blen * q, 256), 256, 0, s>>>(qs, out, nt, blen, q, horizon, done);
+    TSFM_CUDA(cudaGetLastError(), "timestral store: launch");
+    return Status::ok();
+}
+
+Status launch_ts_feedback(const TsFeedbackCall &c, cudaStream_t s) {
+    ts_feedback_kernel<<<grid_for(c.rows * c.keep_t, 256), 256, 0, s>>>(c);
+    TSFM_CUDA(cudaGetLastError(), "timestral feedback: launch");
+    return Status::ok();
+}
+
+Status launch_ts_cap(const TsCapCall &c, cudaStream_t s) {
+    const int64_t n = c.groups * c.v;
+    ts_cap_kernel<<<(unsigned)((n + 63) / 64), 64, 0, s>>>(c);
+    TSFM_CUDA(cudaGetLastError(), "timestral cap: launch");
+    return Status::ok();
+}
+
+Status launch_ts_finish(const float *fwd, const float *mir, const uint8_t *clip_row, float *out, int64_t rows,
+                        int64_t horizon, int q, cudaStream_t s) {
+    ts_finish_kernel<<<grid_for(rows * horizon * q, 256), 256, 0, s>>>(fwd, mir, clip_row, out, rows, horizon, q);
+    TSFM_CUDA(cudaGetLastError(), "timestral finish: launch");
+    return Status::ok();
+}
+
+}  // namespace tsfm

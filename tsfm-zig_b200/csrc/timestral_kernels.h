@@ -1,0 +1,109 @@
+// Launch interface of the Timestral-specific kernels (timestral_kernels.cu).
+#pragma once
+
+#include "kernels.h"
+
+namespace tsfm {
+
+// Window (context, then known futures or blanks when cov), per-row causal statistics, known-row
+// whole statistics, key validity, first observed patch per group, and patch features.
+struct TsStatsCall {
+    const float *ctx = nullptr;
+    const uint8_t *obs = nullptr;
+    int64_t t = 0;                 // context steps (multiple of ps)
+    const float *kf = nullptr;     // known futures of this block (rows, hl) at row stride kf_ld, or null (blanks)
+    const uint8_t *kfm = nullptr;
+    int64_t kf_ld = 0;
+    int64_t hl = 0;                // horizon steps of this block (h * ps)
+    int cov = 0;                   // covariate window: t + hl steps
+    int64_t rows = 0;
+    int ps = 0, vall = 0;
+    const int8_t *roles = nullptr;  // per row of a group: 0 target, 1 past, 2 known
+    double min_scale = 1e-6;
+    int use_asinh = 1, attend_missing = 1;
+    float *loc = nullptr, *scale = nullptr;     // (rows, n)
+    float *kloc = nullptr, *kscale = nullptr;   // (rows)
+    uint8_t *binary = nullptr;                  // (rows)
+    uint8_t *key_valid = nullptr;               // (rows, n)
+    int *first_obs = nullptr;                   // (groups), initialised to INT_MAX
+};
+Status launch_ts_stats(const TsStatsCall &c, float *feats, cudaStream_t s);
+
+Status launch_ts_rope(const int *first_obs, int64_t groups, int64_t sl, int64_t ne, int64_t l, const float *inv_freq,
+                      int half, float *cs, float *sn, cudaStream_t s);
+Status launch_ts_gate(void *o, int64_t ldo, const void *g, int64_t ldg, int64_t rows, int64_t d, int dtype, cudaStream_t s);
+Status launch_ts_swiglu(const void *h, void *a, int64_t rows, int64_t hid, int dtype, cudaStream_t s);
+
+struct TsVariateCall {
+    const void *qkv = nullptr;  // [rows * sl, ld]: q at h*64, k at d + h*64, v at 2d + h*64
+    int64_t ld = 0, d = 0;
+    void *o = nullptr;
+    int64_t ldo = 0;
+    int dtype = E_F16;
+    int64_t groups = 0, sl = 0, ne = 0;
+    int vall = 0, heads = 0;
+    const uint8_t *key_valid = nullptr;  // (rows, ne)
+    const int8_t *roles = nullptr;
+    int cov = 0;
+    float scale = 0.125f;
+};
+Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s);
+
+struct TsHeadCall {
+    const float *raw = nullptr;  // (nt * hl, q) head outputs
+    float *out = nullptr;        // (nt * hl, q)
+    const float *loc = nullptr, *scale = nullptr;  // (rows, n)
+    const int64_t *target_row = nullptr;           // nt -> row
+    int64_t nt = 0, hl = 0, n = 0, l = 0;
+    int q = 0, m = 0;
+    const float *widths = nullptr;
+    float wf = 2.0f;
+    int use_asinh = 1;
+};
+Status launch_ts_head(const TsHeadCall &c, cudaStream_t s);
+
+struct TsRefineCall {
+    float *qs = nullptr;  // (groups * v, h * ps, q), modified in place
+    const float *ctx = nullptr;
+    const uint8_t *mask = nullptr;
+    int64_t t = 0, groups = 0;
+    int vall = 0, v = 0, ps = 0, h = 0, q = 0, med = 0;
+    double min_scale = 1e-6;
+};
+Status launch_ts_refine(const TsRefineCall &c, cudaStream_t s);
+
+Status launch_ts_store(const float *qs, float *out, int64_t nt, int64_t blen, int q, int64_t horizon, int64_t done,
+                       cudaStream_t s);
+
+struct TsFeedbackCall {
+    const float *ctx = nullptr;
+    const uint8_t *mask = nullptr;
+    int64_t t = 0, rows = 0, keep_t = 0, blen = 0;
+    const float *qs = nullptr;  // (groups * v, blen, q)
+    int q = 0, med = 0, vall = 0, v = 0;
+    const int8_t *roles = nullptr;
+    const float *kf = nullptr;  // (rows, hpad) known futures of the whole horizon
+    const uint8_t *kfm = nullptr;
+    int64_t hpad = 0, done = 0;
+    float extreme = 1e30f;
+    float *nctx = nullptr;
+    uint8_t *nmask = nullptr;
+};
+Status launch_ts_feedback(const TsFeedbackCall &c, cudaStream_t s);
+
+struct TsCapCall {
+    float *out = nullptr;  // (groups * v, horizon, q)
+    const float *rows_ctx = nullptr;
+    const uint8_t *mask = nullptr;
+    int64_t t = 0, groups = 0, horizon = 0;
+    int vall = 0, v = 0, q = 0;
+    float cap_k = 1e4f;
+    double min_scale = 1e-6;
+    int *nan_flag = nullptr;
+};
+Status launch_ts_cap(const TsCapCall &c, cudaStream_t s);
+
+Status launch_ts_finish(const float *fwd, const float *mir, const uint8_t *clip_row, float *out, int64_t rows,
+                        int64_t horizon, int q, cudaStream_t s);
+
+}  // namespace tsfm

@@ -3,7 +3,7 @@ Timestral). The compute lives in libtsfm_b200.so (sm_100a CUDA + C++ behind a C 
 package is its Python binding."""
 from . import config, synthetic
 from ._native import (LIB_PATH, STATUS_NAMES, TsfmError, check, device_count, last_error, lib)
-from .model import Model, tensor_table
+from .model import Model, covariates, tensor_table, timestral_options
 
 __all__ = ["Model", "TsfmError", "config", "synthetic", "lib", "check", "last_error", "device_count",
-           "tensor_table", "LIB_PATH", "STATUS_NAMES"]
+           "tensor_table", "covariates", "timestral_options", "LIB_PATH", "STATUS_NAMES"]

@@ -10,7 +10,7 @@ import ctypes
 import numpy as np
 
 from . import config as config_mod
-from ._native import COMPUTE, DTYPE, Tensor, check, lib
+from ._native import COMPUTE, DTYPE, Covariates, Tensor, TimestralOptions, check, lib
 
 _NP_DTYPE = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16", np.dtype(np.uint16): "BF16"}
 
@@ -31,6 +31,37 @@ def tensor_table(tensors):
         arr[i].dtype = DTYPE[_NP_DTYPE[a.dtype]]
         arr[i].numel = a.size
     return arr, keep
+
+
+def covariates(past=None, known=None, cat_past=None, cat_known=None):
+    """(tsfm_covariates, keep-alive list) over (series, channels, len) arrays
+    (timestral/forecaster.zig:37-46): `past` and `cat_past` cover the context (len = t), `known`
+    and `cat_known` the context plus the horizon (len = t + horizon); NaN marks a missing value.
+    Numeric channels are float32, categorical codes float64."""
+    c, keep = Covariates(), []
+    for name, arr, dt in (("past", past, np.float32), ("known", known, np.float32),
+                          ("cat_past", cat_past, np.float64), ("cat_known", cat_known, np.float64)):
+        if arr is None:
+            continue
+        a = np.ascontiguousarray(arr, dtype=dt)
+        if a.ndim != 3:
+            raise ValueError(f"{name} covariates must be (series, channels, len)")
+        keep.append(a)
+        setattr(c, name, a.ctypes.data)
+        setattr(c, "n_" + name, a.shape[1])
+    return c, keep
+
+
+def timestral_options(**kw):
+    """tsfm_timestral_options with the reference defaults (timestral/forecaster.zig:21-32),
+    overridden by keyword."""
+    o = TimestralOptions()
+    lib.tsfm_timestral_default_options(ctypes.byref(o))
+    for k, v in kw.items():
+        if not hasattr(o, k):
+            raise TypeError(f"unknown Timestral option {k}")
+        setattr(o, k, int(v) if isinstance(v, bool) else v)
+    return o
 
 
 class Model:
@@ -97,6 +128,28 @@ class Model:
 
     def forecast_bolt_device(self, in_ptr, b, t, horizon, out_ptr, stream=0):
         check(lib.tsfm_forecast_bolt_device(self._h, in_ptr, b, t, horizon, out_ptr, stream or None))
+
+    # -- Timestral ------------------------------------------------------------------------------
+    def forecast_timestral(self, inputs, horizon, observed=None, cov=None, opts=None, out=None):
+        """(series, variates, horizon, Q) quantiles after (series, variates, t) `inputs`.
+        `observed` defaults to the finite entries of `inputs` (unobserved steps are passed as 0,
+        as the reference expects). `cov` is a `covariates(...)` pair or None; `opts` a
+        `timestral_options(...)` struct or None for the defaults."""
+        x = np.array(inputs, dtype=np.float32, copy=True)
+        if x.ndim != 3:
+            raise ValueError("inputs must be (series, variates, steps)")
+        if observed is None:
+            observed = np.isfinite(x)
+        obs = np.ascontiguousarray(observed, dtype=np.uint8)
+        x[obs == 0] = 0.0
+        b, v, t = x.shape
+        if out is None:
+            out = np.empty((b, v, horizon, self.num_quantiles), np.float32)
+        cstruct = None if cov is None else ctypes.byref(cov[0] if isinstance(cov, tuple) else cov)
+        ostruct = None if opts is None else ctypes.byref(opts)
+        check(lib.tsfm_forecast_timestral(self._h, x.ctypes.data, obs.ctypes.data, b, v, t, horizon, cstruct, ostruct,
+                                          out.ctypes.data))
+        return out
 
     # -- profiling ------------------------------------------------------------------------------
     def profile(self, enable=True):
