@@ -57,9 +57,17 @@ struct Epi {
     int *err;
 };
 
-// 0 none, 1 relu, 2 silu
-__device__ __forceinline__ float apply_act(int act, float v) {
-    return act == 1 ? fmaxf(v, 0.0f) : act == 2 ? v / (1.0f + expf(-v)) : v;
+// Activation over n values: 1 relu, 2 silu (nn.siluInPlace, core/nn.zig:399-407). The branch is
+// uniform and taken outside the element loops, so act == 0 costs nothing.
+template <int N>
+__device__ __forceinline__ void apply_act(int act, float *v) {
+    if (act == 1) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) v[j] = fmaxf(v[j], 0.0f);
+    } else if (act == 2) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) v[j] = v[j] / (1.0f + expf(-v[j]));
+    }
 }
 
 template <typename H>
@@ -111,24 +119,32 @@ __device__ __forceinline__ void store_chunk(const Epi &e, int64_t orow, int64_t 
         }
         const bool vec = nvalid == 32 && ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
         if (e.out_mode == OUT_F32_ACC) {
+            // Read the whole chunk first (eight loads in flight), add, activate, write back.
+            float a[32];
             if (vec) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    float4 a = reinterpret_cast<float4 *>(o)[q];
-                    a.x += v[4 * q];
-                    a.y += v[4 * q + 1];
-                    a.z += v[4 * q + 2];
-                    a.w += v[4 * q + 3];
-                    a.x = apply_act(e.act, a.x);
-                    a.y = apply_act(e.act, a.y);
-                    a.z = apply_act(e.act, a.z);
-                    a.w = apply_act(e.act, a.w);
-                    reinterpret_cast<float4 *>(o)[q] = a;
+                    const float4 t = reinterpret_cast<const float4 *>(o)[q];
+                    a[4 * q] = t.x;
+                    a[4 * q + 1] = t.y;
+                    a[4 * q + 2] = t.z;
+                    a[4 * q + 3] = t.w;
                 }
             } else {
 #pragma unroll
+                for (int j = 0; j < 32; ++j) a[j] = j < nvalid ? o[j] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] += v[j];
+            apply_act<32>(e.act, a);
+            if (vec) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    reinterpret_cast<float4 *>(o)[q] = make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]);
+            } else {
+#pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    if (j < nvalid) o[j] = apply_act(e.act, o[j] + v[j]);
+                    if (j < nvalid) o[j] = a[j];
             }
         } else {
             if (vec) {
@@ -151,14 +167,7 @@ __device__ __forceinline__ void bias_act(const Epi &e, int64_t col0, int nvalid,
             if (j < nvalid) v[j] += __ldg(e.bias + col0 + j);
     }
     // In accumulate mode the activation applies to the accumulated sum (store_chunk).
-    if (e.act == 1 && e.out_mode != OUT_F32_ACC) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-    }
-    if (e.act == 2 && e.out_mode != OUT_F32_ACC) {  // silu (nn.siluInPlace, core/nn.zig:399-407)
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = v[j] / (1.0f + expf(-v[j]));
-    }
+    if (e.out_mode != OUT_F32_ACC) apply_act<32>(e.act, v);
 }
 
 template <typename T, int BN>
