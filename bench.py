@@ -117,11 +117,12 @@ def build_model(device):
 
 
 def traffic_from_profile():
-    """DRAM bytes per launch of the linear kernel from the committed ncu summary, if present."""
+    """DRAM bytes per GEMM launch (averaged over a whole forecast step, like `achieved`) from the
+    committed ncu summary, if present."""
     p = os.path.join(ROOT, "profiles", "linear_tc_chronos2.md")
     try:
         for line in open(p):
-            if line.startswith("traffic_bytes_per_gemm_step:"):
+            if line.startswith("traffic_bytes_per_gemm_launch:"):
                 return float(line.split(":")[1])
     except Exception:
         pass
