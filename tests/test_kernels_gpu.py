@@ -137,6 +137,44 @@ def test_attention_matches_float64_reference(n, mode, with_rel, dtype):
     assert err < (3e-2 if dtype == "bf16" else 5e-3), err
 
 
+@pytest.mark.parametrize("n", [1, 17, 128, 129, 256, 257, 640, 1100])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_attention_tcgen05_path_edges(n, dtype):
+    """The tcgen05 kernel (key-validity mask, no relative bias): one and two query tiles per CTA,
+    partial key tiles, the K / V rings wrapping many times, a group without valid keys (uniform),
+    a group whose first 300 keys are invalid (rows start with an empty max), and scores that grow
+    by more than 2^8 per key tile so the lazy O / row-sum rescale runs on every tile."""
+    heads, G = 2, 4
+    gen = torch.Generator().manual_seed(1000 + n)
+    ld = 3 * heads * 64
+    qkv = torch.randn(G * n, ld, generator=gen) * 0.5
+    u = torch.randn(64, generator=gen)
+    u = u / u.norm()
+    for h in range(heads):  # group 3: q along u, k growing along u with the key index
+        rows = slice(3 * n, 4 * n)
+        qkv[rows, h * 64:(h + 1) * 64] += 2.0 * u
+        ramp = (0.05 * torch.arange(n, dtype=torch.float32))[:, None] * u[None, :]
+        qkv[rows, heads * 64 + h * 64:heads * 64 + (h + 1) * 64] += ramp
+    qkv = qkv.to(TORCH16[dtype]).to(dev())
+    q, k, v = qkv[:, :heads * 64], qkv[:, heads * 64:2 * heads * 64], qkv[:, 2 * heads * 64:]
+    kv = (torch.rand(G, n, generator=gen) > 0.3).to(torch.uint8)
+    kv[1, :] = 0
+    kv[2, :min(n, 300)] = 0
+    if n > 300:
+        kv[2, 300] = 1
+    kv[3, :] = 1
+    o = torch.full((G * n, heads * 64), float("nan"), device=dev(), dtype=TORCH16[dtype])
+    tb.check(tb.lib.tsfm_kernel_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, o.data_ptr(), heads * 64,
+                                          kv.to(dev()).data_ptr(), None, G, heads, n, 1.0, 0,
+                                          CODE16[TORCH16[dtype]], stream_ptr()))
+    torch.cuda.synchronize()
+    ref = attention_ref(q, k, v, kv, None, n, heads, 1.0, 0)
+    got = o.double().cpu()
+    assert torch.isfinite(got).all()
+    err = (got - ref).abs().max().item()
+    assert err < (3e-2 if dtype == "bf16" else 5e-3), err
+
+
 def test_rmsnorm_matches_oracle():
     rows, dim = 1000, 768
     rng = np.random.default_rng(1)

@@ -139,6 +139,7 @@ Status predict_chunk(Replica &r, const tsfm_config &c, const BoltDev &w, const f
         TSFM_TRY(op_linear(r, s, L.qkv, xn, rows, d, qkv, 3 * in, A16, 0));
         {
             AttentionCall ac;
+            ac.err = static_cast<int *>(r.err.p);
             ac.q = qkv;
             ac.k = qkv + in;
             ac.v = qkv + 2 * in;

@@ -530,6 +530,7 @@ int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64
         c.dtype = dtype == TSFM_DTYPE_F16 ? E_F16 : E_BF16;
         c.ne = n;
         c.l = n;
+        c.err = kernel_err_word();
         return launch_attention(c, static_cast<cudaStream_t>(stream));
     });
 }

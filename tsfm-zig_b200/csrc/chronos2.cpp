@@ -281,6 +281,7 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
         TSFM_TRY(op_linear(r, s, L.qkv, xn, rows, d, qkv, 3 * d, A16, 0, &rope));
         {
             AttentionCall ac;
+            ac.err = static_cast<int *>(r.err.p);
             ac.q = qkv;
             ac.k = qkv + d;
             ac.v = qkv + 2 * d;

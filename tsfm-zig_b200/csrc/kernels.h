@@ -88,8 +88,19 @@ struct AttentionCall {
     int mask_mode = 0;
     int ne = 0, l = 0;
     const uint8_t *group_bidir = nullptr;  // per group: 1 = bidirectional encoder rows (mode 1 only)
+    int *err = nullptr;                    // device error word for the bounded waits of the tcgen05 path
+    int force_path = 0;                    // 0: automatic, 1: tcgen05 path only (error if unsupported), 2: mma.sync path
 };
 Status launch_attention(const AttentionCall &c, cudaStream_t stream);
+// The tcgen05 path (attention_tc.cu): true when it handles this call's mask and shapes.
+bool attention_tc_supported(const AttentionCall &c);
+Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream);
+
+// 2-D TMA descriptor with the 128-byte swizzle over a row-major [outer, inner] matrix of 16-bit or
+// 32-bit elements with row stride `ld` elements; box = [box_outer, box_inner]. `map` points to a
+// CUtensorMap (128 bytes).
+Status make_tmap_2d(void *map, const void *base, int dtype, int64_t inner, int64_t outer, int64_t ld,
+                    uint32_t box_inner, uint32_t box_outer);
 
 // RMSNorm: out[r] = x[in_row(r)] * (1 / sqrt(mean(x^2) + eps)) * scale.
 // in_row(r) = (r / g) * G + r % g + off when g > 0. out_mode: OUT_BF16, OUT_F32, OUT_TF32, OUT_F16.

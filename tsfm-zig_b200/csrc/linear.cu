@@ -486,6 +486,11 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
 
 int num_sms() { return sm_count(); }
 
+Status make_tmap_2d(void *map, const void *base, int dtype, int64_t inner, int64_t outer, int64_t ld,
+                    uint32_t box_inner, uint32_t box_outer) {
+    return make_tmap(static_cast<CUtensorMap *>(map), base, dtype, inner, outer, ld, box_inner, box_outer);
+}
+
 Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     if (c.M <= 0 || c.N <= 0 || c.K <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: empty product");
     if (c.M > INT32_MAX || c.N > INT32_MAX || c.K > INT32_MAX)

@@ -22,6 +22,10 @@ enum : int {
     ERR_SITE_GEMM_MMA_EMPTY = 0x0103,
     ERR_SITE_GEMM_EPILOGUE = 0x0104,
     ERR_SITE_GEMM_DRAIN = 0x0105,
+    ERR_SITE_ATTN_PRODUCER = 0x0201,
+    ERR_SITE_ATTN_MMA = 0x0202,
+    ERR_SITE_ATTN_SOFTMAX = 0x0203,
+    ERR_SITE_ATTN_DRAIN = 0x0204,
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
@@ -197,6 +201,58 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// The inverse of tmem_ld32: thread `lane` writes row (lane_base + lane), columns [col, col + 32).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Makes this thread's generic-proxy shared-memory writes visible to the async proxy (the tensor
+// cores reading an operand tile through a matrix descriptor).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Named barrier over `count` threads (a multiple of 32), id 1..15 (0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Named barrier that also returns the OR of `v` over the participating threads.
+__device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
+// 2^x on the SFU (the PTX instruction itself; inputs below -126 flush to +0, -inf gives +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // Round an FP32 value to TF32 (round to nearest, ties away), as the tensor cores consume it.
 __device__ __forceinline__ float to_tf32(float x) {

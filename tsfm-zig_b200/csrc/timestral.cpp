@@ -308,6 +308,7 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
             TSFM_TRY(op_linear(r, s, a.qkvg, xn, rows, d, qkvg, cols, A16, 0, a.is_time ? &rope : nullptr));
             if (a.is_time) {
                 AttentionCall ac;
+                ac.err = static_cast<int *>(r.err.p);
                 ac.q = qkvg;
                 ac.k = qkvg + d;
                 ac.v = qkvg + 2 * d;
