@@ -39,7 +39,10 @@ struct TileCfg {
     static constexpr int A_BYTES = kBM * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
-    static constexpr int SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+    // Epilogue staging for the TMA stores: per epilogue warp two 4 KB boxes (32 rows x 128 B).
+    static constexpr int STAGE_OFF = STAGES * (A_BYTES + B_BYTES);
+    static constexpr int STAGE_BYTES = 4 * 2 * 4096;
+    static constexpr int SMEM = 1024 + STAGE_OFF + STAGE_BYTES + 256;
 };
 
 struct Epi {
@@ -54,6 +57,7 @@ struct Epi {
     const float *rope_sin;
     int rope_cols;               // columns [0, rope_cols) are rotated per 64-wide head
     int64_t rope_p1, rope_p2;    // position index = (r / p1) * p2 + r % p2 (p1 == 0: r % p2)
+    int tma_mode;                // 0: per-thread stores; 1: TMA store of staged boxes; 2: TMA reduce-add (f32)
     int *err;
 };
 
@@ -172,7 +176,8 @@ __device__ __forceinline__ void bias_act(const Epi &e, int64_t col0, int nvalid,
 
 template <typename T, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
-    linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Epi e) {
+    linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmY, Epi e) {
     using C = TileCfg<BN>;
     constexpr int STAGES = C::STAGES;
     constexpr int BK = 128 / (int)sizeof(T);
@@ -184,7 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * C::A_BYTES;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sB + STAGES * C::B_BYTES);
+    uint8_t *sStage = smem + C::STAGE_OFF;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGE_OFF + C::STAGE_BYTES);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
@@ -314,6 +320,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Epilogue warps 2..5 own TMEM lane groups (warp % 4) * 32.
         const int eg = warp & 3;
         const int r_in_tile = eg * 32 + lane;
+        const bool f32_out = e.out_mode == OUT_F32 || e.out_mode == OUT_F32_ACC || e.out_mode == OUT_TF32;
+        // TMA epilogue: each warp stages a box of its 32 rows (128 bytes per row: 32 f32 or 64
+        // 16-bit values, 128-byte swizzle) and one lane stores or reduce-adds it; two boxes per
+        // warp alternate so staging overlaps the previous box's transfer.
+        uint8_t *wstage = sStage + eg * 8192;
+        int sbuf = 0;
+        auto stage_box = [&]() -> uint8_t * {
+            if (lane == 0) bulk_wait_read_1();
+            __syncwarp();
+            uint8_t *b = wstage + sbuf * 4096;
+            sbuf ^= 1;
+            return b;
+        };
+        auto put16 = [&](uint8_t *b, int q, uint4 v) {  // 16-byte chunk q of this lane's row
+            *reinterpret_cast<uint4 *>(b + lane * 128 + ((q ^ (lane & 7)) << 4)) = v;
+        };
+        auto issue_box = [&](const uint8_t *b, int64_t col0, int64_t row0) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if (e.tma_mode == 2)
+                    tma_reduce_add_2d(&tmY, b, (int32_t)col0, (int32_t)row0);
+                else
+                    tma_store_2d(&tmY, b, (int32_t)col0, (int32_t)row0);
+                bulk_commit();
+            }
+        };
+        auto tma_f32 = [&](int64_t col0, int64_t row0, float (&v)[32]) {
+            if (e.out_mode == OUT_TF32) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = to_tf32(v[j]);
+            }
+            uint8_t *b = stage_box();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) put16(b, q, make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                                                                __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3])));
+            issue_box(b, col0, row0);
+        };
+        auto tma_16 = [&](int64_t col0, int64_t row0, const float (&lo)[32], const float (&hi)[32]) {
+            uint8_t *b = stage_box();
+            const bool f16 = e.out_mode == OUT_F16;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float *src = q < 4 ? lo + 8 * q : hi + 8 * (q - 4);
+                uint4 pk;
+                pk.x = f16 ? pack2<__half>(src[0], src[1]) : pack2<__nv_bfloat16>(src[0], src[1]);
+                pk.y = f16 ? pack2<__half>(src[2], src[3]) : pack2<__nv_bfloat16>(src[2], src[3]);
+                pk.z = f16 ? pack2<__half>(src[4], src[5]) : pack2<__nv_bfloat16>(src[4], src[5]);
+                pk.w = f16 ? pack2<__half>(src[6], src[7]) : pack2<__nv_bfloat16>(src[6], src[7]);
+                put16(b, q, pk);
+            }
+            issue_box(b, col0, row0);
+        };
         int acc = 0;
         uint32_t aph = 0;
         for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -323,12 +382,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             const int64_t row = (t / n_tiles) * kBM + r_in_tile;
+            const int64_t wrow0 = (t / n_tiles) * kBM + eg * 32;  // first row of this warp's box
             const int64_t ncol0 = (t % n_tiles) * BN;
             const bool row_ok = row < e.M;
             const int64_t orow = e.rm_g > 0 ? (row / e.rm_g) * e.rm_G + row % e.rm_g + e.rm_off : row;
             const uint32_t tbase = tmem_base + ((uint32_t)(eg * 32) << 16) + (uint32_t)(acc * BN);
-            if (e.rope_cos != nullptr) {
-                // 64-column chunks: one head; rotate-half pairs (i, i + 32) of columns < rope_cols.
+            if (e.rope_cos != nullptr || (e.tma_mode != 0 && !f32_out)) {
+                // 64-column chunks (one head for RoPE): rotate-half pairs (i, i + 32) of columns
+                // < rope_cols.
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 64) {
                     const int64_t col0 = ncol0 + c;
@@ -337,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld32(tbase + c, lo);
                     tmem_ld32(tbase + c + 32, hi);
                     tmem_wait_ld();
-                    if (col0 < e.rope_cols && row_ok) {
+                    if (e.rope_cos != nullptr && col0 < e.rope_cols && row_ok) {
                         const int64_t pidx = e.rope_p1 > 0 ? (row / e.rope_p1) * e.rope_p2 + row % e.rope_p2 : row % e.rope_p2;
                         const float4 *cs = reinterpret_cast<const float4 *>(e.rope_cos + pidx * 32);
                         const float4 *sn = reinterpret_cast<const float4 *>(e.rope_sin + pidx * 32);
@@ -359,7 +420,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int nv1 = rem1 <= 0 ? 0 : (rem1 < 32 ? (int)rem1 : 32);
                     bias_act(e, col0, nv0, lo);
                     if (nv1 > 0) bias_act(e, col0 + 32, nv1, hi);
-                    if (row_ok) {
+                    if (e.tma_mode != 0) {
+                        if (f32_out) {
+                            tma_f32(col0, wrow0, lo);
+                            if (nv1 > 0) tma_f32(col0 + 32, wrow0, hi);
+                        } else {
+                            tma_16(col0, wrow0, lo, hi);
+                        }
+                    } else if (row_ok) {
                         store_chunk(e, orow, col0, nv0, lo);
                         if (nv1 > 0) store_chunk(e, orow, col0 + 32, nv1, hi);
                     }
@@ -375,7 +443,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int64_t rem = e.N - col0;
                     const int nv = rem < 32 ? (int)rem : 32;
                     bias_act(e, col0, nv, v);
-                    if (row_ok) store_chunk(e, orow, col0, nv, v);
+                    if (e.tma_mode != 0)
+                        tma_f32(col0, wrow0, v);
+                    else if (row_ok)
+                        store_chunk(e, orow, col0, nv, v);
                 }
             }
             tc_fence_before();
@@ -385,6 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 aph ^= 1u;
             }
         }
+        // Every staged box has been written (or reduced) before the CTA exits.
+        if (e.tma_mode != 0 && lane == 0) bulk_wait_all();
     }
 
     __syncthreads();
@@ -474,9 +547,19 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     e.rope_p1 = c.rope_p1;
     e.rope_p2 = c.rope_p2;
     e.err = c.err;
+    // TMA epilogue unless rows are remapped or an activation follows the accumulation; the
+    // output base and row stride must suit a tensor map (16-byte alignment).
+    const bool f32_out = c.out_mode == OUT_F32 || c.out_mode == OUT_F32_ACC || c.out_mode == OUT_TF32;
+    e.tma_mode = 0;
+    CUtensorMap ty = tb;
+    if (c.rm_g <= 0 && !(c.out_mode == OUT_F32_ACC && c.act != 0)) {
+        const int ydt = f32_out ? E_F32 : c.out_mode == OUT_F16 ? E_F16 : E_BF16;
+        if (make_tmap(&ty, c.y, ydt, c.N, c.M, c.ldy, f32_out ? 32 : 64, 32).code == 0)
+            e.tma_mode = c.out_mode == OUT_F32_ACC ? 2 : 1;
+    }
     const int64_t tiles = ((c.M + kBM - 1) / kBM) * ((c.N + BN - 1) / BN);
     const int grid = (int)std::min<int64_t>(tiles, sm_count());
-    linear_tc_kernel<T, BN><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, e);
+    linear_tc_kernel<T, BN><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, e);
     ce = cudaGetLastError();
     if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch");
     return Status::ok();
