@@ -117,10 +117,12 @@ Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, 
                 // still required to exist, as the reference loads them.
                 TSFM_TRY(t.get(p + "self_attention.q.weight", d * d, v));
                 TSFM_TRY(t.get(p + "self_attention.k.weight", d * d, v));
-                TSFM_TRY(t.get(p + "self_attention.v.weight", d * d, v));
-                TSFM_TRY(upload_lin(r, v, d, d, act, L.gv));
-                TSFM_TRY(t.get(p + "self_attention.o.weight", d * d, v));
-                TSFM_TRY(upload_lin(r, v, d, d, act, L.go));
+                // o(v(x)) = x (W_o W_v)^T: one GEMM with the product formed in float64 and
+                // rounded once.
+                std::vector<float> wv, wo;
+                TSFM_TRY(t.get(p + "self_attention.v.weight", d * d, wv));
+                TSFM_TRY(t.get(p + "self_attention.o.weight", d * d, wo));
+                TSFM_TRY(upload_lin(r, matmul_f64(wo, wv, d, d, d), d, d, act, L.gvo));
             }
         }
         TSFM_TRY(t.get(strf("encoder.block.%d.layer.2.layer_norm.weight", li), d, v));
@@ -301,8 +303,7 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
         }
         TSFM_TRY(op_linear(r, s, L.o, ao, rows, d, x, d, OUT_F32_ACC, 0));
         TSFM_TRY(op_rmsnorm(r, s, x, L.group_norm, xn, A16, rows, d, eps));
-        TSFM_TRY(op_linear(r, s, L.gv, xn, rows, d, ao, d, A16, 0));
-        TSFM_TRY(op_linear(r, s, L.go, ao, rows, d, x, d, OUT_F32_ACC, 0));
+        TSFM_TRY(op_linear(r, s, L.gvo, xn, rows, d, x, d, OUT_F32_ACC, 0));
         TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps));
         TSFM_TRY(op_linear(r, s, L.wi, xn, rows, d, h, ff, A16, 1));
         TSFM_TRY(op_linear(r, s, L.wo, h, rows, ff, x, d, OUT_F32_ACC, 0));

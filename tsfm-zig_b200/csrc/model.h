@@ -16,7 +16,7 @@ struct C2Dev {
     DLin3 head_hidden, head_output, head_residual;
     struct Layer {
         float *time_norm = nullptr, *group_norm = nullptr, *mlp_norm = nullptr;
-        DLin qkv, o, gv, go, wi, wo;
+        DLin qkv, o, gvo, wi, wo;  // gvo = W_o W_v of the singleton-group attention
     };
     std::vector<Layer> layers;
     float *final_norm = nullptr, *reg = nullptr;

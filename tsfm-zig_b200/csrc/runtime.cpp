@@ -1,7 +1,9 @@
 #include "runtime.h"
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstring>
+#include <thread>
 
 #include <cuda_fp16.h>
 
@@ -204,6 +206,35 @@ Status upload_f32(Replica &r, const std::vector<float> &h, float **out) {
     *out = static_cast<float *>(b.p);
     r.weights.push_back(std::move(b));
     return Status::ok();
+}
+
+std::vector<float> matmul_f64(const std::vector<float> &a, const std::vector<float> &b, int64_t m, int64_t k, int64_t n) {
+    std::vector<double> bt((size_t)(k * n));
+    for (int64_t i = 0; i < k; ++i)
+        for (int64_t j = 0; j < n; ++j) bt[(size_t)(j * k + i)] = b[(size_t)(i * n + j)];
+    std::vector<float> c((size_t)(m * n));
+    const int64_t nth = std::max<int64_t>(1, std::min<int64_t>(m, std::thread::hardware_concurrency()));
+    std::vector<std::thread> th;
+    for (int64_t w = 0; w < nth; ++w)
+        th.emplace_back([&, w] {
+            std::vector<double> row((size_t)k);
+            for (int64_t i = m * w / nth; i < m * (w + 1) / nth; ++i) {
+                for (int64_t x = 0; x < k; ++x) row[(size_t)x] = a[(size_t)(i * k + x)];
+                for (int64_t j = 0; j < n; ++j) {
+                    const double *bj = &bt[(size_t)(j * k)];
+                    double s0 = 0, s1 = 0;
+                    int64_t x = 0;
+                    for (; x + 1 < k; x += 2) {
+                        s0 += row[(size_t)x] * bj[x];
+                        s1 += row[(size_t)x + 1] * bj[x + 1];
+                    }
+                    if (x < k) s0 += row[(size_t)x] * bj[x];
+                    c[(size_t)(i * n + j)] = (float)(s0 + s1);
+                }
+            }
+        });
+    for (auto &t : th) t.join();
+    return c;
 }
 
 Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, int dtype, DLin &dst) {

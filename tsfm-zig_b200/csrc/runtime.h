@@ -152,6 +152,9 @@ struct TensorTable {
 // Upload helpers (run with the replica's device current).
 Status upload_f32(Replica &r, const std::vector<float> &h, float **out);
 Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, int dtype, DLin &dst);
+// a (m, k) times b (k, n), row-major, accumulated in float64 and rounded to float32 once per
+// element; rows split across host threads.
+std::vector<float> matmul_f64(const std::vector<float> &a, const std::vector<float> &b, int64_t m, int64_t k, int64_t n);
 Status upload_bias(Replica &r, const std::vector<float> &b, DLin &dst);
 Status upload_lin3(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, DLin3 &dst);
 
