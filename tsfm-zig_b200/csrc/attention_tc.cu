@@ -1,22 +1,22 @@
 // Flash attention on the 5th-generation tensor cores (sm_100a) for 64-wide heads.
 //
 // Persistent: one CTA per SM walks a contiguous range of work items; an item is one
-// (group, head) and two 128-query tiles A and B that share every K / V tile.
-// Roles (352 threads):
-//   warps 0-3   softmax of tile A (thread = query row; warp w reads TMEM lanes 32 (w % 4) ...)
-//   warps 4-7   softmax of tile B
-//   warp 8      lane 0: TMA of the Q tiles and the K ring; lane 1: TMA of the V ring
-//   warp 9      TMEM allocation and the single MMA-issuing thread
-//   warp 10     key mask of the next item: per-key additive biases (0 / -inf) in shared memory
-// Per key tile j the MMA thread issues S_A = Q_A K_j^T and S_B = Q_B K_j^T (M 128, N 128, K 64,
-// accumulators in TMEM), then O_A += P_A(j-1) V_(j-1) and O_B += P_B(j-1) V_(j-1) (M 128, N 64,
-// K 128; P from shared memory, V as an MN-major operand straight from its TMA tile). While the
-// tensor cores work, the softmax warps read S with tcgen05.ld, add the key biases (tiles with
-// a masked key only), update the running max with the lazy rescale (O and the row sum are
-// rescaled only when the max grows by more than 2^8, so P stays below 256), write P as 16-bit
-// values into the 128-byte-swizzled K-major layout the MMA reads, and arrive on p_ready. The K
-// and V rings and all barrier phases run on across items, so the next item's Q, K and mask
-// loads overlap the current item's last tiles and its output stores.
+// (group, head, 128-query tile). The CTA runs two independent pipelines; pipeline p takes every
+// other item of the range, so the softmax of one pipeline overlaps the other's loads, MMAs and
+// bookkeeping and the SFU (exp2) stays busy.
+// Roles (384 threads):
+//   warps 0-3, 4-7   softmax of pipeline 0 / 1 (thread = query row; warp w reads TMEM lanes
+//                    32 (w % 4) .. + 31)
+//   warp 8           lanes 0 / 1: TMA of Q + the K ring / the V ring of pipeline 0;
+//                    lanes 2 / 3: the same for pipeline 1
+//   warps 9, 10      the MMA-issuing thread of pipeline 0 / 1 (warp 9 also allocates TMEM)
+//   warp 11          key masks of the coming items (bit words per key tile, tile classes)
+// Per key tile j a pipeline issues S = Q K_j^T (M 128, N 128, K 64, FP32 in TMEM), then
+// O += P_(j-1) V_(j-1) (M 128, N 64, K 128) with P read from TMEM (16-bit, written by the
+// softmax threads with tcgen05.st) and V as an MN-major operand straight from its TMA tile.
+// The softmax threads read S with tcgen05.ld, mask it (tile classes: all keys valid, valid
+// prefix, per-key bits), update the running max with the lazy rescale (O and the row sum are
+// rescaled only when the max grows by more than 2^8, so P stays below 256) and write P.
 //
 // Masks: the key-validity mask of chronos2/model.zig:208-233 and chronos_bolt/model.zig (mode 0:
 // key j is visible when it is valid; a group without any valid key attends uniformly to all its
@@ -34,27 +34,37 @@ namespace {
 
 constexpr int kTileRows = 128;                   // queries per tile, keys per tile
 constexpr int kTileBytes = kTileRows * 64 * 2;   // 16 KB: 128 rows of 64 16-bit values (128 B)
-constexpr int kPBytes = 2 * kTileBytes;          // 128 x 128 16-bit P: two 64-key swizzle columns
 constexpr int kMaxKeys = 4096;
-constexpr int kThreadsTc = 352;
-constexpr int kSoftmaxThreads = 256;
+constexpr int kMaxKeyTiles = kMaxKeys / kTileRows;
+constexpr int kThreadsTc = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-// Shared memory map (offsets from the 1024-aligned base).
-constexpr int OFF_Q = 0;                          // 2 tiles
-constexpr int OFF_K = OFF_Q + 2 * kTileBytes;     // 2 stages
-constexpr int OFF_V = OFF_K + 2 * kTileBytes;     // 2 stages
-constexpr int OFF_P = OFF_V + 2 * kTileBytes;     // 2 tiles x 32 KB
-constexpr int OFF_BIAS = OFF_P + 2 * kPBytes;     // 2 slots x kMaxKeys floats
-constexpr int OFF_BIAS_INFO = OFF_BIAS + 2 * kMaxKeys * 4;  // per slot: uniform flag, full-tile bits
-constexpr int OFF_BAR = OFF_BIAS_INFO + 64;
-constexpr int kNumBars = 24;
-constexpr int OFF_MISC = OFF_BAR + kNumBars * 8;
-constexpr int kSmemTc = OFF_MISC + 64 + 1024;     // + alignment slack
+// Tile classes of a key tile.
+enum : uint8_t { TILE_FULL = 0, TILE_PREFIX = 1, TILE_BITS = 2 };
 
-// TMEM columns: S_A, S_B (128 each), O_A, O_B (64 each).
+// Mask of one item: per key tile its class and, for TILE_BITS, 128 validity bits; `uniform`:
+// no valid key (every key below n gets score 0).
+struct MaskSlot {
+    uint32_t bits[kMaxKeys / 32];
+    uint8_t cls[kMaxKeyTiles];
+    uint32_t uniform;
+    uint32_t pad[7];
+};
+
+// Shared memory map (offsets from the 1024-aligned base), per pipeline p.
+constexpr int PIPE_BYTES = 5 * kTileBytes;       // Q, K[2], V[2]
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = kTileBytes;
+constexpr int OFF_V = 3 * kTileBytes;
+constexpr int OFF_MASK = 2 * PIPE_BYTES;         // [pipeline][slot]
+constexpr int OFF_BAR = OFF_MASK + 4 * (int)sizeof(MaskSlot);
+constexpr int kBarsPerPipe = 18;
+constexpr int OFF_MISC = OFF_BAR + (2 * kBarsPerPipe + 2) * 8;
+constexpr int kSmemTc = OFF_MISC + 64 + 1024;    // + alignment slack
+
+// TMEM columns of pipeline p (base p * 256): S (128 FP32), P (64 columns = 128 16-bit), O (64).
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t TM_S = 0, TM_O = 256;
+constexpr uint32_t TM_S = 0, TM_P = 128, TM_O = 192;
 
 struct TcParams {
     const uint8_t *key_valid;
@@ -62,16 +72,10 @@ struct TcParams {
     void *o;
     int64_t ldo;
     int n, heads, groups;
-    int pairs;     // query-tile pairs per (group, head)
+    int qtiles;    // query tiles per (group, head)
     int64_t items;
     float scale_log2;
     int *err;
-};
-
-struct BiasInfo {
-    uint32_t uniform;
-    uint32_t pad;
-    uint64_t full;  // bit t: key tile t has no masked key
 };
 
 template <bool F16>
@@ -85,31 +89,35 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
     }
 }
 
-// The item range [first, last) of this CTA: contiguous, so consecutive items share a group
-// (and its K / V rows in L2).
+struct Item {
+    int g, h, q0;
+};
+__device__ __forceinline__ Item decode_item(const TcParams &p, int64_t it) {
+    Item r;
+    const int qt = (int)(it % p.qtiles);
+    const int64_t gh = it / p.qtiles;
+    r.h = (int)(gh % p.heads);
+    r.g = (int)(gh / p.heads);
+    r.q0 = qt * kTileRows;
+    return r;
+}
+
+// Barriers of one pipeline.
+struct PipeBars {
+    uint64_t q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t s_full, s_free, p_ready, o_done, m_full[2], m_empty[2];
+};
+static_assert(sizeof(PipeBars) == kBarsPerPipe * 8, "barrier block");
+
+// The item range [first, last) of this CTA (contiguous: neighbouring items share K / V rows in
+// L2); pipeline p takes items first + p, first + p + 2, ...
 __device__ __forceinline__ void item_range(const TcParams &p, int64_t &first, int64_t &last) {
     first = p.items * blockIdx.x / gridDim.x;
     last = p.items * (blockIdx.x + 1) / gridDim.x;
 }
 
-struct Item {
-    int g, h, q0;
-    bool hasB;
-};
-__device__ __forceinline__ Item decode_item(const TcParams &p, int64_t it) {
-    Item r;
-    const int pair = (int)(it % p.pairs);
-    const int64_t gh = it / p.pairs;
-    r.h = (int)(gh % p.heads);
-    r.g = (int)(gh / p.heads);
-    r.q0 = pair * 2 * kTileRows;
-    r.hasB = r.q0 + kTileRows < p.n;
-    return r;
-}
-
-// Registers are allocated for warps in groups of four: the 11 warps take 12 warps' worth, so
-// 168 per thread (12 x 32 x 168 = 64,512 of the SM's 65,536). One CTA per SM (the shared memory
-// allows no second one either).
+// Registers are allocated for warps in groups of four; 12 warps x 32 x 168 = 64,512 of the SM's
+// 65,536. One CTA per SM (the shared memory and the 512 TMEM columns allow no second one).
 template <bool F16>
 __global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -120,22 +128,9 @@ __global__ void __maxnreg__(168)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *kbias = reinterpret_cast<float *>(smem + OFF_BIAS);
-    BiasInfo *binfo = reinterpret_cast<BiasInfo *>(smem + OFF_BIAS_INFO);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-    uint64_t *q_full = bars + 0;
-    uint64_t *q_empty = bars + 1;
-    uint64_t *k_full = bars + 2;     // [2]
-    uint64_t *k_empty = bars + 4;    // [2]
-    uint64_t *v_full = bars + 6;     // [2]
-    uint64_t *v_empty = bars + 8;    // [2]
-    uint64_t *s_full = bars + 10;    // [2] per query tile
-    uint64_t *s_free = bars + 12;    // [2]
-    uint64_t *p_ready = bars + 14;   // [2]
-    uint64_t *o_done = bars + 16;    // [2]
-    uint64_t *bias_full = bars + 18;   // [2] per bias slot
-    uint64_t *bias_empty = bars + 20;  // [2]
-    uint64_t *drain = bars + 22;
+    MaskSlot *mslots = reinterpret_cast<MaskSlot *>(smem + OFF_MASK);  // [pipe * 2 + slot]
+    PipeBars *pb = reinterpret_cast<PipeBars *>(smem + OFF_BAR);       // [2]
+    uint64_t *drain = reinterpret_cast<uint64_t *>(smem + OFF_BAR + 2 * kBarsPerPipe * 8);  // [2]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
 
@@ -146,21 +141,24 @@ __global__ void __maxnreg__(168)
     item_range(p, first, last);
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        mbar_init(q_empty, 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&k_full[i], 1);
-            mbar_init(&k_empty[i], 1);
-            mbar_init(&v_full[i], 1);
-            mbar_init(&v_empty[i], 1);
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 128);
-            mbar_init(&p_ready[i], 128);
-            mbar_init(&o_done[i], 1);
-            mbar_init(&bias_full[i], 32);
-            mbar_init(&bias_empty[i], kSoftmaxThreads);
+        for (int q = 0; q < 2; ++q) {
+            PipeBars &b = pb[q];
+            mbar_init(&b.q_full, 1);
+            mbar_init(&b.q_empty, 1);
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&b.k_full[i], 1);
+                mbar_init(&b.k_empty[i], 1);
+                mbar_init(&b.v_full[i], 1);
+                mbar_init(&b.v_empty[i], 1);
+                mbar_init(&b.m_full[i], 32);
+                mbar_init(&b.m_empty[i], 128);
+            }
+            mbar_init(&b.s_full, 1);
+            mbar_init(&b.s_free, 128);
+            mbar_init(&b.p_ready, 128);
+            mbar_init(&b.o_done, 1);
+            mbar_init(&drain[q], 1);
         }
-        mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmQ);
@@ -176,376 +174,307 @@ __global__ void __maxnreg__(168)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 8) {
-        if (lane == 0) {
-            // ---- Q tiles and the K ring ----
-            uint32_t kt = 0;  // K tiles issued so far
-            uint32_t issued = 0, issued_ph = 0;
-            bool ok = true, q_issued = false;
-            uint32_t q_ph = 0;
-            for (int64_t it = first; it < last && ok; ++it) {
-                const Item im = decode_item(p, it);
-                const int32_t row0 = im.g * n, col = im.h * 64;
-                const uint32_t wi = (uint32_t)(it - first);
-                if (wi > 0 && !mbar_wait(q_empty, (wi - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER)) {
+    if (warp == 8 && lane < 4) {
+        // ---- TMA producers: lane 2q + 0 loads Q and the K ring, lane 2q + 1 the V ring ----
+        const int q = lane >> 1;
+        const bool kside = (lane & 1) == 0;
+        PipeBars &b = pb[q];
+        uint8_t *base = smem + q * PIPE_BYTES;
+        uint32_t rt = 0;  // ring position
+        uint32_t issued = 0, issued_ph = 0;
+        bool ok = true, q_issued = false;
+        uint32_t q_ph = 0, wi = 0;
+        for (int64_t it = first + q; it < last && ok; it += 2, ++wi) {
+            const Item im = decode_item(p, it);
+            const int32_t row0 = im.g * n, col = im.h * 64;
+            if (kside) {
+                if (wi > 0 && !mbar_wait(&b.q_empty, (wi - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(q_full, (im.hasB ? 2 : 1) * kTileBytes);
-                tma_load_2d(smem + OFF_Q, &tmQ, q_full, col, row0 + im.q0);
-                if (im.hasB) tma_load_2d(smem + OFF_Q + kTileBytes, &tmQ, q_full, col, row0 + im.q0 + kTileRows);
+                mbar_arrive_expect_tx(&b.q_full, kTileBytes);
+                tma_load_2d(base + OFF_Q, &tmQ, &b.q_full, col, row0 + im.q0);
                 q_issued = true;
                 q_ph = wi & 1;
-                for (int j = 0; j < T; ++j, ++kt) {
-                    const int st = kt & 1;
-                    if (kt >= 2 && !mbar_wait(&k_empty[st], ((kt - 2) >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-                    tma_load_2d(smem + OFF_K + st * kTileBytes, &tmK, &k_full[st], col, row0 + j * kTileRows);
-                    issued |= 1u << st;
-                    issued_ph = (issued_ph & ~(1u << st)) | (((kt >> 1) & 1u) << st);
-                }
             }
-            if (!ok) {
-                // Let the loads in flight land before the CTA can exit (bounded grace period).
-                const unsigned long long t0 = globaltimer_ns();
-                if (q_issued)
-                    while (!mbar_try_wait(q_full, q_ph) && globaltimer_ns() - t0 < 100000000ull) {
-                    }
-                for (int i = 0; i < 2; ++i) {
-                    if (!((issued >> i) & 1u)) continue;
-                    while (!mbar_try_wait(&k_full[i], (issued_ph >> i) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
-                    }
+            for (int j = 0; j < T; ++j, ++rt) {
+                const int st = rt & 1;
+                uint64_t *emp = kside ? &b.k_empty[st] : &b.v_empty[st];
+                uint64_t *ful = kside ? &b.k_full[st] : &b.v_full[st];
+                if (rt >= 2 && !mbar_wait(emp, ((rt - 2) >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER)) {
+                    ok = false;
+                    break;
                 }
+                mbar_arrive_expect_tx(ful, kTileBytes);
+                tma_load_2d(base + (kside ? OFF_K : OFF_V) + st * kTileBytes, kside ? &tmK : &tmV, ful, col,
+                            row0 + j * kTileRows);
+                issued |= 1u << st;
+                issued_ph = (issued_ph & ~(1u << st)) | (((rt >> 1) & 1u) << st);
             }
-        } else if (lane == 1) {
-            // ---- the V ring ----
-            uint32_t vt = 0;
-            uint32_t issued = 0, issued_ph = 0;
-            bool ok = true;
-            for (int64_t it = first; it < last && ok; ++it) {
-                const Item im = decode_item(p, it);
-                const int32_t row0 = im.g * n, col = im.h * 64;
-                for (int j = 0; j < T; ++j, ++vt) {
-                    const int st = vt & 1;
-                    if (vt >= 2 && !mbar_wait(&v_empty[st], ((vt - 2) >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-                    tma_load_2d(smem + OFF_V + st * kTileBytes, &tmV, &v_full[st], col, row0 + j * kTileRows);
-                    issued |= 1u << st;
-                    issued_ph = (issued_ph & ~(1u << st)) | (((vt >> 1) & 1u) << st);
+        }
+        if (!ok) {
+            // Let the loads in flight land before the CTA can exit (bounded grace period).
+            const unsigned long long t0 = globaltimer_ns();
+            if (q_issued)
+                while (!mbar_try_wait(&b.q_full, q_ph) && globaltimer_ns() - t0 < 100000000ull) {
                 }
-            }
-            if (!ok) {
-                const unsigned long long t0 = globaltimer_ns();
-                for (int i = 0; i < 2; ++i) {
-                    if (!((issued >> i) & 1u)) continue;
-                    while (!mbar_try_wait(&v_full[i], (issued_ph >> i) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
-                    }
+            for (int i = 0; i < 2; ++i) {
+                if (!((issued >> i) & 1u)) continue;
+                uint64_t *ful = kside ? &b.k_full[i] : &b.v_full[i];
+                while (!mbar_try_wait(ful, (issued_ph >> i) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
                 }
             }
         }
-    } else if (warp == 10) {
-        // ---- key biases of each item, one slot ahead ----
+    } else if (warp == 11) {
+        // ---- key masks of the coming items, in item order ----
+        uint32_t wi[2] = {0, 0};
         for (int64_t it = first; it < last; ++it) {
-            const uint32_t wi = (uint32_t)(it - first), slot = wi & 1;
-            if (wi >= 2) {
-                const bool got = mbar_wait(&bias_empty[slot], ((wi >> 1) - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER);
+            const int q = (int)((it - first) & 1);
+            PipeBars &b = pb[q];
+            const uint32_t i = wi[q]++, slot = i & 1;
+            if (i >= 2) {
+                const bool got = mbar_wait(&b.m_empty[slot], ((i >> 1) - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER);
                 if (!__all_sync(0xffffffffu, got)) break;
             }
             const Item im = decode_item(p, it);
             const uint8_t *kv = p.key_valid ? p.key_valid + (int64_t)im.g * p.kvs : nullptr;
-            float *b = kbias + slot * kMaxKeys;
-            uint64_t full = 0;
+            MaskSlot &m = mslots[q * 2 + slot];
             bool any = false;
             for (int t = 0; t < T; ++t) {
-                bool tile_ok = true;
+                bool all_valid = true, prefix = true;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int key = t * kTileRows + q * 32 + lane;
-                    const bool v = key < n && (kv == nullptr || key >= p.kvs || kv[key] != 0);
-                    b[key] = v ? 0.0f : -INFINITY;
-                    tile_ok = tile_ok && v;
+                for (int w = 0; w < 4; ++w) {
+                    const int key = t * kTileRows + w * 32 + lane;
+                    const bool inside = key < n;
+                    const bool v = inside && (kv == nullptr || key >= p.kvs || kv[key] != 0);
+                    const uint32_t bits = __ballot_sync(0xffffffffu, v);
+                    if (lane == 0) m.bits[t * 4 + w] = bits;
+                    all_valid = all_valid && v;
+                    prefix = prefix && (v == inside);
                     any = any || v;
                 }
-                if (__all_sync(0xffffffffu, tile_ok)) full |= 1ull << t;
+                all_valid = __all_sync(0xffffffffu, all_valid);
+                prefix = __all_sync(0xffffffffu, prefix);
+                if (lane == 0) m.cls[t] = all_valid ? TILE_FULL : prefix ? TILE_PREFIX : TILE_BITS;
             }
             const bool uniform = !__any_sync(0xffffffffu, any);
-            if (uniform) {
-                // No valid key: every key below n gets bias 0 and score 0 (equal weights).
-                for (int key = lane; key < T * kTileRows; key += 32) b[key] = key < n ? 0.0f : -INFINITY;
-                full = 0;
-            }
-            if (lane == 0) {
-                binfo[slot].uniform = uniform ? 1u : 0u;
-                binfo[slot].full = full;
-            }
+            if (lane == 0) m.uniform = uniform ? 1u : 0u;
             __syncwarp();
-            mbar_arrive(&bias_full[slot]);
+            mbar_arrive(&b.m_full[slot]);
         }
-    } else if (warp == 9) {
-        // ---- MMA issuer ----
+    } else if (warp == 9 || warp == 10) {
+        // ---- MMA issuer of pipeline warp - 9 ----
         if (lane == 0) {
+            const int q = warp - 9;
+            PipeBars &b = pb[q];
+            uint8_t *base = smem + q * PIPE_BYTES;
+            const uint32_t t_s = tmem_base + q * 256 + TM_S, t_p = tmem_base + q * 256 + TM_P;
+            const uint32_t t_o = tmem_base + q * 256 + TM_O;
             bool ok = true;
-            uint32_t kt = 0, vt = 0;     // K / V ring positions
-            uint32_t ns[2] = {0, 0};     // S tiles issued per query tile
-            uint32_t np[2] = {0, 0};     // PV issued per query tile
-            const uint64_t qd0 = sdesc_k128(smem + OFF_Q), qd1 = sdesc_k128(smem + OFF_Q + kTileBytes);
-            // PV of one query tile for the V tile at ring position vt.
-            auto pv_one = [&](int x, bool first_tile) -> bool {
-                if (!mbar_wait(&p_ready[x], np[x] & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
+            uint32_t kt = 0, vt = 0, ns = 0, np = 0, wi = 0;
+            const uint64_t qd = sdesc_k128(base + OFF_Q);
+            auto pv = [&](bool first_tile) -> bool {
+                const int st = vt & 1;
+                if (!mbar_wait(&b.v_full[st], (vt >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
+                if (!mbar_wait(&b.p_ready, np & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
                 tc_fence_after();
-                const uint64_t vd = sdesc_k128(smem + OFF_V + (vt & 1) * kTileBytes);
-                const uint64_t pd = sdesc_k128(smem + OFF_P + x * kPBytes);
+                const uint64_t vd = sdesc_k128(base + OFF_V + st * kTileBytes);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    // A: 16 keys = 32 bytes inside a 64-key swizzle column; B: 16 key rows = 2048 bytes.
-                    const uint64_t a = pd + (uint64_t)((kk >> 2) * (kTileBytes >> 4) + 2 * (kk & 3));
-                    const uint64_t b = vd + (uint64_t)(kk * (2048 >> 4));
-                    mma_f16kind(tmem_base + TM_O + 64 * x, a, b, IDESC_PV, (!first_tile || kk > 0) ? 1u : 0u);
-                }
-                mma_commit(&o_done[x]);
-                ++np[x];
+                for (int kk = 0; kk < 8; ++kk)  // A: 16 keys = 8 TMEM columns; B: 16 key rows = 2048 bytes
+                    mma_f16kind_ts(t_o, t_p + 8 * kk, vd + (uint64_t)(kk * (2048 >> 4)), IDESC_PV,
+                                   (!first_tile || kk > 0) ? 1u : 0u);
+                mma_commit(&b.o_done);
+                mma_commit(&b.v_empty[st]);
+                ++np;
+                ++vt;
                 return true;
             };
-            // Issue order per key tile j: S_A(j), PV_A(j-1), S_B(j), PV_B(j-1). Each PV then waits
-            // in the in-order tensor pipe behind at most its own tile's S, so o_done follows
-            // p_ready closely, and the two query tiles settle into alternating phases.
-            for (int64_t it = first; it < last && ok; ++it) {
-                const Item im = decode_item(p, it);
-                const int ntile = im.hasB ? 2 : 1;
-                const uint32_t wi = (uint32_t)(it - first);
-                if (!mbar_wait(q_full, wi & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+            for (int64_t it = first + q; it < last && ok; it += 2, ++wi) {
+                if (!mbar_wait(&b.q_full, wi & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
                     ok = false;
                     break;
                 }
                 for (int j = 0; j < T && ok; ++j, ++kt) {
                     const int st = kt & 1;
-                    if (!mbar_wait(&k_full[st], (kt >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+                    if (!mbar_wait(&b.k_full[st], (kt >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA) ||
+                        (ns > 0 && !mbar_wait(&b.s_free, (ns - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA))) {
                         ok = false;
                         break;
                     }
-                    if (j > 0 && !mbar_wait(&v_full[vt & 1], (vt >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint64_t kd = sdesc_k128(smem + OFF_K + st * kTileBytes);
-                    for (int x = 0; x < ntile && ok; ++x) {
-                        if (ns[x] > 0 && !mbar_wait(&s_free[x], (ns[x] - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint64_t qd = x ? qd1 : qd0;
+                    tc_fence_after();
+                    const uint64_t kd = sdesc_k128(base + OFF_K + st * kTileBytes);
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            mma_f16kind(tmem_base + TM_S + 128 * x, qd + 2 * kk, kd + 2 * kk, IDESC_S, kk > 0 ? 1u : 0u);
-                        mma_commit(&s_full[x]);
-                        ++ns[x];
-                        if (j > 0 && !pv_one(x, j == 1)) ok = false;
-                    }
-                    if (!ok) break;
-                    mma_commit(&k_empty[st]);
-                    if (j == T - 1) mma_commit(q_empty);  // the Q tiles are free once these S complete
-                    if (j > 0) {
-                        mma_commit(&v_empty[vt & 1]);
-                        ++vt;
-                    }
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_f16kind(t_s, qd + 2 * kk, kd + 2 * kk, IDESC_S, kk > 0 ? 1u : 0u);
+                    mma_commit(&b.s_full);
+                    mma_commit(&b.k_empty[st]);
+                    if (j == T - 1) mma_commit(&b.q_empty);  // Q is free once these S complete
+                    ++ns;
+                    if (j > 0 && !pv(j == 1)) ok = false;
                 }
-                if (!ok) break;
-                // The last key tile's PV.
-                if (!mbar_wait(&v_full[vt & 1], (vt >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
-                    ok = false;
-                    break;
-                }
-                for (int x = 0; x < ntile && ok; ++x)
-                    if (!pv_one(x, T == 1)) ok = false;
-                if (!ok) break;
-                mma_commit(&v_empty[vt & 1]);
-                ++vt;
+                if (ok && !pv(T == 1)) ok = false;
             }
-            mma_commit(drain);
+            mma_commit(&drain[q]);
             const unsigned long long t0 = globaltimer_ns();
-            while (!mbar_try_wait(drain, 0)) {
+            while (!mbar_try_wait(&drain[q], 0)) {
                 if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
                     if (p.err) atomicCAS(p.err, 0, ERR_SITE_ATTN_DRAIN);
                     break;
                 }
             }
         }
-    } else {
-        // ---- softmax warps 0-7 ----
-        const int x = warp >> 2;          // query tile
-        const int quarter = warp & 3;     // TMEM lane quarter
+    } else if (warp < 8) {
+        // ---- softmax of pipeline warp / 4 ----
+        const int q = warp >> 2;
+        const int quarter = warp & 3;  // TMEM lane quarter
         const int r = quarter * 32 + lane;
-        const uint32_t t_s = tmem_base + ((uint32_t)(quarter * 32) << 16) + TM_S + 128 * x;
-        const uint32_t t_o = tmem_base + ((uint32_t)(quarter * 32) << 16) + TM_O + 64 * x;
-        uint8_t *sp = smem + OFF_P + x * kPBytes;
+        PipeBars &b = pb[q];
+        const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+        const uint32_t t_s = tmem_base + lanes + q * 256 + TM_S;
+        const uint32_t t_p = tmem_base + lanes + q * 256 + TM_P;
+        const uint32_t t_o = tmem_base + lanes + q * 256 + TM_O;
         const float sl2 = p.scale_log2;
-        uint32_t cx = 0;  // tiles processed by this query tile so far
+        uint32_t cx = 0, wi = 0;  // tiles / items processed by this pipeline
         bool ok = true;
-        for (int64_t it = first; it < last && ok; ++it) {
+        for (int64_t it = first + q; it < last && ok; it += 2, ++wi) {
             const Item im = decode_item(p, it);
-            const uint32_t wi = (uint32_t)(it - first), slot = wi & 1;
+            const uint32_t slot = wi & 1;
             {
-                const bool got = mbar_wait(&bias_full[slot], (wi >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
+                const bool got = mbar_wait(&b.m_full[slot], (wi >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
                 if (!__all_sync(0xffffffffu, got)) break;
             }
-            if (x == 0 || im.hasB) {
-                const float *bias = kbias + slot * kMaxKeys;
-                const bool uniform = binfo[slot].uniform != 0;
-                const uint64_t full = binfo[slot].full;
-                float m_run = -INFINITY, l_run = 0.0f;
-                for (int j = 0; j < T; ++j, ++cx) {
-                    const bool got = mbar_wait(&s_full[x], cx & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
-                    if (!__all_sync(0xffffffffu, got)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    float s[128];
-                    {
-                        float c0[32], c1[32], c2[32], c3[32];
-                        tmem_ld32(t_s + 0, c0);
-                        tmem_ld32(t_s + 32, c1);
-                        tmem_ld32(t_s + 64, c2);
-                        tmem_ld32(t_s + 96, c3);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            s[i] = c0[i];
-                            s[32 + i] = c1[i];
-                            s[64 + i] = c2[i];
-                            s[96 + i] = c3[i];
-                        }
-                    }
-                    tc_fence_before();
-                    mbar_arrive(&s_free[x]);
-
-                    // Key biases (0 / -inf), broadcast from shared memory; uniform groups replace
-                    // the scores by the biases.
-                    if (!((full >> j) & 1ull)) {
-                        const float4 *b4 = reinterpret_cast<const float4 *>(bias + j * kTileRows);
-                        if (uniform) {
-#pragma unroll
-                            for (int q = 0; q < 32; ++q) {
-                                const float4 bb = b4[q];
-                                s[4 * q] = bb.x;
-                                s[4 * q + 1] = bb.y;
-                                s[4 * q + 2] = bb.z;
-                                s[4 * q + 3] = bb.w;
-                            }
-                        } else {
-#pragma unroll
-                            for (int q = 0; q < 32; ++q) {
-                                const float4 bb = b4[q];
-                                s[4 * q] += bb.x;
-                                s[4 * q + 1] += bb.y;
-                                s[4 * q + 2] += bb.z;
-                                s[4 * q + 3] += bb.w;
-                            }
-                        }
-                    }
-                    // Four partial maxima / sums keep the dependency chains short.
-                    float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-                    for (int i = 0; i < 128; ++i) mxp[i & 3] = fmaxf(mxp[i & 3], s[i]);
-                    const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
-                    // Lazy rescale: keep the stale max unless the new one exceeds it by 2^8.
-                    const float m_new = fmaxf(m_run, mx);
-                    float alpha = 1.0f;
-                    bool rescale = false;
-                    if (m_new > m_run && (m_run == -INFINITY || (m_new - m_run) * sl2 > kRescaleThreshold)) {
-                        alpha = m_run == -INFINITY ? 0.0f : ex2_approx((m_run - m_new) * sl2);
-                        m_run = m_new;
-                        rescale = true;
-                    }
-                    const float mb = m_run == -INFINITY ? 0.0f : m_run * sl2;
-
-                    // P overwrites the previous tile's P, and O is rescaled below: both need the
-                    // previous PV of this query tile complete.
-                    if (cx > 0) {
-                        const bool done = mbar_wait(&o_done[x], (cx - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
-                        if (!__all_sync(0xffffffffu, done)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                    }
-                    // P row r into the K-major, 128-byte-swizzled layout: 16-byte chunk c of the
-                    // row (keys 8c .. 8c + 7) sits in swizzle column c / 8 at chunk (c % 8) ^ (r % 8).
-                    float sp4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float a = ex2_approx(fmaf(s[8 * c + 2 * e], sl2, -mb));
-                            const float b = ex2_approx(fmaf(s[8 * c + 2 * e + 1], sl2, -mb));
-                            sp4[e] += a + b;
-                            pk[e] = pack_p<F16>(a, b);
-                        }
-                        uint8_t *dst = sp + (c >> 3) * kTileBytes + r * 128 + ((((c & 7) ^ (r & 7))) << 4);
-                        *reinterpret_cast<uint4 *>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    }
-                    l_run = l_run * alpha + ((sp4[0] + sp4[1]) + (sp4[2] + sp4[3]));
-                    if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-                        for (int hcol = 0; hcol < 64; hcol += 32) {
-                            float ov[32];
-                            tmem_ld32(t_o + hcol, ov);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-                            tmem_st32(t_o + hcol, ov);
-                        }
-                        tmem_wait_st();
-                    }
-                    fence_proxy_async_smem();
-                    tc_fence_before();
-                    mbar_arrive(&p_ready[x]);
-                }
-                if (!ok) break;
-                // Output rows of this query tile.
-                const bool done = mbar_wait(&o_done[x], (cx - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
-                if (!__all_sync(0xffffffffu, done)) {
+            const MaskSlot &m = mslots[q * 2 + slot];
+            const bool uniform = m.uniform != 0;
+            float m_run = -INFINITY, l_run = 0.0f;
+            for (int j = 0; j < T; ++j, ++cx) {
+                const bool got = mbar_wait(&b.s_full, cx & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
+                if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                float o0[32], o1[32];
-                tmem_ld32(t_o, o0);
-                tmem_ld32(t_o + 32, o1);
-                tmem_wait_ld();
-                const int tok = im.q0 + x * kTileRows + r;
-                if (tok < n) {
-                    const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-                    uint16_t *dst = static_cast<uint16_t *>(p.o) + (int64_t)(im.g * n + tok) * p.ldo + im.h * 64;
+                float s[128];
+                {
+                    float c0[32], c1[32], c2[32], c3[32];
+                    tmem_ld32(t_s + 0, c0);
+                    tmem_ld32(t_s + 32, c1);
+                    tmem_ld32(t_s + 64, c2);
+                    tmem_ld32(t_s + 96, c3);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const float *src = c < 2 ? o0 + 16 * c : o1 + 16 * (c - 2);
-                        uint4 a, b;
-                        a.x = pack_p<F16>(src[0] * inv, src[1] * inv);
-                        a.y = pack_p<F16>(src[2] * inv, src[3] * inv);
-                        a.z = pack_p<F16>(src[4] * inv, src[5] * inv);
-                        a.w = pack_p<F16>(src[6] * inv, src[7] * inv);
-                        b.x = pack_p<F16>(src[8] * inv, src[9] * inv);
-                        b.y = pack_p<F16>(src[10] * inv, src[11] * inv);
-                        b.z = pack_p<F16>(src[12] * inv, src[13] * inv);
-                        b.w = pack_p<F16>(src[14] * inv, src[15] * inv);
-                        reinterpret_cast<uint4 *>(dst)[2 * c] = a;
-                        reinterpret_cast<uint4 *>(dst)[2 * c + 1] = b;
+                    for (int i = 0; i < 32; ++i) {
+                        s[i] = c0[i];
+                        s[32 + i] = c1[i];
+                        s[64 + i] = c2[i];
+                        s[96 + i] = c3[i];
                     }
                 }
+                tc_fence_before();
+                mbar_arrive(&b.s_free);
+
+                // Mask: valid prefix of the tile (keys below n), or per-key bits; uniform groups
+                // give every key below n the score 0.
+                const int cls = m.cls[j];
+                if (uniform || cls == TILE_PREFIX) {
+                    const int cnt = n - j * kTileRows;
+                    const float keep = uniform ? 0.0f : 1.0f;
+#pragma unroll
+                    for (int i = 0; i < 128; ++i) s[i] = i < cnt ? s[i] * keep : -INFINITY;
+                } else if (cls == TILE_BITS) {
+                    const uint32_t wd[4] = {m.bits[4 * j], m.bits[4 * j + 1], m.bits[4 * j + 2], m.bits[4 * j + 3]};
+#pragma unroll
+                    for (int i = 0; i < 128; ++i) s[i] = ((wd[i >> 5] >> (i & 31)) & 1u) ? s[i] : -INFINITY;
+                }
+                // Four partial maxima keep the dependency chains short.
+                float mxp[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+                for (int i = 4; i < 128; ++i) mxp[i & 3] = fmaxf(mxp[i & 3], s[i]);
+                const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+                // Lazy rescale: keep the stale max unless the new one exceeds it by 2^8.
+                const float m_new = fmaxf(m_run, mx);
+                float alpha = 1.0f;
+                bool rescale = false;
+                if (m_new > m_run && (m_run == -INFINITY || (m_new - m_run) * sl2 > kRescaleThreshold)) {
+                    alpha = m_run == -INFINITY ? 0.0f : ex2_approx((m_run - m_new) * sl2);
+                    m_run = m_new;
+                    rescale = true;
+                }
+                const float mb = m_run == -INFINITY ? 0.0f : m_run * sl2;
+
+                // P overwrites the previous tile's P in TMEM, and O is rescaled below: both need
+                // this pipeline's previous PV complete.
+                if (cx > 0) {
+                    const bool done = mbar_wait(&b.o_done, (cx - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
+                    if (!__all_sync(0xffffffffu, done)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                }
+                float sp4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int qc = 0; qc < 4; ++qc) {
+                    uint32_t pk[16];  // 32 keys as 16 packed 16-bit pairs
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const float a = ex2_approx(fmaf(s[32 * qc + 2 * e], sl2, -mb));
+                        const float c = ex2_approx(fmaf(s[32 * qc + 2 * e + 1], sl2, -mb));
+                        sp4[e & 3] += a + c;
+                        pk[e] = pack_p<F16>(a, c);
+                    }
+                    tmem_st16(t_p + 16 * qc, pk);
+                }
+                l_run = l_run * alpha + ((sp4[0] + sp4[1]) + (sp4[2] + sp4[3]));
+                if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+                    for (int hcol = 0; hcol < 64; hcol += 32) {
+                        float ov[32];
+                        tmem_ld32(t_o + hcol, ov);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                        tmem_st32(t_o + hcol, ov);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&b.p_ready);
             }
-            // The bias slot is free once both query tiles are done with this item. The O tile is
-            // in registers: the next item's first PV (accumulate = 0) may overwrite it once this
-            // thread's next p_ready arrives.
-            mbar_arrive(&bias_empty[slot]);
+            if (!ok) break;
+            // The mask slot is free; the output rows of this tile follow once the last PV is done.
+            mbar_arrive(&b.m_empty[slot]);
+            const bool done = mbar_wait(&b.o_done, (cx - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
+            if (!__all_sync(0xffffffffu, done)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float o0[32], o1[32];
+            tmem_ld32(t_o, o0);
+            tmem_ld32(t_o + 32, o1);
+            tmem_wait_ld();
+            // The next item's first PV (accumulate = 0) may overwrite O once this thread's next
+            // p_ready arrives, which follows these loads in program order.
+            const int tok = im.q0 + r;
+            if (tok < n) {
+                const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+                uint16_t *dst = static_cast<uint16_t *>(p.o) + (int64_t)(im.g * n + tok) * p.ldo + im.h * 64;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float *src = c < 2 ? o0 + 16 * c : o1 + 16 * (c - 2);
+                    uint4 a, bb;
+                    a.x = pack_p<F16>(src[0] * inv, src[1] * inv);
+                    a.y = pack_p<F16>(src[2] * inv, src[3] * inv);
+                    a.z = pack_p<F16>(src[4] * inv, src[5] * inv);
+                    a.w = pack_p<F16>(src[6] * inv, src[7] * inv);
+                    bb.x = pack_p<F16>(src[8] * inv, src[9] * inv);
+                    bb.y = pack_p<F16>(src[10] * inv, src[11] * inv);
+                    bb.z = pack_p<F16>(src[12] * inv, src[13] * inv);
+                    bb.w = pack_p<F16>(src[14] * inv, src[15] * inv);
+                    reinterpret_cast<uint4 *>(dst)[2 * c] = a;
+                    reinterpret_cast<uint4 *>(dst)[2 * c + 1] = bb;
+                }
+            }
         }
     }
 
@@ -587,11 +516,11 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     p.n = c.n;
     p.heads = c.heads;
     p.groups = c.groups;
-    p.pairs = (c.n + 2 * kTileRows - 1) / (2 * kTileRows);
-    p.items = (int64_t)c.groups * c.heads * p.pairs;
+    p.qtiles = (c.n + kTileRows - 1) / kTileRows;
+    p.items = (int64_t)c.groups * c.heads * p.qtiles;
     p.scale_log2 = c.scale * 1.4426950408889634f;
     p.err = c.err;
-    const int64_t grid = std::min<int64_t>(p.items, num_sms());
+    const int64_t grid = std::min<int64_t>((p.items + 1) / 2, num_sms());
     cudaError_t e;
     if (c.dtype == E_F16) {
         e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
