@@ -92,13 +92,14 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
 struct Item {
     int g, h, q0;
 };
-__device__ __forceinline__ Item decode_item(const TcParams &p, int64_t it) {
+// Items fit in 31 bits (checked on the host), so the decode uses 32-bit division.
+__device__ __forceinline__ Item decode_item(const TcParams &p, int64_t it64) {
     Item r;
-    const int qt = (int)(it % p.qtiles);
-    const int64_t gh = it / p.qtiles;
-    r.h = (int)(gh % p.heads);
-    r.g = (int)(gh / p.heads);
-    r.q0 = qt * kTileRows;
+    const uint32_t it = (uint32_t)it64, qtiles = (uint32_t)p.qtiles, heads = (uint32_t)p.heads;
+    const uint32_t gh = it / qtiles;
+    r.q0 = (int)(it - gh * qtiles) * kTileRows;
+    r.g = (int)(gh / heads);
+    r.h = (int)(gh - (uint32_t)r.g * heads);
     return r;
 }
 
@@ -345,12 +346,30 @@ __global__ void __maxnreg__(168)
             }
             const MaskSlot &m = mslots[q * 2 + slot];
             const bool uniform = m.uniform != 0;
+            // A warp whose 32 query rows all lie past n has no output: it only keeps the barrier
+            // protocol (its P and O rows are never read back).
+            const bool dead = im.q0 + quarter * 32 >= n;
             float m_run = -INFINITY, l_run = 0.0f;
             for (int j = 0; j < T; ++j, ++cx) {
                 const bool got = mbar_wait(&b.s_full, cx & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
+                }
+                if (dead) {
+                    // p_ready of this tile may only count once the previous phase completed:
+                    // wait for the previous PV like the live warps.
+                    tc_fence_before();
+                    mbar_arrive(&b.s_free);
+                    if (cx > 0) {
+                        const bool done = mbar_wait(&b.o_done, (cx - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
+                        if (!__all_sync(0xffffffffu, done)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    mbar_arrive(&b.p_ready);
+                    continue;
                 }
                 tc_fence_after();
                 float s[128];
@@ -385,11 +404,11 @@ __global__ void __maxnreg__(168)
 #pragma unroll
                     for (int i = 0; i < 128; ++i) s[i] = ((wd[i >> 5] >> (i & 31)) & 1u) ? s[i] : -INFINITY;
                 }
-                // Four partial maxima keep the dependency chains short.
+                // Three-input maxima on four partial chains keep the dependency chains short.
                 float mxp[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-                for (int i = 4; i < 128; ++i) mxp[i & 3] = fmaxf(mxp[i & 3], s[i]);
-                const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+                for (int i = 4; i + 1 < 124; i += 2) mxp[(i >> 1) & 3] = max3(mxp[(i >> 1) & 3], s[i], s[i + 1]);
+                const float mx = max3(max3(mxp[0], mxp[1], mxp[2]), max3(mxp[3], s[124], s[125]), fmaxf(s[126], s[127]));
                 // Lazy rescale: keep the stale max unless the new one exceeds it by 2^8.
                 const float m_new = fmaxf(m_run, mx);
                 float alpha = 1.0f;
@@ -412,9 +431,17 @@ __global__ void __maxnreg__(168)
                     tc_fence_after();
                 }
                 float sp4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                // Quarters of a prefix tile past the last valid key hold only zeros.
+                const int live = (uniform || cls == TILE_PREFIX) ? n - j * kTileRows : kTileRows;
 #pragma unroll
                 for (int qc = 0; qc < 4; ++qc) {
                     uint32_t pk[16];  // 32 keys as 16 packed 16-bit pairs
+                    if (32 * qc >= live) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) pk[e] = 0u;
+                        tmem_st16(t_p + 16 * qc, pk);
+                        continue;
+                    }
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         const float a = ex2_approx(fmaf(s[32 * qc + 2 * e], sl2, -mb));
@@ -443,6 +470,7 @@ __global__ void __maxnreg__(168)
             if (!ok) break;
             // The mask slot is free; the output rows of this tile follow once the last PV is done.
             mbar_arrive(&b.m_empty[slot]);
+            if (dead) continue;
             const bool done = mbar_wait(&b.o_done, (cx - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
             if (!__all_sync(0xffffffffu, done)) {
                 ok = false;
@@ -457,7 +485,7 @@ __global__ void __maxnreg__(168)
             // p_ready arrives, which follows these loads in program order.
             const int tok = im.q0 + r;
             if (tok < n) {
-                const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+                const float inv = l_run > 0.0f ? __frcp_rn(l_run) : 0.0f;
                 uint16_t *dst = static_cast<uint16_t *>(p.o) + (int64_t)(im.g * n + tok) * p.ldo + im.h * 64;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -494,6 +522,7 @@ bool attention_tc_supported(const AttentionCall &c) {
     if (c.dtype != E_F16 && c.dtype != E_BF16) return false;
     if (c.n <= 0 || c.n > kMaxKeys || c.heads <= 0 || c.groups <= 0) return false;
     if ((int64_t)c.groups * c.n > INT32_MAX - 2 * kTileRows) return false;
+    if ((int64_t)c.groups * c.heads * ((c.n + kTileRows - 1) / kTileRows) > INT32_MAX) return false;
     // TMA: 16-byte aligned bases and row strides; 16-byte aligned output rows.
     const auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     if (!a16(c.q) || !a16(c.k) || !a16(c.v) || !a16(c.o) || (c.ld_qkv % 8) || (c.ld_o % 8)) return false;

@@ -292,6 +292,13 @@ __device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t count, bool v
     return r != 0;
 }
 
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // 2^x on the SFU (the PTX instruction itself; inputs below -126 flush to +0, -inf gives +0).
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
