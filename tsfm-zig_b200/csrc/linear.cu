@@ -389,7 +389,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tbase = tmem_base + ((uint32_t)(eg * 32) << 16) + (uint32_t)(acc * BN);
             if (e.rope_cos != nullptr || (e.tma_mode != 0 && !f32_out)) {
                 // 64-column chunks (one head for RoPE): rotate-half pairs (i, i + 32) of columns
-                // < rope_cols.
+                // < rope_cols. The row's cos / sin (same for every head) load once per tile.
+                const bool rope_tile = e.rope_cos != nullptr && ncol0 < e.rope_cols && row_ok;
+                float rc[32], rs[32];
+                if (rope_tile) {
+                    const int64_t pidx = e.rope_p1 > 0 ? (row / e.rope_p1) * e.rope_p2 + row % e.rope_p2 : row % e.rope_p2;
+                    const float4 *cs = reinterpret_cast<const float4 *>(e.rope_cos + pidx * 32);
+                    const float4 *sn = reinterpret_cast<const float4 *>(e.rope_sin + pidx * 32);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 c4 = __ldg(cs + q), s4 = __ldg(sn + q);
+                        rc[4 * q] = c4.x;
+                        rc[4 * q + 1] = c4.y;
+                        rc[4 * q + 2] = c4.z;
+                        rc[4 * q + 3] = c4.w;
+                        rs[4 * q] = s4.x;
+                        rs[4 * q + 1] = s4.y;
+                        rs[4 * q + 2] = s4.z;
+                        rs[4 * q + 3] = s4.w;
+                    }
+                }
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 64) {
                     const int64_t col0 = ncol0 + c;
@@ -398,20 +417,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld32(tbase + c, lo);
                     tmem_ld32(tbase + c + 32, hi);
                     tmem_wait_ld();
-                    if (e.rope_cos != nullptr && col0 < e.rope_cols && row_ok) {
-                        const int64_t pidx = e.rope_p1 > 0 ? (row / e.rope_p1) * e.rope_p2 + row % e.rope_p2 : row % e.rope_p2;
-                        const float4 *cs = reinterpret_cast<const float4 *>(e.rope_cos + pidx * 32);
-                        const float4 *sn = reinterpret_cast<const float4 *>(e.rope_sin + pidx * 32);
+                    if (rope_tile && col0 < e.rope_cols) {
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            const float4 c4 = __ldg(cs + q), s4 = __ldg(sn + q);
-                            const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const float x1 = lo[4 * q + j], x2 = hi[4 * q + j];
-                                lo[4 * q + j] = x1 * cc[j] - x2 * ss[j];
-                                hi[4 * q + j] = x2 * cc[j] + x1 * ss[j];
-                            }
+                        for (int j = 0; j < 32; ++j) {
+                            const float x1 = lo[j], x2 = hi[j];
+                            lo[j] = x1 * rc[j] - x2 * rs[j];
+                            hi[j] = x2 * rc[j] + x1 * rs[j];
                         }
                     }
                     const int64_t rem0 = e.N - col0;
