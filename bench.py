@@ -47,6 +47,9 @@ def parse_args():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--series", type=int, default=SERIES_PER_GPU)
     ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
+    ap.add_argument("--workload", default="chronos2", choices=["chronos2", "bolt-small", "bolt-base", "timestral"],
+                    help="chronos2 is the headline; the others are BASELINE.json's other configs, timed through "
+                         "the host entry points (copies included)")
     return ap.parse_args()
 
 
@@ -68,11 +71,14 @@ class Clocks:
 
     def __init__(self, gpu):
         self.gpu, self.rows, self.proc = gpu, [], None
+        self.window = (0.0, 0.0)
 
-    def __enter__(self):
+    def start(self):
+        """Starts sampling every 50 ms (nvidia-smi needs a moment before its first line, so this
+        runs before the warm-up); only the samples inside mark_begin() .. mark_end() count."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -80,9 +86,20 @@ class Clocks:
             self.proc = None
         return self
 
+    def mark_begin(self):
+        self.window = (time.perf_counter(), float("inf"))
+
+    def mark_end(self):
+        self.window = (self.window[0], time.perf_counter())
+
+    def __enter__(self):
+        return self.start()
+
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+            now = time.perf_counter()
+            if self.window[0] <= now <= self.window[1]:
+                self.rows.append([c.strip() for c in line.split(",")])
 
     def __exit__(self, *a):
         if self.proc:
@@ -176,6 +193,61 @@ def run_reference(a, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_family_workload(a):
+    """BASELINE.json's Chronos-Bolt and Timestral configs on one GPU, through the host entry points
+    (pinned inputs, host->device and device->host copies inside the timed region)."""
+    import torch
+    from tsfm_b200 import Model, covariates, synthetic as syn, timestral_options
+    if a.workload == "bolt-small":
+        cfg = syn.bolt_config()
+        b, horizon, ctx = 64, 64, 2048
+    elif a.workload == "bolt-base":
+        cfg = syn.bolt_config(d_model=768, d_ff=3072, num_heads=12, num_layers=12)
+        b, horizon, ctx = 4096, 256, 2048
+    else:
+        cfg = syn.timestral_config(d_model=1024, num_heads=16, mlp_hidden_dim=4096, num_layers=16, patch=32,
+                                   context_length=4096, block_size=32)
+        b, horizon, ctx = 128, 512, 4096
+    w = syn.random_checkpoint(cfg, seed=20261201)
+    model = Model(cfg, w)
+    del w
+    if a.workload.startswith("bolt"):
+        x = torch.from_numpy(syn.seeded_series(b, ctx, seed=2000)).pin_memory().numpy()
+        out = torch.empty((b, horizon, 9), dtype=torch.float32).pin_memory().numpy()
+        run = lambda: model.forecast_bolt(x, horizon, out=out)
+        h2d, d2h = x.nbytes, out.nbytes
+    else:
+        v = 8
+        xs = syn.seeded_series(b * v, ctx, seed=3000).reshape(b, v, ctx)
+        past = syn.ar1_covariates(b, 2, ctx, seed=31)
+        known = syn.ar1_covariates(b, 1, ctx + horizon, seed=32)
+        cov = covariates(past=past, known=known)
+        opts = timestral_options()
+        out = np.empty((b, v, horizon, 9), np.float32)
+        run = lambda: model.forecast_timestral(xs, horizon, cov=cov, opts=opts, out=out)
+        h2d = xs.size * 5 + past.nbytes + known.nbytes
+        d2h = out.nbytes
+    for _ in range(max(1, min(a.warmup, 2))):
+        run()
+    torch.cuda.synchronize()
+    steps = max(1, min(a.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run()
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) / steps * 1e3
+    line = {"metric": f"forecast series/sec ({a.workload}, BASELINE.json config)", "value": b / (ms / 1e3),
+            "unit": "series/s", "n_gpus": 1, "steps": steps, "ms_per_step": ms, "higher_is_better": True,
+            "dtype": "f16", "data": "synthetic (seeded series, random-init N(0,0.02) weights)",
+            "config": {"workload": a.workload, "series": b, "context": ctx, "horizon": horizon,
+                       "timing": "host entry point, pinned buffers, copies included"},
+            "e2e": {"value": b / (ms / 1e3), "unit": "series/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": model.last_launch_count()}
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
 def main():
     a = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -183,6 +255,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.impl == "reference":
         return run_reference(a, rank)
+    if a.workload != "chronos2":
+        if rank == 0:
+            run_family_workload(a)
+        return
 
     import torch
     import torch.distributed as dist
@@ -209,6 +285,7 @@ def main():
     def step():
         model.forecast_chronos2_device(xd.data_ptr(), b, CONTEXT, HORIZON, out.data_ptr(), sp)
 
+    clk = Clocks(local).start()
     for _ in range(max(3, a.warmup)):
         step()
     torch.cuda.synchronize()
@@ -218,15 +295,17 @@ def main():
     barrier()
     torch.cuda.synchronize()
     total_ms = 0.0
-    with Clocks(local) as clk:
-        for _ in range(a.steps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            step()
-            e1.record(stream)
-            e1.synchronize()
-            total_ms += e0.elapsed_time(e1)
+    clk.mark_begin()
+    for _ in range(a.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        e1.synchronize()
+        total_ms += e0.elapsed_time(e1)
+    clk.mark_end()
+    clk.__exit__()
     torch.cuda.synchronize()
     barrier()
     t = torch.tensor([total_ms], device="cuda")
