@@ -1,4 +1,4 @@
-// Inline-PTX helpers for sm_100a: mbarriers with bounded waits, TMA tile loads (no multicast),
+// Inline-PTX helpers for sm_100a: mbarriers with bounded waits, TMA tile loads into this CTA only,
 // tcgen05 tensor-memory allocation, MMA issue, commit and loads.
 //
 // Every wait on an mbarrier is bounded by wall time (%globaltimer). When a wait gives up it
@@ -101,7 +101,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
 }
 
 // 2-D tiled load of the box at (c0 = innermost, c1) into shared memory; completes on `bar`.
-// No multicast: each CTA loads its own tiles.
+// Each CTA loads its own tiles; no load is shared across the CTAs of a cluster.
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
                                             int32_t c0, int32_t c1) {
     asm volatile(
