@@ -99,6 +99,23 @@ def test_device_entry_point_matches_host_path(tiny):
     assert np.array_equal(out.cpu().numpy(), host)
 
 
+@pytest.mark.parametrize("b", [130, 257])
+def test_chunked_host_path_matches_device_path(tiny, b):
+    # Batches of 128+ series run as 2 or 4 chunks with the copies on a second stream; every series
+    # must come out exactly as from one device-resident forecast (pageable and pinned buffers).
+    _, _, gpu, _ = tiny
+    x = syn.seeded_series(b, 200, seed=11)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty((b, 48, 21), device="cuda")
+    gpu.forecast_chronos2_device(xd.data_ptr(), b, 200, 48, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    want = out.cpu().numpy()
+    assert np.array_equal(gpu.forecast_chronos2(x, 48), want)
+    xp = torch.from_numpy(x).pin_memory().numpy()
+    op = torch.empty((b, 48, 21)).pin_memory().numpy()
+    gpu.forecast_chronos2(xp, 48, out=op)
+    assert np.array_equal(op, want)
+
+
 def test_argument_errors(tiny):
     _, _, gpu, _ = tiny
     with pytest.raises(tb.TsfmError, match="HORIZON_TOO_LONG"):

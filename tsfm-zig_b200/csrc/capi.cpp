@@ -105,33 +105,59 @@ Status for_replicas(size_t n, F &&fn) {
     return Status::ok();
 }
 
-// Forecast `nb` series of one replica from host memory: inputs staged through pinned memory
-// (unless the caller's buffer is pinned already), the family's device forecast, results back.
+// Forecast `nb` series of one replica from host memory. Inputs are staged through pinned memory
+// unless the caller's buffer is pinned already. Large batches run as chunks: every chunk's inputs
+// go up on the copy stream first, the forwards run in order on the compute stream, and each
+// chunk's results come back on the copy stream while the next chunk computes.
 template <class Fwd>
-Status replica_forecast(Replica &r, const void *in, size_t in_bytes, size_t out_bytes, void *out, Fwd &&fwd) {
+Status replica_forecast(Replica &r, const void *in, int64_t nb, size_t in_row, size_t out_row, void *out, Fwd &&fwd) {
     std::lock_guard<std::mutex> lk(r.mu);
     TSFM_CUDA(cudaSetDevice(r.device), "cudaSetDevice");
     r.prof.cur_launches = 0;
+    const size_t in_bytes = (size_t)nb * in_row, out_bytes = (size_t)nb * out_row;
     const size_t in_span = Arena::span(in_bytes);
     if (r.io.bytes < in_span + out_bytes) TSFM_TRY(r.io.alloc(in_span + out_bytes));
-    float *d_in = static_cast<float *>(r.io.p);
-    float *d_out = reinterpret_cast<float *>(static_cast<char *>(r.io.p) + in_span);
+    char *d_in = static_cast<char *>(r.io.p);
+    char *d_out = static_cast<char *>(r.io.p) + in_span;
     const bool pin_in = is_pinned(in), pin_out = is_pinned(out);
-    const void *src = in;
+    const char *src = static_cast<const char *>(in);
     if (!pin_in) {
         TSFM_TRY(r.pin_in.ensure(in_bytes));
         std::memcpy(r.pin_in.p, in, in_bytes);
-        src = r.pin_in.p;
+        src = static_cast<const char *>(r.pin_in.p);
     }
-    TSFM_CUDA(cudaMemcpyAsync(d_in, src, in_bytes, cudaMemcpyHostToDevice, r.stream), "copy inputs");
-    TSFM_TRY(fwd(d_in, d_out, r.stream));
-    void *stage = out;
+    char *dst = static_cast<char *>(out);
     if (!pin_out) {
         TSFM_TRY(r.pin_out.ensure(out_bytes));
-        stage = r.pin_out.p;
+        dst = static_cast<char *>(r.pin_out.p);
     }
-    TSFM_CUDA(cudaMemcpyAsync(stage, d_out, out_bytes, cudaMemcpyDeviceToHost, r.stream), "copy results");
+    // 64 or more series per chunk keep every GEMM and attention launch device-filling.
+    const int64_t chunks = nb >= 256 ? 4 : nb >= 128 ? 2 : 1;
+    while ((int64_t)r.events.size() < 2 * chunks) {
+        cudaEvent_t e;
+        TSFM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+        r.events.push_back(e);
+    }
+    for (int64_t c = 0; c < chunks; ++c) {
+        const int64_t s0 = nb * c / chunks, s1 = nb * (c + 1) / chunks;
+        TSFM_CUDA(cudaMemcpyAsync(d_in + s0 * in_row, src + s0 * in_row, (s1 - s0) * in_row, cudaMemcpyHostToDevice,
+                                  r.copy),
+                  "copy inputs");
+        TSFM_CUDA(cudaEventRecord(r.events[2 * c], r.copy), "cudaEventRecord");
+    }
+    for (int64_t c = 0; c < chunks; ++c) {
+        const int64_t s0 = nb * c / chunks, s1 = nb * (c + 1) / chunks;
+        TSFM_CUDA(cudaStreamWaitEvent(r.stream, r.events[2 * c], 0), "cudaStreamWaitEvent");
+        TSFM_TRY(fwd(reinterpret_cast<const float *>(d_in + s0 * in_row), reinterpret_cast<float *>(d_out + s0 * out_row),
+                     s1 - s0, r.stream));
+        TSFM_CUDA(cudaEventRecord(r.events[2 * c + 1], r.stream), "cudaEventRecord");
+        TSFM_CUDA(cudaStreamWaitEvent(r.copy, r.events[2 * c + 1], 0), "cudaStreamWaitEvent");
+        TSFM_CUDA(cudaMemcpyAsync(dst + s0 * out_row, d_out + s0 * out_row, (s1 - s0) * out_row, cudaMemcpyDeviceToHost,
+                                  r.copy),
+                  "copy results");
+    }
     TSFM_CUDA(cudaStreamSynchronize(r.stream), "forecast");
+    TSFM_CUDA(cudaStreamSynchronize(r.copy), "copy results");
     if (!pin_out) std::memcpy(out, r.pin_out.p, out_bytes);
     TSFM_TRY(check_device_error(r));
     r.prof.collect();
@@ -257,6 +283,7 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
             r->device = devs[i];
             TSFM_CUDA(cudaSetDevice(r->device), "cudaSetDevice");
             TSFM_CUDA(cudaStreamCreateWithFlags(&r->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+            TSFM_CUDA(cudaStreamCreateWithFlags(&r->copy, cudaStreamNonBlocking), "cudaStreamCreate");
             TSFM_TRY(r->err.alloc(16));
             TSFM_CUDA(cudaMemset(r->err.p, 0, 16), "clear error word");
             if (c.family == TSFM_CHRONOS2) {
@@ -310,9 +337,9 @@ int32_t tsfm_forecast_chronos2(tsfm_model *model, const float *inputs, size_t b,
             Replica &r = *model->reps[i];
             const C2Dev &w = *model->c2[i];
             const int64_t nb = s1 - s0;
-            return replica_forecast(r, inputs + s0 * t, (size_t)nb * t * 4, (size_t)nb * horizon * q * 4,
-                                    out + s0 * horizon * q, [&](const float *d_in, float *d_out, cudaStream_t s) {
-                                        return c2_forecast(r, model->cfg, w, d_in, nb, (int64_t)t, (int64_t)horizon,
+            return replica_forecast(r, inputs + s0 * t, nb, t * 4, horizon * q * 4, out + s0 * horizon * q,
+                                    [&](const float *d_in, float *d_out, int64_t nc, cudaStream_t s) {
+                                        return c2_forecast(r, model->cfg, w, d_in, nc, (int64_t)t, (int64_t)horizon,
                                                            d_out, s);
                                     });
         });
@@ -349,9 +376,9 @@ int32_t tsfm_forecast_bolt(tsfm_model *model, const float *inputs, size_t b, siz
             Replica &r = *model->reps[i];
             const BoltDev &w = *model->bolt[i];
             const int64_t nb = s1 - s0;
-            return replica_forecast(r, inputs + s0 * t, (size_t)nb * t * 4, (size_t)nb * horizon * q * 4,
-                                    out + s0 * horizon * q, [&](const float *d_in, float *d_out, cudaStream_t s) {
-                                        return bolt_forecast(r, model->cfg, w, d_in, nb, (int64_t)t, (int64_t)horizon,
+            return replica_forecast(r, inputs + s0 * t, nb, t * 4, horizon * q * 4, out + s0 * horizon * q,
+                                    [&](const float *d_in, float *d_out, int64_t nc, cudaStream_t s) {
+                                        return bolt_forecast(r, model->cfg, w, d_in, nc, (int64_t)t, (int64_t)horizon,
                                                              d_out, s);
                                     });
         });

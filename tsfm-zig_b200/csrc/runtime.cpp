@@ -103,10 +103,10 @@ LaunchScope::~LaunchScope() {
 }
 
 Replica::~Replica() {
-    if (stream) {
-        cudaSetDevice(device);
-        cudaStreamDestroy(stream);
-    }
+    cudaSetDevice(device);
+    for (cudaEvent_t e : events) cudaEventDestroy(e);
+    if (copy) cudaStreamDestroy(copy);
+    if (stream) cudaStreamDestroy(stream);
 }
 
 TensorTable::TensorTable(const tsfm_tensor *t, size_t n) {

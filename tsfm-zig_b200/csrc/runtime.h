@@ -128,6 +128,8 @@ struct Arena {
 struct Replica {
     int device = 0;
     cudaStream_t stream = nullptr;
+    cudaStream_t copy = nullptr;      // host<->device copies that overlap the forward on `stream`
+    std::vector<cudaEvent_t> events;  // chunk hand-offs between the two streams
     DevBuf err;  // device error word(s)
     std::vector<DevBuf> weights;
     Arena ws;   // per-chunk model workspace
