@@ -4,19 +4,28 @@
 // (group, head, 128-query tile). The CTA runs two independent pipelines; pipeline p takes every
 // other item of the range, so the softmax of one pipeline overlaps the other's loads, MMAs and
 // bookkeeping and the SFU (exp2) stays busy.
-// Roles (384 threads):
+// Roles (352 threads):
 //   warps 0-3, 4-7   softmax of pipeline 0 / 1 (thread = query row; warp w reads TMEM lanes
 //                    32 (w % 4) .. + 31)
-//   warp 8           lanes 0 / 1: TMA of Q + the K ring / the V ring of pipeline 0;
-//                    lanes 2 / 3: the same for pipeline 1
-//   warps 9, 10      the MMA-issuing thread of pipeline 0 / 1 (warp 9 also allocates TMEM)
-//   warp 11          key masks of the coming items (bit words per key tile, tile classes)
+//   warps 8, 9       lane 0: the tensor-core thread of pipeline 0 / 1. It issues the MMAs and
+//                    also every TMA transfer of its pipeline (Q, K and V loads, the output
+//                    store), each at the point of its own loop where the buffer has just been
+//                    released, so the loads run one or two key tiles ahead without a producer
+//                    that could fall behind. Warp 8 also allocates TMEM.
+//   warp 10          key masks of the coming items (bit words per key tile, tile classes)
 // Per key tile j a pipeline issues S = Q K_j^T (M 128, N 128, K 64, FP32 in TMEM), then
 // O += P_(j-1) V_(j-1) (M 128, N 64, K 128) with P read from TMEM (16-bit, written by the
-// softmax threads with tcgen05.st) and V as an MN-major operand straight from its TMA tile.
+// softmax threads with tcgen05.st) and V as an MN-major operand straight from its TMA tile. The
+// first S of an item follows the last S of the previous one directly (before that item's last
+// PV), so the softmax finds it computed.
 // The softmax threads read S with tcgen05.ld, mask it (tile classes: all keys valid, valid
 // prefix, per-key bits), update the running max with the lazy rescale (O and the row sum are
 // rescaled only when the max grows by more than 2^8, so P stays below 256) and write P.
+// Output: Q is double-buffered per pipeline. An item's O is read from TMEM during the next item's
+// first tile (before that tile's P is handed over, which lets the next PV overwrite O),
+// normalised and written into the item's own Q buffer (free once its MMAs are done) in the
+// 128-byte-swizzled layout; the tensor-core thread stores it with one TMA store, which clips the
+// rows past n, and then loads the Q of the item after next into the buffer.
 //
 // Masks: the key-validity mask of chronos2/model.zig:208-233 and chronos_bolt/model.zig (mode 0:
 // key j is visible when it is valid; a group without any valid key attends uniformly to all its
@@ -36,7 +45,7 @@ constexpr int kTileRows = 128;                   // queries per tile, keys per t
 constexpr int kTileBytes = kTileRows * 64 * 2;   // 16 KB: 128 rows of 64 16-bit values (128 B)
 constexpr int kMaxKeys = 4096;
 constexpr int kMaxKeyTiles = kMaxKeys / kTileRows;
-constexpr int kThreadsTc = 384;
+constexpr int kThreadsTc = 352;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Tile classes of a key tile.
@@ -52,14 +61,15 @@ struct MaskSlot {
 };
 
 // Shared memory map (offsets from the 1024-aligned base), per pipeline p.
-constexpr int PIPE_BYTES = 5 * kTileBytes;       // Q, K[2], V[2]
+constexpr int PIPE_BYTES = 6 * kTileBytes;       // Q[2] (then the item's output), K[2], V[2]
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = kTileBytes;
-constexpr int OFF_V = 3 * kTileBytes;
+constexpr int OFF_K = 2 * kTileBytes;
+constexpr int OFF_V = 4 * kTileBytes;
 constexpr int OFF_MASK = 2 * PIPE_BYTES;         // [pipeline][slot]
 constexpr int OFF_BAR = OFF_MASK + 4 * (int)sizeof(MaskSlot);
 constexpr int kBarsPerPipe = 18;
-constexpr int OFF_MISC = OFF_BAR + (2 * kBarsPerPipe + 2) * 8;
+constexpr int OFF_LSUM = OFF_BAR + (2 * kBarsPerPipe + 2) * 8;  // [pipeline][row] row sums
+constexpr int OFF_MISC = OFF_LSUM + 2 * kTileRows * 4;
 constexpr int kSmemTc = OFF_MISC + 64 + 1024;    // + alignment slack
 
 // TMEM columns of pipeline p (base p * 256): S (128 FP32), P (64 columns = 128 16-bit), O (64).
@@ -69,8 +79,6 @@ constexpr uint32_t TM_S = 0, TM_P = 128, TM_O = 192;
 struct TcParams {
     const uint8_t *key_valid;
     int64_t kvs;
-    void *o;
-    int64_t ldo;
     int n, heads, groups;
     int qtiles;    // query tiles per (group, head)
     int64_t items;
@@ -105,7 +113,7 @@ __device__ __forceinline__ Item decode_item(const TcParams &p, int64_t it64) {
 
 // Barriers of one pipeline.
 struct PipeBars {
-    uint64_t q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t q_full[2], k_full[2], k_empty[2], v_full[2], v_empty[2];
     uint64_t s_full, s_free, p_ready, o_done, m_full[2], m_empty[2];
 };
 static_assert(sizeof(PipeBars) == kBarsPerPipe * 8, "barrier block");
@@ -122,7 +130,7 @@ __device__ __forceinline__ void item_range(const TcParams &p, int64_t &first, in
 template <bool F16>
 __global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, TcParams p) {
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, TcParams p) {
     constexpr uint32_t FMT = F16 ? 0u : 1u;
     constexpr uint32_t IDESC_S = idesc_f32acc(FMT, 128, 128);
     constexpr uint32_t IDESC_PV = idesc_f32acc(FMT, 128, 64) | (1u << 16);  // B (V) is MN-major
@@ -144,9 +152,8 @@ __global__ void __maxnreg__(168)
     if (threadIdx.x == 0) {
         for (int q = 0; q < 2; ++q) {
             PipeBars &b = pb[q];
-            mbar_init(&b.q_full, 1);
-            mbar_init(&b.q_empty, 1);
             for (int i = 0; i < 2; ++i) {
+                mbar_init(&b.q_full[i], 1);
                 mbar_init(&b.k_full[i], 1);
                 mbar_init(&b.k_empty[i], 1);
                 mbar_init(&b.v_full[i], 1);
@@ -165,8 +172,9 @@ __global__ void __maxnreg__(168)
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
+        tma_prefetch_desc(&tmO);
     }
-    if (warp == 9) {
+    if (warp == 8) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
@@ -175,58 +183,7 @@ __global__ void __maxnreg__(168)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 8 && lane < 4) {
-        // ---- TMA producers: lane 2q + 0 loads Q and the K ring, lane 2q + 1 the V ring ----
-        const int q = lane >> 1;
-        const bool kside = (lane & 1) == 0;
-        PipeBars &b = pb[q];
-        uint8_t *base = smem + q * PIPE_BYTES;
-        uint32_t rt = 0;  // ring position
-        uint32_t issued = 0, issued_ph = 0;
-        bool ok = true, q_issued = false;
-        uint32_t q_ph = 0, wi = 0;
-        for (int64_t it = first + q; it < last && ok; it += 2, ++wi) {
-            const Item im = decode_item(p, it);
-            const int32_t row0 = im.g * n, col = im.h * 64;
-            if (kside) {
-                if (wi > 0 && !mbar_wait(&b.q_empty, (wi - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER)) {
-                    ok = false;
-                    break;
-                }
-                mbar_arrive_expect_tx(&b.q_full, kTileBytes);
-                tma_load_2d(base + OFF_Q, &tmQ, &b.q_full, col, row0 + im.q0);
-                q_issued = true;
-                q_ph = wi & 1;
-            }
-            for (int j = 0; j < T; ++j, ++rt) {
-                const int st = rt & 1;
-                uint64_t *emp = kside ? &b.k_empty[st] : &b.v_empty[st];
-                uint64_t *ful = kside ? &b.k_full[st] : &b.v_full[st];
-                if (rt >= 2 && !mbar_wait(emp, ((rt - 2) >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_PRODUCER)) {
-                    ok = false;
-                    break;
-                }
-                mbar_arrive_expect_tx(ful, kTileBytes);
-                tma_load_2d(base + (kside ? OFF_K : OFF_V) + st * kTileBytes, kside ? &tmK : &tmV, ful, col,
-                            row0 + j * kTileRows);
-                issued |= 1u << st;
-                issued_ph = (issued_ph & ~(1u << st)) | (((rt >> 1) & 1u) << st);
-            }
-        }
-        if (!ok) {
-            // Let the loads in flight land before the CTA can exit (bounded grace period).
-            const unsigned long long t0 = globaltimer_ns();
-            if (q_issued)
-                while (!mbar_try_wait(&b.q_full, q_ph) && globaltimer_ns() - t0 < 100000000ull) {
-                }
-            for (int i = 0; i < 2; ++i) {
-                if (!((issued >> i) & 1u)) continue;
-                uint64_t *ful = kside ? &b.k_full[i] : &b.v_full[i];
-                while (!mbar_try_wait(ful, (issued_ph >> i) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
-                }
-            }
-        }
-    } else if (warp == 11) {
+    if (warp == 10) {
         // ---- key masks of the coming items, in item order ----
         uint32_t wi[2] = {0, 0};
         for (int64_t it = first; it < last; ++it) {
@@ -263,57 +220,142 @@ __global__ void __maxnreg__(168)
             __syncwarp();
             mbar_arrive(&b.m_full[slot]);
         }
-    } else if (warp == 9 || warp == 10) {
-        // ---- MMA issuer of pipeline warp - 9 ----
+    } else if (warp == 8 || warp == 9) {
+        // ---- tensor-core thread of pipeline warp - 8: MMAs and TMA transfers ----
         if (lane == 0) {
-            const int q = warp - 9;
+            const int q = warp - 8;
             PipeBars &b = pb[q];
             uint8_t *base = smem + q * PIPE_BYTES;
             const uint32_t t_s = tmem_base + q * 256 + TM_S, t_p = tmem_base + q * 256 + TM_P;
             const uint32_t t_o = tmem_base + q * 256 + TM_O;
+            const uint32_t uT = (uint32_t)T;
+            const uint32_t nq = last - first > q ? (uint32_t)((last - first - q + 1) / 2) : 0u;  // items
+            const uint32_t NT = nq * uT;                                                        // key tiles
+            auto item_of = [&](uint32_t wi) { return decode_item(p, first + q + 2 * (int64_t)wi); };
+            uint32_t loads[3] = {0, 0, 0};  // Q, K, V loads issued (in ring order)
+            auto load_q = [&](uint32_t wi) {
+                ++loads[0];
+                const Item im = item_of(wi);
+                const uint32_t s = wi & 1;
+                mbar_arrive_expect_tx(&b.q_full[s], kTileBytes);
+                tma_load_2d(base + OFF_Q + s * kTileBytes, &tmQ, &b.q_full[s], im.h * 64, im.g * n + im.q0);
+            };
+            // Key tile g of this pipeline (item g / T, tile g % T) into ring slot g % 2.
+            auto load_kv = [&](bool key, uint32_t g) {
+                ++loads[key ? 1 : 2];
+                const uint32_t wi = g / uT, j = g - wi * uT, s = g & 1;
+                const Item im = item_of(wi);
+                uint64_t *ful = key ? &b.k_full[s] : &b.v_full[s];
+                mbar_arrive_expect_tx(ful, kTileBytes);
+                tma_load_2d(base + (key ? OFF_K : OFF_V) + s * kTileBytes, key ? &tmK : &tmV, ful, im.h * 64,
+                            im.g * n + (int32_t)j * kTileRows);
+            };
             bool ok = true;
-            uint32_t kt = 0, vt = 0, ns = 0, np = 0, wi = 0;
-            const uint64_t qd = sdesc_k128(base + OFF_Q);
-            auto pv = [&](bool first_tile) -> bool {
-                const int st = vt & 1;
-                if (!mbar_wait(&b.v_full[st], (vt >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
-                if (!mbar_wait(&b.p_ready, np & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
+            // O += P V for key tile gg. When gg opens an item, the softmax threads have staged the
+            // previous item's output in its Q buffer before this p_ready: store it, then reuse the
+            // buffer for the Q two items ahead.
+            auto pv = [&](uint32_t gg) -> bool {
+                const uint32_t s = gg & 1;
+                if (!mbar_wait(&b.v_full[s], (gg >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
+                if (!mbar_wait(&b.p_ready, gg & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
                 tc_fence_after();
-                const uint64_t vd = sdesc_k128(base + OFF_V + st * kTileBytes);
+                const uint32_t wi = gg / uT, j = gg - wi * uT;
+                const uint64_t vd = sdesc_k128(base + OFF_V + s * kTileBytes);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)  // A: 16 keys = 8 TMEM columns; B: 16 key rows = 2048 bytes
                     mma_f16kind_ts(t_o, t_p + 8 * kk, vd + (uint64_t)(kk * (2048 >> 4)), IDESC_PV,
-                                   (!first_tile || kk > 0) ? 1u : 0u);
+                                   (j != 0 || kk > 0) ? 1u : 0u);
                 mma_commit(&b.o_done);
-                mma_commit(&b.v_empty[st]);
-                ++np;
-                ++vt;
+                mma_commit(&b.v_empty[s]);
+                if (j == 0 && wi >= 1) {
+                    const uint32_t ps = (wi - 1) & 1;
+                    const Item im = item_of(wi - 1);
+                    tma_store_3d(&tmO, base + OFF_Q + ps * kTileBytes, im.h * 64, im.q0, im.g);
+                    bulk_commit();
+                    if (wi + 1 < nq) {
+                        bulk_wait_read_0();
+                        load_q(wi + 1);
+                    }
+                }
                 return true;
             };
-            for (int64_t it = first + q; it < last && ok; it += 2, ++wi) {
-                if (!mbar_wait(&b.q_full, wi & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+            if (nq > 0) load_q(0);
+            if (nq > 1) load_q(1);
+            for (uint32_t g = 0; g < NT && g < 2; ++g) {
+                load_kv(true, g);
+                load_kv(false, g);
+            }
+            uint32_t g = 0, next_pv = 0;
+            for (uint32_t wi = 0; wi < nq && ok; ++wi) {
+                const uint32_t qs = wi & 1;
+                // With one key tile per item, the pending PV opens the previous item and loads
+                // this item's Q: issue it before waiting for that Q.
+                if (uT == 1 && next_pv < g && !pv(next_pv++)) {
                     ok = false;
                     break;
                 }
-                for (int j = 0; j < T && ok; ++j, ++kt) {
-                    const int st = kt & 1;
-                    if (!mbar_wait(&b.k_full[st], (kt >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA) ||
-                        (ns > 0 && !mbar_wait(&b.s_free, (ns - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA))) {
+                if (!mbar_wait(&b.q_full[qs], (wi >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+                    ok = false;
+                    break;
+                }
+                const uint64_t qd = sdesc_k128(base + OFF_Q + qs * kTileBytes);
+                for (uint32_t j = 0; j < uT; ++j, ++g) {
+                    const uint32_t s = g & 1;
+                    if (!mbar_wait(&b.k_full[s], (g >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA) ||
+                        (g > 0 && !mbar_wait(&b.s_free, (g - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t kd = sdesc_k128(base + OFF_K + st * kTileBytes);
+                    const uint64_t kd = sdesc_k128(base + OFF_K + s * kTileBytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         mma_f16kind(t_s, qd + 2 * kk, kd + 2 * kk, IDESC_S, kk > 0 ? 1u : 0u);
                     mma_commit(&b.s_full);
-                    mma_commit(&b.k_empty[st]);
-                    if (j == T - 1) mma_commit(&b.q_empty);  // Q is free once these S complete
-                    ++ns;
-                    if (j > 0 && !pv(j == 1)) ok = false;
+                    mma_commit(&b.k_empty[s]);
+                    if (next_pv < g && !pv(next_pv++)) {
+                        ok = false;
+                        break;
+                    }
+                    // Refill the rings: K two tiles ahead once this S is done with its slot, V
+                    // one tile ahead once the PV just issued is done with its slot.
+                    if (g + 2 < NT) {
+                        if (!mbar_wait(&b.k_empty[s], (g >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+                            ok = false;
+                            break;
+                        }
+                        load_kv(true, g + 2);
+                    }
+                    if (g >= 1 && g + 1 < NT) {
+                        if (!mbar_wait(&b.v_empty[(g + 1) & 1], ((g - 1) >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+                            ok = false;
+                            break;
+                        }
+                        load_kv(false, g + 1);
+                    }
                 }
-                if (ok && !pv(T == 1)) ok = false;
+            }
+            while (ok && next_pv < NT) ok = pv(next_pv++);
+            // The last item's output: staged by the softmax threads after the last PV, signalled
+            // by one more p_ready phase.
+            if (ok && NT > 0 && mbar_wait(&b.p_ready, NT & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+                const Item im = item_of(nq - 1);
+                tma_store_3d(&tmO, base + OFF_Q + ((nq - 1) & 1) * kTileBytes, im.h * 64, im.q0, im.g);
+                bulk_commit();
+            }
+            bulk_wait_all();
+            if (!ok) {
+                // Let the loads in flight land before the CTA can exit (bounded grace period):
+                // the last load of every ring slot.
+                const unsigned long long t0 = globaltimer_ns();
+                for (int r = 0; r < 3; ++r) {
+                    uint64_t *ful = r == 0 ? b.q_full : r == 1 ? b.k_full : b.v_full;
+                    for (uint32_t back = 1; back <= 2 && back <= loads[r]; ++back) {
+                        const uint32_t i = loads[r] - back;
+                        while (!mbar_try_wait(&ful[i & 1], (i >> 1) & 1) && globaltimer_ns() - t0 < 100000000ull) {
+                        }
+                    }
+                }
             }
             mma_commit(&drain[q]);
             const unsigned long long t0 = globaltimer_ns();
@@ -335,9 +377,36 @@ __global__ void __maxnreg__(168)
         const uint32_t t_p = tmem_base + lanes + q * 256 + TM_P;
         const uint32_t t_o = tmem_base + lanes + q * 256 + TM_O;
         const float sl2 = p.scale_log2;
+        float *l_save = reinterpret_cast<float *>(smem + OFF_LSUM) + q * kTileRows + r;
         uint32_t cx = 0, wi = 0;  // tiles / items processed by this pipeline
         bool ok = true;
-        for (int64_t it = first + q; it < last && ok; it += 2, ++wi) {
+        // This warp's rows of the previous item still wait in TMEM (not past n).
+        bool prev_live = false;
+        // Reads this thread's row of the previous item's O, normalises it by the row sum and writes
+        // it as 16-bit values into that item's Q buffer in the 128-byte-swizzled layout of a TMA
+        // box (16-byte chunk c of row r at chunk c ^ (r % 8)).
+        auto stage_prev_row = [&](uint32_t prev_slot) {
+            const float l = *l_save;
+            const float inv = l > 0.0f ? __frcp_rn(l) : 0.0f;
+            uint8_t *row = smem + q * PIPE_BYTES + OFF_Q + prev_slot * kTileBytes + r * 128;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v[32];
+                tmem_ld32(t_o + 32 * h, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int chunk = (4 * h + c) ^ (r & 7);
+                    *reinterpret_cast<uint4 *>(row + chunk * 16) =
+                        make_uint4(pack_p<F16>(v[8 * c + 0] * inv, v[8 * c + 1] * inv),
+                                   pack_p<F16>(v[8 * c + 2] * inv, v[8 * c + 3] * inv),
+                                   pack_p<F16>(v[8 * c + 4] * inv, v[8 * c + 5] * inv),
+                                   pack_p<F16>(v[8 * c + 6] * inv, v[8 * c + 7] * inv));
+                }
+            }
+            fence_proxy_async_smem();  // visible to the TMA store
+        };
+        for (int32_t it = (int32_t)first + q, it_end = (int32_t)last; it < it_end && ok; it += 2, ++wi) {
             const Item im = decode_item(p, it);
             const uint32_t slot = wi & 1;
             {
@@ -356,6 +425,9 @@ __global__ void __maxnreg__(168)
                     ok = false;
                     break;
                 }
+                // In the first tile of an item the previous item's O is staged once the previous
+                // PV is done and before this tile's p_ready lets the first PV overwrite it.
+                const bool stage = j == 0 && prev_live;
                 if (dead) {
                     // p_ready of this tile may only count once the previous phase completed:
                     // wait for the previous PV like the live warps.
@@ -367,7 +439,10 @@ __global__ void __maxnreg__(168)
                             ok = false;
                             break;
                         }
+                        tc_fence_after();
                     }
+                    if (stage) stage_prev_row(slot ^ 1u);
+                    tc_fence_before();
                     mbar_arrive(&b.p_ready);
                     continue;
                 }
@@ -463,52 +538,31 @@ __global__ void __maxnreg__(168)
                         tmem_st32(t_o + hcol, ov);
                     }
                 }
+                if (stage) stage_prev_row(slot ^ 1u);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&b.p_ready);
             }
             if (!ok) break;
-            // The mask slot is free; the output rows of this tile follow once the last PV is done.
             mbar_arrive(&b.m_empty[slot]);
-            if (dead) continue;
+            prev_live = !dead;
+            *l_save = l_run;
+        }
+        // The last item's output, once its last PV is done; one more p_ready phase tells the
+        // tensor-core thread that it is staged.
+        if (ok && cx > 0) {
             const bool done = mbar_wait(&b.o_done, (cx - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
-            if (!__all_sync(0xffffffffu, done)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            float o0[32], o1[32];
-            tmem_ld32(t_o, o0);
-            tmem_ld32(t_o + 32, o1);
-            tmem_wait_ld();
-            // The next item's first PV (accumulate = 0) may overwrite O once this thread's next
-            // p_ready arrives, which follows these loads in program order.
-            const int tok = im.q0 + r;
-            if (tok < n) {
-                const float inv = l_run > 0.0f ? __frcp_rn(l_run) : 0.0f;
-                uint16_t *dst = static_cast<uint16_t *>(p.o) + (int64_t)(im.g * n + tok) * p.ldo + im.h * 64;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const float *src = c < 2 ? o0 + 16 * c : o1 + 16 * (c - 2);
-                    uint4 a, bb;
-                    a.x = pack_p<F16>(src[0] * inv, src[1] * inv);
-                    a.y = pack_p<F16>(src[2] * inv, src[3] * inv);
-                    a.z = pack_p<F16>(src[4] * inv, src[5] * inv);
-                    a.w = pack_p<F16>(src[6] * inv, src[7] * inv);
-                    bb.x = pack_p<F16>(src[8] * inv, src[9] * inv);
-                    bb.y = pack_p<F16>(src[10] * inv, src[11] * inv);
-                    bb.z = pack_p<F16>(src[12] * inv, src[13] * inv);
-                    bb.w = pack_p<F16>(src[14] * inv, src[15] * inv);
-                    reinterpret_cast<uint4 *>(dst)[2 * c] = a;
-                    reinterpret_cast<uint4 *>(dst)[2 * c + 1] = bb;
-                }
+            if (__all_sync(0xffffffffu, done)) {
+                tc_fence_after();
+                if (prev_live) stage_prev_row((wi - 1) & 1);
+                mbar_arrive(&b.p_ready);
             }
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == 8) {
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
     }
@@ -523,7 +577,7 @@ bool attention_tc_supported(const AttentionCall &c) {
     if (c.n <= 0 || c.n > kMaxKeys || c.heads <= 0 || c.groups <= 0) return false;
     if ((int64_t)c.groups * c.n > INT32_MAX - 2 * kTileRows) return false;
     if ((int64_t)c.groups * c.heads * ((c.n + kTileRows - 1) / kTileRows) > INT32_MAX) return false;
-    // TMA: 16-byte aligned bases and row strides; 16-byte aligned output rows.
+    // TMA: 16-byte aligned bases and row strides.
     const auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     if (!a16(c.q) || !a16(c.k) || !a16(c.v) || !a16(c.o) || (c.ld_qkv % 8) || (c.ld_o % 8)) return false;
     return true;
@@ -533,15 +587,15 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     if (!attention_tc_supported(c)) return Status::fail(TSFM_ERR_UNSUPPORTED, "attention: the tcgen05 path does not take this call");
     const int64_t rows = (int64_t)c.groups * c.n;
     const int64_t width = (int64_t)c.heads * 64;
-    alignas(64) CUtensorMap mq, mk, mv;
+    alignas(64) CUtensorMap mq, mk, mv, mo;
     TSFM_TRY(make_tmap_2d(&mq, c.q, c.dtype, width, rows, c.ld_qkv, 64, kTileRows));
     TSFM_TRY(make_tmap_2d(&mk, c.k, c.dtype, width, rows, c.ld_qkv, 64, kTileRows));
     TSFM_TRY(make_tmap_2d(&mv, c.v, c.dtype, width, rows, c.ld_qkv, 64, kTileRows));
+    // Output rows per group: a query tile that runs past n is clipped at the group's end.
+    TSFM_TRY(make_tmap_grouped_rows(&mo, c.o, c.dtype, width, c.n, c.groups, c.ld_o, 64, kTileRows));
     TcParams p;
     p.key_valid = c.key_valid;
     p.kvs = c.kv_stride > 0 ? c.kv_stride : c.n;
-    p.o = c.o;
-    p.ldo = c.ld_o;
     p.n = c.n;
     p.heads = c.heads;
     p.groups = c.groups;
@@ -553,10 +607,10 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     cudaError_t e;
     if (c.dtype == E_F16) {
         e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
-        if (e == cudaSuccess) attn_tc_kernel<true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, p);
+        if (e == cudaSuccess) attn_tc_kernel<true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
     } else {
         e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
-        if (e == cudaSuccess) attn_tc_kernel<false><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, p);
+        if (e == cudaSuccess) attn_tc_kernel<false><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
     }
     if (e != cudaSuccess) return Status::cuda(e, "attention (tcgen05): set shared memory");
     e = cudaGetLastError();

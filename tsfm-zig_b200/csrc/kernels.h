@@ -101,6 +101,11 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream);
 // CUtensorMap (128 bytes).
 Status make_tmap_2d(void *map, const void *base, int dtype, int64_t inner, int64_t outer, int64_t ld,
                     uint32_t box_inner, uint32_t box_outer);
+// 3-D tensor map over `groups` blocks of `rows` rows (each `width` elements, row stride `ld`,
+// blocks back to back), box (box_inner, box_rows, 1), 128-byte swizzle: a box that runs past the
+// last row of its block is clipped there.
+Status make_tmap_grouped_rows(void *map, const void *base, int dtype, int64_t width, int64_t rows, int64_t groups,
+                              int64_t ld, uint32_t box_inner, uint32_t box_rows);
 
 // RMSNorm: out[r] = x[in_row(r)] * (1 / sqrt(mean(x^2) + eps)) * scale.
 // in_row(r) = (r / g) * G + r % g + off when g > 0. out_mode: OUT_BF16, OUT_F32, OUT_TF32, OUT_F16.

@@ -585,6 +585,26 @@ Status make_tmap_2d(void *map, const void *base, int dtype, int64_t inner, int64
     return make_tmap(static_cast<CUtensorMap *>(map), base, dtype, inner, outer, ld, box_inner, box_outer);
 }
 
+Status make_tmap_grouped_rows(void *map, const void *base, int dtype, int64_t width, int64_t rows, int64_t groups,
+                              int64_t ld, uint32_t box_inner, uint32_t box_rows) {
+    if (!load_encode()) return Status::fail(TSFM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const bool f32 = dtype == E_F32;
+    const int esz = f32 ? 4 : 2;
+    const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                       : dtype == E_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * esz) & 15))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "tensor map: base and row stride must be 16-byte aligned");
+    cuuint64_t dims[3] = {(cuuint64_t)width, (cuuint64_t)rows, (cuuint64_t)groups};
+    cuuint64_t strides[2] = {(cuuint64_t)(ld * esz), (cuuint64_t)(rows * ld * esz)};
+    cuuint32_t box[3] = {box_inner, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(static_cast<CUtensorMap *>(map), dt, 3, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return Status::fail(TSFM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return Status::ok();
+}
+
 Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     if (c.M <= 0 || c.N <= 0 || c.K <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: empty product");
     if (c.M > INT32_MAX || c.N > INT32_MAX || c.K > INT32_MAX)

@@ -74,6 +74,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe of the phase with the given parity: never suspends the thread, so one thread
+// can poll several barriers in turn.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Returns false (after raising the abort
 // flag and recording `site` in *err) when the wait exceeds kWaitTimeoutNs, or when another role
 // of the CTA has already aborted.
@@ -120,6 +134,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void 
                  : "memory");
 }
 
+// 3-D tiled store (c0 = innermost, c1, c2); elements outside the tensor are not written, so a box
+// that runs past the end of dimension 1 is clipped there rather than spilling into the next c2.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem_src, int32_t c0, int32_t c1,
+                                             int32_t c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
 // The same with element-wise addition into global memory (f32: one rounding per element, as a
 // plain read-add-write).
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *smem_src, int32_t c0, int32_t c1) {
@@ -132,6 +156,8 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until at most one of this thread's bulk groups still reads its shared-memory source.
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+// Waits until none of this thread's bulk groups still reads its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Waits until all of this thread's bulk groups have completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
