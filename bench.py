@@ -47,9 +47,11 @@ def parse_args():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--series", type=int, default=SERIES_PER_GPU)
     ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
-    ap.add_argument("--workload", default="chronos2", choices=["chronos2", "bolt-small", "bolt-base", "timestral"],
-                    help="chronos2 is the headline; the others are BASELINE.json's other configs, timed through "
-                         "the host entry points (copies included)")
+    ap.add_argument("--workload", default="chronos2",
+                    choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep"],
+                    help="chronos2 is the headline; bolt-*/timestral are BASELINE.json's other configs, timed "
+                         "through the host entry points (copies included); sweep is its Chronos-2 throughput sweep "
+                         "(batch x context, one JSON line per point)")
     return ap.parse_args()
 
 
@@ -193,6 +195,67 @@ def run_reference(a, rank):
     print(json.dumps(line), flush=True)
 
 
+# Algorithmic GFLOP per series of the Chronos-2-shaped model at horizon 1024, by context length.
+GF_BY_CONTEXT = {512: 20.53, 2048: 41.07, 8192: 130.02}
+
+
+def run_sweep(a):
+    """BASELINE.json's throughput sweep on the Chronos-2-shaped model: batch {1, 16, 256, 2048, 8192}
+    x context {512, 2048, 8192}, horizon 1024, one GPU. Per point: device-resident series/s (CUDA events
+    around each forecast, L2 flushed in between) and end-to-end series/s through the host entry point
+    (pinned buffers, copies included), with the fraction of the measured burst BF16 peak."""
+    import torch
+    from tsfm_b200 import synthetic as syn
+    burst = peaks()[0]
+    cfg, w, model = build_model(0)
+    del w
+    q = 21
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    stream = torch.cuda.current_stream()
+    for ctx in (512, 2048, 8192):
+        for b in (1, 16, 256, 2048, 8192):
+            x = syn.seeded_series(b, ctx, seed=5000 + b)
+            xd = torch.from_numpy(x).cuda()
+            out = torch.empty((b, HORIZON, q), device="cuda")
+            step = lambda: model.forecast_chronos2_device(xd.data_ptr(), b, ctx, HORIZON, out.data_ptr(),
+                                                          stream.cuda_stream)
+            for _ in range(max(3, a.warmup)):
+                step()
+            torch.cuda.synchronize()
+            # About half a second of timed forecasts per point (at least 3).
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            e1.synchronize()
+            est = max(e0.elapsed_time(e1), 1e-3)
+            reps = int(min(50, max(3, 500.0 / est)))
+            total = 0.0
+            for _ in range(reps):
+                flush.zero_()
+                e0.record(stream)
+                step()
+                e1.record(stream)
+                e1.synchronize()
+                total += e0.elapsed_time(e1)
+            ms = total / reps
+            xp = torch.from_numpy(x).pin_memory().numpy()
+            op = torch.empty((b, HORIZON, q), dtype=torch.float32).pin_memory().numpy()
+            model.forecast_chronos2(xp, HORIZON, out=op)
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                model.forecast_chronos2(xp, HORIZON, out=op)
+            e2e_ms = (time.perf_counter() - t0) / reps * 1e3
+            gf = GF_BY_CONTEXT[ctx]
+            print(json.dumps({"workload": "sweep", "batch": b, "context": ctx, "horizon": HORIZON, "n_gpus": 1,
+                              "ms_per_forecast": ms, "series_per_s": b / (ms / 1e3),
+                              "e2e_ms_per_forecast": e2e_ms, "e2e_series_per_s": b / (e2e_ms / 1e3),
+                              "tc_peak_frac": gf * 1e9 * b / (ms / 1e3) / (burst * 1e12), "steps": reps,
+                              "gpu_launches_per_forecast": model.last_launch_count()}), flush=True)
+            del xd, out
+    model.close()
+
+
 def run_family_workload(a):
     """BASELINE.json's Chronos-Bolt and Timestral configs on one GPU, through the host entry points
     (pinned inputs, host->device and device->host copies inside the timed region)."""
@@ -257,7 +320,7 @@ def main():
         return run_reference(a, rank)
     if a.workload != "chronos2":
         if rank == 0:
-            run_family_workload(a)
+            run_sweep(a) if a.workload == "sweep" else run_family_workload(a)
         return
 
     import torch

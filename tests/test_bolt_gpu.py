@@ -90,6 +90,25 @@ def test_replicas_are_bit_identical(tiny):
     assert np.array_equal(gpu.forecast_bolt(x, 40), two.forecast_bolt(x, 40))
 
 
+def test_graph_replays_match_plain_runs(tiny):
+    # The third call with the same shapes and buffers replays a captured CUDA graph; it must read
+    # the new inputs and give exactly what a plain run gives (the host path and the device path).
+    gpu, _ = tiny
+    cfg = tiny_cfg()
+    w = syn.random_checkpoint(cfg, seed=4, norm_jitter=0.1)
+    xs = [syn.seeded_series(6, 230, seed=40 + i) for i in range(4)]
+    plain = [tb.Model(cfg, w).forecast_bolt(x, 40) for x in xs]
+    for x, want in zip(xs, plain):
+        assert np.array_equal(gpu.forecast_bolt(x, 40), want)
+    xd = torch.empty((6, 230), device="cuda")
+    out = torch.empty((6, 40, 9), device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for x, want in zip(xs, plain):
+        xd.copy_(torch.from_numpy(x))
+        gpu.forecast_bolt_device(xd.data_ptr(), 6, 230, 40, out.data_ptr(), s)
+        assert np.array_equal(out.cpu().numpy(), want)
+
+
 def test_bolt_small_shape_matches_oracle():
     # BASELINE configs[0] shape: Bolt-small (512-d, 6 layers, ctx 2048, 9 quantiles, P = 64);
     # horizon 192 runs the first block plus two quantile-path blocks.

@@ -116,6 +116,23 @@ def test_chunked_host_path_matches_device_path(tiny, b):
     assert np.array_equal(op, want)
 
 
+def test_graph_replays_match_plain_runs(tiny):
+    # The third call with the same shapes and buffers replays a captured CUDA graph; it must read
+    # the new inputs and give exactly what a plain run gives (the host path and the device path).
+    cfg, w, gpu, _ = tiny
+    xs = [syn.seeded_series(5, 333, seed=50 + i) for i in range(4)]
+    plain = [tb.Model(cfg, w).forecast_chronos2(x, 48) for x in xs]
+    for x, want in zip(xs, plain):
+        assert np.array_equal(gpu.forecast_chronos2(x, 48), want)
+    xd = torch.empty((5, 333), device="cuda")
+    out = torch.empty((5, 48, 21), device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for x, want in zip(xs, plain):
+        xd.copy_(torch.from_numpy(x))
+        gpu.forecast_chronos2_device(xd.data_ptr(), 5, 333, 48, out.data_ptr(), s)
+        assert np.array_equal(out.cpu().numpy(), want)
+
+
 def test_argument_errors(tiny):
     _, _, gpu, _ = tiny
     with pytest.raises(tb.TsfmError, match="HORIZON_TOO_LONG"):

@@ -604,16 +604,14 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     p.scale_log2 = c.scale * 1.4426950408889634f;
     p.err = c.err;
     const int64_t grid = std::min<int64_t>((p.items + 1) / 2, num_sms());
-    cudaError_t e;
     if (c.dtype == E_F16) {
-        e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
-        if (e == cudaSuccess) attn_tc_kernel<true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
+        TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<true>), kSmemTc));
+        attn_tc_kernel<true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
     } else {
-        e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
-        if (e == cudaSuccess) attn_tc_kernel<false><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
+        TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<false>), kSmemTc));
+        attn_tc_kernel<false><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
     }
-    if (e != cudaSuccess) return Status::cuda(e, "attention (tcgen05): set shared memory");
-    e = cudaGetLastError();
+    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return Status::cuda(e, "attention (tcgen05): launch");
     return Status::ok();
 }

@@ -165,6 +165,22 @@ Status replica_forecast(Replica &r, const void *in, int64_t nb, size_t in_row, s
     return Status::ok();
 }
 
+// Graph-cache key of one forward: family, shapes, and every buffer address it reads or writes
+// (inputs, outputs, workspace, forecaster buffers); weights and the error word are fixed per replica.
+std::vector<uint64_t> fwd_key(const Replica &r, int family, int64_t nb, size_t t, size_t horizon, const void *in,
+                              const void *out) {
+    return {(uint64_t)family,
+            (uint64_t)nb,
+            (uint64_t)t,
+            (uint64_t)horizon,
+            (uint64_t)reinterpret_cast<uintptr_t>(in),
+            (uint64_t)reinterpret_cast<uintptr_t>(out),
+            (uint64_t)reinterpret_cast<uintptr_t>(r.ws.buf.p),
+            (uint64_t)r.ws.buf.bytes,
+            (uint64_t)reinterpret_cast<uintptr_t>(r.fc.buf.p),
+            (uint64_t)r.fc.buf.bytes};
+}
+
 // The same on device pointers (first replica, caller's stream).
 template <class Fwd>
 Status replica_forecast_device(Replica &r, cudaStream_t stream, Fwd &&fwd) {
@@ -339,8 +355,11 @@ int32_t tsfm_forecast_chronos2(tsfm_model *model, const float *inputs, size_t b,
             const int64_t nb = s1 - s0;
             return replica_forecast(r, inputs + s0 * t, nb, t * 4, horizon * q * 4, out + s0 * horizon * q,
                                     [&](const float *d_in, float *d_out, int64_t nc, cudaStream_t s) {
-                                        return c2_forecast(r, model->cfg, w, d_in, nc, (int64_t)t, (int64_t)horizon,
-                                                           d_out, s);
+                                        return run_captured(r, s, fwd_key(r, TSFM_CHRONOS2, nc, t, horizon, d_in, d_out),
+                                                            [&](cudaStream_t cs) {
+                                                                return c2_forecast(r, model->cfg, w, d_in, nc, (int64_t)t,
+                                                                                   (int64_t)horizon, d_out, cs);
+                                                            });
                                     });
         });
     });
@@ -353,7 +372,9 @@ int32_t tsfm_forecast_chronos2_device(tsfm_model *model, const float *inputs, si
         TSFM_TRY(c2_args(model, inputs, b, t, horizon, out));
         Replica &r = *model->reps[0];
         return replica_forecast_device(r, static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
-            return c2_forecast(r, model->cfg, *model->c2[0], inputs, (int64_t)b, (int64_t)t, (int64_t)horizon, out, s);
+            return run_captured(r, s, fwd_key(r, TSFM_CHRONOS2, (int64_t)b, t, horizon, inputs, out), [&](cudaStream_t cs) {
+                return c2_forecast(r, model->cfg, *model->c2[0], inputs, (int64_t)b, (int64_t)t, (int64_t)horizon, out, cs);
+            });
         });
     });
 }
@@ -378,8 +399,11 @@ int32_t tsfm_forecast_bolt(tsfm_model *model, const float *inputs, size_t b, siz
             const int64_t nb = s1 - s0;
             return replica_forecast(r, inputs + s0 * t, nb, t * 4, horizon * q * 4, out + s0 * horizon * q,
                                     [&](const float *d_in, float *d_out, int64_t nc, cudaStream_t s) {
-                                        return bolt_forecast(r, model->cfg, w, d_in, nc, (int64_t)t, (int64_t)horizon,
-                                                             d_out, s);
+                                        return run_captured(r, s, fwd_key(r, TSFM_CHRONOS_BOLT, nc, t, horizon, d_in, d_out),
+                                                            [&](cudaStream_t cs) {
+                                                                return bolt_forecast(r, model->cfg, w, d_in, nc, (int64_t)t,
+                                                                                     (int64_t)horizon, d_out, cs);
+                                                            });
                                     });
         });
     });
@@ -392,7 +416,9 @@ int32_t tsfm_forecast_bolt_device(tsfm_model *model, const float *inputs, size_t
         TSFM_TRY(bolt_args(inputs, b, t, horizon, out));
         Replica &r = *model->reps[0];
         return replica_forecast_device(r, static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
-            return bolt_forecast(r, model->cfg, *model->bolt[0], inputs, (int64_t)b, (int64_t)t, (int64_t)horizon, out, s);
+            return run_captured(r, s, fwd_key(r, TSFM_CHRONOS_BOLT, (int64_t)b, t, horizon, inputs, out), [&](cudaStream_t cs) {
+                return bolt_forecast(r, model->cfg, *model->bolt[0], inputs, (int64_t)b, (int64_t)t, (int64_t)horizon, out, cs);
+            });
         });
     });
 }

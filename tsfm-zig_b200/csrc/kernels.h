@@ -101,6 +101,10 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream);
 // CUtensorMap (128 bytes).
 Status make_tmap_2d(void *map, const void *base, int dtype, int64_t inner, int64_t outer, int64_t ld,
                     uint32_t box_inner, uint32_t box_outer);
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel): the attribute
+// stays set in the context, and setting it on every launch costs host time.
+Status ensure_smem_attr(const void *func, int bytes);
+
 // 3-D tensor map over `groups` blocks of `rows` rows (each `width` elements, row stride `ld`,
 // blocks back to back), box (box_inner, box_rows, 1), 128-byte swizzle: a box that runs past the
 // last row of its block is clipped there.

@@ -24,6 +24,8 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <utility>
+#include <vector>
 #include <type_traits>
 
 namespace tsfm {
@@ -529,6 +531,27 @@ int sm_count() {
     return g_num_sms[dev];
 }
 
+}  // namespace
+
+Status ensure_smem_attr(const void *func, int bytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static std::mutex mu;
+    static std::vector<std::pair<int, const void *>> done;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        for (const auto &d : done)
+            if (d.first == dev && d.second == func) return Status::ok();
+    }
+    const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return Status::cuda(e, "set dynamic shared memory");
+    std::lock_guard<std::mutex> lk(mu);
+    done.push_back({dev, func});
+    return Status::ok();
+}
+
+namespace {
+
 template <typename T, int BN>
 Status launch_t(const LinearCall &c, cudaStream_t stream) {
     using C = TileCfg<BN>;
@@ -538,8 +561,8 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     if (!s) return s;
     s = make_tmap(&tb, c.w, c.dtype, c.K, c.N, c.ldw, BK, BN);
     if (!s) return s;
-    cudaError_t ce = cudaFuncSetAttribute(linear_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (ce != cudaSuccess) return Status::cuda(ce, "linear: set shared memory");
+    TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&linear_tc_kernel<T, BN>), C::SMEM));
+    cudaError_t ce;
     Epi e;
     e.M = c.M;
     e.N = c.N;

@@ -1,5 +1,7 @@
 #include "runtime.h"
 
+#include <cstdlib>
+
 #include <algorithm>
 #include <cstdarg>
 #include <cstring>
@@ -100,6 +102,39 @@ LaunchScope::~LaunchScope() {
         cudaEventRecord(b, s);
         r.prof.pending.push_back({cls, work, a, b});
     }
+}
+
+GraphCache::Entry *GraphCache::find(const std::vector<uint64_t> &key) {
+    for (auto &e : entries)
+        if (e.key == key) return &e;
+    return nullptr;
+}
+
+GraphCache::Entry *GraphCache::insert(const std::vector<uint64_t> &key) {
+    if (entries.size() >= kMax) {
+        size_t lru = 0;
+        for (size_t i = 1; i < entries.size(); ++i)
+            if (entries[i].used < entries[lru].used) lru = i;
+        if (entries[lru].exec) cudaGraphExecDestroy(entries[lru].exec);
+        entries.erase(entries.begin() + (std::ptrdiff_t)lru);
+    }
+    entries.push_back(Entry{});
+    entries.back().key = key;
+    entries.back().used = ++clock;
+    return &entries.back();
+}
+
+GraphCache::~GraphCache() {
+    for (auto &e : entries)
+        if (e.exec) cudaGraphExecDestroy(e.exec);
+}
+
+bool graphs_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("TSFM_CUDA_GRAPHS");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 Replica::~Replica() {

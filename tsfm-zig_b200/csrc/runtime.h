@@ -125,6 +125,27 @@ struct Arena {
     static size_t span(size_t bytes) { return (bytes + 255) & ~size_t(255); }
 };
 
+// Captured forwards. A forward's launch sequence depends only on its shapes and on the addresses of
+// the buffers it touches, so after one plain run under a key (those shapes and addresses) the
+// sequence is captured into a CUDA graph and later calls with the key replay it: one launch instead
+// of ~126 per forward, which is what small batches pay for. TSFM_CUDA_GRAPHS=0 turns this off.
+struct GraphCache {
+    struct Entry {
+        std::vector<uint64_t> key;
+        cudaGraphExec_t exec = nullptr;
+        uint64_t launches = 0;  // kernels in the graph
+        uint64_t used = 0;      // LRU clock
+        bool failed = false;    // capture not possible: always run plainly
+    };
+    std::vector<Entry> entries;
+    uint64_t clock = 0;
+    static constexpr size_t kMax = 16;
+    Entry *find(const std::vector<uint64_t> &key);
+    Entry *insert(const std::vector<uint64_t> &key);  // evicts the least recently used entry when full
+    ~GraphCache();
+};
+bool graphs_enabled();
+
 struct Replica {
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -137,9 +158,47 @@ struct Replica {
     DevBuf io;  // device copies of host inputs / outputs
     PinnedBuf pin_in, pin_out;
     Profiler prof;
+    GraphCache graphs;
     std::mutex mu;
     ~Replica();
 };
+
+// Runs `fwd(stream)` (a forward that enqueues kernels only: no allocation, copy or synchronisation)
+// on `s`, through the replica's graph cache under `key` (see GraphCache). The capture itself runs
+// on the replica's own stream, so `s` may be the legacy default stream.
+template <class Fwd>
+Status run_captured(Replica &r, cudaStream_t s, const std::vector<uint64_t> &key, Fwd &&fwd) {
+    if (r.prof.enabled || !graphs_enabled()) return fwd(s);
+    GraphCache::Entry *e = r.graphs.find(key);
+    if (!e) {
+        r.graphs.insert(key);
+        return fwd(s);  // first sight: the plain run sizes the workspace and sets kernel attributes
+    }
+    if (e->failed) return fwd(s);
+    if (!e->exec) {
+        const uint64_t before = r.prof.cur_launches;
+        cudaGraph_t g = nullptr;
+        bool ok = cudaStreamBeginCapture(r.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+        if (ok) {
+            const Status st = fwd(r.stream);
+            ok = cudaStreamEndCapture(r.stream, &g) == cudaSuccess && st && g != nullptr;
+        }
+        if (ok) ok = cudaGraphInstantiate(&e->exec, g, 0) == cudaSuccess;
+        if (g) cudaGraphDestroy(g);
+        e->launches = r.prof.cur_launches - before;
+        r.prof.cur_launches = before;
+        if (!ok) {
+            (void)cudaGetLastError();
+            e->exec = nullptr;
+            e->failed = true;
+            return fwd(s);
+        }
+    }
+    e->used = ++r.graphs.clock;
+    r.prof.cur_launches += e->launches;
+    TSFM_CUDA(cudaGraphLaunch(e->exec, s), "cudaGraphLaunch");
+    return Status::ok();
+}
 
 // Checkpoint tensor table (core/safetensors.zig:59-97 semantics).
 struct TensorTable {
