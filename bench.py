@@ -299,6 +299,14 @@ def run_family_workload(a):
         run()
     torch.cuda.synchronize()
     ms = (time.perf_counter() - t0) / steps * 1e3
+    # Per-kernel-class device time on one separate, untimed forecast.
+    model.profile(True)
+    model.profile_reset()
+    run()
+    torch.cuda.synchronize()
+    cls = {c: model.profile_read(c) for c in ("gemm", "attention", "rmsnorm", "patch", "head", "other")}
+    model.profile(False)
+    kernels = {c: {"launches": v["launches"], "ms": v["ms"]} for c, v in cls.items() if v["launches"]}
     line = {"metric": f"forecast series/sec ({a.workload}, BASELINE.json config)", "value": b / (ms / 1e3),
             "unit": "series/s", "n_gpus": 1, "steps": steps, "ms_per_step": ms, "higher_is_better": True,
             "dtype": "f16", "data": "synthetic (seeded series, random-init N(0,0.02) weights)",
@@ -306,7 +314,7 @@ def run_family_workload(a):
                        "timing": "host entry point, pinned buffers, copies included"},
             "e2e": {"value": b / (ms / 1e3), "unit": "series/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": model.last_launch_count()}
+            "gpu_launches": model.last_launch_count(), "kernels": kernels}
     print(json.dumps(line), flush=True)
     model.close()
 

@@ -137,13 +137,16 @@ def test_attention_matches_float64_reference(n, mode, with_rel, dtype):
     assert err < (3e-2 if dtype == "bf16" else 5e-3), err
 
 
-@pytest.mark.parametrize("n", [1, 17, 128, 129, 256, 257, 640, 1100])
+@pytest.mark.parametrize("n,with_rel", [(1, False), (17, False), (128, False), (129, False), (256, False),
+                                        (257, False), (640, False), (1100, False), (1, True), (17, True), (130, True),
+                                        (257, True), (512, True), (513, True)])
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_attention_tcgen05_path_edges(n, dtype):
-    """The tcgen05 kernel (key-validity mask, no relative bias): one and two query tiles per CTA,
-    partial key tiles, the K / V rings wrapping many times, a group without valid keys (uniform),
-    a group whose first 300 keys are invalid (rows start with an empty max), and scores that grow
-    by more than 2^8 per key tile so the lazy O / row-sum rescale runs on every tile."""
+def test_attention_tcgen05_path_edges(n, with_rel, dtype):
+    """The tcgen05 kernel (key-validity mask; relative-position bias up to n = 512, the mma.sync
+    kernel beyond): one and two query tiles per CTA, partial key tiles, the K / V rings wrapping
+    many times, a group without valid keys (uniform), a group whose first 300 keys are invalid
+    (rows start with an empty max), and scores that grow by more than 2^8 per key tile so the lazy
+    O / row-sum rescale runs on every tile."""
     heads, G = 2, 4
     gen = torch.Generator().manual_seed(1000 + n)
     ld = 3 * heads * 64
@@ -163,12 +166,14 @@ def test_attention_tcgen05_path_edges(n, dtype):
     if n > 300:
         kv[2, 300] = 1
     kv[3, :] = 1
+    rel = torch.randn(heads, 2 * n - 1, generator=gen) * 2 if with_rel else None
+    reld = rel.to(dev()) if with_rel else None
     o = torch.full((G * n, heads * 64), float("nan"), device=dev(), dtype=TORCH16[dtype])
     tb.check(tb.lib.tsfm_kernel_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, o.data_ptr(), heads * 64,
-                                          kv.to(dev()).data_ptr(), None, G, heads, n, 1.0, 0,
-                                          CODE16[TORCH16[dtype]], stream_ptr()))
+                                          kv.to(dev()).data_ptr(), None if reld is None else reld.data_ptr(), G, heads,
+                                          n, 1.0, 0, CODE16[TORCH16[dtype]], stream_ptr()))
     torch.cuda.synchronize()
-    ref = attention_ref(q, k, v, kv, None, n, heads, 1.0, 0)
+    ref = attention_ref(q, k, v, kv, rel, n, heads, 1.0, 0)
     got = o.double().cpu()
     assert torch.isfinite(got).all()
     err = (got - ref).abs().max().item()

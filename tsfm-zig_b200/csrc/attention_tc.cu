@@ -29,7 +29,10 @@
 //
 // Masks: the key-validity mask of chronos2/model.zig:208-233 and chronos_bolt/model.zig (mode 0:
 // key j is visible when it is valid; a group without any valid key attends uniformly to all its
-// keys, the reference's additive -floatMax mask). Every wait is bounded (ptx.cuh).
+// keys, the reference's additive -floatMax mask). Relative-position bias (Chronos-Bolt's T5
+// encoder, chronos_bolt/model.zig:195-205: score(i, j) += bias_h(j - i)) for n <= 512: the mask warp
+// copies the item's window of the per-head offset table into its mask slot, and each softmax thread
+// adds the 128 entries of its row to S before the row maximum. Every wait is bounded (ptx.cuh).
 #include <algorithm>
 
 #include "kernels.h"
@@ -45,6 +48,8 @@ constexpr int kTileRows = 128;                   // queries per tile, keys per t
 constexpr int kTileBytes = kTileRows * 64 * 2;   // 16 KB: 128 rows of 64 16-bit values (128 B)
 constexpr int kMaxKeys = 4096;
 constexpr int kMaxKeyTiles = kMaxKeys / kTileRows;
+constexpr int kMaxKeysRel = 512;                     // longest sequence with relative-position bias
+constexpr int kRelWin = kMaxKeysRel + kTileRows;     // offsets one item's 128 query rows can see
 constexpr int kThreadsTc = 352;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -53,11 +58,15 @@ enum : uint8_t { TILE_FULL = 0, TILE_PREFIX = 1, TILE_BITS = 2 };
 
 // Mask of one item: per key tile its class and, for TILE_BITS, 128 validity bits; `uniform`:
 // no valid key (every key below n gets score 0).
+// `rel`: relative-position bias of the item's head, rel[i] = bias(i - 127 - q0) for
+// i < T * 128 + 127 (0 outside the table), so query row r of the tile at key c of key tile j reads
+// rel[128 j + c - r + 127].
 struct MaskSlot {
     uint32_t bits[kMaxKeys / 32];
     uint8_t cls[kMaxKeyTiles];
     uint32_t uniform;
     uint32_t pad[7];
+    float rel[kRelWin];
 };
 
 // Shared memory map (offsets from the 1024-aligned base), per pipeline p.
@@ -79,6 +88,8 @@ constexpr uint32_t TM_S = 0, TM_P = 128, TM_O = 192;
 struct TcParams {
     const uint8_t *key_valid;
     int64_t kvs;
+    const float *rel;  // per head, indexed by key - query + rel_center; or null
+    int64_t rel_stride, rel_center;
     int n, heads, groups;
     int qtiles;    // query tiles per (group, head)
     int64_t items;
@@ -217,6 +228,14 @@ __global__ void __maxnreg__(168)
             }
             const bool uniform = !__any_sync(0xffffffffu, any);
             if (lane == 0) m.uniform = uniform ? 1u : 0u;
+            if (p.rel) {
+                const float *tab = p.rel + (int64_t)im.h * p.rel_stride;
+                const int64_t base = p.rel_center - im.q0 - (kTileRows - 1);
+                for (int i = lane; i < T * kTileRows + kTileRows - 1; i += 32) {
+                    const int64_t idx = base + i;
+                    m.rel[i] = idx >= 0 && idx < p.rel_stride ? __ldg(tab + idx) : 0.0f;
+                }
+            }
             __syncwarp();
             mbar_arrive(&b.m_full[slot]);
         }
@@ -465,6 +484,11 @@ __global__ void __maxnreg__(168)
                 }
                 tc_fence_before();
                 mbar_arrive(&b.s_free);
+                if (p.rel) {
+                    const float *rw = m.rel + j * kTileRows - r + (kTileRows - 1);
+#pragma unroll
+                    for (int i = 0; i < 128; ++i) s[i] += rw[i];
+                }
 
                 // Mask: valid prefix of the tile (keys below n), or per-key bits; uniform groups
                 // give every key below n the score 0.
@@ -572,7 +596,7 @@ __global__ void __maxnreg__(168)
 
 bool attention_tc_supported(const AttentionCall &c) {
     if (c.force_path == 2) return false;
-    if (c.mask_mode != 0 || c.rel_bias != nullptr) return false;
+    if (c.mask_mode != 0 || (c.rel_bias != nullptr && c.n > kMaxKeysRel)) return false;
     if (c.dtype != E_F16 && c.dtype != E_BF16) return false;
     if (c.n <= 0 || c.n > kMaxKeys || c.heads <= 0 || c.groups <= 0) return false;
     if ((int64_t)c.groups * c.n > INT32_MAX - 2 * kTileRows) return false;
@@ -596,6 +620,9 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     TcParams p;
     p.key_valid = c.key_valid;
     p.kvs = c.kv_stride > 0 ? c.kv_stride : c.n;
+    p.rel = c.rel_bias;
+    p.rel_stride = c.rel_stride > 0 ? c.rel_stride : 2 * (int64_t)c.n - 1;
+    p.rel_center = c.rel_center >= 0 ? c.rel_center : (int64_t)c.n - 1;
     p.n = c.n;
     p.heads = c.heads;
     p.groups = c.groups;
