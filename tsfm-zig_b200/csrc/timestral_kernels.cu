@@ -5,6 +5,7 @@
 // contiguous and ordered targets, past-only covariates, known-future covariates.
 #include <cfloat>
 #include <climits>
+#include <type_traits>
 
 #include "kernels.h"
 #include "ptx.cuh"
@@ -174,6 +175,68 @@ __global__ void ts_swiglu_kernel(const void *h, void *a, int64_t rows, int64_t h
     }
 }
 
+// 8 consecutive 16-bit values <-> floats.
+template <bool F16>
+__device__ __forceinline__ void unpack8(const uint4 &u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (F16) {
+            const float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        } else {
+            const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        }
+    }
+}
+template <bool F16>
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (F16) {
+            const __half2 t = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t *>(&t);
+        } else {
+            const __nv_bfloat162 t = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t *>(&t);
+        }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The gate and SwiGLU above with 16-byte accesses (columns and strides multiples of 8, 16-byte
+// aligned bases): blocks stride over rows, threads over 8-column chunks of a row.
+template <bool F16>
+__global__ void ts_gate_vec_kernel(uint16_t *o, int64_t ldo, const uint16_t *g, int64_t ldg, int64_t rows, int d) {
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
+        for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {
+            uint4 *po = reinterpret_cast<uint4 *>(o + r * ldo + c);
+            float x[8], gv[8];
+            unpack8<F16>(*po, x);
+            unpack8<F16>(*reinterpret_cast<const uint4 *>(g + r * ldg + c), gv);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] = x[i] / (1.0f + expf(-gv[i]));
+            *po = pack8<F16>(x);
+        }
+}
+
+template <bool F16>
+__global__ void ts_swiglu_vec_kernel(const uint16_t *h, uint16_t *a, int64_t rows, int hid) {
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
+        for (int c = threadIdx.x * 8; c < hid; c += blockDim.x * 8) {
+            float gt[8], up[8];
+            unpack8<F16>(*reinterpret_cast<const uint4 *>(h + r * 2 * hid + c), gt);
+            unpack8<F16>(*reinterpret_cast<const uint4 *>(h + r * 2 * hid + hid + c), up);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) gt[i] = gt[i] * (up[i] / (1.0f + expf(-up[i])));
+            *reinterpret_cast<uint4 *>(a + r * hid + c) = pack8<F16>(gt);
+        }
+}
+
 // Variate attention (VariateJob.run, timestral/model.zig:648-709): at each (group, token) the
 // group's rows attend to each other per head. One warp per (group, token, head); each lane owns
 // head dims (2 lane, 2 lane + 1).
@@ -232,6 +295,90 @@ __global__ void ts_variate_kernel(TsVariateCall c) {
         const int64_t ob = ((r0 + iq) * c.sl + tok) * c.ldo + h * 64 + 2 * lane;
         store16(c.o, ob, c.dtype, o0);
         store16(c.o, ob + 1, c.dtype, o1);
+    }
+}
+
+// The same for V rows per group, known at compile time: 16 lanes per (group, token, head), lane l
+// owning head dims 4l .. 4l + 3, so q / k / v of all rows stay in registers (as 16-bit pairs),
+// every dot product needs 4 shuffles, and the key masks are read once per instance.
+template <int V, bool F16>
+__global__ void ts_variate_vec_kernel(TsVariateCall c) {
+    using H2 = typename std::conditional<F16, __half2, __nv_bfloat162>::type;
+    const int64_t inst = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+    const int hl = threadIdx.x & 15;
+    const int64_t total = c.groups * c.sl * c.heads;
+    // Both halves of a warp take part in the shuffles; an idle half computes instance 0.
+    const bool active = inst < total;
+    const int64_t id = active ? inst : 0;
+    const int h = (int)(id % c.heads);
+    const int64_t tok = (id / c.heads) % c.sl, g = id / (c.heads * c.sl);
+    const int64_t r0 = g * V;
+    auto to_f2 = [](uint32_t w) -> float2 {
+        if constexpr (F16)
+            return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+        else
+            return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
+    };
+    uint2 q[V], k[V], v[V];
+    uint32_t valid = 0;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const uint16_t *row = static_cast<const uint16_t *>(c.qkv) + ((r0 + i) * c.sl + tok) * c.ld + h * 64 + 4 * hl;
+        q[i] = *reinterpret_cast<const uint2 *>(row);
+        k[i] = *reinterpret_cast<const uint2 *>(row + c.d);
+        v[i] = *reinterpret_cast<const uint2 *>(row + 2 * c.d);
+        if (tok >= c.ne || c.key_valid[(r0 + i) * c.ne + tok] != 0) valid |= 1u << i;
+    }
+    int8_t role[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) role[i] = c.cov ? c.roles[i] : (int8_t)0;
+#pragma unroll
+    for (int iq = 0; iq < V; ++iq) {
+        const float2 qa = to_f2(q[iq].x), qb = to_f2(q[iq].y);
+        float s[V];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int ik = 0; ik < V; ++ik) {
+            const float2 ka = to_f2(k[ik].x), kb = to_f2(k[ik].y);
+            float dot = qa.x * ka.x + qa.y * ka.y + qb.x * kb.x + qb.y * kb.y;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            const int rq = role[iq], rk = role[ik];
+            const bool forbidden = (rq != 0 && rk == 0) || (rq == 2 && rk != 2);
+            const bool ok = ik == iq || (((valid >> ik) & 1u) && !forbidden);
+            s[ik] = ok ? dot * c.scale : -INFINITY;
+            mx = fmaxf(mx, s[ik]);
+        }
+        float sum = 0.0f;
+#pragma unroll
+        for (int ik = 0; ik < V; ++ik) {
+            s[ik] = s[ik] == -INFINITY ? 0.0f : expf(s[ik] - mx);
+            sum += s[ik];
+        }
+        const float inv = 1.0f / sum;
+        float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
+#pragma unroll
+        for (int ik = 0; ik < V; ++ik) {
+            const float p = s[ik] * inv;
+            if (p == 0.0f) continue;  // masked rows contribute nothing, whatever their values
+            const float2 va = to_f2(v[ik].x), vb = to_f2(v[ik].y);
+            o0 += p * va.x;
+            o1 += p * va.y;
+            o2 += p * vb.x;
+            o3 += p * vb.y;
+        }
+        if (active) {
+            uint16_t *dst = static_cast<uint16_t *>(c.o) + ((r0 + iq) * c.sl + tok) * c.ldo + h * 64 + 4 * hl;
+            H2 lo, hi;
+            if constexpr (F16) {
+                lo = __floats2half2_rn(o0, o1);
+                hi = __floats2half2_rn(o2, o3);
+            } else {
+                lo = __floats2bfloat162_rn(o0, o1);
+                hi = __floats2bfloat162_rn(o2, o3);
+            }
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+        }
     }
 }
 
@@ -487,20 +634,76 @@ Status launch_ts_rope(const int *first_obs, int64_t groups, int64_t sl, int64_t 
     return Status::ok();
 }
 
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 Status launch_ts_gate(void *o, int64_t ldo, const void *g, int64_t ldg, int64_t rows, int64_t d, int dtype, cudaStream_t s) {
-    ts_gate_kernel<<<grid_for(rows * d, 256), 256, 0, s>>>(o, ldo, g, ldg, rows, d, dtype);
+    if (aligned16(o) && aligned16(g) && d % 8 == 0 && ldo % 8 == 0 && ldg % 8 == 0 && d <= INT_MAX && rows > 0) {
+        const int grid = (int)std::min<int64_t>(rows, (int64_t)num_sms() * 16);
+        if (dtype == E_F16)
+            ts_gate_vec_kernel<true><<<grid, 128, 0, s>>>(static_cast<uint16_t *>(o), ldo,
+                                                          static_cast<const uint16_t *>(g), ldg, rows, (int)d);
+        else
+            ts_gate_vec_kernel<false><<<grid, 128, 0, s>>>(static_cast<uint16_t *>(o), ldo,
+                                                           static_cast<const uint16_t *>(g), ldg, rows, (int)d);
+    } else {
+        ts_gate_kernel<<<grid_for(rows * d, 256), 256, 0, s>>>(o, ldo, g, ldg, rows, d, dtype);
+    }
     TSFM_CUDA(cudaGetLastError(), "timestral gate: launch");
     return Status::ok();
 }
 
 Status launch_ts_swiglu(const void *h, void *a, int64_t rows, int64_t hid, int dtype, cudaStream_t s) {
-    ts_swiglu_kernel<<<grid_for(rows * hid, 256), 256, 0, s>>>(h, a, rows, hid, dtype);
+    if (aligned16(h) && aligned16(a) && hid % 8 == 0 && hid <= INT_MAX / 2 && rows > 0) {
+        const int grid = (int)std::min<int64_t>(rows, (int64_t)num_sms() * 16);
+        if (dtype == E_F16)
+            ts_swiglu_vec_kernel<true><<<grid, 256, 0, s>>>(static_cast<const uint16_t *>(h), static_cast<uint16_t *>(a),
+                                                            rows, (int)hid);
+        else
+            ts_swiglu_vec_kernel<false><<<grid, 256, 0, s>>>(static_cast<const uint16_t *>(h), static_cast<uint16_t *>(a),
+                                                             rows, (int)hid);
+    } else {
+        ts_swiglu_kernel<<<grid_for(rows * hid, 256), 256, 0, s>>>(h, a, rows, hid, dtype);
+    }
     TSFM_CUDA(cudaGetLastError(), "timestral swiglu: launch");
     return Status::ok();
 }
 
+template <int V>
+void variate_vec(const TsVariateCall &c, cudaStream_t s) {
+    const int64_t threads = c.groups * c.sl * c.heads * 16;
+    const unsigned grid = (unsigned)((threads + 255) / 256);
+    if (c.dtype == E_F16)
+        ts_variate_vec_kernel<V, true><<<grid, 256, 0, s>>>(c);
+    else
+        ts_variate_vec_kernel<V, false><<<grid, 256, 0, s>>>(c);
+}
+
 Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s) {
     if (c.vall > kMaxRows) return Status::fail(TSFM_ERR_UNSUPPORTED, "Timestral: more than 16 rows per series");
+    // 8-byte accesses per lane: row strides, the k / v offset and the base even in 4-element units.
+    if ((c.ld % 4) == 0 && (c.d % 4) == 0 && (c.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(c.qkv) & 7) == 0 &&
+        (reinterpret_cast<uintptr_t>(c.o) & 7) == 0 && c.groups * c.sl * c.heads * 16 < (int64_t)UINT_MAX * 256 / 2) {
+        switch (c.vall) {
+        case 1: variate_vec<1>(c, s); break;
+        case 2: variate_vec<2>(c, s); break;
+        case 3: variate_vec<3>(c, s); break;
+        case 4: variate_vec<4>(c, s); break;
+        case 5: variate_vec<5>(c, s); break;
+        case 6: variate_vec<6>(c, s); break;
+        case 7: variate_vec<7>(c, s); break;
+        case 8: variate_vec<8>(c, s); break;
+        case 9: variate_vec<9>(c, s); break;
+        case 10: variate_vec<10>(c, s); break;
+        case 11: variate_vec<11>(c, s); break;
+        case 12: variate_vec<12>(c, s); break;
+        case 13: variate_vec<13>(c, s); break;
+        case 14: variate_vec<14>(c, s); break;
+        case 15: variate_vec<15>(c, s); break;
+        default: variate_vec<16>(c, s); break;
+        }
+        TSFM_CUDA(cudaGetLastError(), "timestral variate attention: launch");
+        return Status::ok();
+    }
     const int64_t warps = c.groups * c.sl * c.heads;
     ts_variate_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(c);
     TSFM_CUDA(cudaGetLastError(), "timestral variate attention: launch");
