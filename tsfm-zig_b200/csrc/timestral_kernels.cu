@@ -209,7 +209,8 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 }
 
 // The gate and SwiGLU above with 16-byte accesses (columns and strides multiples of 8, 16-byte
-// aligned bases): blocks stride over rows, threads over 8-column chunks of a row.
+// aligned bases): blocks stride over rows, threads over 8-column chunks of a row. The logistic
+// uses the fast exponential intrinsic (a few ulp; the result is rounded to 16 bits).
 template <bool F16>
 __global__ void ts_gate_vec_kernel(uint16_t *o, int64_t ldo, const uint16_t *g, int64_t ldg, int64_t rows, int d) {
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
@@ -219,7 +220,7 @@ __global__ void ts_gate_vec_kernel(uint16_t *o, int64_t ldo, const uint16_t *g, 
             unpack8<F16>(*po, x);
             unpack8<F16>(*reinterpret_cast<const uint4 *>(g + r * ldg + c), gv);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) x[i] = x[i] / (1.0f + expf(-gv[i]));
+            for (int i = 0; i < 8; ++i) x[i] = x[i] / (1.0f + __expf(-gv[i]));
             *po = pack8<F16>(x);
         }
 }
@@ -232,7 +233,7 @@ __global__ void ts_swiglu_vec_kernel(const uint16_t *h, uint16_t *a, int64_t row
             unpack8<F16>(*reinterpret_cast<const uint4 *>(h + r * 2 * hid + c), gt);
             unpack8<F16>(*reinterpret_cast<const uint4 *>(h + r * 2 * hid + hid + c), up);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) gt[i] = gt[i] * (up[i] / (1.0f + expf(-up[i])));
+            for (int i = 0; i < 8; ++i) gt[i] = gt[i] * (up[i] / (1.0f + __expf(-up[i])));
             *reinterpret_cast<uint4 *>(a + r * hid + c) = pack8<F16>(gt);
         }
 }
@@ -302,7 +303,7 @@ __global__ void ts_variate_kernel(TsVariateCall c) {
 // owning head dims 4l .. 4l + 3, so q / k / v of all rows stay in registers (as 16-bit pairs),
 // every dot product needs 4 shuffles, and the key masks are read once per instance.
 template <int V, bool F16>
-__global__ void ts_variate_vec_kernel(TsVariateCall c) {
+__global__ void __launch_bounds__(256, V <= 11 ? 2 : 1) ts_variate_vec_kernel(TsVariateCall c) {
     using H2 = typename std::conditional<F16, __half2, __nv_bfloat162>::type;
     const int64_t inst = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
     const int hl = threadIdx.x & 15;
@@ -319,12 +320,13 @@ __global__ void ts_variate_vec_kernel(TsVariateCall c) {
         else
             return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
     };
-    uint2 q[V], k[V], v[V];
+    uint2 k[V], v[V];
     uint32_t valid = 0;
+    const uint16_t *qrow = static_cast<const uint16_t *>(c.qkv) + (r0 * c.sl + tok) * c.ld + h * 64 + 4 * hl;
+    const int64_t row_step = c.sl * c.ld;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-        const uint16_t *row = static_cast<const uint16_t *>(c.qkv) + ((r0 + i) * c.sl + tok) * c.ld + h * 64 + 4 * hl;
-        q[i] = *reinterpret_cast<const uint2 *>(row);
+        const uint16_t *row = qrow + i * row_step;
         k[i] = *reinterpret_cast<const uint2 *>(row + c.d);
         v[i] = *reinterpret_cast<const uint2 *>(row + 2 * c.d);
         if (tok >= c.ne || c.key_valid[(r0 + i) * c.ne + tok] != 0) valid |= 1u << i;
@@ -332,18 +334,27 @@ __global__ void ts_variate_vec_kernel(TsVariateCall c) {
     int8_t role[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) role[i] = c.cov ? c.roles[i] : (int8_t)0;
+    auto role_of = [&](int i) -> int { return c.cov ? c.roles[i] : 0; };
+    float4 kf[V], vf[V];
 #pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const float2 a = to_f2(k[i].x), b = to_f2(k[i].y);
+        kf[i] = make_float4(a.x, a.y, b.x, b.y);
+        const float2 c2 = to_f2(v[i].x), d2 = to_f2(v[i].y);
+        vf[i] = make_float4(c2.x, c2.y, d2.x, d2.y);
+    }
+#pragma unroll 1
     for (int iq = 0; iq < V; ++iq) {
-        const float2 qa = to_f2(q[iq].x), qb = to_f2(q[iq].y);
+        const uint2 qv = *reinterpret_cast<const uint2 *>(qrow + iq * row_step);
+        const float2 qa = to_f2(qv.x), qb = to_f2(qv.y);
         float s[V];
         float mx = -INFINITY;
 #pragma unroll
         for (int ik = 0; ik < V; ++ik) {
-            const float2 ka = to_f2(k[ik].x), kb = to_f2(k[ik].y);
-            float dot = qa.x * ka.x + qa.y * ka.y + qb.x * kb.x + qb.y * kb.y;
+            float dot = qa.x * kf[ik].x + qa.y * kf[ik].y + qb.x * kf[ik].z + qb.y * kf[ik].w;
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-            const int rq = role[iq], rk = role[ik];
+            const int rq = role_of(iq), rk = role[ik];
             const bool forbidden = (rq != 0 && rk == 0) || (rq == 2 && rk != 2);
             const bool ok = ik == iq || (((valid >> ik) & 1u) && !forbidden);
             s[ik] = ok ? dot * c.scale : -INFINITY;
@@ -361,11 +372,10 @@ __global__ void ts_variate_vec_kernel(TsVariateCall c) {
         for (int ik = 0; ik < V; ++ik) {
             const float p = s[ik] * inv;
             if (p == 0.0f) continue;  // masked rows contribute nothing, whatever their values
-            const float2 va = to_f2(v[ik].x), vb = to_f2(v[ik].y);
-            o0 += p * va.x;
-            o1 += p * va.y;
-            o2 += p * vb.x;
-            o3 += p * vb.y;
+            o0 += p * vf[ik].x;
+            o1 += p * vf[ik].y;
+            o2 += p * vf[ik].z;
+            o3 += p * vf[ik].w;
         }
         if (active) {
             uint16_t *dst = static_cast<uint16_t *>(c.o) + ((r0 + iq) * c.sl + tok) * c.ldo + h * 64 + 4 * hl;
