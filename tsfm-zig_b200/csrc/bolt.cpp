@@ -240,19 +240,20 @@ Status predict_block(Replica &r, const tsfm_config &c, const BoltDev &w, const f
 }
 
 Status load_lin(Replica &r, const TensorTable &t, const std::string &name, int64_t out, int64_t in, int act, DLin &dst) {
-    std::vector<float> v;
-    TSFM_TRY(t.get(name, out * in, v));
-    return upload_lin(r, v, out, in, act, dst);
+    const tsfm_tensor *w;
+    TSFM_TRY(t.raw(name, out * in, &w));
+    return upload_lin_raw(r, {w}, nullptr, out, in, act, dst);
 }
 
 Status load_concat(Replica &r, const TensorTable &t, const std::vector<std::string> &names, int64_t out_each, int64_t in,
                    int act, DLin &dst) {
-    std::vector<float> all, v;
+    std::vector<const tsfm_tensor *> parts;
     for (const auto &nm : names) {
-        TSFM_TRY(t.get(nm, out_each * in, v));
-        all.insert(all.end(), v.begin(), v.end());
+        const tsfm_tensor *w;
+        TSFM_TRY(t.raw(nm, out_each * in, &w));
+        parts.push_back(w);
     }
-    return upload_lin(r, all, out_each * (int64_t)names.size(), in, act, dst);
+    return upload_lin_raw(r, parts, nullptr, out_each * (int64_t)names.size(), in, act, dst);
 }
 
 Status load_norm(Replica &r, const TensorTable &t, const std::string &name, int64_t d, float **dst) {

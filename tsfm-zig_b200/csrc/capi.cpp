@@ -294,7 +294,13 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
                 devs.push_back(devices[i]);
             }
         }
-        for (size_t i = 0; i < devs.size(); ++i) {
+        // Replicas load in parallel, one host thread per device (each uploads over its own link).
+        const size_t nrep = devs.size();
+        std::vector<std::unique_ptr<Replica>> reps(nrep);
+        std::vector<std::unique_ptr<C2Dev>> c2w(nrep);
+        std::vector<std::unique_ptr<BoltDev>> boltw(nrep);
+        std::vector<std::unique_ptr<TsDev>> tsw(nrep);
+        TSFM_TRY(for_replicas(nrep, [&](size_t i) -> Status {
             auto r = std::make_unique<Replica>();
             r->device = devs[i];
             TSFM_CUDA(cudaSetDevice(r->device), "cudaSetDevice");
@@ -302,22 +308,27 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
             TSFM_CUDA(cudaStreamCreateWithFlags(&r->copy, cudaStreamNonBlocking), "cudaStreamCreate");
             TSFM_TRY(r->err.alloc(16));
             TSFM_CUDA(cudaMemset(r->err.p, 0, 16), "clear error word");
+            Status st;
             if (c.family == TSFM_CHRONOS2) {
-                auto w = std::make_unique<C2Dev>();
-                TSFM_TRY(c2_load(*r, c, table, act, *w));
-                m->c2.push_back(std::move(w));
+                c2w[i] = std::make_unique<C2Dev>();
+                st = c2_load(*r, c, table, act, *c2w[i]);
             } else if (c.family == TSFM_CHRONOS_BOLT) {
-                auto w = std::make_unique<BoltDev>();
-                TSFM_TRY(bolt_load(*r, c, table, act, *w));
-                m->bolt.push_back(std::move(w));
+                boltw[i] = std::make_unique<BoltDev>();
+                st = bolt_load(*r, c, table, act, *boltw[i]);
             } else {
-                auto w = std::make_unique<TsDev>();
-                TSFM_TRY(ts_load(*r, c, table, act, *w));
-                m->ts.push_back(std::move(w));
+                tsw[i] = std::make_unique<TsDev>();
+                st = ts_load(*r, c, table, act, *tsw[i]);
             }
-            if (i == 0)
-                for (auto &b : r->weights) m->weight_bytes += b.bytes;
-            m->reps.push_back(std::move(r));
+            r->stage.reset();  // staging is needed at load time only
+            reps[i] = std::move(r);
+            return st;
+        }));
+        for (auto &b : reps[0]->weights) m->weight_bytes += b.bytes;
+        for (size_t i = 0; i < nrep; ++i) {
+            if (c2w[i]) m->c2.push_back(std::move(c2w[i]));
+            if (boltw[i]) m->bolt.push_back(std::move(boltw[i]));
+            if (tsw[i]) m->ts.push_back(std::move(tsw[i]));
+            m->reps.push_back(std::move(reps[i]));
         }
         *out = m.release();
         return Status::ok();

@@ -98,39 +98,32 @@ Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, 
     TSFM_TRY(upload_f32(r, reg, &w.reg));
     for (int li = 0; li < c.num_layers; ++li) {
         C2Dev::Layer L;
-        std::vector<float> qkv;
         for (int which = 0; which < 2; ++which) {
             const std::string p = strf("encoder.block.%d.layer.%d.", li, which);
             TSFM_TRY(t.get(p + "layer_norm.weight", d, v));
             TSFM_TRY(upload_f32(r, v, which == 0 ? &L.time_norm : &L.group_norm));
+            const tsfm_tensor *tq, *tk, *tv, *to;
+            TSFM_TRY(t.raw(p + "self_attention.q.weight", d * d, &tq));
+            TSFM_TRY(t.raw(p + "self_attention.k.weight", d * d, &tk));
+            TSFM_TRY(t.raw(p + "self_attention.v.weight", d * d, &tv));
+            TSFM_TRY(t.raw(p + "self_attention.o.weight", d * d, &to));
             if (which == 0) {
-                qkv.clear();
-                for (const char *nm : {"q", "k", "v"}) {
-                    TSFM_TRY(t.get(p + "self_attention." + nm + ".weight", d * d, v));
-                    qkv.insert(qkv.end(), v.begin(), v.end());
-                }
-                TSFM_TRY(upload_lin(r, qkv, 3 * d, d, act, L.qkv));
-                TSFM_TRY(t.get(p + "self_attention.o.weight", d * d, v));
-                TSFM_TRY(upload_lin(r, v, d, d, act, L.o));
+                TSFM_TRY(upload_lin_raw(r, {tq, tk, tv}, nullptr, 3 * d, d, act, L.qkv));
+                TSFM_TRY(upload_lin_raw(r, {to}, nullptr, d, d, act, L.o));
             } else {
                 // Singleton groups: only v and o take part (chronos2/model.zig:265-269); q and k are
-                // still required to exist, as the reference loads them.
-                TSFM_TRY(t.get(p + "self_attention.q.weight", d * d, v));
-                TSFM_TRY(t.get(p + "self_attention.k.weight", d * d, v));
-                // o(v(x)) = x (W_o W_v)^T: one GEMM with the product formed in float64 and
-                // rounded once.
-                std::vector<float> wv, wo;
-                TSFM_TRY(t.get(p + "self_attention.v.weight", d * d, wv));
-                TSFM_TRY(t.get(p + "self_attention.o.weight", d * d, wo));
-                TSFM_TRY(upload_lin(r, matmul_f64(wo, wv, d, d, d), d, d, act, L.gvo));
+                // still required to exist, as the reference loads them. o(v(x)) = x (W_o W_v)^T:
+                // one GEMM with the product formed in float64 and rounded once.
+                TSFM_TRY(upload_fold_raw(r, to, tv, d, d, d, act, L.gvo));
             }
         }
         TSFM_TRY(t.get(strf("encoder.block.%d.layer.2.layer_norm.weight", li), d, v));
         TSFM_TRY(upload_f32(r, v, &L.mlp_norm));
-        TSFM_TRY(t.get(strf("encoder.block.%d.layer.2.mlp.wi.weight", li), hid * d, v));
-        TSFM_TRY(upload_lin(r, v, hid, d, act, L.wi));
-        TSFM_TRY(t.get(strf("encoder.block.%d.layer.2.mlp.wo.weight", li), d * hid, v));
-        TSFM_TRY(upload_lin(r, v, d, hid, act, L.wo));
+        const tsfm_tensor *twi, *two;
+        TSFM_TRY(t.raw(strf("encoder.block.%d.layer.2.mlp.wi.weight", li), hid * d, &twi));
+        TSFM_TRY(t.raw(strf("encoder.block.%d.layer.2.mlp.wo.weight", li), d * hid, &two));
+        TSFM_TRY(upload_lin_raw(r, {twi}, nullptr, hid, d, act, L.wi));
+        TSFM_TRY(upload_lin_raw(r, {two}, nullptr, d, hid, act, L.wo));
         w.layers.push_back(L);
     }
     // RoPE tables for every position a sequence can have (chronos2/model.zig:107-113, 178-187).

@@ -101,6 +101,14 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream);
 // CUtensorMap (128 bytes).
 Status make_tmap_2d(void *map, const void *base, int dtype, int64_t inner, int64_t outer, int64_t ld,
                     uint32_t box_inner, uint32_t box_outer);
+// Weight conversion on the device (weights.cu). dst row r = src row (map ? map[r] : r), converted
+// from src_dt (E_F32 / E_F16 / E_BF16) to dst_dt (E_F16, E_BF16, or E_F32 = TF32-rounded).
+Status launch_convert_rows(const void *src, int src_dt, const int32_t *map, void *dst, int dst_dt, int64_t rows,
+                           int64_t cols, cudaStream_t s);
+// dst = a (m x k) b (k x n) in float64, rounded to float, then to dst_dt (E_F16, E_BF16, E_F32).
+Status launch_fold_f64(const void *a, int a_dt, const void *b, int b_dt, void *dst, int dst_dt, int64_t m, int64_t k,
+                       int64_t n, cudaStream_t s);
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel): the attribute
 // stays set in the context, and setting it on every launch costs host time.
 Status ensure_smem_attr(const void *func, int bytes);

@@ -5,7 +5,6 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstring>
-#include <thread>
 
 #include <cuda_fp16.h>
 
@@ -214,6 +213,125 @@ Status TensorTable::get(const std::string &name, size_t numel, std::vector<float
     return Status::ok();
 }
 
+Status TensorTable::raw(const std::string &name, size_t numel, const tsfm_tensor **out) const {
+    auto it = by_name.find(name);
+    if (it == by_name.end()) return Status::fail(TSFM_ERR_MISSING_TENSOR, "missing tensor: " + name);
+    const tsfm_tensor *t = it->second;
+    if (t->dtype != TSFM_DTYPE_F32 && t->dtype != TSFM_DTYPE_F16 && t->dtype != TSFM_DTYPE_BF16)
+        return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "tensor " + name + " has unsupported dtype");
+    if (t->numel != numel)
+        return Status::fail(TSFM_ERR_SHAPE_MISMATCH, strf("tensor %s: expected %zu elements, file has %llu",
+                                                          name.c_str(), numel, (unsigned long long)t->numel));
+    if (!t->data && numel) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "tensor " + name + " has no data");
+    *out = t;
+    return Status::ok();
+}
+
+static int elem_of(const tsfm_tensor *t) {
+    return t->dtype == TSFM_DTYPE_F32 ? E_F32 : t->dtype == TSFM_DTYPE_F16 ? E_F16 : E_BF16;
+}
+
+// Copies the tensors as stored, back to back, into the replica's staging buffer after `extra`
+// leading bytes left free; returns where the first one starts.
+static Status stage_tensors(Replica &r, const std::vector<const tsfm_tensor *> &parts, size_t extra, char **first) {
+    const size_t esz = elem_of(parts[0]) == E_F32 ? 4 : 2;
+    size_t bytes = extra;
+    for (const tsfm_tensor *t : parts) bytes += Arena::span((size_t)t->numel * esz);
+    if (r.stage.bytes < bytes) TSFM_TRY(r.stage.alloc(bytes));
+    char *dst = static_cast<char *>(r.stage.p) + extra;
+    *first = dst;
+    for (const tsfm_tensor *t : parts) {
+        const size_t n = (size_t)t->numel * esz;
+        TSFM_CUDA(cudaMemcpyAsync(dst, t->data, n, cudaMemcpyHostToDevice, r.stream), "stage weight");
+        dst += n;
+    }
+    return Status::ok();
+}
+
+Status upload_lin_raw(Replica &r, const std::vector<const tsfm_tensor *> &parts, const std::vector<int32_t> *map,
+                      int64_t out, int64_t in, int dtype, DLin &dst) {
+    if (parts.empty()) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "weight upload: no tensors");
+    int64_t rows = 0;
+    bool same = true;
+    for (const tsfm_tensor *t : parts) {
+        if ((int64_t)t->numel % in) return Status::fail(TSFM_ERR_SHAPE_MISMATCH, "weight upload: ragged rows");
+        rows += (int64_t)t->numel / in;
+        same = same && elem_of(t) == elem_of(parts[0]);
+    }
+    if (map ? (int64_t)map->size() != out : rows != out)
+        return Status::fail(TSFM_ERR_SHAPE_MISMATCH, "weight upload: row count");
+    if (!same) {
+        // Mixed storage types: convert on the host (rare).
+        std::vector<float> all((size_t)(rows * in));
+        size_t off = 0;
+        for (const tsfm_tensor *t : parts) {
+            for (size_t i = 0; i < (size_t)t->numel; ++i) {
+                const int dt = elem_of(t);
+                if (dt == E_F32) {
+                    all[off + i] = static_cast<const float *>(t->data)[i];
+                } else {
+                    const uint16_t u = static_cast<const uint16_t *>(t->data)[i];
+                    if (dt == E_BF16) {
+                        const uint32_t bits = (uint32_t)u << 16;
+                        std::memcpy(&all[off + i], &bits, 4);
+                    } else {
+                        all[off + i] = half_bits_to_float(u);
+                    }
+                }
+            }
+            off += (size_t)t->numel;
+        }
+        if (!map) return upload_lin(r, all, out, in, dtype, dst);
+        std::vector<float> perm((size_t)(out * in));
+        for (int64_t i = 0; i < out; ++i)
+            std::memcpy(&perm[(size_t)(i * in)], &all[(size_t)((*map)[(size_t)i] * in)], (size_t)in * 4);
+        return upload_lin(r, perm, out, in, dtype, dst);
+    }
+    const size_t map_bytes = map ? Arena::span(map->size() * 4) : 0;
+    char *src = nullptr;
+    TSFM_TRY(stage_tensors(r, parts, map_bytes, &src));
+    const int32_t *dmap = nullptr;
+    if (map) {
+        for (int32_t v : *map)
+            if (v < 0 || v >= rows) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "weight upload: row map");
+        TSFM_CUDA(cudaMemcpyAsync(r.stage.p, map->data(), map->size() * 4, cudaMemcpyHostToDevice, r.stream),
+                  "stage row map");
+        dmap = static_cast<const int32_t *>(r.stage.p);
+    }
+    DevBuf b;
+    TSFM_TRY(b.alloc((size_t)(out * in) * (dtype == E_F32 ? 4 : 2)));
+    TSFM_TRY(launch_convert_rows(src, elem_of(parts[0]), dmap, b.p, dtype, out, in, r.stream));
+    TSFM_CUDA(cudaStreamSynchronize(r.stream), "weight upload");
+    dst.out = out;
+    dst.in = in;
+    dst.dtype = dtype;
+    dst.w = b.p;
+    r.weights.push_back(std::move(b));
+    return Status::ok();
+}
+
+Status upload_fold_raw(Replica &r, const tsfm_tensor *a, const tsfm_tensor *b, int64_t m, int64_t k, int64_t n,
+                       int dtype, DLin &dst) {
+    if ((int64_t)a->numel != m * k || (int64_t)b->numel != k * n)
+        return Status::fail(TSFM_ERR_SHAPE_MISMATCH, "weight fold: shapes");
+    const size_t esz_a = elem_of(a) == E_F32 ? 4 : 2, esz_b = elem_of(b) == E_F32 ? 4 : 2;
+    const size_t sa = Arena::span((size_t)a->numel * esz_a), sb = Arena::span((size_t)b->numel * esz_b);
+    if (r.stage.bytes < sa + sb) TSFM_TRY(r.stage.alloc(sa + sb));
+    char *pa = static_cast<char *>(r.stage.p), *pb = pa + sa;
+    TSFM_CUDA(cudaMemcpyAsync(pa, a->data, (size_t)a->numel * esz_a, cudaMemcpyHostToDevice, r.stream), "stage weight");
+    TSFM_CUDA(cudaMemcpyAsync(pb, b->data, (size_t)b->numel * esz_b, cudaMemcpyHostToDevice, r.stream), "stage weight");
+    DevBuf w;
+    TSFM_TRY(w.alloc((size_t)(m * n) * (dtype == E_F32 ? 4 : 2)));
+    TSFM_TRY(launch_fold_f64(pa, elem_of(a), pb, elem_of(b), w.p, dtype, m, k, n, r.stream));
+    TSFM_CUDA(cudaStreamSynchronize(r.stream), "weight fold");
+    dst.out = m;
+    dst.in = n;
+    dst.dtype = dtype;
+    dst.w = w.p;
+    r.weights.push_back(std::move(w));
+    return Status::ok();
+}
+
 static uint16_t f32_to_bf16_rne(float f) {
     uint32_t u;
     std::memcpy(&u, &f, 4);
@@ -241,35 +359,6 @@ Status upload_f32(Replica &r, const std::vector<float> &h, float **out) {
     *out = static_cast<float *>(b.p);
     r.weights.push_back(std::move(b));
     return Status::ok();
-}
-
-std::vector<float> matmul_f64(const std::vector<float> &a, const std::vector<float> &b, int64_t m, int64_t k, int64_t n) {
-    std::vector<double> bt((size_t)(k * n));
-    for (int64_t i = 0; i < k; ++i)
-        for (int64_t j = 0; j < n; ++j) bt[(size_t)(j * k + i)] = b[(size_t)(i * n + j)];
-    std::vector<float> c((size_t)(m * n));
-    const int64_t nth = std::max<int64_t>(1, std::min<int64_t>(m, std::thread::hardware_concurrency()));
-    std::vector<std::thread> th;
-    for (int64_t w = 0; w < nth; ++w)
-        th.emplace_back([&, w] {
-            std::vector<double> row((size_t)k);
-            for (int64_t i = m * w / nth; i < m * (w + 1) / nth; ++i) {
-                for (int64_t x = 0; x < k; ++x) row[(size_t)x] = a[(size_t)(i * k + x)];
-                for (int64_t j = 0; j < n; ++j) {
-                    const double *bj = &bt[(size_t)(j * k)];
-                    double s0 = 0, s1 = 0;
-                    int64_t x = 0;
-                    for (; x + 1 < k; x += 2) {
-                        s0 += row[(size_t)x] * bj[x];
-                        s1 += row[(size_t)x + 1] * bj[x + 1];
-                    }
-                    if (x < k) s0 += row[(size_t)x] * bj[x];
-                    c[(size_t)(i * n + j)] = (float)(s0 + s1);
-                }
-            }
-        });
-    for (auto &t : th) t.join();
-    return c;
 }
 
 Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, int dtype, DLin &dst) {

@@ -153,6 +153,7 @@ struct Replica {
     std::vector<cudaEvent_t> events;  // chunk hand-offs between the two streams
     DevBuf err;  // device error word(s)
     std::vector<DevBuf> weights;
+    DevBuf stage;  // raw checkpoint bytes on their way to a device weight (load time only)
     Arena ws;   // per-chunk model workspace
     Arena fc;   // forecaster buffers that live across chunks (Bolt quantile paths)
     DevBuf io;  // device copies of host inputs / outputs
@@ -208,15 +209,23 @@ struct TensorTable {
     // Presence, dtype and element count only (no conversion): lets a model be checked before
     // any device is touched.
     Status check(const std::string &name, size_t numel) const;
+    // The tensor as stored, after the checks of get().
+    Status raw(const std::string &name, size_t numel, const tsfm_tensor **out) const;
 };
 
 // Upload helpers (run with the replica's device current).
 Status upload_f32(Replica &r, const std::vector<float> &h, float **out);
 Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, int dtype, DLin &dst);
-// a (m, k) times b (k, n), row-major, accumulated in float64 and rounded to float32 once per
-// element; rows split across host threads.
-std::vector<float> matmul_f64(const std::vector<float> &a, const std::vector<float> &b, int64_t m, int64_t k, int64_t n);
 Status upload_bias(Replica &r, const std::vector<float> &b, DLin &dst);
+// A device weight [out, in] from checkpoint tensors stacked by rows (each `in` columns wide), copied
+// as stored and converted on the device to `dtype` (E_F16 / E_BF16; E_F32 = TF32-rounded). With
+// `map`, output row r is stacked row (*map)[r]; without, out must equal the stacked row count.
+Status upload_lin_raw(Replica &r, const std::vector<const tsfm_tensor *> &parts, const std::vector<int32_t> *map,
+                      int64_t out, int64_t in, int dtype, DLin &dst);
+// A device weight = a (m x k) b (k x n) formed in float64 on the device and rounded once (to
+// float, then to `dtype`).
+Status upload_fold_raw(Replica &r, const tsfm_tensor *a, const tsfm_tensor *b, int64_t m, int64_t k, int64_t n,
+                       int dtype, DLin &dst);
 Status upload_lin3(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, DLin3 &dst);
 
 // Checks the device error word after a stream sync.

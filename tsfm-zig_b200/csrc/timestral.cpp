@@ -483,29 +483,33 @@ Status ts_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, 
             a.is_time = it[ai];
             a.gate = (it[ai] ? c.time_attn_gate : c.variate_attn_gate) != 0;
             TSFM_TRY(load_norm(r, t, strf("transformer.layers.%d.attn_norms.%d.scale", li, ai), d, &a.norm));
-            std::vector<float> src;
-            TSFM_TRY(t.get(strf("transformer.layers.%d.attns.%d.wQKV.weight", li, ai), 3 * d * d, src));
+            std::vector<const tsfm_tensor *> parts(1);
+            TSFM_TRY(t.raw(strf("transformer.layers.%d.attns.%d.wQKV.weight", li, ai), 3 * d * d, &parts[0]));
             // permuteQkv (timestral/model.zig:72-85): rows (qkv, head_dim, heads) -> (qkv, head, head_dim).
-            std::vector<float> fused(3 * d * d);
+            std::vector<int32_t> map((size_t)(3 * d));
             for (int64_t sel = 0; sel < 3; ++sel)
                 for (int64_t h = 0; h < nh; ++h)
                     for (int64_t dd = 0; dd < hd; ++dd)
-                        std::memcpy(&fused[((sel * nh + h) * hd + dd) * d], &src[(sel * d + dd * nh + h) * d], d * 4);
+                        map[(size_t)((sel * nh + h) * hd + dd)] = (int32_t)(sel * d + dd * nh + h);
             if (a.gate) {
-                TSFM_TRY(t.get(strf("transformer.layers.%d.attns.%d._gate.weight", li, ai), d * d, v));
-                fused.insert(fused.end(), v.begin(), v.end());  // one GEMM yields [q | k | v | gate]
+                // One GEMM yields [q | k | v | gate].
+                parts.resize(2);
+                TSFM_TRY(t.raw(strf("transformer.layers.%d.attns.%d._gate.weight", li, ai), d * d, &parts[1]));
+                for (int64_t i = 0; i < d; ++i) map.push_back((int32_t)(3 * d + i));
             }
-            const int64_t cols = (int64_t)fused.size() / d;
+            const int64_t cols = (int64_t)map.size();
             w.max_qkv_cols = std::max(w.max_qkv_cols, cols);
-            TSFM_TRY(upload_lin(r, fused, cols, d, act, a.qkvg));
-            TSFM_TRY(t.get(strf("transformer.layers.%d.attns.%d.wO.weight", li, ai), d * d, v));
-            TSFM_TRY(upload_lin(r, v, d, d, act, a.o));
+            TSFM_TRY(upload_lin_raw(r, parts, &map, cols, d, act, a.qkvg));
+            const tsfm_tensor *to;
+            TSFM_TRY(t.raw(strf("transformer.layers.%d.attns.%d.wO.weight", li, ai), d * d, &to));
+            TSFM_TRY(upload_lin_raw(r, {to}, nullptr, d, d, act, a.o));
         }
         TSFM_TRY(load_norm(r, t, strf("transformer.layers.%d.mlp_norm.scale", li), d, &L.mlp_norm));
-        TSFM_TRY(t.get(strf("transformer.layers.%d.mlp.w12.weight", li), 2 * hid * d, v));
-        TSFM_TRY(upload_lin(r, v, 2 * hid, d, act, L.w12));
-        TSFM_TRY(t.get(strf("transformer.layers.%d.mlp.w3.weight", li), d * hid, v));
-        TSFM_TRY(upload_lin(r, v, d, hid, act, L.w3));
+        const tsfm_tensor *t12, *t3;
+        TSFM_TRY(t.raw(strf("transformer.layers.%d.mlp.w12.weight", li), 2 * hid * d, &t12));
+        TSFM_TRY(t.raw(strf("transformer.layers.%d.mlp.w3.weight", li), d * hid, &t3));
+        TSFM_TRY(upload_lin_raw(r, {t12}, nullptr, 2 * hid, d, act, L.w12));
+        TSFM_TRY(upload_lin_raw(r, {t3}, nullptr, d, hid, act, L.w3));
         w.layers.push_back(L);
     }
     // inv_freq with zeros past rope_dim / 2 (identity rotation) (timestral/model.zig:180-188).
