@@ -74,20 +74,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Non-blocking probe of the phase with the given parity: never suspends the thread, so one thread
-// can poll several barriers in turn.
-__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
 // Waits for the phase with the given parity to complete. Returns false (after raising the abort
 // flag and recording `site` in *err) when the wait exceeds kWaitTimeoutNs, or when another role
 // of the CTA has already aborted.
@@ -299,23 +285,6 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // cores reading an operand tile through a matrix descriptor).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// Named barrier over `count` threads (a multiple of 32), id 1..15 (0 is __syncthreads).
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
-    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// Named barrier that also returns the OR of `v` over the participating threads.
-__device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t count, bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-        "barrier.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}\n"
-        : "=r"(r)
-        : "r"((uint32_t)v), "r"(id), "r"(count)
-        : "memory");
-    return r != 0;
 }
 
 // max(a, b, c) in one instruction.
