@@ -34,7 +34,10 @@ def linear(x, w, bias, y, out_mode, act, M, N, K):
     torch.cuda.synchronize()
 
 
-SHAPES = [(128, 256, 64), (300, 336, 48), (1000, 768, 768), (257, 128, 3072), (7, 64, 200), (4096, 2304, 768)]
+# M >= 4096 with N > 128 runs on CTA pairs (2-SM MMA, 256-row tiles): full and partial row, column
+# and K tiles.
+SHAPES = [(128, 256, 64), (300, 336, 48), (1000, 768, 768), (257, 128, 3072), (7, 64, 200), (4096, 2304, 768),
+          (4097, 600, 200), (8191, 768, 64), (4500, 1000, 1032)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -67,6 +70,31 @@ def test_linear_matches_torch_fp32(M, N, K, dtype):
     linear(xd, wd, None, y2, 2, 0, M, N, K)
     ref2 = base.double() + xd.double() @ wd.double().T
     assert (y2.double() - ref2).abs().max().item() <= tol
+
+
+def test_linear_pairs_match_single_cta_tiles():
+    # The same products with and without CTA pairs (a child process with TSFM_GEMM_PAIRS=0) agree to
+    # within the FP32 accumulation tolerance.
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys, torch; sys.path[:0] = [%r, %r]; import tsfm_b200 as tb; "
+        "g = torch.Generator().manual_seed(5); x = torch.randn(6000, 768, generator=g).half().cuda(); "
+        "w = (torch.randn(2304, 768, generator=g) * 0.05).half().cuda(); y = torch.zeros(6000, 2304).cuda(); "
+        "tb.check(tb.lib.tsfm_kernel_linear(x.data_ptr(), 1, w.data_ptr(), 1, None, y.data_ptr(), 1, 0, 6000, 2304, "
+        "768, 768, 768, 2304, torch.cuda.current_stream().cuda_stream)); torch.cuda.synchronize(); "
+        "torch.save(y.cpu(), sys.argv[1])"
+    ) % (os.path.join(os.path.dirname(tb.__file__), ".."), os.path.join(os.path.dirname(tb.__file__), "..", ".."))
+    outs = []
+    for flag in ("1", "0"):
+        path = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"tsfm_pairs_{flag}_{os.getpid()}.pt")
+        env = dict(os.environ, TSFM_GEMM_PAIRS=flag)
+        subprocess.run([sys.executable, "-c", code, path], env=env, check=True, timeout=300)
+        outs.append(torch.load(path))
+        os.remove(path)
+    ref = outs[1].double()
+    assert (outs[0].double() - ref).abs().max().item() <= 1e-4 * ref.abs().max().item()
 
 
 def test_linear_padded_output_stride_keeps_padding():

@@ -23,6 +23,7 @@
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -35,11 +36,14 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kThreads = 192;
 
-template <int BN>
+// PAIR: the tile is 256 x BN, computed by a cluster of two CTAs with the 2-SM MMA; each CTA holds
+// 128 rows of x and BN / 2 rows of W per stage and 128 x BN accumulators.
+template <int BN, bool PAIR = false>
 struct TileCfg {
-    static constexpr int STAGES = BN >= 256 ? 4 : 6;
+    static constexpr int STAGES = PAIR ? 6 : BN >= 256 ? 4 : 6;
     static constexpr int A_BYTES = kBM * 128;
-    static constexpr int B_BYTES = BN * 128;
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+    static constexpr int B_BYTES = B_ROWS * 128;
     static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
     // Epilogue staging for the TMA stores: per epilogue warp two 4 KB boxes (32 rows x 128 B).
     static constexpr int STAGE_OFF = STAGES * (A_BYTES + B_BYTES);
@@ -176,16 +180,23 @@ __device__ __forceinline__ void bias_act(const Epi &e, int64_t col0, int nvalid,
     if (e.out_mode != OUT_F32_ACC) apply_act<32>(e.act, v);
 }
 
-template <typename T, int BN>
+template <typename T, int BN, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmY, Epi e) {
-    using C = TileCfg<BN>;
+    using C = TileCfg<BN, PAIR>;
     constexpr int STAGES = C::STAGES;
     constexpr int BK = 128 / (int)sizeof(T);
     // operand format: BF16 = 1, F16 = 0 (kind::f16); TF32 = 2 (kind::tf32)
     constexpr uint32_t FMT = std::is_same<T, float>::value ? 2u : std::is_same<T, __half>::value ? 0u : 1u;
-    constexpr uint32_t IDESC = idesc_f32acc(FMT, kBM, BN);
+    static_assert(!PAIR || FMT != 2u, "the 2-SM path takes 16-bit operands");
+    constexpr uint32_t IDESC = idesc_f32acc(FMT, PAIR ? 2 * kBM : kBM, BN);
+    // CTA pairs: rank 0 issues the MMAs for both; the tile's rows split by rank.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    constexpr int kRows = PAIR ? 2 * kBM : kBM;  // rows of x per tile
+    const int64_t unit = PAIR ? (int64_t)(blockIdx.x >> 1) : (int64_t)blockIdx.x;
+    const int64_t units = PAIR ? (int64_t)(gridDim.x >> 1) : (int64_t)gridDim.x;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -201,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t m_tiles = (e.M + kBM - 1) / kBM, n_tiles = (e.N + BN - 1) / BN;
+    const int64_t m_tiles = (e.M + kRows - 1) / kRows, n_tiles = (e.N + BN - 1) / BN;
     const int64_t tiles = m_tiles * n_tiles;
     const int num_k = (int)((e.K + BK - 1) / BK);
 
@@ -212,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 4 * 32);
+            mbar_init(&tempty[i], (PAIR ? 2 : 1) * 4 * 32);  // the epilogue threads of every CTA of the tile
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -221,11 +232,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, C::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // Both CTAs of a pair have initialised their barriers before either signals the other's.
+    if constexpr (PAIR) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -235,16 +253,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             uint32_t issued = 0, issued_ph = 0;  // per-stage bit: loaded at least once / parity of last load
-            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int32_t m0 = (int32_t)((t / n_tiles) * kBM), n0 = (int32_t)((t % n_tiles) * BN);
+            for (int64_t t = unit; t < tiles && ok; t += units) {
+                const int32_t m0 = (int32_t)((t / n_tiles) * kRows + rank * kBM);
+                const int32_t n0 = (int32_t)((t % n_tiles) * BN + rank * C::B_ROWS);
                 for (int kb = 0; kb < num_k; ++kb) {
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_PRODUCER)) {
+                    const bool got = PAIR ? mbar_wait_cl(&empty[s], ph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_PRODUCER)
+                                          : mbar_wait(&empty[s], ph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_PRODUCER);
+                    if (!got) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
-                    tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * BK, m0);
-                    tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * BK, n0);
+                    if constexpr (PAIR) {
+                        // The pair's first CTA expects the bytes of both CTAs' boxes on its barrier.
+                        if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES));
+                        const uint32_t fb = mapa_shared(&full[s], 0);
+                        tma_load_2d_pair(sA + s * C::A_BYTES, &tmA, fb, kb * BK, m0);
+                        tma_load_2d_pair(sB + s * C::B_BYTES, &tmB, fb, kb * BK, n0);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
+                        tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * BK, m0);
+                        tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * BK, n0);
+                    }
                     issued |= 1u << s;
                     issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
                     if (++s == STAGES) {
@@ -255,31 +284,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok) {
                 // Let loads already in flight land before the CTA can exit: the last load issued
-                // into stage i completes phase issued_ph[i] of full[i]; bounded grace period.
+                // into stage i completes phase issued_ph[i] of full[i]; bounded grace period. (A
+                // pair's second CTA signals its loads on the first CTA's barriers; it waits out
+                // the same grace period by the clock.)
                 const unsigned long long t0 = globaltimer_ns();
-                for (int i = 0; i < STAGES; ++i) {
-                    if (!((issued >> i) & 1u)) continue;
-                    while (!mbar_try_wait(&full[i], (issued_ph >> i) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
+                if (PAIR && !leader) {
+                    while (globaltimer_ns() - t0 < 1000000ull) {
+                    }
+                } else {
+                    for (int i = 0; i < STAGES; ++i) {
+                        if (!((issued >> i) & 1u)) continue;
+                        while (!mbar_try_wait_cl(&full[i], (issued_ph >> i) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
+                        }
                     }
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        // In a pair only the first CTA issues MMAs (for both CTAs' tensor memory).
+        if (lane == 0 && leader) {
             int s = 0;
             uint32_t ph = 0;
             int acc = 0;
             uint32_t aph = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_MMA_EMPTY)) {
+            for (int64_t t = unit; t < tiles && ok; t += units) {
+                const bool freed = PAIR ? mbar_wait_cl(&tempty[acc], aph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_MMA_EMPTY)
+                                        : mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_MMA_EMPTY);
+                if (!freed) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
                 for (int kb = 0; kb < num_k; ++kb) {
-                    if (!mbar_wait(&full[s], ph, abort_flag, e.err, ERR_SITE_GEMM_MMA_FULL)) {
+                    const bool got = PAIR ? mbar_wait_cl(&full[s], ph, abort_flag, e.err, ERR_SITE_GEMM_MMA_FULL)
+                                          : mbar_wait(&full[s], ph, abort_flag, e.err, ERR_SITE_GEMM_MMA_FULL);
+                    if (!got) {
                         ok = false;
                         break;
                     }
@@ -289,19 +330,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         // advance 32 bytes along K inside the 128-byte swizzle atom
-                        if constexpr (sizeof(T) == 2)
+                        if constexpr (PAIR)
+                            mma_f16kind_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
+                        else if constexpr (sizeof(T) == 2)
                             mma_f16kind(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
                         else
                             mma_tf32(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
                     }
-                    mma_commit(&empty[s]);
+                    if constexpr (PAIR) {
+                        mma_commit_pair(mapa_shared(&empty[s], 0));
+                        mma_commit_pair(mapa_shared(&empty[s], 1));
+                    } else {
+                        mma_commit(&empty[s]);
+                    }
                     if (++s == STAGES) {
                         s = 0;
                         ph ^= 1u;
                     }
                 }
                 if (!ok) break;
-                mma_commit(&tfull[acc]);
+                if constexpr (PAIR) {
+                    mma_commit_pair(mapa_shared(&tfull[acc], 0));
+                    mma_commit_pair(mapa_shared(&tfull[acc], 1));
+                } else {
+                    mma_commit(&tfull[acc]);
+                }
                 if (++acc == 2) {
                     acc = 0;
                     aph ^= 1u;
@@ -309,7 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // All MMAs issued by this thread have completed once `drain` fires; the tensor
             // memory can then be released safely even on the abort path.
-            mma_commit(drain);
+            if constexpr (PAIR)
+                mma_commit_pair(mapa_shared(drain, 0));
+            else
+                mma_commit(drain);
             const unsigned long long t0 = globaltimer_ns();
             while (!mbar_try_wait(drain, 0)) {
                 if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
@@ -377,40 +433,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         int acc = 0;
         uint32_t aph = 0;
-        for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-            // Warp-uniform wait: every lane polls the barrier, and the warp leaves together if any
-            // lane gave up, so the .sync.aligned TMEM loads below always run converged.
-            const bool got = mbar_wait(&tfull[acc], aph, abort_flag, e.err, ERR_SITE_GEMM_EPILOGUE);
-            if (!__all_sync(0xffffffffu, got)) break;
-            tc_fence_after();
-            const int64_t row = (t / n_tiles) * kBM + r_in_tile;
-            const int64_t wrow0 = (t / n_tiles) * kBM + eg * 32;  // first row of this warp's box
+        for (int64_t t = unit; t < tiles; t += units) {
+            const int64_t mrow0 = (t / n_tiles) * kRows + rank * kBM;  // this CTA's first row of the tile
+            const int64_t row = mrow0 + r_in_tile;
+            const int64_t wrow0 = mrow0 + eg * 32;  // first row of this warp's box
             const int64_t ncol0 = (t % n_tiles) * BN;
             const bool row_ok = row < e.M;
+            // RoPE: the row's cos / sin (same for every head) load once per tile, before the wait
+            // for the accumulator, so their latency hides behind the main loop.
+            const bool rope_tile = e.rope_cos != nullptr && ncol0 < e.rope_cols && row_ok;
+            float rc[32], rs[32];
+            if (rope_tile) {
+                const int64_t pidx = e.rope_p1 > 0 ? (row / e.rope_p1) * e.rope_p2 + row % e.rope_p2 : row % e.rope_p2;
+                const float4 *cs = reinterpret_cast<const float4 *>(e.rope_cos + pidx * 32);
+                const float4 *sn = reinterpret_cast<const float4 *>(e.rope_sin + pidx * 32);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 c4 = __ldg(cs + q), s4 = __ldg(sn + q);
+                    rc[4 * q] = c4.x;
+                    rc[4 * q + 1] = c4.y;
+                    rc[4 * q + 2] = c4.z;
+                    rc[4 * q + 3] = c4.w;
+                    rs[4 * q] = s4.x;
+                    rs[4 * q + 1] = s4.y;
+                    rs[4 * q + 2] = s4.z;
+                    rs[4 * q + 3] = s4.w;
+                }
+            }
+            // Warp-uniform wait: every lane polls the barrier, and the warp leaves together if any
+            // lane gave up, so the .sync.aligned TMEM loads below always run converged.
+            const bool got = PAIR ? mbar_wait_cl(&tfull[acc], aph, abort_flag, e.err, ERR_SITE_GEMM_EPILOGUE)
+                                  : mbar_wait(&tfull[acc], aph, abort_flag, e.err, ERR_SITE_GEMM_EPILOGUE);
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
             const int64_t orow = e.rm_g > 0 ? (row / e.rm_g) * e.rm_G + row % e.rm_g + e.rm_off : row;
             const uint32_t tbase = tmem_base + ((uint32_t)(eg * 32) << 16) + (uint32_t)(acc * BN);
             if (e.rope_cos != nullptr || (e.tma_mode != 0 && !f32_out)) {
                 // 64-column chunks (one head for RoPE): rotate-half pairs (i, i + 32) of columns
-                // < rope_cols. The row's cos / sin (same for every head) load once per tile.
-                const bool rope_tile = e.rope_cos != nullptr && ncol0 < e.rope_cols && row_ok;
-                float rc[32], rs[32];
-                if (rope_tile) {
-                    const int64_t pidx = e.rope_p1 > 0 ? (row / e.rope_p1) * e.rope_p2 + row % e.rope_p2 : row % e.rope_p2;
-                    const float4 *cs = reinterpret_cast<const float4 *>(e.rope_cos + pidx * 32);
-                    const float4 *sn = reinterpret_cast<const float4 *>(e.rope_sin + pidx * 32);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 c4 = __ldg(cs + q), s4 = __ldg(sn + q);
-                        rc[4 * q] = c4.x;
-                        rc[4 * q + 1] = c4.y;
-                        rc[4 * q + 2] = c4.z;
-                        rc[4 * q + 3] = c4.w;
-                        rs[4 * q] = s4.x;
-                        rs[4 * q + 1] = s4.y;
-                        rs[4 * q + 2] = s4.z;
-                        rs[4 * q + 3] = s4.w;
-                    }
-                }
+                // < rope_cols.
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 64) {
                     const int64_t col0 = ncol0 + c;
@@ -463,7 +523,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            if constexpr (PAIR)
+                mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));  // the MMA-issuing CTA's barrier
+            else
+                mbar_arrive(&tempty[acc]);
             if (++acc == 2) {
                 acc = 0;
                 aph ^= 1u;
@@ -474,11 +537,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     __syncthreads();
+    // A pair frees its tensor memory once both CTAs are done with it (the first CTA's MMAs have
+    // drained and both epilogues have read their accumulators), and neither CTA exits while the
+    // other could still reach its shared memory.
+    if constexpr (PAIR) cluster_sync_all();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::TMEM_COLS);
+        if constexpr (PAIR)
+            tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
+    if constexpr (PAIR) cluster_sync_all();
 }
 
 // ---- host side ------------------------------------------------------------------------------
@@ -552,16 +623,16 @@ Status ensure_smem_attr(const void *func, int bytes) {
 
 namespace {
 
-template <typename T, int BN>
+template <typename T, int BN, bool PAIR>
 Status launch_t(const LinearCall &c, cudaStream_t stream) {
-    using C = TileCfg<BN>;
+    using C = TileCfg<BN, PAIR>;
     constexpr int BK = 128 / (int)sizeof(T);
     CUtensorMap ta, tb;
     Status s = make_tmap(&ta, c.x, c.dtype, c.K, c.M, c.ldx, BK, kBM);
     if (!s) return s;
-    s = make_tmap(&tb, c.w, c.dtype, c.K, c.N, c.ldw, BK, BN);
+    s = make_tmap(&tb, c.w, c.dtype, c.K, c.N, c.ldw, BK, C::B_ROWS);
     if (!s) return s;
-    TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&linear_tc_kernel<T, BN>), C::SMEM));
+    TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&linear_tc_kernel<T, BN, PAIR>), C::SMEM));
     cudaError_t ce;
     Epi e;
     e.M = c.M;
@@ -591,9 +662,29 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
         if (make_tmap(&ty, c.y, ydt, c.N, c.M, c.ldy, f32_out ? 32 : 64, 32).code == 0)
             e.tma_mode = c.out_mode == OUT_F32_ACC ? 2 : 1;
     }
-    const int64_t tiles = ((c.M + kBM - 1) / kBM) * ((c.N + BN - 1) / BN);
-    const int grid = (int)std::min<int64_t>(tiles, sm_count());
-    linear_tc_kernel<T, BN><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, e);
+    if constexpr (PAIR) {
+        // Clusters of two CTAs, one per SM pair, persistent over 256-row tiles.
+        const int64_t tiles = ((c.M + 2 * kBM - 1) / (2 * kBM)) * ((c.N + BN - 1) / BN);
+        const int grid = 2 * (int)std::min<int64_t>(tiles, sm_count() / 2);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        ce = cudaLaunchKernelEx(&cfg, linear_tc_kernel<T, BN, true>, ta, tb, ty, e);
+        if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch (CTA pairs)");
+    } else {
+        const int64_t tiles = ((c.M + kBM - 1) / kBM) * ((c.N + BN - 1) / BN);
+        const int grid = (int)std::min<int64_t>(tiles, sm_count());
+        linear_tc_kernel<T, BN, false><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, e);
+    }
     ce = cudaGetLastError();
     if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch");
     return Status::ok();
@@ -628,6 +719,15 @@ Status make_tmap_grouped_rows(void *map, const void *base, int dtype, int64_t wi
     return Status::ok();
 }
 
+// TSFM_GEMM_PAIRS=0 keeps every product on single-CTA tiles.
+static bool gemm_pairs_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("TSFM_GEMM_PAIRS");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     if (c.M <= 0 || c.N <= 0 || c.K <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: empty product");
     if (c.M > INT32_MAX || c.N > INT32_MAX || c.K > INT32_MAX)
@@ -636,10 +736,18 @@ Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     if (c.rope_cos && (c.out_mode == OUT_F32_ACC || c.rope_cols % 64))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad rope");
     const bool small_n = c.N <= 128;
+    // Large 16-bit products run on CTA pairs (2-SM MMA, 256 x 256 tiles): each SM then streams half
+    // of W's tile instead of all of it.
+    const bool pair = !small_n && c.M >= 4096 && gemm_pairs_enabled();
     switch (c.dtype) {
-        case E_F32: return small_n ? launch_t<float, 128>(c, stream) : launch_t<float, 256>(c, stream);
-        case E_F16: return small_n ? launch_t<__half, 128>(c, stream) : launch_t<__half, 256>(c, stream);
-        case E_BF16: return small_n ? launch_t<__nv_bfloat16, 128>(c, stream) : launch_t<__nv_bfloat16, 256>(c, stream);
+        case E_F32: return small_n ? launch_t<float, 128, false>(c, stream) : launch_t<float, 256, false>(c, stream);
+        case E_F16:
+            return small_n ? launch_t<__half, 128, false>(c, stream)
+                           : pair ? launch_t<__half, 256, true>(c, stream) : launch_t<__half, 256, false>(c, stream);
+        case E_BF16:
+            return small_n ? launch_t<__nv_bfloat16, 128, false>(c, stream)
+                           : pair ? launch_t<__nv_bfloat16, 256, true>(c, stream)
+                                  : launch_t<__nv_bfloat16, 256, false>(c, stream);
         default: return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "linear: operand type");
     }
 }
