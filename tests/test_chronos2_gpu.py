@@ -99,15 +99,16 @@ def test_device_entry_point_matches_host_path(tiny):
     assert np.array_equal(out.cpu().numpy(), host)
 
 
-@pytest.mark.parametrize("b", [130, 257])
-def test_chunked_host_path_matches_device_path(tiny, b):
-    # Batches of 128+ series run as 2 or 4 chunks with the copies on a second stream; every series
-    # must come out exactly as from one device-resident forecast (pageable and pinned buffers).
+@pytest.mark.parametrize("b,t", [(130, 200), (2100, 8192), (8200, 8192)])
+def test_chunked_host_path_matches_device_path(tiny, b, t):
+    # The host entry point splits a batch into 1, 2 or 4 chunks by its copy volume (under 64 MB, up
+    # to 256 MB, more), with the copies on a second stream; every series must come out exactly as
+    # from one device-resident forecast (pageable and pinned buffers).
     _, _, gpu, _ = tiny
-    x = syn.seeded_series(b, 200, seed=11)
+    x = syn.seeded_series(b, t, seed=11)
     xd = torch.from_numpy(x).cuda()
     out = torch.empty((b, 48, 21), device="cuda")
-    gpu.forecast_chronos2_device(xd.data_ptr(), b, 200, 48, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    gpu.forecast_chronos2_device(xd.data_ptr(), b, t, 48, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     want = out.cpu().numpy()
     assert np.array_equal(gpu.forecast_chronos2(x, 48), want)
     xp = torch.from_numpy(x).pin_memory().numpy()

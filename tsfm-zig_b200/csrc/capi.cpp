@@ -131,8 +131,11 @@ Status replica_forecast(Replica &r, const void *in, int64_t nb, size_t in_row, s
         TSFM_TRY(r.pin_out.ensure(out_bytes));
         dst = static_cast<char *>(r.pin_out.p);
     }
-    // 64 or more series per chunk keep every GEMM and attention launch device-filling.
-    const int64_t chunks = nb >= 256 ? 4 : nb >= 128 ? 2 : 1;
+    // Chunks overlap the copies with the forwards, but every chunk repeats the forward's ~126 kernel
+    // launches (about 1 ms of launch latency and tail per chunk): split only when the copies are
+    // large enough to pay for it (at ~50 GB/s, 64 MB of copies take ~1.3 ms).
+    const size_t copy_bytes = in_bytes + out_bytes;
+    const int64_t chunks = std::min<int64_t>(nb, copy_bytes >= (size_t)256 << 20 ? 4 : copy_bytes >= (size_t)64 << 20 ? 2 : 1);
     while ((int64_t)r.events.size() < 2 * chunks) {
         cudaEvent_t e;
         TSFM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
