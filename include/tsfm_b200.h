@@ -264,7 +264,10 @@ int32_t tsfm_sgemm_nt_noalloc(int m, int n, int k, float alpha, const float *A, 
  *   x_dtype/w_dtype: TSFM_DTYPE_BF16 or TSFM_DTYPE_F16 (kind::f16), or TSFM_DTYPE_F32 (read as
  *   TF32, kind::tf32); both equal.
  *   out_mode: 0 = store in the 16-bit operand type, 1 = store f32, 2 = accumulate into f32.
- *   act: 0 none, 1 relu. bias may be null. Replaces nn.linear (core/nn.zig:270-293). */
+ *   act: 0 none, 1 relu, 3 gated pairs (W's rows in 256-row blocks [g (128) | u (128)], y of
+ *   N / 2 columns with y[:, 128 t + c] = g[c] * silu(u[c]) for block t; N % 256 == 0, out_mode 0,
+ *   16-bit operands, no bias: mulSilu of core/nn.zig:302-563 fused into the product).
+ *   bias may be null. Replaces nn.linear (core/nn.zig:270-293). */
 int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_t w_dtype,
                            const float *bias, void *y, int32_t out_mode, int32_t act,
                            int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldy,

@@ -72,6 +72,25 @@ def test_linear_matches_torch_fp32(M, N, K, dtype):
     assert (y2.double() - ref2).abs().max().item() <= tol
 
 
+@pytest.mark.parametrize("M", [300, 5000])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_linear_gated_pairs(M, dtype):
+    # act 3: y[:, 128 t + c] = g * silu(u) with g, u = columns c and 128 + c of the product's
+    # 256-column block t (single-CTA tiles at M = 300, CTA pairs at M = 5000).
+    N, K = 768, 320
+    g = torch.Generator(device="cpu").manual_seed(M + 11)
+    x = torch.randn(M, K, generator=g).to(dev(), TORCH16[dtype])
+    w = (torch.randn(N, K, generator=g) * 0.05).to(dev(), TORCH16[dtype])
+    y = torch.full((M, N // 2), float("nan"), device=dev(), dtype=TORCH16[dtype])
+    tb.check(tb.lib.tsfm_kernel_linear(x.data_ptr(), CODE16[x.dtype], w.data_ptr(), CODE16[w.dtype], None, y.data_ptr(),
+                                       0, 3, M, N, K, K, K, N // 2, stream_ptr()))
+    torch.cuda.synchronize()
+    p = (x.double() @ w.double().T).view(M, N // 256, 2, 128)
+    ref = (p[:, :, 0] * torch.nn.functional.silu(p[:, :, 1])).reshape(M, N // 2)
+    tol = 2 ** -7 * ref.abs().max().item() + 1e-3
+    assert (y.double() - ref).abs().max().item() <= tol
+
+
 def test_linear_pairs_match_single_cta_tiles():
     # The same products with and without CTA pairs (a child process with TSFM_GEMM_PAIRS=0) agree to
     # within the FP32 accumulation tolerance.

@@ -550,7 +550,7 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
         const int elem = x_dtype == TSFM_DTYPE_F32 ? E_F32 : x_dtype == TSFM_DTYPE_F16 ? E_F16 : E_BF16;
         if (out_mode == 0 && elem == E_F32)
             return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: out_mode 0 stores the 16-bit operand type");
-        if (out_mode < 0 || out_mode > 2 || act < 0 || act > 1)
+        if (out_mode < 0 || out_mode > 2 || (act != 0 && act != 1 && act != ACT_GLU))
             return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode / act");
         LinearCall c;
         c.x = x;

@@ -48,6 +48,8 @@ struct Status {
 
 // y = epilogue(x[M, K] · w[N, K]^T). x and w share one element type: BF16 or FP16 (kind::f16) or
 // FP32 read as TF32 (kind::tf32).
+enum : int { ACT_GLU = 3 };
+
 struct LinearCall {
     const void *x = nullptr;
     const void *w = nullptr;
@@ -57,7 +59,10 @@ struct LinearCall {
     int64_t ldy = 0;
     int out_mode = OUT_BF16;  // OutMode; OUT_F32_ACC: y += result
     const float *bias = nullptr;
-    int act = 0;       // 0 none, 1 relu, 2 silu
+    // 0 none, 1 relu, 2 silu, ACT_GLU: gated pairs. With ACT_GLU the weight's rows come in 256-row
+    // blocks [g (128) | u (128)] and y has N / 2 columns: y[:, 128 t + c] = g[c] * silu(u[c]) for
+    // block t (mulSilu, core/nn.zig:302-563; N a multiple of 256, 16-bit y, no bias or remap).
+    int act = 0;
     // output row remap: y row = (r / rm_g) * rm_G + r % rm_g + rm_off when rm_g > 0
     int64_t rm_g = 0, rm_G = 0, rm_off = 0;
     // rotate-half RoPE on columns [0, rope_cols), 64-wide heads; tables [positions, 32]

@@ -68,7 +68,8 @@ struct Epi {
 };
 
 // Activation over n values: 1 relu, 2 silu (nn.siluInPlace, core/nn.zig:399-407). The branch is
-// uniform and taken outside the element loops, so act == 0 costs nothing.
+// uniform and taken outside the element loops, so act == 0 costs nothing. ACT_GLU (gated pairs,
+// handled in the epilogue loop) never reaches here.
 template <int N>
 __device__ __forceinline__ void apply_act(int act, float *v) {
     if (act == 1) {
@@ -468,7 +469,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int64_t orow = e.rm_g > 0 ? (row / e.rm_g) * e.rm_G + row % e.rm_g + e.rm_off : row;
             const uint32_t tbase = tmem_base + ((uint32_t)(eg * 32) << 16) + (uint32_t)(acc * BN);
-            if (e.rope_cos != nullptr || (e.tma_mode != 0 && !f32_out)) {
+            if (BN == 256 && e.act == ACT_GLU) {
+                // Gated pairs: the tile's columns are [g (128) | u (128)]; output column
+                // (tile * 128 + c) = g[c] * silu(u[c]), staged and stored in 64-column boxes. The
+                // logistic uses the fast exponential and division intrinsics (a few ulp; the result
+                // is rounded to 16 bits), so the epilogue keeps pace with the main loop.
+#pragma unroll 1
+                for (int c = 0; c < 128; c += 64) {
+                    uint8_t *b = stage_box();
+                    const bool f16 = e.out_mode == OUT_F16;
+#pragma unroll
+                    for (int h = 0; h < 64; h += 32) {
+                        float g[32], u[32];
+                        tmem_ld32(tbase + c + h, g);
+                        tmem_ld32(tbase + 128 + c + h, u);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) g[j] = g[j] * __fdividef(u[j], 1.0f + __expf(-u[j]));
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float *src = g + 8 * q;
+                            uint4 pk;
+                            pk.x = f16 ? pack2<__half>(src[0], src[1]) : pack2<__nv_bfloat16>(src[0], src[1]);
+                            pk.y = f16 ? pack2<__half>(src[2], src[3]) : pack2<__nv_bfloat16>(src[2], src[3]);
+                            pk.z = f16 ? pack2<__half>(src[4], src[5]) : pack2<__nv_bfloat16>(src[4], src[5]);
+                            pk.w = f16 ? pack2<__half>(src[6], src[7]) : pack2<__nv_bfloat16>(src[6], src[7]);
+                            put16(b, h / 8 + q, pk);
+                        }
+                    }
+                    issue_box(b, ncol0 / 2 + c, wrow0);
+                }
+            } else if (e.rope_cos != nullptr || (e.tma_mode != 0 && !f32_out)) {
                 // 64-column chunks (one head for RoPE): rotate-half pairs (i, i + 32) of columns
                 // < rope_cols.
 #pragma unroll 1
@@ -659,9 +690,12 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     CUtensorMap ty = tb;
     if (c.rm_g <= 0 && !(c.out_mode == OUT_F32_ACC && c.act != 0)) {
         const int ydt = f32_out ? E_F32 : c.out_mode == OUT_F16 ? E_F16 : E_BF16;
-        if (make_tmap(&ty, c.y, ydt, c.N, c.M, c.ldy, f32_out ? 32 : 64, 32).code == 0)
+        const int64_t ycols = c.act == ACT_GLU ? c.N / 2 : c.N;
+        if (make_tmap(&ty, c.y, ydt, ycols, c.M, c.ldy, f32_out ? 32 : 64, 32).code == 0)
             e.tma_mode = c.out_mode == OUT_F32_ACC ? 2 : 1;
     }
+    if (c.act == ACT_GLU && e.tma_mode != 1)
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: gated pairs need a 16-byte-aligned 16-bit output");
     if constexpr (PAIR) {
         // Clusters of two CTAs, one per SM pair, persistent over 256-row tiles.
         const int64_t tiles = ((c.M + 2 * kBM - 1) / (2 * kBM)) * ((c.N + BN - 1) / BN);
@@ -735,6 +769,9 @@ Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     if (c.out_mode < OUT_BF16 || c.out_mode > OUT_F16) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode");
     if (c.rope_cos && (c.out_mode == OUT_F32_ACC || c.rope_cols % 64))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad rope");
+    if (c.act == ACT_GLU && (c.N % 256 || (c.out_mode != OUT_F16 && c.out_mode != OUT_BF16) || c.bias || c.rm_g > 0 ||
+                             c.rope_cos || c.dtype == E_F32))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: gated pairs need N % 256 == 0, 16-bit operands and output");
     const bool small_n = c.N <= 128;
     // Large 16-bit products run on CTA pairs (2-SM MMA, 256 x 256 tiles): each SM then streams half
     // of W's tile instead of all of it.

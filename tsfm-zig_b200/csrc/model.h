@@ -64,6 +64,7 @@ struct TsDev {
         Attn attns[2];
         float *mlp_norm = nullptr;
         DLin w12, w3;
+        bool glu = false;  // w12 rows interleaved in 128-row [gate | up] blocks for the fused epilogue
     };
     std::vector<Layer> layers;
     int64_t max_qkv_cols = 0;

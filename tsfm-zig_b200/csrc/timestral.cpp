@@ -355,8 +355,10 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
             TSFM_TRY(op_linear(r, s, a.o, o16, rows, d, x, d, OUT_F32_ACC, 0));
         }
         TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps));
-        TSFM_TRY(op_linear(r, s, L.w12, xn, rows, d, h16, 2 * hid, A16, 0));
-        {
+        if (L.glu) {
+            TSFM_TRY(op_linear(r, s, L.w12, xn, rows, d, a16, hid, A16, ACT_GLU));
+        } else {
+            TSFM_TRY(op_linear(r, s, L.w12, xn, rows, d, h16, 2 * hid, A16, 0));
             LaunchScope ls(r, s, K_OTHER, (double)rows * hid * 6);
             TSFM_TRY(launch_ts_swiglu(h16, a16, rows, hid, w.act, s));
         }
@@ -508,7 +510,20 @@ Status ts_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, 
         const tsfm_tensor *t12, *t3;
         TSFM_TRY(t.raw(strf("transformer.layers.%d.mlp.w12.weight", li), 2 * hid * d, &t12));
         TSFM_TRY(t.raw(strf("transformer.layers.%d.mlp.w3.weight", li), d * hid, &t3));
-        TSFM_TRY(upload_lin_raw(r, {t12}, nullptr, 2 * hid, d, act, L.w12));
+        if (hid % 128 == 0) {
+            // [gate | up] per 128-unit block, so one GEMM tile holds matching gate and up columns
+            // and its epilogue writes gate * silu(up) (MlpAct.run, timestral/model.zig:159-165).
+            std::vector<int32_t> map((size_t)(2 * hid));
+            for (int64_t blk = 0; blk < hid / 128; ++blk)
+                for (int64_t i = 0; i < 128; ++i) {
+                    map[(size_t)(blk * 256 + i)] = (int32_t)(blk * 128 + i);
+                    map[(size_t)(blk * 256 + 128 + i)] = (int32_t)(hid + blk * 128 + i);
+                }
+            TSFM_TRY(upload_lin_raw(r, {t12}, &map, 2 * hid, d, act, L.w12));
+            L.glu = true;
+        } else {
+            TSFM_TRY(upload_lin_raw(r, {t12}, nullptr, 2 * hid, d, act, L.w12));
+        }
         TSFM_TRY(upload_lin_raw(r, {t3}, nullptr, d, hid, act, L.w3));
         w.layers.push_back(L);
     }
