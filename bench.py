@@ -48,10 +48,11 @@ def parse_args():
     ap.add_argument("--series", type=int, default=SERIES_PER_GPU)
     ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
     ap.add_argument("--workload", default="chronos2",
-                    choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep"],
+                    choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv"],
                     help="chronos2 is the headline; bolt-*/timestral are BASELINE.json's other configs, timed "
                          "through the host entry points (copies included); sweep is its Chronos-2 throughput sweep "
-                         "(batch x context, one JSON line per point)")
+                         "(batch x context, one JSON line per point); csv renders the CLI's CSV output of an "
+                         "8192-series, horizon-1024, 21-level forecast")
     return ap.parse_args()
 
 
@@ -320,6 +321,103 @@ def run_family_workload(a):
     model.close()
 
 
+def forecast_like_values(series, horizon, q, seed):
+    """Quantile forecasts shaped like the models' output: a per-series level and scale, a random
+    walk over the horizon and increasing quantile offsets, in float32 (full-precision digits)."""
+    rng = np.random.default_rng(seed)
+    level = rng.lognormal(3.0, 2.0, size=(series, 1, 1, 1))
+    walk = np.cumsum(rng.standard_normal((series, 1, horizon, 1)), axis=2) * 0.05
+    offs = np.sort(rng.standard_normal((series, 1, horizon, q)), axis=3)
+    return (level * (1.0 + walk + 0.1 * offs)).astype(np.float32)
+
+
+def run_csv(a):
+    """The CLI's CSV output (writeCsv, src/main.zig:181-198) of an 8192-series, horizon-1024,
+    21-level forecast on one GPU: 176 M numbers. value: series/s with the forecast resident in HBM
+    (tsfm_csv_format_device, CUDA events); e2e: series/s through tsfm_csv_format from pinned host
+    values into a pinned host text buffer (copies both ways inside the timed region)."""
+    import ctypes
+    import torch
+    import tsfm_b200 as tb
+    from tsfm_b200 import csv
+    series, horizon, q = 8192, 1024, 21
+    levels = np.array([0.01, 0.05] + [round(0.05 * i, 2) for i in range(2, 19)] + [0.95, 0.99], np.float64)
+    assert levels.size == q
+    vals = forecast_like_values(series, horizon, q, seed=77)
+    stream = torch.cuda.current_stream()
+    dv = torch.from_numpy(vals).cuda()
+    need = ctypes.c_size_t(0)
+    tb.lib.tsfm_csv_format_device(dv.data_ptr(), series, 1, horizon, levels.ctypes.data, q, None, 0,
+                                  ctypes.byref(need), stream.cuda_stream)
+    text_bytes = need.value
+    dout = torch.empty(text_bytes, dtype=torch.uint8, device="cuda")
+    run_dev = lambda: csv.format_csv_device(dv.data_ptr(), series, 1, horizon, levels, dout.data_ptr(),
+                                            text_bytes, stream.cuda_stream)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    for _ in range(max(3, a.warmup)):
+        run_dev()
+    torch.cuda.synchronize()
+    steps = max(3, a.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    csv.profile(True)
+    total = 0.0
+    with Clocks(0) as clocks:
+        time.sleep(0.3)
+        clocks.mark_begin()
+        for _ in range(steps):
+            flush.zero_()
+            e0.record(stream)
+            run_dev()
+            e1.record(stream)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        clocks.mark_end()
+    kern = {k: csv.profile_read(k) for k in ("length", "scan", "text")}
+    csv.profile(False)
+    ms = total / steps
+    # e2e: pinned host values in, pinned host text out.
+    hv = torch.from_numpy(vals).pin_memory()
+    hout = torch.empty(text_bytes, dtype=torch.uint8).pin_memory()
+    n = ctypes.c_size_t(0)
+    run_host = lambda: tb.check(tb.lib.tsfm_csv_format(hv.data_ptr(), series, 1, horizon, levels.ctypes.data, q, 0,
+                                                       hout.data_ptr(), text_bytes, ctypes.byref(n)))
+    for _ in range(2):
+        run_host()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run_host()
+    e2e_ms = (time.perf_counter() - t0) / steps * 1e3
+    clk = clocks.summary()
+    # Roofline of the text kernel: it reads the values once and writes the text once.
+    hbm_burst = peaks()[2]
+    text_ms = kern["text"]["ms"] / max(1, kern["text"]["launches"])
+    alg = vals.nbytes + text_bytes
+    achieved = alg / (text_ms / 1e3) / 1e9
+    # CPU baseline: the oracle's writeCsv restatement (all host threads) on 256 series.
+    from oracle import binding as ob
+    sample = vals[:256]
+    t0 = time.perf_counter()
+    ob.csv_format(sample, levels)
+    cpu_dt = time.perf_counter() - t0
+    line = {"metric": "CSV output series/sec (writeCsv of an 8192-series H1024 21-level forecast)",
+            "value": series / (ms / 1e3), "unit": "series/s", "n_gpus": 1, "steps": steps, "warmup": a.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (seeded quantile forecasts, float32)",
+            "config": {"workload": "csv", "series": series, "horizon": horizon, "levels": q,
+                       "text_bytes": text_bytes, "l2": "flushed between steps (256 MiB write)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_burst, "unit": "GB/s",
+                         "frac": achieved / hbm_burst, "traffic": None, "kernel": "csv_write_kernel",
+                         "algorithmic_bytes": alg},
+            "kernels": kern,
+            "cpu_baseline": {"value": 256 / cpu_dt, "unit": "series/s", "cores": ob.get_threads(), "kind": "port",
+                             "sample": "256 series x 1024 steps x 21 levels (oracle writeCsv restatement)"},
+            "e2e": {"value": series / (e2e_ms / 1e3), "unit": "series/s", "h2d_bytes_per_step": int(vals.nbytes),
+                    "d2h_bytes_per_step": int(text_bytes)},
+            "gpu_launches": sum(v["launches"] for v in kern.values()) // steps,
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -329,7 +427,7 @@ def main():
         return run_reference(a, rank)
     if a.workload != "chronos2":
         if rank == 0:
-            run_sweep(a) if a.workload == "sweep" else run_family_workload(a)
+            {"sweep": run_sweep, "csv": run_csv}.get(a.workload, run_family_workload)(a)
         return
 
     import torch

@@ -56,7 +56,9 @@ typedef enum tsfm_status {
     TSFM_ERR_DEGENERATE_INPUT = 12,  /* error.DegenerateInput (timestral/forecaster.zig:419) */
     TSFM_ERR_ASYMMETRIC_QUANTILES = 13, /* error.AsymmetricQuantiles (timestral/forecaster.zig:110) */
     TSFM_ERR_COVARIATES_UNSUPPORTED = 14, /* error.CovariatesUnsupported / KnownCovariatesUnsupported */
-    TSFM_ERR_NO_DEVICE = 15          /* no CUDA device, or the device ordinal is out of range */
+    TSFM_ERR_NO_DEVICE = 15,         /* no CUDA device, or the device ordinal is out of range */
+    TSFM_ERR_BUFFER_TOO_SMALL = 16,  /* an output buffer is shorter than the result (the needed size is returned) */
+    TSFM_ERR_IO = 17                 /* writing to a file descriptor failed */
 } tsfm_status;
 
 typedef enum tsfm_family {
@@ -289,6 +291,37 @@ int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64
  * f32 (out_dtype). Replaces nn.rmsNorm (core/nn.zig:367-396). */
 int32_t tsfm_kernel_rmsnorm(const float *x, const float *scale, void *out, int32_t out_dtype,
                             int64_t rows, int64_t dim, float eps, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * CSV output of a forecast. Replaces the CLI's writeCsv (src/main.zig:181-198): a header
+ * "series,variate,step" followed by ",q<level>" per quantile level, then one line per
+ * (series, variate, step) of values (series, variates, horizon, num_levels) f32 row-major:
+ * "s,v,step+1" followed by ",<value>" per level, each line ended by '\n'. Numbers are printed as
+ * Zig's "{d}": integers in decimal, floats in decimal notation (no exponent) with the shortest
+ * digits that read back to the same value (f32 values, f64 levels); "nan", "inf", "-inf", "-0"
+ * as Zig prints them. The text is rendered on the GPU.
+ *
+ * tsfm_csv_format: values in host memory; the text goes to out[0, capacity). *length receives
+ * the text's byte count; when it exceeds capacity (out may then be NULL with capacity 0) the
+ * call returns TSFM_ERR_BUFFER_TOO_SMALL and writes nothing past the header.
+ * tsfm_csv_write: values in host memory; the text is written to the file descriptor fd (the
+ * reference writes stdout), *length = bytes written.
+ * tsfm_csv_format_device: values and out in the current device's memory, ordered on stream;
+ * returns after the text is complete. At most 500 levels. */
+int32_t tsfm_csv_format(const float *values, size_t series, size_t variates, size_t horizon,
+                        const double *levels, size_t num_levels, int32_t device, char *out,
+                        size_t capacity, size_t *length);
+int32_t tsfm_csv_write(const float *values, size_t series, size_t variates, size_t horizon,
+                       const double *levels, size_t num_levels, int32_t device, int32_t fd,
+                       size_t *length);
+int32_t tsfm_csv_format_device(const float *values, size_t series, size_t variates, size_t horizon,
+                               const double *levels, size_t num_levels, char *out, size_t capacity,
+                               size_t *length, void *stream);
+
+/* Per-kernel device time of the CSV kernels on a device ("length", "scan", "text"): launches and
+ * milliseconds since the last enable (CUDA events around each launch while enabled). */
+int32_t tsfm_csv_profile_enable(int32_t device, int32_t enable);
+int32_t tsfm_csv_profile_read(int32_t device, const char *kernel, uint64_t *launches, double *ms);
 
 #ifdef __cplusplus
 }

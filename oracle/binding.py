@@ -35,6 +35,11 @@ def _load():
                                       ctypes.POINTER(SZ)]),
         "oracle_linear": (I32, [P, P, P, P, SZ, SZ, SZ]),
         "oracle_rmsnorm": (I32, [P, P, P, SZ, SZ, F]),
+        "oracle_f32_digits_batch": (None, [P, SZ, P, P]),
+        "oracle_f32_digits_search_batch": (None, [P, SZ, P, P]),
+        "oracle_f32_text": (SZ, [F, ctypes.c_char_p]),
+        "oracle_f64_text": (SZ, [ctypes.c_double, ctypes.c_char_p]),
+        "oracle_csv_format": (SZ, [P, SZ, SZ, SZ, P, SZ, P, SZ]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -101,3 +106,43 @@ def set_threads(n):
 
 def get_threads():
     return lib.oracle_get_threads()
+
+
+# CSV output (oracle_csv.cpp).
+def f32_digits(x, search=False):
+    """(digits, exponent) arrays of the shortest round-trip decimal of each float32 magnitude:
+    Ryu, or (search=True) the printf / strtof digit-count search."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    e = np.empty(x.size, dtype=np.int32)
+    if search:
+        d = np.empty(x.size, dtype=np.uint64)
+        lib.oracle_f32_digits_search_batch(x.ctypes.data, x.size, d.ctypes.data, e.ctypes.data)
+    else:
+        d = np.empty(x.size, dtype=np.uint32)
+        lib.oracle_f32_digits_batch(x.ctypes.data, x.size, d.ctypes.data, e.ctypes.data)
+    return d.astype(np.uint64), e
+
+
+def f32_text(x):
+    buf = ctypes.create_string_buffer(64)
+    n = lib.oracle_f32_text(float(np.float32(x)), buf)
+    return buf.raw[:n].decode()
+
+
+def f64_text(x):
+    buf = ctypes.create_string_buffer(64)
+    n = lib.oracle_f64_text(float(x), buf)
+    return buf.raw[:n].decode()
+
+
+def csv_format(values, levels):
+    """writeCsv text (bytes) of a (series, variates, horizon, levels) forecast."""
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    if v.ndim == 3:
+        v = v[:, None]
+    lv = np.ascontiguousarray(levels, dtype=np.float64)
+    s, nv, h, q = v.shape
+    n = lib.oracle_csv_format(v.ctypes.data, s, nv, h, lv.ctypes.data, q, None, 0)
+    out = np.empty(max(n, 1), dtype=np.uint8)
+    lib.oracle_csv_format(v.ctypes.data, s, nv, h, lv.ctypes.data, q, out.ctypes.data, out.size)
+    return out[:n].tobytes()

@@ -65,6 +65,17 @@ int32_t oracle_linear(const float *x, const float *w, const float *bias, float *
 int32_t oracle_rmsnorm(const float *x, const float *scale, float *out, size_t rows, size_t dim,
                        float eps);
 
+/* CSV output (oracle_csv.cpp): writeCsv of src/main.zig:181-198 and Zig's "{d}" rendering.
+ * oracle_csv_format returns the text's length and fills out when capacity allows. */
+void oracle_f32_digits(float x, uint32_t *digits, int32_t *exponent);
+void oracle_f32_digits_search(float x, uint64_t *digits, int32_t *exponent);
+void oracle_f32_digits_batch(const float *x, size_t n, uint32_t *digits, int32_t *exponent);
+void oracle_f32_digits_search_batch(const float *x, size_t n, uint64_t *digits, int32_t *exponent);
+size_t oracle_f32_text(float x, char *out);
+size_t oracle_f64_text(double x, char *out);
+size_t oracle_csv_format(const float *values, size_t series, size_t variates, size_t horizon,
+                         const double *levels, size_t num_levels, char *out, size_t capacity);
+
 #ifdef __cplusplus
 }
 #endif

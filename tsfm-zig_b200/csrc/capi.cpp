@@ -240,6 +240,8 @@ const char *tsfm_status_string(int32_t s) {
         case TSFM_ERR_ASYMMETRIC_QUANTILES: return "asymmetric quantiles";
         case TSFM_ERR_COVARIATES_UNSUPPORTED: return "covariates unsupported";
         case TSFM_ERR_NO_DEVICE: return "no device";
+        case TSFM_ERR_BUFFER_TOO_SMALL: return "buffer too small";
+        case TSFM_ERR_IO: return "I/O error";
         default: return "unknown status";
     }
 }

@@ -71,7 +71,6 @@ struct TsDev {
     int act = E_F16;
     // Per-forecast roles of one series' rows (0 target, 1 past covariate, 2 known covariate).
     const int8_t *roles = nullptr;
-    std::vector<int8_t> roles_host;
 };
 
 struct tsfm_model_impl {

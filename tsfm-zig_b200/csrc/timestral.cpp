@@ -275,21 +275,9 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
         TSFM_TRY(launch_ts_rope(first_obs, k.groups, sl, ne, l, w.inv_freq, 32, cs, sn, s));
     }
     {
-        std::vector<uint8_t> bd(R);
-        std::vector<int64_t> hr(nt * k.h), tr(nt);
-        int64_t oi = 0;
-        for (int64_t row = 0; row < R; ++row) {
-            const int role = w.roles_host[row % k.vall];
-            bd[row] = k.cov && role == 2;
-            if (role != 0) continue;
-            tr[oi] = row;
-            for (int64_t j = 0; j < k.h; ++j) hr[oi * k.h + j] = row * sl + ne + j;
-            ++oi;
-        }
-        TSFM_CUDA(cudaMemcpyAsync(bidir, bd.data(), R, cudaMemcpyHostToDevice, s), "timestral: flags");
-        TSFM_CUDA(cudaMemcpyAsync(head_rows, hr.data(), hr.size() * 8, cudaMemcpyHostToDevice, s), "timestral: rows");
-        TSFM_CUDA(cudaMemcpyAsync(target_row, tr.data(), tr.size() * 8, cudaMemcpyHostToDevice, s), "timestral: rows");
-        TSFM_CUDA(cudaStreamSynchronize(s), "timestral: flags");  // the host vectors go out of scope
+        LaunchScope ls(r, s, K_OTHER, (double)R + (double)nt * (k.h + 1) * 8);
+        TSFM_TRY(launch_ts_rows(w.roles, R, (int)k.vall, (int)k.v, sl, ne, (int)k.h, k.cov, bidir, head_rows,
+                                target_row, s));
     }
     // 4. transformer (runTransformer, timestral/model.zig:434-482).
     for (const TsDev::Layer &L : w.layers) {
@@ -663,7 +651,6 @@ Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inpu
     // Roles of one series' rows: targets, past-only, known-future.
     std::vector<int8_t> roles(vall);
     for (size_t i = 0; i < vall; ++i) roles[i] = i < v ? 0 : (i < v + n_past ? 1 : 2);
-    w.roles_host.assign(roles.begin(), roles.end());
     const bool covw = vall > v;
     const int64_t nt = groups * (int64_t)v;
     const int med = median_index(c);

@@ -155,6 +155,22 @@ __global__ void ts_rope_kernel(const int *first_obs, int64_t groups, int64_t sl,
     }
 }
 
+// Per-block row maps (model.zig:379-410, 600): the bidirectional flag of every row (known-future
+// rows of a covariate window), and for each target row (the first v rows of each group, in order)
+// its index and the indices of its h decoder tokens in the (rows * sl) token matrix.
+__global__ void ts_rows_kernel(const int8_t *roles, int64_t rows, int vall, int v, int64_t sl, int64_t ne, int h,
+                               bool cov, uint8_t *bidir, int64_t *head_rows, int64_t *target_row) {
+    for (int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; row < rows; row += (int64_t)gridDim.x * blockDim.x) {
+        const int j = (int)(row % vall);
+        const int role = roles[j];
+        bidir[row] = cov && role == 2;
+        if (j >= v) continue;
+        const int64_t oi = row / vall * v + j;
+        target_row[oi] = row;
+        for (int jj = 0; jj < h; ++jj) head_rows[oi * h + jj] = row * sl + ne + jj;
+    }
+}
+
 // o = o * sigmoid(g) (nn.mulSigmoid, core/nn.zig:423-433).
 __global__ void ts_gate_kernel(void *o, int64_t ldo, const void *g, int64_t ldg, int64_t rows, int64_t d, int dtype) {
     const int64_t total = rows * d;
@@ -641,6 +657,14 @@ Status launch_ts_rope(const int *first_obs, int64_t groups, int64_t sl, int64_t 
                       int half, float *cs, float *sn, cudaStream_t s) {
     ts_rope_kernel<<<grid_for(groups * sl * half, 256), 256, 0, s>>>(first_obs, groups, sl, ne, l, inv_freq, half, cs, sn);
     TSFM_CUDA(cudaGetLastError(), "timestral rope: launch");
+    return Status::ok();
+}
+
+Status launch_ts_rows(const int8_t *roles, int64_t rows, int vall, int v, int64_t sl, int64_t ne, int h, bool cov,
+                      uint8_t *bidir, int64_t *head_rows, int64_t *target_row, cudaStream_t s) {
+    if (rows <= 0) return Status::ok();
+    ts_rows_kernel<<<grid_for(rows, 256), 256, 0, s>>>(roles, rows, vall, v, sl, ne, h, cov, bidir, head_rows, target_row);
+    TSFM_CUDA(cudaGetLastError(), "timestral rows: launch");
     return Status::ok();
 }
 

@@ -31,6 +31,10 @@ Status launch_ts_stats(const TsStatsCall &c, float *feats, cudaStream_t s);
 
 Status launch_ts_rope(const int *first_obs, int64_t groups, int64_t sl, int64_t ne, int64_t l, const float *inv_freq,
                       int half, float *cs, float *sn, cudaStream_t s);
+// Row flags and head / target row indices of one block; target rows are the first v of every
+// group of vall rows (role 0).
+Status launch_ts_rows(const int8_t *roles, int64_t rows, int vall, int v, int64_t sl, int64_t ne, int h, bool cov,
+                      uint8_t *bidir, int64_t *head_rows, int64_t *target_row, cudaStream_t s);
 Status launch_ts_gate(void *o, int64_t ldo, const void *g, int64_t ldg, int64_t rows, int64_t d, int dtype, cudaStream_t s);
 Status launch_ts_swiglu(const void *h, void *a, int64_t rows, int64_t hid, int dtype, cudaStream_t s);
 

@@ -15,7 +15,7 @@ STATUS_NAMES = {
     0: "OK", 1: "INVALID_ARGUMENT", 2: "INVALID_CONFIG", 3: "MISSING_TENSOR", 4: "SHAPE_MISMATCH",
     5: "UNSUPPORTED_DTYPE", 6: "CUDA", 7: "OUT_OF_MEMORY", 8: "DEVICE_TIMEOUT", 9: "EMPTY_INPUT",
     10: "HORIZON_TOO_LONG", 11: "UNSUPPORTED", 12: "DEGENERATE_INPUT", 13: "ASYMMETRIC_QUANTILES",
-    14: "COVARIATES_UNSUPPORTED", 15: "NO_DEVICE",
+    14: "COVARIATES_UNSUPPORTED", 15: "NO_DEVICE", 16: "BUFFER_TOO_SMALL", 17: "IO",
 }
 FAMILY = {"chronos2": 1, "chronos_bolt": 2, "timestral": 3}
 DTYPE = {"F32": 0, "F16": 1, "BF16": 2}
@@ -110,6 +110,12 @@ SIGNATURES = {
                                   _I64, _P]),
     "tsfm_kernel_attention": (_I32, [_P, _P, _P, _I64, _P, _I64, _P, _P, _I32, _I32, _I32, _F, _I32, _I32, _P]),
     "tsfm_kernel_rmsnorm": (_I32, [_P, _P, _P, _I32, _I64, _I64, _F, _P]),
+    "tsfm_csv_format": (_I32, [_P, _SZ, _SZ, _SZ, _P, _SZ, _I32, _P, _SZ, ctypes.POINTER(_SZ)]),
+    "tsfm_csv_write": (_I32, [_P, _SZ, _SZ, _SZ, _P, _SZ, _I32, _I32, ctypes.POINTER(_SZ)]),
+    "tsfm_csv_format_device": (_I32, [_P, _SZ, _SZ, _SZ, _P, _SZ, _P, _SZ, ctypes.POINTER(_SZ), _P]),
+    "tsfm_csv_profile_enable": (_I32, [_I32, _I32]),
+    "tsfm_csv_profile_read": (_I32, [_I32, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64),
+                                     ctypes.POINTER(ctypes.c_double)]),
 }
 
 
