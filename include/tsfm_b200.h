@@ -307,7 +307,7 @@ int32_t tsfm_kernel_rmsnorm(const float *x, const float *scale, void *out, int32
  * tsfm_csv_write: values in host memory; the text is written to the file descriptor fd (the
  * reference writes stdout), *length = bytes written.
  * tsfm_csv_format_device: values and out in the current device's memory, ordered on stream;
- * returns after the text is complete. At most 500 levels. */
+ * returns after the text is complete. At most 1000 levels. */
 int32_t tsfm_csv_format(const float *values, size_t series, size_t variates, size_t horizon,
                         const double *levels, size_t num_levels, int32_t device, char *out,
                         size_t capacity, size_t *length);
@@ -318,7 +318,7 @@ int32_t tsfm_csv_format_device(const float *values, size_t series, size_t variat
                                const double *levels, size_t num_levels, char *out, size_t capacity,
                                size_t *length, void *stream);
 
-/* Per-kernel device time of the CSV kernels on a device ("length", "scan", "text"): launches and
+/* Per-kernel device time of the CSV kernels on a device ("describe", "scan", "text"): launches and
  * milliseconds since the last enable (CUDA events around each launch while enabled). */
 int32_t tsfm_csv_profile_enable(int32_t device, int32_t enable);
 int32_t tsfm_csv_profile_read(int32_t device, const char *kernel, uint64_t *launches, double *ms);

@@ -113,7 +113,7 @@ def test_capi_csv_argument_checks_need_no_device():
     assert tb.lib.tsfm_csv_format(None, 1, 1, 1, lv.ctypes.data, 1, 0, None, 0, ctypes.byref(n)) == 1
     assert tb.lib.tsfm_csv_write(None, 1, 1, 1, lv.ctypes.data, 1, 0, -1, ctypes.byref(n)) == 1
     # More levels than the kernels' line buffers hold.
-    many = np.full(501, 0.5)
-    vals = np.zeros(501, np.float32)
-    assert tb.lib.tsfm_csv_format(vals.ctypes.data, 1, 1, 1, many.ctypes.data, 501, 0, None, 0,
+    many = np.full(1001, 0.5)
+    vals = np.zeros(1001, np.float32)
+    assert tb.lib.tsfm_csv_format(vals.ctypes.data, 1, 1, 1, many.ctypes.data, 1001, 0, None, 0,
                                   ctypes.byref(n)) == 11

@@ -39,7 +39,8 @@ def levels_for(q):
 
 
 @pytest.mark.parametrize("shape", [(1, 1, 1, 1), (3, 2, 17, 9), (5, 1, 64, 21), (2, 3, 5, 40), (7, 1, 33, 32),
-                                   (1, 1, 100, 65), (0, 1, 16, 9), (4, 4, 1, 3)])
+                                   (1, 1, 100, 65), (0, 1, 16, 9), (4, 4, 1, 3), (2, 1, 9, 200), (1, 1, 3, 1000),
+                                   (1, 1, 40, 0)])
 def test_format_matches_oracle(csvmod, shape):
     v = forecast_values(shape, seed=sum(shape))
     lv = levels_for(shape[3])

@@ -5,15 +5,21 @@
 // line ended by '\n'. Levels are f64 and values f32, both printed as Zig's "{d}" (decimal
 // notation, shortest round-trip digits; csv_digits.cuh).
 //
-// Three kernels per chunk of lines: (1) one warp per line sums the text lengths of the line's
-// numbers (block sums of 32 lines); (2) one block scans the block sums into byte offsets; (3) one
-// warp per line renders the line into a shared-memory buffer and copies it to its offset with
-// consecutive byte stores. The digit generation runs twice (lengths, then text) instead of
-// keeping 8 bytes per value between the passes: it is cheaper than the HBM round trip.
+// Three kernels per chunk of lines, each block owning `lpb` consecutive lines:
+//   describe  the shortest digits of every value (Ryu), packed in 8 bytes per value, and the
+//             block's text length;
+//   scan      one block turns the block lengths into byte offsets (and the chunk's total);
+//   text      the block renders its lines into shared memory (each thread a contiguous run of
+//             prefixes, values and newlines, placed by a block-wide scan of their lengths) and
+//             copies them out with 16-byte stores aligned to the destination.
+// The host entry points stream chunks through three CUDA streams: host-to-device copies of
+// the next chunk's values, the kernels, and device-to-host copies of the previous chunk's text
+// overlap one another.
 #include <cuda_runtime.h>
 #include <errno.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -32,21 +38,44 @@ namespace {
 
 __constant__ csv::Pow5Tables c_pow5;
 
-constexpr int kWarps = 8, kLinesPerWarp = 4, kLinesPerBlock = kWarps * kLinesPerWarp;
-constexpr int kPrefixMax = 3 * 20 + 3;  // "s,v,step\n" with 20-digit integers
+constexpr int kThreads = 256;
+constexpr int kPrefixMax = 3 * 20 + 2;  // "s,v,step" with 20-digit integers
 constexpr int kValueMax = 50;           // ',' + at most 49 bytes of f32 text ("-0.000...0ddddddddd")
+constexpr int kMaxLevels = 1000;
+
+// Lines per block: about 768 numbers per block, at most 32 lines.
+inline int lines_per_block(int q) { return std::min(32, std::max(1, 768 / (q + 2))); }
 
 struct Lines {
     const float *values;  // (lines, q) f32 of this chunk
     int64_t first;        // global index of the chunk's first line
     int64_t lines;
     int64_t variates, horizon;
-    int q;
+    int q, lpb;
 };
+
+// A value's text description in 8 bytes: digits (30 bits) | exponent + 64 (7) | digit count (4)
+// | text length (6) | kind (2) | sign (1).
+__device__ __forceinline__ uint64_t pack(const csv::F32Text &f) {
+    return (uint64_t)f.digits | ((uint64_t)(f.exponent + 64) << 30) | ((uint64_t)f.ndigits << 37) |
+           ((uint64_t)f.len << 41) | ((uint64_t)f.kind << 47) | ((uint64_t)(f.neg ? 1 : 0) << 49);
+}
+
+__device__ __forceinline__ csv::F32Text unpack(uint64_t p) {
+    csv::F32Text f;
+    f.digits = (uint32_t)(p & 0x3fffffffu);
+    f.exponent = (int32_t)((p >> 30) & 0x7f) - 64;
+    f.ndigits = (int8_t)((p >> 37) & 0xf);
+    f.len = (int16_t)((p >> 41) & 0x3f);
+    f.kind = (int8_t)((p >> 47) & 0x3);
+    f.neg = ((p >> 49) & 1) != 0;
+    return f;
+}
 
 struct Prefix {
     uint64_t s, v, step;
-    int ls, lv, lst, len;
+    int ls, lv, lst;
+    __device__ int len() const { return ls + lv + lst + 2; }  // "s,v,step"
 };
 
 __device__ __forceinline__ Prefix prefix_of(int64_t line, int64_t variates, int64_t horizon) {
@@ -57,48 +86,68 @@ __device__ __forceinline__ Prefix prefix_of(int64_t line, int64_t variates, int6
     p.ls = csv::u64_length(p.s);
     p.lv = csv::u64_length(p.v);
     p.lst = csv::u64_length(p.step);
-    p.len = p.ls + p.lv + p.lst + 3;  // two commas and the newline
     return p;
 }
 
-__device__ __forceinline__ void load_tables(csv::Pow5Tables *t) {
-    const uint64_t *src = reinterpret_cast<const uint64_t *>(&c_pow5);
-    uint64_t *dst = reinterpret_cast<uint64_t *>(t);
-    for (int i = threadIdx.x; i < (int)(sizeof(csv::Pow5Tables) / 8); i += blockDim.x) dst[i] = src[i];
+__device__ __forceinline__ void emit_prefix(const Prefix &p, char *o) {
+    csv::emit_u64(p.s, p.ls, o);
+    o[p.ls] = ',';
+    csv::emit_u64(p.v, p.lv, o + p.ls + 1);
+    o[p.ls + 1 + p.lv] = ',';
+    csv::emit_u64(p.step, p.lst, o + p.ls + p.lv + 2);
 }
 
-// (1) line lengths and per-block sums.
-__global__ void __launch_bounds__(kWarps * 32) csv_len_kernel(Lines c, uint32_t *line_len, uint32_t *block_sum) {
-    __shared__ csv::Pow5Tables tab;
-    __shared__ uint32_t wsum[kWarps];
-    load_tables(&tab);
+// Block-wide exclusive scan of one value per thread; *total receives the block's sum.
+__device__ __forceinline__ uint32_t block_scan(uint32_t v, uint32_t *wsum, uint32_t *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t base = (int64_t)blockIdx.x * kLinesPerBlock + warp * kLinesPerWarp;
-    const uint32_t *bits = reinterpret_cast<const uint32_t *>(c.values);
-    uint32_t mine = 0;
-    for (int li = 0; li < kLinesPerWarp; ++li) {
-        const int64_t line = base + li;
-        if (line >= c.lines) break;
-        uint32_t len = 0;
-        for (int j = lane; j < c.q; j += 32) len += 1 + (uint32_t)csv::describe(bits[line * c.q + j], tab).len;
-        for (int o = 16; o > 0; o >>= 1) len += __shfl_xor_sync(0xffffffffu, len, o);
-        if (lane == 0) {
-            len += (uint32_t)prefix_of(c.first + line, c.variates, c.horizon).len;
-            line_len[line] = len;
-            mine += len;
+    if (warp == 0) {
+        uint32_t w = lane < kThreads / 32 ? wsum[lane] : 0;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
         }
+        if (lane < kThreads / 32) wsum[lane] = w;
     }
-    if (lane == 0) wsum[warp] = mine;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        uint32_t t = 0;
-        for (int w = 0; w < kWarps; ++w) t += wsum[w];
-        block_sum[blockIdx.x] = t;
-    }
+    *total = wsum[kThreads / 32 - 1];
+    return x - v + (warp ? wsum[warp - 1] : 0);
 }
 
-// (2) exclusive scan of the block sums (one block of 1024 threads) and the chunk's byte total.
+// (1) digits of every value, packed; the text length of each block of lines.
+__global__ void __launch_bounds__(kThreads) csv_describe_kernel(Lines c, uint64_t *packed, uint32_t *block_sum) {
+    __shared__ csv::Pow5Tables tab;
+    __shared__ uint32_t wsum[kThreads / 32];
+    {
+        const uint64_t *src = reinterpret_cast<const uint64_t *>(&c_pow5);
+        uint64_t *dst = reinterpret_cast<uint64_t *>(&tab);
+        for (int i = threadIdx.x; i < (int)(sizeof(csv::Pow5Tables) / 8); i += kThreads) dst[i] = src[i];
+    }
+    __syncthreads();
+    const int64_t l0 = (int64_t)blockIdx.x * c.lpb;
+    const int nl = (int)min((int64_t)c.lpb, c.lines - l0);
+    const int n = nl * c.q;
+    const int64_t base = l0 * c.q;
+    const uint32_t *bits = reinterpret_cast<const uint32_t *>(c.values);
+    uint32_t acc = 0;
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+        const csv::F32Text f = csv::describe(bits[base + i], tab);
+        packed[base + i] = pack(f);
+        acc += 1 + (uint32_t)f.len;
+    }
+    if (threadIdx.x < nl) acc += (uint32_t)prefix_of(c.first + l0 + threadIdx.x, c.variates, c.horizon).len() + 1;
+    uint32_t total;
+    block_scan(acc, wsum, &total);
+    if (threadIdx.x == 0) block_sum[blockIdx.x] = total;
+}
+
+// (2) exclusive scan of the block lengths (one block of 1024 threads) and the chunk's total.
 __global__ void __launch_bounds__(1024) csv_scan_kernel(const uint32_t *in, int64_t n, uint64_t *excl, uint64_t *total) {
     __shared__ uint64_t wtot[32];
     __shared__ uint64_t carry;
@@ -133,68 +182,72 @@ __global__ void __launch_bounds__(1024) csv_scan_kernel(const uint32_t *in, int6
     if (threadIdx.x == 0) *total = carry;
 }
 
-// (3) text. Dynamic shared memory: the tables, 32 line offsets, one line buffer per warp.
-__global__ void __launch_bounds__(kWarps * 32) csv_write_kernel(Lines c, const uint32_t *line_len,
-                                                               const uint64_t *block_off, char *out, int buf_bytes) {
+// Dynamic shared memory of the text kernel: packed values, then the text (16-byte aligned).
+__host__ __device__ inline size_t packed_smem(int q, int lpb) { return ((size_t)lpb * q * 8 + 15) / 16 * 16; }
+__host__ __device__ inline size_t text_smem(int q, int lpb) {
+    return (size_t)lpb * (kPrefixMax + 1 + (size_t)kValueMax * q) + 16;
+}
+
+// (3) the text of each block of lines at its offset.
+__global__ void __launch_bounds__(kThreads) csv_text_kernel(Lines c, const uint64_t *packed, const uint64_t *block_off,
+                                                           char *out) {
     extern __shared__ __align__(16) unsigned char smem[];
-    csv::Pow5Tables &tab = *reinterpret_cast<csv::Pow5Tables *>(smem);
-    uint64_t *line_off = reinterpret_cast<uint64_t *>(smem + sizeof(csv::Pow5Tables));
-    char *bufs = reinterpret_cast<char *>(line_off + kLinesPerBlock);
-    load_tables(&tab);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t first = (int64_t)blockIdx.x * kLinesPerBlock;
-    if (warp == 0) {
-        const int64_t line = first + lane;
-        const uint64_t v = line < c.lines ? line_len[line] : 0;
-        uint64_t x = v;
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
-            if (lane >= o) x += y;
+    __shared__ uint32_t wsum[kThreads / 32];
+    __shared__ uint8_t plen[32];
+    uint64_t *pk = reinterpret_cast<uint64_t *>(smem);
+    char *text = reinterpret_cast<char *>(smem + packed_smem(c.q, c.lpb));
+    const int64_t l0 = (int64_t)blockIdx.x * c.lpb;
+    const int nl = (int)min((int64_t)c.lpb, c.lines - l0);
+    const int n = nl * c.q;
+    const int64_t base = l0 * c.q;
+    for (int i = threadIdx.x; i < n; i += kThreads) pk[i] = packed[base + i];
+    if (threadIdx.x < nl) plen[threadIdx.x] = (uint8_t)prefix_of(c.first + l0 + threadIdx.x, c.variates, c.horizon).len();
+    __syncthreads();
+
+    // Items of a line: its prefix, its q values, its newline. Each thread owns a contiguous run.
+    const int per = c.q + 2, items = nl * per;
+    const int ipt = (items + kThreads - 1) / kThreads;
+    const int k0 = min(items, (int)threadIdx.x * ipt), k1 = min(items, k0 + ipt);
+    uint32_t mine = 0;
+    {
+        int li = k0 / per, r = k0 - li * per;
+        for (int k = k0; k < k1; ++k) {
+            mine += r == 0 ? plen[li] : (r <= c.q ? 1 + (uint32_t)((pk[li * c.q + r - 1] >> 41) & 0x3f) : 1);
+            if (++r == per) r = 0, ++li;
         }
-        line_off[lane] = block_off[blockIdx.x] + x - v;
+    }
+    uint32_t total;
+    const uint32_t off = block_scan(mine, wsum, &total);
+    char *dst = out + block_off[blockIdx.x];
+    const int pad = (int)(reinterpret_cast<uintptr_t>(dst) & 15);
+    {
+        int li = k0 / per, r = k0 - li * per;
+        uint32_t o = (uint32_t)pad + off;
+        for (int k = k0; k < k1; ++k) {
+            if (r == 0) {
+                emit_prefix(prefix_of(c.first + l0 + li, c.variates, c.horizon), text + o);
+                o += plen[li];
+            } else if (r <= c.q) {
+                const csv::F32Text f = unpack(pk[li * c.q + r - 1]);
+                text[o] = ',';
+                csv::emit(f, text + o + 1);
+                o += 1 + (uint32_t)f.len;
+            } else {
+                text[o++] = '\n';
+            }
+            if (++r == per) r = 0, ++li;
+        }
     }
     __syncthreads();
-    char *buf = bufs + (size_t)warp * buf_bytes;
-    const uint32_t *bits = reinterpret_cast<const uint32_t *>(c.values);
-    for (int li = 0; li < kLinesPerWarp; ++li) {
-        const int lb = warp * kLinesPerWarp + li;
-        const int64_t line = first + lb;
-        if (line >= c.lines) break;
-        const Prefix p = prefix_of(c.first + line, c.variates, c.horizon);
-        if (lane == 0) {
-            csv::emit_u64(p.s, p.ls, buf);
-            buf[p.ls] = ',';
-            csv::emit_u64(p.v, p.lv, buf + p.ls + 1);
-            buf[p.ls + 1 + p.lv] = ',';
-            csv::emit_u64(p.step, p.lst, buf + p.ls + p.lv + 2);
+    // text[pad, pad + total) -> dst[0, total), in 16-byte chunks aligned to the destination.
+    char *abase = dst - pad;
+    const int end = pad + (int)total;
+    for (int i = threadIdx.x * 16; i < end; i += kThreads * 16) {
+        if (i >= pad && i + 16 <= end) {
+            *reinterpret_cast<uint4 *>(abase + i) = *reinterpret_cast<const uint4 *>(text + i);
+        } else {
+            for (int b = max(i, pad); b < min(i + 16, end); ++b) abase[b] = text[b];
         }
-        int pos = p.len - 1;
-        for (int j0 = 0; j0 < c.q; j0 += 32) {
-            const int j = j0 + lane;
-            csv::F32Text f{};
-            int n = 0;
-            if (j < c.q) {
-                f = csv::describe(bits[line * c.q + j], tab);
-                n = 1 + f.len;
-            }
-            int x = n;
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, x, o);
-                if (lane >= o) x += y;
-            }
-            if (j < c.q) {
-                char *at = buf + pos + x - n;
-                at[0] = ',';
-                csv::emit(f, at + 1);
-            }
-            pos += __shfl_sync(0xffffffffu, x, 31);
-        }
-        if (lane == 0) buf[pos] = '\n';
-        const int len = pos + 1;
-        __syncwarp();
-        char *dst = out + line_off[lb];
-        for (int i = lane; i < len; i += 32) dst[i] = buf[i];
-        __syncwarp();
     }
 }
 
@@ -287,21 +340,25 @@ std::string header_text(const double *levels, size_t nq) {
     return h;
 }
 
-// Per-device state: a stream, the tables, scratch and staging buffers (grown on demand).
+// Per-device state: streams, events, scratch and staging buffers (grown on demand). Two slots
+// of values and text let consecutive chunks overlap.
 struct Ctx {
     std::mutex mu;
     bool ready = false;
-    cudaStream_t stream = nullptr;
-    float *d_values = nullptr;
-    size_t values_cap = 0;
-    uint32_t *d_line_len = nullptr, *d_block_sum = nullptr;
+    cudaStream_t comp = nullptr, h2d = nullptr, d2h = nullptr;
+    cudaEvent_t ev_in[2] = {}, ev_text[2] = {}, ev_out[2] = {}, ev_total[2] = {};
+    float *d_values[2] = {nullptr, nullptr};
+    size_t values_cap[2] = {0, 0};
+    char *d_text[2] = {nullptr, nullptr};
+    size_t text_cap[2] = {0, 0};
+    uint64_t *d_packed = nullptr;
+    size_t packed_cap = 0;
+    uint32_t *d_block_sum = nullptr;
     uint64_t *d_block_off = nullptr, *d_total = nullptr;
-    size_t lines_cap = 0;
-    char *d_text = nullptr;
-    size_t text_cap = 0;
+    size_t blocks_cap = 0;
     char *h_text[2] = {nullptr, nullptr};
-    size_t h_text_cap = 0;
-    uint64_t *h_total = nullptr;
+    size_t h_text_cap[2] = {0, 0};
+    uint64_t *h_total = nullptr;  // pinned, one per slot
     // Optional per-kernel device time (CUDA events around each launch; read after each sync).
     bool prof = false;
     cudaEvent_t ev[6] = {};
@@ -310,7 +367,7 @@ struct Ctx {
     double ms[3] = {0, 0, 0};
 };
 
-enum { K_LENGTH = 0, K_SCAN = 1, K_TEXT = 2 };
+enum { K_DESCRIBE = 0, K_SCAN = 1, K_TEXT = 2 };
 
 void prof_mark(Ctx &x, int k, bool end, cudaStream_t s) {
     if (!x.prof) return;
@@ -318,7 +375,7 @@ void prof_mark(Ctx &x, int k, bool end, cudaStream_t s) {
     if (end) x.recorded[k] = true;
 }
 
-// After a stream synchronisation: adds the recorded launches' times.
+// After a synchronisation that covers the recorded launches: adds their times.
 void prof_collect(Ctx &x) {
     for (int k = 0; k < 3; ++k) {
         if (!x.recorded[k]) continue;
@@ -345,54 +402,58 @@ Status grow_dev(T **p, size_t *cap, size_t bytes, const char *what) {
     return Status::ok();
 }
 
+size_t max_text_smem() {
+    size_t m = 0;
+    for (int q = 0; q <= kMaxLevels; ++q) {
+        const int l = lines_per_block(q);
+        m = std::max(m, packed_smem(q, l) + text_smem(q, l));
+    }
+    return m;
+}
+
 Status ctx_init(Ctx &x, int device) {
     TSFM_CUDA(cudaSetDevice(device), "csv: cudaSetDevice");
     if (x.ready) return Status::ok();
     const csv::Pow5Tables t = make_tables();
     TSFM_CUDA(cudaMemcpyToSymbol(c_pow5, &t, sizeof t), "csv: tables");
-    TSFM_CUDA(cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking), "csv: stream");
+    TSFM_CUDA(cudaFuncSetAttribute(csv_text_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_text_smem()),
+              "csv: shared memory attribute");
+    for (cudaStream_t *s : {&x.comp, &x.h2d, &x.d2h})
+        TSFM_CUDA(cudaStreamCreateWithFlags(s, cudaStreamNonBlocking), "csv: stream");
+    for (int i = 0; i < 2; ++i)
+        for (cudaEvent_t *e : {&x.ev_in[i], &x.ev_text[i], &x.ev_out[i], &x.ev_total[i]})
+            TSFM_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "csv: event");
     TSFM_CUDA(cudaMallocHost(reinterpret_cast<void **>(&x.h_total), 16), "csv: pinned total");
     x.ready = true;
     return Status::ok();
 }
 
-Status ensure_lines(Ctx &x, int64_t lines) {
-    const size_t cap = (size_t)lines + kLinesPerBlock;
-    if (x.lines_cap >= cap) return Status::ok();
-    size_t dummy = 0;
-    const size_t blocks = cap / kLinesPerBlock + 1;
-    TSFM_TRY(grow_dev(&x.d_line_len, &dummy, cap * 4, "csv: line lengths"));
-    dummy = 0;
-    TSFM_TRY(grow_dev(&x.d_block_sum, &dummy, blocks * 4, "csv: block sums"));
-    dummy = 0;
-    TSFM_TRY(grow_dev(&x.d_block_off, &dummy, blocks * 8, "csv: block offsets"));
-    dummy = 0;
-    TSFM_TRY(grow_dev(&x.d_total, &dummy, 16, "csv: total"));
-    x.lines_cap = cap;
+Status ensure_scratch(Ctx &x, int64_t lines, int q) {
+    const int lpb = lines_per_block(q);
+    const size_t blocks = (size_t)((lines + lpb - 1) / lpb) + 1;
+    if (x.blocks_cap < blocks) {
+        size_t c1 = 0, c2 = 0;
+        TSFM_TRY(grow_dev(&x.d_block_sum, &c1, blocks * 4, "csv: block lengths"));
+        TSFM_TRY(grow_dev(&x.d_block_off, &c2, blocks * 8, "csv: block offsets"));
+        x.blocks_cap = blocks;
+    }
+    size_t ct = x.d_total ? 16 : 0;
+    TSFM_TRY(grow_dev(&x.d_total, &ct, 16, "csv: total"));
+    TSFM_TRY(grow_dev(&x.d_packed, &x.packed_cap, (size_t)lines * q * 8 + 16, "csv: packed digits"));
     return Status::ok();
 }
 
-int line_buffer_bytes(int q) { return (kPrefixMax + kValueMax * q + 1 + 15) / 16 * 16; }
-
-size_t write_smem_bytes(int q) {
-    return sizeof(csv::Pow5Tables) + kLinesPerBlock * 8 + (size_t)kWarps * line_buffer_bytes(q);
-}
-
-// Largest level count whose line buffers fit in shared memory.
-constexpr int kMaxLevels = 500;
-
-// Lengths, offsets and total of `lines` lines at values (device); then the text into out
-// (device) unless out is null. The total lands in x.d_total.
+// describe + scan for one chunk on stream s; the byte total lands in x.d_total.
 Status run_lengths(Ctx &x, const Lines &c, cudaStream_t s) {
-    const int64_t blocks = (c.lines + kLinesPerBlock - 1) / kLinesPerBlock;
+    const int64_t blocks = (c.lines + c.lpb - 1) / c.lpb;
     if (blocks == 0) {
         TSFM_CUDA(cudaMemsetAsync(x.d_total, 0, 8, s), "csv: total");
         return Status::ok();
     }
-    prof_mark(x, K_LENGTH, false, s);
-    csv_len_kernel<<<(unsigned)blocks, kWarps * 32, 0, s>>>(c, x.d_line_len, x.d_block_sum);
-    TSFM_CUDA(cudaGetLastError(), "csv: length kernel");
-    prof_mark(x, K_LENGTH, true, s);
+    prof_mark(x, K_DESCRIBE, false, s);
+    csv_describe_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(c, x.d_packed, x.d_block_sum);
+    TSFM_CUDA(cudaGetLastError(), "csv: describe kernel");
+    prof_mark(x, K_DESCRIBE, true, s);
     prof_mark(x, K_SCAN, false, s);
     csv_scan_kernel<<<1, 1024, 0, s>>>(x.d_block_sum, blocks, x.d_block_off, x.d_total);
     TSFM_CUDA(cudaGetLastError(), "csv: scan kernel");
@@ -401,21 +462,11 @@ Status run_lengths(Ctx &x, const Lines &c, cudaStream_t s) {
 }
 
 Status run_text(Ctx &x, const Lines &c, char *out, cudaStream_t s) {
-    const int64_t blocks = (c.lines + kLinesPerBlock - 1) / kLinesPerBlock;
+    const int64_t blocks = (c.lines + c.lpb - 1) / c.lpb;
     if (blocks == 0) return Status::ok();
-    const size_t smem = write_smem_bytes(c.q);
-    static std::once_flag once[kMaxDevices];
-    int dev = 0;
-    TSFM_CUDA(cudaGetDevice(&dev), "csv: device");
-    cudaError_t attr = cudaSuccess;
-    std::call_once(once[dev % kMaxDevices], [&] {
-        attr = cudaFuncSetAttribute(csv_write_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)write_smem_bytes(kMaxLevels));
-    });
-    TSFM_CUDA(attr, "csv: shared memory attribute");
+    const size_t smem = packed_smem(c.q, c.lpb) + text_smem(c.q, c.lpb);
     prof_mark(x, K_TEXT, false, s);
-    csv_write_kernel<<<(unsigned)blocks, kWarps * 32, smem, s>>>(c, x.d_line_len, x.d_block_off, out,
-                                                                  line_buffer_bytes(c.q));
+    csv_text_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(c, x.d_packed, x.d_block_off, out);
     TSFM_CUDA(cudaGetLastError(), "csv: text kernel");
     prof_mark(x, K_TEXT, true, s);
     return Status::ok();
@@ -434,70 +485,111 @@ Status check_shape(const float *values, size_t series, size_t variates, size_t h
     return Status::ok();
 }
 
-// Lines per chunk of the host entry points: 64 MiB of values (and at least one block).
+// Lines per chunk of the host entry points: 32 MiB of values, whole blocks.
 int64_t chunk_lines(int q) {
+    const int lpb = lines_per_block(q);
     const int64_t per = std::max<int64_t>(1, (int64_t)q) * 4;
-    return std::max<int64_t>(kLinesPerBlock, ((int64_t)64 << 20) / per / kLinesPerBlock * kLinesPerBlock);
+    return std::max<int64_t>(lpb, ((int64_t)32 << 20) / per / lpb * lpb);
 }
 
-// The host entry points' loop: per chunk, values in, lengths, total back; then `sink` gets the
-// chunk's byte count and renders / delivers the text.
-template <class Sink>
-Status for_chunks(Ctx &x, const float *values, int64_t lines, int64_t variates, int64_t horizon, int q, Sink &&sink) {
-    const int64_t chunk = chunk_lines(q);
-    const size_t text_max = (size_t)std::min<int64_t>(chunk, lines) * (size_t)line_buffer_bytes(q);
-    TSFM_TRY(ensure_lines(x, std::min<int64_t>(chunk, lines)));
-    TSFM_TRY(grow_dev(&x.d_values, &x.values_cap, (size_t)std::min<int64_t>(chunk, lines) * q * 4 + 16, "csv: values"));
-    TSFM_TRY(grow_dev(&x.d_text, &x.text_cap, text_max + 16, "csv: text"));
-    cudaStream_t s = x.stream;
-    for (int64_t l0 = 0; l0 < lines; l0 += chunk) {
-        const int64_t n = std::min<int64_t>(chunk, lines - l0);
-        if (q > 0)
-            TSFM_CUDA(cudaMemcpyAsync(x.d_values, values + l0 * q, (size_t)n * q * 4, cudaMemcpyHostToDevice, s),
-                      "csv: values in");
-        Lines c{x.d_values, l0, n, variates, horizon, q};
-        TSFM_TRY(run_lengths(x, c, s));
-        TSFM_CUDA(cudaMemcpyAsync(x.h_total, x.d_total, 8, cudaMemcpyDeviceToHost, s), "csv: total out");
-        TSFM_CUDA(cudaStreamSynchronize(s), "csv: lengths");
-        prof_collect(x);
-        TSFM_TRY(sink(c, (size_t)*x.h_total));
+// The host entry points' pipeline. Per chunk c (slot c % 2): values in on the copy-in stream;
+// describe + scan + the total back on the compute stream; the host reads the total, then the
+// text kernel and the copy-out (stream d2h) of `sink.dest`. The next chunk's values go in
+// while the host waits for this chunk's total; sink.done(c) runs once chunk c's copy-out ended.
+struct Sink {
+    virtual ~Sink() = default;
+    // Where chunk c's text goes (host memory), or nullptr to skip rendering it.
+    virtual Status dest(int64_t c, int slot, size_t bytes, char **p) = 0;
+    virtual Status done(int64_t c, int slot, size_t bytes) = 0;
+};
+
+Status pipeline(Ctx &x, const float *values, int64_t lines, int64_t variates, int64_t horizon, int q, Sink &sink) {
+    const int lpb = lines_per_block(q);
+    const int64_t chunk = chunk_lines(q), nchunks = (lines + chunk - 1) / chunk;
+    const int64_t cl = std::min<int64_t>(chunk, lines);
+    TSFM_TRY(ensure_scratch(x, cl, q));
+    for (int i = 0; i < 2; ++i) {
+        TSFM_TRY(grow_dev(&x.d_values[i], &x.values_cap[i], (size_t)cl * q * 4 + 16, "csv: values"));
+        TSFM_TRY(grow_dev(&x.d_text[i], &x.text_cap[i], (size_t)cl * (kPrefixMax + 1 + (size_t)kValueMax * q) + 16,
+                          "csv: text"));
     }
+    auto copy_in = [&](int64_t c) -> Status {
+        const int slot = (int)(c & 1);
+        const int64_t n = std::min<int64_t>(chunk, lines - c * chunk);
+        TSFM_CUDA(cudaStreamWaitEvent(x.h2d, x.ev_text[slot], 0), "csv: wait");
+        if (q > 0)
+            TSFM_CUDA(cudaMemcpyAsync(x.d_values[slot], values + c * chunk * q, (size_t)n * q * 4,
+                                      cudaMemcpyHostToDevice, x.h2d),
+                      "csv: values in");
+        TSFM_CUDA(cudaEventRecord(x.ev_in[slot], x.h2d), "csv: event");
+        return Status::ok();
+    };
+    size_t sizes[2] = {0, 0};
+    bool pending[2] = {false, false};
+    if (nchunks > 0) TSFM_TRY(copy_in(0));
+    for (int64_t c = 0; c < nchunks; ++c) {
+        const int slot = (int)(c & 1);
+        const int64_t n = std::min<int64_t>(chunk, lines - c * chunk);
+        Lines lc{x.d_values[slot], c * chunk, n, variates, horizon, q, lpb};
+        TSFM_CUDA(cudaStreamWaitEvent(x.comp, x.ev_in[slot], 0), "csv: wait");
+        TSFM_TRY(run_lengths(x, lc, x.comp));
+        TSFM_CUDA(cudaMemcpyAsync(x.h_total + slot, x.d_total, 8, cudaMemcpyDeviceToHost, x.comp), "csv: total out");
+        TSFM_CUDA(cudaEventRecord(x.ev_total[slot], x.comp), "csv: event");
+        if (c + 1 < nchunks) TSFM_TRY(copy_in(c + 1));
+        TSFM_CUDA(cudaEventSynchronize(x.ev_total[slot]), "csv: lengths");
+        const size_t bytes = (size_t)x.h_total[slot];
+        char *p = nullptr;
+        TSFM_TRY(sink.dest(c, slot, bytes, &p));
+        if (p != nullptr) {
+            TSFM_CUDA(cudaStreamWaitEvent(x.comp, x.ev_out[slot], 0), "csv: wait");
+            TSFM_TRY(run_text(x, lc, x.d_text[slot], x.comp));
+            TSFM_CUDA(cudaEventRecord(x.ev_text[slot], x.comp), "csv: event");
+            TSFM_CUDA(cudaStreamWaitEvent(x.d2h, x.ev_text[slot], 0), "csv: wait");
+            TSFM_CUDA(cudaMemcpyAsync(p, x.d_text[slot], bytes, cudaMemcpyDeviceToHost, x.d2h), "csv: text out");
+            TSFM_CUDA(cudaEventRecord(x.ev_out[slot], x.d2h), "csv: event");
+        } else {
+            TSFM_CUDA(cudaEventRecord(x.ev_text[slot], x.comp), "csv: event");
+        }
+        // Chunk c - 1 has had its copy-out issued: finish it while this one renders.
+        const int prev = 1 - slot;
+        if (pending[prev]) {
+            TSFM_CUDA(cudaEventSynchronize(x.ev_out[prev]), "csv: text");
+            TSFM_TRY(sink.done(c - 1, prev, sizes[prev]));
+            pending[prev] = false;
+        }
+        sizes[slot] = bytes;
+        pending[slot] = p != nullptr;
+        if (x.prof) {
+            TSFM_CUDA(cudaStreamSynchronize(x.comp), "csv: profile");
+            prof_collect(x);
+        }
+    }
+    for (int i = 0; i < 2; ++i)
+        if (pending[i]) {
+            TSFM_CUDA(cudaEventSynchronize(x.ev_out[i]), "csv: text");
+            TSFM_TRY(sink.done(nchunks - 1, i, sizes[i]));
+        }
+    TSFM_CUDA(cudaStreamSynchronize(x.d2h), "csv: text");
+    TSFM_CUDA(cudaStreamSynchronize(x.comp), "csv: kernels");
     return Status::ok();
 }
 
-Status format_host(int device, const float *values, size_t series, size_t variates, size_t horizon,
-                   const double *levels, size_t nq, char *out, size_t capacity, size_t *length) {
-    TSFM_TRY(check_shape(values, series, variates, horizon, levels, nq, length));
-    if (out == nullptr && capacity > 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "csv: out is null");
-    if (device < 0 || device >= kMaxDevices) return Status::fail(TSFM_ERR_NO_DEVICE, "csv: device ordinal");
-    Ctx &x = g_ctx[device];
-    std::lock_guard<std::mutex> lock(x.mu);
-    TSFM_TRY(ctx_init(x, device));
-    const std::string head = header_text(levels, nq);
-    size_t pos = head.size();
-    bool fits = pos <= capacity;
-    if (fits) std::memcpy(out, head.data(), head.size());
-    const int64_t lines = (int64_t)(series * variates * horizon);
-    TSFM_TRY(for_chunks(x, values, lines, (int64_t)variates, (int64_t)horizon, (int)nq,
-                        [&](const Lines &c, size_t bytes) -> Status {
-                            if (fits && pos + bytes <= capacity) {
-                                TSFM_TRY(run_text(x, c, x.d_text, x.stream));
-                                TSFM_CUDA(cudaMemcpyAsync(out + pos, x.d_text, bytes, cudaMemcpyDeviceToHost, x.stream),
-                                          "csv: text out");
-                                TSFM_CUDA(cudaStreamSynchronize(x.stream), "csv: text");
-                                prof_collect(x);
-                            } else {
-                                fits = false;
-                            }
-                            pos += bytes;
-                            return Status::ok();
-                        }));
-    *length = pos;
-    if (!fits)
-        return Status::fail(TSFM_ERR_BUFFER_TOO_SMALL,
-                            "csv: the text needs " + std::to_string(pos) + " bytes, capacity " + std::to_string(capacity));
-    return Status::ok();
-}
+struct BufferSink : Sink {
+    char *out;
+    size_t capacity, pos;
+    bool fits;
+    Status dest(int64_t, int, size_t bytes, char **p) override {
+        if (fits && pos + bytes <= capacity) {
+            *p = out + pos;
+        } else {
+            fits = false;
+            *p = nullptr;
+        }
+        pos += bytes;
+        return Status::ok();
+    }
+    Status done(int64_t, int, size_t) override { return Status::ok(); }
+};
 
 Status write_all(int fd, const char *p, size_t n) {
     while (n > 0) {
@@ -512,6 +604,54 @@ Status write_all(int fd, const char *p, size_t n) {
     return Status::ok();
 }
 
+// Text copied into pinned staging (one buffer per slot) and written to fd.
+struct FdSink : Sink {
+    Ctx *x;
+    int fd;
+    size_t pos = 0;
+    Status dest(int64_t, int slot, size_t bytes, char **p) override {
+        if (x->h_text_cap[slot] < bytes) {
+            if (x->h_text[slot]) cudaFreeHost(x->h_text[slot]);
+            x->h_text[slot] = nullptr;
+            x->h_text_cap[slot] = 0;
+            TSFM_CUDA(cudaMallocHost(reinterpret_cast<void **>(&x->h_text[slot]), std::max<size_t>(bytes, 1)),
+                      "csv: pinned text");
+            x->h_text_cap[slot] = std::max<size_t>(bytes, 1);
+        }
+        *p = x->h_text[slot];
+        return Status::ok();
+    }
+    Status done(int64_t, int slot, size_t bytes) override {
+        TSFM_TRY(write_all(fd, x->h_text[slot], bytes));
+        pos += bytes;
+        return Status::ok();
+    }
+};
+
+Status format_host(int device, const float *values, size_t series, size_t variates, size_t horizon,
+                   const double *levels, size_t nq, char *out, size_t capacity, size_t *length) {
+    TSFM_TRY(check_shape(values, series, variates, horizon, levels, nq, length));
+    if (out == nullptr && capacity > 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "csv: out is null");
+    if (device < 0 || device >= kMaxDevices) return Status::fail(TSFM_ERR_NO_DEVICE, "csv: device ordinal");
+    Ctx &x = g_ctx[device];
+    std::lock_guard<std::mutex> lock(x.mu);
+    TSFM_TRY(ctx_init(x, device));
+    const std::string head = header_text(levels, nq);
+    BufferSink sink;
+    sink.out = out;
+    sink.capacity = capacity;
+    sink.pos = head.size();
+    sink.fits = head.size() <= capacity;
+    if (sink.fits) std::memcpy(out, head.data(), head.size());
+    TSFM_TRY(pipeline(x, values, (int64_t)(series * variates * horizon), (int64_t)variates, (int64_t)horizon, (int)nq,
+                      sink));
+    *length = sink.pos;
+    if (!sink.fits)
+        return Status::fail(TSFM_ERR_BUFFER_TOO_SMALL, "csv: the text needs " + std::to_string(sink.pos) +
+                                                           " bytes, capacity " + std::to_string(capacity));
+    return Status::ok();
+}
+
 Status write_fd(int device, const float *values, size_t series, size_t variates, size_t horizon, const double *levels,
                 size_t nq, int fd, size_t *length) {
     TSFM_TRY(check_shape(values, series, variates, horizon, levels, nq, length));
@@ -522,33 +662,18 @@ Status write_fd(int device, const float *values, size_t series, size_t variates,
     TSFM_TRY(ctx_init(x, device));
     const std::string head = header_text(levels, nq);
     TSFM_TRY(write_all(fd, head.data(), head.size()));
-    size_t pos = head.size();
-    const int64_t lines = (int64_t)(series * variates * horizon);
-    TSFM_TRY(for_chunks(x, values, lines, (int64_t)variates, (int64_t)horizon, (int)nq,
-                        [&](const Lines &c, size_t bytes) -> Status {
-                            if (x.h_text_cap < bytes) {
-                                if (x.h_text[0]) cudaFreeHost(x.h_text[0]);
-                                x.h_text[0] = nullptr;
-                                x.h_text_cap = 0;
-                                TSFM_CUDA(cudaMallocHost(reinterpret_cast<void **>(&x.h_text[0]), bytes),
-                                          "csv: pinned text");
-                                x.h_text_cap = bytes;
-                            }
-                            TSFM_TRY(run_text(x, c, x.d_text, x.stream));
-                            TSFM_CUDA(cudaMemcpyAsync(x.h_text[0], x.d_text, bytes, cudaMemcpyDeviceToHost, x.stream),
-                                      "csv: text out");
-                            TSFM_CUDA(cudaStreamSynchronize(x.stream), "csv: text");
-                            prof_collect(x);
-                            TSFM_TRY(write_all(fd, x.h_text[0], bytes));
-                            pos += bytes;
-                            return Status::ok();
-                        }));
-    *length = pos;
+    FdSink sink;
+    sink.x = &x;
+    sink.fd = fd;
+    sink.pos = head.size();
+    TSFM_TRY(pipeline(x, values, (int64_t)(series * variates * horizon), (int64_t)variates, (int64_t)horizon, (int)nq,
+                      sink));
+    *length = sink.pos;
     return Status::ok();
 }
 
 Status format_device(const float *values, size_t series, size_t variates, size_t horizon, const double *levels,
-                     size_t nq, char *out, size_t capacity, size_t *length, cudaStream_t user_stream) {
+                     size_t nq, char *out, size_t capacity, size_t *length, cudaStream_t s) {
     TSFM_TRY(check_shape(values, series, variates, horizon, levels, nq, length));
     if (out == nullptr && capacity > 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "csv: out is null");
     int device = 0;
@@ -559,20 +684,20 @@ Status format_device(const float *values, size_t series, size_t variates, size_t
     TSFM_TRY(ctx_init(x, device));
     const std::string head = header_text(levels, nq);
     const int64_t lines = (int64_t)(series * variates * horizon);
-    TSFM_TRY(ensure_lines(x, lines));
-    Lines c{values, 0, lines, (int64_t)variates, (int64_t)horizon, (int)nq};
-    TSFM_TRY(run_lengths(x, c, user_stream));
-    TSFM_CUDA(cudaMemcpyAsync(x.h_total, x.d_total, 8, cudaMemcpyDeviceToHost, user_stream), "csv: total out");
-    TSFM_CUDA(cudaStreamSynchronize(user_stream), "csv: lengths");
+    TSFM_TRY(ensure_scratch(x, lines, (int)nq));
+    Lines c{values, 0, lines, (int64_t)variates, (int64_t)horizon, (int)nq, lines_per_block((int)nq)};
+    TSFM_TRY(run_lengths(x, c, s));
+    TSFM_CUDA(cudaMemcpyAsync(x.h_total, x.d_total, 8, cudaMemcpyDeviceToHost, s), "csv: total out");
+    TSFM_CUDA(cudaStreamSynchronize(s), "csv: lengths");
     prof_collect(x);
-    const size_t total = head.size() + (size_t)*x.h_total;
+    const size_t total = head.size() + (size_t)x.h_total[0];
     *length = total;
     if (total > capacity)
         return Status::fail(TSFM_ERR_BUFFER_TOO_SMALL,
                             "csv: the text needs " + std::to_string(total) + " bytes, capacity " + std::to_string(capacity));
-    TSFM_CUDA(cudaMemcpyAsync(out, head.data(), head.size(), cudaMemcpyHostToDevice, user_stream), "csv: header");
-    TSFM_TRY(run_text(x, c, out + head.size(), user_stream));
-    TSFM_CUDA(cudaStreamSynchronize(user_stream), "csv: text");
+    TSFM_CUDA(cudaMemcpyAsync(out, head.data(), head.size(), cudaMemcpyHostToDevice, s), "csv: header");
+    TSFM_TRY(run_text(x, c, out + head.size(), s));
+    TSFM_CUDA(cudaStreamSynchronize(s), "csv: text");
     prof_collect(x);
     return Status::ok();
 }
@@ -598,8 +723,8 @@ Status profile_read(int device, const char *kernel, uint64_t *launches, double *
     if (kernel == nullptr || launches == nullptr || ms == nullptr)
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "csv: null profile argument");
     const std::string k = kernel;
-    const int id = k == "length" ? K_LENGTH : k == "scan" ? K_SCAN : k == "text" ? K_TEXT : -1;
-    if (id < 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "csv: kernel is one of length, scan, text");
+    const int id = k == "describe" ? K_DESCRIBE : k == "scan" ? K_SCAN : k == "text" ? K_TEXT : -1;
+    if (id < 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "csv: kernel is one of describe, scan, text");
     Ctx &x = g_ctx[device];
     std::lock_guard<std::mutex> lock(x.mu);
     *launches = x.launches[id];

@@ -73,7 +73,7 @@ def profile(enable=True, device=0):
 
 
 def profile_read(kernel, device=0):
-    """{"launches", "ms"} of one CSV kernel ("length", "scan" or "text") since profiling started."""
+    """{"launches", "ms"} of one CSV kernel ("describe", "scan" or "text") since profiling started."""
     n, ms = ctypes.c_uint64(0), ctypes.c_double(0)
     check(lib.tsfm_csv_profile_read(device, kernel.encode(), ctypes.byref(n), ctypes.byref(ms)))
     return {"launches": n.value, "ms": ms.value}
