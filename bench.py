@@ -47,6 +47,7 @@ def parse_args():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--series", type=int, default=SERIES_PER_GPU)
     ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
+    ap.add_argument("--csv-series", type=int, default=8192, help="series of the csv workload")
     ap.add_argument("--workload", default="chronos2",
                     choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv"],
                     help="chronos2 is the headline; bolt-*/timestral are BASELINE.json's other configs, timed "
@@ -340,7 +341,7 @@ def run_csv(a):
     import torch
     import tsfm_b200 as tb
     from tsfm_b200 import csv
-    series, horizon, q = 8192, 1024, 21
+    series, horizon, q = a.csv_series, 1024, 21
     levels = np.array([0.01, 0.05] + [round(0.05 * i, 2) for i in range(2, 19)] + [0.95, 0.99], np.float64)
     assert levels.size == q
     vals = forecast_like_values(series, horizon, q, seed=77)
@@ -400,7 +401,7 @@ def run_csv(a):
     t0 = time.perf_counter()
     ob.csv_format(sample, levels)
     cpu_dt = time.perf_counter() - t0
-    line = {"metric": "CSV output series/sec (writeCsv of an 8192-series H1024 21-level forecast)",
+    line = {"metric": f"CSV output series/sec (writeCsv of a {series}-series H1024 21-level forecast)",
             "value": series / (ms / 1e3), "unit": "series/s", "n_gpus": 1, "steps": steps, "warmup": a.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic (seeded quantile forecasts, float32)",

@@ -35,7 +35,7 @@ def forecast_values(shape, seed, kind="normal"):
 
 
 def levels_for(q):
-    return np.round(np.linspace(0.01, 0.99, q), 4) if q > 1 else np.array([0.5])
+    return np.round(np.linspace(0.01, 0.99, q), 4) if q > 1 else np.array([0.5] * q)
 
 
 @pytest.mark.parametrize("shape", [(1, 1, 1, 1), (3, 2, 17, 9), (5, 1, 64, 21), (2, 3, 5, 40), (7, 1, 33, 32),
@@ -117,7 +117,7 @@ def test_device_resident_variant(csvmod):
 
 
 def test_chunked_full_size_digest(csvmod):
-    # 2048 series x 1024 steps x 21 levels (44 M values, several 64 MiB chunks): the digest of the
+    # 2048 series x 1024 steps x 21 levels (44 M values, six 32 MiB chunks): the digest of the
     # GPU text equals the oracle's.
     v = forecast_values((2048, 1, 1024, 21), seed=12)
     lv = levels_for(21)

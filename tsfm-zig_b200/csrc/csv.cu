@@ -72,29 +72,70 @@ __device__ __forceinline__ csv::F32Text unpack(uint64_t p) {
     return f;
 }
 
-struct Prefix {
-    uint64_t s, v, step;
-    int ls, lv, lst;
-    __device__ int len() const { return ls + lv + lst + 2; }  // "s,v,step"
-};
-
-__device__ __forceinline__ Prefix prefix_of(int64_t line, int64_t variates, int64_t horizon) {
-    Prefix p;
-    p.s = (uint64_t)(line / (variates * horizon));
-    p.v = (uint64_t)((line / horizon) % variates);
-    p.step = (uint64_t)(line % horizon) + 1;
-    p.ls = csv::u64_length(p.s);
-    p.lv = csv::u64_length(p.v);
-    p.lst = csv::u64_length(p.step);
-    return p;
+// Digit count of v (1..20) by comparison with powers of ten.
+__device__ __forceinline__ int u64_digits(uint64_t v) {
+    int n = 1;
+    uint64_t p = 10;
+    while (n < 20 && v >= p) {
+        ++n;
+        p *= 10;
+    }
+    return n;
 }
 
-__device__ __forceinline__ void emit_prefix(const Prefix &p, char *o) {
-    csv::emit_u64(p.s, p.ls, o);
-    o[p.ls] = ',';
-    csv::emit_u64(p.v, p.lv, o + p.ls + 1);
-    o[p.ls + 1 + p.lv] = ',';
-    csv::emit_u64(p.step, p.lst, o + p.ls + p.lv + 2);
+__device__ __forceinline__ void emit_uint(uint64_t v, int len, char *o) {
+    if (v < (1ull << 32)) {
+        uint32_t w = (uint32_t)v;
+        for (int i = len - 1; i >= 0; --i) {
+            o[i] = (char)('0' + w % 10);
+            w /= 10;
+        }
+    } else {
+        csv::emit_u64(v, len, o);
+    }
+}
+
+// The (series, variate, step) of a block's lines, one line per thread of the first warp; 32-bit
+// divisions when the indices fit (the usual case), 64-bit ones otherwise.
+struct LineIds {
+    uint64_t s[32], v[32], step[32];
+    uint8_t ls[32], lv[32], lst[32];
+};
+
+__device__ __forceinline__ void line_ids(const Lines &c, int64_t l0, int li, LineIds &ids) {
+    const int64_t line = c.first + l0 + li, per_series = c.variates * c.horizon;
+    uint64_t s, v, step;
+    if (c.first + c.lines <= (int64_t)UINT32_MAX && per_series <= (int64_t)UINT32_MAX) {
+        const uint32_t l = (uint32_t)line, ps = (uint32_t)per_series, h = (uint32_t)c.horizon;
+        const uint32_t s32 = l / ps, rem = l - s32 * ps, v32 = rem / h;
+        s = s32;
+        v = v32;
+        step = rem - v32 * h + 1;
+    } else {
+        s = (uint64_t)(line / per_series);
+        const int64_t rem = line - (int64_t)s * per_series;
+        v = (uint64_t)(rem / c.horizon);
+        step = (uint64_t)(rem - (int64_t)v * c.horizon) + 1;
+    }
+    ids.s[li] = s;
+    ids.v[li] = v;
+    ids.step[li] = step;
+    ids.ls[li] = (uint8_t)u64_digits(s);
+    ids.lv[li] = (uint8_t)u64_digits(v);
+    ids.lst[li] = (uint8_t)u64_digits(step);
+}
+
+__device__ __forceinline__ int prefix_len(const LineIds &ids, int li) {
+    return ids.ls[li] + ids.lv[li] + ids.lst[li] + 2;  // "s,v,step"
+}
+
+__device__ __forceinline__ void emit_prefix(const LineIds &ids, int li, char *o) {
+    const int ls = ids.ls[li], lv = ids.lv[li];
+    emit_uint(ids.s[li], ls, o);
+    o[ls] = ',';
+    emit_uint(ids.v[li], lv, o + ls + 1);
+    o[ls + 1 + lv] = ',';
+    emit_uint(ids.step[li], ids.lst[li], o + ls + lv + 2);
 }
 
 // Block-wide exclusive scan of one value per thread; *total receives the block's sum.
@@ -124,6 +165,7 @@ __device__ __forceinline__ uint32_t block_scan(uint32_t v, uint32_t *wsum, uint3
 __global__ void __launch_bounds__(kThreads) csv_describe_kernel(Lines c, uint64_t *packed, uint32_t *block_sum) {
     __shared__ csv::Pow5Tables tab;
     __shared__ uint32_t wsum[kThreads / 32];
+    __shared__ LineIds ids;
     {
         const uint64_t *src = reinterpret_cast<const uint64_t *>(&c_pow5);
         uint64_t *dst = reinterpret_cast<uint64_t *>(&tab);
@@ -141,7 +183,10 @@ __global__ void __launch_bounds__(kThreads) csv_describe_kernel(Lines c, uint64_
         packed[base + i] = pack(f);
         acc += 1 + (uint32_t)f.len;
     }
-    if (threadIdx.x < nl) acc += (uint32_t)prefix_of(c.first + l0 + threadIdx.x, c.variates, c.horizon).len() + 1;
+    if (threadIdx.x < nl) {  // each thread reads back only its own line's entries
+        line_ids(c, l0, threadIdx.x, ids);
+        acc += (uint32_t)prefix_len(ids, threadIdx.x) + 1;
+    }
     uint32_t total;
     block_scan(acc, wsum, &total);
     if (threadIdx.x == 0) block_sum[blockIdx.x] = total;
@@ -193,15 +238,15 @@ __global__ void __launch_bounds__(kThreads) csv_text_kernel(Lines c, const uint6
                                                            char *out) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ uint32_t wsum[kThreads / 32];
-    __shared__ uint8_t plen[32];
+    __shared__ LineIds ids;
     uint64_t *pk = reinterpret_cast<uint64_t *>(smem);
     char *text = reinterpret_cast<char *>(smem + packed_smem(c.q, c.lpb));
     const int64_t l0 = (int64_t)blockIdx.x * c.lpb;
     const int nl = (int)min((int64_t)c.lpb, c.lines - l0);
     const int n = nl * c.q;
     const int64_t base = l0 * c.q;
+    if (threadIdx.x < nl) line_ids(c, l0, threadIdx.x, ids);
     for (int i = threadIdx.x; i < n; i += kThreads) pk[i] = packed[base + i];
-    if (threadIdx.x < nl) plen[threadIdx.x] = (uint8_t)prefix_of(c.first + l0 + threadIdx.x, c.variates, c.horizon).len();
     __syncthreads();
 
     // Items of a line: its prefix, its q values, its newline. Each thread owns a contiguous run.
@@ -212,7 +257,8 @@ __global__ void __launch_bounds__(kThreads) csv_text_kernel(Lines c, const uint6
     {
         int li = k0 / per, r = k0 - li * per;
         for (int k = k0; k < k1; ++k) {
-            mine += r == 0 ? plen[li] : (r <= c.q ? 1 + (uint32_t)((pk[li * c.q + r - 1] >> 41) & 0x3f) : 1);
+            mine += r == 0 ? (uint32_t)prefix_len(ids, li)
+                           : (r <= c.q ? 1 + (uint32_t)((pk[li * c.q + r - 1] >> 41) & 0x3f) : 1);
             if (++r == per) r = 0, ++li;
         }
     }
@@ -225,8 +271,8 @@ __global__ void __launch_bounds__(kThreads) csv_text_kernel(Lines c, const uint6
         uint32_t o = (uint32_t)pad + off;
         for (int k = k0; k < k1; ++k) {
             if (r == 0) {
-                emit_prefix(prefix_of(c.first + l0 + li, c.variates, c.horizon), text + o);
-                o += plen[li];
+                emit_prefix(ids, li, text + o);
+                o += (uint32_t)prefix_len(ids, li);
             } else if (r <= c.q) {
                 const csv::F32Text f = unpack(pk[li * c.q + r - 1]);
                 text[o] = ',';

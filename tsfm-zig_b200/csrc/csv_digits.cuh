@@ -243,24 +243,33 @@ TSFM_HD void emit(const F32Text &f, char *p) {
         return;
     }
     const int nd = f.ndigits, dp = f.exponent + nd;
-    char dig[10];
+    // Digits are written from the least significant one straight to their places.
     uint32_t v = f.digits;
-    for (int i = nd - 1; i >= 0; --i) {
-        dig[i] = (char)('0' + v % 10);
-        v /= 10;
-    }
-    if (dp <= 0) {
-        *p++ = '0';
-        *p++ = '.';
-        for (int i = 0; i < -dp; ++i) *p++ = '0';
-        for (int i = 0; i < nd; ++i) *p++ = dig[i];
-    } else if (dp >= nd) {
-        for (int i = 0; i < nd; ++i) *p++ = dig[i];
-        for (int i = nd; i < dp; ++i) *p++ = '0';
-    } else {
-        for (int i = 0; i < dp; ++i) *p++ = dig[i];
-        *p++ = '.';
-        for (int i = dp; i < nd; ++i) *p++ = dig[i];
+    if (dp <= 0) {  // 0.000ddd
+        p[0] = '0';
+        p[1] = '.';
+        for (int i = 0; i < -dp; ++i) p[2 + i] = '0';
+        char *d = p + 2 - dp;
+        for (int i = nd - 1; i >= 0; --i) {
+            d[i] = (char)('0' + v % 10);
+            v /= 10;
+        }
+    } else if (dp >= nd) {  // ddd000
+        for (int i = nd - 1; i >= 0; --i) {
+            p[i] = (char)('0' + v % 10);
+            v /= 10;
+        }
+        for (int i = nd; i < dp; ++i) p[i] = '0';
+    } else {  // dd.ddd
+        for (int i = nd - 1; i >= dp; --i) {
+            p[i + 1] = (char)('0' + v % 10);
+            v /= 10;
+        }
+        p[dp] = '.';
+        for (int i = dp - 1; i >= 0; --i) {
+            p[i] = (char)('0' + v % 10);
+            v /= 10;
+        }
     }
 }
 
