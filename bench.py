@@ -49,11 +49,12 @@ def parse_args():
     ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
     ap.add_argument("--csv-series", type=int, default=8192, help="series of the csv workload")
     ap.add_argument("--workload", default="chronos2",
-                    choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv"],
+                    choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv", "parse"],
                     help="chronos2 is the headline; bolt-*/timestral are BASELINE.json's other configs, timed "
                          "through the host entry points (copies included); sweep is its Chronos-2 throughput sweep "
                          "(batch x context, one JSON line per point); csv renders the CLI's CSV output of an "
-                         "8192-series, horizon-1024, 21-level forecast")
+                         "8192-series, horizon-1024, 21-level forecast; parse reads an 8192-series x 8192-step "
+                         "series file")
     return ap.parse_args()
 
 
@@ -421,6 +422,85 @@ def run_csv(a):
     print(json.dumps(line), flush=True)
 
 
+def run_parse(a):
+    """The reader's parseBlocks (core/series.zig:21-68) of a series file with 8192 series of 8192
+    steps, one series per comma-separated line (5 % empty tokens = missing). value: series/s with
+    the text resident in HBM (tsfm_parse_blocks_device to f32, as the forecast consumes it);
+    e2e: series/s through tsfm_parse_blocks from pinned host text to pinned host f64 values."""
+    import ctypes
+    import torch
+    import tsfm_b200 as tb
+    from tsfm_b200 import synthetic as syn
+    series, steps = a.csv_series, CONTEXT
+    # 256 distinct seeded series, repeated to the full count (every line is still parsed).
+    base = syn.seeded_series(256, steps, seed=4242)
+    lines = [",".join("" if np.isnan(v) else repr(float(v)) for v in row).encode() for row in base]
+    text = b"\n".join(lines[i % 256] for i in range(series)) + b"\n"
+    n = len(text)
+    stream = torch.cuda.current_stream()
+    dt = torch.from_numpy(np.frombuffer(text, np.uint8).copy()).cuda()
+    out32 = torch.empty(series * steps, dtype=torch.float32, device="cuda")
+    b, r, l = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+    run_dev = lambda: tb.check(tb.lib.tsfm_parse_blocks_device(dt.data_ptr(), n, None, out32.data_ptr(),
+                                                               out32.numel(), ctypes.byref(b), ctypes.byref(r),
+                                                               ctypes.byref(l), stream.cuda_stream))
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    for _ in range(max(3, a.warmup)):
+        run_dev()
+    assert (b.value, r.value, l.value) == (1, series, steps)
+    steps_t = max(3, a.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total = 0.0
+    with Clocks(0) as clocks:
+        time.sleep(0.3)
+        clocks.mark_begin()
+        for _ in range(steps_t):
+            flush.zero_()
+            e0.record(stream)
+            run_dev()
+            e1.record(stream)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        clocks.mark_end()
+    ms = total / steps_t
+    ht = torch.from_numpy(np.frombuffer(text, np.uint8).copy()).pin_memory()
+    hv = torch.empty(series * steps, dtype=torch.float64).pin_memory()
+    run_host = lambda: tb.check(tb.lib.tsfm_parse_blocks(ht.data_ptr(), n, 0, hv.data_ptr(), hv.numel(),
+                                                         ctypes.byref(b), ctypes.byref(r), ctypes.byref(l)))
+    for _ in range(2):
+        run_host()
+    t0 = time.perf_counter()
+    for _ in range(steps_t):
+        run_host()
+    e2e_ms = (time.perf_counter() - t0) / steps_t * 1e3
+    # CPU baseline: the oracle's parseBlocks restatement (one thread, as the reference) on 64 series.
+    from oracle import binding as ob
+    sample = b"\n".join(lines[:64]) + b"\n"
+    vals = np.zeros(64 * steps + 16, np.float64)
+    t0 = time.perf_counter()
+    ob.lib.oracle_parse_blocks(sample, vals.ctypes.data, vals.size, ctypes.byref(b), ctypes.byref(r),
+                               ctypes.byref(l))
+    cpu_dt = time.perf_counter() - t0
+    hbm_burst = peaks()[2]
+    alg = n + series * steps * 4  # text read once, f32 values written once
+    achieved = alg / (ms / 1e3) / 1e9
+    line = {"metric": f"series file parse series/sec ({series} series x {steps} steps, parseBlocks)",
+            "value": series / (ms / 1e3), "unit": "series/s", "n_gpus": 1, "steps": steps_t, "warmup": a.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded series, Python repr of float32 values, 5 % empty)",
+            "config": {"workload": "parse", "series": series, "steps": steps, "text_bytes": n,
+                       "l2": "flushed between steps (256 MiB write)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_burst, "unit": "GB/s",
+                         "frac": achieved / hbm_burst, "traffic": None,
+                         "kernel": "whole reader (6 kernels, CUDA events around the call)", "algorithmic_bytes": alg},
+            "cpu_baseline": {"value": 64 / cpu_dt, "unit": "series/s", "cores": 1, "kind": "port",
+                             "sample": f"64 series x {steps} steps (oracle parseBlocks restatement, strtod)"},
+            "e2e": {"value": series / (e2e_ms / 1e3), "unit": "series/s", "h2d_bytes_per_step": n,
+                    "d2h_bytes_per_step": series * steps * 8},
+            "gpu_launches": 6, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -430,7 +510,7 @@ def main():
         return run_reference(a, rank)
     if a.workload != "chronos2":
         if rank == 0:
-            {"sweep": run_sweep, "csv": run_csv}.get(a.workload, run_family_workload)(a)
+            {"sweep": run_sweep, "csv": run_csv, "parse": run_parse}.get(a.workload, run_family_workload)(a)
         return
 
     import torch

@@ -58,7 +58,9 @@ typedef enum tsfm_status {
     TSFM_ERR_COVARIATES_UNSUPPORTED = 14, /* error.CovariatesUnsupported / KnownCovariatesUnsupported */
     TSFM_ERR_NO_DEVICE = 15,         /* no CUDA device, or the device ordinal is out of range */
     TSFM_ERR_BUFFER_TOO_SMALL = 16,  /* an output buffer is shorter than the result (the needed size is returned) */
-    TSFM_ERR_IO = 17                 /* writing to a file descriptor failed */
+    TSFM_ERR_IO = 17,                /* writing to a file descriptor failed */
+    TSFM_ERR_RAGGED_INPUT = 18,      /* error.RaggedInput (core/series.zig:58) */
+    TSFM_ERR_RAGGED_BLOCKS = 19      /* error.RaggedBlocks (core/series.zig:39, 64) */
 } tsfm_status;
 
 typedef enum tsfm_family {
@@ -317,6 +319,25 @@ int32_t tsfm_csv_write(const float *values, size_t series, size_t variates, size
 int32_t tsfm_csv_format_device(const float *values, size_t series, size_t variates, size_t horizon,
                                const double *levels, size_t num_levels, char *out, size_t capacity,
                                size_t *length, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Series CSV input. Replaces the reader's parseBlocks (core/series.zig:21-68): blank-line-
+ * separated blocks of equal-length rows; '#' lines skipped; comma-separated tokens when a line
+ * holds a comma, else space / tab separated; each token trimmed of " \t\r" and parsed as f64
+ * (correctly rounded; NaN when empty or not a number). The values are (blocks, rows, len)
+ * row-major. Errors: TSFM_ERR_RAGGED_INPUT, TSFM_ERR_RAGGED_BLOCKS, TSFM_ERR_EMPTY_INPUT, in the
+ * reference's order. The text is split and parsed on the GPU.
+ *
+ * tsfm_parse_blocks: text in host memory, values to host memory. values == NULL only returns
+ * the shape; a capacity (in values) below blocks * rows * len returns TSFM_ERR_BUFFER_TOO_SMALL.
+ * tsfm_parse_blocks_device: text and outputs in the current device's memory, ordered on stream;
+ * values (f64) and values_f32 (toF32, core/series.zig:78-82: round to nearest) may each be NULL;
+ * returns after the values are complete. */
+int32_t tsfm_parse_blocks(const char *text, size_t length, int32_t device, double *values,
+                          size_t capacity, size_t *blocks, size_t *rows, size_t *len);
+int32_t tsfm_parse_blocks_device(const char *text, size_t length, double *values, float *values_f32,
+                                 size_t capacity, size_t *blocks, size_t *rows, size_t *len,
+                                 void *stream);
 
 /* Per-kernel device time of the CSV kernels on a device ("describe", "scan", "text"): launches and
  * milliseconds since the last enable (CUDA events around each launch while enabled). */

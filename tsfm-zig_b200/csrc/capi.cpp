@@ -242,6 +242,8 @@ const char *tsfm_status_string(int32_t s) {
         case TSFM_ERR_NO_DEVICE: return "no device";
         case TSFM_ERR_BUFFER_TOO_SMALL: return "buffer too small";
         case TSFM_ERR_IO: return "I/O error";
+        case TSFM_ERR_RAGGED_INPUT: return "ragged input";
+        case TSFM_ERR_RAGGED_BLOCKS: return "ragged blocks";
         default: return "unknown status";
     }
 }

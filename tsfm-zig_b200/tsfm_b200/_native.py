@@ -16,6 +16,7 @@ STATUS_NAMES = {
     5: "UNSUPPORTED_DTYPE", 6: "CUDA", 7: "OUT_OF_MEMORY", 8: "DEVICE_TIMEOUT", 9: "EMPTY_INPUT",
     10: "HORIZON_TOO_LONG", 11: "UNSUPPORTED", 12: "DEGENERATE_INPUT", 13: "ASYMMETRIC_QUANTILES",
     14: "COVARIATES_UNSUPPORTED", 15: "NO_DEVICE", 16: "BUFFER_TOO_SMALL", 17: "IO",
+    18: "RAGGED_INPUT", 19: "RAGGED_BLOCKS",
 }
 FAMILY = {"chronos2": 1, "chronos_bolt": 2, "timestral": 3}
 DTYPE = {"F32": 0, "F16": 1, "BF16": 2}
@@ -113,6 +114,10 @@ SIGNATURES = {
     "tsfm_csv_format": (_I32, [_P, _SZ, _SZ, _SZ, _P, _SZ, _I32, _P, _SZ, ctypes.POINTER(_SZ)]),
     "tsfm_csv_write": (_I32, [_P, _SZ, _SZ, _SZ, _P, _SZ, _I32, _I32, ctypes.POINTER(_SZ)]),
     "tsfm_csv_format_device": (_I32, [_P, _SZ, _SZ, _SZ, _P, _SZ, _P, _SZ, ctypes.POINTER(_SZ), _P]),
+    "tsfm_parse_blocks": (_I32, [_P, _SZ, _I32, _P, _SZ, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ),
+                                 ctypes.POINTER(_SZ)]),
+    "tsfm_parse_blocks_device": (_I32, [_P, _SZ, _P, _P, _SZ, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ),
+                                        ctypes.POINTER(_SZ), _P]),
     "tsfm_csv_profile_enable": (_I32, [_I32, _I32]),
     "tsfm_csv_profile_read": (_I32, [_I32, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64),
                                      ctypes.POINTER(ctypes.c_double)]),
