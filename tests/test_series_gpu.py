@@ -179,6 +179,23 @@ def test_device_variant_f32(series):
     assert ((np.isnan(f) & np.isnan(g)) | (f.view(np.uint32) == g.view(np.uint32))).all()
 
 
+@pytest.mark.parametrize("offset", [1, 3, 7, 13])
+def test_device_variant_unaligned_text(series, offset):
+    # The text starts at an odd address: edge chunks are read byte by byte.
+    import torch
+    rng = np.random.default_rng(30 + offset)
+    text = make_file(rng, 2, 2, 300, sep=" " if offset % 2 else ",").encode()
+    st, want = oracle_parse(text)
+    buf = torch.zeros(len(text) + 32, dtype=torch.uint8, device="cuda")
+    buf[offset:offset + len(text)] = torch.from_numpy(np.frombuffer(text, np.uint8).copy()).cuda()
+    ptr = buf.data_ptr() + offset
+    assert series.parse_blocks_device(ptr, len(text)) == want.shape
+    o64 = torch.empty(want.size, dtype=torch.float64, device="cuda")
+    series.parse_blocks_device(ptr, len(text), o64.data_ptr(), None, want.size)
+    torch.cuda.synchronize()
+    same(o64.cpu().numpy().reshape(want.shape), want)
+
+
 def test_long_lines_full_size(series):
     # 1024 series x 8192 values, one series per line (the CLI's input layout at context 8192).
     rng = np.random.default_rng(5)

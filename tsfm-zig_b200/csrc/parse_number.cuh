@@ -297,8 +297,33 @@ TSFM_PHD double parse_hex(const char *p, int n, bool neg, bool *ok) {
     return round_scaled(m, shift, sticky, neg);
 }
 
-// Parses the whole of p[0, n) (already trimmed); NaN when it is not a number.
-TSFM_PHD_NOINLINE double parse_number(const char *p, int n) {
+// High 128 bits of the 256-bit product a * b.
+TSFM_PHD u128 mulhi128(u128 a, u128 b) {
+    const uint64_t a0 = (uint64_t)a, a1 = (uint64_t)(a >> 64), b0 = (uint64_t)b, b1 = (uint64_t)(b >> 64);
+    const u128 p00 = (u128)a0 * b0, p01 = (u128)a0 * b1, p10 = (u128)a1 * b0, p11 = (u128)a1 * b1;
+    const u128 mid = (p00 >> 64) + (uint64_t)p01 + (uint64_t)p10;  // < 3 * 2^64
+    return p11 + (p01 >> 64) + (p10 >> 64) + (mid >> 64);
+}
+
+// floor(2^128 / 10^m) for m in [1, 19] (index m), the reciprocals of path (2): the quotient
+// estimate mulhi(num, r) is at most 2 below the true quotient and is corrected exactly.
+struct Recip10 {
+    u128 r[20];
+};
+
+inline Recip10 make_recip10() {
+    Recip10 t{};
+    u128 d = 1;
+    for (int m = 1; m < 20; ++m) {
+        d *= 10;
+        t.r[m] = (~(u128)0) / d;  // floor((2^128 - 1) / d) == floor(2^128 / d) for d not a power of 2
+    }
+    return t;
+}
+
+// Parses the whole of p[0, n) (already trimmed); NaN when it is not a number. `recip`, when
+// given, replaces the 128-bit division of path (2) by a multiply and at most two corrections.
+TSFM_PHD_NOINLINE double parse_number(const char *p, int n, const Recip10 *recip = nullptr) {
     int i = 0;
     bool neg = false;
     if (i < n && (p[i] == '+' || p[i] == '-')) neg = p[i++] == '-';
@@ -366,8 +391,19 @@ TSFM_PHD_NOINLINE double parse_number(const char *p, int n) {
             const int s = 127 - bitlen128((u128)w);
             const u128 num = ((u128)w) << s;
             const uint64_t den = pow10_u64(-e10);
-            const u128 q = num / den;
-            return round_scaled(q, -s, (num - q * den) != 0, neg);
+            u128 q, rem;
+            if (recip != nullptr) {
+                q = mulhi128(num, recip->r[-e10]);
+                rem = num - q * den;
+                while (rem >= den) {
+                    rem -= den;
+                    ++q;
+                }
+            } else {
+                q = num / den;
+                rem = num - q * den;
+            }
+            return round_scaled(q, -s, rem != 0, neg);
         }
     }
     // Path (3): gather up to kMaxDigits significant digits again.

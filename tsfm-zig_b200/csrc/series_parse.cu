@@ -37,11 +37,43 @@ constexpr int kTile = 4096;  // bytes per block of the newline kernels (256 thre
 __device__ __forceinline__ bool is_trim(char c) { return c == ' ' || c == '\t' || c == '\r'; }
 __device__ __forceinline__ bool is_sep(char c) { return c == ' ' || c == '\t'; }
 
-// (1a) newlines per tile.
+// Lines are read 16 bytes per lane (one aligned 16-byte chunk each, 512 bytes per warp step).
+// Chunk k covers text positions [16k - mis, 16k - mis + 16), mis = the text pointer's offset in
+// its 16-byte granule; a chunk inside [0, n) is one vector load, an edge chunk is read byte by
+// byte (only its in-range bytes).
+struct Chunk {
+    uint32_t w[4];
+    __device__ __forceinline__ char at(int j) const { return (char)((w[j >> 2] >> (8 * (j & 3))) & 0xff); }
+};
+
+__device__ __forceinline__ Chunk load_chunk(const char *text, int64_t n, int mis, int64_t k) {
+    Chunk c;
+    const int64_t q0 = k * 16 - mis;
+    if (q0 >= 0 && q0 + 16 <= n) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(text + q0);
+        c.w[0] = v.x, c.w[1] = v.y, c.w[2] = v.z, c.w[3] = v.w;
+    } else {
+        c.w[0] = c.w[1] = c.w[2] = c.w[3] = 0x20202020u;  // spaces
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (q0 + j >= 0 && q0 + j < n) c.w[j >> 2] = (c.w[j >> 2] & ~(0xffu << (8 * (j & 3)))) |
+                                                         ((uint32_t)(uint8_t)text[q0 + j] << (8 * (j & 3)));
+    }
+    return c;
+}
+
+__device__ __forceinline__ uint32_t newline_mask(const Chunk &c, int64_t q0, int64_t n) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) m |= (q0 + j >= 0 && q0 + j < n && c.at(j) == '\n') ? (1u << j) : 0u;
+    return m;
+}
+
+// (1a) newlines per tile (tile t = aligned chunks [256 t, 256 t + 256)).
 __global__ void __launch_bounds__(256) nl_count_kernel(const char *text, int64_t n, uint32_t *tile_count) {
-    const int64_t base = (int64_t)blockIdx.x * kTile + threadIdx.x * 16;
-    uint32_t c = 0;
-    for (int i = 0; i < 16; ++i) c += (base + i < n && text[base + i] == '\n') ? 1u : 0u;
+    const int mis = (int)(reinterpret_cast<uintptr_t>(text) & 15);
+    const int64_t k = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    uint32_t c = __popc(newline_mask(load_chunk(text, n, mis, k), k * 16 - mis, n));
     for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
     __shared__ uint32_t ws[8];
     if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = c;
@@ -91,9 +123,10 @@ __global__ void __launch_bounds__(1024) scan_u32_kernel(const uint32_t *in, int6
 // (1c) newline positions, in order.
 __global__ void __launch_bounds__(256) nl_pos_kernel(const char *text, int64_t n, const uint64_t *tile_off,
                                                     uint64_t *pos) {
-    const int64_t base = (int64_t)blockIdx.x * kTile + threadIdx.x * 16;
-    uint32_t c = 0;
-    for (int i = 0; i < 16; ++i) c += (base + i < n && text[base + i] == '\n') ? 1u : 0u;
+    const int mis = (int)(reinterpret_cast<uintptr_t>(text) & 15);
+    const int64_t k = (int64_t)blockIdx.x * 256 + threadIdx.x, q0 = k * 16 - mis;
+    uint32_t m = newline_mask(load_chunk(text, n, mis, k), q0, n);
+    const uint32_t c = __popc(m);
     // exclusive block scan of c
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t x = c;
@@ -106,9 +139,12 @@ __global__ void __launch_bounds__(256) nl_pos_kernel(const char *text, int64_t n
     __syncthreads();
     uint32_t before = 0;
     for (int w = 0; w < warp; ++w) before += ws[w];
-    uint64_t k = tile_off[blockIdx.x] + before + x - c;
-    for (int i = 0; i < 16; ++i)
-        if (base + i < n && text[base + i] == '\n') pos[k++] = (uint64_t)(base + i);
+    uint64_t at = tile_off[blockIdx.x] + before + x - c;
+    while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        pos[at++] = (uint64_t)(q0 + j);
+    }
 }
 
 struct LineInfo {
@@ -124,53 +160,110 @@ __device__ __forceinline__ void line_span(const uint64_t *nl, int64_t n_nl, int6
     *e = line < n_nl ? nl[line] : (uint64_t)total;
 }
 
+template <class T>
+__device__ __forceinline__ T warp_excl_scan(T v, T *total) {
+    const int lane = threadIdx.x & 31;
+    T x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const T y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    *total = __shfl_sync(0xffffffffu, x, 31);
+    return x - v;
+}
+
 // (2) one warp per line: trimmed bounds, kind, separator, token count.
 __global__ void __launch_bounds__(256) line_kernel(const char *text, int64_t total, const uint64_t *nl, int64_t n_nl,
                                                   LineInfo *info, uint32_t *meta) {
     const int lane = threadIdx.x & 31;
     const int64_t line = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (line > n_nl) return;
+    const int mis = (int)(reinterpret_cast<uintptr_t>(text) & 15);
     uint64_t s, e;
     line_span(nl, n_nl, total, line, &s, &e);
-    // First and last bytes that are not " \t\r".
-    uint64_t a = e, b = s;
-    for (uint64_t p = s; p < e; p += 32) {
-        const uint64_t q = p + lane;
-        const unsigned m = __ballot_sync(0xffffffffu, q < e && !is_trim(text[q]));
-        if (m) {
-            a = p + (__ffs(m) - 1);
+    const int64_t k_first = ((int64_t)s + mis) >> 4, k_last = ((int64_t)e - 1 + mis) >> 4;
+    // First byte that is not " \t\r".
+    int64_t a = (int64_t)e;
+    for (int64_t w = k_first; s < e && w <= k_last; w += 32) {
+        const int64_t k = w + lane;
+        int64_t mine = INT64_MAX;
+        if (k <= k_last) {
+            const Chunk c = load_chunk(text, total, mis, k);
+#pragma unroll
+            for (int j = 15; j >= 0; --j) {
+                const int64_t q = k * 16 + j - mis;
+                if (q >= (int64_t)s && q < (int64_t)e && !is_trim(c.at(j))) mine = q;
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) mine = min(mine, (int64_t)__shfl_xor_sync(0xffffffffu, (long long)mine, o));
+        if (mine != INT64_MAX) {
+            a = mine;
             break;
         }
     }
-    if (a < e) {
-        for (uint64_t p = e; p > a;) {
-            const uint64_t step = p - a < 32 ? p - a : 32, lo = p - step;
-            const uint64_t q = lo + lane;
-            const unsigned m = __ballot_sync(0xffffffffu, q < p && !is_trim(text[q]));
-            if (m) {
-                b = lo + (31 - __clz(m)) + 1;
+    // Last such byte (scanning back from the end).
+    int64_t b = a;
+    if (a < (int64_t)e) {
+        const int64_t k_a = (a + mis) >> 4;
+        for (int64_t w = k_last; w >= k_a; w -= 32) {
+            const int64_t k = w - lane;
+            int64_t mine = -1;
+            if (k >= k_a) {
+                const Chunk c = load_chunk(text, total, mis, k);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int64_t q = k * 16 + j - mis;
+                    if (q >= a && q < (int64_t)e && !is_trim(c.at(j))) mine = q;
+                }
+            }
+            for (int o = 16; o > 0; o >>= 1) mine = max(mine, (int64_t)__shfl_xor_sync(0xffffffffu, (long long)mine, o));
+            if (mine >= 0) {
+                b = mine + 1;
                 break;
             }
-            p = lo;
         }
     }
     LineInfo li{};
-    li.a = a;
-    li.b = a < e ? b : a;
-    if (a >= e) {
+    li.a = (uint64_t)a;
+    li.b = (uint64_t)b;
+    if (a >= (int64_t)e) {
         li.kind = 0;
     } else if (text[a] == '#') {
         li.kind = 1;
     } else {
         li.kind = 2;
+        // Commas, and starts of space / tab separated tokens, over [a, b).
         uint32_t commas = 0, starts = 0;
-        for (uint64_t p = a; p < li.b; p += 32) {
-            const uint64_t q = p + lane;
-            const bool in = q < li.b;
-            const char c = in ? text[q] : ' ';
-            const char prev = (in && q > a) ? text[q - 1] : ' ';
-            commas += __popc(__ballot_sync(0xffffffffu, in && c == ','));
-            starts += __popc(__ballot_sync(0xffffffffu, in && !is_sep(c) && is_sep(prev)));
+        char carry_last = ' ';  // byte before this step's first chunk
+        const int64_t ka = (a + mis) >> 4, kb = (b - 1 + mis) >> 4;
+        for (int64_t w = ka; w <= kb; w += 32) {
+            const int64_t k = w + lane;
+            Chunk c;
+            if (k <= kb) {
+                c = load_chunk(text, total, mis, k);
+            } else {
+                c.w[0] = c.w[1] = c.w[2] = c.w[3] = 0x20202020u;
+            }
+            const char last = c.at(15);
+            char prev = __shfl_up_sync(0xffffffffu, last, 1);
+            if (lane == 0) prev = carry_last;
+            uint32_t cm = 0, st = 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int64_t q = k * 16 + j - mis;
+                const char ch = c.at(j);
+                const bool in = q >= a && q < b;
+                cm += (in && ch == ',') ? 1u : 0u;
+                st += (in && !is_sep(ch) && (q == a || is_sep(prev))) ? 1u : 0u;
+                prev = in ? ch : ' ';
+            }
+            for (int o = 16; o > 0; o >>= 1) {
+                cm += __shfl_xor_sync(0xffffffffu, cm, o);
+                st += __shfl_xor_sync(0xffffffffu, st, o);
+            }
+            commas += cm;
+            starts += st;
+            carry_last = __shfl_sync(0xffffffffu, last, 31);
         }
         li.comma = commas > 0;
         li.tokens = commas > 0 ? commas + 1 : starts;
@@ -182,61 +275,119 @@ __global__ void __launch_bounds__(256) line_kernel(const char *text, int64_t tot
 }
 
 // (4) one warp per data line: each token's [start, end) (before trimming).
-__global__ void __launch_bounds__(256) token_kernel(const char *text, const LineInfo *info, const int64_t *data_lines,
-                                                   int64_t n_data, int64_t len, uint64_t *tok_s, uint64_t *tok_e) {
+__global__ void __launch_bounds__(256) token_kernel(const char *text, int64_t total, const LineInfo *info,
+                                                   const int64_t *data_lines, int64_t n_data, int64_t len,
+                                                   uint64_t *tok_s, uint64_t *tok_e) {
     const int lane = threadIdx.x & 31;
     const int64_t d = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (d >= n_data) return;
+    const int mis = (int)(reinterpret_cast<uintptr_t>(text) & 15);
     const LineInfo li = info[data_lines[d]];
-    const int64_t base = d * len;
-    uint32_t k = 0;  // tokens seen so far
-    if (li.comma) {
-        if (lane == 0) tok_s[base] = li.a;
-        for (uint64_t p = li.a; p < li.b; p += 32) {
-            const uint64_t q = p + lane;
-            const bool hit = q < li.b && text[q] == ',';
-            const unsigned m = __ballot_sync(0xffffffffu, hit);
-            if (hit) {
-                const uint32_t r = k + __popc(m & ((1u << lane) - 1));
-                tok_e[base + r] = q;
-                tok_s[base + r + 1] = q + 1;
+    const int64_t a = (int64_t)li.a, b = (int64_t)li.b, base = d * len;
+    const int64_t ka = (a + mis) >> 4, kb = (b - 1 + mis) >> 4;
+    uint64_t k_tok = 0;  // tokens (comma mode: commas; space mode: starts) before this step
+    char carry_last = ' ';
+    if (li.comma && lane == 0) {
+        tok_s[base] = (uint64_t)a;
+        tok_e[base + len - 1] = (uint64_t)b;
+    }
+    for (int64_t w = ka; w <= kb; w += 32) {
+        const int64_t k = w + lane;
+        Chunk c;
+        if (k <= kb) {
+            c = load_chunk(text, total, mis, k);
+        } else {
+            c.w[0] = c.w[1] = c.w[2] = c.w[3] = 0x20202020u;
+        }
+        const char last = c.at(15);
+        char prev = __shfl_up_sync(0xffffffffu, last, 1);
+        if (lane == 0) prev = carry_last;
+        char next = __shfl_down_sync(0xffffffffu, c.at(0), 1);
+        if (lane == 31) next = (k + 1) * 16 - mis < b ? text[(k + 1) * 16 - mis] : ' ';
+        uint32_t mine = 0;
+        {
+            char p = prev;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int64_t q = k * 16 + j - mis;
+                const char ch = c.at(j);
+                const bool in = q >= a && q < b;
+                if (li.comma) mine += (in && ch == ',') ? 1u : 0u;
+                else mine += (in && !is_sep(ch) && (q == a || is_sep(p))) ? 1u : 0u;
+                p = in ? ch : ' ';
             }
-            k += __popc(m);
         }
-        if (lane == 0) tok_e[base + k] = li.b;
-    } else {
-        for (uint64_t p = li.a; p < li.b; p += 32) {
-            const uint64_t q = p + lane;
-            const bool in = q < li.b;
-            const char c = in ? text[q] : ' ';
-            const bool start = in && !is_sep(c) && (q == li.a || is_sep(text[q - 1]));
-            const bool end = in && !is_sep(c) && (q + 1 == li.b || is_sep(text[q + 1]));
-            const unsigned ms = __ballot_sync(0xffffffffu, start), me = __ballot_sync(0xffffffffu, end);
-            if (start) tok_s[base + k + __popc(ms & ((1u << lane) - 1))] = q;
-            // An end closes the token of the latest start at or before it (possibly in an earlier
-            // window): index k - 1 + (starts in this window up to and including this lane).
-            if (end) tok_e[base + k - 1 + __popc(ms & ((2u << lane) - 1))] = q + 1;
-            (void)me;
-            k += __popc(ms);
+        uint32_t step_total;
+        const uint32_t before = warp_excl_scan(mine, &step_total);
+        uint64_t idx = k_tok + before;
+        char p = prev;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int64_t q = k * 16 + j - mis;
+            const char ch = c.at(j);
+            const bool in = q >= a && q < b;
+            if (li.comma) {
+                if (in && ch == ',') {
+                    tok_e[base + idx] = (uint64_t)q;
+                    tok_s[base + idx + 1] = (uint64_t)q + 1;
+                    ++idx;
+                }
+            } else if (in && !is_sep(ch)) {
+                if (q == a || is_sep(p)) tok_s[base + idx++] = (uint64_t)q;
+                const char nx = j < 15 ? c.at(j + 1) : next;
+                if (q + 1 == b || is_sep(nx)) tok_e[base + idx - 1] = (uint64_t)q + 1;
+            }
+            p = in ? ch : ' ';
         }
+        k_tok += step_total;
+        carry_last = __shfl_sync(0xffffffffu, last, 31);
     }
 }
 
+__constant__ numparse::Recip10 c_recip;
+
+constexpr int kStage = 16384;  // bytes of token text a block stages in shared memory
+
 // (5) one thread per token: trim, parse, store f64 (and f32 when asked: @floatCast, nearest).
-__global__ void __launch_bounds__(256) parse_kernel(const char *text, const uint64_t *tok_s, const uint64_t *tok_e,
-                                                   int64_t n, double *out, float *out32) {
-    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// A block's 256 tokens are consecutive in the text: their span is staged in shared memory with
+// 16-byte loads when it fits, so each thread reads its token from there.
+__global__ void __launch_bounds__(256) parse_kernel(const char *text, int64_t total, const uint64_t *tok_s,
+                                                   const uint64_t *tok_e, int64_t n, double *out, float *out32) {
+    __shared__ __align__(16) char stage[kStage + 32];
+    __shared__ numparse::Recip10 recip;
+    __shared__ int64_t span_lo, span_hi;
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x, t = t0 + threadIdx.x;
+    const int64_t last = min(n, t0 + (int64_t)blockDim.x) - 1;
+    for (int i = threadIdx.x; i < (int)(sizeof(recip) / 16); i += blockDim.x)
+        reinterpret_cast<uint4 *>(&recip)[i] = reinterpret_cast<const uint4 *>(&c_recip)[i];
+    if (threadIdx.x == 0) {
+        span_lo = (int64_t)tok_s[t0];
+        span_hi = (int64_t)tok_e[last];
+    }
+    __syncthreads();
+    const int mis = (int)(reinterpret_cast<uintptr_t>(text) & 15);
+    const int64_t lo = span_lo, hi = span_hi;
+    // Aligned chunks covering [lo, hi): stage[0] holds text position (k_lo * 16 - mis).
+    const int64_t k_lo = (lo + mis) >> 4, k_hi = (hi - 1 + mis) >> 4;
+    const bool staged = hi > lo && (k_hi - k_lo + 1) * 16 <= kStage;
+    if (staged) {
+        for (int64_t k = k_lo + threadIdx.x; k <= k_hi; k += blockDim.x) {
+            const Chunk c = load_chunk(text, total, mis, k);
+            *reinterpret_cast<uint4 *>(stage + (k - k_lo) * 16) = make_uint4(c.w[0], c.w[1], c.w[2], c.w[3]);
+        }
+    }
+    __syncthreads();
     if (t >= n) return;
-    uint64_t a = tok_s[t], b = tok_e[t];
-    while (a < b && is_trim(text[a])) ++a;
-    while (b > a && is_trim(text[b - 1])) --b;
+    const int64_t origin = k_lo * 16 - mis;
+    const char *src = staged ? stage - origin : text;  // src[q] is text position q
+    int64_t a = (int64_t)tok_s[t], b = (int64_t)tok_e[t];
+    while (a < b && is_trim(src[a])) ++a;
+    while (b > a && is_trim(src[b - 1])) --b;
     double v;
-    if (a == b) {
-        v = numparse::quiet_nan(false);
-    } else if (b - a > (1u << 20)) {
-        v = numparse::quiet_nan(false);  // over a MiB is never a number the reader accepts
+    if (a == b || b - a > (1 << 20)) {
+        v = numparse::quiet_nan(false);  // empty, or over a MiB (never a number the reader accepts)
     } else {
-        v = numparse::parse_number(text + a, (int)(b - a));
+        v = numparse::parse_number(src + a, (int)(b - a), &recip);
     }
     if (out) out[t] = v;
     if (out32) out32[t] = (float)v;
@@ -292,6 +443,8 @@ Status pctx_init(PCtx &x, int device) {
     if (x.ready) return Status::ok();
     TSFM_CUDA(cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking), "series: stream");
     TSFM_CUDA(cudaMallocHost(reinterpret_cast<void **>(&x.h_total), 16), "series: pinned total");
+    const numparse::Recip10 r = numparse::make_recip10();
+    TSFM_CUDA(cudaMemcpyToSymbol(c_recip, &r, sizeof r), "series: reciprocals");
     x.ready = true;
     return Status::ok();
 }
@@ -304,7 +457,8 @@ struct Shape {
 // Steps (1)-(3) over text[0, n) on the device: the shape and each data line's index, or the
 // reference's error.
 Status structure(PCtx &x, const char *text, int64_t n, cudaStream_t s, Shape &sh) {
-    const int64_t tiles = std::max<int64_t>(1, (n + kTile - 1) / kTile);
+    const int mis = (int)(reinterpret_cast<uintptr_t>(text) & 15);
+    const int64_t tiles = std::max<int64_t>(1, (n + mis + kTile - 1) / kTile);
     TSFM_TRY(grow(&x.d_tile, &x.tile_cap, tiles * 4, "series: tiles"));
     TSFM_TRY(grow(&x.d_tile_off, &x.tile_off_cap, tiles * 8, "series: tiles"));
     TSFM_TRY(grow(&x.d_total, &x.total_cap, 16, "series: total"));
@@ -368,16 +522,18 @@ Status structure(PCtx &x, const char *text, int64_t n, cudaStream_t s, Shape &sh
 }
 
 // Steps (4)-(5): values (f64 and / or f32, device) of the data lines.
-Status tokens_and_values(PCtx &x, const char *text, const Shape &sh, double *out, float *out32, cudaStream_t s) {
+Status tokens_and_values(PCtx &x, const char *text, int64_t total_bytes, const Shape &sh, double *out, float *out32,
+                         cudaStream_t s) {
     const int64_t n_data = (int64_t)sh.data_lines.size(), len = (int64_t)sh.len, n = n_data * len;
     TSFM_TRY(grow(&x.d_data, &x.data_cap, (size_t)n_data * 8, "series: data lines"));
     TSFM_TRY(grow(&x.d_ts, &x.ts_cap, (size_t)n * 8, "series: tokens"));
     TSFM_TRY(grow(&x.d_te, &x.te_cap, (size_t)n * 8, "series: tokens"));
     TSFM_CUDA(cudaMemcpyAsync(x.d_data, sh.data_lines.data(), (size_t)n_data * 8, cudaMemcpyHostToDevice, s),
               "series: data lines");
-    token_kernel<<<(unsigned)((n_data + 7) / 8), 256, 0, s>>>(text, x.d_info, x.d_data, n_data, len, x.d_ts, x.d_te);
+    token_kernel<<<(unsigned)((n_data + 7) / 8), 256, 0, s>>>(text, total_bytes, x.d_info, x.d_data, n_data, len,
+                                                               x.d_ts, x.d_te);
     TSFM_CUDA(cudaGetLastError(), "series: tokens");
-    parse_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(text, x.d_ts, x.d_te, n, out, out32);
+    parse_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(text, total_bytes, x.d_ts, x.d_te, n, out, out32);
     TSFM_CUDA(cudaGetLastError(), "series: parse");
     TSFM_CUDA(cudaStreamSynchronize(s), "series: parse");
     return Status::ok();
@@ -410,7 +566,7 @@ Status parse_host(int device, const char *text, size_t length, double *values, s
         return Status::fail(TSFM_ERR_BUFFER_TOO_SMALL,
                             "series: " + std::to_string(need) + " values, capacity " + std::to_string(capacity));
     TSFM_TRY(grow(&x.d_vals, &x.vals_cap, need * 8, "series: values"));
-    TSFM_TRY(tokens_and_values(x, x.d_text, sh, x.d_vals, nullptr, x.stream));
+    TSFM_TRY(tokens_and_values(x, x.d_text, (int64_t)length, sh, x.d_vals, nullptr, x.stream));
     TSFM_CUDA(cudaMemcpyAsync(values, x.d_vals, need * 8, cudaMemcpyDeviceToHost, x.stream), "series: values out");
     TSFM_CUDA(cudaStreamSynchronize(x.stream), "series: values out");
     return Status::ok();
@@ -436,7 +592,7 @@ Status parse_device(const char *text, size_t length, double *values, float *valu
     if (capacity < need)
         return Status::fail(TSFM_ERR_BUFFER_TOO_SMALL,
                             "series: " + std::to_string(need) + " values, capacity " + std::to_string(capacity));
-    return tokens_and_values(x, text, sh, values, values32, s);
+    return tokens_and_values(x, text, (int64_t)length, sh, values, values32, s);
 }
 
 template <class F>
