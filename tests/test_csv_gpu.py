@@ -125,3 +125,32 @@ def test_chunked_full_size_digest(csvmod):
     want = ob.csv_format(v, lv)
     assert len(got) == len(want)
     assert hashlib.sha256(got).digest() == hashlib.sha256(want).digest()
+
+
+def test_csv_reads_back_bit_exactly_full_size(csvmod):
+    # Property at the bench's full size (8192 series x 1024 steps x 21 levels): the GPU reader
+    # (core/series.zig parseBlocks, f64 then f32 as the reference's toF32) turns the GPU writer's
+    # text back into exactly the forecast's f32 values; the prefix columns are the line indices.
+    import torch
+    from tsfm_b200 import series
+    rng = np.random.default_rng(99)
+    v = (rng.standard_normal((8192, 1, 1024, 21)) * 10.0 ** rng.integers(-4, 5, (8192, 1, 1, 1))).astype(np.float32)
+    lv = levels_for(21)
+    dv = torch.from_numpy(v).cuda()
+    import tsfm_b200 as tb
+    need = ctypes.c_size_t(0)
+    tb.lib.tsfm_csv_format_device(dv.data_ptr(), 8192, 1, 1024, lv.ctypes.data, 21, None, 0, ctypes.byref(need),
+                                  None)
+    text = torch.empty(need.value, dtype=torch.uint8, device="cuda")
+    n = csvmod.format_csv_device(dv.data_ptr(), 8192, 1, 1024, lv, text.data_ptr(), text.numel())
+    shape = series.parse_blocks_device(text.data_ptr(), n)
+    assert shape == (1, 8192 * 1024 + 1, 24)
+    back = torch.empty(shape[1] * shape[2], dtype=torch.float32, device="cuda")
+    series.parse_blocks_device(text.data_ptr(), n, None, back.data_ptr(), back.numel())
+    torch.cuda.synchronize()
+    back = back.view(shape[1], shape[2])
+    assert torch.isnan(back[0]).all()  # the header's tokens are not numbers
+    assert torch.equal(back[1:, 3:].contiguous().view(torch.int32), dv.view(-1, 21).view(torch.int32))
+    idx = torch.arange(8192 * 1024, device="cuda")
+    assert torch.equal(back[1:, 0], (idx // 1024).float())
+    assert torch.equal(back[1:, 2], (idx % 1024 + 1).float())
