@@ -115,63 +115,6 @@ void target_encode(const double *target, const double *past, size_t t, const dou
         }
 }
 
-struct HostRows {
-    std::vector<float> rows;   // (b * vall, t)
-    std::vector<uint8_t> mask;
-    std::vector<float> kf;     // (b * vall, hpad)
-    std::vector<uint8_t> kfm;
-};
-
-// forecastRaw's input preparation (forecaster.zig:319-388): forward-filled targets, covariate
-// rows, the last `keep` steps left-padded to a patch multiple, and the known futures.
-void prepare_rows(const float *inputs, const uint8_t *observed, size_t b, size_t v, size_t t0, size_t horizon,
-                  const float *past, size_t n_past, const float *known, size_t n_known, size_t keep, size_t t,
-                  size_t hpad, HostRows &h) {
-    const size_t vall = v + n_past + n_known, nrows = b * vall;
-    h.rows.assign(nrows * t, 0.0f);
-    h.mask.assign(nrows * t, 0);
-    h.kf.assign(nrows * hpad, 0.0f);
-    h.kfm.assign(nrows * hpad, 0);
-    for (size_t s = 0; s < b; ++s)
-        for (size_t i = 0; i < vall; ++i) {
-            const size_t r = s * vall + i;
-            float last = 0.0f;
-            bool seen = false;
-            for (size_t j = 0; j < t0; ++j) {
-                float val;
-                bool ob;
-                if (i < v) {
-                    const size_t idx = (s * v + i) * t0 + j;
-                    if (observed[idx]) {
-                        last = inputs[idx];
-                        seen = true;
-                    }
-                    val = seen ? last : 0.0f;
-                    ob = observed[idx] != 0;
-                } else if (i < v + n_past) {
-                    const float x = past[(s * n_past + (i - v)) * t0 + j];
-                    ob = !std::isnan(x);
-                    val = ob ? x : 0.0f;
-                } else {
-                    const float x = known[(s * n_known + (i - v - n_past)) * (t0 + horizon) + j];
-                    ob = !std::isnan(x);
-                    val = ob ? x : 0.0f;
-                }
-                if (j >= t0 - keep) {
-                    const size_t dst = r * t + (t - keep) + (j - (t0 - keep));
-                    h.rows[dst] = val;
-                    h.mask[dst] = ob;
-                }
-            }
-            if (i >= v + n_past)
-                for (size_t j = 0; j < horizon; ++j) {
-                    const float x = known[(s * n_known + (i - v - n_past)) * (t0 + horizon) + t0 + j];
-                    h.kfm[r * hpad + j] = !std::isnan(x);
-                    h.kf[r * hpad + j] = h.kfm[r * hpad + j] ? x : 0.0f;
-                }
-        }
-}
-
 // ---------------------------------------------------------------------------------------------
 // Device forward
 
@@ -611,43 +554,7 @@ Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inpu
     const size_t t = (keep + ps - 1) / ps * ps;
     const size_t hpad = (horizon + ps - 1) / ps * ps;
     const int passes = o.symmetric_averaging ? 2 : 1;
-    HostRows fwd, mir;
-    prepare_rows(inputs, observed, b, v, t0, horizon, past_rows.data(), n_past, known_rows.data(), n_known, keep, t,
-                 hpad, fwd);
-    if (passes == 2) {
-        std::vector<float> neg(b * v * t0), npast(past_rows.size()), nknown(known_rows.size());
-        for (size_t i = 0; i < neg.size(); ++i) neg[i] = -inputs[i];
-        for (size_t i = 0; i < npast.size(); ++i) npast[i] = -past_rows[i];
-        for (size_t i = 0; i < nknown.size(); ++i) nknown[i] = -known_rows[i];
-        prepare_rows(neg.data(), observed, b, v, t0, horizon, npast.data(), n_past, nknown.data(), n_known, keep, t,
-                     hpad, mir);
-    }
     const int64_t groups = (int64_t)b * passes, R = groups * (int64_t)vall;
-    std::vector<float> rows0(R * t), kf(R * hpad);
-    std::vector<uint8_t> mask0(R * t), kfm(R * hpad);
-    std::memcpy(rows0.data(), fwd.rows.data(), fwd.rows.size() * 4);
-    std::memcpy(mask0.data(), fwd.mask.data(), fwd.mask.size());
-    std::memcpy(kf.data(), fwd.kf.data(), fwd.kf.size() * 4);
-    std::memcpy(kfm.data(), fwd.kfm.data(), fwd.kfm.size());
-    if (passes == 2) {
-        std::memcpy(rows0.data() + fwd.rows.size(), mir.rows.data(), mir.rows.size() * 4);
-        std::memcpy(mask0.data() + fwd.mask.size(), mir.mask.data(), mir.mask.size());
-        std::memcpy(kf.data() + fwd.kf.size(), mir.kf.data(), mir.kf.size() * 4);
-        std::memcpy(kfm.data() + fwd.kfm.size(), mir.kfm.data(), mir.kfm.size());
-    }
-    // Non-negative clip flags per (series, variate) (forecaster.zig:163-180).
-    std::vector<uint8_t> clip_row(b * v, 0);
-    if (o.clip_nonnegative)
-        for (size_t rr = 0; rr < b * v; ++rr) {
-            bool any = false, nonneg = true;
-            for (size_t i = 0; i < t0; ++i)
-                if (observed[rr * t0 + i] && std::isfinite(inputs[rr * t0 + i])) {
-                    any = true;
-                    nonneg = nonneg && inputs[rr * t0 + i] >= 0;
-                }
-            clip_row[rr] = any && nonneg;
-        }
-
     // Roles of one series' rows: targets, past-only, known-future.
     std::vector<int8_t> roles(vall);
     for (size_t i = 0; i < vall; ++i) roles[i] = i < v ? 0 : (i < v + n_past ? 1 : 2);
@@ -660,7 +567,8 @@ Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inpu
     size_t fc_bytes = Arena::span(R * t * 4) + Arena::span(R * t) + 2 * Arena::span(R * max_t * 4) +
                       2 * Arena::span(R * max_t) + Arena::span(R * hpad * 4) + Arena::span(R * hpad) +
                       Arena::span(nt * horizon * q * 4) * 2 + Arena::span(nt * o.per_shot_horizon_patches * ps * q * 4) +
-                      Arena::span(b * v) + Arena::span(vall) + Arena::span(16);
+                      Arena::span(b * v) + Arena::span(vall) + Arena::span(16) + Arena::span(b * v * t0 * 4) +
+                      Arena::span(b * v * t0) + Arena::span(past_rows.size() * 4) + Arena::span(known_rows.size() * 4);
     TSFM_TRY(r.fc.reserve(fc_bytes));
     Arena &fc = r.fc;
     fc.reset();
@@ -676,16 +584,49 @@ Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inpu
     uint8_t *d_clip = fc.take<uint8_t>(b * v);
     int8_t *d_roles = fc.take<int8_t>(vall);
     int *d_nan = fc.take<int>(4);
+    float *d_in = fc.take<float>(b * v * t0);
+    uint8_t *d_obs = fc.take<uint8_t>(b * v * t0);
+    float *d_past = fc.take<float>(past_rows.size());
+    float *d_known = fc.take<float>(known_rows.size());
     if (fc.used > fc.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Timestral: forecaster buffers too small");
     cudaStream_t s = r.stream;
-    TSFM_CUDA(cudaMemcpyAsync(d_rows0, rows0.data(), rows0.size() * 4, cudaMemcpyHostToDevice, s), "timestral: rows");
-    TSFM_CUDA(cudaMemcpyAsync(d_mask0, mask0.data(), mask0.size(), cudaMemcpyHostToDevice, s), "timestral: mask");
-    TSFM_CUDA(cudaMemcpyAsync(ctx_a, rows0.data(), rows0.size() * 4, cudaMemcpyHostToDevice, s), "timestral: rows");
-    TSFM_CUDA(cudaMemcpyAsync(msk_a, mask0.data(), mask0.size(), cudaMemcpyHostToDevice, s), "timestral: mask");
-    TSFM_CUDA(cudaMemcpyAsync(d_kf, kf.data(), kf.size() * 4, cudaMemcpyHostToDevice, s), "timestral: known");
-    TSFM_CUDA(cudaMemcpyAsync(d_kfm, kfm.data(), kfm.size(), cudaMemcpyHostToDevice, s), "timestral: known");
-    TSFM_CUDA(cudaMemcpyAsync(d_clip, clip_row.data(), clip_row.size(), cudaMemcpyHostToDevice, s), "timestral: clip");
+    // The raw arrays go up once; the rows (both passes), masks, known futures and clip flags are
+    // built on the device.
+    TSFM_CUDA(cudaMemcpyAsync(d_in, inputs, b * v * t0 * 4, cudaMemcpyHostToDevice, s), "timestral: inputs");
+    TSFM_CUDA(cudaMemcpyAsync(d_obs, observed, b * v * t0, cudaMemcpyHostToDevice, s), "timestral: observed");
+    if (!past_rows.empty())
+        TSFM_CUDA(cudaMemcpyAsync(d_past, past_rows.data(), past_rows.size() * 4, cudaMemcpyHostToDevice, s),
+                  "timestral: past covariates");
+    if (!known_rows.empty())
+        TSFM_CUDA(cudaMemcpyAsync(d_known, known_rows.data(), known_rows.size() * 4, cudaMemcpyHostToDevice, s),
+                  "timestral: known covariates");
     TSFM_CUDA(cudaMemcpyAsync(d_roles, roles.data(), vall, cudaMemcpyHostToDevice, s), "timestral: roles");
+    {
+        TsPrepareCall pc;
+        pc.inputs = d_in;
+        pc.observed = d_obs;
+        pc.past = n_past ? d_past : nullptr;
+        pc.known = n_known ? d_known : nullptr;
+        pc.b = (int64_t)b;
+        pc.v = (int64_t)v;
+        pc.n_past = (int64_t)n_past;
+        pc.n_known = (int64_t)n_known;
+        pc.t0 = (int64_t)t0;
+        pc.horizon = (int64_t)horizon;
+        pc.keep = (int64_t)keep;
+        pc.t = (int64_t)t;
+        pc.hpad = (int64_t)hpad;
+        pc.passes = passes;
+        pc.rows = d_rows0;
+        pc.rows2 = ctx_a;
+        pc.mask = d_mask0;
+        pc.mask2 = msk_a;
+        pc.kf = d_kf;
+        pc.kfm = d_kfm;
+        pc.clip = o.clip_nonnegative ? d_clip : nullptr;
+        LaunchScope ls(r, s, K_PATCH, (double)R * t * 10);
+        TSFM_TRY(launch_ts_prepare(pc, s));
+    }
     TSFM_CUDA(cudaMemsetAsync(d_nan, 0, 16, s), "timestral: nan flag");
     w.roles = d_roles;
 

@@ -155,6 +155,87 @@ __global__ void ts_rope_kernel(const int *first_obs, int64_t groups, int64_t sl,
     }
 }
 
+// One warp per output row, 32 steps per iteration: the forward fill takes, for each lane, the
+// value of the last observed step at or before it in this chunk (a ballot), else the carry from
+// the previous chunks.
+__global__ void __launch_bounds__(256) ts_prepare_kernel(TsPrepareCall c) {
+    const int lane = threadIdx.x & 31;
+    const int64_t vall = c.v + c.n_past + c.n_known, per_pass = c.b * vall;
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (r >= per_pass * c.passes) return;
+    const bool neg = r >= per_pass;
+    const int64_t rr = r % per_pass, s = rr / vall, i = rr % vall;
+    const int64_t first = c.t0 - c.keep, pad = c.t - c.keep;
+    float *row = c.rows + r * c.t;
+    uint8_t *msk = c.mask + r * c.t;
+    float *row2 = c.rows2 ? c.rows2 + r * c.t : nullptr;
+    uint8_t *msk2 = c.mask2 ? c.mask2 + r * c.t : nullptr;
+    for (int64_t j = lane; j < pad; j += 32) {
+        row[j] = 0.0f;
+        msk[j] = 0;
+        if (row2) row2[j] = 0.0f, msk2[j] = 0;
+    }
+    if (i < c.v) {
+        const float *x = c.inputs + (s * c.v + i) * c.t0;
+        const uint8_t *ob = c.observed + (s * c.v + i) * c.t0;
+        float carry = 0.0f;
+        bool seen = false, any = false, nonneg = true;
+        for (int64_t j0 = 0; j0 < c.t0; j0 += 32) {
+            const int64_t j = j0 + lane;
+            const bool in = j < c.t0;
+            const bool o = in && ob[j] != 0;
+            const float raw = in ? x[j] : 0.0f;
+            const float val = neg ? -raw : raw;
+            if (o && isfinite(raw)) {
+                any = true;
+                nonneg = nonneg && raw >= 0.0f;
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, o);
+            const unsigned upto = m & (0xffffffffu >> (31 - lane));
+            const float from = __shfl_sync(0xffffffffu, val, upto ? 31 - __clz(upto) : 0);
+            const float filled = upto ? from : (seen ? carry : 0.0f);
+            if (in && j >= first) {
+                row[pad + j - first] = filled;
+                msk[pad + j - first] = o ? 1 : 0;
+                if (row2) row2[pad + j - first] = filled, msk2[pad + j - first] = o ? 1 : 0;
+            }
+            if (m) {
+                carry = __shfl_sync(0xffffffffu, val, 31 - __clz(m));
+                seen = true;
+            }
+        }
+        if (c.clip && !neg) {
+            const bool a = __any_sync(0xffffffffu, any), nn = __all_sync(0xffffffffu, nonneg);
+            if (lane == 0) c.clip[s * c.v + i] = a && nn;
+        }
+    } else {
+        const bool is_past = i < c.v + c.n_past;
+        const float *x = is_past ? c.past + (s * c.n_past + (i - c.v)) * c.t0
+                                 : c.known + (s * c.n_known + (i - c.v - c.n_past)) * (c.t0 + c.horizon);
+        for (int64_t j = first + lane; j < c.t0; j += 32) {
+            const float raw = x[j], val = neg ? -raw : raw;
+            const bool o = !isnan(val);
+            row[pad + j - first] = o ? val : 0.0f;
+            msk[pad + j - first] = o ? 1 : 0;
+            if (row2) row2[pad + j - first] = o ? val : 0.0f, msk2[pad + j - first] = o ? 1 : 0;
+        }
+    }
+    // Known futures (zeros for the other rows and past the horizon).
+    const bool known_row = i >= c.v + c.n_past;
+    const float *xf = known_row ? c.known + (s * c.n_known + (i - c.v - c.n_past)) * (c.t0 + c.horizon) + c.t0 : nullptr;
+    for (int64_t j = lane; j < c.hpad; j += 32) {
+        float val = 0.0f;
+        uint8_t o = 0;
+        if (known_row && j < c.horizon) {
+            const float raw = xf[j], x = neg ? -raw : raw;
+            o = !isnan(x);
+            val = o ? x : 0.0f;
+        }
+        c.kf[r * c.hpad + j] = val;
+        c.kfm[r * c.hpad + j] = o;
+    }
+}
+
 // Per-block row maps (model.zig:379-410, 600): the bidirectional flag of every row (known-future
 // rows of a covariate window), and for each target row (the first v rows of each group, in order)
 // its index and the indices of its h decoder tokens in the (rows * sl) token matrix.
@@ -657,6 +738,15 @@ Status launch_ts_rope(const int *first_obs, int64_t groups, int64_t sl, int64_t 
                       int half, float *cs, float *sn, cudaStream_t s) {
     ts_rope_kernel<<<grid_for(groups * sl * half, 256), 256, 0, s>>>(first_obs, groups, sl, ne, l, inv_freq, half, cs, sn);
     TSFM_CUDA(cudaGetLastError(), "timestral rope: launch");
+    return Status::ok();
+}
+
+Status launch_ts_prepare(const TsPrepareCall &c, cudaStream_t s) {
+    const int64_t rows = (c.v + c.n_past + c.n_known) * c.b * c.passes;
+    if (rows <= 0) return Status::ok();
+    if (c.keep > c.t0 || c.keep > c.t) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "timestral prepare: keep");
+    ts_prepare_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(c);
+    TSFM_CUDA(cudaGetLastError(), "timestral prepare: launch");
     return Status::ok();
 }
 

@@ -31,6 +31,26 @@ Status launch_ts_stats(const TsStatsCall &c, float *feats, cudaStream_t s);
 
 Status launch_ts_rope(const int *first_obs, int64_t groups, int64_t sl, int64_t ne, int64_t l, const float *inv_freq,
                       int half, float *cs, float *sn, cudaStream_t s);
+// forecastRaw's input rows (forecaster.zig:319-388) built on the device from the raw arrays:
+// per (pass, series, row) the last `keep` steps left-padded to t, targets forward-filled from their
+// last observed step (0 before the first), covariates with NaN as unobserved (0), the known
+// futures; the second pass (symmetric averaging) negates every value. Optionally the non-negative
+// clip flag per (series, target) (forecaster.zig:163-180).
+struct TsPrepareCall {
+    const float *inputs = nullptr;     // (b, v, t0)
+    const uint8_t *observed = nullptr; // (b, v, t0)
+    const float *past = nullptr;       // (b, n_past, t0) or null
+    const float *known = nullptr;      // (b, n_known, t0 + horizon) or null
+    int64_t b = 0, v = 0, n_past = 0, n_known = 0, t0 = 0, horizon = 0, keep = 0, t = 0, hpad = 0;
+    int passes = 1;
+    float *rows = nullptr, *rows2 = nullptr;    // (passes * b * vall, t); rows2: optional copy
+    uint8_t *mask = nullptr, *mask2 = nullptr;  // same shape
+    float *kf = nullptr;                        // (passes * b * vall, hpad)
+    uint8_t *kfm = nullptr;
+    uint8_t *clip = nullptr;                    // (b * v) or null
+};
+Status launch_ts_prepare(const TsPrepareCall &c, cudaStream_t s);
+
 // Row flags and head / target row indices of one block; target rows are the first v of every
 // group of vall rows (role 0).
 Status launch_ts_rows(const int8_t *roles, int64_t rows, int vall, int v, int64_t sl, int64_t ne, int h, bool cov,

@@ -135,13 +135,14 @@ class Model:
         `observed` defaults to the finite entries of `inputs` (unobserved steps are passed as 0,
         as the reference expects). `cov` is a `covariates(...)` pair or None; `opts` a
         `timestral_options(...)` struct or None for the defaults."""
-        x = np.array(inputs, dtype=np.float32, copy=True)
+        x = np.ascontiguousarray(inputs, dtype=np.float32)
         if x.ndim != 3:
             raise ValueError("inputs must be (series, variates, steps)")
         if observed is None:
             observed = np.isfinite(x)
-        obs = np.ascontiguousarray(observed, dtype=np.uint8)
-        x[obs == 0] = 0.0
+        obs = observed.view(np.uint8) if (isinstance(observed, np.ndarray) and observed.dtype == np.bool_
+                                          and observed.flags.c_contiguous) else np.ascontiguousarray(observed, np.uint8)
+        # The library reads inputs only where observed, so unobserved steps need no zero fill.
         b, v, t = x.shape
         if out is None:
             out = np.empty((b, v, horizon, self.num_quantiles), np.float32)
