@@ -49,7 +49,8 @@ def parse_args():
     ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
     ap.add_argument("--csv-series", type=int, default=8192, help="series of the csv workload")
     ap.add_argument("--workload", default="chronos2",
-                    choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv", "parse"],
+                    choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv", "parse",
+                             "attention"],
                     help="chronos2 is the headline; bolt-*/timestral are BASELINE.json's other configs, timed "
                          "through the host entry points (copies included); sweep is its Chronos-2 throughput sweep "
                          "(batch x context, one JSON line per point); csv renders the CLI's CSV output of an "
@@ -501,6 +502,47 @@ def run_parse(a):
     print(json.dumps(line), flush=True)
 
 
+def run_attention(a):
+    """The self-attention kernel alone at the families' shapes (tsfm_kernel_attention, CUDA events,
+    L2 flushed between launches): Chronos-2 (256 sequences of 577 tokens, 12 heads, key-validity
+    mask) and Chronos-Bolt-base (4096 sequences of 129 tokens, 12 heads, relative-position bias).
+    TFLOP/s counts 4 * n^2 * 64 per (sequence, head), the useful work only."""
+    import torch
+    import tsfm_b200 as tb
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    burst = peaks()[0]
+    for name, G, n, heads, rel in (("chronos2", 256, 577, 12, False), ("bolt-base", a.csv_series // 2, 129, 12, True)):
+        g = torch.Generator(device="cuda").manual_seed(7)
+        ld = 3 * heads * 64
+        qkv = (torch.randn(G * n, ld, device="cuda", generator=g) * 0.5).half()
+        kv = (torch.rand(G, n, device="cuda", generator=g) > 0.05).to(torch.uint8)
+        relb = torch.randn(heads, 2 * n - 1, device="cuda", generator=g) if rel else None
+        o = torch.empty(G * n, heads * 64, device="cuda", dtype=torch.float16)
+        run = lambda: tb.check(tb.lib.tsfm_kernel_attention(
+            qkv.data_ptr(), qkv.data_ptr() + heads * 64 * 2, qkv.data_ptr() + 2 * heads * 64 * 2, ld, o.data_ptr(),
+            heads * 64, kv.data_ptr(), None if relb is None else relb.data_ptr(), G, heads, n, 0.125, 0, 1,
+            stream.cuda_stream))
+        for _ in range(max(3, a.warmup)):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        total, steps = 0.0, max(3, a.steps)
+        for _ in range(steps):
+            flush.zero_()
+            e0.record(stream)
+            run()
+            e1.record(stream)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        ms = total / steps
+        tf = 4.0 * n * n * 64 * heads * G / (ms / 1e3) / 1e12
+        print(json.dumps({"workload": "attention", "shape": name, "sequences": G, "tokens": n, "heads": heads,
+                          "rel_bias": rel, "ms": ms, "tflops": tf, "tc_peak_frac": tf / burst,
+                          "us_per_sequence_head": ms * 1e3 / (G * heads)}), flush=True)
+        del qkv, o
+
+
 def main():
     a = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -510,7 +552,8 @@ def main():
         return run_reference(a, rank)
     if a.workload != "chronos2":
         if rank == 0:
-            {"sweep": run_sweep, "csv": run_csv, "parse": run_parse}.get(a.workload, run_family_workload)(a)
+            {"sweep": run_sweep, "csv": run_csv, "parse": run_parse, "attention": run_attention}.get(
+                a.workload, run_family_workload)(a)
         return
 
     import torch
