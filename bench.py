@@ -278,7 +278,6 @@ def run_family_workload(a):
         b, horizon, ctx = 128, 512, 4096
     w = syn.random_checkpoint(cfg, seed=20261201)
     model = Model(cfg, w)
-    del w
     if a.workload.startswith("bolt"):
         x = torch.from_numpy(syn.seeded_series(b, ctx, seed=2000)).pin_memory().numpy()
         out = torch.empty((b, horizon, 9), dtype=torch.float32).pin_memory().numpy()
@@ -312,6 +311,23 @@ def run_family_workload(a):
     cls = {c: model.profile_read(c) for c in ("gemm", "attention", "rmsnorm", "patch", "head", "other")}
     model.profile(False)
     kernels = {c: {"launches": v["launches"], "ms": v["ms"]} for c, v in cls.items() if v["launches"]}
+    # CPU baseline: the oracle (the reference algorithm restated, all host threads) on a bounded
+    # sample of the same workload.
+    from oracle import binding as ob
+    from tsfm_b200 import config as cm, tensor_table
+    ob.set_threads(os.cpu_count() or 1)
+    om = ob.OracleModel(cm.parse(cfg), w, tensor_table)
+    if a.workload.startswith("bolt"):
+        ns = 16 if a.workload == "bolt-small" else 2
+        t0 = time.perf_counter()
+        om.forecast_bolt(x[:ns], horizon)
+    else:
+        ns = 1
+        sub_cov = covariates(past=past[:ns], known=known[:ns])
+        t0 = time.perf_counter()
+        om.forecast_timestral(xs[:ns], np.isfinite(xs[:ns]), horizon, cov=sub_cov[0], opts=opts)
+    cpu_dt = time.perf_counter() - t0
+    del om, w
     line = {"metric": f"forecast series/sec ({a.workload}, BASELINE.json config)", "value": b / (ms / 1e3),
             "unit": "series/s", "n_gpus": 1, "steps": steps, "ms_per_step": ms, "higher_is_better": True,
             "dtype": "f16", "data": "synthetic (seeded series, random-init N(0,0.02) weights)",
@@ -319,7 +335,9 @@ def run_family_workload(a):
                        "timing": "host entry point, pinned buffers, copies included"},
             "e2e": {"value": b / (ms / 1e3), "unit": "series/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": model.last_launch_count(), "kernels": kernels}
+            "gpu_launches": model.last_launch_count(), "kernels": kernels,
+            "cpu_baseline": {"value": ns / cpu_dt, "unit": "series/s", "cores": ob.get_threads(), "kind": "port",
+                             "sample": f"{ns} series of the same workload (oracle restatement)"}}
     print(json.dumps(line), flush=True)
     model.close()
 
