@@ -175,14 +175,6 @@ TSFM_HD int decimal_length(uint32_t v) {
     }
     return n;
 }
-TSFM_HD int u64_length(uint64_t v) {
-    int n = 1;
-    while (v >= 10) {
-        v /= 10;
-        ++n;
-    }
-    return n;
-}
 
 // A formatted f32: sign, kind and digits; `len` is the byte count of its text.
 struct F32Text {
@@ -273,7 +265,7 @@ TSFM_HD void emit(const F32Text &f, char *p) {
     }
 }
 
-// Writes the decimal text of v at p (u64_length(v) bytes).
+// Writes the `len` decimal digits of v at p (len = its digit count).
 TSFM_HD void emit_u64(uint64_t v, int len, char *p) {
     for (int i = len - 1; i >= 0; --i) {
         p[i] = (char)('0' + v % 10);
