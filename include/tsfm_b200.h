@@ -289,6 +289,14 @@ int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64
                               const float *rel_bias, int32_t groups, int32_t heads, int32_t n,
                               float scale, int32_t mask_mode, int32_t dtype, void *stream);
 
+/* tsfm_kernel_target_encode: Timestral's categorical target encoding (timestral/forecaster.zig:
+ * 201-238) on device pointers: inputs (b, t) f32 and observed (b, t) u8 of a univariate target,
+ * codes (b, nc, len) f64 with len = t (past) or t + horizon (known); out (b, nc, len) f32.
+ * have_target == 0 only rounds the codes. The forecaster runs the same kernels. */
+int32_t tsfm_kernel_target_encode(const float *inputs, const uint8_t *observed, int64_t b, int64_t t,
+                                  int64_t max_context, const double *codes, int64_t nc, int64_t len,
+                                  int32_t have_target, float *out, void *stream);
+
 /* tsfm_kernel_rmsnorm: out[r, :] = x[r, :] / sqrt(mean(x^2) + eps) * scale, x f32, out bf16 or
  * f32 (out_dtype). Replaces nn.rmsNorm (core/nn.zig:367-396). */
 int32_t tsfm_kernel_rmsnorm(const float *x, const float *scale, void *out, int32_t out_dtype,

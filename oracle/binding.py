@@ -35,6 +35,7 @@ def _load():
                                       ctypes.POINTER(SZ)]),
         "oracle_linear": (I32, [P, P, P, P, SZ, SZ, SZ]),
         "oracle_rmsnorm": (I32, [P, P, P, SZ, SZ, F]),
+        "oracle_target_encode": (I32, [P, P, SZ, SZ, SZ, P, SZ, SZ, I32, P]),
         "oracle_f32_digits_batch": (None, [P, SZ, P, P]),
         "oracle_f32_digits_search_batch": (None, [P, SZ, P, P]),
         "oracle_f32_text": (SZ, [F, ctypes.c_char_p]),

@@ -1883,6 +1883,40 @@ int32_t oracle_mask_pick(int32_t causal, int32_t all_keys_valid, int32_t additiv
     return (int32_t)mask_pick(causal != 0, all_keys_valid != 0, additive != 0);
 }
 
+// encodingTarget + encodeCategorical (timestral/forecaster.zig:201-238) for one kind of
+// categorical covariate: codes (b, nc, len), len = t (past) or t + horizon (known); out f32 of the
+// same shape. With have_target == 0 the codes are only rounded.
+int32_t oracle_target_encode(const float *inputs, const uint8_t *observed, size_t b, size_t t, size_t max_context,
+                             const double *codes, size_t nc, size_t len, int32_t have_target, float *out) {
+    std::vector<double> target(b * t);
+    for (size_t s = 0; s < b; ++s) {
+        bool started = false;
+        float last = 0.0f;
+        for (size_t i = 0; i < t; ++i) {
+            if (observed[s * t + i]) {
+                started = true;
+                last = inputs[s * t + i];
+            }
+            const bool in_window = t <= max_context || i >= t - max_context;
+            target[s * t + i] = started && in_window ? (double)last : std::nan("");
+        }
+    }
+    for (size_t s = 0; s < b; ++s)
+        for (size_t j = 0; j < nc; ++j) {
+            const double *row = codes + (s * nc + j) * len;
+            float *dst = out + (s * nc + j) * len;
+            if (!have_target) {
+                for (size_t i = 0; i < len; ++i) dst[i] = (float)row[i];
+                continue;
+            }
+            Timestral::target_encode(&target[s * t], row, t, len > t ? row + t : nullptr, len - t, dst,
+                                     len > t ? dst + t : nullptr);
+            for (size_t i = 0; i < t; ++i)
+                if (std::isnan(target[s * t + i]) && std::isnan(row[i])) dst[i] = std::nanf("");
+        }
+    return 0;
+}
+
 // series.parseBlocks (core/series.zig:21-68).
 int32_t oracle_parse_blocks(const char *text, double *values, size_t cap, size_t *blocks_out,
                             size_t *rows_out, size_t *len_out) {

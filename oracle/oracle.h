@@ -59,6 +59,10 @@ int32_t oracle_mask_pick(int32_t causal, int32_t all_keys_valid, int32_t additiv
  * nonzero error codes: 1 RaggedInput, 2 RaggedBlocks, 3 EmptyInput, 4 capacity. */
 int32_t oracle_parse_blocks(const char *text, double *values, size_t cap, size_t *blocks,
                             size_t *rows, size_t *len);
+/* Timestral's categorical target encoding (forecaster.zig:201-238) for one kind of covariate. */
+int32_t oracle_target_encode(const float *inputs, const uint8_t *observed, size_t b, size_t t,
+                             size_t max_context, const double *codes, size_t nc, size_t len,
+                             int32_t have_target, float *out);
 /* nn.linear (y = x W^T + b) and nn.rmsNorm, for kernel-level parity tests. */
 int32_t oracle_linear(const float *x, const float *w, const float *bias, float *y, size_t rows,
                       size_t out, size_t in);

@@ -185,3 +185,37 @@ def test_asymmetric_quantiles_error():
     assert e.value.name == "ASYMMETRIC_QUANTILES"
     out = gpu.forecast_timestral(x, 16, opts=tb.timestral_options(symmetric_averaging=False))
     assert out.shape == (2, 1, 16, 5) and np.isfinite(out).all()
+
+
+@pytest.mark.parametrize("max_context,have_target", [(10 ** 9, 1), (300, 1), (64, 1), (10 ** 9, 0)])
+def test_target_encoding_bit_exact(max_context, have_target):
+    """The device categorical target encoding (forecaster.zig:201-238) equals the oracle's bit for
+    bit: NaN and infinite codes (their own slot in the context, the mean or the NaN slot in the
+    future), codes never seen in the context, unobserved steps before the first observation, and a
+    --max-context window that blanks the target before it."""
+    import ctypes
+    import torch
+    rng = np.random.default_rng(17 + max_context % 97)
+    b, t, horizon, nc = 5, 700, 64, 3
+    x = (rng.standard_normal((b, t)) * 10).astype(np.float32)
+    obs = (rng.random((b, t)) > 0.2).astype(np.uint8)
+    obs[:, :25] = 0
+    codes = rng.integers(0, 6, (b, nc, t + horizon)).astype(np.float64)
+    codes[rng.random(codes.shape) < 0.05] = np.nan
+    codes[:, 1, 100:110] = np.inf
+    codes[:, 2, 200:205] = -np.inf
+    codes[:, :, t + 10:t + 20] = 42.0      # never in the context
+    codes[:, 0, t + 30:t + 33] = np.inf    # not finite in the future: the mean
+    codes[:, 0, 5] = -0.0                  # equal to 0.0
+    for kind_len in (t, t + horizon):
+        cc = np.ascontiguousarray(codes[:, :, :kind_len])
+        want = np.empty_like(cc, dtype=np.float32)
+        ob.check(ob.lib.oracle_target_encode(x.ctypes.data, obs.ctypes.data, b, t, max_context, cc.ctypes.data, nc,
+                                             kind_len, have_target, want.ctypes.data))
+        dx, do, dc = torch.from_numpy(x).cuda(), torch.from_numpy(obs).cuda(), torch.from_numpy(cc).cuda()
+        out = torch.empty(cc.shape, dtype=torch.float32, device="cuda")
+        tb.check(tb.lib.tsfm_kernel_target_encode(dx.data_ptr(), do.data_ptr(), b, t, max_context, dc.data_ptr(), nc,
+                                                  kind_len, have_target, out.data_ptr(),
+                                                  torch.cuda.current_stream().cuda_stream))
+        got = out.cpu().numpy()
+        assert ((np.isnan(got) & np.isnan(want)) | (got.view(np.uint32) == want.view(np.uint32))).all()

@@ -9,6 +9,7 @@
 #include <thread>
 
 #include "model.h"
+#include "timestral_kernels.h"
 
 using namespace tsfm;
 
@@ -603,6 +604,29 @@ int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64
         c.l = n;
         c.err = kernel_err_word();
         return launch_attention(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t tsfm_kernel_target_encode(const float *inputs, const uint8_t *observed, int64_t b, int64_t t,
+                                  int64_t max_context, const double *codes, int64_t nc, int64_t len,
+                                  int32_t have_target, float *out, void *stream) {
+    return guarded([&]() -> Status {
+        if (!codes || !out || (have_target && (!inputs || !observed)))
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        if (b <= 0 || t <= 0 || nc <= 0 || len < t) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "target encode: shape");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        double *target = nullptr;
+        if (have_target) {
+            TSFM_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&target), (size_t)(b * t) * 8, s), "target encode: scratch");
+            const Status st = launch_ts_target(inputs, observed, b, t, max_context, target, s);
+            if (!st) {
+                cudaFreeAsync(target, s);
+                return st;
+            }
+        }
+        const Status st = launch_ts_cat_encode(codes, b, nc, len, t, target, out, nc, 0, s);
+        if (target) TSFM_CUDA(cudaFreeAsync(target, s), "target encode: scratch");
+        return st;
     });
 }
 

@@ -1,11 +1,11 @@
 // Timestral on the device: the decoder-only time/variate transformer of timestral/model.zig and
 // the block-autoregressive forecaster of timestral/forecaster.zig.
 //
-// Host side (C++, per series; timestral/forecaster.zig:57-141, 201-421): options, categorical
-// target encoding, covariate channels, the mirrored inputs of the symmetric pass, forward-fill and
-// left padding to a patch multiple. Both passes of the symmetric average are batched as one
-// device run over twice the series (series are independent).
-// Device side: per block, statistics + features, patch embedding, the transformer over
+// Host side (C++; timestral/forecaster.zig:57-141): options and argument checks, the uploads of the
+// raw arrays. Device side, once per forecast: categorical target encoding and the covariate
+// channels, the input rows of the forward and mirrored passes (forward fill, left padding to a
+// patch multiple; both passes of the symmetric average batched as one run over twice the series);
+// then per block: statistics + features, patch embedding, the transformer over
 // [Enc ; Dec] tokens (fused QKV|gate GEMM with partial RoPE in its epilogue, flash attention with
 // the encoder causal_keys / decoder-chain masks, 11x11 variate attention, gated output, SwiGLU
 // MLP), the FP32-accurate head with the monotone quantile construction, the refine frame, the
@@ -62,57 +62,6 @@ int median_index(const tsfm_config &c) {
     for (int i = 0; i < c.num_quantiles; ++i)
         if (c.quantiles[i] == 0.5) return i;
     return 0;
-}
-
-// ---------------------------------------------------------------------------------------------
-// Host preprocessing (timestral/forecaster.zig)
-
-long slot_of(const std::vector<double> &cats, double code) {
-    if (std::isnan(code)) return -1;
-    auto it = std::lower_bound(cats.begin(), cats.end(), code);
-    return it != cats.end() && *it == code ? it - cats.begin() : -1;
-}
-
-// targetEncode (forecaster.zig:243-289), smooth = 1.
-void target_encode(const double *target, const double *past, size_t t, const double *future, size_t nf, float *out_past,
-                   float *out_future) {
-    double item_count = 0, item_sum = 0;
-    for (size_t i = 0; i < t; ++i)
-        if (std::isfinite(target[i])) {
-            item_count += 1;
-            item_sum += target[i];
-        }
-    const double mean = item_count > 0 ? item_sum / item_count : 0.0;
-    std::vector<double> cats;
-    for (size_t i = 0; i < t; ++i)
-        if (std::isfinite(past[i])) cats.push_back(past[i]);
-    std::sort(cats.begin(), cats.end());
-    cats.erase(std::unique(cats.begin(), cats.end()), cats.end());
-    const size_t nc = cats.size();
-    std::vector<double> sums(nc + 1, 0.0), counts(nc + 1, 0.0);
-    for (size_t i = 0; i < t; ++i) {
-        if (!std::isfinite(target[i])) continue;
-        const long s = slot_of(cats, past[i]);
-        const size_t slot = s < 0 ? nc : (size_t)s;
-        sums[slot] += target[i];
-        counts[slot] += 1;
-    }
-    for (size_t i = 0; i < t; ++i) {
-        const long s = slot_of(cats, past[i]);
-        const size_t slot = s < 0 ? nc : (size_t)s;
-        out_past[i] = (float)((mean + sums[slot]) / (1.0 + counts[slot]));
-    }
-    if (future)
-        for (size_t i = 0; i < nf; ++i) {
-            double v;
-            if (std::isnan(future[i])) {
-                v = (mean + sums[nc]) / (1.0 + counts[nc]);
-            } else {
-                const long s = slot_of(cats, future[i]);
-                v = s >= 0 ? (mean + sums[s]) / (1.0 + counts[s]) : mean;
-            }
-            out_future[i] = (float)v;
-        }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -489,58 +438,11 @@ Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inpu
     if ((cov.known || cov.cat_known) && !supports_known(c))
         return Status::fail(TSFM_ERR_COVARIATES_UNSUPPORTED, "KnownCovariatesUnsupported");
 
-    // Categorical codes: target-encoded against a univariate target, else raw (forecaster.zig:92-103).
-    std::vector<double> target;
+    // Covariate channels of a series: numeric past / known first, then the categorical ones (target-
+    // encoded on the device against a univariate target, else rounded; forecaster.zig:92-103).
     const bool have_target = (cov.cat_past || cov.cat_known) && v == 1;
-    if (have_target) {
-        target.resize(b * t0);
-        for (size_t s = 0; s < b; ++s) {
-            bool started = false;
-            float last = 0.0f;
-            for (size_t i = 0; i < t0; ++i) {
-                if (observed[s * t0 + i]) {
-                    started = true;
-                    last = inputs[s * t0 + i];
-                }
-                const bool in_window = t0 <= o.max_context || i >= t0 - o.max_context;
-                target[s * t0 + i] = started && in_window ? (double)last : std::nan("");
-            }
-        }
-    }
-    auto encode_cat = [&](const double *codes, size_t nc, size_t len) {
-        std::vector<float> outv(b * nc * len);
-        for (size_t s = 0; s < b; ++s)
-            for (size_t j = 0; j < nc; ++j) {
-                const double *row = codes + (s * nc + j) * len;
-                float *dst = &outv[(s * nc + j) * len];
-                if (!have_target) {
-                    for (size_t i = 0; i < len; ++i) dst[i] = (float)row[i];
-                    continue;
-                }
-                target_encode(&target[s * t0], row, t0, len > t0 ? row + t0 : nullptr, len - t0, dst,
-                              len > t0 ? dst + t0 : nullptr);
-                for (size_t i = 0; i < t0; ++i)
-                    if (std::isnan(target[s * t0 + i]) && std::isnan(row[i])) dst[i] = std::nanf("");
-            }
-        return outv;
-    };
-    std::vector<float> enc_past, enc_known;
-    if (cov.cat_past) enc_past = encode_cat(cov.cat_past, cov.n_cat_past, t0);
-    if (cov.cat_known) enc_known = encode_cat(cov.cat_known, cov.n_cat_known, t0 + horizon);
-    auto cat_channels = [&](const float *a, size_t ca, const std::vector<float> &bb, size_t cb, size_t len) {
-        std::vector<float> outv;
-        if (ca + cb == 0) return outv;
-        outv.resize(b * (ca + cb) * len);
-        for (size_t i = 0; i < b; ++i) {
-            if (a) std::memcpy(&outv[i * (ca + cb) * len], a + i * ca * len, ca * len * 4);
-            if (!bb.empty()) std::memcpy(&outv[(i * (ca + cb) + ca) * len], &bb[i * cb * len], cb * len * 4);
-        }
-        return outv;
-    };
     const size_t np = cov.past ? cov.n_past : 0, nk = cov.known ? cov.n_known : 0;
     const size_t ncp = cov.cat_past ? cov.n_cat_past : 0, nck = cov.cat_known ? cov.n_cat_known : 0;
-    std::vector<float> past_rows = cat_channels(cov.past, np, enc_past, ncp, t0);
-    std::vector<float> known_rows = cat_channels(cov.known, nk, enc_known, nck, t0 + horizon);
     const size_t n_past = np + ncp, n_known = nk + nck;
     if (n_past == 0 && n_known == 0 && any_cov) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "InvalidInput");
     if (o.symmetric_averaging)
@@ -568,7 +470,9 @@ Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inpu
                       2 * Arena::span(R * max_t) + Arena::span(R * hpad * 4) + Arena::span(R * hpad) +
                       Arena::span(nt * horizon * q * 4) * 2 + Arena::span(nt * o.per_shot_horizon_patches * ps * q * 4) +
                       Arena::span(b * v) + Arena::span(vall) + Arena::span(16) + Arena::span(b * v * t0 * 4) +
-                      Arena::span(b * v * t0) + Arena::span(past_rows.size() * 4) + Arena::span(known_rows.size() * 4);
+                      Arena::span(b * v * t0) + Arena::span(b * n_past * t0 * 4) +
+                      Arena::span(b * n_known * (t0 + horizon) * 4) + Arena::span(b * ncp * t0 * 8) +
+                      Arena::span(b * nck * (t0 + horizon) * 8) + (have_target ? Arena::span(b * t0 * 8) : 0);
     TSFM_TRY(r.fc.reserve(fc_bytes));
     Arena &fc = r.fc;
     fc.reset();
@@ -586,20 +490,40 @@ Status ts_forecast(Replica &r, const tsfm_config &c, TsDev &w, const float *inpu
     int *d_nan = fc.take<int>(4);
     float *d_in = fc.take<float>(b * v * t0);
     uint8_t *d_obs = fc.take<uint8_t>(b * v * t0);
-    float *d_past = fc.take<float>(past_rows.size());
-    float *d_known = fc.take<float>(known_rows.size());
+    float *d_past = fc.take<float>(b * n_past * t0);
+    float *d_known = fc.take<float>(b * n_known * (t0 + horizon));
+    double *d_cat_past = fc.take<double>(b * ncp * t0);
+    double *d_cat_known = fc.take<double>(b * nck * (t0 + horizon));
+    double *d_target = have_target ? fc.take<double>(b * t0) : nullptr;
     if (fc.used > fc.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Timestral: forecaster buffers too small");
     cudaStream_t s = r.stream;
     // The raw arrays go up once; the rows (both passes), masks, known futures and clip flags are
     // built on the device.
     TSFM_CUDA(cudaMemcpyAsync(d_in, inputs, b * v * t0 * 4, cudaMemcpyHostToDevice, s), "timestral: inputs");
     TSFM_CUDA(cudaMemcpyAsync(d_obs, observed, b * v * t0, cudaMemcpyHostToDevice, s), "timestral: observed");
-    if (!past_rows.empty())
-        TSFM_CUDA(cudaMemcpyAsync(d_past, past_rows.data(), past_rows.size() * 4, cudaMemcpyHostToDevice, s),
+    const size_t kl = t0 + horizon;
+    if (np)
+        TSFM_CUDA(cudaMemcpy2DAsync(d_past, n_past * t0 * 4, cov.past, np * t0 * 4, np * t0 * 4, b,
+                                    cudaMemcpyHostToDevice, s),
                   "timestral: past covariates");
-    if (!known_rows.empty())
-        TSFM_CUDA(cudaMemcpyAsync(d_known, known_rows.data(), known_rows.size() * 4, cudaMemcpyHostToDevice, s),
+    if (nk)
+        TSFM_CUDA(cudaMemcpy2DAsync(d_known, n_known * kl * 4, cov.known, nk * kl * 4, nk * kl * 4, b,
+                                    cudaMemcpyHostToDevice, s),
                   "timestral: known covariates");
+    if (ncp)
+        TSFM_CUDA(cudaMemcpyAsync(d_cat_past, cov.cat_past, b * ncp * t0 * 8, cudaMemcpyHostToDevice, s),
+                  "timestral: categorical past covariates");
+    if (nck)
+        TSFM_CUDA(cudaMemcpyAsync(d_cat_known, cov.cat_known, b * nck * kl * 8, cudaMemcpyHostToDevice, s),
+                  "timestral: categorical known covariates");
+    if (ncp || nck) {
+        LaunchScope ls(r, s, K_PATCH, (double)b * (ncp + nck) * t0 * kl);
+        if (have_target) TSFM_TRY(launch_ts_target(d_in, d_obs, (int64_t)b, (int64_t)t0, (int64_t)o.max_context, d_target, s));
+        TSFM_TRY(launch_ts_cat_encode(d_cat_past, (int64_t)b, (int64_t)ncp, (int64_t)t0, (int64_t)t0, d_target, d_past,
+                                      (int64_t)n_past, (int64_t)np, s));
+        TSFM_TRY(launch_ts_cat_encode(d_cat_known, (int64_t)b, (int64_t)nck, (int64_t)kl, (int64_t)t0, d_target,
+                                      d_known, (int64_t)n_known, (int64_t)nk, s));
+    }
     TSFM_CUDA(cudaMemcpyAsync(d_roles, roles.data(), vall, cudaMemcpyHostToDevice, s), "timestral: roles");
     {
         TsPrepareCall pc;

@@ -236,6 +236,85 @@ __global__ void __launch_bounds__(256) ts_prepare_kernel(TsPrepareCall c) {
     }
 }
 
+// One warp per series: the forward-filled target of the encoding (values as f64).
+__global__ void __launch_bounds__(256) ts_target_kernel(const float *inputs, const uint8_t *observed, int64_t b,
+                                                       int64_t t0, int64_t max_context, double *target) {
+    const int lane = threadIdx.x & 31;
+    const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (s >= b) return;
+    const float *x = inputs + s * t0;
+    const uint8_t *ob = observed + s * t0;
+    float carry = 0.0f;
+    bool seen = false;
+    for (int64_t j0 = 0; j0 < t0; j0 += 32) {
+        const int64_t j = j0 + lane;
+        const bool o = j < t0 && ob[j] != 0;
+        const float val = j < t0 ? x[j] : 0.0f;
+        const unsigned m = __ballot_sync(0xffffffffu, o);
+        const unsigned upto = m & (0xffffffffu >> (31 - lane));
+        const float from = __shfl_sync(0xffffffffu, val, upto ? 31 - __clz(upto) : 0);
+        const bool started = upto != 0 || seen;
+        const float last = upto ? from : carry;
+        if (j < t0) {
+            const bool in_window = t0 <= max_context || j >= t0 - max_context;
+            target[s * t0 + j] = started && in_window ? (double)last : (double)NAN;
+        }
+        if (m) {
+            carry = __shfl_sync(0xffffffffu, val, 31 - __clz(m));
+            seen = true;
+        }
+    }
+}
+
+// One block per (series, categorical channel).
+__global__ void __launch_bounds__(256) ts_cat_encode_kernel(const double *codes, int64_t ncat, int64_t len, int64_t t0,
+                                                           const double *target, float *out, int64_t chan_total,
+                                                           int64_t chan0) {
+    const int64_t s = blockIdx.x, ch = blockIdx.y;
+    const double *row = codes + (s * ncat + ch) * len;
+    float *dst = out + (s * chan_total + chan0 + ch) * len;
+    if (target == nullptr) {
+        for (int64_t i = threadIdx.x; i < len; i += blockDim.x) dst[i] = (float)row[i];
+        return;
+    }
+    const double *tg = target + s * t0;
+    __shared__ double s_mean;
+    if (threadIdx.x == 0) {
+        double count = 0.0, sum = 0.0;
+        for (int64_t k = 0; k < t0; ++k)
+            if (isfinite(tg[k])) {
+                count += 1.0;
+                sum += tg[k];
+            }
+        s_mean = count > 0.0 ? sum / count : 0.0;
+    }
+    __syncthreads();
+    const double mean = s_mean;
+    for (int64_t i = threadIdx.x; i < len; i += blockDim.x) {
+        const double c = row[i];
+        const bool other = i < t0 ? !isfinite(c) : isnan(c);
+        double sum = 0.0, count = 0.0;
+        bool known = other;
+        for (int64_t k = 0; k < t0; ++k) {
+            const double ck = row[k];
+            const bool same = other ? !isfinite(ck) : (isfinite(ck) && ck == c);
+            known |= same;
+            const double tk = tg[k];
+            if (same && isfinite(tk)) {
+                sum += tk;
+                count += 1.0;
+            }
+        }
+        float v;
+        if (i < t0) {
+            v = (isnan(tg[i]) && isnan(c)) ? NAN : (float)((mean + sum) / (1.0 + count));
+        } else {
+            v = (float)(known ? (mean + sum) / (1.0 + count) : mean);
+        }
+        dst[i] = v;
+    }
+}
+
 // Per-block row maps (model.zig:379-410, 600): the bidirectional flag of every row (known-future
 // rows of a covariate window), and for each target row (the first v rows of each group, in order)
 // its index and the indices of its h decoder tokens in the (rows * sl) token matrix.
@@ -747,6 +826,24 @@ Status launch_ts_prepare(const TsPrepareCall &c, cudaStream_t s) {
     if (c.keep > c.t0 || c.keep > c.t) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "timestral prepare: keep");
     ts_prepare_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(c);
     TSFM_CUDA(cudaGetLastError(), "timestral prepare: launch");
+    return Status::ok();
+}
+
+Status launch_ts_target(const float *inputs, const uint8_t *observed, int64_t b, int64_t t0, int64_t max_context,
+                        double *target, cudaStream_t s) {
+    if (b <= 0 || t0 <= 0) return Status::ok();
+    ts_target_kernel<<<(unsigned)((b + 7) / 8), 256, 0, s>>>(inputs, observed, b, t0, max_context, target);
+    TSFM_CUDA(cudaGetLastError(), "timestral target: launch");
+    return Status::ok();
+}
+
+Status launch_ts_cat_encode(const double *codes, int64_t b, int64_t ncat, int64_t len, int64_t t0, const double *target,
+                            float *out, int64_t chan_total, int64_t chan0, cudaStream_t s) {
+    if (b <= 0 || ncat <= 0 || len <= 0) return Status::ok();
+    if (b > INT_MAX || ncat > 65535) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "timestral categorical: too many rows");
+    ts_cat_encode_kernel<<<dim3((unsigned)b, (unsigned)ncat), 256, 0, s>>>(codes, ncat, len, t0, target, out, chan_total,
+                                                                          chan0);
+    TSFM_CUDA(cudaGetLastError(), "timestral categorical: launch");
     return Status::ok();
 }
 

@@ -51,6 +51,18 @@ struct TsPrepareCall {
 };
 Status launch_ts_prepare(const TsPrepareCall &c, cudaStream_t s);
 
+// Categorical covariates (forecaster.zig:92-103, 201-301). With a univariate target, each code row
+// is target-encoded: target = the series' forward-filled observed value inside the --max-context
+// window (NaN elsewhere); a context step maps to (mean + sum) / (1 + count) over the earlier and
+// later context steps with the same code and a finite target (sums in step order, f64); codes that
+// are not finite share one slot; a future step with a code never seen in the context gets the
+// mean. Without a target the codes are only rounded to f32. `out` rows are (b, chan_total, len)
+// and the encoded channels start at chan0.
+Status launch_ts_target(const float *inputs, const uint8_t *observed, int64_t b, int64_t t0, int64_t max_context,
+                        double *target, cudaStream_t s);
+Status launch_ts_cat_encode(const double *codes, int64_t b, int64_t ncat, int64_t len, int64_t t0, const double *target,
+                            float *out, int64_t chan_total, int64_t chan0, cudaStream_t s);
+
 // Row flags and head / target row indices of one block; target rows are the first v of every
 // group of vall rows (role 0).
 Status launch_ts_rows(const int8_t *roles, int64_t rows, int vall, int v, int64_t sl, int64_t ne, int h, bool cov,
