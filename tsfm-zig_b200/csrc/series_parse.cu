@@ -270,7 +270,8 @@ __global__ void __launch_bounds__(256) line_kernel(const char *text, int64_t tot
     }
     if (lane == 0) {
         info[line] = li;
-        meta[line] = ((uint32_t)li.kind << 30) | (li.tokens & 0x3fffffffu);
+        // 2^30 - 1 tokens or more on one line saturate the count (the host reports it).
+        meta[line] = ((uint32_t)li.kind << 30) | min(li.tokens, 0x3fffffffu);
     }
 }
 
@@ -504,6 +505,8 @@ Status structure(PCtx &x, const char *text, int64_t n, cudaStream_t s, Shape &sh
             TSFM_TRY(close_block());
             continue;
         }
+        if (tokens == 0x3fffffffu)
+            return Status::fail(TSFM_ERR_UNSUPPORTED, "series: a line holds 2^30 - 1 or more values");
         if (!have_len) {
             len = tokens;
             have_len = true;
