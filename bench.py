@@ -663,6 +663,12 @@ def main():
                    "share": v["ms"] / max(1e-9, sum(u["ms"] for u in cls.values()))} for c, v in cls.items()}
     if cls["attention"]["ms"] > 0:
         kernels["attention"]["tflops"] = cls["attention"]["work"] / (cls["attention"]["ms"] / 1e3) / 1e12
+    # Memory-bound classes: algorithmic bytes (recorded per launch) over their device time, and the
+    # fraction of the measured HBM copy bandwidth.
+    for c in ("rmsnorm",):
+        if cls[c]["ms"] > 0 and cls[c]["work"] > 0:
+            kernels[c]["gbs"] = cls[c]["work"] / (cls[c]["ms"] / 1e3) / 1e9
+            kernels[c]["hbm_frac"] = kernels[c]["gbs"] / peaks()[2]
 
     if rank == 0:
         cpu = None
