@@ -523,14 +523,17 @@ def run_parse(a):
 def run_attention(a):
     """The self-attention kernel alone at the families' shapes (tsfm_kernel_attention, CUDA events,
     L2 flushed between launches): Chronos-2 (256 sequences of 577 tokens, 12 heads, key-validity
-    mask) and Chronos-Bolt-base (4096 sequences of 129 tokens, 12 heads, relative-position bias).
-    TFLOP/s counts 4 * n^2 * 64 per (sequence, head), the useful work only."""
+    mask), Chronos-Bolt-base (4096 sequences of 129 tokens, 12 heads, relative-position bias) and
+    Timestral (2816 rows of 160 tokens, 16 heads, causal over valid keys). TFLOP/s counts
+    4 * n^2 * 64 per (sequence, head), halved for the causal mask: the useful work only."""
     import torch
     import tsfm_b200 as tb
     stream = torch.cuda.current_stream()
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
     burst = peaks()[0]
-    for name, G, n, heads, rel in (("chronos2", 256, 577, 12, False), ("bolt-base", a.csv_series // 2, 129, 12, True)):
+    shapes = (("chronos2", 256, 577, 12, False, 0), ("bolt-base", a.csv_series // 2, 129, 12, True, 0),
+              ("timestral", 2816 * a.csv_series // 8192, 160, 16, False, 1))
+    for name, G, n, heads, rel, mode in shapes:
         g = torch.Generator(device="cuda").manual_seed(7)
         ld = 3 * heads * 64
         qkv = (torch.randn(G * n, ld, device="cuda", generator=g) * 0.5).half()
@@ -539,7 +542,7 @@ def run_attention(a):
         o = torch.empty(G * n, heads * 64, device="cuda", dtype=torch.float16)
         run = lambda: tb.check(tb.lib.tsfm_kernel_attention(
             qkv.data_ptr(), qkv.data_ptr() + heads * 64 * 2, qkv.data_ptr() + 2 * heads * 64 * 2, ld, o.data_ptr(),
-            heads * 64, kv.data_ptr(), None if relb is None else relb.data_ptr(), G, heads, n, 0.125, 0, 1,
+            heads * 64, kv.data_ptr(), None if relb is None else relb.data_ptr(), G, heads, n, 0.125, mode, 1,
             stream.cuda_stream))
         for _ in range(max(3, a.warmup)):
             run()
@@ -554,9 +557,9 @@ def run_attention(a):
             e1.synchronize()
             total += e0.elapsed_time(e1)
         ms = total / steps
-        tf = 4.0 * n * n * 64 * heads * G / (ms / 1e3) / 1e12
+        tf = 4.0 * n * n * 64 * heads * G / (ms / 1e3) / 1e12 / (2.0 if mode == 1 else 1.0)
         print(json.dumps({"workload": "attention", "shape": name, "sequences": G, "tokens": n, "heads": heads,
-                          "rel_bias": rel, "ms": ms, "tflops": tf, "tc_peak_frac": tf / burst,
+                          "rel_bias": rel, "mask_mode": mode, "ms": ms, "tflops": tf, "tc_peak_frac": tf / burst,
                           "us_per_sequence_head": ms * 1e3 / (G * heads)}), flush=True)
         del qkv, o
 

@@ -54,45 +54,6 @@ __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ void ldsm_x4(const void *p, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(const void *p, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(smem_u32(p)));
-}
-
-template <bool F16>
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    if constexpr (F16) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-    } else {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-    }
-}
-
-template <bool F16>
-__device__ __forceinline__ uint32_t pack16(float lo, float hi) {
-    if constexpr (F16) {
-        __half2 v = __floats2half2_rn(lo, hi);
-        return *reinterpret_cast<uint32_t *>(&v);
-    } else {
-        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-        return *reinterpret_cast<uint32_t *>(&v);
-    }
-}
-
 template <int MODE, bool F16>
 __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
     __shared__ __align__(128) uint16_t sQ[BQ * HD];
@@ -310,9 +271,9 @@ Status launch_attention(const AttentionCall &c, cudaStream_t stream) {
     p.l = c.l;
     p.bidir = c.group_bidir;
     p.bidir_all = c.mask_mode == 2;
-    dim3 grid((c.n + BQ - 1) / BQ, c.heads, c.groups);
     const bool f16 = c.dtype == E_F16;
     if (c.dtype != E_F16 && c.dtype != E_BF16) return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "attention: dtype");
+    dim3 grid((c.n + BQ - 1) / BQ, c.heads, c.groups);
     if (c.mask_mode == 0)
         f16 ? attn_kernel<0, true><<<grid, 128, 0, stream>>>(p) : attn_kernel<0, false><<<grid, 128, 0, stream>>>(p);
     else

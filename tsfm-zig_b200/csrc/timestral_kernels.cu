@@ -568,6 +568,130 @@ __global__ void __launch_bounds__(256, V <= 11 ? 2 : 1) ts_variate_vec_kernel(Ts
     }
 }
 
+// The same attention on the tensor cores, one block per (group, token): the q / k / v slices of
+// the group's V rows (all heads) are staged in shared memory by asynchronous 16-byte copies (rows
+// padded to 16, row stride d + 8 elements so ldmatrix rows fall in different banks); one warp per
+// head computes S = Q K^T (16 x 16, k = 64: eight m16n8k16 MMAs), the masked softmax in registers
+// (rows spread over lane quads), and O = P V (16 x 64, k = 16: eight MMAs); the output rows go back
+// through shared memory (over the q slices) to coalesced 16-byte stores.
+template <int V, bool F16>
+__global__ void __launch_bounds__(256) ts_variate_mma_kernel(TsVariateCall c) {
+    static_assert(V <= 16, "at most 16 rows per group");
+    extern __shared__ __align__(16) unsigned char vsm[];
+    const int rs = (int)c.d + 8;  // row stride (elements)
+    uint16_t *qs = reinterpret_cast<uint16_t *>(vsm);
+    uint16_t *ks = qs + 16 * rs;
+    uint16_t *vs = ks + 16 * rs;
+    __shared__ uint32_t s_valid;
+    const int64_t g = blockIdx.x / c.sl, tok = blockIdx.x % c.sl;
+    const int64_t r0 = g * V;
+    const int chunks = (int)(c.d / 8);
+    const uint16_t *src = static_cast<const uint16_t *>(c.qkv);
+    for (int idx = threadIdx.x; idx < V * 3 * chunks; idx += blockDim.x) {
+        const int i = idx / (3 * chunks), rem = idx - i * 3 * chunks, sec = rem / chunks, ch = rem - sec * chunks;
+        const uint16_t *g16 = src + ((r0 + i) * c.sl + tok) * c.ld + sec * c.d + ch * 8;
+        const uint32_t s16 = smem_u32(qs + sec * 16 * rs + i * rs + ch * 8);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s16), "l"(g16) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    // Padding rows of K and V are zero (their P is 0; a zero row keeps 0 * row finite).
+    if constexpr (V < 16) {
+        for (int idx = threadIdx.x; idx < 2 * (16 - V) * chunks; idx += blockDim.x) {
+            const int half = idx / ((16 - V) * chunks), rem = idx - half * (16 - V) * chunks;
+            const int i = V + rem / chunks, ch = rem % chunks;
+            *reinterpret_cast<uint4 *>((half ? vs : ks) + i * rs + ch * 8) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    if (threadIdx.x == 0) {
+        uint32_t vb = 0;
+        for (int i = 0; i < V; ++i)
+            if (tok >= c.ne || c.key_valid[(r0 + i) * c.ne + tok] != 0) vb |= 1u << i;
+        s_valid = vb;
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    const uint32_t valid = s_valid;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i0 = lane >> 2, i1 = i0 + 8;  // this thread's two query rows
+    const int rq0 = (c.cov && i0 < V) ? c.roles[i0] : 0, rq1 = (c.cov && i1 < V) ? c.roles[i1] : 0;
+    for (int h = warp; h < c.heads; h += (int)(blockDim.x >> 5)) {
+        float sacc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t a[4], b0, b1, b2, b3;
+            const int ar = (lane & 7) + ((lane >> 3) & 1) * 8, ac = h * 64 + kk * 16 + (lane >> 4) * 8;
+            ldsm_x4(qs + ar * rs + ac, a[0], a[1], a[2], a[3]);
+            const int key = (lane & 7) + (lane >> 4) * 8, dim = h * 64 + kk * 16 + ((lane >> 3) & 1) * 8;
+            ldsm_x4(ks + key * rs + dim, b0, b1, b2, b3);
+            mma16816<F16>(sacc[0], a, b0, b1);
+            mma16816<F16>(sacc[1], a, b2, b3);
+        }
+        // Mask, scale, softmax per row (the four values of a row per thread, then the lane quad).
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int iq = e < 2 ? i0 : i1, ik = nt * 8 + (lane & 3) * 2 + (e & 1);
+                const int rq = e < 2 ? rq0 : rq1, rk = (c.cov && ik < V) ? c.roles[ik] : 0;
+                const bool forbidden = (rq != 0 && rk == 0) || (rq == 2 && rk != 2);
+                const bool ok = iq < V && ik < V && (ik == iq || (((valid >> ik) & 1u) && !forbidden));
+                const float x = ok ? sacc[nt][e] * c.scale : -INFINITY;
+                sacc[nt][e] = x;
+                if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+            }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float m0 = mx0 == -INFINITY ? 0.0f : mx0, m1 = mx1 == -INFINITY ? 0.0f : mx1;
+        float l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float ev = sacc[nt][e] == -INFINITY ? 0.0f : expf(sacc[nt][e] - (e < 2 ? m0 : m1));
+                sacc[nt][e] = ev;
+                if (e < 2) l0 += ev; else l1 += ev;
+            }
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+        const uint32_t pa[4] = {pack16<F16>(sacc[0][0], sacc[0][1]), pack16<F16>(sacc[0][2], sacc[0][3]),
+                                pack16<F16>(sacc[1][0], sacc[1][1]), pack16<F16>(sacc[1][2], sacc[1][3])};
+        float o[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
+#pragma unroll
+        for (int dp = 0; dp < 4; ++dp) {
+            uint32_t b0, b1, b2, b3;
+            const int key = (lane & 7) + ((lane >> 3) & 1) * 8, dim = h * 64 + dp * 16 + (lane >> 4) * 8;
+            ldsm_x4_t(vs + key * rs + dim, b0, b1, b2, b3);
+            mma16816<F16>(o[2 * dp], pa, b0, b1);
+            mma16816<F16>(o[2 * dp + 1], pa, b2, b3);
+        }
+        const float inv0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, inv1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
+        // Only this warp reads head h's q columns: its output rows replace them.
+        __syncwarp();
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            const int col = h * 64 + nt * 8 + (lane & 3) * 2;
+            if (i0 < V) *reinterpret_cast<uint32_t *>(qs + i0 * rs + col) = pack16<F16>(o[nt][0] * inv0, o[nt][1] * inv0);
+            if (i1 < V) *reinterpret_cast<uint32_t *>(qs + i1 * rs + col) = pack16<F16>(o[nt][2] * inv1, o[nt][3] * inv1);
+        }
+    }
+    __syncthreads();
+    uint16_t *dst = static_cast<uint16_t *>(c.o);
+    for (int idx = threadIdx.x; idx < V * chunks; idx += blockDim.x) {
+        const int i = idx / chunks, ch = idx - i * chunks;
+        *reinterpret_cast<uint4 *>(dst + ((r0 + i) * c.sl + tok) * c.ldo + ch * 8) =
+            *reinterpret_cast<const uint4 *>(qs + i * rs + ch * 8);
+    }
+}
+
 __device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 // nn.clampNonfinite (core/nn.zig:522-563) over q values.
@@ -891,6 +1015,23 @@ Status launch_ts_swiglu(const void *h, void *a, int64_t rows, int64_t hid, int d
 
 template <int V>
 void variate_vec(const TsVariateCall &c, cudaStream_t s) {
+    // Block per (group, token) on the tensor cores when the rows are 16-byte aligned and the group's
+    // slices (16 padded rows of q, k and v) fit.
+    const size_t smem = (size_t)3 * 16 * (c.d + 8) * 2;
+    const bool a16 = (reinterpret_cast<uintptr_t>(c.qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(c.o) & 15) == 0 &&
+                     c.ld % 8 == 0 && c.d % 8 == 0 && c.ldo % 8 == 0 && c.d == (int64_t)c.heads * 64;
+    if (a16 && smem <= 200 * 1024 && c.groups * c.sl <= INT_MAX) {
+        const void *fn = c.dtype == E_F16 ? reinterpret_cast<const void *>(&ts_variate_mma_kernel<V, true>)
+                                          : reinterpret_cast<const void *>(&ts_variate_mma_kernel<V, false>);
+        if (ensure_smem_attr(fn, (int)smem)) {
+            const unsigned grid = (unsigned)(c.groups * c.sl);
+            if (c.dtype == E_F16)
+                ts_variate_mma_kernel<V, true><<<grid, 256, smem, s>>>(c);
+            else
+                ts_variate_mma_kernel<V, false><<<grid, 256, smem, s>>>(c);
+            return;
+        }
+    }
     const int64_t threads = c.groups * c.sl * c.heads * 16;
     const unsigned grid = (unsigned)((threads + 255) / 256);
     if (c.dtype == E_F16)
