@@ -400,7 +400,8 @@ __global__ void __launch_bounds__(256) parse_kernel(const char *text, int64_t to
 struct PCtx {
     std::mutex mu;
     bool ready = false;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr, copy = nullptr;
+    cudaEvent_t ev[16] = {};
     char *d_text = nullptr;
     size_t text_cap = 0;
     uint32_t *d_tile = nullptr;
@@ -443,6 +444,8 @@ Status pctx_init(PCtx &x, int device) {
     TSFM_CUDA(cudaSetDevice(device), "series: cudaSetDevice");
     if (x.ready) return Status::ok();
     TSFM_CUDA(cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking), "series: stream");
+    TSFM_CUDA(cudaStreamCreateWithFlags(&x.copy, cudaStreamNonBlocking), "series: stream");
+    for (cudaEvent_t &e : x.ev) TSFM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "series: event");
     TSFM_CUDA(cudaMallocHost(reinterpret_cast<void **>(&x.h_total), 16), "series: pinned total");
     const numparse::Recip10 r = numparse::make_recip10();
     TSFM_CUDA(cudaMemcpyToSymbol(c_recip, &r, sizeof r), "series: reciprocals");
@@ -525,8 +528,10 @@ Status structure(PCtx &x, const char *text, int64_t n, cudaStream_t s, Shape &sh
 }
 
 // Steps (4)-(5): values (f64 and / or f32, device) of the data lines.
+// Steps (4)-(5). With host_out, the values are parsed in chunks and each chunk is copied to
+// host_out on the copy stream while the next one is parsed.
 Status tokens_and_values(PCtx &x, const char *text, int64_t total_bytes, const Shape &sh, double *out, float *out32,
-                         cudaStream_t s) {
+                         cudaStream_t s, double *host_out = nullptr) {
     const int64_t n_data = (int64_t)sh.data_lines.size(), len = (int64_t)sh.len, n = n_data * len;
     TSFM_TRY(grow(&x.d_data, &x.data_cap, (size_t)n_data * 8, "series: data lines"));
     TSFM_TRY(grow(&x.d_ts, &x.ts_cap, (size_t)n * 8, "series: tokens"));
@@ -536,8 +541,26 @@ Status tokens_and_values(PCtx &x, const char *text, int64_t total_bytes, const S
     token_kernel<<<(unsigned)((n_data + 7) / 8), 256, 0, s>>>(text, total_bytes, x.d_info, x.d_data, n_data, len,
                                                                x.d_ts, x.d_te);
     TSFM_CUDA(cudaGetLastError(), "series: tokens");
-    parse_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(text, total_bytes, x.d_ts, x.d_te, n, out, out32);
-    TSFM_CUDA(cudaGetLastError(), "series: parse");
+    if (host_out == nullptr) {
+        parse_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(text, total_bytes, x.d_ts, x.d_te, n, out, out32);
+        TSFM_CUDA(cudaGetLastError(), "series: parse");
+        TSFM_CUDA(cudaStreamSynchronize(s), "series: parse");
+        return Status::ok();
+    }
+    constexpr int kChunks = 16;
+    const int64_t per = std::max<int64_t>(256, ((n + kChunks - 1) / kChunks + 255) / 256 * 256);
+    int k = 0;
+    for (int64_t t0 = 0; t0 < n; t0 += per, ++k) {
+        const int64_t cnt = std::min(per, n - t0);
+        parse_kernel<<<(unsigned)((cnt + 255) / 256), 256, 0, s>>>(text, total_bytes, x.d_ts + t0, x.d_te + t0, cnt,
+                                                                   out + t0, nullptr);
+        TSFM_CUDA(cudaGetLastError(), "series: parse");
+        TSFM_CUDA(cudaEventRecord(x.ev[k], s), "series: event");
+        TSFM_CUDA(cudaStreamWaitEvent(x.copy, x.ev[k], 0), "series: wait");
+        TSFM_CUDA(cudaMemcpyAsync(host_out + t0, out + t0, (size_t)cnt * 8, cudaMemcpyDeviceToHost, x.copy),
+                  "series: values out");
+    }
+    TSFM_CUDA(cudaStreamSynchronize(x.copy), "series: values out");
     TSFM_CUDA(cudaStreamSynchronize(s), "series: parse");
     return Status::ok();
 }
@@ -569,10 +592,7 @@ Status parse_host(int device, const char *text, size_t length, double *values, s
         return Status::fail(TSFM_ERR_BUFFER_TOO_SMALL,
                             "series: " + std::to_string(need) + " values, capacity " + std::to_string(capacity));
     TSFM_TRY(grow(&x.d_vals, &x.vals_cap, need * 8, "series: values"));
-    TSFM_TRY(tokens_and_values(x, x.d_text, (int64_t)length, sh, x.d_vals, nullptr, x.stream));
-    TSFM_CUDA(cudaMemcpyAsync(values, x.d_vals, need * 8, cudaMemcpyDeviceToHost, x.stream), "series: values out");
-    TSFM_CUDA(cudaStreamSynchronize(x.stream), "series: values out");
-    return Status::ok();
+    return tokens_and_values(x, x.d_text, (int64_t)length, sh, x.d_vals, nullptr, x.stream, values);
 }
 
 Status parse_device(const char *text, size_t length, double *values, float *values32, size_t capacity, size_t *blocks,
