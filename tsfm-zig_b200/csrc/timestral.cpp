@@ -225,10 +225,14 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
                 vc.roles = w.roles;
                 vc.cov = k.cov;
                 vc.scale = 1.0f / std::sqrt((float)hd_of(c));
+                if (a.gate) {  // applied as the output is written
+                    vc.gate = qkvg + 3 * d;
+                    vc.ldg = cols;
+                }
                 LaunchScope ls(r, s, K_ATTN, 4.0 * (double)k.groups * sl * nh * k.vall * k.vall * 64);
                 TSFM_TRY(launch_ts_variate(vc, s));
             }
-            if (a.gate) {
+            if (a.gate && a.is_time) {
                 LaunchScope ls(r, s, K_OTHER, (double)rows * d * 6);
                 TSFM_TRY(launch_ts_gate(o16, d, qkvg + 3 * d, cols, rows, d, w.act, s));
             }

@@ -685,10 +685,20 @@ __global__ void __launch_bounds__(256) ts_variate_mma_kernel(TsVariateCall c) {
     }
     __syncthreads();
     uint16_t *dst = static_cast<uint16_t *>(c.o);
+    const uint16_t *gate = static_cast<const uint16_t *>(c.gate);
     for (int idx = threadIdx.x; idx < V * chunks; idx += blockDim.x) {
         const int i = idx / chunks, ch = idx - i * chunks;
-        *reinterpret_cast<uint4 *>(dst + ((r0 + i) * c.sl + tok) * c.ldo + ch * 8) =
-            *reinterpret_cast<const uint4 *>(qs + i * rs + ch * 8);
+        const int64_t row = (r0 + i) * c.sl + tok;
+        uint4 v = *reinterpret_cast<const uint4 *>(qs + i * rs + ch * 8);
+        if (gate != nullptr) {  // the gate kernel's arithmetic on the rounded output
+            float x[8], gv[8];
+            unpack8<F16>(v, x);
+            unpack8<F16>(*reinterpret_cast<const uint4 *>(gate + row * c.ldg + ch * 8), gv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = x[e] / (1.0f + __expf(-gv[e]));
+            v = pack8<F16>(x);
+        }
+        *reinterpret_cast<uint4 *>(dst + row * c.ldo + ch * 8) = v;
     }
 }
 
@@ -1014,12 +1024,13 @@ Status launch_ts_swiglu(const void *h, void *a, int64_t rows, int64_t hid, int d
 }
 
 template <int V>
-void variate_vec(const TsVariateCall &c, cudaStream_t s) {
+bool variate_vec(const TsVariateCall &c, cudaStream_t s) {  // true: gate applied
     // Block per (group, token) on the tensor cores when the rows are 16-byte aligned and the group's
     // slices (16 padded rows of q, k and v) fit.
     const size_t smem = (size_t)3 * 16 * (c.d + 8) * 2;
     const bool a16 = (reinterpret_cast<uintptr_t>(c.qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(c.o) & 15) == 0 &&
-                     c.ld % 8 == 0 && c.d % 8 == 0 && c.ldo % 8 == 0 && c.d == (int64_t)c.heads * 64;
+                     c.ld % 8 == 0 && c.d % 8 == 0 && c.ldo % 8 == 0 && c.d == (int64_t)c.heads * 64 &&
+                     (c.gate == nullptr || ((reinterpret_cast<uintptr_t>(c.gate) & 15) == 0 && c.ldg % 8 == 0));
     if (a16 && smem <= 200 * 1024 && c.groups * c.sl <= INT_MAX) {
         const void *fn = c.dtype == E_F16 ? reinterpret_cast<const void *>(&ts_variate_mma_kernel<V, true>)
                                           : reinterpret_cast<const void *>(&ts_variate_mma_kernel<V, false>);
@@ -1029,7 +1040,7 @@ void variate_vec(const TsVariateCall &c, cudaStream_t s) {
                 ts_variate_mma_kernel<V, true><<<grid, 256, smem, s>>>(c);
             else
                 ts_variate_mma_kernel<V, false><<<grid, 256, smem, s>>>(c);
-            return;
+            return true;
         }
     }
     const int64_t threads = c.groups * c.sl * c.heads * 16;
@@ -1038,6 +1049,7 @@ void variate_vec(const TsVariateCall &c, cudaStream_t s) {
         ts_variate_vec_kernel<V, true><<<grid, 256, 0, s>>>(c);
     else
         ts_variate_vec_kernel<V, false><<<grid, 256, 0, s>>>(c);
+    return false;
 }
 
 Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s) {
@@ -1045,30 +1057,34 @@ Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s) {
     // 8-byte accesses per lane: row strides, the k / v offset and the base even in 4-element units.
     if ((c.ld % 4) == 0 && (c.d % 4) == 0 && (c.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(c.qkv) & 7) == 0 &&
         (reinterpret_cast<uintptr_t>(c.o) & 7) == 0 && c.groups * c.sl * c.heads * 16 < (int64_t)UINT_MAX * 256 / 2) {
+        bool gated = false;
         switch (c.vall) {
-        case 1: variate_vec<1>(c, s); break;
-        case 2: variate_vec<2>(c, s); break;
-        case 3: variate_vec<3>(c, s); break;
-        case 4: variate_vec<4>(c, s); break;
-        case 5: variate_vec<5>(c, s); break;
-        case 6: variate_vec<6>(c, s); break;
-        case 7: variate_vec<7>(c, s); break;
-        case 8: variate_vec<8>(c, s); break;
-        case 9: variate_vec<9>(c, s); break;
-        case 10: variate_vec<10>(c, s); break;
-        case 11: variate_vec<11>(c, s); break;
-        case 12: variate_vec<12>(c, s); break;
-        case 13: variate_vec<13>(c, s); break;
-        case 14: variate_vec<14>(c, s); break;
-        case 15: variate_vec<15>(c, s); break;
-        default: variate_vec<16>(c, s); break;
+        case 1: gated = variate_vec<1>(c, s); break;
+        case 2: gated = variate_vec<2>(c, s); break;
+        case 3: gated = variate_vec<3>(c, s); break;
+        case 4: gated = variate_vec<4>(c, s); break;
+        case 5: gated = variate_vec<5>(c, s); break;
+        case 6: gated = variate_vec<6>(c, s); break;
+        case 7: gated = variate_vec<7>(c, s); break;
+        case 8: gated = variate_vec<8>(c, s); break;
+        case 9: gated = variate_vec<9>(c, s); break;
+        case 10: gated = variate_vec<10>(c, s); break;
+        case 11: gated = variate_vec<11>(c, s); break;
+        case 12: gated = variate_vec<12>(c, s); break;
+        case 13: gated = variate_vec<13>(c, s); break;
+        case 14: gated = variate_vec<14>(c, s); break;
+        case 15: gated = variate_vec<15>(c, s); break;
+        default: gated = variate_vec<16>(c, s); break;
         }
         TSFM_CUDA(cudaGetLastError(), "timestral variate attention: launch");
+        if (c.gate && !gated)
+            return launch_ts_gate(c.o, c.ldo, c.gate, c.ldg, c.groups * c.vall * c.sl, c.d, c.dtype, s);
         return Status::ok();
     }
     const int64_t warps = c.groups * c.sl * c.heads;
     ts_variate_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(c);
     TSFM_CUDA(cudaGetLastError(), "timestral variate attention: launch");
+    if (c.gate) return launch_ts_gate(c.o, c.ldo, c.gate, c.ldg, c.groups * c.vall * c.sl, c.d, c.dtype, s);
     return Status::ok();
 }
 

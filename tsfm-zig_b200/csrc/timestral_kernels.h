@@ -82,7 +82,11 @@ struct TsVariateCall {
     const int8_t *roles = nullptr;
     int cov = 0;
     float scale = 0.125f;
+    // Optional output gate (nn.mulSigmoid): o *= sigmoid(gate[row, :]), gate rows at stride ldg.
+    const void *gate = nullptr;
+    int64_t ldg = 0;
 };
+// With c.gate set the output comes back gated.
 Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s);
 
 struct TsHeadCall {
