@@ -47,6 +47,9 @@ def parse_args():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--series", type=int, default=SERIES_PER_GPU)
     ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="series of the bolt-*/timestral workloads (default: the BASELINE.json config's batch; "
+                         "smaller batches are for profiling captures)")
     ap.add_argument("--csv-series", type=int, default=8192, help="series of the csv workload")
     ap.add_argument("--workload", default="chronos2",
                     choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv", "parse",
@@ -276,6 +279,8 @@ def run_family_workload(a):
         cfg = syn.timestral_config(d_model=1024, num_heads=16, mlp_hidden_dim=4096, num_layers=16, patch=32,
                                    context_length=4096, block_size=32)
         b, horizon, ctx = 128, 512, 4096
+    if a.batch:
+        b = a.batch
     w = syn.random_checkpoint(cfg, seed=20261201)
     model = Model(cfg, w)
     if a.workload.startswith("bolt"):
