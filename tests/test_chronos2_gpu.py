@@ -71,6 +71,26 @@ def test_tiny_matches_oracle(tiny, t, horizon):
     assert rel_err(got, want, x[:, -512:]) <= TOL
 
 
+@pytest.mark.parametrize("b,t,compute", [(8, 500, "f16"), (130, 512, "f16"), (130, 512, "bf16")])
+def test_fused_norm_path_matches_oracle(b, t, compute):
+    # d_model a multiple of 256: the time-attention RMSNorm of layers 1.. runs inside the previous
+    # layer's wo GEMM (16-bit copy of x * s_r * gamma plus per-tile sums of squares) and the QKV
+    # GEMM that reads it (rows scaled by rs / s_r). 130 series x 41 tokens (5,330 rows) takes the
+    # CTA-pair tiles, 8 series the single-CTA ones; norm weights are jittered so that a wrong
+    # gamma shows.
+    cfg = tiny_cfg(d_model=256, d_ff=512, num_heads=4, num_layers=3)
+    w = syn.random_checkpoint(cfg, seed=21, norm_jitter=0.1)
+    gpu = tb.Model(cfg, w, compute=compute)
+    ora = ob.OracleModel(gpu.parsed, w, tb.tensor_table)
+    x = syn.seeded_series(b, t, seed=31)
+    x[1, :] = np.nan
+    x[2, 40:120] = np.nan
+    got = gpu.forecast_chronos2(x, 100)
+    want = ora.forecast_chronos2(x, 100)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want, x) <= (TOL if compute == "f16" else TOL_BF16_RANGE)
+
+
 def test_bf16_operands_run_and_stay_close(tiny):
     cfg, w, _, ora = tiny
     bf = tb.Model(cfg, w, compute="bf16")

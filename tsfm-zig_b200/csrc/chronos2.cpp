@@ -11,6 +11,7 @@
 // the REG token and the future-patch embeddings, identical for every series, are computed once
 // at load and broadcast. The head runs only on the future-patch rows.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "model.h"
@@ -181,6 +182,17 @@ static void c2_geometry(const tsfm_config &c, int64_t t_in, int64_t horizon, int
     seq = n_ctx + 1 + n_out;
 }
 
+// The time-attention RMSNorm of encoder layers 1.. runs inside the GEMMs around it
+// (LinearCall::norm_*) when d_model is a multiple of 256 and the operands are 16-bit;
+// TSFM_FUSED_NORM=0 keeps the separate norm kernel.
+static bool c2_fused_norm(const tsfm_config &c) {
+    static const bool on = [] {
+        const char *v = std::getenv("TSFM_FUSED_NORM");
+        return !(v && v[0] == '0');
+    }();
+    return on && c.d_model % 256 == 0;
+}
+
 static size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64_t horizon) {
     int64_t t, start, pad, n_ctx, n_out, seq;
     c2_geometry(c, t_in, horizon, t, start, pad, n_ctx, n_out, seq);
@@ -197,6 +209,10 @@ static size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64
     b += Arena::span(nb * n_out * q * ps * 4);
     b += Arena::span(nb * n_out * d * 4) * 2;   // head input, hi / lo
     b += Arena::span(nb * n_out * ff * 4) * 2;  // head hidden, hi / lo
+    if (c2_fused_norm(c)) {
+        b += Arena::span(rows * 4);              // row factors
+        b += Arena::span(rows * (d / 256) * 4);  // row sums of squares per column tile
+    }
     return b;
 }
 
@@ -224,6 +240,10 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
     float *raw = ws.take<float>(b * n_out * q * ps);
     float *hid_hi = ws.take<float>(b * n_out * d), *hid_lo = ws.take<float>(b * n_out * d);
     float *hh_hi = ws.take<float>(b * n_out * ff), *hh_lo = ws.take<float>(b * n_out * ff);
+    const bool fused = c2_fused_norm(c) && (w.act == E_F16 || w.act == E_BF16);
+    const int np = (int)(d / 256);
+    float *nS = fused ? ws.take<float>(rows) : nullptr;       // row factors of the MLP norm
+    float *nP = fused ? ws.take<float>(rows * np) : nullptr;  // row sums of squares per column tile
     if (ws.used > ws.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Chronos-2: workspace too small");
 
     // 1. instance norm + patch features (TF32-rounded FP32) + key validity.
@@ -265,6 +285,69 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
         TSFM_TRY(launch_broadcast_rows(x, b, seq, n_ctx + 1, w.fut_emb, n_out, d, s));
     }
     // 3. encoder layers.
+    if (fused) {
+        // The time-attention RMSNorm of layers 1.. is fused into the GEMMs around it: the previous
+        // layer's wo GEMM (K = d_ff, whose long main loop hides the extra epilogue work) also
+        // writes x * s_r * gamma in 16 bits to xn, s_r = the MLP norm's row factor, and the row's
+        // sums of squares per 256-column tile; the QKV GEMM multiplies its rows by rs / s_r. The
+        // other two norms stay separate: fused into the K = d_model residual GEMMs, the epilogue's
+        // residual reads outlast their main loop (measured slower than the separate norm kernel).
+        for (size_t li = 0; li < w.layers.size(); ++li) {
+            const C2Dev::Layer &L = w.layers[li];
+            LinearCall qc;
+            qc.rope_cos = w.rope_cos;
+            qc.rope_sin = w.rope_sin;
+            qc.rope_cols = (int)(2 * d);
+            qc.rope_p1 = 0;
+            qc.rope_p2 = seq;
+            if (li == 0) {
+                TSFM_TRY(op_rmsnorm(r, s, x, L.time_norm, xn, A16, rows, d, eps));
+            } else {
+                qc.norm_in = nP;
+                qc.norm_parts = np;
+                qc.norm_dim = d;
+                qc.norm_eps = eps;
+                qc.norm_s_in = nS;
+            }
+            TSFM_TRY(op_linear(r, s, L.qkv, xn, rows, d, qkv, 3 * d, A16, 0, &qc));
+            {
+                AttentionCall ac;
+                ac.err = static_cast<int *>(r.err.p);
+                ac.q = qkv;
+                ac.k = qkv + d;
+                ac.v = qkv + 2 * d;
+                ac.dtype = w.act;
+                ac.ld_qkv = 3 * d;
+                ac.o = ao;
+                ac.ld_o = d;
+                ac.key_valid = kv;
+                ac.kv_stride = seq;
+                ac.groups = (int)b;
+                ac.heads = (int)nh;
+                ac.n = (int)seq;
+                ac.scale = 1.0f;
+                ac.mask_mode = 0;
+                LaunchScope ls(r, s, K_ATTN, 4.0 * (double)b * nh * seq * seq * 64);
+                TSFM_TRY(launch_attention(ac, s));
+            }
+            TSFM_TRY(op_linear(r, s, L.o, ao, rows, d, x, d, OUT_F32_ACC, 0));
+            TSFM_TRY(op_rmsnorm(r, s, x, L.group_norm, xn, A16, rows, d, eps));
+            TSFM_TRY(op_linear(r, s, L.gvo, xn, rows, d, x, d, OUT_F32_ACC, 0));
+            const bool last = li + 1 == w.layers.size();
+            TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps, 0, 0, 0, last ? nullptr : nS));
+            TSFM_TRY(op_linear(r, s, L.wi, xn, rows, d, h, ff, A16, 1));
+            LinearCall wc;
+            if (!last) {
+                wc.norm_out = nP;
+                wc.norm_x16 = xn;
+                wc.ld_x16 = d;
+                wc.norm_gamma = w.layers[li + 1].time_norm;
+                wc.norm_s_in = nS;
+            }
+            TSFM_TRY(op_linear(r, s, L.wo, h, rows, ff, x, d, OUT_F32_ACC, 0, &wc));
+        }
+    }
+    if (!fused)
     for (const C2Dev::Layer &L : w.layers) {
         TSFM_TRY(op_rmsnorm(r, s, x, L.time_norm, xn, A16, rows, d, eps));
         LinearCall rope;

@@ -70,6 +70,27 @@ struct LinearCall {
     int rope_cols = 0;
     int64_t rope_p1 = 0, rope_p2 = 1;  // position index = (r / p1) * p2 + r % p2 (p1 == 0: r % p2)
     int *err = nullptr;                // device error word
+    // Fused RMSNorm (rmsNorm, core/nn.zig:367-396) across a residual GEMM and the GEMM that reads
+    // its normalised rows, without a pass of its own over the FP32 residual stream.
+    // Reader side (norm_in set): the product's row r is multiplied by rs / norm_s_in[r] (1 when
+    // norm_s_in is null) before bias, activation and RoPE, where
+    // rs = 1 / sqrt(sum_p norm_in[p * M + r] / norm_dim + norm_eps); rs goes to norm_s_out[r].
+    const float *norm_in = nullptr;
+    int norm_parts = 0;
+    int64_t norm_dim = 0;
+    float norm_eps = 1e-6f;
+    const float *norm_s_in = nullptr;
+    float *norm_s_out = nullptr;
+    // Residual side (norm_out set; out_mode OUT_F32_ACC, 16-bit operands, N % 256 == 0, no
+    // activation, remap or RoPE): y += result as usual, and also
+    //   norm_x16[r, c] = y[r, c] * s_r * norm_gamma[c] in the operand type, with s_r = rs of the
+    //   reader side when norm_in is set, else norm_s_in[r];
+    //   norm_out[(c / 256) * M + r] = sum over the 256 columns of column tile c / 256 of y[r, c]^2.
+    // Any positive s_r keeps the 16-bit copy in range; the next GEMM's reader side undoes it.
+    float *norm_out = nullptr;
+    void *norm_x16 = nullptr;
+    int64_t ld_x16 = 0;
+    const float *norm_gamma = nullptr;
 };
 Status launch_linear(const LinearCall &c, cudaStream_t stream);
 
@@ -135,6 +156,7 @@ struct RmsNormCall {
     float eps = 1e-6f;
     int64_t g = 0, G = 0, off = 0;
     const int64_t *rows_idx = nullptr;  // when set: in_row(r) = rows_idx[r]
+    float *inv_out = nullptr;           // when set: the row's factor 1 / sqrt(mean(x^2) + eps)
 };
 Status launch_rmsnorm(const RmsNormCall &c, cudaStream_t stream);
 

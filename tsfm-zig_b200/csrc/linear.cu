@@ -38,16 +38,18 @@ constexpr int kThreads = 192;
 
 // PAIR: the tile is 256 x BN, computed by a cluster of two CTAs with the 2-SM MMA; each CTA holds
 // 128 rows of x and BN / 2 rows of W per stage and 128 x BN accumulators.
-template <int BN, bool PAIR = false>
+// NORM: the residual epilogue of a fused RMSNorm (see Epi) needs a 2 KB staging box per epilogue
+// warp for the 16-bit row copy, paid for with one pipeline stage.
+template <int BN, bool PAIR = false, bool NORM = false>
 struct TileCfg {
-    static constexpr int STAGES = PAIR ? 6 : BN >= 256 ? 4 : 6;
+    static constexpr int STAGES = (PAIR ? 6 : BN >= 256 ? 4 : 6) - (NORM ? 1 : 0);
     static constexpr int A_BYTES = kBM * 128;
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
     static constexpr int B_BYTES = B_ROWS * 128;
     static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
     // Epilogue staging for the TMA stores: per epilogue warp two 4 KB boxes (32 rows x 128 B).
     static constexpr int STAGE_OFF = STAGES * (A_BYTES + B_BYTES);
-    static constexpr int STAGE_BYTES = 4 * 2 * 4096;
+    static constexpr int STAGE_BYTES = 4 * 2 * 4096 + (NORM ? 4 * 2048 : 0);
     static constexpr int SMEM = 1024 + STAGE_OFF + STAGE_BYTES + 256;
 };
 
@@ -65,6 +67,19 @@ struct Epi {
     int64_t rope_p1, rope_p2;    // position index = (r / p1) * p2 + r % p2 (p1 == 0: r % p2)
     int tma_mode;                // 0: per-thread stores; 1: TMA store of staged boxes; 2: TMA reduce-add (f32)
     int *err;
+    // Fused RMSNorm (LinearCall::norm_*). Reader side: rows scaled by rs / ns_in[r] with
+    // rs = 1 / sqrt(sum_p nin[p * M + r] / ndim + neps); rs written to ns_out[r] by column tile 0.
+    const float *nin;
+    int nparts;
+    float ndim, neps;
+    const float *ns_in;
+    float *ns_out;
+    // Residual side (NORM kernels): y += result, then nx16[r, c] = y[r, c] * xs * ngamma[c] in 16
+    // bits (xs = rs when nin is set, else ns_in[r]) and nout[tile * M + r] = sum over the tile of y^2.
+    float *nout;
+    void *nx16;
+    int64_t ldx16;
+    const float *ngamma;
 };
 
 // Activation over n values: 1 relu, 2 silu (nn.siluInPlace, core/nn.zig:399-407). The branch is
@@ -181,11 +196,11 @@ __device__ __forceinline__ void bias_act(const Epi &e, int64_t col0, int nvalid,
     if (e.out_mode != OUT_F32_ACC) apply_act<32>(e.act, v);
 }
 
-template <typename T, int BN, bool PAIR>
+template <typename T, int BN, bool PAIR, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmY, Epi e) {
-    using C = TileCfg<BN, PAIR>;
+    using C = TileCfg<BN, PAIR, NORM>;
     constexpr int STAGES = C::STAGES;
     constexpr int BK = 128 / (int)sizeof(T);
     // operand format: BF16 = 1, F16 = 0 (kind::f16); TF32 = 2 (kind::tf32)
@@ -434,7 +449,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         int acc = 0;
         uint32_t aph = 0;
+        // NORM: the old residual of this warp's 32 rows of a tile, prefetched into L2 one tile
+        // ahead (the epilogue then reads it from L2 instead of waiting on DRAM box by box).
+        auto prefetch_tile = [&](int64_t tt) {
+            if (!NORM || lane != 0 || tt >= tiles) return;
+            const int64_t r0 = (tt / n_tiles) * kRows + rank * kBM + eg * 32;
+            if (r0 >= e.M) return;
+            const int64_t c0 = (tt % n_tiles) * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) tma_prefetch_l2_2d(&tmY, (int32_t)(c0 + c), (int32_t)r0);
+        };
+        prefetch_tile(unit);
         for (int64_t t = unit; t < tiles; t += units) {
+            prefetch_tile(t + units);
             const int64_t mrow0 = (t / n_tiles) * kRows + rank * kBM;  // this CTA's first row of the tile
             const int64_t row = mrow0 + r_in_tile;
             const int64_t wrow0 = mrow0 + eg * 32;  // first row of this warp's box
@@ -461,6 +488,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                     rs[4 * q + 3] = s4.w;
                 }
             }
+            // Fused RMSNorm factors of this thread's row (loads issued before the accumulator wait).
+            float rsc = 1.0f, xs = 1.0f;
+            if (e.nin != nullptr) {
+                if (row_ok) {
+                    float sum = 0.0f;
+                    for (int p = 0; p < e.nparts; ++p) sum += e.nin[(int64_t)p * e.M + row];
+                    const float rs = 1.0f / sqrtf(sum / e.ndim + e.neps);
+                    rsc = e.ns_in ? rs / e.ns_in[row] : rs;
+                    xs = rs;
+                    if (e.ns_out && ncol0 == 0) e.ns_out[row] = rs;
+                }
+            } else if (NORM && e.ns_in != nullptr && row_ok) {
+                xs = e.ns_in[row];
+            }
+            // NORM: the old residual of the tile's first 32-column box, read in row-contiguous
+            // order (lane -> row wrow0 + 4 i + lane / 8, columns 4 (lane % 8) .. + 3).
+            float4 old_nxt[8];
+            auto load_old = [&](int64_t col0) {
+                const float *yb = reinterpret_cast<const float *>(e.out);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int64_t gr = wrow0 + 4 * i + (lane >> 3);
+                    old_nxt[i] = gr < e.M ? *reinterpret_cast<const float4 *>(yb + gr * e.ldo + col0 + 4 * (lane & 7))
+                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+            };
+            if constexpr (NORM) load_old(ncol0);
             // Warp-uniform wait: every lane polls the barrier, and the warp leaves together if any
             // lane gave up, so the .sync.aligned TMEM loads below always run converged.
             const bool got = PAIR ? mbar_wait_cl(&tfull[acc], aph, abort_flag, e.err, ERR_SITE_GEMM_EPILOGUE)
@@ -469,7 +523,85 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int64_t orow = e.rm_g > 0 ? (row / e.rm_g) * e.rm_G + row % e.rm_g + e.rm_off : row;
             const uint32_t tbase = tmem_base + ((uint32_t)(eg * 32) << 16) + (uint32_t)(acc * BN);
-            if (BN == 256 && e.act == ACT_GLU) {
+            if constexpr (NORM) {
+                // Residual with the next RMSNorm's inputs: per 32-column box, the old values pass
+                // through the staging box (row-contiguous global reads -> one row per thread), the
+                // new values leave by TMA store, and the scaled 16-bit copy passes through this
+                // warp's 2 KB box (64-byte rows, 16-byte chunks swizzled by (row / 2) % 4) to
+                // row-contiguous global stores.
+                uint8_t *xst = sStage + 4 * 2 * 4096 + eg * 2048;
+                float ss = 0.0f;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    const int64_t col0 = ncol0 + c;
+                    float4 cur[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) cur[i] = old_nxt[i];
+                    if (c + 32 < BN) load_old(col0 + 32);
+                    float v[32];
+                    tmem_ld32(tbase + c, v);
+                    uint8_t *b = stage_box();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int rr = 4 * i + (lane >> 3), q = lane & 7;
+                        *reinterpret_cast<float4 *>(b + rr * 128 + ((q ^ (rr & 7)) << 4)) = cur[i];
+                    }
+                    tmem_wait_ld();
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 o = *reinterpret_cast<const float4 *>(b + lane * 128 + ((q ^ (lane & 7)) << 4));
+                        v[4 * q] = v[4 * q] * rsc;
+                        v[4 * q + 1] = v[4 * q + 1] * rsc;
+                        v[4 * q + 2] = v[4 * q + 2] * rsc;
+                        v[4 * q + 3] = v[4 * q + 3] * rsc;
+                        if (e.bias) {
+                            v[4 * q] += __ldg(e.bias + col0 + 4 * q);
+                            v[4 * q + 1] += __ldg(e.bias + col0 + 4 * q + 1);
+                            v[4 * q + 2] += __ldg(e.bias + col0 + 4 * q + 2);
+                            v[4 * q + 3] += __ldg(e.bias + col0 + 4 * q + 3);
+                        }
+                        v[4 * q] += o.x;
+                        v[4 * q + 1] += o.y;
+                        v[4 * q + 2] += o.z;
+                        v[4 * q + 3] += o.w;
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) put16(b, q, make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                                                                        __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3])));
+                    issue_box(b, col0, wrow0);
+                    // 16-bit copy for the next GEMM: y * xs * gamma.
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 g0 = __ldg(reinterpret_cast<const float4 *>(e.ngamma + col0 + 8 * q));
+                        const float4 g1 = __ldg(reinterpret_cast<const float4 *>(e.ngamma + col0 + 8 * q + 4));
+                        const float *src = v + 8 * q;
+                        const float a0 = src[0] * xs * g0.x, a1 = src[1] * xs * g0.y, a2 = src[2] * xs * g0.z,
+                                    a3 = src[3] * xs * g0.w, a4 = src[4] * xs * g1.x, a5 = src[5] * xs * g1.y,
+                                    a6 = src[6] * xs * g1.z, a7 = src[7] * xs * g1.w;
+                        uint4 pk;
+                        pk.x = pack2<T>(a0, a1);
+                        pk.y = pack2<T>(a2, a3);
+                        pk.z = pack2<T>(a4, a5);
+                        pk.w = pack2<T>(a6, a7);
+                        *reinterpret_cast<uint4 *>(xst + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = pk;
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int rr = 8 * i + (lane >> 2), q = lane & 3;
+                        const uint4 pk = *reinterpret_cast<const uint4 *>(xst + rr * 64 + ((q ^ ((rr >> 1) & 3)) << 4));
+                        const int64_t gr = wrow0 + rr;
+                        if (gr < e.M)
+                            *reinterpret_cast<uint4 *>(reinterpret_cast<T *>(e.nx16) + gr * e.ldx16 + col0 + 8 * q) = pk;
+                    }
+                    __syncwarp();
+                }
+                if (row_ok) e.nout[(ncol0 / BN) * e.M + row] = ss;
+            } else if (BN == 256 && e.act == ACT_GLU) {
                 // Gated pairs: the tile's columns are [g (128) | u (128)]; output column
                 // (tile * 128 + c) = g[c] * silu(u[c]), staged and stored in 64-column boxes. The
                 // logistic uses the fast exponential and division intrinsics (a few ulp; the result
@@ -510,6 +642,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld32(tbase + c, lo);
                     tmem_ld32(tbase + c + 32, hi);
                     tmem_wait_ld();
+                    if (e.nin != nullptr) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            lo[j] *= rsc;
+                            hi[j] *= rsc;
+                        }
+                    }
                     if (rope_tile && col0 < e.rope_cols) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
@@ -544,6 +683,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float v[32];
                     tmem_ld32(tbase + c, v);
                     tmem_wait_ld();
+                    if (e.nin != nullptr) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] *= rsc;
+                    }
                     const int64_t rem = e.N - col0;
                     const int nv = rem < 32 ? (int)rem : 32;
                     bias_act(e, col0, nv, v);
@@ -654,16 +797,16 @@ Status ensure_smem_attr(const void *func, int bytes) {
 
 namespace {
 
-template <typename T, int BN, bool PAIR>
+template <typename T, int BN, bool PAIR, bool NORM = false>
 Status launch_t(const LinearCall &c, cudaStream_t stream) {
-    using C = TileCfg<BN, PAIR>;
+    using C = TileCfg<BN, PAIR, NORM>;
     constexpr int BK = 128 / (int)sizeof(T);
     CUtensorMap ta, tb;
     Status s = make_tmap(&ta, c.x, c.dtype, c.K, c.M, c.ldx, BK, kBM);
     if (!s) return s;
     s = make_tmap(&tb, c.w, c.dtype, c.K, c.N, c.ldw, BK, C::B_ROWS);
     if (!s) return s;
-    TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&linear_tc_kernel<T, BN, PAIR>), C::SMEM));
+    TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&linear_tc_kernel<T, BN, PAIR, NORM>), C::SMEM));
     cudaError_t ce;
     Epi e;
     e.M = c.M;
@@ -683,6 +826,16 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     e.rope_p1 = c.rope_p1;
     e.rope_p2 = c.rope_p2;
     e.err = c.err;
+    e.nin = c.norm_in;
+    e.nparts = c.norm_parts;
+    e.ndim = (float)c.norm_dim;
+    e.neps = c.norm_eps;
+    e.ns_in = c.norm_s_in;
+    e.ns_out = c.norm_s_out;
+    e.nout = c.norm_out;
+    e.nx16 = c.norm_x16;
+    e.ldx16 = c.ld_x16;
+    e.ngamma = c.norm_gamma;
     // TMA epilogue unless rows are remapped or an activation follows the accumulation; the
     // output base and row stride must suit a tensor map (16-byte alignment).
     const bool f32_out = c.out_mode == OUT_F32 || c.out_mode == OUT_F32_ACC || c.out_mode == OUT_TF32;
@@ -693,6 +846,11 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
         const int64_t ycols = c.act == ACT_GLU ? c.N / 2 : c.N;
         if (make_tmap(&ty, c.y, ydt, ycols, c.M, c.ldy, f32_out ? 32 : 64, 32).code == 0)
             e.tma_mode = c.out_mode == OUT_F32_ACC ? 2 : 1;
+    }
+    if constexpr (NORM) {
+        // The residual side reads the old rows itself and stores the new ones.
+        if (e.tma_mode != 2) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: fused norm needs an aligned f32 residual");
+        e.tma_mode = 1;
     }
     if (c.act == ACT_GLU && e.tma_mode != 1)
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: gated pairs need a 16-byte-aligned 16-bit output");
@@ -712,12 +870,12 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        ce = cudaLaunchKernelEx(&cfg, linear_tc_kernel<T, BN, true>, ta, tb, ty, e);
+        ce = cudaLaunchKernelEx(&cfg, linear_tc_kernel<T, BN, true, NORM>, ta, tb, ty, e);
         if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch (CTA pairs)");
     } else {
         const int64_t tiles = ((c.M + kBM - 1) / kBM) * ((c.N + BN - 1) / BN);
         const int grid = (int)std::min<int64_t>(tiles, sm_count());
-        linear_tc_kernel<T, BN, false><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, e);
+        linear_tc_kernel<T, BN, false, NORM><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, e);
     }
     ce = cudaGetLastError();
     if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch");
@@ -772,6 +930,21 @@ Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     if (c.act == ACT_GLU && (c.N % 256 || (c.out_mode != OUT_F16 && c.out_mode != OUT_BF16) || c.bias || c.rm_g > 0 ||
                              c.rope_cos || c.dtype == E_F32))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: gated pairs need N % 256 == 0, 16-bit operands and output");
+    if (c.norm_in && (c.norm_parts <= 0 || c.norm_dim <= 0 || c.act == ACT_GLU || c.norm_s_in == c.norm_s_out))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad fused-norm reader arguments");
+    if (c.norm_out) {
+        const bool ok = (c.dtype == E_F16 || c.dtype == E_BF16) && c.out_mode == OUT_F32_ACC && c.N % 256 == 0 &&
+                        c.act == 0 && c.rm_g <= 0 && !c.rope_cos && c.norm_x16 && c.norm_gamma && c.ld_x16 >= c.N &&
+                        c.ld_x16 % 8 == 0 && (reinterpret_cast<uintptr_t>(c.norm_x16) & 15) == 0 &&
+                        (reinterpret_cast<uintptr_t>(c.norm_gamma) & 15) == 0 && c.norm_x16 != c.x &&
+                        (c.norm_in || c.norm_s_in);
+        if (!ok) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad fused-norm residual arguments");
+        const bool pair = c.M >= 4096 && gemm_pairs_enabled();
+        if (c.dtype == E_F16)
+            return pair ? launch_t<__half, 256, true, true>(c, stream) : launch_t<__half, 256, false, true>(c, stream);
+        return pair ? launch_t<__nv_bfloat16, 256, true, true>(c, stream)
+                    : launch_t<__nv_bfloat16, 256, false, true>(c, stream);
+    }
     const bool small_n = c.N <= 128;
     // Large 16-bit products run on CTA pairs (2-SM MMA, 256 x 256 tiles): each SM then streams half
     // of W's tile instead of all of it.

@@ -45,8 +45,9 @@ Status op_linear(Replica &r, cudaStream_t s, const DLin &L, const void *x, int64
 }
 
 Status op_rmsnorm(Replica &r, cudaStream_t s, const float *x, const float *scale, void *out, int out_mode, int64_t rows,
-               int64_t dim, float eps, int64_t g, int64_t G, int64_t off) {
+               int64_t dim, float eps, int64_t g, int64_t G, int64_t off, float *inv_out) {
     RmsNormCall c;
+    c.inv_out = inv_out;
     c.x = x;
     c.scale = scale;
     c.out = out;

@@ -20,6 +20,7 @@ Status op_linear3(Replica &r, cudaStream_t s, const DLin3 &L, const float *x_hi,
 // Splits x [rows, cols] (row stride ld) in place into x_hi (written over x) and x_lo.
 Status op_split(Replica &r, cudaStream_t s, float *x, float *x_lo, int64_t rows, int64_t cols, int64_t ld);
 Status op_rmsnorm(Replica &r, cudaStream_t s, const float *x, const float *scale, void *out, int out_mode,
-                  int64_t rows, int64_t dim, float eps, int64_t g = 0, int64_t G = 0, int64_t off = 0);
+                  int64_t rows, int64_t dim, float eps, int64_t g = 0, int64_t G = 0, int64_t off = 0,
+                  float *inv_out = nullptr);
 
 }  // namespace tsfm

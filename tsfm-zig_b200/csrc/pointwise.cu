@@ -45,6 +45,7 @@ __global__ void rmsnorm_kernel(RmsNormCall c) {
     }
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / (float)c.dim + c.eps);
+    if (c.inv_out && lane == 0) c.inv_out[r] = inv;
     const int64_t ob = r * c.dim;
     if (vec) {
         for (int64_t i = lane * 4; i < c.dim; i += 128) {

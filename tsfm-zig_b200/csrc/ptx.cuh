@@ -208,6 +208,14 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const 
                  : "memory");
 }
 
+// 2-D tiled prefetch of the box at (c0 = innermost, c1) into L2 only: no shared memory, no
+// completion to wait for.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int32_t c0, int32_t c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until at most one of this thread's bulk groups still reads its shared-memory source.
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
