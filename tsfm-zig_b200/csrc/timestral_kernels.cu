@@ -568,32 +568,55 @@ __global__ void __launch_bounds__(256, V <= 11 ? 2 : 1) ts_variate_vec_kernel(Ts
     }
 }
 
-// The same attention on the tensor cores, one block per (group, token): the q / k / v slices of
-// the group's V rows (all heads) are staged in shared memory by asynchronous 16-byte copies (rows
-// padded to 16, row stride d + 8 elements so ldmatrix rows fall in different banks); one warp per
-// head computes S = Q K^T (16 x 16, k = 64: eight m16n8k16 MMAs), the masked softmax in registers
-// (rows spread over lane quads), and O = P V (16 x 64, k = 16: eight MMAs); the output rows go back
-// through shared memory (over the q slices) to coalesced 16-byte stores.
+// The same attention on the tensor cores, one block per (group, token, half of the heads): the
+// q / k / v slices of the group's V rows for those heads are staged in shared memory by
+// asynchronous 16-byte copies (rows padded to 16, row stride + 8 elements so ldmatrix rows fall in
+// different banks; ≈ 50 KB at 8 heads, four blocks per SM); one warp per head computes S = Q K^T
+// (16 x 16, k = 64: eight m16n8k16 MMAs), the masked softmax in registers (rows spread over lane
+// quads), and O = P V (16 x 64, k = 16: eight MMAs); the output rows go back through shared
+// memory (over the q slices) to coalesced 16-byte stores. The output gate's rows are loaded into
+// registers while the copies land, so the gated store phase waits on no global load.
 template <int V, bool F16>
-__global__ void __launch_bounds__(256) ts_variate_mma_kernel(TsVariateCall c) {
+__global__ void __launch_bounds__(256, 2) ts_variate_mma_kernel(TsVariateCall c, int nsplit) {
     static_assert(V <= 16, "at most 16 rows per group");
     extern __shared__ __align__(16) unsigned char vsm[];
-    const int rs = (int)c.d + 8;  // row stride (elements)
+    const int64_t dw = c.d / nsplit;  // columns of this block's heads
+    const int rs = (int)dw + 8;       // row stride (elements)
     uint16_t *qs = reinterpret_cast<uint16_t *>(vsm);
     uint16_t *ks = qs + 16 * rs;
     uint16_t *vs = ks + 16 * rs;
     __shared__ uint32_t s_valid;
-    const int64_t g = blockIdx.x / c.sl, tok = blockIdx.x % c.sl;
+    const int64_t gt = blockIdx.x / nsplit;
+    const int hs = (int)(blockIdx.x - gt * nsplit);
+    const int64_t g = gt / c.sl, tok = gt % c.sl;
     const int64_t r0 = g * V;
-    const int chunks = (int)(c.d / 8);
+    const int64_t hc0 = hs * dw;  // first column of this block's heads
+    const int chunks = (int)(dw / 8);
+    const int nt = (int)blockDim.x;
     const uint16_t *src = static_cast<const uint16_t *>(c.qkv);
-    for (int idx = threadIdx.x; idx < V * 3 * chunks; idx += blockDim.x) {
-        const int i = idx / (3 * chunks), rem = idx - i * 3 * chunks, sec = rem / chunks, ch = rem - sec * chunks;
-        const uint16_t *g16 = src + ((r0 + i) * c.sl + tok) * c.ld + sec * c.d + ch * 8;
+    // chunks is a power of two (checked on the host): the copy index splits by shifts.
+    const int csh = __ffs(chunks) - 1;
+    for (int idx = threadIdx.x; idx < V * 3 * chunks; idx += nt) {
+        const int seg = idx >> csh, ch = idx & (chunks - 1), i = seg / 3, sec = seg - 3 * i;
+        const uint16_t *g16 = src + ((r0 + i) * c.sl + tok) * c.ld + sec * c.d + hc0 + ch * 8;
         const uint32_t s16 = smem_u32(qs + sec * 16 * rs + i * rs + ch * 8);
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s16), "l"(g16) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
+    // This thread's gate chunks for the store phase (output chunk idx = threadIdx.x + nt k).
+    const uint16_t *gate = static_cast<const uint16_t *>(c.gate);
+    constexpr int kPre = 6;
+    uint4 gpre[kPre];
+    if (gate != nullptr) {
+#pragma unroll
+        for (int k = 0; k < kPre; ++k) {
+            const int idx = threadIdx.x + nt * k;
+            if (idx < V * chunks) {
+                const int i = idx >> csh, ch = idx & (chunks - 1);
+                gpre[k] = __ldg(reinterpret_cast<const uint4 *>(gate + ((r0 + i) * c.sl + tok) * c.ldg + hc0 + ch * 8));
+            }
+        }
+    }
     // Padding rows of K and V are zero (their P is 0; a zero row keeps 0 * row finite).
     if constexpr (V < 16) {
         for (int idx = threadIdx.x; idx < 2 * (16 - V) * chunks; idx += blockDim.x) {
@@ -614,7 +637,8 @@ __global__ void __launch_bounds__(256) ts_variate_mma_kernel(TsVariateCall c) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i0 = lane >> 2, i1 = i0 + 8;  // this thread's two query rows
     const int rq0 = (c.cov && i0 < V) ? c.roles[i0] : 0, rq1 = (c.cov && i1 < V) ? c.roles[i1] : 0;
-    for (int h = warp; h < c.heads; h += (int)(blockDim.x >> 5)) {
+    const int lheads = c.heads / nsplit;
+    for (int h = warp; h < lheads; h += (int)(blockDim.x >> 5)) {
         float sacc[2][4];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
@@ -685,22 +709,29 @@ __global__ void __launch_bounds__(256) ts_variate_mma_kernel(TsVariateCall c) {
     }
     __syncthreads();
     uint16_t *dst = static_cast<uint16_t *>(c.o);
-    const uint16_t *gate = static_cast<const uint16_t *>(c.gate);
-    for (int idx = threadIdx.x; idx < V * chunks; idx += blockDim.x) {
-        const int i = idx / chunks, ch = idx - i * chunks;
+    auto store = [&](int idx, bool pre, uint4 gp) {
+        const int i = idx >> csh, ch = idx & (chunks - 1);
         const int64_t row = (r0 + i) * c.sl + tok;
         uint4 v = *reinterpret_cast<const uint4 *>(qs + i * rs + ch * 8);
         if (gate != nullptr) {  // the gate kernel's arithmetic on the rounded output
             float x[8], gv[8];
             unpack8<F16>(v, x);
-            unpack8<F16>(*reinterpret_cast<const uint4 *>(gate + row * c.ldg + ch * 8), gv);
+            unpack8<F16>(pre ? gp : __ldg(reinterpret_cast<const uint4 *>(gate + row * c.ldg + hc0 + ch * 8)), gv);
 #pragma unroll
             for (int e = 0; e < 8; ++e) x[e] = x[e] / (1.0f + __expf(-gv[e]));
             v = pack8<F16>(x);
         }
-        *reinterpret_cast<uint4 *>(dst + row * c.ldo + ch * 8) = v;
+        *reinterpret_cast<uint4 *>(dst + row * c.ldo + hc0 + ch * 8) = v;
+    };
+#pragma unroll
+    for (int k = 0; k < kPre; ++k) {
+        const int idx = threadIdx.x + nt * k;
+        if (idx < V * chunks) store(idx, true, gpre[k]);
     }
+    for (int idx = threadIdx.x + nt * kPre; idx < V * chunks; idx += nt)
+        store(idx, false, make_uint4(0u, 0u, 0u, 0u));
 }
+
 
 __device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
@@ -1027,19 +1058,25 @@ template <int V>
 bool variate_vec(const TsVariateCall &c, cudaStream_t s) {  // true: gate applied
     // Block per (group, token) on the tensor cores when the rows are 16-byte aligned and the group's
     // slices (16 padded rows of q, k and v) fit.
-    const size_t smem = (size_t)3 * 16 * (c.d + 8) * 2;
+    // Heads split over two blocks of 128 threads when their count is even (four blocks per SM,
+    // each with half the copies, so one block's copies overlap another's arithmetic).
+    const int nsplit = c.heads % 2 == 0 ? 2 : 1;
+    const unsigned nthr = nsplit == 2 ? 128u : 256u;
+    const int64_t chunks = c.d / nsplit / 8;
+    const size_t smem = (size_t)3 * 16 * (c.d / nsplit + 8) * 2;
     const bool a16 = (reinterpret_cast<uintptr_t>(c.qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(c.o) & 15) == 0 &&
                      c.ld % 8 == 0 && c.d % 8 == 0 && c.ldo % 8 == 0 && c.d == (int64_t)c.heads * 64 &&
-                     (c.gate == nullptr || ((reinterpret_cast<uintptr_t>(c.gate) & 15) == 0 && c.ldg % 8 == 0));
-    if (a16 && smem <= 200 * 1024 && c.groups * c.sl <= INT_MAX) {
+                     (c.gate == nullptr || ((reinterpret_cast<uintptr_t>(c.gate) & 15) == 0 && c.ldg % 8 == 0)) &&
+                     chunks > 0 && (chunks & (chunks - 1)) == 0;
+    if (a16 && smem <= 200 * 1024 && c.groups * c.sl * nsplit <= INT_MAX) {
         const void *fn = c.dtype == E_F16 ? reinterpret_cast<const void *>(&ts_variate_mma_kernel<V, true>)
                                           : reinterpret_cast<const void *>(&ts_variate_mma_kernel<V, false>);
         if (ensure_smem_attr(fn, (int)smem)) {
-            const unsigned grid = (unsigned)(c.groups * c.sl);
+            const unsigned grid = (unsigned)(c.groups * c.sl * nsplit);
             if (c.dtype == E_F16)
-                ts_variate_mma_kernel<V, true><<<grid, 256, smem, s>>>(c);
+                ts_variate_mma_kernel<V, true><<<grid, nthr, smem, s>>>(c, nsplit);
             else
-                ts_variate_mma_kernel<V, false><<<grid, 256, smem, s>>>(c);
+                ts_variate_mma_kernel<V, false><<<grid, nthr, smem, s>>>(c, nsplit);
             return true;
         }
     }
