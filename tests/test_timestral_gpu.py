@@ -92,6 +92,21 @@ def test_univariate_matches_oracle(tiny, t, horizon):
     assert rel_err(got, want, x[:, :, -512:]) <= TOL
 
 
+@pytest.mark.parametrize("b", [4, 40])
+def test_fused_norm_path_matches_oracle(b):
+    # d_model a multiple of 256: the first RMSNorm of layers 1.. runs inside the previous layer's
+    # w3 GEMM (16-bit copy of x * s_r * gamma plus per-tile sums of squares) and the q/k/v/gate GEMM
+    # that reads it (rows scaled by rs / s_r), for time and variate layers; 40 groups of 3 rows
+    # reach the CTA-pair tiles. Norm weights are jittered so that a wrong gamma shows.
+    cfg = tiny_cfg(d_model=256, num_heads=4, mlp_hidden_dim=512, num_layers=3)
+    gpu, ora, _ = models(cfg, seed=19)
+    x = edge_inputs(b, 3, 260, seed=12)
+    got, want = run_both(gpu, ora, x, 40)
+    assert got.shape == (b, 3, 40, 9)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want, x) <= TOL
+
+
 def test_multivariate_matches_oracle(tiny):
     gpu, ora, _ = tiny
     x = edge_inputs(4, 3, 260, seed=8)

@@ -13,6 +13,7 @@
 // symmetric average and the non-negative clip.
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 
@@ -72,6 +73,19 @@ struct Block {
     bool cov;
 };
 
+// The first RMSNorm of layers 1.. runs inside the GEMMs around it (LinearCall::norm_*): the
+// previous layer's w3 GEMM (K = the MLP width, whose long main loop hides the extra epilogue
+// work) also writes x * s_r * gamma in 16 bits, s_r = the MLP norm's row factor, and the row's
+// sums of squares per 256-column tile; the layer's first q/k/v(/gate) GEMM multiplies its rows by
+// rs / s_r. Needs d_model a multiple of 256 and 16-bit operands; TSFM_FUSED_NORM=0 turns it off.
+static bool ts_fused_norm(const tsfm_config &c, int act) {
+    static const bool on = [] {
+        const char *v = std::getenv("TSFM_FUSED_NORM");
+        return !(v && v[0] == '0');
+    }();
+    return on && c.d_model % 256 == 0 && (act == E_F16 || act == E_BF16);
+}
+
 size_t block_workspace(const tsfm_config &c, const TsDev &w, const Block &k) {
     const int64_t d = c.d_model, hid = c.d_ff, q = c.num_quantiles, ps = k.ps;
     const int64_t R = k.groups * k.vall, hl = k.h * ps, wlen = k.cov ? k.t + hl : k.t, n = wlen / ps;
@@ -85,6 +99,7 @@ size_t block_workspace(const tsfm_config &c, const TsDev &w, const Block &k) {
     b += Arena::span(rows * std::max<int64_t>(2 * hid, 4 * d) * 2) + Arena::span(rows * hid * 2);
     b += Arena::span(nt * k.h * 8) + Arena::span(nt * 8);
     b += Arena::span(nt * k.h * d * 4) * 2 + Arena::span(nt * k.h * 4 * d * 4) * 2 + Arena::span(nt * hl * q * 4) * 2;
+    if (ts_fused_norm(c, w.act)) b += Arena::span(rows * 4) + Arena::span(rows * (d / 256) * 4);
     return b;
 }
 
@@ -117,6 +132,10 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
     float *hid_hi = ws.take<float>(nt * k.h * d), *hid_lo = ws.take<float>(nt * k.h * d);
     float *hh_hi = ws.take<float>(nt * k.h * 4 * d), *hh_lo = ws.take<float>(nt * k.h * 4 * d);
     float *raw = ws.take<float>(nt * hl * q);
+    const bool fused = ts_fused_norm(c, w.act);
+    const int np = (int)(d / 256);
+    float *nS = fused ? ws.take<float>(rows) : nullptr;       // row factors of the MLP norm
+    float *nP = fused ? ws.take<float>(rows * np) : nullptr;  // row sums of squares per column tile
     if (ws.used > ws.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Timestral: workspace too small");
 
     // 1. statistics, features, key validity, first observed patch.
@@ -172,12 +191,21 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
                                 target_row, s));
     }
     // 4. transformer (runTransformer, timestral/model.zig:434-482).
-    for (const TsDev::Layer &L : w.layers) {
+    for (size_t li = 0; li < w.layers.size(); ++li) {
+        const TsDev::Layer &L = w.layers[li];
         for (int ai = 0; ai < L.n_attn; ++ai) {
             const TsDev::Attn &a = L.attns[ai];
             const int64_t cols = a.qkvg.out;
-            TSFM_TRY(op_rmsnorm(r, s, x, a.norm, xn, A16, rows, d, eps));
+            const bool pre = fused && li > 0 && ai == 0;  // xn holds the previous w3's fused norm input
+            if (!pre) TSFM_TRY(op_rmsnorm(r, s, x, a.norm, xn, A16, rows, d, eps));
             LinearCall rope;
+            if (pre) {
+                rope.norm_in = nP;
+                rope.norm_parts = np;
+                rope.norm_dim = d;
+                rope.norm_eps = eps;
+                rope.norm_s_in = nS;
+            }
             if (a.is_time) {
                 rope.rope_cos = cs;
                 rope.rope_sin = sn;
@@ -185,7 +213,7 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
                 rope.rope_p1 = sl * k.vall;
                 rope.rope_p2 = sl;
             }
-            TSFM_TRY(op_linear(r, s, a.qkvg, xn, rows, d, qkvg, cols, A16, 0, a.is_time ? &rope : nullptr));
+            TSFM_TRY(op_linear(r, s, a.qkvg, xn, rows, d, qkvg, cols, A16, 0, (a.is_time || pre) ? &rope : nullptr));
             if (a.is_time) {
                 AttentionCall ac;
                 ac.err = static_cast<int *>(r.err.p);
@@ -238,7 +266,8 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
             }
             TSFM_TRY(op_linear(r, s, a.o, o16, rows, d, x, d, OUT_F32_ACC, 0));
         }
-        TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps));
+        const bool next = fused && li + 1 < w.layers.size();
+        TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps, 0, 0, 0, next ? nS : nullptr));
         if (L.glu) {
             TSFM_TRY(op_linear(r, s, L.w12, xn, rows, d, a16, hid, A16, ACT_GLU));
         } else {
@@ -246,7 +275,15 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
             LaunchScope ls(r, s, K_OTHER, (double)rows * hid * 6);
             TSFM_TRY(launch_ts_swiglu(h16, a16, rows, hid, w.act, s));
         }
-        TSFM_TRY(op_linear(r, s, L.w3, a16, rows, hid, x, d, OUT_F32_ACC, 0));
+        LinearCall wc;
+        if (next) {
+            wc.norm_out = nP;
+            wc.norm_x16 = xn;
+            wc.ld_x16 = d;
+            wc.norm_gamma = w.layers[li + 1].attns[0].norm;
+            wc.norm_s_in = nS;
+        }
+        TSFM_TRY(op_linear(r, s, L.w3, a16, rows, hid, x, d, OUT_F32_ACC, 0, &wc));
     }
     // 5. out_norm on the target rows' decoder tokens, FP32-accurate head, monotone quantiles.
     const int64_t mh = nt * k.h;
