@@ -39,6 +39,21 @@ HORIZON = 1024
 GF_PER_SERIES = 130.02  # algorithmic GFLOP per series at ctx 8192, H 1024 (2 FLOPs per MAC)
 
 
+def series_seed(rank, b):
+    """First generator seed of a rank's b series: ranks draw disjoint seeded blocks (weak scaling)."""
+    return 1000 + rank * b
+
+
+def max_over_ranks(x, world, device):
+    """The slowest rank's figure: an all-reduce MAX over the job (x itself when world == 1)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -597,7 +612,7 @@ def main():
     cfg, w, model = build_model(local)
     del w
     b, q = a.series, 21
-    x = syn.seeded_series(b, CONTEXT, seed=1000 + rank * b)
+    x = syn.seeded_series(b, CONTEXT, seed=series_seed(rank, b))
     xd = torch.from_numpy(x).cuda()
     out = torch.empty((b, HORIZON, q), device="cuda")
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
@@ -630,10 +645,7 @@ def main():
     clk.__exit__()
     torch.cuda.synchronize()
     barrier()
-    t = torch.tensor([total_ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step = t.item() / a.steps
+    ms_step = max_over_ranks(total_ms, world, "cuda") / a.steps
     value = b * world / (ms_step / 1e3)
 
     # End to end through the host entry point: pinned inputs in, quantiles out.
@@ -650,10 +662,7 @@ def main():
         model.forecast_chronos2(xnp, HORIZON, out=onp)
     e2e_s = (time.perf_counter() - t0) / a.steps
     barrier()
-    te = torch.tensor([e2e_s], device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e = b * world / te.item()
+    e2e = b * world / max_over_ranks(e2e_s, world, "cuda")
 
     # Per-kernel-class timing (events around every launch) on separate, untimed steps.
     model.profile(True)
