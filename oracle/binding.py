@@ -21,6 +21,8 @@ def _load():
     sig = {
         "oracle_set_threads": (I32, [I32]),
         "oracle_get_threads": (I32, []),
+        "oracle_set_operand_emulation": (I32, [I32]),
+        "oracle_set_operand_emulation_class": (I32, [I32, I32]),
         "oracle_last_error": (ctypes.c_char_p, []),
         "oracle_model_create": (I32, [P, P, SZ, ctypes.POINTER(P)]),
         "oracle_model_destroy": (None, [P]),
@@ -61,7 +63,7 @@ def check(st):
 
 
 class OracleModel:
-    """A checkpoint loaded into the CPU restatement. `parsed` is a tsfm_b200.config.ParsedConfig."""
+    """A checkpoint loaded into the CPU restatement. `parsed` is a tsfm_spec.config.ParsedConfig."""
 
     def __init__(self, parsed, tensors, table_fn):
         table, keep = table_fn(tensors)

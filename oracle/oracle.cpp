@@ -19,6 +19,9 @@
 namespace oracle {
 void matmul_nt_packed(const float *x, const float *wt, float *y, size_t rows, size_t out, size_t in,
                       float alpha);
+void emul_matmul(float *y, const float *x, size_t rows, const float *w, size_t out, size_t in, int scheme,
+                 bool tf32);
+float emul_store16(float v, int scheme);
 }
 
 namespace {
@@ -30,6 +33,34 @@ const float kInf = std::numeric_limits<float>::infinity();
 struct Fail {
     int32_t code;
 };
+
+// Precision study (oracle_set_operand_emulation, oracle_emul.cpp): when g_emul is non-zero, the
+// Chronos-2 forward rounds the operands of its products the way the device's reduced-precision
+// tensor-core products consume them. g_emul_scope is set around each product by the caller:
+// 0 = not emulated (FP32, e.g. the FP32-accurate head), 1 = TF32 device operands, 2 = 16-bit
+// device operands. g_emul_class names the product (0 unnamed, 1 q/k/v, 2 attention output o,
+// 3 group v, 4 group o, 5 MLP wi, 6 MLP wo, 7 patch-embedding output); g_emul_by_class[c] >= 0
+// overrides the scheme for that class. Off (0) by default: the restatement's own arithmetic is
+// the reference's FP32.
+int g_emul = 0;
+int g_emul_scope = 0;
+int g_emul_class = 0;
+int g_emul_by_class[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
+struct EmulScope {
+    int saved, saved_class;
+    explicit EmulScope(int s, int cls = -1) : saved(g_emul_scope), saved_class(g_emul_class) {
+        g_emul_scope = s;
+        if (cls >= 0) g_emul_class = cls;
+    }
+    ~EmulScope() {
+        g_emul_scope = saved;
+        g_emul_class = saved_class;
+    }
+};
+int emul_scheme() {
+    const int o = g_emul_by_class[g_emul_class & 7];
+    return o >= 0 ? o : g_emul;
+}
 [[noreturn]] void fail(int32_t code, const std::string &msg) {
     g_err = msg;
     throw Fail{code};
@@ -55,7 +86,10 @@ struct Weight {
 
 // nn.linear (core/nn.zig:270-293): y = x w^T, then bias added per row (linearCols :252-258).
 void linear(float *y, const float *x, size_t rows, const Weight &w, const float *bias) {
-    oracle::matmul_nt_packed(x, w.wt.data(), y, rows, w.out, w.in, 1.0f);
+    if (g_emul != 0 && g_emul_scope != 0 && emul_scheme() != 0)
+        oracle::emul_matmul(y, x, rows, w.data.data(), w.out, w.in, emul_scheme(), g_emul_scope == 1);
+    else
+        oracle::matmul_nt_packed(x, w.wt.data(), y, rows, w.out, w.in, 1.0f);
     if (bias)
         for (size_t r = 0; r < rows; ++r)
             for (size_t j = 0; j < w.out; ++j) y[r * w.out + j] += bias[j];
@@ -228,6 +262,8 @@ void self_attend(Mask mask, float *scores, const float *q, const float *k, const
     gemm_nt(scores, n, q, ldq, k, ldk, n, n, hd, scale);
     if (bias) add_in_place(scores, bias, n * n);
     masked_softmax(mask, scores, n, key_valid);
+    if (g_emul != 0 && g_emul_scope == 2)
+        for (size_t i = 0; i < n * n; ++i) scores[i] = oracle::emul_store16(scores[i], g_emul);
     gemm_nn(o, ldo, scores, n, v, ldv, n, hd, n);
 }
 
@@ -237,16 +273,27 @@ struct ResBlock {
     std::vector<float> hb, ob, rb;
     bool bias = true;
     bool silu = false;
+    // Emulation scopes of the three products (precision study only): input side and output.
+    int emul_in = 0, emul_out = 0;
     void forward(float *y, const float *x, size_t rows) const {
         std::vector<float> h(rows * hidden.out);
-        linear(h.data(), x, rows, hidden, bias ? hb.data() : nullptr);
+        {
+            EmulScope sc(emul_in);
+            linear(h.data(), x, rows, hidden, bias ? hb.data() : nullptr);
+        }
         if (silu)
             for (auto &e : h) e = silu_vec(e);
         else
             relu(h.data(), h.size());
-        linear(y, h.data(), rows, output, bias ? ob.data() : nullptr);
+        {
+            EmulScope sc(emul_out, 7);
+            linear(y, h.data(), rows, output, bias ? ob.data() : nullptr);
+        }
         std::vector<float> r(rows * output.out);
-        linear(r.data(), x, rows, residual, bias ? rb.data() : nullptr);
+        {
+            EmulScope sc(emul_in);
+            linear(r.data(), x, rows, residual, bias ? rb.data() : nullptr);
+        }
         add_in_place(y, r.data(), rows * output.out);
     }
 };
@@ -368,6 +415,8 @@ struct Chronos2 {
     void load(const Table &w) {
         const size_t d = c.d_model, ps = c.patch_size, hid = c.d_ff, q = c.num_quantiles;
         input_embed = w.resblock("input_patch_embedding", 3 * ps, hid, d, true, false);
+        input_embed.emul_in = 1;   // device: TF32 patch features
+        input_embed.emul_out = 2;  // device: 16-bit hidden activations
         output_embed = w.resblock("output_patch_embedding", d, hid, q * ps, true, false);
         final_norm = w.get("encoder.final_layer_norm.weight", d);
         std::vector<float> shared = w.get("shared.weight", 2 * d);
@@ -414,8 +463,10 @@ struct Chronos2 {
                 sin_t[tok * half + i] = std::sin(ang);
             }
         const Mask mask = mask_pick(false, all_valid, true);
+        EmulScope enc_scope(2, 0);  // every encoder product takes 16-bit device operands
         for (const C2Layer &L : layers) {
             rms_norm(xn.data(), x, rows, d, L.time.norm.data(), eps);
+            g_emul_class = 1;
             linear(qb.data(), xn.data(), rows, L.time.q, nullptr);
             linear(kb.data(), xn.data(), rows, L.time.k, nullptr);
             linear(vb.data(), xn.data(), rows, L.time.v, nullptr);
@@ -426,6 +477,12 @@ struct Chronos2 {
                     rope_half(&kb[r * d + h * hd], &cos_t[tok * half], &sin_t[tok * half], half);
                 }
             }
+            if (g_emul != 0)  // q, k, v stored in 16 bits on the device
+                for (size_t i = 0; i < rows * d; ++i) {
+                    qb[i] = oracle::emul_store16(qb[i], g_emul);
+                    kb[i] = oracle::emul_store16(kb[i], g_emul);
+                    vb[i] = oracle::emul_store16(vb[i], g_emul);
+                }
 #pragma omp parallel
             {
                 std::vector<float> scores(seq * seq);
@@ -436,17 +493,22 @@ struct Chronos2 {
                                 d, seq, hd, 1.0f, key_valid + r * seq, nullptr);
                 }
             }
+            g_emul_class = 2;
             linear(delta.data(), ab.data(), rows, L.time.o, nullptr);
             add_in_place(x, delta.data(), rows * d);
 
             rms_norm(xn.data(), x, rows, d, L.group.norm.data(), eps);
+            g_emul_class = 3;
             linear(vb.data(), xn.data(), rows, L.group.v, nullptr);
+            g_emul_class = 4;
             linear(delta.data(), vb.data(), rows, L.group.o, nullptr);
             add_in_place(x, delta.data(), rows * d);
 
             rms_norm(xn.data(), x, rows, d, L.mlp_norm.data(), eps);
+            g_emul_class = 5;
             linear(mlp_h.data(), xn.data(), rows, L.wi, nullptr);
             relu(mlp_h.data(), mlp_h.size());
+            g_emul_class = 6;
             linear(delta.data(), mlp_h.data(), rows, L.wo, nullptr);
             add_in_place(x, delta.data(), rows * d);
         }
@@ -1788,6 +1850,17 @@ int32_t oracle_set_threads(int32_t n) {
     return TSFM_OK;
 }
 int32_t oracle_get_threads(void) { return omp_get_max_threads(); }
+int32_t oracle_set_operand_emulation(int32_t scheme) {
+    if (scheme < 0 || scheme > 7) return TSFM_ERR_INVALID_ARGUMENT;
+    g_emul = scheme;
+    for (int &c : g_emul_by_class) c = -1;
+    return TSFM_OK;
+}
+int32_t oracle_set_operand_emulation_class(int32_t cls, int32_t scheme) {
+    if (cls < 1 || cls > 7 || scheme < -1 || scheme > 7) return TSFM_ERR_INVALID_ARGUMENT;
+    g_emul_by_class[cls] = scheme;
+    return TSFM_OK;
+}
 const char *oracle_last_error(void) { return g_err.c_str(); }
 
 int32_t oracle_model_create(const tsfm_config *cfg, const tsfm_tensor *tensors, size_t n_tensors,

@@ -31,6 +31,13 @@ typedef struct oracle_model oracle_model;
 
 int32_t oracle_set_threads(int32_t n);
 int32_t oracle_get_threads(void);
+/* Precision study only (oracle_emul.cpp): 0 (default) = the reference's FP32 arithmetic; 1-7 =
+ * the Chronos-2 forward with operands rounded as a reduced-precision device product consumes
+ * them (schemes listed in oracle_emul.cpp). Process-wide; not for concurrent forecasts. */
+int32_t oracle_set_operand_emulation(int32_t scheme);
+/* Overrides the scheme for one class of products (1 q/k/v, 2 attention output, 3 group v, 4 group
+ * o, 5 MLP wi, 6 MLP wo, 7 patch-embedding output; -1 = back to the global scheme). */
+int32_t oracle_set_operand_emulation_class(int32_t cls, int32_t scheme);
 const char *oracle_last_error(void);
 
 int32_t oracle_model_create(const tsfm_config *cfg, const tsfm_tensor *tensors, size_t n_tensors,

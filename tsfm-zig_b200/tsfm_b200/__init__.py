@@ -1,7 +1,9 @@
 """tsfm_b200: B200-native forecast backend for tsfm-zig checkpoints (Chronos-2, Chronos-Bolt,
 Timestral). The compute lives in libtsfm_b200.so (sm_100a CUDA + C++ behind a C ABI); this
 package is its Python binding."""
-from . import config, csv, series, synthetic
+from tsfm_spec import config, synthetic
+
+from . import csv, series
 from ._native import (LIB_PATH, STATUS_NAMES, TsfmError, check, device_count, last_error, lib)
 from .model import Model, covariates, tensor_table, timestral_options
 

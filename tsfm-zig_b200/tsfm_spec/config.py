@@ -8,7 +8,7 @@ rest.
 """
 import ctypes
 
-from ._native import FAMILY, LAYER_KIND, Config
+from .abi import FAMILY, LAYER_KIND, Config
 
 REGISTRY_ORDER = ("timestral", "chronos2", "chronos_bolt")
 FAMILY_NAMES = {"timestral": "Timestral", "chronos2": "Chronos-2", "chronos_bolt": "Chronos-Bolt"}
