@@ -6,7 +6,8 @@ pool may own all device memory). For them the library keeps its scratch in a fix
 own. This test checks, on two calls in a row, that the allocation-free entry point returns what
 the ordinary seam entry point tsfm_sgemm_nt returns (same 1e-4 tolerance as the seam's own test),
 that device free memory does not change across a call once the first call has set the array up,
-and that a product too large for the array is rejected rather than run.
+that strided operands leave the padding of C untouched, and that the size limit holds exactly on
+both sides of its boundary (a product too large for the array is rejected rather than run).
 
 The file is named to be collected last, so a run that stops at the first failure has already run
 every other test; it passes alone in a fresh process as well.
@@ -63,6 +64,49 @@ def test_noalloc_matches_seam_on_two_calls_in_a_row():
         assert (C.double() - ref).abs().max().item() <= 1e-4
 
 
+def test_noalloc_strided_operands_keep_padding():
+    # Row strides above the logical widths: lda, ldb > k and ldc > n (a multiple of 4, so the
+    # output goes through the TMA-store epilogue). The padding columns of C hold NaN sentinels that
+    # must survive; the padding of A and B holds NaN that must never be read.
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator().manual_seed(99)
+    m, n, k, lda, ldb, ldc = 200, 72, 100, 112, 104, 80
+    Ab = torch.full((m, lda), float("nan"))
+    Bb = torch.full((n, ldb), float("nan"))
+    Ab[:, :k] = torch.rand(m, k, generator=g) * 2 - 1
+    Bb[:, :k] = torch.rand(n, k, generator=g) * 2 - 1
+    Ab, Bb = Ab.to(dev), Bb.to(dev)
+    Cb = torch.full((m, ldc), float("nan"), device=dev)
+    st = tb.lib.tsfm_sgemm_nt_noalloc(m, n, k, 1.0, Ab.data_ptr(), lda, Bb.data_ptr(), ldb, Cb.data_ptr(), ldc,
+                                      stream)
+    assert st == 0, tb.last_error()
+    ref = Ab[:, :k].double() @ Bb[:, :k].double().T
+    assert (Cb[:, :n].double() - ref).abs().max().item() <= 1e-4
+    assert torch.isnan(Cb[:, n:]).all()
+
+
+def test_noalloc_limit_on_both_sides_of_the_boundary():
+    # k = 64: the four split parts take (m + n) * 64 floats each pair, and the array holds
+    # 2^21 - 64 floats of parts: m + n = 32767 is the largest product that fits.
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device=dev).manual_seed(5)
+    k, n = 64, 767
+    for m, ok in ((32000, True), (32001, False)):
+        A = torch.rand(m, k, device=dev, generator=g) * 2 - 1
+        B = torch.rand(n, k, device=dev, generator=g) * 2 - 1
+        C = torch.zeros(m, n, device=dev)
+        st = tb.lib.tsfm_sgemm_nt_noalloc(m, n, k, 1.0, A.data_ptr(), k, B.data_ptr(), k, C.data_ptr(), n, stream)
+        if ok:
+            assert st == 0, tb.last_error()
+            ref = A.double() @ B.double().T
+            assert (C.double() - ref).abs().max().item() <= 1e-4
+        else:
+            assert tb.STATUS_NAMES[st] == "INVALID_ARGUMENT"
+            assert "scratch limit" in tb.last_error()
+
+
 def test_noalloc_rejects_products_beyond_its_scratch():
     dev = torch.device("cuda:0")
     m, n, k = 2048, 2048, 1024  # (m + n) * k = 4M floats > 2M
@@ -71,4 +115,4 @@ def test_noalloc_rejects_products_beyond_its_scratch():
     C = torch.zeros(m, n, device=dev)
     st = noalloc(A, B, C, 1.0, torch.cuda.current_stream().cuda_stream)
     assert tb.STATUS_NAMES[st] == "INVALID_ARGUMENT"
-    assert "scratch" in tb.last_error()
+    assert "scratch limit" in tb.last_error()

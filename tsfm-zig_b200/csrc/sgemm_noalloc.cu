@@ -7,10 +7,14 @@
 // B, and the device error word) lives in the file-scope array below, a fixed 16 MiB that every GPU
 // which loads the library holds until the process exits.
 //
-// Limits and sharing: the split operands must fit the array, (m + n) * round_up(k, 4) <= 2^21 - 64
-// floats; larger products are rejected with TSFM_ERR_INVALID_ARGUMENT. Every call shares the one
-// array and its contents persist from the previous call, so the error word is cleared on entry;
-// calls that overlap on the GPU (other host threads, or other streams) race on the array.
+// Limits and sharing: the array holds the error word (256 bytes) and four split operands, A's hi and
+// lo parts of m * round_up(k, 4) floats and B's of n * round_up(k, 4), each sub-buffer rounded up
+// to 64 floats (256 bytes). So a product fits when
+//   round_up(m * round_up(k, 4), 64) + round_up(n * round_up(k, 4), 64) <= 2^21 - 64 floats
+// (for k a multiple of 64: m + n <= 32767); larger products are rejected with
+// TSFM_ERR_INVALID_ARGUMENT before anything runs. Every call shares the one array and its contents
+// persist from the previous call, so the error word is cleared on entry; calls that overlap on the
+// GPU (other host threads, or other streams) race on the array.
 //
 // Set-up: the first call on each device looks up the array's device address with
 // cudaGetSymbolAddress (with that device current) and caches it; that lookup may load this
@@ -25,7 +29,8 @@ namespace {
 
 constexpr size_t kScratchBytes = size_t(16) << 20;          // 16 MiB
 constexpr size_t kHeaderBytes = 256;                          // device error word + padding
-constexpr size_t kMaxSplitFloats = (kScratchBytes - kHeaderBytes) / sizeof(float) / 2;  // hi + lo
+// Floats for one hi and one lo part of each operand, sub-buffers in 64-float steps: 2^21 - 64.
+constexpr int64_t kMaxPartFloats = (int64_t)((kScratchBytes - kHeaderBytes) / sizeof(float) / 2) / 64 * 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
@@ -54,18 +59,17 @@ Status run(int m, int n, int k, float alpha, const float *A, int lda, const floa
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm_noalloc: bad operands");
     const int64_t kp = (k + 3) / 4 * 4;  // TF32 rows padded to 16-byte strides for the tensor map
     const int64_t need_m = (int64_t)m * kp, need_n = (int64_t)n * kp;
-    if (need_m + need_n + 64 > (int64_t)kMaxSplitFloats)
+    const auto span = [](int64_t floats) { return (floats + 63) / 64 * 64; };  // 256-byte sub-buffers
+    if (span(need_m) + span(need_n) > kMaxPartFloats)
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT,
-                            strf("sgemm_noalloc: (m + n) * round_up(k, 4) = %lld exceeds the %zu-float scratch limit",
-                                 (long long)(need_m + need_n), kMaxSplitFloats - 64));
+                            strf("sgemm_noalloc: round_up(m*round_up(k,4),64) + round_up(n*round_up(k,4),64) = %lld "
+                                 "exceeds the scratch limit of %lld floats",
+                                 (long long)(span(need_m) + span(need_n)), (long long)kMaxPartFloats));
     void *base = nullptr;
     TSFM_TRY(scratch_address(&base));
     int *err = static_cast<int *>(base);
     float *split = reinterpret_cast<float *>(static_cast<char *>(base) + kHeaderBytes);
-    const auto span = [](int64_t floats) { return (floats + 63) / 64 * 64; };  // 256-byte sub-buffers
     float *ahi = split, *alo = ahi + span(need_m), *bhi = alo + span(need_m), *blo = bhi + span(need_n);
-    if ((size_t)((blo + span(need_n)) - split) * sizeof(float) > kScratchBytes - kHeaderBytes)
-        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm_noalloc: operands exceed the scratch array");
     TSFM_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s), "sgemm_noalloc: clear error word");
     TSFM_TRY(launch_split_tf32(A, m, k, lda, alpha, ahi, alo, kp, s));
     TSFM_TRY(launch_split_tf32(B, n, k, ldb, 1.0f, bhi, blo, kp, s));
