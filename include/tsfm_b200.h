@@ -78,11 +78,18 @@ typedef enum tsfm_dtype {
 
 /* Operand type of the tensor-core contractions; accumulation and the residual stream are always
  * FP32. F16 and BF16 run at the same tensor-core rate; F16 keeps 3 more mantissa bits (the
- * precision of TF32), BF16 the FP32 exponent range. TF32 is reserved. */
+ * precision of TF32), BF16 the FP32 exponent range. TF32 is reserved.
+ * F16C ("FP16, corrected") adds to every FP16 product the two first-order rounding terms
+ * x_hi * (W - f16(W)) + (x - x_hi) * f16(W), computed as FP8 (E4M3) products with power-of-two
+ * scales into the same FP32 accumulator: weights and activations act as if kept to about 15
+ * significant bits, at twice the tensor-core work of F16 (the FP8 rate is twice the FP16 rate).
+ * It is the mode that meets the 1e-2 * scale forecast bound at Chronos-2's full shape (F16
+ * alone does not). Chronos-2 only for now. */
 typedef enum tsfm_compute {
     TSFM_COMPUTE_BF16 = 0,
     TSFM_COMPUTE_TF32 = 1,
-    TSFM_COMPUTE_F16 = 2
+    TSFM_COMPUTE_F16 = 2,
+    TSFM_COMPUTE_F16C = 3
 } tsfm_compute;
 
 /* Timestral layer kinds, the entries of `block_schedule` (timestral/config.zig:94-100). */
@@ -279,6 +286,18 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
                            const float *bias, void *y, int32_t out_mode, int32_t act,
                            int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldy,
                            void *stream);
+
+/* tsfm_kernel_linear_corrected: the corrected product of TSFM_COMPUTE_F16C on FP32 device inputs
+ * x [M, K] and W [N, K] (dense rows, K % 8 == 0): both are split into FP16 operands and FP8
+ * correction companions exactly as a TSFM_COMPUTE_F16C model holds them, then
+ * y[M, N] (dense) = act(x W^T + bias) with out_mode 0 = FP16 (and, when y8 is not null, its FP8
+ * companion [M, 2N] bytes: e4m3(y16 / 32) then e4m3((y - y16) * 128)), 1 = store f32,
+ * 2 = accumulate into f32; act 0 none, 1 relu. Allocates its temporaries on `stream` and returns
+ * after the product is enqueued. The kernel-level test of nn.linear's corrected form
+ * (core/nn.zig:270-293). */
+int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float *bias, void *y,
+                                     void *y8, int32_t out_mode, int32_t act, int64_t M, int64_t N,
+                                     int64_t K, void *stream);
 
 /* tsfm_kernel_attention: o = softmax(mask(scale · q k^T + bias)) v per (group, head) over `n`
  * tokens of head width 64, q/k/v bf16 with row stride ld_qkv (elements), o bf16 with row stride

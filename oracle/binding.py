@@ -23,6 +23,7 @@ def _load():
         "oracle_get_threads": (I32, []),
         "oracle_set_operand_emulation": (I32, [I32]),
         "oracle_set_operand_emulation_class": (I32, [I32, I32]),
+        "oracle_set_operand_emulation_tf32": (I32, [I32]),
         "oracle_last_error": (ctypes.c_char_p, []),
         "oracle_model_create": (I32, [P, P, SZ, ctypes.POINTER(P)]),
         "oracle_model_destroy": (None, [P]),

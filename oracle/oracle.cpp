@@ -20,7 +20,7 @@ namespace oracle {
 void matmul_nt_packed(const float *x, const float *wt, float *y, size_t rows, size_t out, size_t in,
                       float alpha);
 void emul_matmul(float *y, const float *x, size_t rows, const float *w, size_t out, size_t in, int scheme,
-                 bool tf32);
+                 bool tf32, bool tf32_round);
 float emul_store16(float v, int scheme);
 }
 
@@ -46,6 +46,7 @@ int g_emul = 0;
 int g_emul_scope = 0;
 int g_emul_class = 0;
 int g_emul_by_class[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
+bool g_emul_tf32_round = false;  // round TF32-operand products in every scheme
 struct EmulScope {
     int saved, saved_class;
     explicit EmulScope(int s, int cls = -1) : saved(g_emul_scope), saved_class(g_emul_class) {
@@ -87,7 +88,8 @@ struct Weight {
 // nn.linear (core/nn.zig:270-293): y = x w^T, then bias added per row (linearCols :252-258).
 void linear(float *y, const float *x, size_t rows, const Weight &w, const float *bias) {
     if (g_emul != 0 && g_emul_scope != 0 && emul_scheme() != 0)
-        oracle::emul_matmul(y, x, rows, w.data.data(), w.out, w.in, emul_scheme(), g_emul_scope == 1);
+        oracle::emul_matmul(y, x, rows, w.data.data(), w.out, w.in, emul_scheme(), g_emul_scope == 1,
+                            g_emul_tf32_round);
     else
         oracle::matmul_nt_packed(x, w.wt.data(), y, rows, w.out, w.in, 1.0f);
     if (bias)
@@ -1854,6 +1856,11 @@ int32_t oracle_set_operand_emulation(int32_t scheme) {
     if (scheme < 0 || scheme > 7) return TSFM_ERR_INVALID_ARGUMENT;
     g_emul = scheme;
     for (int &c : g_emul_by_class) c = -1;
+    g_emul_tf32_round = false;
+    return TSFM_OK;
+}
+int32_t oracle_set_operand_emulation_tf32(int32_t round) {
+    g_emul_tf32_round = round != 0;
     return TSFM_OK;
 }
 int32_t oracle_set_operand_emulation_class(int32_t cls, int32_t scheme) {

@@ -38,6 +38,9 @@ int32_t oracle_set_operand_emulation(int32_t scheme);
 /* Overrides the scheme for one class of products (1 q/k/v, 2 attention output, 3 group v, 4 group
  * o, 5 MLP wi, 6 MLP wo, 7 patch-embedding output; -1 = back to the global scheme). */
 int32_t oracle_set_operand_emulation_class(int32_t cls, int32_t scheme);
+/* Rounds the operands of TF32-operand products (the patch features' products) to TF32 in every
+ * scheme, not only in 1 and 5 (reset by oracle_set_operand_emulation). */
+int32_t oracle_set_operand_emulation_tf32(int32_t round);
 const char *oracle_last_error(void);
 
 int32_t oracle_model_create(const tsfm_config *cfg, const tsfm_tensor *tensors, size_t n_tensors,

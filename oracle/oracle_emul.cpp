@@ -17,7 +17,7 @@
 // floor(log2(448 / max|w|)) + 12), so every correction product carries the scale 2^(sb-5) and the
 // FP16 product's weight w_hi 2^(sb-5) stays within FP16's range (at most 448 * 128 = 57344).
 // Products with TF32 device operands round both operands to TF32 (round to nearest, ties away) in
-// schemes 1 and 5 and stay FP32 otherwise.
+// schemes 1 and 5, and in the other schemes when `tf32_round` is set (FP32 otherwise).
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -69,7 +69,7 @@ static int floor_log2(double v) { return (int)std::floor(std::log2(v)); }
 
 // y[rows, out] = x w^T under `scheme`; `tf32` marks a product with TF32 device operands.
 void emul_matmul(float *y, const float *x, size_t rows, const float *w, size_t out, size_t in, int scheme,
-                 bool tf32) {
+                 bool tf32, bool tf32_round) {
     const size_t nx = rows * in, nw = out * in;
     std::vector<float> wt(nw), xa(nx), wa(nw);
     auto transpose_into = [&](const std::vector<float> &src, std::vector<float> &dst) {
@@ -77,7 +77,7 @@ void emul_matmul(float *y, const float *x, size_t rows, const float *w, size_t o
             for (size_t c = 0; c < in; ++c) dst[c * out + r] = src[r * in + c];
     };
     if (tf32) {
-        const bool round = scheme == 1 || scheme == 5;
+        const bool round = scheme == 1 || scheme == 5 || tf32_round;
         for (size_t i = 0; i < nw; ++i) wa[i] = round ? round_tf32(w[i]) : w[i];
         for (size_t i = 0; i < nx; ++i) xa[i] = round ? round_tf32(x[i]) : x[i];
         transpose_into(wa, wt);

@@ -17,7 +17,8 @@ operand precision meets the 1e-2 * sigma bound before any kernel is written for 
 A run is a scheme number, optionally followed by per-class overrides: "6:2=2,6=2" applies scheme
 6 to every 16-bit product except the attention output (class 2) and the MLP's wo (class 6),
 which take scheme 2 (classes: 1 q/k/v, 2 attention output, 3 group v, 4 group o, 5 MLP wi,
-6 MLP wo, 7 patch-embedding output).
+6 MLP wo, 7 patch-embedding output). A trailing "t" ("2t") also rounds the TF32-operand
+products of the patch features to TF32, as a single-pass TF32 product on the device does.
 """
 import argparse
 import os
@@ -65,8 +66,10 @@ def main():
     print(f"FP32 reference: {a.series} series in {time.time() - t0:.1f} s", flush=True)
     for run in [r.strip() for r in a.runs.split(";") if r.strip()]:
         base, _, over = run.partition(":")
-        sc = int(base)
+        tf32 = base.endswith("t")
+        sc = int(base.rstrip("t"))
         ob.check(ob.lib.oracle_set_operand_emulation(sc))
+        ob.check(ob.lib.oracle_set_operand_emulation_tf32(int(tf32)))
         for item in [o for o in over.split(",") if o]:
             cls, _, sch = item.partition("=")
             ob.check(ob.lib.oracle_set_operand_emulation_class(int(cls), int(sch)))
@@ -75,7 +78,7 @@ def main():
         ob.check(ob.lib.oracle_set_operand_emulation(0))
         err = np.abs(got - ref) / sig
         per = err.reshape(a.series, -1).max(axis=1)
-        label = SCHEMES[sc] + (f"; overrides {over}" if over else "")
+        label = SCHEMES[sc] + ("; TF32 patch products" if tf32 else "") + (f"; overrides {over}" if over else "")
         print(f"run {run} ({label}): max |dq|/sigma = {err.max():.3e}, p99 = "
               f"{np.quantile(err, 0.99):.3e}, per series max = "
               f"[{', '.join(f'{v:.2e}' for v in per)}] ({time.time() - t0:.1f} s)", flush=True)

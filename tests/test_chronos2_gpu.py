@@ -6,9 +6,11 @@ Tolerance: max |dq| <= 1e-2 * sigma per series (the BF16-class bound), sigma = t
 std of the observed context (the instance-norm scale), plus 4 float32 ulps of the larger of |q|
 and |loc|: the reference itself stores q = sinh(v) * sigma + loc in float32, so two correct
 implementations can differ by that much (it matters only for near-constant series, where sigma
-falls to 1e-5). The default compute type is FP16 operands with FP32 accumulation (the BF16
-tensor-core rate); BF16 operands are checked against a looser bound, since their 8-bit
-significand cannot meet 1e-2 * sigma once sinh amplifies the head's output."""
+falls to 1e-5). The tiny configs run FP16 operands with FP32 accumulation; the full BASELINE
+shape meets the bound in the corrected mode (FP16 + FP8 correction products, TSFM_COMPUTE_F16C),
+which is tested there and on the tiny configs too. BF16 operands are checked against a looser
+bound, since their 8-bit significand cannot meet 1e-2 * sigma once sinh amplifies the head's
+output."""
 import numpy as np
 import pytest
 
@@ -162,27 +164,63 @@ def test_argument_errors(tiny):
         gpu.forecast_chronos2(np.zeros((0, 32), np.float32), 8)
 
 
-def test_full_shape_chronos2_matches_oracle():
-    # BASELINE configs[2] shape: 768-d, 12 layers, ctx 8192, H 1024 (2 series; the oracle needs
-    # ~130 GFLOP per series).
-    #
-    # Bound: |dq| <= 1e-2 * sigma * max(1, cosh(v) / cosh(2)), v = asinh((q - loc) / sigma) the
-    # model's pre-sinh output. Inside |v| <= 2 this is the plain 1e-2 * sigma bound; beyond it the
-    # same error in v is allowed, since q = sinh(v) * sigma + loc multiplies any error in v by
-    # cosh(v) (6.8 at |v| = 2.6). An oracle that rounds the encoder's GEMM operands to FP16
-    # reproduces the GPU's tail error (1.8e-2 vs 1.65e-2 sigma), so the tail term is the 10-bit
-    # significand of single-pass FP16 operands, not a path difference. The p99 stays below 5e-3.
+@pytest.mark.parametrize("t,horizon", [(500, 100), (33, 17)])
+def test_tiny_corrected_matches_oracle(tiny, t, horizon):
+    # TSFM_COMPUTE_F16C on the edge inputs (all missing, constant, long gaps, t not a multiple of
+    # the patch): the corrected products write and read the FP8 companions of every GEMM input.
+    cfg, w, _, ora = tiny
+    gpu = tb.Model(cfg, w, compute="f16c")
+    x = edge_inputs(t)
+    got = gpu.forecast_chronos2(x, horizon)
+    want = ora.forecast_chronos2(x, horizon)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want, x[:, -512:]) <= TOL
+
+
+@pytest.mark.parametrize("b", [8, 130])
+def test_fused_norm_corrected_matches_oracle(b):
+    # The corrected products through the fused-norm GEMMs (the wo epilogue writes the next layer's
+    # FP16 input and its FP8 companion), single-CTA (8 series) and CTA-pair (130 series) tiles.
+    cfg = tiny_cfg(d_model=256, d_ff=512, num_heads=4, num_layers=3)
+    w = syn.random_checkpoint(cfg, seed=21, norm_jitter=0.1)
+    gpu = tb.Model(cfg, w, compute="f16c")
+    ora = ob.OracleModel(gpu.parsed, w, tb.tensor_table)
+    x = syn.seeded_series(b, 512, seed=31)
+    x[1, :] = np.nan
+    x[2, 40:120] = np.nan
+    got = gpu.forecast_chronos2(x, 100)
+    want = ora.forecast_chronos2(x, 100)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want, x) <= TOL
+
+
+def full_shape(compute, b, seed=100):
     cfg = syn.chronos2_config()
     w = syn.random_checkpoint(cfg, seed=20261201)
-    gpu = tb.Model(cfg, w)
+    gpu = tb.Model(cfg, w, compute=compute)
     ora = ob.OracleModel(gpu.parsed, w, tb.tensor_table)
-    x = syn.seeded_series(2, 8192, seed=100)
+    x = syn.seeded_series(b, 8192, seed=seed)
     got = gpu.forecast_chronos2(x, 1024)
     want = ora.forecast_chronos2(x, 1024)
     assert np.isfinite(got).all()
-    sig = instance_scale(x)[:, None, None]
-    loc = np.array([np.nanmean(r) for r in x])[:, None, None]
-    v = np.arcsinh((want - loc) / sig)
-    err = np.abs(got - want) / sig
-    assert np.max(err / np.maximum(1.0, np.cosh(v) / np.cosh(2.0))) <= TOL
+    return got, want, x
+
+
+def test_full_shape_chronos2_matches_oracle():
+    # BASELINE configs[2] shape (768-d, 12 layers, ctx 8192, H 1024) on 8 series in the corrected
+    # mode (TSFM_COMPUTE_F16C), against the plain bound max |dq| <= 1e-2 * sigma on every quantile,
+    # the tails included. (oracle/precision_study.py predicts 2.7e-3 for this scheme.)
+    got, want, x = full_shape("f16c", 8)
+    err = np.abs(got - want) / instance_scale(x)[:, None, None]
+    assert np.max(err) <= TOL
+    assert np.quantile(err, 0.99) <= 1e-3
+
+
+def test_full_shape_plain_f16_characterised():
+    # Single-pass FP16 operands at the same shape: not a parity claim (the tails exceed 1e-2 *
+    # sigma: q = sinh(v) * sigma + loc multiplies the error of v by cosh(v)); a sanity bound and
+    # the bulk of the distribution only.
+    got, want, x = full_shape("f16", 2)
+    err = np.abs(got - want) / instance_scale(x)[:, None, None]
+    assert np.max(err) <= 5e-2
     assert np.quantile(err, 0.99) <= 5e-3

@@ -1,5 +1,7 @@
 """Kernel-level parity on the GPU, through the C ABI: the tcgen05 linear kernel against a torch
-fp32 reference of the same product (BF16 and TF32 operands, partial tiles, every epilogue), the
+fp32 reference of the same product (BF16 and TF32 operands, partial tiles, every epilogue), its
+corrected form (FP16 + FP8 correction terms) against float64 with its FP8 companion output bit for
+bit, the
 flash-attention kernel against a float64 reference of the reference's masks, RMSNorm against the
 oracle, and the reference's own padded-stride GEMM-seam test (core/gpu_test.zig:56-101)."""
 import ctypes
@@ -274,3 +276,64 @@ def test_gemm_seam_padded_strides_like_reference_gpu_test():
     assert tb.lib.tsfm_sgemm_nn(m, n, k, a.ctypes.data, lda, bnn.ctypes.data, ldb, out.ctypes.data, ldc, None) == 0
     np.testing.assert_allclose(o[:, :n], A @ BNN, atol=1e-4)
     assert np.all(o[:, n:] == -12345.0)
+
+
+# Corrected products (TSFM_COMPUTE_F16C): FP16 operands plus the FP8 first-order correction terms.
+CORR_SHAPES = [(300, 336, 48), (1000, 768, 768), (257, 128, 3072), (4096, 2304, 768), (4500, 1000, 1032),
+               (7, 64, 200)]
+
+
+def linear_corrected(x, w, bias, y, y8, out_mode, act):
+    M, K = x.shape
+    N = w.shape[0]
+    tb.check(tb.lib.tsfm_kernel_linear_corrected(x.data_ptr(), w.data_ptr(), None if bias is None else bias.data_ptr(),
+                                                 y.data_ptr(), None if y8 is None else y8.data_ptr(), out_mode, act,
+                                                 M, N, K, stream_ptr()))
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("M,N,K", CORR_SHAPES)
+def test_linear_corrected_matches_float64(M, N, K):
+    # The corrected product of FP32 x and W against float64: every element within 2^-12 of
+    # sum_k |x_k w_k| (twice the first-order bound; a single FP16 product is off by up to 2^-10), and the RMS error at
+    # least 8x below that of the plain FP16 product of the same operands.
+    g = torch.Generator(device="cpu").manual_seed(M * 5 + N + K)
+    x = torch.randn(M, K, generator=g).to(dev())
+    w = (torch.randn(N, K, generator=g) * 0.05).to(dev())
+    bias = torch.randn(N, generator=g).to(dev())
+    ref = x.double() @ w.double().T + bias.double()
+    mag = x.double().abs() @ w.double().abs().T + bias.double().abs()
+    y = torch.full((M, N), float("nan"), device=dev())
+    linear_corrected(x, w, bias, y, None, 1, 0)
+    err = (y.double() - ref).abs()
+    assert (err <= 2.0 ** -12 * mag + 1e-6).all()
+    y16 = torch.full((M, N), float("nan"), device=dev())
+    linear(x.half(), w.half(), bias, y16, 1, 0, M, N, K)
+    rms = lambda t: t.pow(2).mean().sqrt().item()  # noqa: E731
+    assert rms(err) * 8 <= rms(y16.double() - ref)
+    # accumulate mode
+    base = torch.randn(M, N, generator=g).to(dev())
+    y2 = base.clone()
+    linear_corrected(x, w, None, y2, None, 2, 0)
+    assert ((y2.double() - base.double() - (ref - bias.double())).abs() <= 2.0 ** -12 * mag + 1e-5).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 320, 48), (4096, 2304, 768), (257, 128, 3072)])
+def test_linear_corrected_fp8_companion_bits(M, N, K):
+    # A 16-bit output with its FP8 companion: y16 = f16(y) and the companion's bytes are exactly
+    # e4m3(y16 / 32) and e4m3((y - y16) * 128), with y the same product stored in f32.
+    from helpers import e4m3_bits
+    g = torch.Generator(device="cpu").manual_seed(M + N + K + 1)
+    x = torch.randn(M, K, generator=g).to(dev())
+    w = (torch.randn(N, K, generator=g) * 0.05).to(dev())
+    bias = torch.randn(N, generator=g).to(dev())
+    y32 = torch.zeros((M, N), device=dev())
+    linear_corrected(x, w, bias, y32, None, 1, 1)
+    y16 = torch.zeros((M, N), device=dev(), dtype=torch.float16)
+    y8 = torch.zeros((M, 2 * N), device=dev(), dtype=torch.uint8)
+    linear_corrected(x, w, bias, y16, y8, 0, 1)
+    a32, a16, a8 = y32.cpu().numpy(), y16.cpu().numpy(), y8.cpu().numpy()
+    assert np.array_equal(a16.view(np.uint16), a32.astype(np.float16).view(np.uint16))
+    h = a16.astype(np.float32)
+    assert np.array_equal(a8[:, :N], e4m3_bits(h * np.float32(1 / 32)))
+    assert np.array_equal(a8[:, N:], e4m3_bits((a32 - h) * np.float32(128)))

@@ -146,3 +146,13 @@ def test_oracle_threads_do_not_change_results():
         ys.append(y)
     ob.set_threads(orig)
     assert np.array_equal(ys[0], ys[1])
+
+
+def test_e4m3_encoder_known_values():
+    # The test-side E4M3 encoder used for the FP8 companions: exact values, subnormals, rounding
+    # to nearest even at a tie, saturation.
+    from helpers import e4m3_bits
+    vals = np.array([0.0, 2.0 ** -9, 2.0 ** -6, 1.0, 1.125, 1.0625, 1.1875, 448.0, 500.0, -1.5, 2.0 ** -10,
+                     3 * 2.0 ** -10, 240.0, 0.0146484375], np.float32)
+    want = [0x00, 0x01, 0x08, 0x38, 0x39, 0x38, 0x3A, 0x7E, 0x7E, 0xBC, 0x00, 0x02, 0x77, 0x08]
+    assert e4m3_bits(vals).tolist() == want

@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
 Status launch_attention(const AttentionCall &c, cudaStream_t stream) {
     if (c.groups <= 0 || c.heads <= 0 || c.n <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: empty");
     if (c.force_path == 1 || (c.force_path == 0 && attention_tc_supported(c))) return launch_attention_tc(c, stream);
+    if (c.o8) return Status::fail(TSFM_ERR_UNSUPPORTED, "attention: FP8 companion output on the tcgen05 path only");
     if ((c.ld_qkv % 8) || (c.ld_o % 2) || (reinterpret_cast<uintptr_t>(c.q) & 15) ||
         (reinterpret_cast<uintptr_t>(c.k) & 15) || (reinterpret_cast<uintptr_t>(c.v) & 15))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: q/k/v must be 16-byte aligned with ld % 8 == 0");

@@ -37,6 +37,7 @@
 
 #include "kernels.h"
 #include "ptx.cuh"
+#include "x8.cuh"
 
 #include <cuda_fp16.h>
 
@@ -95,6 +96,10 @@ struct TcParams {
     int64_t items;
     float scale_log2;
     int *err;
+    // FP8 companion of the FP16 output (corrected products): row (g * n + i) at o8 + row * ld_o8,
+    // head h's 64 values at byte h * 64, their low parts o8_half bytes further.
+    uint8_t *o8;
+    int64_t ld_o8, o8_half;
 };
 
 template <bool F16>
@@ -138,7 +143,9 @@ __device__ __forceinline__ void item_range(const TcParams &p, int64_t &first, in
 
 // Registers are allocated for warps in groups of four; 12 warps x 32 x 168 = 64,512 of the SM's
 // 65,536. One CTA per SM (the shared memory and the 512 TMEM columns allow no second one).
-template <bool F16>
+// O8: also writes the FP8 companion of the FP16 output (corrected products; a separate instance, so
+// the plain kernel keeps its registers).
+template <bool F16, bool O8 = false>
 __global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, TcParams p) {
@@ -401,6 +408,7 @@ __global__ void __maxnreg__(168)
         bool ok = true;
         // This warp's rows of the previous item still wait in TMEM (not past n).
         bool prev_live = false;
+        Item prev_im{0, 0, 0};
         // Reads this thread's row of the previous item's O, normalises it by the row sum and writes
         // it as 16-bit values into that item's Q buffer in the 128-byte-swizzled layout of a TMA
         // box (16-byte chunk c of row r at chunk c ^ (r % 8)).
@@ -408,11 +416,16 @@ __global__ void __maxnreg__(168)
             const float l = *l_save;
             const float inv = l > 0.0f ? __frcp_rn(l) : 0.0f;
             uint8_t *row = smem + q * PIPE_BYTES + OFF_Q + prev_slot * kTileBytes + r * 128;
+            // The FP8 companion goes straight to global memory (rows past n are not written).
+            uint8_t *row8 = nullptr;
+            if (O8 && prev_im.q0 + r < n)
+                row8 = p.o8 + ((int64_t)prev_im.g * n + prev_im.q0 + r) * p.ld_o8;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[32];
                 tmem_ld32(t_o + 32 * h, v);
                 tmem_wait_ld();
+                if (row8 != nullptr) store_x8_32(row8, p.o8_half, (int64_t)prev_im.h * 64 + 32 * h, v, inv);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const int chunk = (4 * h + c) ^ (r & 7);
@@ -570,6 +583,7 @@ __global__ void __maxnreg__(168)
             if (!ok) break;
             mbar_arrive(&b.m_empty[slot]);
             prev_live = !dead;
+            prev_im = im;
             *l_save = l_run;
         }
         // The last item's output, once its last PV is done; one more p_ready phase tells the
@@ -630,8 +644,16 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     p.items = (int64_t)c.groups * c.heads * p.qtiles;
     p.scale_log2 = c.scale * 1.4426950408889634f;
     p.err = c.err;
+    p.o8 = static_cast<uint8_t *>(c.o8);
+    p.ld_o8 = c.ld_o8;
+    p.o8_half = width;
+    if (c.o8 && (c.dtype != E_F16 || c.ld_o8 % 16 || c.ld_o8 < 2 * width || (reinterpret_cast<uintptr_t>(c.o8) & 15)))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: an FP8 companion needs an FP16 output");
     const int64_t grid = std::min<int64_t>((p.items + 1) / 2, num_sms());
-    if (c.dtype == E_F16) {
+    if (c.dtype == E_F16 && c.o8) {
+        TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<true, true>), kSmemTc));
+        attn_tc_kernel<true, true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
+    } else if (c.dtype == E_F16) {
         TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<true>), kSmemTc));
         attn_tc_kernel<true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
     } else {

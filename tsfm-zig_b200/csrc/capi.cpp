@@ -264,9 +264,13 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
     return guarded([&]() -> Status {
         if (!config || !out || (!tensors && n_tensors)) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null argument");
         *out = nullptr;
-        if (compute != TSFM_COMPUTE_BF16 && compute != TSFM_COMPUTE_F16)
-            return Status::fail(TSFM_ERR_UNSUPPORTED, "compute type: TSFM_COMPUTE_BF16 and TSFM_COMPUTE_F16 are implemented");
-        const int act = compute == TSFM_COMPUTE_F16 ? E_F16 : E_BF16;
+        if (compute != TSFM_COMPUTE_BF16 && compute != TSFM_COMPUTE_F16 && compute != TSFM_COMPUTE_F16C)
+            return Status::fail(TSFM_ERR_UNSUPPORTED,
+                                "compute type: TSFM_COMPUTE_BF16, TSFM_COMPUTE_F16 and TSFM_COMPUTE_F16C are implemented");
+        if (compute == TSFM_COMPUTE_F16C && config->family != TSFM_CHRONOS2)
+            return Status::fail(TSFM_ERR_UNSUPPORTED, "TSFM_COMPUTE_F16C: Chronos-2 only in this build");
+        // act: the weights' upload type (E_F16C: FP16 operands with FP8 correction companions).
+        const int act = compute == TSFM_COMPUTE_F16C ? E_F16C : compute == TSFM_COMPUTE_F16 ? E_F16 : E_BF16;
         std::unique_ptr<tsfm_model> m(new tsfm_model());
         m->cfg = *config;
         if (config->num_quantiles > 0 && config->quantiles)
@@ -573,6 +577,52 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
         c.act = act;
         c.err = kernel_err_word();
         return launch_linear(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float *bias, void *y, void *y8,
+                                     int32_t out_mode, int32_t act, int64_t M, int64_t N, int64_t K, void *stream) {
+    return guarded([&]() -> Status {
+        if (!x || !w || !y) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        if (M <= 0 || N <= 0 || K <= 0 || K % 8) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad shape");
+        if (out_mode < 0 || out_mode > 2 || (act != 0 && act != 1) || (y8 && out_mode != 0))
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode / act / y8");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        // Temporaries: the FP16 operands and their FP8 companions, as a corrected model holds them.
+        void *buf = nullptr;
+        const size_t xb = Arena::span((size_t)(M * K) * 2), wb = Arena::span((size_t)(N * K) * 2);
+        TSFM_CUDA(cudaMallocAsync(&buf, 2 * xb + 2 * wb, st), "linear (corrected): temporaries");
+        char *x16 = static_cast<char *>(buf), *x8 = x16 + xb, *w16 = x8 + xb, *w8 = w16 + wb;
+        int sh = 0;
+        Status res = launch_split_x8(x, M, K, K, x16, K, x8, 2 * K, st);
+        if (res) res = build_corrected_weight(w, N, K, w16, w8, &sh, st);
+        if (res) {
+            LinearCall c;
+            c.x = x16;
+            c.w = w16;
+            c.dtype = E_F16;
+            c.M = M;
+            c.N = N;
+            c.K = K;
+            c.ldx = K;
+            c.ldw = K;
+            c.y = y;
+            c.ldy = N;
+            c.out_mode = out_mode == 0 ? OUT_F16 : out_mode == 1 ? OUT_F32 : OUT_F32_ACC;
+            c.bias = bias;
+            c.act = act;
+            c.err = kernel_err_word();
+            c.x8 = x8;
+            c.ldx8 = 2 * K;
+            c.w8 = w8;
+            c.ldw8 = 2 * K;
+            c.acc_scale = std::ldexp(1.0f, -sh);
+            c.y8 = y8;
+            c.ldy8 = 2 * N;
+            res = launch_linear(c, st);
+        }
+        cudaFreeAsync(buf, st);
+        return res;
     });
 }
 

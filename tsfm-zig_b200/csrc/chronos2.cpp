@@ -6,7 +6,9 @@
 //   flash attention (scale 1, T5 key mask);  x += o Wo^T (accumulate epilogue);
 //   rmsnorm(x) -> xn;  v = xn Wv^T;  x += v Wo^T  (singleton-group attention, model.zig:265-269);
 //   rmsnorm(x) -> xn;  h = relu(xn Wi^T);  x += h Wo^T.
-// The residual stream x stays FP32 in HBM; GEMM operands are BF16 with FP32 accumulation.
+// The residual stream x stays FP32 in HBM; GEMM operands are FP16 (or BF16) with FP32
+// accumulation; in the corrected mode (TSFM_COMPUTE_F16C) every 16-bit GEMM input is written with
+// its FP8 companion and every product adds the FP8 correction terms (kernels.h).
 // The patch embedding writes straight into each series' sequence rows (row-remapped epilogue);
 // the REG token and the future-patch embeddings, identical for every series, are computed once
 // at load and broadcast. The head runs only on the future-patch rows.
@@ -71,7 +73,10 @@ Status c2_check_tensors(const tsfm_config &c, const TensorTable &t) {
 
 Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, C2Dev &w) {
     const int64_t d = c.d_model, ps = c.patch_size, hid = c.d_ff, q = c.num_quantiles;
-    w.act = act;
+    // act: the 16-bit weights' upload type; E_F16C = FP16 weights with FP8 correction companions
+    // (FP16 activations, each GEMM input written with its companion).
+    w.corr = act == E_F16C;
+    w.act = w.corr ? E_F16 : act;
     // The patch features enter a TF32 product (K = 3 * patch); every other product takes 16-bit
     // operands of type `act`.
     TSFM_TRY(load_resblock(r, t, "input_patch_embedding", 3 * ps, hid, d, true, E_F32, act, w.in_embed));
@@ -160,12 +165,19 @@ Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, 
     float *d_ff = nullptr;
     TSFM_TRY(upload_f32(r, ff, &d_ff));
     TSFM_TRY(upload_f32(r, std::vector<float>(nf * d, 0.0f), &w.fut_emb));
-    DevBuf tmp;
+    DevBuf tmp, tmp8;
     TSFM_TRY(tmp.alloc(nf * hid * 2));  // 16-bit hidden activations
+    LinearCall hx, ox;                   // their FP8 companion (corrected products)
+    if (w.corr) {
+        TSFM_TRY(tmp8.alloc(nf * hid * 2));
+        hx.y8 = tmp8.p;
+        ox.x8 = tmp8.p;
+        hx.ldy8 = ox.ldx8 = 2 * hid;
+    }
     cudaStream_t s = r.stream;
-    TSFM_TRY(op_linear(r, s, w.in_embed.hidden, d_ff, nf, 3 * ps, tmp.p, hid, out_mode_for(act), 1));
+    TSFM_TRY(op_linear(r, s, w.in_embed.hidden, d_ff, nf, 3 * ps, tmp.p, hid, out_mode_for(w.act), 1, &hx));
     TSFM_TRY(op_linear(r, s, w.in_embed.residual, d_ff, nf, 3 * ps, w.fut_emb, d, OUT_F32, 0));
-    TSFM_TRY(op_linear(r, s, w.in_embed.output, tmp.p, nf, hid, w.fut_emb, d, OUT_F32_ACC, 0));
+    TSFM_TRY(op_linear(r, s, w.in_embed.output, tmp.p, nf, hid, w.fut_emb, d, OUT_F32_ACC, 0, &ox));
     TSFM_CUDA(cudaStreamSynchronize(s), "Chronos-2 future embeddings");
     TSFM_TRY(check_device_error(r));
     return Status::ok();
@@ -193,7 +205,7 @@ static bool c2_fused_norm(const tsfm_config &c) {
     return on && c.d_model % 256 == 0;
 }
 
-static size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64_t horizon) {
+static size_t c2_workspace(const tsfm_config &c, bool corr, int64_t nb, int64_t t_in, int64_t horizon) {
     int64_t t, start, pad, n_ctx, n_out, seq;
     c2_geometry(c, t_in, horizon, t, start, pad, n_ctx, n_out, seq);
     const int64_t d = c.d_model, ff = c.d_ff, ps = c.patch_size, q = c.num_quantiles, rows = nb * seq;
@@ -212,6 +224,10 @@ static size_t c2_workspace(const tsfm_config &c, int64_t nb, int64_t t_in, int64
     if (c2_fused_norm(c)) {
         b += Arena::span(rows * 4);              // row factors
         b += Arena::span(rows * (d / 256) * 4);  // row sums of squares per column tile
+    }
+    if (corr) {  // FP8 companions of xn, ao and h
+        b += Arena::span(rows * 2 * d) * 2;
+        b += Arena::span(rows * 2 * ff);
     }
     return b;
 }
@@ -244,6 +260,14 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
     const int np = (int)(d / 256);
     float *nS = fused ? ws.take<float>(rows) : nullptr;       // row factors of the MLP norm
     float *nP = fused ? ws.take<float>(rows * np) : nullptr;  // row sums of squares per column tile
+    // Corrected products: FP8 companions of the GEMM inputs xn, ao and h.
+    uint8_t *xn8 = w.corr ? ws.take<uint8_t>(rows * 2 * d) : nullptr;
+    uint8_t *ao8 = w.corr ? ws.take<uint8_t>(rows * 2 * d) : nullptr;
+    uint8_t *h8 = w.corr ? ws.take<uint8_t>(rows * 2 * ff) : nullptr;
+    auto in8 = [](LinearCall &lc, uint8_t *x8, int64_t cols) {  // the product's input companion
+        lc.x8 = x8;
+        lc.ldx8 = 2 * cols;
+    };
     if (ws.used > ws.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Chronos-2: workspace too small");
 
     // 1. instance norm + patch features (TF32-rounded FP32) + key validity.
@@ -273,12 +297,16 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
     // 2. patch embedding ResBlock straight into the sequence rows: x = res(f) + out(relu(hid(f))).
     {
         const int64_t m = b * n_ctx;
-        TSFM_TRY(op_linear(r, s, w.in_embed.hidden, feats, m, 3 * ps, h, ff, A16, 1));
+        LinearCall hx;
+        hx.y8 = h8;
+        hx.ldy8 = 2 * ff;
+        TSFM_TRY(op_linear(r, s, w.in_embed.hidden, feats, m, 3 * ps, h, ff, A16, 1, &hx));
         LinearCall remap;
         remap.rm_g = n_ctx;
         remap.rm_G = seq;
         remap.rm_off = 0;
         TSFM_TRY(op_linear(r, s, w.in_embed.residual, feats, m, 3 * ps, x, d, OUT_F32, 0, &remap));
+        in8(remap, h8, ff);
         TSFM_TRY(op_linear(r, s, w.in_embed.output, h, m, ff, x, d, OUT_F32_ACC, 0, &remap));
         LaunchScope ls(r, s, K_OTHER, (double)b * (1 + n_out) * d * 8);
         TSFM_TRY(launch_broadcast_rows(x, b, seq, n_ctx, w.reg, 1, d, s));
@@ -300,8 +328,9 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
             qc.rope_cols = (int)(2 * d);
             qc.rope_p1 = 0;
             qc.rope_p2 = seq;
+            in8(qc, xn8, d);
             if (li == 0) {
-                TSFM_TRY(op_rmsnorm(r, s, x, L.time_norm, xn, A16, rows, d, eps));
+                TSFM_TRY(op_rmsnorm(r, s, x, L.time_norm, xn, A16, rows, d, eps, 0, 0, 0, nullptr, xn8));
             } else {
                 qc.norm_in = nP;
                 qc.norm_parts = np;
@@ -327,30 +356,41 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
                 ac.n = (int)seq;
                 ac.scale = 1.0f;
                 ac.mask_mode = 0;
+                ac.o8 = ao8;
+                ac.ld_o8 = 2 * d;
                 LaunchScope ls(r, s, K_ATTN, 4.0 * (double)b * nh * seq * seq * 64);
                 TSFM_TRY(launch_attention(ac, s));
             }
-            TSFM_TRY(op_linear(r, s, L.o, ao, rows, d, x, d, OUT_F32_ACC, 0));
-            TSFM_TRY(op_rmsnorm(r, s, x, L.group_norm, xn, A16, rows, d, eps));
-            TSFM_TRY(op_linear(r, s, L.gvo, xn, rows, d, x, d, OUT_F32_ACC, 0));
+            LinearCall oc, gc, ic, wc;
+            in8(oc, ao8, d);
+            in8(gc, xn8, d);
+            in8(ic, xn8, d);
+            in8(wc, h8, ff);
+            ic.y8 = h8;
+            ic.ldy8 = 2 * ff;
+            TSFM_TRY(op_linear(r, s, L.o, ao, rows, d, x, d, OUT_F32_ACC, 0, &oc));
+            TSFM_TRY(op_rmsnorm(r, s, x, L.group_norm, xn, A16, rows, d, eps, 0, 0, 0, nullptr, xn8));
+            TSFM_TRY(op_linear(r, s, L.gvo, xn, rows, d, x, d, OUT_F32_ACC, 0, &gc));
             const bool last = li + 1 == w.layers.size();
-            TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps, 0, 0, 0, last ? nullptr : nS));
-            TSFM_TRY(op_linear(r, s, L.wi, xn, rows, d, h, ff, A16, 1));
-            LinearCall wc;
+            TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps, 0, 0, 0, last ? nullptr : nS, xn8));
+            TSFM_TRY(op_linear(r, s, L.wi, xn, rows, d, h, ff, A16, 1, &ic));
             if (!last) {
                 wc.norm_out = nP;
                 wc.norm_x16 = xn;
                 wc.ld_x16 = d;
                 wc.norm_gamma = w.layers[li + 1].time_norm;
                 wc.norm_s_in = nS;
+                wc.norm_x8 = xn8;
+                wc.ld_nx8 = 2 * d;
             }
             TSFM_TRY(op_linear(r, s, L.wo, h, rows, ff, x, d, OUT_F32_ACC, 0, &wc));
         }
     }
     if (!fused)
     for (const C2Dev::Layer &L : w.layers) {
-        TSFM_TRY(op_rmsnorm(r, s, x, L.time_norm, xn, A16, rows, d, eps));
+        TSFM_TRY(op_rmsnorm(r, s, x, L.time_norm, xn, A16, rows, d, eps, 0, 0, 0, nullptr, xn8));
         LinearCall rope;
+        in8(rope, xn8, d);
         rope.rope_cos = w.rope_cos;
         rope.rope_sin = w.rope_sin;
         rope.rope_cols = (int)(2 * d);
@@ -374,15 +414,24 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
             ac.n = (int)seq;
             ac.scale = 1.0f;
             ac.mask_mode = 0;
+            ac.o8 = ao8;
+            ac.ld_o8 = 2 * d;
             LaunchScope ls(r, s, K_ATTN, 4.0 * (double)b * nh * seq * seq * 64);
             TSFM_TRY(launch_attention(ac, s));
         }
-        TSFM_TRY(op_linear(r, s, L.o, ao, rows, d, x, d, OUT_F32_ACC, 0));
-        TSFM_TRY(op_rmsnorm(r, s, x, L.group_norm, xn, A16, rows, d, eps));
-        TSFM_TRY(op_linear(r, s, L.gvo, xn, rows, d, x, d, OUT_F32_ACC, 0));
-        TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps));
-        TSFM_TRY(op_linear(r, s, L.wi, xn, rows, d, h, ff, A16, 1));
-        TSFM_TRY(op_linear(r, s, L.wo, h, rows, ff, x, d, OUT_F32_ACC, 0));
+        LinearCall oc, gc, ic, wc;
+        in8(oc, ao8, d);
+        in8(gc, xn8, d);
+        in8(ic, xn8, d);
+        in8(wc, h8, ff);
+        ic.y8 = h8;
+        ic.ldy8 = 2 * ff;
+        TSFM_TRY(op_linear(r, s, L.o, ao, rows, d, x, d, OUT_F32_ACC, 0, &oc));
+        TSFM_TRY(op_rmsnorm(r, s, x, L.group_norm, xn, A16, rows, d, eps, 0, 0, 0, nullptr, xn8));
+        TSFM_TRY(op_linear(r, s, L.gvo, xn, rows, d, x, d, OUT_F32_ACC, 0, &gc));
+        TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps, 0, 0, 0, nullptr, xn8));
+        TSFM_TRY(op_linear(r, s, L.wi, xn, rows, d, h, ff, A16, 1, &ic));
+        TSFM_TRY(op_linear(r, s, L.wo, h, rows, ff, x, d, OUT_F32_ACC, 0, &wc));
     }
     // 4. final norm on the future-patch rows only, then the quantile head.
     const int64_t m = b * n_out;
@@ -416,11 +465,11 @@ static Status c2_forward(Replica &r, const tsfm_config &c, const C2Dev &w, const
 // scratch the same way: chronos2/forecaster.zig:42-57).
 Status c2_forecast(Replica &r, const tsfm_config &c, const C2Dev &w, const float *d_in, int64_t b, int64_t t_in,
                    int64_t horizon, float *d_out, cudaStream_t s) {
-    const size_t per = c2_workspace(c, 1, t_in, horizon);
+    const size_t per = c2_workspace(c, w.corr, 1, t_in, horizon);
     int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(b, (int64_t)(workspace_budget(r) / std::max<size_t>(per, 1))));
     const int64_t nchunks = (b + chunk - 1) / chunk;
     chunk = (b + nchunks - 1) / nchunks;
-    TSFM_TRY(r.ws.reserve(c2_workspace(c, chunk, t_in, horizon)));
+    TSFM_TRY(r.ws.reserve(c2_workspace(c, w.corr, chunk, t_in, horizon)));
     const int64_t q = c.num_quantiles;
     for (int64_t s0 = 0; s0 < b; s0 += chunk) {
         const int64_t n = std::min(chunk, b - s0);

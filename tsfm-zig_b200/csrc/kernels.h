@@ -11,8 +11,23 @@
 
 namespace tsfm {
 
-// Element types of tensor-core operands and 16-bit activations.
-enum ElemType { E_BF16 = 0, E_F16 = 1, E_F32 = 2 };
+// Element types of tensor-core operands and 16-bit activations. E_F16C is a weight-upload request
+// only: an FP16 weight with its FP8 correction companion (DLin::w8), for corrected products.
+// E_U8 names byte tensors (the FP8 companions) in tensor maps.
+// E_F32X is exact FP32 (no TF32 rounding), a conversion target of the weight kernels.
+enum ElemType { E_BF16 = 0, E_F16 = 1, E_F32 = 2, E_F16C = 3, E_U8 = 4, E_F32X = 5 };
+
+// Corrected products (FP16 operands plus FP8 correction terms; TSFM_COMPUTE_F16C).
+// A 16-bit activation x [M, K] of a corrected product has an FP8 companion x8 [M, 2K] (bytes):
+//   x8[r, c]     = e4m3(x_hi[r, c] * kX8HiScale),      x_hi = f16(x)
+//   x8[r, K + c] = e4m3((x - x_hi)[r, c] * kX8LoScale)
+// and a weight W [N, K] is stored as W16 = f16(W) * 2^s with the companion
+//   w8[n, c]     = e4m3(w_lo[n, c] * 2^sb),            w_lo = W - f16(W)
+//   w8[n, K + c] = e4m3(f16(W)[n, c] * 2^(sb - 12)),   s = sb - 5,
+// so x8 . w8 over 2K columns = 2^s (x_hi w_lo + x_lo f16(W)) and the accumulator holds
+// 2^s (x_hi f16(W) + x_hi w_lo + x_lo f16(W)) ~= 2^s x W; the epilogue multiplies by 2^-s.
+constexpr float kX8HiScale = 1.0f / 32.0f;
+constexpr float kX8LoScale = 128.0f;
 // Output modes of the kernels that write activations.
 enum OutMode { OUT_BF16 = 0, OUT_F32 = 1, OUT_F32_ACC = 2, OUT_TF32 = 3, OUT_F16 = 4 };
 inline int out_mode_for(int elem) { return elem == E_F16 ? OUT_F16 : elem == E_BF16 ? OUT_BF16 : OUT_TF32; }
@@ -91,6 +106,21 @@ struct LinearCall {
     void *norm_x16 = nullptr;
     int64_t ld_x16 = 0;
     const float *norm_gamma = nullptr;
+    // Corrected product (x8 set; dtype E_F16, K % 8 == 0): the FP8 companions of x and w (layouts
+    // above, row strides in bytes) add the correction terms, and the result is multiplied by
+    // acc_scale = 2^-s before the epilogue. Runs the FP8 stages first, then the FP16 ones.
+    const void *x8 = nullptr;
+    int64_t ldx8 = 0;
+    const void *w8 = nullptr;
+    int64_t ldw8 = 0;
+    float acc_scale = 1.0f;
+    // FP8 companion of a 16-bit output (y8 set; the output's column count a multiple of 64):
+    // y8 row r = [e4m3(f16(y) * kX8HiScale) | e4m3((y - f16(y)) * kX8LoScale)], each part as
+    // wide as y, row stride ldy8 bytes. With norm_out, norm_x8 is the companion of norm_x16.
+    void *y8 = nullptr;
+    int64_t ldy8 = 0;
+    void *norm_x8 = nullptr;
+    int64_t ld_nx8 = 0;
 };
 Status launch_linear(const LinearCall &c, cudaStream_t stream);
 
@@ -116,6 +146,10 @@ struct AttentionCall {
     const uint8_t *group_bidir = nullptr;  // per group: 1 = bidirectional encoder rows (mode 1 only)
     int *err = nullptr;                    // device error word for the bounded waits of the tcgen05 path
     int force_path = 0;                    // 0: automatic, 1: tcgen05 path only (error if unsupported), 2: mma.sync path
+    // FP8 companion of the FP16 output (kernels.h layout, width heads * 64; tcgen05 path only: a
+    // call the tcgen05 path does not take fails rather than leave it unwritten).
+    void *o8 = nullptr;
+    int64_t ld_o8 = 0;
 };
 Status launch_attention(const AttentionCall &c, cudaStream_t stream);
 // The tcgen05 path (attention_tc.cu): true when it handles this call's mask and shapes.
@@ -131,9 +165,20 @@ Status make_tmap_2d(void *map, const void *base, int dtype, int64_t inner, int64
 // from src_dt (E_F32 / E_F16 / E_BF16) to dst_dt (E_F16, E_BF16, or E_F32 = TF32-rounded).
 Status launch_convert_rows(const void *src, int src_dt, const int32_t *map, void *dst, int dst_dt, int64_t rows,
                            int64_t cols, cudaStream_t s);
-// dst = a (m x k) b (k x n) in float64, rounded to float, then to dst_dt (E_F16, E_BF16, E_F32).
+// dst = a (m x k) b (k x n) in float64, rounded to float, then to dst_dt (E_F16, E_BF16, or E_F32 /
+// E_F32X: the float itself).
 Status launch_fold_f64(const void *a, int a_dt, const void *b, int b_dt, void *dst, int dst_dt, int64_t m, int64_t k,
                        int64_t n, cudaStream_t s);
+
+// Corrected-product weight (kernels.h layouts above) from an exact FP32 weight w [rows, cols] on
+// the device: w16 = f16(w) * 2^s, w8 [rows, 2 cols] its FP8 companion; returns s (the epilogue
+// multiplies by 2^-s). Reads back the weight's range (a stream synchronisation).
+Status build_corrected_weight(const float *w, int64_t rows, int64_t cols, void *w16, void *w8, int *s_out,
+                              cudaStream_t s);
+// An FP16 activation and its FP8 companion from FP32 values: x16 = f16(x), x8 row r =
+// [e4m3(x16 * kX8HiScale) | e4m3((x - x16) * kX8LoScale)] (row strides in elements / bytes).
+Status launch_split_x8(const float *x, int64_t rows, int64_t cols, int64_t ldx, void *x16, int64_t ld16, void *x8,
+                       int64_t ld8, cudaStream_t s);
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel): the attribute
 // stays set in the context, and setting it on every launch costs host time.
@@ -157,6 +202,10 @@ struct RmsNormCall {
     int64_t g = 0, G = 0, off = 0;
     const int64_t *rows_idx = nullptr;  // when set: in_row(r) = rows_idx[r]
     float *inv_out = nullptr;           // when set: the row's factor 1 / sqrt(mean(x^2) + eps)
+    // FP8 companion of an FP16 output (kernels.h layout; dim % 4 == 0): row r at out8 + r * ld8
+    // bytes, the low part `dim` bytes after the high part.
+    void *out8 = nullptr;
+    int64_t ld8 = 0;
 };
 Status launch_rmsnorm(const RmsNormCall &c, cudaStream_t stream);
 

@@ -19,6 +19,7 @@
 // so results do not depend on the grid size or the number of GPUs.
 #include "kernels.h"
 #include "ptx.cuh"
+#include "x8.cuh"
 
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -80,6 +81,14 @@ struct Epi {
     void *nx16;
     int64_t ldx16;
     const float *ngamma;
+    // Corrected products: the accumulator is multiplied by acc_scale before the epilogue; y8 /
+    // nx8 (bytes, row strides ldy8 / ldnx8) receive the FP8 companions of the 16-bit outputs, the
+    // low-part block `y8_half` / `nx8_half` bytes after the high part.
+    float acc_scale;
+    uint8_t *y8;
+    int64_t ldy8, y8_half;
+    uint8_t *nx8;
+    int64_t ldnx8, nx8_half;
 };
 
 // Activation over n values: 1 relu, 2 silu (nn.siluInPlace, core/nn.zig:399-407). The branch is
@@ -196,16 +205,24 @@ __device__ __forceinline__ void bias_act(const Epi &e, int64_t col0, int nvalid,
     if (e.out_mode != OUT_F32_ACC) apply_act<32>(e.act, v);
 }
 
-template <typename T, int BN, bool PAIR, bool NORM>
+// CORR: corrected product; tmA8 / tmB8 map the FP8 companions of x and W ([rows, 2K] bytes).
+// The K loop runs ceil(2K / 128) FP8 stages (kind::f8f6f4, the small correction terms first),
+// then ceil(K / BK) FP16 stages (kind::f16), all into one FP32 accumulator.
+template <typename T, int BN, bool PAIR, bool NORM, bool CORR>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmY, Epi e) {
+                     const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmA8,
+                     const __grid_constant__ CUtensorMap tmB8, Epi e) {
     using C = TileCfg<BN, PAIR, NORM>;
     constexpr int STAGES = C::STAGES;
     constexpr int BK = 128 / (int)sizeof(T);
+    // FP8 companions of FP16 outputs are written by the FP16 and TF32 instances (BF16 never
+    // feeds a corrected product).
+    constexpr bool CORR_OUT = !std::is_same<T, __nv_bfloat16>::value;
     // operand format: BF16 = 1, F16 = 0 (kind::f16); TF32 = 2 (kind::tf32)
     constexpr uint32_t FMT = std::is_same<T, float>::value ? 2u : std::is_same<T, __half>::value ? 0u : 1u;
     static_assert(!PAIR || FMT != 2u, "the 2-SM path takes 16-bit operands");
+    static_assert(!CORR || FMT == 0u, "corrected products take FP16 operands");
     constexpr uint32_t IDESC = idesc_f32acc(FMT, PAIR ? 2 * kBM : kBM, BN);
     // CTA pairs: rank 0 issues the MMAs for both; the tile's rows split by rank.
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
@@ -230,7 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t m_tiles = (e.M + kRows - 1) / kRows, n_tiles = (e.N + BN - 1) / BN;
     const int64_t tiles = m_tiles * n_tiles;
-    const int num_k = (int)((e.K + BK - 1) / BK);
+    const int num_k8 = CORR ? (int)((2 * e.K + 127) / 128) : 0;  // FP8 correction stages
+    const int num_k = num_k8 + (int)((e.K + BK - 1) / BK);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -246,6 +264,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if constexpr (CORR) {
+            tma_prefetch_desc(&tmA8);
+            tma_prefetch_desc(&tmB8);
+        }
     }
     if (warp == 1) {
         if constexpr (PAIR) {
@@ -279,16 +301,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
+                    // FP8 stages load 128 bytes of the companions' rows; the boxes have the
+                    // same byte size as the 16-bit ones.
+                    const bool f8 = CORR && kb < num_k8;
+                    const CUtensorMap *ma = f8 ? &tmA8 : &tmA;
+                    const CUtensorMap *mb = f8 ? &tmB8 : &tmB;
+                    const int32_t kc = f8 ? kb * 128 : (kb - num_k8) * BK;
                     if constexpr (PAIR) {
                         // The pair's first CTA expects the bytes of both CTAs' boxes on its barrier.
                         if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES));
                         const uint32_t fb = mapa_shared(&full[s], 0);
-                        tma_load_2d_pair(sA + s * C::A_BYTES, &tmA, fb, kb * BK, m0);
-                        tma_load_2d_pair(sB + s * C::B_BYTES, &tmB, fb, kb * BK, n0);
+                        tma_load_2d_pair(sA + s * C::A_BYTES, ma, fb, kc, m0);
+                        tma_load_2d_pair(sB + s * C::B_BYTES, mb, fb, kc, n0);
                     } else {
                         mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
-                        tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * BK, m0);
-                        tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * BK, n0);
+                        tma_load_2d(sA + s * C::A_BYTES, ma, &full[s], kc, m0);
+                        tma_load_2d(sB + s * C::B_BYTES, mb, &full[s], kc, n0);
                     }
                     issued |= 1u << s;
                     issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
@@ -343,15 +371,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint64_t ad = sdesc_k128(sA + s * C::A_BYTES);
                     const uint64_t bd = sdesc_k128(sB + s * C::B_BYTES);
+                    const bool f8 = CORR && kb < num_k8;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         // advance 32 bytes along K inside the 128-byte swizzle atom
-                        if constexpr (PAIR)
+                        if (f8) {
+                            if constexpr (PAIR)
+                                mma_f8kind_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
+                            else
+                                mma_f8kind(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
+                        } else if constexpr (PAIR) {
                             mma_f16kind_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
-                        else if constexpr (sizeof(T) == 2)
+                        } else if constexpr (sizeof(T) == 2) {
                             mma_f16kind(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
-                        else
+                        } else {
                             mma_tf32(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
+                        }
                     }
                     if constexpr (PAIR) {
                         mma_commit_pair(mapa_shared(&empty[s], 0));
@@ -489,13 +524,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             // Fused RMSNorm factors of this thread's row (loads issued before the accumulator wait).
-            float rsc = 1.0f, xs = 1.0f;
+            // rsc: the row's factor applied to the accumulator (corrected products: times 2^-s).
+            float rsc = e.acc_scale, xs = 1.0f;
             if (e.nin != nullptr) {
                 if (row_ok) {
                     float sum = 0.0f;
                     for (int p = 0; p < e.nparts; ++p) sum += e.nin[(int64_t)p * e.M + row];
                     const float rs = 1.0f / sqrtf(sum / e.ndim + e.neps);
-                    rsc = e.ns_in ? rs / e.ns_in[row] : rs;
+                    rsc = (e.ns_in ? rs / e.ns_in[row] : rs) * e.acc_scale;
                     xs = rs;
                     if (e.ns_out && ncol0 == 0) e.ns_out[row] = rs;
                 }
@@ -573,7 +609,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int q = 0; q < 8; ++q) put16(b, q, make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
                                                                         __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3])));
                     issue_box(b, col0, wrow0);
-                    // 16-bit copy for the next GEMM: y * xs * gamma.
+                    // 16-bit copy for the next GEMM: y * xs * gamma (and its FP8 companion).
+                    float nv[32];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float4 g0 = __ldg(reinterpret_cast<const float4 *>(e.ngamma + col0 + 8 * q));
@@ -582,6 +619,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const float a0 = src[0] * xs * g0.x, a1 = src[1] * xs * g0.y, a2 = src[2] * xs * g0.z,
                                     a3 = src[3] * xs * g0.w, a4 = src[4] * xs * g1.x, a5 = src[5] * xs * g1.y,
                                     a6 = src[6] * xs * g1.z, a7 = src[7] * xs * g1.w;
+                        nv[8 * q] = a0;
+                        nv[8 * q + 1] = a1;
+                        nv[8 * q + 2] = a2;
+                        nv[8 * q + 3] = a3;
+                        nv[8 * q + 4] = a4;
+                        nv[8 * q + 5] = a5;
+                        nv[8 * q + 6] = a6;
+                        nv[8 * q + 7] = a7;
                         uint4 pk;
                         pk.x = pack2<T>(a0, a1);
                         pk.y = pack2<T>(a2, a3);
@@ -589,6 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         pk.w = pack2<T>(a6, a7);
                         *reinterpret_cast<uint4 *>(xst + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = pk;
                     }
+                    if (CORR_OUT && e.nx8 != nullptr && row_ok) store_x8_32(e.nx8 + row * e.ldnx8, e.nx8_half, col0, nv);
                     __syncwarp();
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -616,8 +662,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tmem_ld32(tbase + c + h, g);
                         tmem_ld32(tbase + 128 + c + h, u);
                         tmem_wait_ld();
+                        if (rsc != 1.0f) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                g[j] *= rsc;
+                                u[j] *= rsc;
+                            }
+                        }
 #pragma unroll
                         for (int j = 0; j < 32; ++j) g[j] = g[j] * __fdividef(u[j], 1.0f + __expf(-u[j]));
+                        if (CORR_OUT && e.y8 != nullptr && row_ok)
+                            store_x8_32(e.y8 + orow * e.ldy8, e.y8_half, ncol0 / 2 + c + h, g);
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             const float *src = g + 8 * q;
@@ -642,7 +697,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld32(tbase + c, lo);
                     tmem_ld32(tbase + c + 32, hi);
                     tmem_wait_ld();
-                    if (e.nin != nullptr) {
+                    if (rsc != 1.0f) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             lo[j] *= rsc;
@@ -663,6 +718,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int nv1 = rem1 <= 0 ? 0 : (rem1 < 32 ? (int)rem1 : 32);
                     bias_act(e, col0, nv0, lo);
                     if (nv1 > 0) bias_act(e, col0 + 32, nv1, hi);
+                    if (CORR_OUT && e.y8 != nullptr && row_ok) {  // 16-bit output, N % 64 == 0
+                        uint8_t *r8 = e.y8 + orow * e.ldy8;
+                        store_x8_32(r8, e.y8_half, col0, lo);
+                        store_x8_32(r8, e.y8_half, col0 + 32, hi);
+                    }
                     if (e.tma_mode != 0) {
                         if (f32_out) {
                             tma_f32(col0, wrow0, lo);
@@ -683,13 +743,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float v[32];
                     tmem_ld32(tbase + c, v);
                     tmem_wait_ld();
-                    if (e.nin != nullptr) {
+                    if (rsc != 1.0f) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) v[j] *= rsc;
                     }
                     const int64_t rem = e.N - col0;
                     const int nv = rem < 32 ? (int)rem : 32;
                     bias_act(e, col0, nv, v);
+                    if (CORR_OUT && e.y8 != nullptr && row_ok && !f32_out)
+                        store_x8_32(e.y8 + orow * e.ldy8, e.y8_half, col0, v);
                     if (e.tma_mode != 0)
                         tma_f32(col0, wrow0, v);
                     else if (row_ok)
@@ -747,9 +809,10 @@ Status make_tmap(CUtensorMap *map, const void *base, int dtype, int64_t inner, i
                  uint32_t box_inner, uint32_t box_outer) {
     if (!load_encode()) return Status::fail(TSFM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const bool f32 = dtype == E_F32;
-    const int esz = f32 ? 4 : 2;
+    const int esz = f32 ? 4 : dtype == E_U8 ? 1 : 2;
     const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                       : dtype == E_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+                                   : dtype == E_U8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : dtype == E_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * esz) & 15))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: operand base and row stride must be 16-byte aligned");
     cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
@@ -797,7 +860,7 @@ Status ensure_smem_attr(const void *func, int bytes) {
 
 namespace {
 
-template <typename T, int BN, bool PAIR, bool NORM = false>
+template <typename T, int BN, bool PAIR, bool NORM = false, bool CORR = false>
 Status launch_t(const LinearCall &c, cudaStream_t stream) {
     using C = TileCfg<BN, PAIR, NORM>;
     constexpr int BK = 128 / (int)sizeof(T);
@@ -806,7 +869,12 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     if (!s) return s;
     s = make_tmap(&tb, c.w, c.dtype, c.K, c.N, c.ldw, BK, C::B_ROWS);
     if (!s) return s;
-    TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&linear_tc_kernel<T, BN, PAIR, NORM>), C::SMEM));
+    CUtensorMap ta8 = ta, tb8 = tb;  // unused unless CORR
+    if constexpr (CORR) {
+        TSFM_TRY(make_tmap(&ta8, c.x8, E_U8, 2 * c.K, c.M, c.ldx8, 128, kBM));
+        TSFM_TRY(make_tmap(&tb8, c.w8, E_U8, 2 * c.K, c.N, c.ldw8, 128, C::B_ROWS));
+    }
+    TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&linear_tc_kernel<T, BN, PAIR, NORM, CORR>), C::SMEM));
     cudaError_t ce;
     Epi e;
     e.M = c.M;
@@ -836,6 +904,13 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     e.nx16 = c.norm_x16;
     e.ldx16 = c.ld_x16;
     e.ngamma = c.norm_gamma;
+    e.acc_scale = CORR ? c.acc_scale : 1.0f;
+    e.y8 = static_cast<uint8_t *>(c.y8);
+    e.ldy8 = c.ldy8;
+    e.y8_half = c.act == ACT_GLU ? c.N / 2 : c.N;
+    e.nx8 = static_cast<uint8_t *>(c.norm_x8);
+    e.ldnx8 = c.ld_nx8;
+    e.nx8_half = c.N;
     // TMA epilogue unless rows are remapped or an activation follows the accumulation; the
     // output base and row stride must suit a tensor map (16-byte alignment).
     const bool f32_out = c.out_mode == OUT_F32 || c.out_mode == OUT_F32_ACC || c.out_mode == OUT_TF32;
@@ -870,12 +945,12 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        ce = cudaLaunchKernelEx(&cfg, linear_tc_kernel<T, BN, true, NORM>, ta, tb, ty, e);
+        ce = cudaLaunchKernelEx(&cfg, linear_tc_kernel<T, BN, true, NORM, CORR>, ta, tb, ty, ta8, tb8, e);
         if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch (CTA pairs)");
     } else {
         const int64_t tiles = ((c.M + kBM - 1) / kBM) * ((c.N + BN - 1) / BN);
         const int grid = (int)std::min<int64_t>(tiles, sm_count());
-        linear_tc_kernel<T, BN, false, NORM><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, e);
+        linear_tc_kernel<T, BN, false, NORM, CORR><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, ta8, tb8, e);
     }
     ce = cudaGetLastError();
     if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch");
@@ -932,6 +1007,21 @@ Status launch_linear(const LinearCall &c, cudaStream_t stream) {
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: gated pairs need N % 256 == 0, 16-bit operands and output");
     if (c.norm_in && (c.norm_parts <= 0 || c.norm_dim <= 0 || c.act == ACT_GLU || c.norm_s_in == c.norm_s_out))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad fused-norm reader arguments");
+    const auto a16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool corr = c.x8 != nullptr;
+    if (corr && (c.dtype != E_F16 || !c.w8 || c.K % 8 || c.ldx8 % 16 || c.ldw8 % 16 || c.ldx8 < 2 * c.K ||
+                 c.ldw8 < 2 * c.K || !a16(c.x8) || !a16(c.w8) || !(c.acc_scale > 0.0f)))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT,
+                            "linear: corrected products need FP16 operands, K % 8 == 0 and 16-byte-aligned FP8 companions");
+    if (c.y8) {
+        const int64_t ycols = c.act == ACT_GLU ? c.N / 2 : c.N;
+        if (c.out_mode != OUT_F16 || ycols % 64 || c.ldy8 % 16 || c.ldy8 < 2 * ycols || !a16(c.y8) ||
+            c.dtype == E_BF16)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT,
+                                "linear: an FP8 companion output needs an FP16 output of a multiple of 64 columns");
+    }
+    if (c.norm_x8 && (!c.norm_out || c.dtype != E_F16 || c.ld_nx8 % 16 || c.ld_nx8 < 2 * c.N || !a16(c.norm_x8)))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad FP8 companion of the fused norm");
     if (c.norm_out) {
         const bool ok = (c.dtype == E_F16 || c.dtype == E_BF16) && c.out_mode == OUT_F32_ACC && c.N % 256 == 0 &&
                         c.act == 0 && c.rm_g <= 0 && !c.rope_cos && c.norm_x16 && c.norm_gamma && c.ld_x16 >= c.N &&
@@ -940,6 +1030,9 @@ Status launch_linear(const LinearCall &c, cudaStream_t stream) {
                         (c.norm_in || c.norm_s_in);
         if (!ok) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad fused-norm residual arguments");
         const bool pair = c.M >= 4096 && gemm_pairs_enabled();
+        if (corr)
+            return pair ? launch_t<__half, 256, true, true, true>(c, stream)
+                        : launch_t<__half, 256, false, true, true>(c, stream);
         if (c.dtype == E_F16)
             return pair ? launch_t<__half, 256, true, true>(c, stream) : launch_t<__half, 256, false, true>(c, stream);
         return pair ? launch_t<__nv_bfloat16, 256, true, true>(c, stream)
@@ -949,6 +1042,10 @@ Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     // Large 16-bit products run on CTA pairs (2-SM MMA, 256 x 256 tiles): each SM then streams half
     // of W's tile instead of all of it.
     const bool pair = !small_n && c.M >= 4096 && gemm_pairs_enabled();
+    if (corr)
+        return small_n ? launch_t<__half, 128, false, false, true>(c, stream)
+                       : pair ? launch_t<__half, 256, true, false, true>(c, stream)
+                              : launch_t<__half, 256, false, false, true>(c, stream);
     switch (c.dtype) {
         case E_F32: return small_n ? launch_t<float, 128, false>(c, stream) : launch_t<float, 256, false>(c, stream);
         case E_F16:

@@ -24,6 +24,9 @@ struct C2Dev {
     float *fut_emb = nullptr;                        // [max_output_patches, d]: shared future-patch embeddings
     int64_t max_seq = 0;
     int act = E_F16;  // element type of GEMM operands / 16-bit activations
+    // Corrected products (TSFM_COMPUTE_F16C): every 16-bit weight carries its FP8 companion and
+    // every 16-bit GEMM input is written with one.
+    bool corr = false;
 };
 
 // Chronos-Bolt weights on one device (chronos_bolt/model.zig:101-172).

@@ -40,14 +40,25 @@ Status op_linear(Replica &r, cudaStream_t s, const DLin &L, const void *x, int64
     c.bias = L.b;
     c.act = act;
     c.err = static_cast<int *>(r.err.p);
+    // A corrected weight needs its activation's FP8 companion; a plain weight ignores one.
+    if (L.w8) {
+        if (!c.x8) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: a corrected weight needs the input's FP8 companion");
+        c.w8 = L.w8;
+        c.ldw8 = 2 * L.in;
+        c.acc_scale = L.acc_scale;
+    } else {
+        c.x8 = nullptr;
+    }
     LaunchScope ls(r, s, K_GEMM, 2.0 * (double)M * (double)L.out * (double)L.in);
     return launch_linear(c, s);
 }
 
 Status op_rmsnorm(Replica &r, cudaStream_t s, const float *x, const float *scale, void *out, int out_mode, int64_t rows,
-               int64_t dim, float eps, int64_t g, int64_t G, int64_t off, float *inv_out) {
+               int64_t dim, float eps, int64_t g, int64_t G, int64_t off, float *inv_out, void *out8) {
     RmsNormCall c;
     c.inv_out = inv_out;
+    c.out8 = out8;
+    c.ld8 = 2 * dim;
     c.x = x;
     c.scale = scale;
     c.out = out;
@@ -58,7 +69,8 @@ Status op_rmsnorm(Replica &r, cudaStream_t s, const float *x, const float *scale
     c.g = g;
     c.G = G;
     c.off = off;
-    LaunchScope ls(r, s, K_NORM, (double)rows * dim * (4.0 + (out_mode == 0 ? 2.0 : 4.0)));
+    LaunchScope ls(r, s, K_NORM, (double)rows * dim * (4.0 + (out_mode == OUT_F16 || out_mode == OUT_BF16 ? 2.0 : 4.0) +
+                                                       (out8 ? 2.0 : 0.0)));
     return launch_rmsnorm(c, s);
 }
 

@@ -64,6 +64,16 @@ __global__ void rmsnorm_kernel(RmsNormCall c) {
                 pk.x = *reinterpret_cast<uint32_t *>(&a);
                 pk.y = *reinterpret_cast<uint32_t *>(&b);
                 *reinterpret_cast<uint2 *>(reinterpret_cast<__half *>(c.out) + ob + i) = pk;
+                if (c.out8) {
+                    const float2 fa = __half22float2(a), fb = __half22float2(b);
+                    uint8_t *row8 = static_cast<uint8_t *>(c.out8) + r * c.ld8;
+                    *reinterpret_cast<uint32_t *>(row8 + i) =
+                        e4m3x2(fa.x * kX8HiScale, fa.y * kX8HiScale) |
+                        (e4m3x2(fb.x * kX8HiScale, fb.y * kX8HiScale) << 16);
+                    *reinterpret_cast<uint32_t *>(row8 + c.dim + i) =
+                        e4m3x2((o0 - fa.x) * kX8LoScale, (o1 - fa.y) * kX8LoScale) |
+                        (e4m3x2((o2 - fb.x) * kX8LoScale, (o3 - fb.y) * kX8LoScale) << 16);
+                }
             } else {
                 float4 w = c.out_mode == OUT_TF32 ? make_float4(to_tf32(o0), to_tf32(o1), to_tf32(o2), to_tf32(o3))
                                            : make_float4(o0, o1, o2, o3);
@@ -230,6 +240,9 @@ Status launch_rmsnorm(const RmsNormCall &c, cudaStream_t stream) {
     if ((c.dim % 4) == 0 && ((reinterpret_cast<uintptr_t>(c.x) | reinterpret_cast<uintptr_t>(c.scale) |
                               reinterpret_cast<uintptr_t>(c.out)) & 15))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "rmsnorm: buffers must be 16-byte aligned");
+    if (c.out8 && (c.out_mode != OUT_F16 || c.dim % 4 || c.ld8 % 4 || c.ld8 < 2 * c.dim ||
+                   (reinterpret_cast<uintptr_t>(c.out8) & 3)))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "rmsnorm: an FP8 companion needs an FP16 output, dim % 4 == 0");
     const int64_t blocks = (c.rows + 7) / 8;
     rmsnorm_kernel<<<(unsigned)blocks, 256, 0, stream>>>(c);
     TSFM_CUDA(cudaGetLastError(), "rmsnorm: launch");

@@ -311,6 +311,35 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// FP8 operands (kind::f8f6f4; E4M3 for A and B is format 0 in the instruction descriptor, so
+// idesc_f32acc(0, m, n) serves both this kind and FP16): K = 32 per instruction, i.e. the same
+// 32-byte step along a 128-byte-swizzled K-major row as a 16-bit K = 16 step.
+__device__ __forceinline__ void mma_f8kind(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_f8kind_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Two FP32 values to two E4M3 bytes (round to nearest even, saturating at +-448); `first` in the
+// low byte.
+__device__ __forceinline__ uint32_t e4m3x2(float first, float second) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(second), "f"(first));
+    return r;
+}
+
 // Arrives on `bar` once all previously issued tcgen05 operations of this thread complete.
 // D (TMEM of both CTAs, 128 rows each) += A (128 rows from each CTA's shared memory) * B (N / 2
 // rows from each CTA's shared memory); issued by one thread of the pair's first CTA.

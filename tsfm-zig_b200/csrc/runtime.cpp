@@ -3,6 +3,7 @@
 #include <cstdlib>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstring>
 
@@ -299,8 +300,14 @@ Status upload_lin_raw(Replica &r, const std::vector<const tsfm_tensor *> &parts,
         dmap = static_cast<const int32_t *>(r.stage.p);
     }
     DevBuf b;
-    TSFM_TRY(b.alloc((size_t)(out * in) * (dtype == E_F32 ? 4 : 2)));
-    TSFM_TRY(launch_convert_rows(src, elem_of(parts[0]), dmap, b.p, dtype, out, in, r.stream));
+    const bool corr = dtype == E_F16C;
+    TSFM_TRY(b.alloc((size_t)(out * in) * (dtype == E_F32 || corr ? 4 : 2)));
+    TSFM_TRY(launch_convert_rows(src, elem_of(parts[0]), dmap, b.p, corr ? E_F32X : dtype, out, in, r.stream));
+    if (corr) {
+        TSFM_TRY(upload_corrected(r, static_cast<const float *>(b.p), out, in, dst));
+        TSFM_CUDA(cudaStreamSynchronize(r.stream), "weight upload");
+        return Status::ok();
+    }
     TSFM_CUDA(cudaStreamSynchronize(r.stream), "weight upload");
     dst.out = out;
     dst.in = in;
@@ -321,8 +328,14 @@ Status upload_fold_raw(Replica &r, const tsfm_tensor *a, const tsfm_tensor *b, i
     TSFM_CUDA(cudaMemcpyAsync(pa, a->data, (size_t)a->numel * esz_a, cudaMemcpyHostToDevice, r.stream), "stage weight");
     TSFM_CUDA(cudaMemcpyAsync(pb, b->data, (size_t)b->numel * esz_b, cudaMemcpyHostToDevice, r.stream), "stage weight");
     DevBuf w;
-    TSFM_TRY(w.alloc((size_t)(m * n) * (dtype == E_F32 ? 4 : 2)));
-    TSFM_TRY(launch_fold_f64(pa, elem_of(a), pb, elem_of(b), w.p, dtype, m, k, n, r.stream));
+    const bool corr = dtype == E_F16C;
+    TSFM_TRY(w.alloc((size_t)(m * n) * (dtype == E_F32 || corr ? 4 : 2)));
+    TSFM_TRY(launch_fold_f64(pa, elem_of(a), pb, elem_of(b), w.p, corr ? E_F32X : dtype, m, k, n, r.stream));
+    if (corr) {
+        TSFM_TRY(upload_corrected(r, static_cast<const float *>(w.p), m, n, dst));
+        TSFM_CUDA(cudaStreamSynchronize(r.stream), "weight fold");
+        return Status::ok();
+    }
     TSFM_CUDA(cudaStreamSynchronize(r.stream), "weight fold");
     dst.out = m;
     dst.in = n;
@@ -361,11 +374,36 @@ Status upload_f32(Replica &r, const std::vector<float> &h, float **out) {
     return Status::ok();
 }
 
+Status upload_corrected(Replica &r, const float *w32, int64_t out, int64_t in, DLin &dst) {
+    if (in % 8) return Status::fail(TSFM_ERR_UNSUPPORTED, "corrected weights need in % 8 == 0");
+    DevBuf w16, w8;
+    TSFM_TRY(w16.alloc((size_t)(out * in) * 2));
+    TSFM_TRY(w8.alloc((size_t)(out * in) * 2));
+    int sh = 0;
+    TSFM_TRY(build_corrected_weight(w32, out, in, w16.p, w8.p, &sh, r.stream));
+    dst.out = out;
+    dst.in = in;
+    dst.dtype = E_F16;
+    dst.w = w16.p;
+    dst.w8 = w8.p;
+    dst.acc_scale = std::ldexp(1.0f, -sh);
+    r.weights.push_back(std::move(w16));
+    r.weights.push_back(std::move(w8));
+    return Status::ok();
+}
+
 Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, int dtype, DLin &dst) {
     DevBuf b;
     dst.out = out;
     dst.in = in;
     dst.dtype = dtype;
+    if (dtype == E_F16C) {
+        TSFM_TRY(b.alloc(w.size() * 4));
+        TSFM_CUDA(cudaMemcpyAsync(b.p, w.data(), w.size() * 4, cudaMemcpyHostToDevice, r.stream), "upload weight");
+        TSFM_TRY(upload_corrected(r, static_cast<const float *>(b.p), out, in, dst));
+        TSFM_CUDA(cudaStreamSynchronize(r.stream), "upload weight");
+        return Status::ok();
+    }
     if (dtype == E_F16) {
         std::vector<__half> t(w.size());
         for (size_t i = 0; i < w.size(); ++i) t[i] = __float2half_rn(w[i]);

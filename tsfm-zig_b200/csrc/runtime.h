@@ -60,6 +60,10 @@ struct DLin {
     int dtype = E_BF16;  // E_BF16, E_F16, or E_F32 (stored TF32-rounded, read as TF32)
     int64_t out = 0, in = 0;
     float *b = nullptr;
+    // Corrected product (uploaded as E_F16C): w holds f16(W) * 2^s, w8 [out, 2 in] its FP8
+    // companion (kernels.h), acc_scale = 2^-s. Null for plain weights.
+    void *w8 = nullptr;
+    float acc_scale = 1.0f;
 };
 
 struct DResBlock {
@@ -218,8 +222,9 @@ Status upload_f32(Replica &r, const std::vector<float> &h, float **out);
 Status upload_lin(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, int dtype, DLin &dst);
 Status upload_bias(Replica &r, const std::vector<float> &b, DLin &dst);
 // A device weight [out, in] from checkpoint tensors stacked by rows (each `in` columns wide), copied
-// as stored and converted on the device to `dtype` (E_F16 / E_BF16; E_F32 = TF32-rounded). With
-// `map`, output row r is stacked row (*map)[r]; without, out must equal the stacked row count.
+// as stored and converted on the device to `dtype` (E_F16 / E_BF16; E_F32 = TF32-rounded; E_F16C =
+// the corrected-product form). With `map`, output row r is stacked row (*map)[r]; without, out
+// must equal the stacked row count.
 Status upload_lin_raw(Replica &r, const std::vector<const tsfm_tensor *> &parts, const std::vector<int32_t> *map,
                       int64_t out, int64_t in, int dtype, DLin &dst);
 // A device weight = a (m x k) b (k x n) formed in float64 on the device and rounded once (to
@@ -227,6 +232,9 @@ Status upload_lin_raw(Replica &r, const std::vector<const tsfm_tensor *> &parts,
 Status upload_fold_raw(Replica &r, const tsfm_tensor *a, const tsfm_tensor *b, int64_t m, int64_t k, int64_t n,
                        int dtype, DLin &dst);
 Status upload_lin3(Replica &r, const std::vector<float> &w, int64_t out, int64_t in, DLin3 &dst);
+// The corrected-product form (E_F16C) of an exact FP32 device weight [out, in]; `w32` stays the
+// caller's.
+Status upload_corrected(Replica &r, const float *w32, int64_t out, int64_t in, DLin &dst);
 
 // Checks the device error word after a stream sync.
 Status check_device_error(Replica &r);

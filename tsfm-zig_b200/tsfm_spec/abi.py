@@ -6,7 +6,7 @@ import ctypes
 
 FAMILY = {"chronos2": 1, "chronos_bolt": 2, "timestral": 3}
 DTYPE = {"F32": 0, "F16": 1, "BF16": 2}
-COMPUTE = {"bf16": 0, "tf32": 1, "f16": 2}
+COMPUTE = {"bf16": 0, "tf32": 1, "f16": 2, "f16c": 3}
 LAYER_KIND = {"time": 0, "variate": 1, "time_variate": 2, "variate_time": 3}
 
 
