@@ -60,6 +60,11 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--compute", default="f16c", choices=["f16c", "f16", "bf16"],
+                    help="operand mode of the headline (f16c: FP16 + FP8 correction products, the mode that "
+                         "meets the 1e-2 * sigma bound at this shape)")
+    ap.add_argument("--no-compare", action="store_true",
+                    help="skip the extra measurement of plain FP16 operands beside the headline")
     ap.add_argument("--series", type=int, default=SERIES_PER_GPU)
     ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
     ap.add_argument("--batch", type=int, default=None,
@@ -150,11 +155,12 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_model(device):
-    from tsfm_b200 import Model, synthetic as syn
+def build_model(devices, compute):
+    from tsfm_b200 import Model
+    from tsfm_spec import synthetic as syn
     cfg = syn.chronos2_config(context_length=CONTEXT, max_output_patches=64)
     w = syn.random_checkpoint(cfg, seed=20261201)
-    return cfg, w, Model(cfg, w, devices=(device,))
+    return cfg, w, Model(cfg, w, devices=tuple(devices), compute=compute)
 
 
 def traffic_from_profile():
@@ -173,11 +179,12 @@ def traffic_from_profile():
 def cpu_baseline(sample):
     """The oracle (CPU restatement of the reference path) on `sample` series of the workload."""
     from oracle import binding as ob
-    from tsfm_b200 import config as cm, synthetic as syn, tensor_table
+    from tsfm_spec import config as cm, synthetic as syn
+    from tsfm_spec.table import tensor_table
     cfg = syn.chronos2_config(context_length=CONTEXT, max_output_patches=64)
     w = syn.random_checkpoint(cfg, seed=20261201)
     m = ob.OracleModel(cm.parse(cfg), w, tensor_table)
-    x = syn.seeded_series(sample, CONTEXT, seed=1000)
+    x = syn.seeded_series(sample, CONTEXT, seed=series_seed(0, SERIES_PER_GPU))  # the GPU arm's first series
     t0 = time.perf_counter()
     m.forecast_chronos2(x, HORIZON)
     dt = time.perf_counter() - t0
@@ -187,14 +194,16 @@ def cpu_baseline(sample):
 def run_reference(a, rank):
     if rank != 0:
         return
+    # The oracle and the pure-Python formats only: nothing of the CUDA backend is loaded here.
     from oracle import binding as ob
-    from tsfm_b200 import config as cm, synthetic as syn, tensor_table
+    from tsfm_spec import config as cm, synthetic as syn
+    from tsfm_spec.table import tensor_table
     ob.set_threads(os.cpu_count() or 1)
     cfg = syn.chronos2_config(context_length=CONTEXT, max_output_patches=64)
     w = syn.random_checkpoint(cfg, seed=20261201)
     m = ob.OracleModel(cm.parse(cfg), w, tensor_table)
     n = max(1, a.cpu_sample)
-    x = syn.seeded_series(n, CONTEXT, seed=1000)
+    x = syn.seeded_series(n, CONTEXT, seed=series_seed(0, SERIES_PER_GPU))  # the GPU arm's first series
     for _ in range(max(0, min(a.warmup, 1))):
         m.forecast_chronos2(x[:1], HORIZON)
     times = []
@@ -584,6 +593,114 @@ def run_attention(a):
         del qkv, o
 
 
+def measure(model, a, x, world, barrier, clk=None):
+    """One operand mode of the headline workload: device-resident series/s (CUDA events on the
+    launching stream, L2 flushed between steps, max over ranks), end-to-end series/s through the
+    host entry point (pinned buffers, copies inside the timed region), and per-kernel-class
+    device times from separate, untimed steps."""
+    import torch
+    b, q = x.shape[0], 21
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty((b, HORIZON, q), device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        model.forecast_chronos2_device(xd.data_ptr(), b, CONTEXT, HORIZON, out.data_ptr(), sp)
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    launches = model.last_launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    total_ms = 0.0
+    if clk:
+        clk.mark_begin()
+    for _ in range(a.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        e1.synchronize()
+        total_ms += e0.elapsed_time(e1)
+    if clk:
+        clk.mark_end()
+    torch.cuda.synchronize()
+    barrier()
+    ms_step = max_over_ranks(total_ms, world, "cuda") / a.steps
+    value = b * world / (ms_step / 1e3)
+
+    # End to end through the host entry point: pinned inputs in, quantiles out. Warm-up as above
+    # (the second call with these buffers captures the CUDA graphs; later calls replay them).
+    xp = torch.from_numpy(x).pin_memory()
+    op = torch.empty((b, HORIZON, q), dtype=torch.float32).pin_memory()
+    xnp, onp = xp.numpy(), op.numpy()
+    for _ in range(max(3, a.warmup)):
+        model.forecast_chronos2(xnp, HORIZON, out=onp)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        model.forecast_chronos2(xnp, HORIZON, out=onp)
+    e2e_s = (time.perf_counter() - t0) / a.steps
+    barrier()
+    e2e = b * world / max_over_ranks(e2e_s, world, "cuda")
+
+    model.profile(True)
+    model.profile_reset()
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    cls = {c: model.profile_read(c) for c in ("gemm", "attention", "rmsnorm", "patch", "head", "other")}
+    model.profile(False)
+    g = cls["gemm"]
+    achieved = g["work"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else None
+    kernels = {c: {"launches_per_step": v["launches"] / 2, "ms_per_step": v["ms"] / 2,
+                   "share": v["ms"] / max(1e-9, sum(u["ms"] for u in cls.values()))} for c, v in cls.items()}
+    if cls["attention"]["ms"] > 0:
+        kernels["attention"]["tflops"] = cls["attention"]["work"] / (cls["attention"]["ms"] / 1e3) / 1e12
+    # Memory-bound classes: algorithmic bytes (recorded per launch) over their device time, and the
+    # fraction of the measured HBM copy bandwidth.
+    for c in ("rmsnorm",):
+        if cls[c]["ms"] > 0 and cls[c]["work"] > 0:
+            kernels[c]["gbs"] = cls[c]["work"] / (cls[c]["ms"] / 1e3) / 1e9
+            kernels[c]["hbm_frac"] = kernels[c]["gbs"] / peaks()[2]
+    burst = peaks()[0]
+    return {"value": value, "ms_per_step": ms_step, "e2e": e2e, "launches": launches, "kernels": kernels,
+            "gemm_tflops": achieved, "tc_peak_frac": (GF_PER_SERIES * 1e9 * b / (ms_step / 1e3)) / (burst * 1e12)}
+
+
+def library_multi_device(a, world):
+    """The library's own multi-GPU path (rank 0 only, the other ranks waiting): one model with a
+    replica on each of the job's `world` devices forecasts world x 256 series through the host
+    entry point (strong scaling of one call: series sharded by the library, one host thread per
+    device), timed by the wall clock around the blocking call; the result is compared bit for bit
+    with a one-device model's."""
+    from tsfm_spec import synthetic as syn
+    _, w, multi = build_model(range(world), a.compute)
+    b = a.series * world
+    x = syn.seeded_series(b, CONTEXT, seed=series_seed(0, a.series))
+    for _ in range(2):
+        got = multi.forecast_chronos2(x, HORIZON)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        got = multi.forecast_chronos2(x, HORIZON)
+    dt = (time.perf_counter() - t0) / a.steps
+    multi.close()
+    _, _, one = build_model([0], a.compute)
+    ref = one.forecast_chronos2(x, HORIZON)
+    t0 = time.perf_counter()
+    ref = one.forecast_chronos2(x, HORIZON)
+    dt1 = time.perf_counter() - t0
+    one.close()
+    del w
+    return {"devices": world, "series_per_call": b, "e2e": b / dt, "e2e_one_device": b / dt1,
+            "unit": "series/s", "bit_identical_to_one_device": bool(np.array_equal(got, ref)),
+            "how": "one tsfm_model with a replica per device, host buffers, wall clock around the blocking call"}
+
+
 def main():
     a = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -602,121 +719,85 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    from tsfm_b200 import synthetic as syn
-    cfg, w, model = build_model(local)
-    del w
-    b, q = a.series, 21
+    from tsfm_spec import synthetic as syn
+    b = a.series
     x = syn.seeded_series(b, CONTEXT, seed=series_seed(rank, b))
-    xd = torch.from_numpy(x).cuda()
-    out = torch.empty((b, HORIZON, q), device="cuda")
-    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-
-    def step():
-        model.forecast_chronos2_device(xd.data_ptr(), b, CONTEXT, HORIZON, out.data_ptr(), sp)
-
+    _, w, model = build_model([local], a.compute)
+    del w
     clk = Clocks(local).start()
-    for _ in range(max(3, a.warmup)):
-        step()
-    torch.cuda.synchronize()
-    launches = model.last_launch_count()
-
-    # Device-resident throughput: events per step on the launching stream, L2 flushed in between.
-    barrier()
-    torch.cuda.synchronize()
-    total_ms = 0.0
-    clk.mark_begin()
-    for _ in range(a.steps):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        step()
-        e1.record(stream)
-        e1.synchronize()
-        total_ms += e0.elapsed_time(e1)
-    clk.mark_end()
+    head = measure(model, a, x, world, barrier, clk)
     clk.__exit__()
-    torch.cuda.synchronize()
-    barrier()
-    ms_step = max_over_ranks(total_ms, world, "cuda") / a.steps
-    value = b * world / (ms_step / 1e3)
-
-    # End to end through the host entry point: pinned inputs in, quantiles out.
-    xp = torch.from_numpy(x).pin_memory()
-    op = torch.empty((b, HORIZON, q), dtype=torch.float32).pin_memory()
-    xnp, onp = xp.numpy(), op.numpy()
-    # Warm-up as for the device-resident loop (the host entry point's second call with these buffers
-    # captures its CUDA graphs; later calls replay them).
-    for _ in range(max(3, a.warmup)):
-        model.forecast_chronos2(xnp, HORIZON, out=onp)
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(a.steps):
-        model.forecast_chronos2(xnp, HORIZON, out=onp)
-    e2e_s = (time.perf_counter() - t0) / a.steps
-    barrier()
-    e2e = b * world / max_over_ranks(e2e_s, world, "cuda")
-
-    # Per-kernel-class timing (events around every launch) on separate, untimed steps.
-    model.profile(True)
-    model.profile_reset()
-    for _ in range(2):
-        step()
-    torch.cuda.synchronize()
-    cls = {c: model.profile_read(c) for c in ("gemm", "attention", "rmsnorm", "patch", "head", "other")}
-    model.profile(False)
-    burst, sustained, hbm, src = peaks()
-    g = cls["gemm"]
-    achieved = g["work"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else None
-    traffic = traffic_from_profile()
-    kernels = {c: {"launches_per_step": v["launches"] / 2, "ms_per_step": v["ms"] / 2,
-                   "share": v["ms"] / max(1e-9, sum(u["ms"] for u in cls.values()))} for c, v in cls.items()}
-    if cls["attention"]["ms"] > 0:
-        kernels["attention"]["tflops"] = cls["attention"]["work"] / (cls["attention"]["ms"] / 1e3) / 1e12
-    # Memory-bound classes: algorithmic bytes (recorded per launch) over their device time, and the
-    # fraction of the measured HBM copy bandwidth.
-    for c in ("rmsnorm",):
-        if cls[c]["ms"] > 0 and cls[c]["work"] > 0:
-            kernels[c]["gbs"] = cls[c]["work"] / (cls[c]["ms"] / 1e3) / 1e9
-            kernels[c]["hbm_frac"] = kernels[c]["gbs"] / peaks()[2]
+    model.close()
+    fast = None
+    if not a.no_compare and a.compute != "f16":
+        _, w, m16 = build_model([local], "f16")
+        del w
+        fast = measure(m16, a, x, world, barrier)
+        m16.close()
+    multi = None
+    if world > 1:
+        # Rank 0 alone drives every GPU through one library model while the other ranks wait on the
+        # host (a gloo barrier): no collective kernel sits on a GPU that rank 0's kernels use.
+        host = dist.new_group(backend="gloo")
+        torch.cuda.synchronize()
+        dist.barrier(group=host)
+        if rank == 0:
+            try:
+                multi = library_multi_device(a, world)
+            except Exception as ex:  # reported, never hides the headline
+                multi = {"failed": str(ex)}
+        dist.barrier(group=host)
 
     if rank == 0:
+        burst, sustained, hbm, src = peaks()
         cpu = None
         try:
             v, cores, dt = cpu_baseline(a.cpu_sample)
             cpu = {"value": v, "unit": "series/s", "cores": cores, "kind": "port",
-                   "sample": f"{a.cpu_sample} series x 8192 steps, horizon 1024 ({dt:.1f} s)"}
+                   "sample": f"{a.cpu_sample} series x 8192 steps, horizon 1024, the GPU arm's first series "
+                             f"({dt:.1f} s)"}
         except Exception as ex:  # the baseline leg must not hide the GPU number
             cpu = {"value": None, "unit": "series/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
+        corr = a.compute == "f16c"
+        achieved = head["gemm_tflops"]
+        dtype = {"f16c": "f16+f8 (FP16 operands plus FP8 correction products, FP32 accumulation)",
+                 "f16": "f16 (FP32 accumulation)", "bf16": "bf16 (FP32 accumulation)"}[a.compute]
         line = {
-            "metric": METRIC, "value": value, "unit": "series/s", "n_gpus": world, "steps": a.steps,
-            "warmup": max(3, a.warmup), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded sine + random walk + noise, 5% NaN; "
-                                                             "random-init N(0,0.02) weights)",
-            "config": {"workload": "chronos2-ctx8192-h1024", "d_model": 768, "layers": 12, "heads": 12, "d_ff": 3072,
-                       "patch": 16, "quantiles": 21, "series_per_gpu": b, "global_batch": b * world,
-                       "context": CONTEXT, "horizon": HORIZON, "parallelism": f"series-sharded x{world}",
-                       "l2": "flushed between steps (256 MB write)"},
-            "tc_peak_frac": (GF_PER_SERIES * 1e9 * b / (ms_step / 1e3)) / (burst * 1e12),
+            "metric": METRIC, "value": head["value"], "unit": "series/s", "n_gpus": world, "steps": a.steps,
+            "warmup": max(3, a.warmup), "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic (seeded sine + random walk + noise, 5% NaN; random-init N(0,0.02) weights)",
+            "config": {"workload": "chronos2-ctx8192-h1024", "compute": a.compute, "d_model": 768, "layers": 12,
+                       "heads": 12, "d_ff": 3072, "patch": 16, "quantiles": 21, "series_per_gpu": b,
+                       "global_batch": b * world, "context": CONTEXT, "horizon": HORIZON,
+                       "parallelism": f"series-sharded x{world}", "l2": "flushed between steps (256 MB write)",
+                       "parity": ("max |dq| <= 1e-2 * sigma at this shape (tests/test_chronos2_gpu.py)" if corr
+                                  else "plain operands: the quantile tails exceed 1e-2 * sigma at this shape")},
+            "tc_peak_frac": head["tc_peak_frac"],
             "roofline": {"bound": "tensor", "kernel": "linear_tc_kernel (tcgen05 GEMM)", "achieved": achieved,
                          "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained if achieved else None,
-                         "peak_source": f"{src} bf16_tflops_sustained", "traffic": traffic},
-            "kernels": kernels,
+                         "peak_source": f"{src} bf16_tflops_sustained", "traffic": traffic_from_profile(),
+                         "tensor_work_per_algorithmic_flop": 2.0 if corr else 1.0},
+            "kernels": head["kernels"],
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e, "unit": "series/s", "h2d_bytes_per_step": b * CONTEXT * 4,
-                    "d2h_bytes_per_step": b * HORIZON * q * 4},
-            "gpu_launches": launches * a.steps,
+            "e2e": {"value": head["e2e"], "unit": "series/s", "h2d_bytes_per_step": b * CONTEXT * 4,
+                    "d2h_bytes_per_step": b * HORIZON * 21 * 4},
+            "gpu_launches": head["launches"] * a.steps,
             "clocks": clk.summary(),
         }
+        if fast:
+            line["f16_mode"] = {"value": fast["value"], "e2e": fast["e2e"], "ms_per_step": fast["ms_per_step"],
+                                "tc_peak_frac": fast["tc_peak_frac"], "gemm_tflops": fast["gemm_tflops"],
+                                "parity": "single-pass FP16 operands: quantile tails exceed 1e-2 * sigma here"}
+        if multi:
+            line["library_multi_gpu"] = multi
         print(json.dumps(line), flush=True)
-    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
