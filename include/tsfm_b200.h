@@ -292,12 +292,12 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
  * correction companions exactly as a TSFM_COMPUTE_F16C model holds them, then
  * y[M, N] (dense) = act(x W^T + bias) with out_mode 0 = FP16 (and, when y8 is not null, its FP8
  * companion [M, 2N] bytes: e4m3(y16 / 32) then e4m3((y - y16) * 128)), 1 = store f32,
- * 2 = accumulate into f32; act 0 none, 1 relu. Allocates its temporaries on `stream` and returns
- * after the product is enqueued. The kernel-level test of nn.linear's corrected form
- * (core/nn.zig:270-293). */
+ * 2 = accumulate into f32; act 0 none, 1 relu. terms = 2 adds both correction terms, 1 only the
+ * weight term x_hi (W - f16(W)). Allocates its temporaries on `stream` and returns after the
+ * product is enqueued. The kernel-level test of nn.linear's corrected form (core/nn.zig:270-293). */
 int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float *bias, void *y,
                                      void *y8, int32_t out_mode, int32_t act, int64_t M, int64_t N,
-                                     int64_t K, void *stream);
+                                     int64_t K, int32_t terms, void *stream);
 
 /* tsfm_kernel_attention: o = softmax(mask(scale · q k^T + bias)) v per (group, head) over `n`
  * tokens of head width 64, q/k/v bf16 with row stride ld_qkv (elements), o bf16 with row stride

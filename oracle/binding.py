@@ -38,6 +38,10 @@ def _load():
                                       ctypes.POINTER(SZ)]),
         "oracle_linear": (I32, [P, P, P, P, SZ, SZ, SZ]),
         "oracle_rmsnorm": (I32, [P, P, P, SZ, SZ, F]),
+        "oracle_chronos2_patch": (I32, [P, SZ, SZ, SZ, SZ, F, I32, P, P, P, P]),
+        "oracle_bolt_patch": (I32, [P, SZ, SZ, SZ, SZ, I32, P, P, P, P]),
+        "oracle_timestral_block_inputs": (I32, [P, P, SZ, SZ, SZ, SZ, P, I32, ctypes.c_double, I32, I32, P, P, P, P,
+                                                P]),
         "oracle_target_encode": (I32, [P, P, SZ, SZ, SZ, P, SZ, SZ, I32, P]),
         "oracle_f32_digits_batch": (None, [P, SZ, P, P]),
         "oracle_f32_digits_search_batch": (None, [P, SZ, P, P]),

@@ -406,6 +406,61 @@ struct C2Layer {
     Weight wi, wo;
 };
 
+// runChunk's masked instance norm and context-patch features (chronos2/forecaster.zig:94-143)
+// for nb series (row li at inputs + li * stride + start, t steps, left-padded by pad): loc, scale
+// (f64 sums, population std, 0 -> 1e-5, all missing -> 0 / 1), features [time, value, mask] per
+// patch and each patch's validity (any observed step).
+void c2_patch_features(const float *inputs, size_t stride, size_t start, size_t t, size_t pad, size_t n_ctx,
+                       size_t ps, float tscale, bool arcsinh, size_t nb, float *loc, float *scale, float *feats,
+                       uint8_t *ctx_valid) {
+    for (size_t li = 0; li < nb; ++li) {
+        const float *row = inputs + li * stride + start;
+        double count = 0, sum = 0;
+        for (size_t i = 0; i < t; ++i)
+            if (!std::isnan(row[i])) {
+                count += 1;
+                sum += row[i];
+            }
+        float lo = 0.0f, sc = 1.0f;
+        if (count > 0) {
+            lo = (float)(sum / count);
+            double ss = 0;
+            for (size_t i = 0; i < t; ++i)
+                if (!std::isnan(row[i])) {
+                    const float dv = row[i] - lo;
+                    ss += (double)dv * (double)dv;
+                }
+            sc = (float)std::sqrt(ss / count);
+            if (sc == 0.0f) sc = 1e-5f;
+        }
+        loc[li] = lo;
+        scale[li] = sc;
+        for (size_t p = 0; p < n_ctx; ++p) {
+            bool any = false;
+            const size_t base = (li * n_ctx + p) * 3 * ps;
+            for (size_t i = 0; i < ps; ++i) {
+                const size_t j = p * ps + i;
+                const long src = (long)j - (long)pad;
+                bool obs = false;
+                float val = 0.0f;
+                if (src >= 0 && src < (long)t) {
+                    const float xv = row[src];
+                    if (!std::isnan(xv)) {
+                        obs = true;
+                        val = (xv - lo) / sc;
+                        if (arcsinh) val = std::asinh(val);
+                    }
+                }
+                feats[base + i] = ((float)j - (float)(n_ctx * ps)) / tscale;
+                feats[base + ps + i] = val;
+                feats[base + 2 * ps + i] = obs ? 1.0f : 0.0f;
+                any = any || obs;
+            }
+            ctx_valid[li * n_ctx + p] = any;
+        }
+    }
+}
+
 struct Chronos2 {
     tsfm_config c{};
     std::vector<double> quantiles;
@@ -541,51 +596,9 @@ struct Chronos2 {
         const bool arcsinh = c.use_arcsinh != 0;
         std::vector<float> loc(nb), scale(nb), feats(nb * n_ctx * 3 * ps), fut(nb * n_out * 3 * ps);
         std::vector<uint8_t> ctx_valid(nb * n_ctx);
+        c2_patch_features(inputs + s0 * stride, stride, start, t, pad, n_ctx, ps, tscale, arcsinh, nb, loc.data(),
+                          scale.data(), feats.data(), ctx_valid.data());
         for (size_t li = 0; li < nb; ++li) {
-            const float *row = inputs + (s0 + li) * stride + start;
-            double count = 0, sum = 0;
-            for (size_t i = 0; i < t; ++i)
-                if (!std::isnan(row[i])) {
-                    count += 1;
-                    sum += row[i];
-                }
-            float lo = 0.0f, sc = 1.0f;
-            if (count > 0) {
-                lo = (float)(sum / count);
-                double ss = 0;
-                for (size_t i = 0; i < t; ++i)
-                    if (!std::isnan(row[i])) {
-                        const float dv = row[i] - lo;
-                        ss += (double)dv * (double)dv;
-                    }
-                sc = (float)std::sqrt(ss / count);
-                if (sc == 0.0f) sc = 1e-5f;
-            }
-            loc[li] = lo;
-            scale[li] = sc;
-            for (size_t p = 0; p < n_ctx; ++p) {
-                bool any = false;
-                const size_t base = (li * n_ctx + p) * 3 * ps;
-                for (size_t i = 0; i < ps; ++i) {
-                    const size_t j = p * ps + i;
-                    const long src = (long)j - (long)pad;
-                    bool obs = false;
-                    float val = 0.0f;
-                    if (src >= 0 && src < (long)t) {
-                        const float xv = row[src];
-                        if (!std::isnan(xv)) {
-                            obs = true;
-                            val = (xv - lo) / sc;
-                            if (arcsinh) val = std::asinh(val);
-                        }
-                    }
-                    feats[base + i] = ((float)j - (float)(n_ctx * ps)) / tscale;
-                    feats[base + ps + i] = val;
-                    feats[base + 2 * ps + i] = obs ? 1.0f : 0.0f;
-                    any = any || obs;
-                }
-                ctx_valid[li * n_ctx + p] = any;
-            }
             for (size_t p = 0; p < n_out; ++p) {
                 const size_t base = (li * n_out + p) * 3 * ps;
                 for (size_t i = 0; i < ps; ++i) {
@@ -667,6 +680,59 @@ struct BoltDec {
     std::vector<float> self_norm, cross_norm, ffn_norm;
     Weight self_v, self_o, cross_q, cross_k, cross_v, cross_o, wi, wo;
 };
+
+// runChunk's instance norm and patch features (chronos_bolt/forecaster.zig:150-197) for nb rows
+// (row li at ctx + li * stride + offset, len steps, left-padded by pad): loc, scale, features
+// [value, mask] per patch, each patch's validity in kv (row stride seq), and the REG token's
+// validity after the patches when use_reg.
+void bolt_patch_features(const float *ctx, size_t stride, size_t offset, size_t len, size_t pad, size_t n_patch,
+                         size_t ps, size_t seq, bool use_reg, size_t nb, float *loc, float *scale, float *feats,
+                         uint8_t *kv) {
+    for (size_t li = 0; li < nb; ++li) {
+        const float *row = ctx + li * stride + offset;
+        double count = 0, sum = 0;
+        for (size_t i = 0; i < len; ++i)
+            if (!std::isnan(row[i])) {
+                count += 1;
+                sum += row[i];
+            }
+        float lo = 0.0f, sc = 1.0f;
+        if (count > 0) {
+            lo = (float)(sum / count);
+            double ss = 0;
+            for (size_t i = 0; i < len; ++i)
+                if (!std::isnan(row[i])) {
+                    const float dv = row[i] - lo;
+                    ss += (double)dv * (double)dv;
+                }
+            sc = (float)std::sqrt(ss / count);
+            if (sc == 0.0f) sc = 1e-5f;
+        }
+        loc[li] = lo;
+        scale[li] = sc;
+        for (size_t p = 0; p < n_patch; ++p) {
+            bool any = false;
+            const size_t base = (li * n_patch + p) * 2 * ps;
+            for (size_t i = 0; i < ps; ++i) {
+                const long src = (long)(p * ps + i) - (long)pad;
+                bool obs = false;
+                float val = 0.0f;
+                if (src >= 0) {
+                    const float xv = row[src];
+                    if (!std::isnan(xv)) {
+                        obs = true;
+                        val = (xv - lo) / sc;
+                    }
+                }
+                feats[base + i] = val;
+                feats[base + ps + i] = obs ? 1.0f : 0.0f;
+                any = any || obs;
+            }
+            kv[li * seq + p] = any;
+        }
+        if (use_reg) kv[li * seq + n_patch] = 1;
+    }
+}
 
 struct Bolt {
     tsfm_config c{};
@@ -824,50 +890,8 @@ struct Bolt {
         const size_t seq = n_patch + (use_reg ? 1 : 0), nb = s1 - s0;
         std::vector<float> loc(nb), scale(nb), feats(nb * n_patch * 2 * ps);
         std::vector<uint8_t> kv(nb * seq);
-        for (size_t li = 0; li < nb; ++li) {
-            const float *row = ctx + (s0 + li) * stride + offset;
-            double count = 0, sum = 0;
-            for (size_t i = 0; i < len; ++i)
-                if (!std::isnan(row[i])) {
-                    count += 1;
-                    sum += row[i];
-                }
-            float lo = 0.0f, sc = 1.0f;
-            if (count > 0) {
-                lo = (float)(sum / count);
-                double ss = 0;
-                for (size_t i = 0; i < len; ++i)
-                    if (!std::isnan(row[i])) {
-                        const float dv = row[i] - lo;
-                        ss += (double)dv * (double)dv;
-                    }
-                sc = (float)std::sqrt(ss / count);
-                if (sc == 0.0f) sc = 1e-5f;
-            }
-            loc[li] = lo;
-            scale[li] = sc;
-            for (size_t p = 0; p < n_patch; ++p) {
-                bool any = false;
-                const size_t base = (li * n_patch + p) * 2 * ps;
-                for (size_t i = 0; i < ps; ++i) {
-                    const long src = (long)(p * ps + i) - (long)pad;
-                    bool obs = false;
-                    float val = 0.0f;
-                    if (src >= 0) {
-                        const float xv = row[src];
-                        if (!std::isnan(xv)) {
-                            obs = true;
-                            val = (xv - lo) / sc;
-                        }
-                    }
-                    feats[base + i] = val;
-                    feats[base + ps + i] = obs ? 1.0f : 0.0f;
-                    any = any || obs;
-                }
-                kv[li * seq + p] = any;
-            }
-            if (use_reg) kv[li * seq + n_patch] = 1;
-        }
+        bolt_patch_features(ctx + s0 * stride, stride, offset, len, pad, n_patch, ps, seq, use_reg, nb, loc.data(),
+                            scale.data(), feats.data(), kv.data());
         std::vector<float> emb(nb * n_patch * d);
         input_embed.forward(emb.data(), feats.data(), nb * n_patch);
         std::vector<float> x(nb * seq * d);
@@ -978,6 +1002,112 @@ Welford welford_combine(Welford a, Welford b) {  // timestral/forecaster.zig:567
     return {w, a.mean + delta * b.w / w_safe, a.m2 + b.m2 + delta * delta * a.w * b.w / w_safe};
 }
 
+// patchStats / StatsJob (timestral/model.zig:213-216, 712-750): causal per-patch loc and scale of
+// each row, f64 running sums over the observed steps, rounded to f32.
+void ts_patch_stats(float *loc, float *scale, const float *data, const uint8_t *observed, size_t rows, size_t t,
+                size_t ps, double min_scale) {
+    const size_t n = t / ps;
+    for (size_t r = 0; r < rows; ++r) {
+        double cum_w = 0, cum_x = 0, m2 = 0, prev_mean = 0;
+        for (size_t p = 0; p < n; ++p) {
+            for (size_t k = 0; k < ps; ++k) {
+                const size_t i = p * ps + k;
+                const double w = observed[r * t + i] ? 1.0 : 0.0;
+                const double x = data[r * t + i];
+                cum_w += w;
+                cum_x += w * x;
+                const double den = std::max(cum_w, 1.0);
+                const double mean = cum_x / den;
+                m2 += (x - prev_mean) * (x - mean) * w;
+                prev_mean = mean;
+            }
+            const double den = std::max(cum_w, 1.0);
+            const double variance = m2 / std::max(den - 1.0, 1.0);
+            loc[r * n + p] = (float)prev_mean;
+            scale[r * n + p] = (float)std::max(std::sqrt(variance), min_scale);
+        }
+    }
+}
+
+// predictBlock's window statistics and patch features (timestral/model.zig:253-327) over rows of
+// w steps (full / full_obs): causal per-patch loc and scale, known rows (role 2, with covariates)
+// normalised by their whole-row mean and std (binary rows unscaled and without asinh), features
+// [asinh((x - loc) / scale), missing] per step (emb_in rows of 2 * ps per patch).
+void ts_block_features(float *loc, float *scale, float *emb_in, const float *full, const uint8_t *full_obs,
+                       size_t rows, size_t w, size_t ps, size_t vall, const std::vector<Role> &roles, bool cov,
+                       double min_scale, bool use_arcsinh) {
+    const size_t n = w / ps;
+    ts_patch_stats(loc, scale, full, full_obs, rows, w, ps, min_scale);
+    const float eps32 = std::numeric_limits<float>::epsilon();
+    for (size_t r = 0; r < rows; ++r) {
+        const bool known = cov && roles[r % vall] == R_KNOWN;
+        float kloc = 0.0f, kscale = 1.0f;
+        bool binary = false;
+        if (known) {
+            float cnt = 0.0f, sum = 0.0f;
+            bool zero_one = true, any = false;
+            for (size_t i = 0; i < w; ++i)
+                if (full_obs[r * w + i]) {
+                    const float xv = full[r * w + i];
+                    cnt += 1.0f;
+                    sum += xv;
+                    zero_one = zero_one && (xv == 0.0f || xv == 1.0f);
+                    any = true;
+                }
+            kloc = sum / std::max(cnt, 1.0f);
+            float ss = 0.0f;
+            for (size_t i = 0; i < w; ++i)
+                if (full_obs[r * w + i]) {
+                    const float dv = full[r * w + i] - kloc;
+                    ss += dv * dv;
+                }
+            kscale = std::max(std::sqrt(ss / std::max(cnt, 1.0f)), (float)min_scale);
+            binary = zero_one && any;
+            if (binary) {
+                kloc = 0.0f;
+                kscale = 1.0f;
+            }
+        }
+        for (size_t p = 0; p < n; ++p) {
+            const float lo = known ? kloc : loc[r * n + p];
+            const float sc = std::max(known ? kscale : scale[r * n + p], eps32);
+            float *dst = &emb_in[(r * n + p) * 2 * ps];
+            for (size_t i = 0; i < ps; ++i) {
+                const bool o = full_obs[r * w + p * ps + i];
+                float v = 0.0f;
+                if (o) {
+                    v = (full[r * w + p * ps + i] - lo) / sc;
+                    if (use_arcsinh && !(known && binary)) v = std::asinh(v);
+                }
+                dst[i] = v;
+                dst[ps + i] = o ? 0.0f : 1.0f;
+            }
+        }
+    }
+}
+
+// predictBlock's key validity and first observed patch per group (timestral/model.zig:344-362):
+// a patch is a valid key when any step is observed (or, with attend_missing, once the row has
+// started); first_obs[g] = the group's first observed patch (0 when none).
+void ts_key_valid(uint8_t *key_valid, size_t *first_obs, const uint8_t *full_obs, size_t rows, size_t w, size_t ps,
+                  size_t vall, size_t groups, bool attend_missing) {
+    const size_t ne = w / ps;
+    for (size_t g = 0; g < groups; ++g) first_obs[g] = ne;
+    for (size_t r = 0; r < rows; ++r) {
+        const size_t grp = r / vall;
+        bool started = false;
+        for (size_t p = 0; p < ne; ++p) {
+            bool o = false;
+            for (size_t i = 0; i < ps; ++i) o = o || full_obs[r * w + p * ps + i];
+            if (o) first_obs[grp] = std::min(first_obs[grp], p);
+            started = started || o;
+            key_valid[r * ne + p] = attend_missing ? (o || started) : o;
+        }
+    }
+    for (size_t g = 0; g < groups; ++g)
+        if (first_obs[g] == ne) first_obs[g] = 0;
+}
+
 struct Timestral {
     tsfm_config c{};
     std::vector<double> knots;
@@ -1068,28 +1198,7 @@ struct Timestral {
     // patchStats / StatsJob (timestral/model.zig:213-216, 712-750).
     void patch_stats(float *loc, float *scale, const float *data, const uint8_t *observed,
                      size_t rows, size_t t) const {
-        const size_t ps = c.patch_size, n = t / ps;
-        const double min_scale = c.minimum_scale;
-        for (size_t r = 0; r < rows; ++r) {
-            double cum_w = 0, cum_x = 0, m2 = 0, prev_mean = 0;
-            for (size_t p = 0; p < n; ++p) {
-                for (size_t k = 0; k < ps; ++k) {
-                    const size_t i = p * ps + k;
-                    const double w = observed[r * t + i] ? 1.0 : 0.0;
-                    const double x = data[r * t + i];
-                    cum_w += w;
-                    cum_x += w * x;
-                    const double den = std::max(cum_w, 1.0);
-                    const double mean = cum_x / den;
-                    m2 += (x - prev_mean) * (x - mean) * w;
-                    prev_mean = mean;
-                }
-                const double den = std::max(cum_w, 1.0);
-                const double variance = m2 / std::max(den - 1.0, 1.0);
-                loc[r * n + p] = (float)prev_mean;
-                scale[r * n + p] = (float)std::max(std::sqrt(variance), min_scale);
-            }
-        }
+        ts_patch_stats(loc, scale, data, observed, rows, t, c.patch_size, c.minimum_scale);
     }
 
     struct Geo {
@@ -1299,54 +1408,9 @@ struct Timestral {
             full_obs = fobuf.data();
         }
         std::vector<float> loc(rows * n), scale(rows * n);
-        patch_stats(loc.data(), scale.data(), full, full_obs, rows, w);
-        const float eps32 = std::numeric_limits<float>::epsilon();
         std::vector<float> emb_in(rows * n * 2 * ps);
-        for (size_t r = 0; r < rows; ++r) {
-            const bool known = cov && roles[r % vall] == R_KNOWN;
-            float kloc = 0.0f, kscale = 1.0f;
-            bool binary = false;
-            if (known) {
-                float cnt = 0.0f, sum = 0.0f;
-                bool zero_one = true, any = false;
-                for (size_t i = 0; i < w; ++i)
-                    if (full_obs[r * w + i]) {
-                        const float xv = full[r * w + i];
-                        cnt += 1.0f;
-                        sum += xv;
-                        zero_one = zero_one && (xv == 0.0f || xv == 1.0f);
-                        any = true;
-                    }
-                kloc = sum / std::max(cnt, 1.0f);
-                float ss = 0.0f;
-                for (size_t i = 0; i < w; ++i)
-                    if (full_obs[r * w + i]) {
-                        const float dv = full[r * w + i] - kloc;
-                        ss += dv * dv;
-                    }
-                kscale = std::max(std::sqrt(ss / std::max(cnt, 1.0f)), (float)c.minimum_scale);
-                binary = zero_one && any;
-                if (binary) {
-                    kloc = 0.0f;
-                    kscale = 1.0f;
-                }
-            }
-            for (size_t p = 0; p < n; ++p) {
-                const float lo = known ? kloc : loc[r * n + p];
-                const float sc = std::max(known ? kscale : scale[r * n + p], eps32);
-                float *dst = &emb_in[(r * n + p) * 2 * ps];
-                for (size_t i = 0; i < ps; ++i) {
-                    const bool o = full_obs[r * w + p * ps + i];
-                    float v = 0.0f;
-                    if (o) {
-                        v = (full[r * w + p * ps + i] - lo) / sc;
-                        if (c.use_arcsinh && !(known && binary)) v = std::asinh(v);
-                    }
-                    dst[i] = v;
-                    dst[ps + i] = o ? 0.0f : 1.0f;
-                }
-            }
-        }
+        ts_block_features(loc.data(), scale.data(), emb_in.data(), full, full_obs, rows, w, ps, vall, roles, cov,
+                          c.minimum_scale, c.use_arcsinh != 0);
         const size_t ne = n, sl = ne + h;
         std::vector<float> x(rows * sl * d), enc(rows * ne * d);
         patch_proj.forward(enc.data(), emb_in.data(), rows * ne);
@@ -1356,19 +1420,8 @@ struct Timestral {
         }
         std::vector<uint8_t> key_valid(rows * ne);
         std::vector<size_t> first_obs(groups, ne);
-        for (size_t r = 0; r < rows; ++r) {
-            const size_t grp = r / vall;
-            bool started = false;
-            for (size_t p = 0; p < ne; ++p) {
-                bool o = false;
-                for (size_t i = 0; i < ps; ++i) o = o || full_obs[r * w + p * ps + i];
-                if (o) first_obs[grp] = std::min(first_obs[grp], p);
-                started = started || o;
-                key_valid[r * ne + p] = c.attend_missing_patches ? (o || started) : o;
-            }
-        }
-        for (auto &f : first_obs)
-            if (f == ne) f = 0;
+        ts_key_valid(key_valid.data(), first_obs.data(), full_obs, rows, w, c.patch_size, vall, groups,
+                     c.attend_missing_patches != 0);
         bool all_valid = true;
         for (uint8_t v : key_valid) all_valid = all_valid && v;
         Geo g{rows, groups, vall, ne, l, h, &roles, cov, &key_valid, all_valid, &first_obs};
@@ -2084,6 +2137,41 @@ int32_t oracle_linear(const float *x, const float *w, const float *bias, float *
         Weight wt;
         wt.init(std::vector<float>(w, w + out * in), out, in);
         linear(y, x, rows, wt, bias);
+    });
+}
+
+int32_t oracle_chronos2_patch(const float *inputs, size_t b, size_t t_in, size_t context_length, size_t ps,
+                              float tscale, int32_t arcsinh, float *loc, float *scale, float *feats,
+                              uint8_t *key_valid) {
+    return guarded([&] {
+        const size_t t = std::min(t_in, context_length), pad = (ps - t % ps) % ps, n_ctx = (t + pad) / ps;
+        c2_patch_features(inputs, t_in, t_in - t, t, pad, n_ctx, ps, tscale, arcsinh != 0, b, loc, scale, feats,
+                          key_valid);
+    });
+}
+
+int32_t oracle_bolt_patch(const float *inputs, size_t b, size_t t_in, size_t context_length, size_t ps,
+                          int32_t use_reg, float *loc, float *scale, float *feats, uint8_t *key_valid) {
+    return guarded([&] {
+        const size_t len = std::min(t_in, context_length), pad = (ps - len % ps) % ps, n_patch = (len + pad) / ps;
+        bolt_patch_features(inputs, t_in, t_in - len, len, pad, n_patch, ps, n_patch + (use_reg ? 1 : 0),
+                            use_reg != 0, b, loc, scale, feats, key_valid);
+    });
+}
+
+int32_t oracle_timestral_block_inputs(const float *full, const uint8_t *full_obs, size_t rows, size_t w, size_t ps,
+                                      size_t vall, const int8_t *roles, int32_t cov, double min_scale,
+                                      int32_t use_asinh, int32_t attend_missing, float *loc, float *scale,
+                                      float *feats, uint8_t *key_valid, int32_t *first_obs) {
+    return guarded([&] {
+        if (ps == 0 || vall == 0 || rows % vall || w % ps) fail(TSFM_ERR_INVALID_ARGUMENT, "block geometry");
+        std::vector<Role> rv(vall);
+        for (size_t i = 0; i < vall; ++i) rv[i] = (Role)roles[i];
+        ts_block_features(loc, scale, feats, full, full_obs, rows, w, ps, vall, rv, cov != 0, min_scale,
+                          use_asinh != 0);
+        std::vector<size_t> fo(rows / vall);
+        ts_key_valid(key_valid, fo.data(), full_obs, rows, w, ps, vall, rows / vall, attend_missing != 0);
+        for (size_t g = 0; g < fo.size(); ++g) first_obs[g] = (int32_t)fo[g];
     });
 }
 

@@ -78,6 +78,21 @@ int32_t oracle_linear(const float *x, const float *w, const float *bias, float *
                       size_t out, size_t in);
 int32_t oracle_rmsnorm(const float *x, const float *scale, float *out, size_t rows, size_t dim,
                        float eps);
+/* The indexing work of the three forecasters, for the bit-exact tests: Chronos-2's instance norm
+ * and context-patch features [time, value, mask] with patch validity (chronos2/forecaster.zig:
+ * 94-143; feats (b, n_ctx, 3 ps), key_valid (b, n_ctx)); Chronos-Bolt's [value, mask] features and
+ * validity with the REG slot (chronos_bolt/forecaster.zig:150-197; key_valid (b, n_patch + reg));
+ * Timestral's window statistics, features, key validity and first observed patch per group
+ * (timestral/model.zig:253-362; roles: one per row of a group, 0 target, 1 past, 2 known). */
+int32_t oracle_chronos2_patch(const float *inputs, size_t b, size_t t_in, size_t context_length, size_t ps,
+                              float tscale, int32_t arcsinh, float *loc, float *scale, float *feats,
+                              uint8_t *key_valid);
+int32_t oracle_bolt_patch(const float *inputs, size_t b, size_t t_in, size_t context_length, size_t ps,
+                          int32_t use_reg, float *loc, float *scale, float *feats, uint8_t *key_valid);
+int32_t oracle_timestral_block_inputs(const float *full, const uint8_t *full_obs, size_t rows, size_t w, size_t ps,
+                                      size_t vall, const int8_t *roles, int32_t cov, double min_scale,
+                                      int32_t use_asinh, int32_t attend_missing, float *loc, float *scale,
+                                      float *feats, uint8_t *key_valid, int32_t *first_obs);
 
 /* CSV output (oracle_csv.cpp): writeCsv of src/main.zig:181-198 and Zig's "{d}" rendering.
  * oracle_csv_format returns the text's length and fills out when capacity allows. */

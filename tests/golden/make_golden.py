@@ -1,7 +1,7 @@
 """Extract the reference's own known-answer vectors into tests/golden/kat.json.
 
-Run in a container that has the reference tree (default /root/reference, or the path in
-$TSFM_REFERENCE); the tests read only the JSON this writes, so the reference is not needed at
+Run in a checkout that has the reference tree beside the repository (../reference), or set
+$TSFM_REFERENCE to its path; the tests read only the JSON this writes, so the reference is not needed at
 test time. Every vector is read from the reference's test blocks, not retyped:
 
   - chronos_bolt/model.zig    test "relativeBucket matches transformers for -140..140"
@@ -18,7 +18,8 @@ import os
 import re
 import sys
 
-REF = os.environ.get("TSFM_REFERENCE", "/root/reference")
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+REF = os.environ.get("TSFM_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
 
 
 def read(rel):

@@ -283,12 +283,12 @@ CORR_SHAPES = [(300, 336, 48), (1000, 768, 768), (257, 128, 3072), (4096, 2304, 
                (7, 64, 200)]
 
 
-def linear_corrected(x, w, bias, y, y8, out_mode, act):
+def linear_corrected(x, w, bias, y, y8, out_mode, act, terms=2):
     M, K = x.shape
     N = w.shape[0]
     tb.check(tb.lib.tsfm_kernel_linear_corrected(x.data_ptr(), w.data_ptr(), None if bias is None else bias.data_ptr(),
                                                  y.data_ptr(), None if y8 is None else y8.data_ptr(), out_mode, act,
-                                                 M, N, K, stream_ptr()))
+                                                 M, N, K, terms, stream_ptr()))
     torch.cuda.synchronize()
 
 
@@ -337,3 +337,19 @@ def test_linear_corrected_fp8_companion_bits(M, N, K):
     h = a16.astype(np.float32)
     assert np.array_equal(a8[:, :N], e4m3_bits(h * np.float32(1 / 32)))
     assert np.array_equal(a8[:, N:], e4m3_bits((a32 - h) * np.float32(128)))
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 336, 48), (4096, 2304, 768), (257, 128, 3072)])
+def test_linear_weight_term_only(M, N, K):
+    # terms = 1: only x_hi (W - f16(W)) is added, so the result is the product of the FP16-rounded
+    # input with the full-precision weight: against float64 of (f16(x), W), within 2^-12 of
+    # sum_k |x_k w_k|.
+    g = torch.Generator(device="cpu").manual_seed(M + 3 * N + K)
+    x = torch.randn(M, K, generator=g).to(dev())
+    w = (torch.randn(N, K, generator=g) * 0.05).to(dev())
+    y = torch.full((M, N), float("nan"), device=dev())
+    linear_corrected(x, w, None, y, None, 1, 0, terms=1)
+    xh = x.half().double()
+    ref = xh @ w.double().T
+    mag = xh.abs() @ w.double().abs().T
+    assert ((y.double() - ref).abs() <= 2.0 ** -12 * mag + 1e-6).all()

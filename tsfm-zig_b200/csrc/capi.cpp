@@ -581,12 +581,13 @@ int32_t tsfm_kernel_linear(const void *x, int32_t x_dtype, const void *w, int32_
 }
 
 int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float *bias, void *y, void *y8,
-                                     int32_t out_mode, int32_t act, int64_t M, int64_t N, int64_t K, void *stream) {
+                                     int32_t out_mode, int32_t act, int64_t M, int64_t N, int64_t K, int32_t terms,
+                                     void *stream) {
     return guarded([&]() -> Status {
         if (!x || !w || !y) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
         if (M <= 0 || N <= 0 || K <= 0 || K % 8) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad shape");
-        if (out_mode < 0 || out_mode > 2 || (act != 0 && act != 1) || (y8 && out_mode != 0))
-            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode / act / y8");
+        if (out_mode < 0 || out_mode > 2 || (act != 0 && act != 1) || (y8 && out_mode != 0) || (terms != 1 && terms != 2))
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode / act / y8 / terms");
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         // Temporaries: the FP16 operands and their FP8 companions, as a corrected model holds them.
         void *buf = nullptr;
@@ -617,6 +618,7 @@ int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float
             c.w8 = w8;
             c.ldw8 = 2 * K;
             c.acc_scale = std::ldexp(1.0f, -sh);
+            c.x8_cols = terms == 1 ? K : 2 * K;
             c.y8 = y8;
             c.ldy8 = 2 * N;
             res = launch_linear(c, st);

@@ -114,6 +114,9 @@ struct LinearCall {
     const void *w8 = nullptr;
     int64_t ldw8 = 0;
     float acc_scale = 1.0f;
+    // Correction columns: 2K (0 = default) adds both terms; K adds only the weight term
+    // x_hi (W - f16(W)) (the first half of both companions), half the FP8 work.
+    int64_t x8_cols = 0;
     // FP8 companion of a 16-bit output (y8 set; the output's column count a multiple of 64):
     // y8 row r = [e4m3(f16(y) * kX8HiScale) | e4m3((y - f16(y)) * kX8LoScale)], each part as
     // wide as y, row stride ldy8 bytes. With norm_out, norm_x8 is the companion of norm_x16.

@@ -81,9 +81,11 @@ struct Epi {
     void *nx16;
     int64_t ldx16;
     const float *ngamma;
-    // Corrected products: the accumulator is multiplied by acc_scale before the epilogue; y8 /
+    // Corrected products: K8 companion columns per row take part (2K: both correction terms; K:
+    // the weight term only); the accumulator is multiplied by acc_scale before the epilogue; y8 /
     // nx8 (bytes, row strides ldy8 / ldnx8) receive the FP8 companions of the 16-bit outputs, the
     // low-part block `y8_half` / `nx8_half` bytes after the high part.
+    int64_t K8;
     float acc_scale;
     uint8_t *y8;
     int64_t ldy8, y8_half;
@@ -247,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t m_tiles = (e.M + kRows - 1) / kRows, n_tiles = (e.N + BN - 1) / BN;
     const int64_t tiles = m_tiles * n_tiles;
-    const int num_k8 = CORR ? (int)((2 * e.K + 127) / 128) : 0;  // FP8 correction stages
+    const int num_k8 = CORR ? (int)((e.K8 + 127) / 128) : 0;  // FP8 correction stages
     const int num_k = num_k8 + (int)((e.K + BK - 1) / BK);
 
     if (threadIdx.x == 0) {
@@ -871,8 +873,9 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     if (!s) return s;
     CUtensorMap ta8 = ta, tb8 = tb;  // unused unless CORR
     if constexpr (CORR) {
-        TSFM_TRY(make_tmap(&ta8, c.x8, E_U8, 2 * c.K, c.M, c.ldx8, 128, kBM));
-        TSFM_TRY(make_tmap(&tb8, c.w8, E_U8, 2 * c.K, c.N, c.ldw8, 128, C::B_ROWS));
+        const int64_t k8 = c.x8_cols > 0 ? c.x8_cols : 2 * c.K;
+        TSFM_TRY(make_tmap(&ta8, c.x8, E_U8, k8, c.M, c.ldx8, 128, kBM));
+        TSFM_TRY(make_tmap(&tb8, c.w8, E_U8, k8, c.N, c.ldw8, 128, C::B_ROWS));
     }
     TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&linear_tc_kernel<T, BN, PAIR, NORM, CORR>), C::SMEM));
     cudaError_t ce;
@@ -905,6 +908,7 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     e.ldx16 = c.ld_x16;
     e.ngamma = c.norm_gamma;
     e.acc_scale = CORR ? c.acc_scale : 1.0f;
+    e.K8 = c.x8_cols > 0 ? c.x8_cols : 2 * c.K;
     e.y8 = static_cast<uint8_t *>(c.y8);
     e.ldy8 = c.ldy8;
     e.y8_half = c.act == ACT_GLU ? c.N / 2 : c.N;
@@ -1010,7 +1014,8 @@ Status launch_linear(const LinearCall &c, cudaStream_t stream) {
     const auto a16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     const bool corr = c.x8 != nullptr;
     if (corr && (c.dtype != E_F16 || !c.w8 || c.K % 8 || c.ldx8 % 16 || c.ldw8 % 16 || c.ldx8 < 2 * c.K ||
-                 c.ldw8 < 2 * c.K || !a16(c.x8) || !a16(c.w8) || !(c.acc_scale > 0.0f)))
+                 c.ldw8 < 2 * c.K || !a16(c.x8) || !a16(c.w8) || !(c.acc_scale > 0.0f) ||
+                 (c.x8_cols != 0 && c.x8_cols != c.K && c.x8_cols != 2 * c.K)))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT,
                             "linear: corrected products need FP16 operands, K % 8 == 0 and 16-byte-aligned FP8 companions");
     if (c.y8) {
