@@ -299,6 +299,41 @@ int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float
                                      void *y8, int32_t out_mode, int32_t act, int64_t M, int64_t N,
                                      int64_t K, int32_t terms, void *stream);
 
+/* The indexing work of the forecasters, exposed for bit-exact parity tests. All return after
+ * enqueueing on `stream`; pointers are device pointers.
+ *
+ * tsfm_relative_bucket: relativeBucket (chronos_bolt/model.zig:74-85), the T5 bucket of key - query
+ *   offset `rel` that the Bolt encoder's bias table is built from (host function; -1 on bad
+ *   arguments).
+ * tsfm_kernel_patch: the instance norm and context-patch features of one forecast call, as the
+ *   forward computes them before its first product (features here in exact FP32, not rounded to
+ *   the TF32 operand): family TSFM_CHRONOS2 (chronos2/forecaster.zig:94-143; features
+ *   [time, value, mask] of 3 * patch per patch, key_valid (b, n_ctx)) or TSFM_CHRONOS_BOLT
+ *   (chronos_bolt/forecaster.zig:150-197; [value, mask] of 2 * patch, key_valid (b, n_ctx + reg)
+ *   with the REG slot valid); inputs (b, t_in) with NaN = missing, the last context_length steps
+ *   used, left-padded to a multiple of patch; loc, scale (b).
+ * tsfm_kernel_timestral_block_inputs: predictBlock's window statistics (f64 causal Welford, f32
+ *   results), features [asinh((x - loc) / scale), missing] per step (exact FP32), key validity and
+ *   first observed patch per group (timestral/model.zig:253-362; INT32_MAX for a group without an
+ *   observed patch, which the forward treats as 0) over rows of t context steps, then with
+ *   covariates hl known-future steps (rows of role 2 normalised by their whole-row statistics);
+ *   roles: one int8 per row of a group of vall rows (0 target, 1 past, 2 known). loc / scale /
+ *   key_valid (rows, n), feats (rows, n, 2 * patch), n = (t + hl) / patch. Allocates a few bytes per
+ *   row of temporaries on `stream`. */
+int32_t tsfm_relative_bucket(int64_t rel, int32_t num_buckets, int32_t max_distance);
+int32_t tsfm_kernel_patch(int32_t family, const float *inputs, int64_t b, int64_t t_in,
+                          int64_t context_length, int32_t patch, float time_encoding_scale,
+                          int32_t use_arcsinh, int32_t use_reg_token, float *loc, float *scale,
+                          float *feats, uint8_t *key_valid, void *stream);
+int32_t tsfm_kernel_timestral_block_inputs(const float *ctx, const uint8_t *observed, int64_t rows,
+                                           int64_t t, const float *known_future,
+                                           const uint8_t *known_future_observed, int64_t hl,
+                                           int32_t patch, int32_t vall, const int8_t *roles,
+                                           int32_t covariates, double minimum_scale,
+                                           int32_t use_asinh, int32_t attend_missing, float *loc,
+                                           float *scale, float *feats, uint8_t *key_valid,
+                                           int32_t *first_obs, void *stream);
+
 /* tsfm_kernel_attention: o = softmax(mask(scale · q k^T + bias)) v per (group, head) over `n`
  * tokens of head width 64, q/k/v bf16 with row stride ld_qkv (elements), o bf16 with row stride
  * ld_o; group g's tokens are rows [g*n, (g+1)*n). key_valid: (groups, n) bytes, or null = all

@@ -131,3 +131,18 @@ def test_synthetic_series_statistics():
     frac = np.isnan(x).mean()
     assert 0.03 < frac < 0.07
     assert np.array_equal(np.isnan(x), np.isnan(syn.seeded_series(8, 2048, seed=1)))
+
+
+def test_product_relative_bucket_matches_reference_table(kat):
+    # The library's own relativeBucket (host code that builds the Bolt encoder's bias table) against
+    # the reference's 281 expected bucket ids (chronos_bolt/model.zig test block, via kat.json), bit
+    # for bit, and against transformers' T5 over a wider range of offsets.
+    k = kat["relative_bucket"]
+    got = [tb.lib.tsfm_relative_bucket(k["rel_start"] + i, k["num_buckets"], k["max_distance"])
+           for i in range(len(k["expected"]))]
+    assert got == k["expected"]
+    t5 = pytest.importorskip("transformers.models.t5.modeling_t5")
+    torch = pytest.importorskip("torch")
+    rel = torch.arange(-700, 701)
+    want = t5.T5Attention._relative_position_bucket(rel, bidirectional=True, num_buckets=32, max_distance=128)
+    assert [tb.lib.tsfm_relative_bucket(int(r), 32, 128) for r in rel] == want.tolist()

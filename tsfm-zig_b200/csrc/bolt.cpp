@@ -17,11 +17,6 @@
 
 namespace tsfm {
 
-namespace {
-
-int64_t inner_dim(const tsfm_config &c) { return (int64_t)c.num_heads * c.d_kv; }
-int64_t vocab(const tsfm_config &c) { return c.use_reg_token ? 2 : 1; }
-
 // relativeBucket (chronos_bolt/model.zig:74-85): T5 bidirectional bucket with the float32 log.
 int64_t relative_bucket(int64_t rel, uint32_t num_buckets, uint32_t max_distance) {
     const uint32_t half = num_buckets / 2;
@@ -35,6 +30,11 @@ int64_t relative_bucket(int64_t rel, uint32_t num_buckets, uint32_t max_distance
     const uint32_t large = max_exact + (uint32_t)large_f;
     return base + std::min(large, half - 1);
 }
+
+namespace {
+
+int64_t inner_dim(const tsfm_config &c) { return (int64_t)c.num_heads * c.d_kv; }
+int64_t vocab(const tsfm_config &c) { return c.use_reg_token ? 2 : 1; }
 
 struct Geo {
     int64_t pad, n_patch, seq;

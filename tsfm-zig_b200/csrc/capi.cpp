@@ -628,6 +628,98 @@ int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float
     });
 }
 
+int32_t tsfm_relative_bucket(int64_t rel, int32_t num_buckets, int32_t max_distance) {
+    if (num_buckets < 2 || max_distance < 1) return -1;
+    return (int32_t)relative_bucket(rel, (uint32_t)num_buckets, (uint32_t)max_distance);
+}
+
+int32_t tsfm_kernel_patch(int32_t family, const float *inputs, int64_t b, int64_t t_in, int64_t context_length,
+                          int32_t patch, float time_encoding_scale, int32_t use_arcsinh, int32_t use_reg_token,
+                          float *loc, float *scale, float *feats, uint8_t *key_valid, void *stream) {
+    return guarded([&]() -> Status {
+        if (!inputs || !loc || !scale || !feats || !key_valid) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        if (family != TSFM_CHRONOS2 && family != TSFM_CHRONOS_BOLT)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "patch: family must be Chronos-2 or Chronos-Bolt");
+        if (b <= 0 || t_in <= 0 || context_length <= 0 || patch <= 0)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "patch: empty");
+        const bool bolt = family == TSFM_CHRONOS_BOLT;
+        const int64_t t = std::min(t_in, context_length), pad = (patch - t % patch) % patch;
+        const int64_t n_ctx = (t + pad) / patch;
+        PatchCall pc;
+        pc.inputs = inputs;
+        pc.stride = t_in;
+        pc.start = t_in - t;
+        pc.t = t;
+        pc.b = b;
+        pc.ps = patch;
+        pc.pad = (int)pad;
+        pc.n_ctx = (int)n_ctx;
+        pc.feat_kind = bolt ? 1 : 0;
+        pc.tscale = time_encoding_scale;
+        pc.arcsinh = bolt ? 0 : use_arcsinh;
+        pc.feat_mode = OUT_F32;
+        pc.feats = feats;
+        pc.loc = loc;
+        pc.scale = scale;
+        pc.key_valid = key_valid;
+        pc.seq = n_ctx + (bolt && use_reg_token ? 1 : 0);
+        pc.extra_valid = bolt && use_reg_token ? 1 : 0;
+        return launch_patch(pc, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t tsfm_kernel_timestral_block_inputs(const float *ctx, const uint8_t *observed, int64_t rows, int64_t t,
+                                           const float *known_future, const uint8_t *known_future_observed,
+                                           int64_t hl, int32_t patch, int32_t vall, const int8_t *roles,
+                                           int32_t covariates, double minimum_scale, int32_t use_asinh,
+                                           int32_t attend_missing, float *loc, float *scale, float *feats,
+                                           uint8_t *key_valid, int32_t *first_obs, void *stream) {
+    return guarded([&]() -> Status {
+        if (!ctx || !observed || !roles || !loc || !scale || !feats || !key_valid || !first_obs)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        if (rows <= 0 || t <= 0 || patch <= 0 || vall <= 0 || rows % vall || t % patch || (covariates && hl % patch) ||
+            hl < 0)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "timestral block inputs: bad geometry");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        void *buf = nullptr;
+        TSFM_CUDA(cudaMallocAsync(&buf, (size_t)rows * 9, st), "timestral block inputs: temporaries");
+        float *kloc = static_cast<float *>(buf), *kscale = kloc + rows;
+        uint8_t *binary = reinterpret_cast<uint8_t *>(kscale + rows);
+        Status res = Status::ok();
+        const cudaError_t e = cudaMemsetAsync(first_obs, 0x7f, (size_t)(rows / vall) * sizeof(int32_t), st);
+        if (e != cudaSuccess) res = Status::cuda(e, "timestral block inputs: first_obs");
+        if (res) {
+            TsStatsCall sc;
+            sc.ctx = ctx;
+            sc.obs = observed;
+            sc.t = t;
+            sc.kf = covariates ? known_future : nullptr;
+            sc.kfm = covariates ? known_future_observed : nullptr;
+            sc.kf_ld = hl;
+            sc.hl = covariates ? hl : 0;
+            sc.cov = covariates != 0;
+            sc.rows = rows;
+            sc.ps = patch;
+            sc.vall = vall;
+            sc.roles = roles;
+            sc.min_scale = minimum_scale;
+            sc.use_asinh = use_asinh;
+            sc.attend_missing = attend_missing;
+            sc.loc = loc;
+            sc.scale = scale;
+            sc.kloc = kloc;
+            sc.kscale = kscale;
+            sc.binary = binary;
+            sc.key_valid = key_valid;
+            sc.first_obs = first_obs;
+            sc.raw_feats = 1;
+            res = launch_ts_stats(sc, feats, st);
+        }
+        cudaFreeAsync(buf, st);
+        return res;
+    });
+}
+
 int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64_t ld_qkv, void *o, int64_t ld_o,
                               const uint8_t *key_valid, const float *rel_bias, int32_t groups, int32_t heads, int32_t n,
                               float scale, int32_t mask_mode, int32_t dtype, void *stream) {

@@ -95,6 +95,9 @@ Status c2_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, 
 Status c2_forecast(Replica &r, const tsfm_config &c, const C2Dev &w, const float *d_in, int64_t b, int64_t t_in,
                    int64_t horizon, float *d_out, cudaStream_t s);
 
+// relativeBucket (chronos_bolt/model.zig:74-85): the bucket of key - query offset `rel`; the bias
+// table of the Bolt encoder is built from it at load.
+int64_t relative_bucket(int64_t rel, uint32_t num_buckets, uint32_t max_distance);
 Status bolt_validate(const tsfm_config &c);
 Status bolt_check_tensors(const tsfm_config &c, const TensorTable &t);
 Status bolt_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, BoltDev &w);

@@ -133,7 +133,7 @@ __global__ void ts_feat_kernel(TsStatsCall c, float *feats) {
             if (c.use_asinh && !(known && c.binary[r])) v = asinhf(v);
         }
         float *dst = feats + (r * n + p) * 2 * c.ps;
-        dst[i] = to_tf32(v);
+        dst[i] = c.raw_feats ? v : to_tf32(v);
         dst[c.ps + i] = ob ? 0.0f : 1.0f;
     }
 }

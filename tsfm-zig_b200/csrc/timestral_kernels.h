@@ -26,6 +26,7 @@ struct TsStatsCall {
     uint8_t *binary = nullptr;                  // (rows)
     uint8_t *key_valid = nullptr;               // (rows, n)
     int *first_obs = nullptr;                   // (groups), initialised to INT_MAX
+    int raw_feats = 0;                          // features as computed (else TF32-rounded operands)
 };
 Status launch_ts_stats(const TsStatsCall &c, float *feats, cudaStream_t s);
 
