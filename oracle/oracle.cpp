@@ -69,6 +69,10 @@ int emul_scheme() {
 
 // ---------------------------------------------------------------------------------------------
 // core/nn.zig
+//
+// Zig's @max / @min on floats return the other operand when one is NaN; they are restated as
+// std::fmax / std::fmin (std::max / std::min would propagate a NaN in the first position), and
+// std.math.clamp(v, lo, hi) = @max(lo, @min(v, hi)) as std::fmax(lo, std::fmin(v, hi)).
 
 // A weight matrix [out, in] (host f32) with its transposed copy for the blocked product.
 struct Weight {
@@ -126,7 +130,7 @@ void gemm_nn(float *c, size_t ldc, const float *a, size_t lda, const float *b, s
 
 // expVec (nn.zig:344-359): Cephes expf range reduction + degree-6 polynomial.
 float exp_vec(float x_in) {
-    float x = std::min(std::max(x_in, -87.33654f), 88.72284f);
+    float x = std::fmin(std::fmax(x_in, -87.33654f), 88.72284f);
     float fx = std::round(x * 1.44269504088896341f);
     float r = x - fx * 0.693359375f;
     r = r - fx * -2.12194440e-4f;
@@ -147,7 +151,7 @@ float exp_vec(float x_in) {
 // nn.softmax (nn.zig:470-505): max-subtract, -inf gets exactly 0, normalise by 1/sum.
 void softmax(float *row, size_t n) {
     float mx = -kInf;
-    for (size_t i = 0; i < n; ++i) mx = std::max(mx, row[i]);
+    for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, row[i]);
     float sum = 0.0f;
     for (size_t i = 0; i < n; ++i) {
         const float e = row[i] == -kInf ? 0.0f : exp_vec(row[i] - mx);
@@ -175,7 +179,7 @@ inline float silu_vec(float v) { return v / (1.0f + exp_vec(-v)); }  // siluInPl
 inline float softplus(float x) { return x > 20.0f ? x : std::log1p(std::exp(x)); }  // nn.zig:516
 
 void relu(float *x, size_t n) {
-    for (size_t i = 0; i < n; ++i) x[i] = std::max(x[i], 0.0f);
+    for (size_t i = 0; i < n; ++i) x[i] = std::fmax(x[i], 0.0f);
 }
 void add_in_place(float *dst, const float *src, size_t n) {
     for (size_t i = 0; i < n; ++i) dst[i] += src[i];
@@ -197,8 +201,8 @@ void clamp_nonfinite(float *v, size_t n) {
     for (size_t i = 0; i < n; ++i) {
         const float x = v[i];
         if (std::isfinite(x)) {
-            hi = std::max(hi, x);
-            lo = std::min(lo, x);
+            hi = std::fmax(hi, x);
+            lo = std::fmin(lo, x);
         } else if (std::isinf(x)) {
             any_inf = true;
         }
@@ -997,7 +1001,7 @@ struct Welford {
 Welford welford_combine(Welford a, Welford b) {  // timestral/forecaster.zig:567-577
     const double w = a.w + b.w;
     if (w == 0) return {0, 0, 0};
-    const double w_safe = std::max(w, std::numeric_limits<double>::min());
+    const double w_safe = std::fmax(w, std::numeric_limits<double>::min());
     const double delta = b.mean - a.mean;
     return {w, a.mean + delta * b.w / w_safe, a.m2 + b.m2 + delta * delta * a.w * b.w / w_safe};
 }
@@ -1016,15 +1020,15 @@ void ts_patch_stats(float *loc, float *scale, const float *data, const uint8_t *
                 const double x = data[r * t + i];
                 cum_w += w;
                 cum_x += w * x;
-                const double den = std::max(cum_w, 1.0);
+                const double den = std::fmax(cum_w, 1.0);
                 const double mean = cum_x / den;
                 m2 += (x - prev_mean) * (x - mean) * w;
                 prev_mean = mean;
             }
-            const double den = std::max(cum_w, 1.0);
-            const double variance = m2 / std::max(den - 1.0, 1.0);
+            const double den = std::fmax(cum_w, 1.0);
+            const double variance = m2 / std::fmax(den - 1.0, 1.0);
             loc[r * n + p] = (float)prev_mean;
-            scale[r * n + p] = (float)std::max(std::sqrt(variance), min_scale);
+            scale[r * n + p] = (float)std::fmax(std::sqrt(variance), min_scale);
         }
     }
 }
@@ -1054,14 +1058,14 @@ void ts_block_features(float *loc, float *scale, float *emb_in, const float *ful
                     zero_one = zero_one && (xv == 0.0f || xv == 1.0f);
                     any = true;
                 }
-            kloc = sum / std::max(cnt, 1.0f);
+            kloc = sum / std::fmax(cnt, 1.0f);
             float ss = 0.0f;
             for (size_t i = 0; i < w; ++i)
                 if (full_obs[r * w + i]) {
                     const float dv = full[r * w + i] - kloc;
                     ss += dv * dv;
                 }
-            kscale = std::max(std::sqrt(ss / std::max(cnt, 1.0f)), (float)min_scale);
+            kscale = std::fmax(std::sqrt(ss / std::fmax(cnt, 1.0f)), (float)min_scale);
             binary = zero_one && any;
             if (binary) {
                 kloc = 0.0f;
@@ -1070,7 +1074,7 @@ void ts_block_features(float *loc, float *scale, float *emb_in, const float *ful
         }
         for (size_t p = 0; p < n; ++p) {
             const float lo = known ? kloc : loc[r * n + p];
-            const float sc = std::max(known ? kscale : scale[r * n + p], eps32);
+            const float sc = std::fmax(known ? kscale : scale[r * n + p], eps32);
             float *dst = &emb_in[(r * n + p) * 2 * ps];
             for (size_t i = 0; i < ps; ++i) {
                 const bool o = full_obs[r * w + p * ps + i];
@@ -1452,13 +1456,13 @@ struct Timestral {
                 float acc = 0.0f;
                 for (size_t i = m + 1; i < q; ++i) {
                     acc += wf * widths[i] * softplus(rv[i]);
-                    ov[i] = std::min(std::max(med + acc, -kFloatMax), kFloatMax);
+                    ov[i] = std::fmax(-kFloatMax, std::fmin(med + acc, kFloatMax));  // std.math.clamp
                 }
                 acc = 0.0f;
                 for (size_t i = m; i > 0;) {
                     --i;
                     acc += wf * widths[i] * softplus(rv[i]);
-                    ov[i] = std::min(std::max(med - acc, -kFloatMax), kFloatMax);
+                    ov[i] = std::fmax(-kFloatMax, std::fmin(med - acc, kFloatMax));
                 }
                 ov[m] = med;
                 for (size_t i = 0; i < q; ++i) {
@@ -1498,7 +1502,7 @@ struct Timestral {
                         }
                     Welford pm{cnt, 0, 0};
                     if (cnt > 0) {
-                        pm.mean = sum / std::max(cnt, 1.0);
+                        pm.mean = sum / std::fmax(cnt, 1.0);
                         for (size_t k = 0; k < ps; ++k)
                             if (row_mask[p * ps + k]) {
                                 const double dv = (double)row_ctx[p * ps + k] - pm.mean;
@@ -1509,13 +1513,13 @@ struct Timestral {
                 }
                 const double offset = state.mean;
                 for (size_t j = 0; j < h; ++j) {
-                    const double variance = std::max(state.m2 / std::max(state.w - 1.0, 1.0), 0.0);
-                    const double sc = std::max(std::sqrt(variance), c.minimum_scale);
+                    const double variance = std::fmax(state.m2 / std::fmax(state.w - 1.0, 1.0), 0.0);
+                    const double sc = std::fmax(std::sqrt(variance), c.minimum_scale);
                     loc_j[j] = (float)state.mean;
                     scale_j[j] = (float)sc;
                     double bsum = 0;
                     for (size_t k = 0; k < ps; ++k) {
-                        folded[k] = std::min(std::max(sinh_med[j * ps + k] * sc + state.mean - offset, -clip), clip) + offset;
+                        folded[k] = std::fmax(-clip, std::fmin(sinh_med[j * ps + k] * sc + state.mean - offset, clip)) + offset;
                         bsum += folded[k];
                     }
                     const double bmean = bsum / (double)ps;
@@ -1692,15 +1696,15 @@ struct Timestral {
                     float mx = -kInf, mn = kInf;
                     for (size_t j = 0; j < t; ++j)
                         if (mask[r * t + j]) {
-                            mx = std::max(mx, rows[r * t + j]);
-                            mn = std::min(mn, rows[r * t + j]);
+                            mx = std::fmax(mx, rows[r * t + j]);
+                            mn = std::fmin(mn, rows[r * t + j]);
                         }
                     if (std::isinf(mx)) mx = 0.0f;
                     if (std::isinf(mn)) mn = 0.0f;
                     const float a = scale[n - 1] * o.quantile_real_cap_k;
                     float *dst = &out[(s * v + i) * horizon * q];
                     for (size_t k = 0; k < horizon * q; ++k)
-                        dst[k] = std::min(std::max(dst[k], mn - a), mx + a);
+                        dst[k] = std::fmax(mn - a, std::fmin(dst[k], mx + a));  // std.math.clamp
                 }
         }
         for (float xv : out)
@@ -1866,7 +1870,7 @@ struct Timestral {
                     }
                 if (any && all_nonneg)
                     for (size_t k = 0; k < horizon * q; ++k)
-                        res[r * horizon * q + k] = std::max(res[r * horizon * q + k], 0.0f);
+                        res[r * horizon * q + k] = std::fmax(res[r * horizon * q + k], 0.0f);
             }
         std::memcpy(result, res.data(), res.size() * 4);
     }

@@ -771,12 +771,12 @@ __global__ void ts_head_kernel(TsHeadCall c) {
         float acc = 0.0f;
         for (int i = c.m + 1; i < c.q; ++i) {
             acc += c.wf * c.widths[i] * softplus(rv[i]);
-            ov[i] = fminf(fmaxf(med + acc, -FLT_MAX), FLT_MAX);
+            ov[i] = fmaxf(-FLT_MAX, fminf(med + acc, FLT_MAX));  // std.math.clamp
         }
         acc = 0.0f;
         for (int i = c.m - 1; i >= 0; --i) {
             acc += c.wf * c.widths[i] * softplus(rv[i]);
-            ov[i] = fminf(fmaxf(med - acc, -FLT_MAX), FLT_MAX);
+            ov[i] = fmaxf(-FLT_MAX, fminf(med - acc, FLT_MAX));
         }
         ov[c.m] = med;
         for (int i = 0; i < c.q; ++i) {
@@ -852,13 +852,13 @@ __global__ void ts_refine_kernel(TsRefineCall c) {
         double bsum = 0;
         for (int k = 0; k < c.ps; ++k) {
             const double sm = ((double)block[(j * c.ps + k) * c.q + c.med] - (double)loc0) / (double)scale0;
-            bsum += fmin(fmax(sm * sc + st.mean - offset, -clip), clip) + offset;
+            bsum += fmax(-clip, fmin(sm * sc + st.mean - offset, clip)) + offset;  // std.math.clamp
         }
         const double bmean = bsum / (double)c.ps;
         double bm2 = 0;
         for (int k = 0; k < c.ps; ++k) {
             const double sm = ((double)block[(j * c.ps + k) * c.q + c.med] - (double)loc0) / (double)scale0;
-            const double f = fmin(fmax(sm * sc + st.mean - offset, -clip), clip) + offset;
+            const double f = fmax(-clip, fmin(sm * sc + st.mean - offset, clip)) + offset;
             bm2 += (f - bmean) * (f - bmean);
         }
         st = combine(st, {(double)c.ps, bmean, bm2});
@@ -945,7 +945,7 @@ __global__ void ts_cap_kernel(TsCapCall c) {
         if (isinf(mx)) mx = 0.0f;
         if (isinf(mn)) mn = 0.0f;
         const float a = scale_last * c.cap_k;
-        for (int64_t k = 0; k < c.horizon * c.q; ++k) o[k] = fminf(fmaxf(o[k], mn - a), mx + a);
+        for (int64_t k = 0; k < c.horizon * c.q; ++k) o[k] = fmaxf(mn - a, fminf(o[k], mx + a));  // std.math.clamp
     }
     for (int64_t k = 0; k < c.horizon * c.q; ++k)
         if (isnan(o[k])) atomicOr(c.nan_flag, 1);
