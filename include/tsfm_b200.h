@@ -314,8 +314,8 @@ int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float
  *   used, left-padded to a multiple of patch; loc, scale (b).
  * tsfm_kernel_timestral_block_inputs: predictBlock's window statistics (f64 causal Welford, f32
  *   results), features [asinh((x - loc) / scale), missing] per step (exact FP32), key validity and
- *   first observed patch per group (timestral/model.zig:253-362; INT32_MAX for a group without an
- *   observed patch, which the forward treats as 0) over rows of t context steps, then with
+ *   first observed patch per group (timestral/model.zig:253-362; a value >= n for a group without
+ *   an observed patch, which the forward reads as 0) over rows of t context steps, then with
  *   covariates hl known-future steps (rows of role 2 normalised by their whole-row statistics);
  *   roles: one int8 per row of a group of vall rows (0 target, 1 past, 2 known). loc / scale /
  *   key_valid (rows, n), feats (rows, n, 2 * patch), n = (t + hl) / patch. Allocates a few bytes per
