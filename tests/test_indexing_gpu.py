@@ -27,12 +27,17 @@ def bits(a):
 
 
 def ulps(a, b):
-    """|a - b| in float32 ulps (sign-aware integer distance)."""
+    """|a - b| in float32 ulps (sign-aware integer distance); NaN against NaN counts as equal, NaN
+    against a number as far apart."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
     ia = bits(a).astype(np.int64)
     ib = bits(b).astype(np.int64)
     ia = np.where(ia >= 0x80000000, 0x80000000 - ia, ia)
     ib = np.where(ib >= 0x80000000, 0x80000000 - ib, ib)
-    return np.abs(ia - ib)
+    d = np.abs(ia - ib)
+    na, nb = np.isnan(a), np.isnan(b)
+    return np.where(na & nb, 0, np.where(na | nb, 1 << 31, d))
 
 
 def edge_series(b, t, seed):
@@ -116,7 +121,8 @@ def test_bolt_patch_indexing_bit_exact(t_in, context, use_reg):
 def test_timestral_block_inputs_bit_exact(cov, attend_missing):
     # 5 groups of rows [target, target, past, known] (covariates) or [target, target] (none), t
     # context steps then (with covariates) hl known-future steps; leading gaps, whole missing
-    # patches, an unobserved group, a binary known row.
+    # patches, an unobserved group, a binary known row, and NaN values marked observed (their
+    # statistics follow Zig's NaN-skipping @max).
     rng = np.random.default_rng(11 + int(cov) + 2 * attend_missing)
     ps, groups, t, hl = 32, 5, 256, 64
     roles = np.array([0, 0, 1, 2] if cov else [0, 0], np.int8)
