@@ -234,3 +234,29 @@ def test_target_encoding_bit_exact(max_context, have_target):
                                                   torch.cuda.current_stream().cuda_stream))
         got = out.cpu().numpy()
         assert ((np.isnan(got) & np.isnan(want)) | (got.view(np.uint32) == want.view(np.uint32))).all()
+
+
+def test_variate_attention_after_a_smaller_launch():
+    # In a fresh process, a model whose variate attention needs little shared memory runs first,
+    # then one that needs more (d_model 128, then 256): the kernel's shared-memory limit must rise
+    # for the second launch, not stay at the first one's size.
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = (
+        "import sys; sys.path[:0] = [%r, %r, %r]\n"
+        "import numpy as np, tsfm_b200 as tb\n"
+        "from tsfm_b200 import synthetic as syn\n"
+        "for d, h, f in ((128, 2, 256), (256, 4, 512)):\n"
+        "    cfg = syn.timestral_config(d_model=d, num_heads=h, mlp_hidden_dim=f, num_layers=2, patch=16,\n"
+        "                               context_length=512, block_size=8)\n"
+        "    m = tb.Model(cfg, syn.random_checkpoint(cfg, seed=3))\n"
+        "    x = syn.seeded_series(12, 260, seed=8).reshape(4, 3, 260)\n"
+        "    o = np.isfinite(x)\n"
+        "    out = m.forecast_timestral(np.where(o, x, 0).astype(np.float32), 40, observed=o.astype(np.uint8))\n"
+        "    assert np.isfinite(out).all()\n"
+        "print('ok')\n"
+    ) % (os.path.dirname(here), os.path.join(os.path.dirname(here), "tsfm-zig_b200"), here)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]

@@ -183,8 +183,9 @@ Status build_corrected_weight(const float *w, int64_t rows, int64_t cols, void *
 Status launch_split_x8(const float *x, int64_t rows, int64_t cols, int64_t ldx, void *x16, int64_t ld16, void *x8,
                        int64_t ld8, cudaStream_t s);
 
-// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel): the attribute
-// stays set in the context, and setting it on every launch costs host time.
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) per (device, kernel) only when `bytes` exceeds
+// what was set before: the attribute stays set in the context (a ceiling for every later launch),
+// and setting it on every launch costs host time.
 Status ensure_smem_attr(const void *func, int bytes);
 
 // 3-D tensor map over `groups` blocks of `rows` rows (each `width` elements, row stride `ld`,

@@ -844,19 +844,29 @@ int sm_count() {
 }  // namespace
 
 Status ensure_smem_attr(const void *func, int bytes) {
+    // The attribute is a ceiling on the dynamic shared memory of every later launch of `func`, so
+    // it only ever rises: a launch with more bytes than an earlier one raises it, one with fewer
+    // leaves it.
     int dev = 0;
     cudaGetDevice(&dev);
+    struct Entry {
+        int dev;
+        const void *func;
+        int bytes;
+    };
     static std::mutex mu;
-    static std::vector<std::pair<int, const void *>> done;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        for (const auto &d : done)
-            if (d.first == dev && d.second == func) return Status::ok();
-    }
+    static std::vector<Entry> done;
+    std::lock_guard<std::mutex> lk(mu);
+    Entry *hit = nullptr;
+    for (auto &d : done)
+        if (d.dev == dev && d.func == func) hit = &d;
+    if (hit && hit->bytes >= bytes) return Status::ok();
     const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return Status::cuda(e, "set dynamic shared memory");
-    std::lock_guard<std::mutex> lk(mu);
-    done.push_back({dev, func});
+    if (hit)
+        hit->bytes = bytes;
+    else
+        done.push_back({dev, func, bytes});
     return Status::ok();
 }
 

@@ -167,7 +167,9 @@ def tensor_shapes(cfg):
 
 
 def random_checkpoint(cfg, seed=20261201, std=0.02, norm_jitter=0.0, dtype=np.float32):
-    """Name -> array of a random-init checkpoint for `cfg` (generated in sorted-name order)."""
+    """Name -> array of a random-init checkpoint for `cfg` (generated in sorted-name order).
+    dtype: np.float32, np.float16, or "bf16" (raw bfloat16 bits as uint16, round to nearest even),
+    the safetensors storage types the reference loads (core/safetensors.zig:81-92)."""
     shapes, norms = tensor_shapes(cfg)
     rng = np.random.default_rng(seed)
     out = {}
@@ -179,7 +181,10 @@ def random_checkpoint(cfg, seed=20261201, std=0.02, norm_jitter=0.0, dtype=np.fl
                 a += rng.standard_normal(shp, dtype=np.float32) * np.float32(norm_jitter)
         else:
             a = rng.standard_normal(shp, dtype=np.float32) * np.float32(std)
-        out[name] = a.astype(dtype) if dtype != np.float32 else a
+        if isinstance(dtype, str) and dtype == "bf16":
+            out[name] = to_bf16_bits(a)
+        else:
+            out[name] = a.astype(dtype) if dtype != np.float32 else a
     return out
 
 
