@@ -118,3 +118,21 @@ def test_bolt_small_shape_matches_oracle():
     want = ora.forecast_bolt(x, 192)
     assert np.isfinite(got).all()
     assert rel_err(got, want, x) <= TOL
+
+
+@pytest.mark.parametrize("dtype", [np.float32, "bf16"])
+def test_bolt_base_shape_matches_oracle(dtype):
+    # BASELINE configs[1] shape: Bolt-base (768-d, 12 layers, 12 heads, d_ff 3072, ctx 2048,
+    # 9 quantiles, P = 64) at horizon 256 = 4 passes, every quantile path fed back
+    # (chronos_bolt/forecaster.zig:45-78), from an F32 and from a BF16 checkpoint (converted on
+    # the device like the reference converts at load, core/safetensors.zig:81-92).
+    cfg = syn.bolt_config(d_model=768, d_ff=3072, num_heads=12, num_layers=12)
+    w = syn.random_checkpoint(cfg, seed=20261201, dtype=dtype)
+    gpu = tb.Model(cfg, w)
+    ora = ob.OracleModel(gpu.parsed, w, tb.tensor_table)
+    x = syn.seeded_series(3, 2048, seed=2000)
+    got = gpu.forecast_bolt(x, 256)
+    want = ora.forecast_bolt(x, 256)
+    assert got.shape == (3, 256, 9)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want, x) <= TOL
