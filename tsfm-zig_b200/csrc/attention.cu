@@ -31,6 +31,8 @@ struct AttnP {
     int64_t ld;
     uint16_t *o;
     int64_t ldo;
+    float *o32;  // FP32 output instead of o when set
+    int64_t ldo32;
     const uint8_t *key_valid;
     int64_t kvs;
     const float *rel;
@@ -232,6 +234,17 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
     }
     const float inv0 = l_run[0] > 0.0f ? 1.0f / l_run[0] : 0.0f;
     const float inv1 = l_run[1] > 0.0f ? 1.0f / l_run[1] : 0.0f;
+    if (p.o32 != nullptr) {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            const int col = h * HD + nt * 8 + (lane & 3) * 2;
+            if (qi0 < n)
+                *reinterpret_cast<float2 *>(p.o32 + (row0 + qi0) * p.ldo32 + col) = make_float2(o[nt][0] * inv0, o[nt][1] * inv0);
+            if (qi1 < n)
+                *reinterpret_cast<float2 *>(p.o32 + (row0 + qi1) * p.ldo32 + col) = make_float2(o[nt][2] * inv1, o[nt][3] * inv1);
+        }
+        return;
+    }
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
         const int col = h * HD + nt * 8 + (lane & 3) * 2;
@@ -246,7 +259,10 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnP p) {
 
 Status launch_attention(const AttentionCall &c, cudaStream_t stream) {
     if (c.groups <= 0 || c.heads <= 0 || c.n <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: empty");
-    if (c.force_path == 1 || (c.force_path == 0 && attention_tc_supported(c))) return launch_attention_tc(c, stream);
+    if (c.o32 == nullptr && (c.force_path == 1 || (c.force_path == 0 && attention_tc_supported(c))))
+        return launch_attention_tc(c, stream);
+    if (c.o32 && (c.ld_o32 % 2 || (reinterpret_cast<uintptr_t>(c.o32) & 7)))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: FP32 output needs 8-byte alignment");
     if (c.o8) return Status::fail(TSFM_ERR_UNSUPPORTED, "attention: FP8 companion output on the tcgen05 path only");
     if ((c.ld_qkv % 8) || (c.ld_o % 2) || (reinterpret_cast<uintptr_t>(c.q) & 15) ||
         (reinterpret_cast<uintptr_t>(c.k) & 15) || (reinterpret_cast<uintptr_t>(c.v) & 15))
@@ -260,6 +276,8 @@ Status launch_attention(const AttentionCall &c, cudaStream_t stream) {
     p.ld = c.ld_qkv;
     p.o = static_cast<uint16_t *>(c.o);
     p.ldo = c.ld_o;
+    p.o32 = c.o32;
+    p.ldo32 = c.ld_o32;
     p.key_valid = c.key_valid;
     p.kvs = c.kv_stride > 0 ? c.kv_stride : c.n;
     p.rel = c.rel_bias;

@@ -267,8 +267,8 @@ int32_t tsfm_model_create(const tsfm_config *config, const tsfm_tensor *tensors,
         if (compute != TSFM_COMPUTE_BF16 && compute != TSFM_COMPUTE_F16 && compute != TSFM_COMPUTE_F16C)
             return Status::fail(TSFM_ERR_UNSUPPORTED,
                                 "compute type: TSFM_COMPUTE_BF16, TSFM_COMPUTE_F16 and TSFM_COMPUTE_F16C are implemented");
-        if (compute == TSFM_COMPUTE_F16C && config->family != TSFM_CHRONOS2)
-            return Status::fail(TSFM_ERR_UNSUPPORTED, "TSFM_COMPUTE_F16C: Chronos-2 only in this build");
+        if (compute == TSFM_COMPUTE_F16C && config->family == TSFM_CHRONOS_BOLT)
+            return Status::fail(TSFM_ERR_UNSUPPORTED, "TSFM_COMPUTE_F16C: Chronos-2 and Timestral only in this build");
         // act: the weights' upload type (E_F16C: FP16 operands with FP8 correction companions).
         const int act = compute == TSFM_COMPUTE_F16C ? E_F16C : compute == TSFM_COMPUTE_F16 ? E_F16 : E_BF16;
         std::unique_ptr<tsfm_model> m(new tsfm_model());

@@ -72,6 +72,7 @@ struct TsDev {
     std::vector<Layer> layers;
     int64_t max_qkv_cols = 0;
     int act = E_F16;
+    bool corr = false;  // corrected products (TSFM_COMPUTE_F16C), as C2Dev::corr
     // Per-forecast roles of one series' rows (0 target, 1 past covariate, 2 known covariate).
     const int8_t *roles = nullptr;
 };

@@ -100,6 +100,9 @@ size_t block_workspace(const tsfm_config &c, const TsDev &w, const Block &k) {
     b += Arena::span(nt * k.h * 8) + Arena::span(nt * 8);
     b += Arena::span(nt * k.h * d * 4) * 2 + Arena::span(nt * k.h * 4 * d * 4) * 2 + Arena::span(nt * hl * q * 4) * 2;
     if (ts_fused_norm(c, w.act)) b += Arena::span(rows * 4) + Arena::span(rows * (d / 256) * 4);
+    if (w.corr)  // FP8 companions of xn, the attention output (and its FP32 form), a and the patch hidden
+        b += Arena::span(rows * 2 * d) * 2 + Arena::span(rows * d * 4) + Arena::span(rows * 2 * hid) +
+             Arena::span(R * n * 2 * 4 * d);
     return b;
 }
 
@@ -136,6 +139,13 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
     const int np = (int)(d / 256);
     float *nS = fused ? ws.take<float>(rows) : nullptr;       // row factors of the MLP norm
     float *nP = fused ? ws.take<float>(rows * np) : nullptr;  // row sums of squares per column tile
+    // Corrected products: FP8 companions of the GEMM inputs, and the attention output in FP32 (its
+    // FP16 value and companion are formed after the output gate).
+    uint8_t *xn8 = w.corr ? ws.take<uint8_t>(rows * 2 * d) : nullptr;
+    uint8_t *o8 = w.corr ? ws.take<uint8_t>(rows * 2 * d) : nullptr;
+    float *o32 = w.corr ? ws.take<float>(rows * d) : nullptr;
+    uint8_t *a8 = w.corr ? ws.take<uint8_t>(rows * 2 * hid) : nullptr;
+    uint8_t *h8 = w.corr ? ws.take<uint8_t>(R * n * 2 * 4 * d) : nullptr;
     if (ws.used > ws.buf.bytes) return Status::fail(TSFM_ERR_OUT_OF_MEMORY, "Timestral: workspace too small");
 
     // 1. statistics, features, key validity, first observed patch.
@@ -170,11 +180,16 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
     // 2. patch embedding into the encoder rows; forecast queries into the decoder rows.
     {
         const int64_t m = R * n;
-        TSFM_TRY(op_linear(r, s, w.patch_proj.hidden, feats, m, 2 * ps, h16, 4 * d, A16, 2));
+        LinearCall hx;
+        hx.y8 = h8;
+        hx.ldy8 = 8 * d;
+        TSFM_TRY(op_linear(r, s, w.patch_proj.hidden, feats, m, 2 * ps, h16, 4 * d, A16, 2, &hx));
         LinearCall remap;
         remap.rm_g = n;
         remap.rm_G = sl;
         TSFM_TRY(op_linear(r, s, w.patch_proj.residual, feats, m, 2 * ps, x, d, OUT_F32, 0, &remap));
+        remap.x8 = h8;
+        remap.ldx8 = 8 * d;
         TSFM_TRY(op_linear(r, s, w.patch_proj.output, h16, m, 4 * d, x, d, OUT_F32_ACC, 0, &remap));
         LaunchScope ls(r, s, K_OTHER, (double)R * k.h * d * 8);
         TSFM_TRY(launch_broadcast_rows(x, R, sl, ne, w.fq_rep, k.h, d, s));
@@ -197,8 +212,10 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
             const TsDev::Attn &a = L.attns[ai];
             const int64_t cols = a.qkvg.out;
             const bool pre = fused && li > 0 && ai == 0;  // xn holds the previous w3's fused norm input
-            if (!pre) TSFM_TRY(op_rmsnorm(r, s, x, a.norm, xn, A16, rows, d, eps));
+            if (!pre) TSFM_TRY(op_rmsnorm(r, s, x, a.norm, xn, A16, rows, d, eps, 0, 0, 0, nullptr, xn8));
             LinearCall rope;
+            rope.x8 = xn8;
+            rope.ldx8 = 2 * d;
             if (pre) {
                 rope.norm_in = nP;
                 rope.norm_parts = np;
@@ -213,7 +230,7 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
                 rope.rope_p1 = sl * k.vall;
                 rope.rope_p2 = sl;
             }
-            TSFM_TRY(op_linear(r, s, a.qkvg, xn, rows, d, qkvg, cols, A16, 0, (a.is_time || pre) ? &rope : nullptr));
+            TSFM_TRY(op_linear(r, s, a.qkvg, xn, rows, d, qkvg, cols, A16, 0, &rope));
             if (a.is_time) {
                 AttentionCall ac;
                 ac.err = static_cast<int *>(r.err.p);
@@ -234,6 +251,8 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
                 ac.ne = (int)ne;
                 ac.l = (int)l;
                 ac.group_bidir = bidir;
+                ac.o32 = o32;  // corrected products: FP32 output, gated below
+                ac.ld_o32 = d;
                 LaunchScope ls(r, s, K_ATTN, 2.0 * (double)R * nh * sl * sl * 64);
                 TSFM_TRY(launch_attention(ac, s));
             } else {
@@ -253,35 +272,53 @@ Status predict_block(Replica &r, const tsfm_config &c, const TsDev &w, const Blo
                 vc.roles = w.roles;
                 vc.cov = k.cov;
                 vc.scale = 1.0f / std::sqrt((float)hd_of(c));
-                if (a.gate) {  // applied as the output is written
+                if (w.corr) {  // FP32 output, gated below
+                    vc.o32 = o32;
+                    vc.ld_o32 = d;
+                } else if (a.gate) {  // applied as the output is written
                     vc.gate = qkvg + 3 * d;
                     vc.ldg = cols;
                 }
                 LaunchScope ls(r, s, K_ATTN, 4.0 * (double)k.groups * sl * nh * k.vall * k.vall * 64);
                 TSFM_TRY(launch_ts_variate(vc, s));
             }
-            if (a.gate && a.is_time) {
+            if (w.corr) {
+                LaunchScope ls(r, s, K_OTHER, (double)rows * d * 10);
+                TSFM_TRY(launch_ts_gate_x8(o32, d, a.gate ? qkvg + 3 * d : nullptr, cols, rows, d, o16, d, o8, 2 * d, s));
+            } else if (a.gate && a.is_time) {
                 LaunchScope ls(r, s, K_OTHER, (double)rows * d * 6);
                 TSFM_TRY(launch_ts_gate(o16, d, qkvg + 3 * d, cols, rows, d, w.act, s));
             }
-            TSFM_TRY(op_linear(r, s, a.o, o16, rows, d, x, d, OUT_F32_ACC, 0));
+            LinearCall oc;
+            oc.x8 = o8;
+            oc.ldx8 = 2 * d;
+            TSFM_TRY(op_linear(r, s, a.o, o16, rows, d, x, d, OUT_F32_ACC, 0, &oc));
         }
         const bool next = fused && li + 1 < w.layers.size();
-        TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps, 0, 0, 0, next ? nS : nullptr));
+        TSFM_TRY(op_rmsnorm(r, s, x, L.mlp_norm, xn, A16, rows, d, eps, 0, 0, 0, next ? nS : nullptr, xn8));
         if (L.glu) {
-            TSFM_TRY(op_linear(r, s, L.w12, xn, rows, d, a16, hid, A16, ACT_GLU));
+            LinearCall gc;
+            gc.x8 = xn8;
+            gc.ldx8 = 2 * d;
+            gc.y8 = a8;
+            gc.ldy8 = 2 * hid;
+            TSFM_TRY(op_linear(r, s, L.w12, xn, rows, d, a16, hid, A16, ACT_GLU, &gc));
         } else {
             TSFM_TRY(op_linear(r, s, L.w12, xn, rows, d, h16, 2 * hid, A16, 0));
             LaunchScope ls(r, s, K_OTHER, (double)rows * hid * 6);
             TSFM_TRY(launch_ts_swiglu(h16, a16, rows, hid, w.act, s));
         }
         LinearCall wc;
+        wc.x8 = a8;
+        wc.ldx8 = 2 * hid;
         if (next) {
             wc.norm_out = nP;
             wc.norm_x16 = xn;
             wc.ld_x16 = d;
             wc.norm_gamma = w.layers[li + 1].attns[0].norm;
             wc.norm_s_in = nS;
+            wc.norm_x8 = xn8;
+            wc.ld_nx8 = 2 * d;
         }
         TSFM_TRY(op_linear(r, s, L.w3, a16, rows, hid, x, d, OUT_F32_ACC, 0, &wc));
     }
@@ -382,7 +419,9 @@ Status ts_check_tensors(const tsfm_config &c, const TensorTable &t) {
 
 Status ts_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, TsDev &w) {
     const int64_t d = c.d_model, ps = c.patch_size, hid = c.d_ff, q = c.num_quantiles, nh = c.num_heads, hd = hd_of(c);
-    w.act = act;
+    // act: the 16-bit weights' upload type; E_F16C = FP16 weights with FP8 correction companions.
+    w.corr = act == E_F16C;
+    w.act = w.corr ? E_F16 : act;
     TSFM_TRY(load_resblock(r, t, "representation.patch_proj", 2 * ps, 4 * d, d, true, E_F32, act, w.patch_proj));
     std::vector<float> v;
     TSFM_TRY(t.get("representation.forecast_query", d, v));
@@ -443,6 +482,8 @@ Status ts_load(Replica &r, const tsfm_config &c, const TensorTable &t, int act, 
             TSFM_TRY(upload_lin_raw(r, {t12}, &map, 2 * hid, d, act, L.w12));
             L.glu = true;
         } else {
+            if (w.corr)
+                return Status::fail(TSFM_ERR_UNSUPPORTED, "TSFM_COMPUTE_F16C: Timestral needs mlp_hidden_dim % 128 == 0");
             TSFM_TRY(upload_lin_raw(r, {t12}, nullptr, 2 * hid, d, act, L.w12));
         }
         TSFM_TRY(upload_lin_raw(r, {t3}, nullptr, d, hid, act, L.w3));

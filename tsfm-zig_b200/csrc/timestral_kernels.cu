@@ -401,6 +401,36 @@ __global__ void ts_gate_vec_kernel(uint16_t *o, int64_t ldo, const uint16_t *g, 
         }
 }
 
+// v = o32 * sigmoid(g) (or o32) in FP32, then its FP16 value and FP8 companion; 8 columns per
+// thread (two float4 loads, one 16-byte FP16 store, 8-byte stores of each companion part).
+__global__ void ts_gate_x8_kernel(const float *o32, int64_t ld32, const uint16_t *g, int64_t ldg, int64_t rows, int d,
+                                  __half *o16, int64_t ldo, uint8_t *o8, int64_t ld8) {
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
+        for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {
+            const float4 a = *reinterpret_cast<const float4 *>(o32 + r * ld32 + c);
+            const float4 b = *reinterpret_cast<const float4 *>(o32 + r * ld32 + c + 4);
+            float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            if (g != nullptr) {
+                float gv[8];
+                unpack8<true>(*reinterpret_cast<const uint4 *>(g + r * ldg + c), gv);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) x[i] = x[i] / (1.0f + expf(-gv[i]));
+            }
+            uint32_t hw[4], hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                const __half2 h2 = __floats2half2_rn(x[i], x[i + 1]);
+                hw[i / 2] = *reinterpret_cast<const uint32_t *>(&h2);
+                const float2 f = __half22float2(h2);
+                hi[i / 4] |= e4m3x2(f.x * kX8HiScale, f.y * kX8HiScale) << (16 * ((i / 2) & 1));
+                lo[i / 4] |= e4m3x2((x[i] - f.x) * kX8LoScale, (x[i + 1] - f.y) * kX8LoScale) << (16 * ((i / 2) & 1));
+            }
+            *reinterpret_cast<uint4 *>(o16 + r * ldo + c) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint2 *>(o8 + r * ld8 + c) = make_uint2(hi[0], hi[1]);
+            *reinterpret_cast<uint2 *>(o8 + r * ld8 + d + c) = make_uint2(lo[0], lo[1]);
+        }
+}
+
 template <bool F16>
 __global__ void ts_swiglu_vec_kernel(const uint16_t *h, uint16_t *a, int64_t rows, int hid) {
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
@@ -698,6 +728,19 @@ __global__ void __launch_bounds__(256, 2) ts_variate_mma_kernel(TsVariateCall c,
             mma16816<F16>(o[2 * dp + 1], pa, b2, b3);
         }
         const float inv0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, inv1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
+        if (c.o32 != nullptr) {  // FP32 rows straight from the accumulators (no gate, no staging)
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                const int col = (int)hc0 + h * 64 + nt * 8 + (lane & 3) * 2;
+                if (i0 < V)
+                    *reinterpret_cast<float2 *>(c.o32 + ((r0 + i0) * c.sl + tok) * c.ld_o32 + col) =
+                        make_float2(o[nt][0] * inv0, o[nt][1] * inv0);
+                if (i1 < V)
+                    *reinterpret_cast<float2 *>(c.o32 + ((r0 + i1) * c.sl + tok) * c.ld_o32 + col) =
+                        make_float2(o[nt][2] * inv1, o[nt][3] * inv1);
+            }
+            continue;
+        }
         // Only this warp reads head h's q columns: its output rows replace them.
         __syncwarp();
 #pragma unroll
@@ -707,6 +750,7 @@ __global__ void __launch_bounds__(256, 2) ts_variate_mma_kernel(TsVariateCall c,
             if (i1 < V) *reinterpret_cast<uint32_t *>(qs + i1 * rs + col) = pack16<F16>(o[nt][2] * inv1, o[nt][3] * inv1);
         }
     }
+    if (c.o32 != nullptr) return;  // every thread: the FP32 rows are written
     __syncthreads();
     uint16_t *dst = static_cast<uint16_t *>(c.o);
     auto store = [&](int idx, bool pre, uint4 gp) {
@@ -1038,6 +1082,19 @@ Status launch_ts_gate(void *o, int64_t ldo, const void *g, int64_t ldg, int64_t 
     return Status::ok();
 }
 
+Status launch_ts_gate_x8(const float *o32, int64_t ld32, const void *g, int64_t ldg, int64_t rows, int64_t d, void *o16,
+                         int64_t ldo, void *o8, int64_t ld8, cudaStream_t s) {
+    if (rows <= 0) return Status::ok();
+    if (!aligned16(o32) || !aligned16(o16) || !aligned16(o8) || (g && (!aligned16(g) || ldg % 8)) || d % 8 ||
+        ld32 % 4 || ldo % 8 || ld8 % 16 || ld8 < 2 * d || d > INT_MAX)
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "timestral gate (corrected): alignment");
+    const int grid = (int)std::min<int64_t>(rows, (int64_t)num_sms() * 16);
+    ts_gate_x8_kernel<<<grid, 128, 0, s>>>(o32, ld32, static_cast<const uint16_t *>(g), ldg, rows, (int)d,
+                                           static_cast<__half *>(o16), ldo, static_cast<uint8_t *>(o8), ld8);
+    TSFM_CUDA(cudaGetLastError(), "timestral gate (corrected): launch");
+    return Status::ok();
+}
+
 Status launch_ts_swiglu(const void *h, void *a, int64_t rows, int64_t hid, int dtype, cudaStream_t s) {
     if (aligned16(h) && aligned16(a) && hid % 8 == 0 && hid <= INT_MAX / 2 && rows > 0) {
         const int grid = (int)std::min<int64_t>(rows, (int64_t)num_sms() * 16);
@@ -1080,6 +1137,7 @@ bool variate_vec(const TsVariateCall &c, cudaStream_t s) {  // true: gate applie
             return true;
         }
     }
+    if (c.o32 != nullptr) return false;  // FP32 output: tensor-core path only (the caller reports it)
     const int64_t threads = c.groups * c.sl * c.heads * 16;
     const unsigned grid = (unsigned)((threads + 255) / 256);
     if (c.dtype == E_F16)
@@ -1091,6 +1149,8 @@ bool variate_vec(const TsVariateCall &c, cudaStream_t s) {  // true: gate applie
 
 Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s) {
     if (c.vall > kMaxRows) return Status::fail(TSFM_ERR_UNSUPPORTED, "Timestral: more than 16 rows per series");
+    if (c.o32 && (c.gate || c.ld_o32 % 2 || (reinterpret_cast<uintptr_t>(c.o32) & 7)))
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "timestral variate attention: FP32 output is ungated, 8-byte aligned");
     // 8-byte accesses per lane: row strides, the k / v offset and the base even in 4-element units.
     if ((c.ld % 4) == 0 && (c.d % 4) == 0 && (c.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(c.qkv) & 7) == 0 &&
         (reinterpret_cast<uintptr_t>(c.o) & 7) == 0 && c.groups * c.sl * c.heads * 16 < (int64_t)UINT_MAX * 256 / 2) {
@@ -1114,10 +1174,13 @@ Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s) {
         default: gated = variate_vec<16>(c, s); break;
         }
         TSFM_CUDA(cudaGetLastError(), "timestral variate attention: launch");
+        if (c.o32 && !gated)
+            return Status::fail(TSFM_ERR_UNSUPPORTED, "timestral variate attention: FP32 output needs the tensor-core path");
         if (c.gate && !gated)
             return launch_ts_gate(c.o, c.ldo, c.gate, c.ldg, c.groups * c.vall * c.sl, c.d, c.dtype, s);
         return Status::ok();
     }
+    if (c.o32) return Status::fail(TSFM_ERR_UNSUPPORTED, "timestral variate attention: FP32 output needs the tensor-core path");
     const int64_t warps = c.groups * c.sl * c.heads;
     ts_variate_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(c);
     TSFM_CUDA(cudaGetLastError(), "timestral variate attention: launch");

@@ -69,6 +69,11 @@ Status launch_ts_cat_encode(const double *codes, int64_t b, int64_t ncat, int64_
 Status launch_ts_rows(const int8_t *roles, int64_t rows, int vall, int v, int64_t sl, int64_t ne, int h, bool cov,
                       uint8_t *bidir, int64_t *head_rows, int64_t *target_row, cudaStream_t s);
 Status launch_ts_gate(void *o, int64_t ldo, const void *g, int64_t ldg, int64_t rows, int64_t d, int dtype, cudaStream_t s);
+// o16 = f16(v) and its FP8 companion (kernels.h layout) from v = o32 * sigmoid(g) (nn.mulSigmoid,
+// in FP32), or v = o32 when g is null: the input of a corrected output projection. d % 8 == 0,
+// 16-byte aligned rows.
+Status launch_ts_gate_x8(const float *o32, int64_t ld32, const void *g, int64_t ldg, int64_t rows, int64_t d, void *o16,
+                         int64_t ldo, void *o8, int64_t ld8, cudaStream_t s);
 Status launch_ts_swiglu(const void *h, void *a, int64_t rows, int64_t hid, int dtype, cudaStream_t s);
 
 struct TsVariateCall {
@@ -86,6 +91,10 @@ struct TsVariateCall {
     // Optional output gate (nn.mulSigmoid): o *= sigmoid(gate[row, :]), gate rows at stride ldg.
     const void *gate = nullptr;
     int64_t ldg = 0;
+    // FP32 output instead of o, ungated (row stride ld_o32; the tensor-core path only): for a
+    // corrected product, whose FP16 input and FP8 companion launch_ts_gate_x8 then forms.
+    float *o32 = nullptr;
+    int64_t ld_o32 = 0;
 };
 // With c.gate set the output comes back gated.
 Status launch_ts_variate(const TsVariateCall &c, cudaStream_t s);
