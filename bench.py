@@ -73,7 +73,7 @@ def parse_args():
     ap.add_argument("--csv-series", type=int, default=8192, help="series of the csv workload")
     ap.add_argument("--workload", default="chronos2",
                     choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv", "parse",
-                             "attention"],
+                             "attention", "gemm"],
                     help="chronos2 is the headline; bolt-*/timestral are BASELINE.json's other configs, timed "
                          "through the host entry points (copies included); sweep is its Chronos-2 throughput sweep "
                          "(batch x context, one JSON line per point); csv renders the CLI's CSV output of an "
@@ -600,6 +600,67 @@ def run_attention(a):
         del qkv, o
 
 
+def run_gemm(a):
+    """The encoder's linear layers alone at the Chronos-2 headline shape (M = 256 x 577 = 147,712
+    rows): qkv (2304 x 768, FP16 out), o and the folded group projection (768 x 768, FP32
+    accumulate), wi (3072 x 768, ReLU, FP16 out), wo (768 x 3072, FP32 accumulate), each with plain
+    FP16 operands (tsfm_kernel_linear) and as the corrected product (tsfm_kernel_linear_f16c with the
+    FP8 companions, FP16 outputs with their companion as the forward writes them). CUDA events per
+    launch, L2 flushed between launches; TFLOP/s = 2 M N K / time (the algorithmic work; the
+    corrected product executes twice the tensor-core work)."""
+    import ctypes
+    import torch
+    import tsfm_b200 as tb
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    burst = peaks()[0]
+    M = 256 * 577
+    g = torch.Generator(device="cuda").manual_seed(3)
+    shapes = (("qkv", 2304, 768, 0, 0), ("o", 768, 768, 2, 0), ("wi", 3072, 768, 0, 1), ("wo", 768, 3072, 2, 0))
+    for name, N, K, out_mode, act in shapes:
+        x = torch.randn(M, K, device="cuda", generator=g)
+        w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+        x16, w16 = x.half(), w.half()
+        xc16 = torch.empty(M, K, device="cuda", dtype=torch.float16)
+        x8 = torch.empty(M, 2 * K, device="cuda", dtype=torch.uint8)
+        wc16 = torch.empty(N, K, device="cuda", dtype=torch.float16)
+        w8 = torch.empty(N, 2 * K, device="cuda", dtype=torch.uint8)
+        scale = ctypes.c_float(0.0)
+        tb.check(tb.lib.tsfm_kernel_split_f16c(x.data_ptr(), M, K, xc16.data_ptr(), x8.data_ptr(), sp))
+        tb.check(tb.lib.tsfm_kernel_weight_f16c(w.data_ptr(), N, K, wc16.data_ptr(), w8.data_ptr(), ctypes.byref(scale),
+                                                sp))
+        del x, w
+        y = torch.zeros(M, N, device="cuda", dtype=torch.float16 if out_mode == 0 else torch.float32)
+        y8 = torch.empty(M, 2 * N, device="cuda", dtype=torch.uint8) if out_mode == 0 else None
+        runs = {
+            "f16": lambda: tb.check(tb.lib.tsfm_kernel_linear(x16.data_ptr(), 1, w16.data_ptr(), 1, None, y.data_ptr(),
+                                                              out_mode, act, M, N, K, K, K, N, sp)),
+            "f16c": lambda: tb.check(tb.lib.tsfm_kernel_linear_f16c(
+                xc16.data_ptr(), x8.data_ptr(), wc16.data_ptr(), w8.data_ptr(), scale.value, None, y.data_ptr(),
+                None if y8 is None else y8.data_ptr(), out_mode, act, M, N, K, 2, sp)),
+        }
+        for mode, run in runs.items():
+            for _ in range(max(3, a.warmup)):
+                run()
+            torch.cuda.synchronize()
+            total, steps = 0.0, max(3, a.steps)
+            for _ in range(steps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                run()
+                e1.record(stream)
+                e1.synchronize()
+                total += e0.elapsed_time(e1)
+            ms = total / steps
+            tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+            print(json.dumps({"workload": "gemm", "shape": name, "mode": mode, "M": M, "N": N, "K": K, "ms": ms,
+                              "tflops": tf, "tensor_tflops_executed": tf * (2 if mode == "f16c" else 1),
+                              "frac_of_burst": tf / burst}), flush=True)
+        del x16, w16, xc16, x8, wc16, w8, y, y8
+
+
 def measure(model, a, x, world, barrier, clk=None):
     """One operand mode of the headline workload: device-resident series/s (CUDA events on the
     launching stream, L2 flushed between steps, max over ranks), end-to-end series/s through the
@@ -717,7 +778,7 @@ def main():
         return run_reference(a, rank)
     if a.workload != "chronos2":
         if rank == 0:
-            {"sweep": run_sweep, "csv": run_csv, "parse": run_parse, "attention": run_attention}.get(
+            {"sweep": run_sweep, "csv": run_csv, "parse": run_parse, "attention": run_attention, "gemm": run_gemm}.get(
                 a.workload, run_family_workload)(a)
         return
 

@@ -299,6 +299,20 @@ int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float
                                      void *y8, int32_t out_mode, int32_t act, int64_t M, int64_t N,
                                      int64_t K, int32_t terms, void *stream);
 
+/* The corrected product's pieces on device pointers, for benches and tests that time the product
+ * alone: tsfm_kernel_split_f16c writes x16 = f16(x) [rows, cols] and its FP8 companion x8
+ * [rows, 2 cols]; tsfm_kernel_weight_f16c writes w16 = f16(w) * 2^s and w8 [rows, 2 cols] and
+ * returns *acc_scale = 2^-s (it waits for `stream`); tsfm_kernel_linear_f16c runs
+ * tsfm_kernel_linear_corrected's product on such operands (dense rows). */
+int32_t tsfm_kernel_split_f16c(const float *x, int64_t rows, int64_t cols, void *x16, void *x8,
+                               void *stream);
+int32_t tsfm_kernel_weight_f16c(const float *w, int64_t rows, int64_t cols, void *w16, void *w8,
+                                float *acc_scale, void *stream);
+int32_t tsfm_kernel_linear_f16c(const void *x16, const void *x8, const void *w16, const void *w8,
+                                float acc_scale, const float *bias, void *y, void *y8,
+                                int32_t out_mode, int32_t act, int64_t M, int64_t N, int64_t K,
+                                int32_t terms, void *stream);
+
 /* The indexing work of the forecasters, exposed for bit-exact parity tests. All return after
  * enqueueing on `stream`; pointers are device pointers.
  *

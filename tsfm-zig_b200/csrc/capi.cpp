@@ -628,6 +628,59 @@ int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float
     });
 }
 
+int32_t tsfm_kernel_split_f16c(const float *x, int64_t rows, int64_t cols, void *x16, void *x8, void *stream) {
+    return guarded([&]() -> Status {
+        if (!x || !x16 || !x8 || rows <= 0 || cols <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "split: bad arguments");
+        return launch_split_x8(x, rows, cols, cols, x16, cols, x8, 2 * cols, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t tsfm_kernel_weight_f16c(const float *w, int64_t rows, int64_t cols, void *w16, void *w8, float *acc_scale,
+                                void *stream) {
+    return guarded([&]() -> Status {
+        if (!w || !w16 || !w8 || !acc_scale || rows <= 0 || cols <= 0 || cols % 8)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "weight split: bad arguments");
+        int sh = 0;
+        TSFM_TRY(build_corrected_weight(w, rows, cols, w16, w8, &sh, static_cast<cudaStream_t>(stream)));
+        *acc_scale = std::ldexp(1.0f, -sh);
+        return Status::ok();
+    });
+}
+
+int32_t tsfm_kernel_linear_f16c(const void *x16, const void *x8, const void *w16, const void *w8, float acc_scale,
+                                const float *bias, void *y, void *y8, int32_t out_mode, int32_t act, int64_t M,
+                                int64_t N, int64_t K, int32_t terms, void *stream) {
+    return guarded([&]() -> Status {
+        if (!x16 || !x8 || !w16 || !w8 || !y) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        if (out_mode < 0 || out_mode > 2 || (act != 0 && act != 1) || (y8 && out_mode != 0) || (terms != 1 && terms != 2))
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: bad out_mode / act / y8 / terms");
+        LinearCall c;
+        c.x = x16;
+        c.w = w16;
+        c.dtype = E_F16;
+        c.M = M;
+        c.N = N;
+        c.K = K;
+        c.ldx = K;
+        c.ldw = K;
+        c.y = y;
+        c.ldy = N;
+        c.out_mode = out_mode == 0 ? OUT_F16 : out_mode == 1 ? OUT_F32 : OUT_F32_ACC;
+        c.bias = bias;
+        c.act = act;
+        c.err = kernel_err_word();
+        c.x8 = x8;
+        c.ldx8 = 2 * K;
+        c.w8 = w8;
+        c.ldw8 = 2 * K;
+        c.acc_scale = acc_scale;
+        c.x8_cols = terms == 1 ? K : 2 * K;
+        c.y8 = y8;
+        c.ldy8 = 2 * N;
+        return launch_linear(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
 int32_t tsfm_relative_bucket(int64_t rel, int32_t num_buckets, int32_t max_distance) {
     if (num_buckets < 2 || max_distance < 1) return -1;
     return (int32_t)relative_bucket(rel, (uint32_t)num_buckets, (uint32_t)max_distance);
