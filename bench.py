@@ -71,6 +71,9 @@ def parse_args():
                     help="series of the bolt-*/timestral workloads (default: the BASELINE.json config's batch; "
                          "smaller batches are for profiling captures)")
     ap.add_argument("--csv-series", type=int, default=8192, help="series of the csv workload")
+    ap.add_argument("--gemm-rows", type=int, default=256 * 577,
+                    help="rows M of the gemm workload (default: the headline's 256 series x 577 tokens; smaller for "
+                         "profiling captures)")
     ap.add_argument("--workload", default="chronos2",
                     choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv", "parse",
                              "attention", "gemm"],
@@ -615,7 +618,7 @@ def run_gemm(a):
     sp = stream.cuda_stream
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
     burst = peaks()[0]
-    M = 256 * 577
+    M = a.gemm_rows
     g = torch.Generator(device="cuda").manual_seed(3)
     shapes = (("qkv", 2304, 768, 0, 0), ("o", 768, 768, 2, 0), ("wi", 3072, 768, 0, 1), ("wo", 768, 3072, 2, 0))
     for name, N, K, out_mode, act in shapes:
