@@ -71,6 +71,9 @@ def parse_args():
                     help="series of the bolt-*/timestral workloads (default: the BASELINE.json config's batch; "
                          "smaller batches are for profiling captures)")
     ap.add_argument("--csv-series", type=int, default=8192, help="series of the csv workload")
+    ap.add_argument("--gemm-controls", action="store_true",
+                    help="gemm workload: also time the weight-term-only corrected product and a plain FP16 product "
+                         "with K doubled")
     ap.add_argument("--gemm-rows", type=int, default=256 * 577,
                     help="rows M of the gemm workload (default: the headline's 256 series x 577 tokens; smaller for "
                          "profiling captures)")
@@ -643,6 +646,16 @@ def run_gemm(a):
                 xc16.data_ptr(), x8.data_ptr(), wc16.data_ptr(), w8.data_ptr(), scale.value, None, y.data_ptr(),
                 None if y8 is None else y8.data_ptr(), out_mode, act, M, N, K, 2, sp)),
         }
+        if a.gemm_controls:
+            # Controls: the weight term only (x_hi (W - f16(W)): 1.5x the FP16 stages), and a plain FP16
+            # product with K doubled (the corrected product's stage count, every stage FP16).
+            x2 = torch.randn(M, 2 * K, device="cuda", generator=g).half()
+            w2 = (torch.randn(N, 2 * K, device="cuda", generator=g) * 0.02).half()
+            runs["f16c-weight-term"] = lambda: tb.check(tb.lib.tsfm_kernel_linear_f16c(
+                xc16.data_ptr(), x8.data_ptr(), wc16.data_ptr(), w8.data_ptr(), scale.value, None, y.data_ptr(),
+                None if y8 is None else y8.data_ptr(), out_mode, act, M, N, K, 1, sp))
+            runs["f16-2k"] = lambda: tb.check(tb.lib.tsfm_kernel_linear(
+                x2.data_ptr(), 1, w2.data_ptr(), 1, None, y.data_ptr(), out_mode, act, M, N, 2 * K, 2 * K, 2 * K, N, sp))
         for mode, run in runs.items():
             for _ in range(max(3, a.warmup)):
                 run()
@@ -658,8 +671,9 @@ def run_gemm(a):
                 total += e0.elapsed_time(e1)
             ms = total / steps
             tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+            work = {"f16": 1.0, "f16c": 2.0, "f16c-weight-term": 1.5, "f16-2k": 2.0}[mode]
             print(json.dumps({"workload": "gemm", "shape": name, "mode": mode, "M": M, "N": N, "K": K, "ms": ms,
-                              "tflops": tf, "tensor_tflops_executed": tf * (2 if mode == "f16c" else 1),
+                              "tflops": tf, "tensor_tflops_executed": tf * work,
                               "frac_of_burst": tf / burst}), flush=True)
         del x16, w16, xc16, x8, wc16, w8, y, y8
 
