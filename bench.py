@@ -79,7 +79,7 @@ def parse_args():
                          "profiling captures)")
     ap.add_argument("--workload", default="chronos2",
                     choices=["chronos2", "bolt-small", "bolt-base", "timestral", "sweep", "csv", "parse",
-                             "attention", "gemm"],
+                             "attention", "gemm", "seam"],
                     help="chronos2 is the headline; bolt-*/timestral are BASELINE.json's other configs, timed "
                          "through the host entry points (copies included); sweep is its Chronos-2 throughput sweep "
                          "(batch x context, one JSON line per point); csv renders the CLI's CSV output of an "
@@ -678,6 +678,62 @@ def run_gemm(a):
         del x16, w16, xc16, x8, wc16, w8, y, y8
 
 
+SEAM_SHAPES = (("qkv", 2304, 768), ("o", 768, 768), ("wi", 3072, 768), ("wo", 768, 3072))
+
+
+def run_seam(a, reference=False):
+    """The reference's GEMM seam (platform/cuda/gemm.c:232-330): C[m, n] = A[m, k] W[n, k]^T with
+    host operands (pinned), W registered once (cuda_weight_register / tsfm_weight_register, as
+    nn.linear does), on the Chronos-2 linear shapes at M = 147,712 rows; one JSON line per shape
+    with the wall time per call (copies included: the call returns when C is on the host) and the
+    error against float64 on 256 sampled rows. This arm: tsfm_sgemm_nt (split-TF32 on the tcgen05
+    kernel); `--impl reference`: the reference's own gemm.c compiled from its source
+    (oracle/_ref/libgemm_ref.so, cuBLAS SGEMM)."""
+    import ctypes
+    import torch
+    if reference:
+        lib = ctypes.CDLL(os.path.join(ROOT, "oracle", "_ref", "libgemm_ref.so"))
+        reg, nt = lib.cuda_weight_register, lib.cuda_sgemm_nt
+    else:
+        import tsfm_b200 as tb
+        reg, nt = tb.lib.tsfm_weight_register, tb.lib.tsfm_sgemm_nt
+    reg.restype, reg.argtypes = ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_size_t]
+    nt.restype = ctypes.c_int
+    nt.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_int,
+                   ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    M = a.gemm_rows
+    rng = np.random.default_rng(9)
+    for name, N, K in SEAM_SHAPES:
+        A = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).pin_memory()
+        W = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)
+        C = torch.empty((M, N), dtype=torch.float32).pin_memory()
+        h = reg(W.ctypes.data, W.size)
+        if not h:
+            print(json.dumps({"workload": "seam", "shape": name, "failed": "weight registration"}), flush=True)
+            continue
+        call = lambda: nt(M, N, K, 1.0, A.data_ptr(), K, None, K, C.data_ptr(), N, h)  # noqa: E731
+        st = call()
+        for _ in range(max(0, a.warmup - 1)):
+            st = st or call()
+        times = []
+        for _ in range(max(1, min(a.steps, 5))):
+            t0 = time.perf_counter()
+            st = st or call()
+            times.append(time.perf_counter() - t0)
+        rows = rng.choice(M, 256, replace=False)
+        ref = A.numpy()[rows].astype(np.float64) @ W.astype(np.float64).T
+        mag = np.abs(A.numpy()[rows]).astype(np.float64) @ np.abs(W).astype(np.float64).T
+        err = float(np.max(np.abs(C.numpy()[rows] - ref) / mag))
+        ms = float(np.median(times)) * 1e3
+        line = {"workload": "seam", "impl": "reference" if reference else "b200", "shape": name, "M": M, "N": N,
+                "K": K, "status": int(st), "ms_per_call": ms, "tflops": 2.0 * M * N * K / (ms / 1e3) / 1e12,
+                "max_err_over_abs_products": err,
+                "bytes_copied_per_call": (M * K + M * N) * 4, "what": "cuBLAS SGEMM via gemm.c" if reference
+                else "split-TF32 tcgen05 (tsfm_sgemm_nt)"}
+        print(json.dumps(line), flush=True)
+        del A, C
+
+
 def measure(model, a, x, world, barrier, clk=None):
     """One operand mode of the headline workload: device-resident series/s (CUDA events on the
     launching stream, L2 flushed between steps, max over ranks), end-to-end series/s through the
@@ -792,10 +848,13 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.impl == "reference":
+        if a.workload == "seam":
+            return run_seam(a, reference=True) if rank == 0 else None
         return run_reference(a, rank)
     if a.workload != "chronos2":
         if rank == 0:
-            {"sweep": run_sweep, "csv": run_csv, "parse": run_parse, "attention": run_attention, "gemm": run_gemm}.get(
+            {"sweep": run_sweep, "csv": run_csv, "parse": run_parse, "attention": run_attention, "gemm": run_gemm,
+             "seam": run_seam}.get(
                 a.workload, run_family_workload)(a)
         return
 

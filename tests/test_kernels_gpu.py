@@ -276,6 +276,20 @@ def test_gemm_seam_padded_strides_like_reference_gpu_test():
     assert tb.lib.tsfm_sgemm_nn(m, n, k, a.ctypes.data, lda, bnn.ctypes.data, ldb, out.ctypes.data, ldc, None) == 0
     np.testing.assert_allclose(o[:, :n], A @ BNN, atol=1e-4)
     assert np.all(o[:, n:] == -12345.0)
+    # Registered weights read in place on the device with their padded row strides: NT over
+    # [n, ldb] rows and NN over [k, ldb] rows (transposed on the device, never copied back).
+    for kind, buf, want in (("nt", bnt, 0.7 * A @ BNT.T), ("nn", bnn, A @ BNN)):
+        h = tb.lib.tsfm_weight_register(buf.ctypes.data, buf.size)
+        assert h
+        out[:] = -12345.0
+        if kind == "nt":
+            st = tb.lib.tsfm_sgemm_nt(m, n, k, 0.7, a.ctypes.data, lda, None, ldb, out.ctypes.data, ldc, h)
+        else:
+            st = tb.lib.tsfm_sgemm_nn(m, n, k, a.ctypes.data, lda, None, ldb, out.ctypes.data, ldc, h)
+        tb.lib.tsfm_weight_release(h)
+        assert st == 0, tb.last_error()
+        np.testing.assert_allclose(o[:, :n], want, atol=1e-4)
+        assert np.all(o[:, n:] == -12345.0)
 
 
 # Corrected products (TSFM_COMPUTE_F16C): FP16 operands plus the FP8 first-order correction terms.

@@ -182,6 +182,10 @@ Status launch_fold_f64(const void *a, int a_dt, const void *b, int b_dt, void *d
 // multiplies by 2^-s). Reads back the weight's range (a stream synchronisation).
 Status build_corrected_weight(const float *w, int64_t rows, int64_t cols, void *w16, void *w8, int *s_out,
                               cudaStream_t s);
+// dst[c, r] = src[r, c] for a [rows, cols] FP32 matrix (row strides ld_src, ld_dst), 32 x 32 tiles
+// through shared memory.
+Status launch_transpose_f32(const float *src, int64_t rows, int64_t cols, int64_t ld_src, float *dst, int64_t ld_dst,
+                            cudaStream_t s);
 // An FP16 activation and its FP8 companion from FP32 values: x16 = f16(x), x8 row r =
 // [e4m3(x16 * kX8HiScale) | e4m3((x - x16) * kX8LoScale)] (row strides in elements / bytes).
 Status launch_split_x8(const float *x, int64_t rows, int64_t cols, int64_t ldx, void *x16, int64_t ld16, void *x8,

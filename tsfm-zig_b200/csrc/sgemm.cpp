@@ -5,6 +5,7 @@
 // FP32, which keeps FP32 SGEMM accuracy. Only the n columns of each output row are written, so
 // the padding of a strided output survives (the reference's gpu_test.zig:18-23 sentinel check).
 #include <cstring>
+#include <memory>
 #include <vector>
 
 #include "runtime.h"
@@ -16,8 +17,9 @@ namespace {
 struct SeamCtx {
     int device = -1;
     cudaStream_t stream = nullptr;
-    DevBuf raw_a, raw_b, ahi, alo, bhi, blo, c;
+    DevBuf raw_a, raw_b, raw_bt, ahi, alo, bhi, blo, c;
     DevBuf err;
+    PinnedBuf err_host;  // the error word's copy, read after the one synchronisation per call
     ~SeamCtx() {
         if (stream) cudaStreamDestroy(stream);
     }
@@ -39,6 +41,7 @@ Status ctx(SeamCtx **out) {
         TSFM_CUDA(cudaStreamCreateWithFlags(&g_ctx->stream, cudaStreamNonBlocking), "cudaStreamCreate");
         TSFM_TRY(g_ctx->err.alloc(16));
         TSFM_CUDA(cudaMemset(g_ctx->err.p, 0, 16), "clear error word");
+        TSFM_TRY(g_ctx->err_host.ensure(16));
     }
     *out = g_ctx.get();
     return Status::ok();
@@ -46,17 +49,22 @@ Status ctx(SeamCtx **out) {
 
 Status grow(DevBuf &b, size_t n) { return n <= b.bytes ? Status::ok() : b.alloc(n); }
 
-// C[m, n] = alpha * A[m, k] B[n, k]^T; `b_rows` is B as [n, k] (ldb), on the device when
-// b_is_device.
-Status sgemm_nt_impl(int m, int n, int k, float alpha, const float *A, int lda, const float *B, int ldb, float *C,
-                     int ldc, bool b_is_device) {
+// Where B comes from: host rows [n, k] (NT), host rows [k, n] (NN), or the same on the device (a
+// registered weight, read in place).
+enum BSource { B_HOST_NK, B_HOST_KN, B_DEV_NK, B_DEV_KN };
+
+// C[m, n] = alpha * A[m, k] B^T with B as [n, k] (or B as [k, n] for the NN forms, transposed on
+// the device): A and C host rows (lda, ldc), B per `src` with row stride ldb.
+Status sgemm_impl(int m, int n, int k, float alpha, const float *A, int lda, const float *B, int ldb, float *C, int ldc,
+                  BSource src) {
     if (m <= 0 || n <= 0 || k <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: empty product");
-    if (!A || !B || !C || lda < k || ldb < k || ldc < n) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: bad operands");
+    const bool nk = src == B_HOST_NK || src == B_DEV_NK;
+    if (!A || !B || !C || lda < k || ldb < (nk ? k : n) || ldc < n)
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: bad operands");
     SeamCtx *x = nullptr;
     TSFM_TRY(ctx(&x));
     const int64_t kp = (k + 3) / 4 * 4, np = (n + 3) / 4 * 4;
     TSFM_TRY(grow(x->raw_a, (size_t)m * k * 4));
-    TSFM_TRY(grow(x->raw_b, (size_t)n * k * 4));
     TSFM_TRY(grow(x->ahi, (size_t)m * kp * 4));
     TSFM_TRY(grow(x->alo, (size_t)m * kp * 4));
     TSFM_TRY(grow(x->bhi, (size_t)n * kp * 4));
@@ -65,13 +73,37 @@ Status sgemm_nt_impl(int m, int n, int k, float alpha, const float *A, int lda, 
     cudaStream_t s = x->stream;
     TSFM_CUDA(cudaMemcpy2DAsync(x->raw_a.p, (size_t)k * 4, A, (size_t)lda * 4, (size_t)k * 4, m, cudaMemcpyHostToDevice, s),
               "sgemm: copy A");
-    TSFM_CUDA(cudaMemcpy2DAsync(x->raw_b.p, (size_t)k * 4, B, (size_t)ldb * 4, (size_t)k * 4, n,
-                                b_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s),
-              "sgemm: copy B");
+    // B as [n, k] rows at b_nk with stride ld_nk: in place (registered NT), copied (host NT), or
+    // transposed on the device (NN).
+    const float *b_nk = B;
+    int64_t ld_nk = ldb;
+    if (src == B_HOST_NK) {
+        TSFM_TRY(grow(x->raw_b, (size_t)n * k * 4));
+        TSFM_CUDA(cudaMemcpy2DAsync(x->raw_b.p, (size_t)k * 4, B, (size_t)ldb * 4, (size_t)k * 4, n,
+                                    cudaMemcpyHostToDevice, s),
+                  "sgemm: copy B");
+        b_nk = static_cast<const float *>(x->raw_b.p);
+        ld_nk = k;
+    } else if (src != B_DEV_NK) {
+        const float *b_kn = B;
+        int64_t ld_kn = ldb;
+        if (src == B_HOST_KN) {
+            TSFM_TRY(grow(x->raw_bt, (size_t)k * n * 4));
+            TSFM_CUDA(cudaMemcpy2DAsync(x->raw_bt.p, (size_t)n * 4, B, (size_t)ldb * 4, (size_t)n * 4, k,
+                                        cudaMemcpyHostToDevice, s),
+                      "sgemm: copy B");
+            b_kn = static_cast<const float *>(x->raw_bt.p);
+            ld_kn = n;
+        }
+        TSFM_TRY(grow(x->raw_b, (size_t)n * k * 4));
+        TSFM_TRY(launch_transpose_f32(b_kn, k, n, ld_kn, static_cast<float *>(x->raw_b.p), k, s));
+        b_nk = static_cast<const float *>(x->raw_b.p);
+        ld_nk = k;
+    }
     float *ahi = static_cast<float *>(x->ahi.p), *alo = static_cast<float *>(x->alo.p);
     float *bhi = static_cast<float *>(x->bhi.p), *blo = static_cast<float *>(x->blo.p);
     TSFM_TRY(launch_split_tf32(static_cast<const float *>(x->raw_a.p), m, k, k, alpha, ahi, alo, kp, s));
-    TSFM_TRY(launch_split_tf32(static_cast<const float *>(x->raw_b.p), n, k, k, 1.0f, bhi, blo, kp, s));
+    TSFM_TRY(launch_split_tf32(b_nk, n, k, ld_nk, 1.0f, bhi, blo, kp, s));
     LinearCall lc;
     lc.dtype = E_F32;
     lc.M = m;
@@ -95,12 +127,14 @@ Status sgemm_nt_impl(int m, int n, int k, float alpha, const float *A, int lda, 
     TSFM_TRY(launch_linear(lc, s));
     TSFM_CUDA(cudaMemcpy2DAsync(C, (size_t)ldc * 4, x->c.p, (size_t)np * 4, (size_t)n * 4, m, cudaMemcpyDeviceToHost, s),
               "sgemm: copy C");
+    int *code = static_cast<int *>(x->err_host.p);
+    TSFM_CUDA(cudaMemcpyAsync(code, x->err.p, 4, cudaMemcpyDeviceToHost, s), "sgemm: error word");
     TSFM_CUDA(cudaStreamSynchronize(s), "sgemm");
-    int code = 0;
-    TSFM_CUDA(cudaMemcpy(&code, x->err.p, 4, cudaMemcpyDeviceToHost), "sgemm: error word");
-    if (code) {
+    if (*code) {
+        const int site = *code;
         cudaMemset(x->err.p, 0, 4);
-        return Status::fail(TSFM_ERR_DEVICE_TIMEOUT, strf("sgemm: a kernel wait gave up (site 0x%04x)", code));
+        *code = 0;
+        return Status::fail(TSFM_ERR_DEVICE_TIMEOUT, strf("sgemm: a kernel wait gave up (site 0x%04x)", site));
     }
     return Status::ok();
 }
@@ -132,10 +166,12 @@ int tsfm_sgemm_nt(int m, int n, int k, float alpha, const float *A, int lda, con
     try {
         if (b_buf) {
             RegWeight *w = static_cast<RegWeight *>(b_buf);
-            if ((size_t)(n - 1) * ldb + k > w->len) return seam_status(Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: registered weight too small"));
-            return seam_status(sgemm_nt_impl(m, n, k, alpha, A, lda, static_cast<const float *>(w->data.p), ldb, C, ldc, true));
+            if (n <= 0 || k <= 0 || (size_t)(n - 1) * ldb + k > w->len)
+                return seam_status(Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: registered weight too small"));
+            return seam_status(sgemm_impl(m, n, k, alpha, A, lda, static_cast<const float *>(w->data.p), ldb, C, ldc,
+                                          B_DEV_NK));
         }
-        return seam_status(sgemm_nt_impl(m, n, k, alpha, A, lda, B, ldb, C, ldc, false));
+        return seam_status(sgemm_impl(m, n, k, alpha, A, lda, B, ldb, C, ldc, B_HOST_NK));
     } catch (...) {
         return seam_status(Status::fail(TSFM_ERR_OUT_OF_MEMORY, "sgemm: host allocation failed"));
     }
@@ -143,24 +179,16 @@ int tsfm_sgemm_nt(int m, int n, int k, float alpha, const float *A, int lda, con
 
 int tsfm_sgemm_nn(int m, int n, int k, const float *A, int lda, const float *B, int ldb, float *C, int ldc, void *b_buf) {
     try {
-        if (m <= 0 || n <= 0 || k <= 0 || !A || !C || ldb < n)
-            return seam_status(Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: bad operands"));
-        // B is [k, n] row-major: transpose to [n, k] for the NT product.
-        std::vector<float> host_b;
-        const float *src = B;
+        // B is [k, n] row-major: transposed to [n, k] on the device for the NT product (a registered
+        // weight is read where it lives; it never returns to the host).
         if (b_buf) {
             RegWeight *w = static_cast<RegWeight *>(b_buf);
-            if ((size_t)(k - 1) * ldb + n > w->len) return seam_status(Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: registered weight too small"));
-            host_b.resize((size_t)(k - 1) * ldb + n);
-            if (cudaMemcpy(host_b.data(), w->data.p, host_b.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
-                return seam_status(Status::fail(TSFM_ERR_CUDA, "sgemm: read registered weight"));
-            src = host_b.data();
+            if (n <= 0 || k <= 0 || (size_t)(k - 1) * ldb + n > w->len)
+                return seam_status(Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: registered weight too small"));
+            return seam_status(sgemm_impl(m, n, k, 1.0f, A, lda, static_cast<const float *>(w->data.p), ldb, C, ldc,
+                                          B_DEV_KN));
         }
-        if (!src) return seam_status(Status::fail(TSFM_ERR_INVALID_ARGUMENT, "sgemm: null B"));
-        std::vector<float> bt((size_t)n * k);
-        for (int p = 0; p < k; ++p)
-            for (int j = 0; j < n; ++j) bt[(size_t)j * k + p] = src[(size_t)p * ldb + j];
-        return seam_status(sgemm_nt_impl(m, n, k, 1.0f, A, lda, bt.data(), k, C, ldc, false));
+        return seam_status(sgemm_impl(m, n, k, 1.0f, A, lda, B, ldb, C, ldc, B_HOST_KN));
     } catch (...) {
         return seam_status(Status::fail(TSFM_ERR_OUT_OF_MEMORY, "sgemm: host allocation failed"));
     }

@@ -121,6 +121,23 @@ __global__ void fold_f64_kernel(const void *a, int a_dt, const void *b, int b_dt
         static_cast<float *>(dst)[o] = v;
 }
 
+// dst[c, r] = src[r, c]; a 32 x 32 tile per block of 32 x 8 threads, staged in shared memory
+// (one padding column, so the transposed reads hit 32 different banks).
+__global__ void transpose_f32_kernel(const float *src, int64_t rows, int64_t cols, int64_t ld_src, float *dst,
+                                     int64_t ld_dst) {
+    __shared__ float tile[32][33];
+    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const int64_t r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[i][threadIdx.x] = src[r * ld_src + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const int64_t c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) dst[c * ld_dst + r] = tile[threadIdx.x][i];
+    }
+}
+
 }  // namespace
 
 Status launch_convert_rows(const void *src, int src_dt, const int32_t *map, void *dst, int dst_dt, int64_t rows,
@@ -166,6 +183,16 @@ Status build_corrected_weight(const float *w, int64_t rows, int64_t cols, void *
                                            static_cast<uint8_t *>(w8));
     TSFM_CUDA(cudaGetLastError(), "corrected weight: split");
     *s_out = sh;
+    return Status::ok();
+}
+
+Status launch_transpose_f32(const float *src, int64_t rows, int64_t cols, int64_t ld_src, float *dst, int64_t ld_dst,
+                            cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return Status::ok();
+    const int64_t ty = (rows + 31) / 32, tx = (cols + 31) / 32;
+    if (ty > 65535) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "transpose: too many rows");
+    transpose_f32_kernel<<<dim3((unsigned)tx, (unsigned)ty), dim3(32, 8), 0, s>>>(src, rows, cols, ld_src, dst, ld_dst);
+    TSFM_CUDA(cudaGetLastError(), "transpose: launch");
     return Status::ok();
 }
 
