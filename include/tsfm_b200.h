@@ -299,6 +299,19 @@ int32_t tsfm_kernel_linear_corrected(const float *x, const float *w, const float
                                      void *y8, int32_t out_mode, int32_t act, int64_t M, int64_t N,
                                      int64_t K, int32_t terms, void *stream);
 
+/* tsfm_test_bounded_wait: the failure-detection check of the device waits. Every wait of the
+ * warp-specialised kernels (TMA and tensor-core barriers) gives up after 2 s, records its site in
+ * the device error word and lets the kernel return, and the host reports
+ * TSFM_ERR_DEVICE_TIMEOUT; this entry runs that same bounded wait on a barrier that nothing
+ * arrives on, with a limit of limit_ns (1 us .. 2 s), and returns what the host then reports
+ * (TSFM_ERR_DEVICE_TIMEOUT). The context stays usable. No counterpart in the reference (its GPU
+ * seam has no device waits).
+ * Host-side failure injection: with the environment variable TSFM_FAIL_REPLICA=<i>, the forecast
+ * worker of replica i of a multi-device model fails before touching its device while the other
+ * workers run and are joined (the forecast returns TSFM_ERR_INVALID_ARGUMENT); unset in normal
+ * use. */
+int32_t tsfm_test_bounded_wait(int64_t limit_ns, void *stream);
+
 /* The corrected product's pieces on device pointers, for benches and tests that time the product
  * alone: tsfm_kernel_split_f16c writes x16 = f16(x) [rows, cols] and its FP8 companion x8
  * [rows, 2 cols]; tsfm_kernel_weight_f16c writes w16 = f16(w) * 2^s and w8 [rows, 2 cols] and

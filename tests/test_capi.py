@@ -146,3 +146,20 @@ def test_product_relative_bucket_matches_reference_table(kat):
     rel = torch.arange(-700, 701)
     want = t5.T5Attention._relative_position_bucket(rel, bidirectional=True, num_buckets=32, max_distance=128)
     assert [tb.lib.tsfm_relative_bucket(int(r), 32, 128) for r in rel] == want.tolist()
+
+
+def test_truncated_tensor_table_is_refused_before_any_device_work():
+    # A checkpoint table cut short (the last tensors missing, as a truncated safetensors header
+    # would leave it) fails with MISSING_TENSOR naming the first absent tensor, on the CPU.
+    cfg = syn.chronos2_config(d_model=128, d_ff=256, num_heads=2, num_layers=2, context_length=512,
+                              max_output_patches=8)
+    w = syn.random_checkpoint(cfg, seed=3)
+    names = sorted(w)
+    kept = {k: w[k] for k in names[: len(names) // 2]}
+    parsed = cm.parse(cfg)
+    table, keep = tb.tensor_table(kept)
+    h = ctypes.c_void_p()
+    st = tb.lib.tsfm_model_create(ctypes.byref(parsed.struct), table, len(kept), 2, None, 0, ctypes.byref(h))
+    assert tb.STATUS_NAMES[st] == "MISSING_TENSOR"
+    assert "missing tensor" in tb.last_error()
+    assert not h.value

@@ -4,11 +4,13 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <thread>
 
 #include "model.h"
+#include "ptx.cuh"
 #include "timestral_kernels.h"
 
 using namespace tsfm;
@@ -85,6 +87,16 @@ bool is_pinned(const void *p) {
 
 // Runs fn(i) for every replica, one host thread per replica beyond the first; returns the first
 // failure in replica order after all threads joined.
+// Host-side failure injection for the tests of the sharded forecasts: with TSFM_FAIL_REPLICA=<i>
+// the forecast worker of replica i fails before it touches its device, while the other workers
+// run and are joined as usual (read on every call; unset in normal use).
+Status injected_failure(size_t i) {
+    const char *v = std::getenv("TSFM_FAIL_REPLICA");
+    if (v && *v && std::strtoul(v, nullptr, 10) == i)
+        return Status::fail(TSFM_ERR_INVALID_ARGUMENT, strf("injected failure in the worker of replica %zu", i));
+    return Status::ok();
+}
+
 template <class F>
 Status for_replicas(size_t n, F &&fn) {
     if (n == 1) return fn(0);
@@ -371,6 +383,7 @@ int32_t tsfm_forecast_chronos2(tsfm_model *model, const float *inputs, size_t b,
         const size_t n = model->reps.size();
         const int64_t q = model->cfg.num_quantiles;
         return for_replicas(n, [&](size_t i) -> Status {
+            TSFM_TRY(injected_failure(i));
             const int64_t s0 = (int64_t)(b * i / n), s1 = (int64_t)(b * (i + 1) / n);
             if (s1 <= s0) return Status::ok();
             Replica &r = *model->reps[i];
@@ -415,6 +428,7 @@ int32_t tsfm_forecast_bolt(tsfm_model *model, const float *inputs, size_t b, siz
         const size_t n = model->reps.size();
         const int64_t q = model->cfg.num_quantiles;
         return for_replicas(n, [&](size_t i) -> Status {
+            TSFM_TRY(injected_failure(i));
             const int64_t s0 = (int64_t)(b * i / n), s1 = (int64_t)(b * (i + 1) / n);
             if (s1 <= s0) return Status::ok();
             Replica &r = *model->reps[i];
@@ -476,6 +490,7 @@ int32_t tsfm_forecast_timestral(tsfm_model *model, const float *inputs, const ui
         // Series shard across replicas; every array is (b, channels, len), so a shard is a
         // contiguous slice of each.
         return for_replicas(n, [&](size_t i) -> Status {
+            TSFM_TRY(injected_failure(i));
             const size_t s0 = b * i / n, s1 = b * (i + 1) / n;
             if (s1 <= s0) return Status::ok();
             Replica &r = *model->reps[i];
@@ -678,6 +693,25 @@ int32_t tsfm_kernel_linear_f16c(const void *x16, const void *x8, const void *w16
         c.y8 = y8;
         c.ldy8 = 2 * N;
         return launch_linear(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int32_t tsfm_test_bounded_wait(int64_t limit_ns, void *stream) {
+    return guarded([&]() -> Status {
+        if (limit_ns < 1000 || limit_ns > (int64_t)kWaitTimeoutNs)
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "bounded wait: limit outside [1 us, 2 s]");
+        int *err = kernel_err_word();
+        if (!err) return Status::fail(TSFM_ERR_CUDA, "bounded wait: no error word");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        int code = 0;
+        TSFM_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st), "bounded wait: clear error word");
+        TSFM_TRY(launch_bounded_wait(err, (unsigned long long)limit_ns, st));
+        TSFM_CUDA(cudaMemcpyAsync(&code, err, sizeof(int), cudaMemcpyDeviceToHost, st), "bounded wait: error word");
+        TSFM_CUDA(cudaStreamSynchronize(st), "bounded wait");
+        TSFM_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st), "bounded wait: clear error word");
+        TSFM_CUDA(cudaStreamSynchronize(st), "bounded wait");
+        if (code) return Status::fail(TSFM_ERR_DEVICE_TIMEOUT, strf("a kernel's bounded wait gave up (site 0x%04x)", code));
+        return Status::ok();
     });
 }
 

@@ -258,6 +258,10 @@ struct HeadPostCall {
 };
 Status launch_head_post(const HeadPostCall &c, cudaStream_t stream);
 
+// A kernel whose only work is one bounded mbarrier wait on a barrier that nothing arrives on (the
+// failure-detection test): it records its site in *err after `limit_ns` and returns.
+Status launch_bounded_wait(int *err, unsigned long long limit_ns, cudaStream_t stream);
+
 // FP32 -> OutMode conversion of a device buffer.
 Status launch_convert(const float *src, void *dst, int64_t n, int mode, cudaStream_t stream);
 

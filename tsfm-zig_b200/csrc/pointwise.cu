@@ -235,6 +235,26 @@ int grid_for(int64_t total, int block) {
 
 }  // namespace
 
+// The bounded mbarrier wait of the warp-specialised kernels, on a barrier that nothing arrives on:
+// the wait gives up after `limit_ns`, records its site in *err and the kernel returns.
+__global__ void bounded_wait_kernel(int *err, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) (void)mbar_wait(&bar, 0, &abort_flag, err, ERR_SITE_WAIT_TEST, limit_ns);
+}
+
+Status launch_bounded_wait(int *err, unsigned long long limit_ns, cudaStream_t stream) {
+    bounded_wait_kernel<<<1, 32, 0, stream>>>(err, limit_ns);
+    TSFM_CUDA(cudaGetLastError(), "bounded wait: launch");
+    return Status::ok();
+}
+
 Status launch_rmsnorm(const RmsNormCall &c, cudaStream_t stream) {
     if (c.rows <= 0 || c.dim <= 0) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "rmsnorm: empty");
     if ((c.dim % 4) == 0 && ((reinterpret_cast<uintptr_t>(c.x) | reinterpret_cast<uintptr_t>(c.scale) |

@@ -27,6 +27,7 @@ enum : int {
     ERR_SITE_ATTN_MMA = 0x0202,
     ERR_SITE_ATTN_SOFTMAX = 0x0203,
     ERR_SITE_ATTN_DRAIN = 0x0204,
+    ERR_SITE_WAIT_TEST = 0x0301,
 };
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
@@ -76,17 +77,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Returns false (after raising the abort
-// flag and recording `site` in *err) when the wait exceeds kWaitTimeoutNs, or when another role
-// of the CTA has already aborted.
+// flag and recording `site` in *err) when the wait exceeds `limit_ns` (kWaitTimeoutNs in every
+// kernel; the bounded-wait test passes a shorter one), or when another role of the CTA has
+// already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          int *err, int site) {
+                                          int *err, int site, unsigned long long limit_ns = kWaitTimeoutNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 255u) == 0) {
             if (*abort_flag) return false;
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 *abort_flag = 1;
                 if (err) atomicCAS(err, 0, site);
                 return false;

@@ -73,6 +73,7 @@ SIGNATURES = {
     "tsfm_kernel_weight_f16c": (_I32, [_P, _I64, _I64, _P, _P, ctypes.POINTER(_F), _P]),
     "tsfm_kernel_linear_f16c": (_I32, [_P, _P, _P, _P, _F, _P, _P, _P, _I32, _I32, _I64, _I64, _I64, _I32, _P]),
     "tsfm_relative_bucket": (_I32, [_I64, _I32, _I32]),
+    "tsfm_test_bounded_wait": (_I32, [_I64, _P]),
     "tsfm_kernel_patch": (_I32, [_I32, _P, _I64, _I64, _I64, _I32, _F, _I32, _I32, _P, _P, _P, _P, _P]),
     "tsfm_kernel_timestral_block_inputs": (_I32, [_P, _P, _I64, _I64, _P, _P, _I64, _I32, _I32, _P, _I32,
                                                   ctypes.c_double, _I32, _I32, _P, _P, _P, _P, _P, _P]),
