@@ -692,6 +692,12 @@ def run_seam(a, reference=False):
     import ctypes
     import torch
     if reference:
+        # gemm.c dlopens cuBLAS from TSFM_CUDA_LIB_DIR (its documented setting). Point it at the
+        # cuBLAS that torch has already loaded: a second cuBLAS build would bind its DT_NEEDED
+        # cuBLASLt by soname to torch's copy and fail to load.
+        if "TSFM_CUDA_LIB_DIR" not in os.environ:
+            import nvidia.cublas
+            os.environ["TSFM_CUDA_LIB_DIR"] = os.path.join(list(nvidia.cublas.__path__)[0], "lib")
         lib = ctypes.CDLL(os.path.join(ROOT, "oracle", "_ref", "libgemm_ref.so"))
         reg, nt = lib.cuda_weight_register, lib.cuda_sgemm_nt
     else:

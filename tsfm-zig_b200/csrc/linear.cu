@@ -293,22 +293,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             uint32_t issued = 0, issued_ph = 0;  // per-stage bit: loaded at least once / parity of last load
-            for (int64_t t = unit; t < tiles && ok; t += units) {
-                const int32_t m0 = (int32_t)((t / n_tiles) * kRows + rank * kBM);
-                const int32_t n0 = (int32_t)((t % n_tiles) * BN + rank * C::B_ROWS);
-                for (int kb = 0; kb < num_k; ++kb) {
+            // Stages [kb0, kb1) of one operand kind: FP8 stages load 128 bytes of the companions'
+            // rows (boxes of the same byte size as the 16-bit ones). One loop per kind, so no
+            // stage branches on it.
+            auto load_stages = [&](auto kind, int32_t m0, int32_t n0, int kb0, int kb1) -> bool {
+                constexpr bool F8 = decltype(kind)::value;
+                const CUtensorMap *ma = F8 ? &tmA8 : &tmA;
+                const CUtensorMap *mb = F8 ? &tmB8 : &tmB;
+                for (int kb = kb0; kb < kb1; ++kb) {
                     const bool got = PAIR ? mbar_wait_cl(&empty[s], ph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_PRODUCER)
                                           : mbar_wait(&empty[s], ph ^ 1u, abort_flag, e.err, ERR_SITE_GEMM_PRODUCER);
-                    if (!got) {
-                        ok = false;
-                        break;
-                    }
-                    // FP8 stages load 128 bytes of the companions' rows; the boxes have the
-                    // same byte size as the 16-bit ones.
-                    const bool f8 = CORR && kb < num_k8;
-                    const CUtensorMap *ma = f8 ? &tmA8 : &tmA;
-                    const CUtensorMap *mb = f8 ? &tmB8 : &tmB;
-                    const int32_t kc = f8 ? kb * 128 : (kb - num_k8) * BK;
+                    if (!got) return false;
+                    const int32_t kc = F8 ? kb * 128 : (kb - kb0) * BK;
                     if constexpr (PAIR) {
                         // The pair's first CTA expects the bytes of both CTAs' boxes on its barrier.
                         if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES));
@@ -327,6 +323,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ph ^= 1u;
                     }
                 }
+                return true;
+            };
+            for (int64_t t = unit; t < tiles && ok; t += units) {
+                const int32_t m0 = (int32_t)((t / n_tiles) * kRows + rank * kBM);
+                const int32_t n0 = (int32_t)((t % n_tiles) * BN + rank * C::B_ROWS);
+                if constexpr (CORR) ok = load_stages(std::true_type{}, m0, n0, 0, num_k8);
+                ok = ok && load_stages(std::false_type{}, m0, n0, num_k8, num_k);
             }
             if (!ok) {
                 // Let loads already in flight land before the CTA can exit: the last load issued
@@ -363,21 +366,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < num_k; ++kb) {
+                // Stages [kb0, kb1) of one operand kind (one loop per kind, no per-stage branch).
+                auto mma_stages = [&](auto kind, int kb0, int kb1) -> bool {
+                  constexpr bool F8 = decltype(kind)::value;
+                  for (int kb = kb0; kb < kb1; ++kb) {
                     const bool got = PAIR ? mbar_wait_cl(&full[s], ph, abort_flag, e.err, ERR_SITE_GEMM_MMA_FULL)
                                           : mbar_wait(&full[s], ph, abort_flag, e.err, ERR_SITE_GEMM_MMA_FULL);
-                    if (!got) {
-                        ok = false;
-                        break;
-                    }
+                    if (!got) return false;
                     tc_fence_after();
                     const uint64_t ad = sdesc_k128(sA + s * C::A_BYTES);
                     const uint64_t bd = sdesc_k128(sB + s * C::B_BYTES);
-                    const bool f8 = CORR && kb < num_k8;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         // advance 32 bytes along K inside the 128-byte swizzle atom
-                        if (f8) {
+                        if constexpr (F8) {
                             if constexpr (PAIR)
                                 mma_f8kind_pair(d_tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
                             else
@@ -400,7 +402,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         s = 0;
                         ph ^= 1u;
                     }
-                }
+                  }
+                  return true;
+                };
+                if constexpr (CORR) ok = mma_stages(std::true_type{}, 0, num_k8);
+                ok = ok && mma_stages(std::false_type{}, num_k8, num_k);
                 if (!ok) break;
                 if constexpr (PAIR) {
                     mma_commit_pair(mapa_shared(&tfull[acc], 0));
