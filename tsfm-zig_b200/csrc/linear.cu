@@ -89,6 +89,7 @@ struct Epi {
     float acc_scale;
     uint8_t *y8;
     int64_t ldy8, y8_half;
+    int y8_tma;  // y8 written by TMA stores of staged boxes (tmY8: bytes [rows, 2 y8_half], 64-byte boxes)
     uint8_t *nx8;
     int64_t ldnx8, nx8_half;
 };
@@ -214,7 +215,7 @@ template <typename T, int BN, bool PAIR, bool NORM, bool CORR>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmA8,
-                     const __grid_constant__ CUtensorMap tmB8, Epi e) {
+                     const __grid_constant__ CUtensorMap tmB8, const __grid_constant__ CUtensorMap tmY8, Epi e) {
     using C = TileCfg<BN, PAIR, NORM>;
     constexpr int STAGES = C::STAGES;
     constexpr int BK = 128 / (int)sizeof(T);
@@ -490,6 +491,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             issue_box(b, col0, row0);
         };
+        // The FP8 companion of this warp's 32 rows x 64 columns (col0 in output columns): staged as
+        // 64 hi and 64 lo bytes per row in a 64-byte-swizzled box and stored with two TMA stores.
+        auto stage_issue_x8 = [&](int64_t col0, int64_t row0, const uint32_t (&xh)[2][8], const uint32_t (&xl)[2][8]) {
+            uint8_t *b = stage_box();
+            stage_x8_32(b, lane, 0, xh[0], xl[0]);
+            stage_x8_32(b, lane, 1, xh[1], xl[1]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&tmY8, b, (int32_t)col0, (int32_t)row0);
+                tma_store_2d(&tmY8, b + 2048, (int32_t)(e.y8_half + col0), (int32_t)row0);
+                bulk_commit();
+            }
+        };
         int acc = 0;
         uint32_t aph = 0;
         // NORM: the old residual of this warp's 32 rows of a tile, prefetched into L2 one tile
@@ -664,6 +679,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < 128; c += 64) {
                     uint8_t *b = stage_box();
                     const bool f16 = e.out_mode == OUT_F16;
+                    uint32_t x8h[2][8], x8l[2][8];  // companion bytes of the 64 columns (y8_tma)
 #pragma unroll
                     for (int h = 0; h < 64; h += 32) {
                         float g[32], u[32];
@@ -679,8 +695,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
 #pragma unroll
                         for (int j = 0; j < 32; ++j) g[j] = g[j] * __fdividef(u[j], 1.0f + __expf(-u[j]));
-                        if (CORR_OUT && e.y8 != nullptr && row_ok)
-                            store_x8_32(e.y8 + orow * e.ldy8, e.y8_half, ncol0 / 2 + c + h, g);
+                        if (CORR_OUT && e.y8 != nullptr) {
+                            if (e.y8_tma)
+                                pack_x8_32(g, x8h[h / 32], x8l[h / 32]);
+                            else if (row_ok)
+                                store_x8_32(e.y8 + orow * e.ldy8, e.y8_half, ncol0 / 2 + c + h, g);
+                        }
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             const float *src = g + 8 * q;
@@ -693,6 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     issue_box(b, ncol0 / 2 + c, wrow0);
+                    if (CORR_OUT && e.y8 != nullptr && e.y8_tma) stage_issue_x8(ncol0 / 2 + c, wrow0, x8h, x8l);
                 }
             } else if (e.rope_cos != nullptr || (e.tma_mode != 0 && !f32_out)) {
                 // 64-column chunks (one head for RoPE): rotate-half pairs (i, i + 32) of columns
@@ -726,7 +747,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int nv1 = rem1 <= 0 ? 0 : (rem1 < 32 ? (int)rem1 : 32);
                     bias_act(e, col0, nv0, lo);
                     if (nv1 > 0) bias_act(e, col0 + 32, nv1, hi);
-                    if (CORR_OUT && e.y8 != nullptr && row_ok) {  // 16-bit output, N % 64 == 0
+                    const bool x8_direct = CORR_OUT && e.y8 != nullptr && !e.y8_tma;
+                    if (x8_direct && row_ok) {  // 16-bit output, N % 64 == 0
                         uint8_t *r8 = e.y8 + orow * e.ldy8;
                         store_x8_32(r8, e.y8_half, col0, lo);
                         store_x8_32(r8, e.y8_half, col0 + 32, hi);
@@ -737,6 +759,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (nv1 > 0) tma_f32(col0 + 32, wrow0, hi);
                         } else {
                             tma_16(col0, wrow0, lo, hi);
+                            if (CORR_OUT && e.y8 != nullptr && e.y8_tma) {
+                                uint32_t x8h[2][8], x8l[2][8];
+                                pack_x8_32(lo, x8h[0], x8l[0]);
+                                pack_x8_32(hi, x8h[1], x8l[1]);
+                                stage_issue_x8(col0, wrow0, x8h, x8l);
+                            }
                         }
                     } else if (row_ok) {
                         store_chunk(e, orow, col0, nv0, lo);
@@ -814,7 +842,7 @@ bool load_encode() {
 }
 
 Status make_tmap(CUtensorMap *map, const void *base, int dtype, int64_t inner, int64_t outer, int64_t ld,
-                 uint32_t box_inner, uint32_t box_outer) {
+                 uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     if (!load_encode()) return Status::fail(TSFM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const bool f32 = dtype == E_F32;
     const int esz = f32 ? 4 : dtype == E_U8 ? 1 : 2;
@@ -829,7 +857,7 @@ Status make_tmap(CUtensorMap *map, const void *base, int dtype, int64_t inner, i
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(map, dt, 2,
                           const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return Status::fail(TSFM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
     return Status::ok();
@@ -949,6 +977,14 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
     }
     if (c.act == ACT_GLU && e.tma_mode != 1)
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "linear: gated pairs need a 16-byte-aligned 16-bit output");
+    // The FP8 companion of a 16-bit output stored by TMA leaves by TMA too: bytes [M, 2 ycols] at
+    // row stride ldy8, 64-byte x 32-row boxes in the 64-byte swizzle.
+    CUtensorMap ty8 = tb;
+    e.y8_tma = 0;
+    if (c.y8 && e.tma_mode == 1 && !f32_out) {
+        if (make_tmap(&ty8, c.y8, E_U8, 2 * e.y8_half, c.M, c.ldy8, 64, 32, CU_TENSOR_MAP_SWIZZLE_64B).code == 0)
+            e.y8_tma = 1;
+    }
     if constexpr (PAIR) {
         // Clusters of two CTAs, one per SM pair, persistent over 256-row tiles.
         const int64_t tiles = ((c.M + 2 * kBM - 1) / (2 * kBM)) * ((c.N + BN - 1) / BN);
@@ -965,12 +1001,12 @@ Status launch_t(const LinearCall &c, cudaStream_t stream) {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        ce = cudaLaunchKernelEx(&cfg, linear_tc_kernel<T, BN, true, NORM, CORR>, ta, tb, ty, ta8, tb8, e);
+        ce = cudaLaunchKernelEx(&cfg, linear_tc_kernel<T, BN, true, NORM, CORR>, ta, tb, ty, ta8, tb8, ty8, e);
         if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch (CTA pairs)");
     } else {
         const int64_t tiles = ((c.M + kBM - 1) / kBM) * ((c.N + BN - 1) / BN);
         const int grid = (int)std::min<int64_t>(tiles, sm_count());
-        linear_tc_kernel<T, BN, false, NORM, CORR><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, ta8, tb8, e);
+        linear_tc_kernel<T, BN, false, NORM, CORR><<<grid, kThreads, C::SMEM, stream>>>(ta, tb, ty, ta8, tb8, ty8, e);
     }
     ce = cudaGetLastError();
     if (ce != cudaSuccess) return Status::cuda(ce, "linear: launch");
