@@ -66,7 +66,8 @@ def parse_args():
     ap.add_argument("--no-compare", action="store_true",
                     help="skip the extra measurement of plain FP16 operands beside the headline")
     ap.add_argument("--series", type=int, default=SERIES_PER_GPU)
-    ap.add_argument("--cpu-sample", type=int, default=4, help="series timed on the CPU baseline leg")
+    ap.add_argument("--cpu-sample", type=int, default=4,
+                    help="series timed on the CPU baseline leg (bolt-*/timestral: 0 skips it, for profiling captures)")
     ap.add_argument("--batch", type=int, default=None,
                     help="series of the bolt-*/timestral workloads (default: the BASELINE.json config's batch; "
                          "smaller batches are for profiling captures)")
@@ -351,7 +352,13 @@ def run_family_workload(a):
     model.profile(False)
     kernels = {c: {"launches": v["launches"], "ms": v["ms"]} for c, v in cls.items() if v["launches"]}
     # CPU baseline: the oracle (the reference algorithm restated, all host threads) on a bounded
-    # sample of the same workload.
+    # sample of the same workload (skipped with --cpu-sample 0, for profiling captures).
+    if a.cpu_sample == 0:
+        line = {"workload": a.workload, "series": b, "ms_per_step": ms, "value": b / (ms / 1e3), "unit": "series/s",
+                "gpu_launches": model.last_launch_count(), "kernels": kernels, "cpu_baseline": None}
+        print(json.dumps(line), flush=True)
+        model.close()
+        return
     from oracle import binding as ob
     from tsfm_spec import config as cm
     from tsfm_spec.table import tensor_table
