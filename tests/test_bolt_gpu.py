@@ -117,7 +117,9 @@ def test_bolt_small_shape_matches_oracle():
     got = gpu.forecast_bolt(x, 192)
     want = ora.forecast_bolt(x, 192)
     assert np.isfinite(got).all()
-    assert rel_err(got, want, x) <= TOL
+    err = rel_err(got, want, x)
+    print(f"Bolt-small configs[0]: max |dq|/sigma = {err:.3e}")
+    assert err <= TOL
 
 
 @pytest.mark.parametrize("dtype", [np.float32, "bf16"])
@@ -135,4 +137,6 @@ def test_bolt_base_shape_matches_oracle(dtype):
     want = ora.forecast_bolt(x, 256)
     assert got.shape == (3, 256, 9)
     assert np.isfinite(got).all()
-    assert rel_err(got, want, x) <= TOL
+    err = rel_err(got, want, x)
+    print(f"Bolt-base configs[1] ({dtype if isinstance(dtype, str) else 'f32'} checkpoint): max |dq|/sigma = {err:.3e}")
+    assert err <= TOL
