@@ -218,8 +218,9 @@ def test_attention_tcgen05_path_edges(n, with_rel, dtype):
     rel = torch.randn(heads, 2 * n - 1, generator=gen) * 2 if with_rel else None
     reld = rel.to(dev()) if with_rel else None
     o = torch.full((G * n, heads * 64), float("nan"), device=dev(), dtype=TORCH16[dtype])
+    kvd = kv.to(dev())
     tb.check(tb.lib.tsfm_kernel_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, o.data_ptr(), heads * 64,
-                                          kv.to(dev()).data_ptr(), None if reld is None else reld.data_ptr(), G, heads,
+                                          kvd.data_ptr(), None if reld is None else reld.data_ptr(), G, heads,
                                           n, 1.0, 0, CODE16[TORCH16[dtype]], stream_ptr()))
     torch.cuda.synchronize()
     ref = attention_ref(q, k, v, kv, rel, n, heads, 1.0, 0)
@@ -227,6 +228,71 @@ def test_attention_tcgen05_path_edges(n, with_rel, dtype):
     assert torch.isfinite(got).all()
     err = (got - ref).abs().max().item()
     assert err < (3e-2 if dtype == "bf16" else 5e-3), err
+
+
+def timestral_attention_ref(q, k, v, kv, bidir, n, heads, scale, ne, l):
+    """float64 restatement of Timestral's time-attention masks (timestral/model.zig:558-635):
+    encoder queries i < ne see j < ne with j == i or (valid(j) and (bidirectional or j <= i));
+    decoder queries i >= ne see valid j < l plus ne <= j <= i."""
+    G = q.shape[0] // n
+    out = torch.zeros(q.shape[0], heads * 64, dtype=torch.float64)
+    qd, kd, vd = q.double().cpu(), k.double().cpu(), v.double().cpu()
+    i = torch.arange(n)[:, None]
+    j = torch.arange(n)[None, :]
+    for g in range(G):
+        valid = kv[g].bool()[None, :]
+        bd = bool(bidir[g])
+        enc = (j < ne) & ((j == i) | (valid & (bd | (j <= i))))
+        dec = ((j < l) & valid) | ((j >= ne) & (j <= i))
+        allowed = torch.where(i < ne, enc, dec)
+        for h in range(heads):
+            sl = slice(h * 64, (h + 1) * 64)
+            s = qd[g * n:(g + 1) * n, sl] @ kd[g * n:(g + 1) * n, sl].T * scale
+            p = torch.softmax(s.masked_fill(~allowed, float("-inf")), dim=1)
+            out[g * n:(g + 1) * n, sl] = p @ vd[g * n:(g + 1) * n, sl]
+    return out
+
+
+@pytest.mark.parametrize("n,ne,l,mode", [(160, 144, 128, 1), (160, 160, 160, 1), (17, 12, 8, 1), (129, 100, 64, 1),
+                                         (300, 256, 200, 1), (700, 600, 512, 1), (200, 150, 150, 2), (1, 1, 1, 1),
+                                         (256, 128, 0, 1)])
+@pytest.mark.parametrize("out32", [False, True])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_attention_timestral_masks_both_paths(n, ne, l, mode, out32, dtype):
+    """Timestral's causal / bidirectional / decoder-chain masks on the tcgen05 kernel (force_path 1)
+    and the mma.sync kernel (force_path 2), 16-bit and FP32 outputs, against float64: groups with
+    per-group bidirectional rows, invalid keys everywhere but the diagonal, and decoder rows."""
+    heads, G = 2, 5
+    gen = torch.Generator().manual_seed(7 * n + ne + l + mode)
+    ld = 3 * heads * 64 + 8
+    qkv = (torch.randn(G * n, ld, generator=gen) * 0.7).to(TORCH16[dtype]).to(dev())
+    q, k, v = qkv[:, :heads * 64], qkv[:, heads * 64:2 * heads * 64], qkv[:, 2 * heads * 64:3 * heads * 64]
+    kv = (torch.rand(G, ne, generator=gen) > 0.3).to(torch.uint8)
+    kv[1, :] = 0  # only the diagonal (and the decoder chain) visible
+    kv[2, :] = 1
+    bidir = torch.tensor([0, 1, 0, 1, 0], dtype=torch.uint8)
+    if mode == 2:
+        bidir[:] = 1
+    kv_full = torch.ones(G, n, dtype=torch.uint8)
+    kv_full[:, :ne] = kv
+    scale = 0.125
+    ref = timestral_attention_ref(q, k, v, kv_full, bidir, n, heads, scale, ne, l)
+    kvd, bidird = kv.to(dev()), bidir.to(dev())  # kept alive until the kernels have run
+    outs = {}
+    for path in (1, 2):
+        o = torch.full((G * n, heads * 64), float("nan"), device=dev(), dtype=TORCH16[dtype])
+        o32 = torch.full((G * n, heads * 64), float("nan"), device=dev(), dtype=torch.float32) if out32 else None
+        tb.check(tb.lib.tsfm_kernel_attention_ex(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, None if out32 else o.data_ptr(), heads * 64,
+            o32.data_ptr() if out32 else None, heads * 64, kvd.data_ptr(), ne,
+            bidird.data_ptr(), G, heads, n, scale, mode, ne, l, CODE16[TORCH16[dtype]], path, stream_ptr()))
+        torch.cuda.synchronize()
+        outs[path] = (o32 if out32 else o).double().cpu()
+        assert torch.isfinite(outs[path]).all(), path
+        err = (outs[path] - ref).abs().max().item()
+        assert err < (3e-2 if dtype == "bf16" else 5e-3), (path, err)
+    if out32:
+        assert (outs[1] - outs[2]).abs().max().item() < (3e-2 if dtype == "bf16" else 5e-3)
 
 
 def test_rmsnorm_matches_oracle():

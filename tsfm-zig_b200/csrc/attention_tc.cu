@@ -29,7 +29,13 @@
 //
 // Masks: the key-validity mask of chronos2/model.zig:208-233 and chronos_bolt/model.zig (mode 0:
 // key j is visible when it is valid; a group without any valid key attends uniformly to all its
-// keys, the reference's additive -floatMax mask). Relative-position bias (Chronos-Bolt's T5
+// keys, the reference's additive -floatMax mask), and Timestral's time-attention masks
+// (timestral/model.zig:558-635, modes 1-2): encoder queries i < ne see the valid keys j <= i (any
+// valid j < ne in a bidirectional group) and always j == i; decoder queries i >= ne see the valid
+// keys below l and their chain ne <= j <= i. An item then reads only the key tiles up to the last
+// key one of its rows can see, and tiles where the rows differ are masked per row from the
+// validity bits (TILE_ROWS). The output is 16-bit (TMA store) or FP32 (written by the softmax
+// threads, for corrected products). Relative-position bias (Chronos-Bolt's T5
 // encoder, chronos_bolt/model.zig:195-205: score(i, j) += bias_h(j - i)) for n <= 512: the mask warp
 // copies the item's window of the per-head offset table into its mask slot, and each softmax thread
 // adds the 128 entries of its row to S before the row maximum. Every wait is bounded (ptx.cuh).
@@ -54,19 +60,24 @@ constexpr int kRelWin = kMaxKeysRel + kTileRows;     // offsets one item's 128 q
 constexpr int kThreadsTc = 352;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-// Tile classes of a key tile.
-enum : uint8_t { TILE_FULL = 0, TILE_PREFIX = 1, TILE_BITS = 2 };
+// Tile classes of a key tile. TILE_ROWS (Timestral's causal / decoder masks): the visible keys
+// depend on the query row; each softmax thread builds its row's bits from the validity bits.
+enum : uint8_t { TILE_FULL = 0, TILE_PREFIX = 1, TILE_BITS = 2, TILE_ROWS = 3 };
 
 // Mask of one item: per key tile its class and, for TILE_BITS, 128 validity bits; `uniform`:
 // no valid key (every key below n gets score 0).
 // `rel`: relative-position bias of the item's head, rel[i] = bias(i - 127 - q0) for
 // i < T * 128 + 127 (0 outside the table), so query row r of the tile at key c of key tile j reads
 // rel[128 j + c - r + 127].
+// `ntiles`: key tiles the item reads (all of them in mode 0; up to the last visible key in modes
+// 1-2); `bidir`: the item's group is bidirectional (mode 1-2).
 struct MaskSlot {
     uint32_t bits[kMaxKeys / 32];
     uint8_t cls[kMaxKeyTiles];
     uint32_t uniform;
-    uint32_t pad[7];
+    int32_t ntiles;
+    int32_t bidir;
+    uint32_t pad[5];
     float rel[kRelWin];
 };
 
@@ -100,7 +111,32 @@ struct TcParams {
     // head h's 64 values at byte h * 64, their low parts o8_half bytes further.
     uint8_t *o8;
     int64_t ld_o8, o8_half;
+    // Masks of modes 1-2 (AttentionCall): encoder queries i < ne, decoder queries i >= ne reading
+    // valid keys below l and their chain [ne, i]; per-group bidirectional flags.
+    int mode, ne, l, bidir_all;
+    const uint8_t *bidir;
+    // FP32 output instead of the 16-bit one (row (g * n + i) at o32 + row * ld_o32, head h at h * 64).
+    float *o32;
+    int64_t ld_o32;
 };
+
+// Key tiles an item reads: every tile in mode 0; in modes 1-2 the tiles up to the last key any of
+// its rows can see (the causal bound, or the encoder for a bidirectional group), as the mma.sync
+// kernel bounds its key loop.
+__device__ __forceinline__ bool item_bidir(const TcParams &p, int g) {
+    return p.mode != 0 && (p.bidir_all || (p.bidir != nullptr && p.bidir[g] != 0));
+}
+__device__ __forceinline__ int item_tiles(const TcParams &p, int g, int q0) {
+    if (p.mode == 0) return (p.n + kTileRows - 1) / kTileRows;
+    const int qhi = min(p.n, q0 + kTileRows);
+    const int kv_end = item_bidir(p, g) ? max(p.ne, qhi) : qhi;
+    return (kv_end + kTileRows - 1) / kTileRows;
+}
+
+// Lanes [0, x) of a 32-bit word (x clamped to [0, 32]).
+__device__ __forceinline__ uint32_t low_bits(int x) {
+    return x <= 0 ? 0u : x >= 32 ? 0xffffffffu : ((1u << x) - 1u);
+}
 
 template <bool F16>
 __device__ __forceinline__ uint32_t pack_p(float a, float b) {
@@ -216,7 +252,12 @@ __global__ void __maxnreg__(168)
             const uint8_t *kv = p.key_valid ? p.key_valid + (int64_t)im.g * p.kvs : nullptr;
             MaskSlot &m = mslots[q * 2 + slot];
             bool any = false;
-            for (int t = 0; t < T; ++t) {
+            const int Ti = item_tiles(p, im.g, im.q0);
+            const bool bid = item_bidir(p, im.g);
+            // Modes 1-2: rows [i0, i1] of the item; a tile whose keys all lie below every row (or,
+            // for a bidirectional group, hold no diagonal key) shows each row exactly the valid keys.
+            const int i0 = im.q0, i1 = min(n, im.q0 + kTileRows) - 1;
+            for (int t = 0; t < Ti; ++t) {
                 bool all_valid = true, prefix = true;
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
@@ -231,10 +272,23 @@ __global__ void __maxnreg__(168)
                 }
                 all_valid = __all_sync(0xffffffffu, all_valid);
                 prefix = __all_sync(0xffffffffu, prefix);
-                if (lane == 0) m.cls[t] = all_valid ? TILE_FULL : prefix ? TILE_PREFIX : TILE_BITS;
+                bool per_row = false;
+                if (p.mode != 0) {
+                    const int k0 = t * kTileRows, k1 = min(n, k0 + kTileRows) - 1;
+                    const bool below = i1 < p.ne && k1 < i0;
+                    const bool bidir_clear = bid && i1 < p.ne && k1 < p.ne && (k1 < i0 || k0 > i1);
+                    per_row = !(below || bidir_clear);
+                }
+                if (lane == 0) m.cls[t] = per_row ? TILE_ROWS : all_valid ? TILE_FULL : prefix ? TILE_PREFIX : TILE_BITS;
             }
-            const bool uniform = !__any_sync(0xffffffffu, any);
-            if (lane == 0) m.uniform = uniform ? 1u : 0u;
+            // Modes 1-2 never leave a row without a visible key (the diagonal, or the decoder
+            // chain's own position), so no group attends uniformly.
+            const bool uniform = p.mode == 0 && !__any_sync(0xffffffffu, any);
+            if (lane == 0) {
+                m.uniform = uniform ? 1u : 0u;
+                m.ntiles = Ti;
+                m.bidir = bid ? 1 : 0;
+            }
             if (p.rel) {
                 const float *tab = p.rel + (int64_t)im.h * p.rel_stride;
                 const int64_t base = p.rel_center - im.q0 - (kTileRows - 1);
@@ -254,10 +308,26 @@ __global__ void __maxnreg__(168)
             uint8_t *base = smem + q * PIPE_BYTES;
             const uint32_t t_s = tmem_base + q * 256 + TM_S, t_p = tmem_base + q * 256 + TM_P;
             const uint32_t t_o = tmem_base + q * 256 + TM_O;
-            const uint32_t uT = (uint32_t)T;
             const uint32_t nq = last - first > q ? (uint32_t)((last - first - q + 1) / 2) : 0u;  // items
-            const uint32_t NT = nq * uT;                                                        // key tiles
             auto item_of = [&](uint32_t wi) { return decode_item(p, first + q + 2 * (int64_t)wi); };
+            auto tiles_of = [&](uint32_t wi) {
+                const Item im = item_of(wi);
+                return (uint32_t)item_tiles(p, im.g, im.q0);
+            };
+            // The pipeline's key tiles in order (item by item; items may read different numbers of
+            // tiles in modes 1-2). A cursor walks them: item, tile within the item, and the item's
+            // tile count.
+            struct Cursor {
+                uint32_t wi, j, n;
+            };
+            auto cursor_start = [&]() { return Cursor{0u, 0u, nq > 0 ? tiles_of(0) : 0u}; };
+            auto advance = [&](Cursor &c) {
+                if (++c.j == c.n) {
+                    ++c.wi;
+                    c.j = 0;
+                    c.n = c.wi < nq ? tiles_of(c.wi) : 0u;
+                }
+            };
             uint32_t loads[3] = {0, 0, 0};  // Q, K, V loads issued (in ring order)
             auto load_q = [&](uint32_t wi) {
                 ++loads[0];
@@ -266,26 +336,38 @@ __global__ void __maxnreg__(168)
                 mbar_arrive_expect_tx(&b.q_full[s], kTileBytes);
                 tma_load_2d(base + OFF_Q + s * kTileBytes, &tmQ, &b.q_full[s], im.h * 64, im.g * n + im.q0);
             };
-            // Key tile g of this pipeline (item g / T, tile g % T) into ring slot g % 2.
-            auto load_kv = [&](bool key, uint32_t g) {
-                ++loads[key ? 1 : 2];
-                const uint32_t wi = g / uT, j = g - wi * uT, s = g & 1;
-                const Item im = item_of(wi);
-                uint64_t *ful = key ? &b.k_full[s] : &b.v_full[s];
-                mbar_arrive_expect_tx(ful, kTileBytes);
-                tma_load_2d(base + (key ? OFF_K : OFF_V) + s * kTileBytes, key ? &tmK : &tmV, ful, im.h * 64,
-                            im.g * n + (int32_t)j * kTileRows);
+            // Key tile g of this pipeline (the tile under the K or V cursor) into ring slot g % 2.
+            Cursor kc = cursor_start(), vc = cursor_start(), pc = cursor_start();
+            auto load_k = [&](uint32_t g) {
+                ++loads[1];
+                const Item im = item_of(kc.wi);
+                const uint32_t s = g & 1;
+                mbar_arrive_expect_tx(&b.k_full[s], kTileBytes);
+                tma_load_2d(base + OFF_K + s * kTileBytes, &tmK, &b.k_full[s], im.h * 64,
+                            im.g * n + (int32_t)kc.j * kTileRows);
+                advance(kc);
+            };
+            auto load_v = [&](uint32_t g) {
+                ++loads[2];
+                const Item im = item_of(vc.wi);
+                const uint32_t s = g & 1;
+                mbar_arrive_expect_tx(&b.v_full[s], kTileBytes);
+                tma_load_2d(base + OFF_V + s * kTileBytes, &tmV, &b.v_full[s], im.h * 64,
+                            im.g * n + (int32_t)vc.j * kTileRows);
+                advance(vc);
             };
             bool ok = true;
-            // O += P V for key tile gg. When gg opens an item, the softmax threads have staged the
-            // previous item's output in its Q buffer before this p_ready: store it, then reuse the
-            // buffer for the Q two items ahead.
+            // O += P V for key tile gg (the tile under the PV cursor). When gg opens an item, the
+            // softmax threads have staged the previous item's output in its Q buffer before this
+            // p_ready: store it (16-bit outputs; an FP32 output was written by the softmax threads),
+            // then reuse the buffer for the Q two items ahead.
             auto pv = [&](uint32_t gg) -> bool {
                 const uint32_t s = gg & 1;
                 if (!mbar_wait(&b.v_full[s], (gg >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
                 if (!mbar_wait(&b.p_ready, gg & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) return false;
                 tc_fence_after();
-                const uint32_t wi = gg / uT, j = gg - wi * uT;
+                const uint32_t wi = pc.wi, j = pc.j;
+                advance(pc);
                 const uint64_t vd = sdesc_k128(base + OFF_V + s * kTileBytes);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)  // A: 16 keys = 8 TMEM columns; B: 16 key rows = 2048 bytes
@@ -294,10 +376,12 @@ __global__ void __maxnreg__(168)
                 mma_commit(&b.o_done);
                 mma_commit(&b.v_empty[s]);
                 if (j == 0 && wi >= 1) {
-                    const uint32_t ps = (wi - 1) & 1;
-                    const Item im = item_of(wi - 1);
-                    tma_store_3d(&tmO, base + OFF_Q + ps * kTileBytes, im.h * 64, im.q0, im.g);
-                    bulk_commit();
+                    if (p.o32 == nullptr) {
+                        const uint32_t ps = (wi - 1) & 1;
+                        const Item im = item_of(wi - 1);
+                        tma_store_3d(&tmO, base + OFF_Q + ps * kTileBytes, im.h * 64, im.q0, im.g);
+                        bulk_commit();
+                    }
                     if (wi + 1 < nq) {
                         bulk_wait_read_0();
                         load_q(wi + 1);
@@ -307,16 +391,16 @@ __global__ void __maxnreg__(168)
             };
             if (nq > 0) load_q(0);
             if (nq > 1) load_q(1);
-            for (uint32_t g = 0; g < NT && g < 2; ++g) {
-                load_kv(true, g);
-                load_kv(false, g);
+            for (uint32_t g = 0; g < 2 && kc.wi < nq; ++g) {
+                load_k(g);
+                load_v(g);
             }
             uint32_t g = 0, next_pv = 0;
             for (uint32_t wi = 0; wi < nq && ok; ++wi) {
                 const uint32_t qs = wi & 1;
-                // With one key tile per item, the pending PV opens the previous item and loads
-                // this item's Q: issue it before waiting for that Q.
-                if (uT == 1 && next_pv < g && !pv(next_pv++)) {
+                // When the pending PV opens the previous item (an item of one key tile), it stores
+                // the output before it and loads this item's Q: issue it before waiting for that Q.
+                if (next_pv < g && pc.j == 0 && !pv(next_pv++)) {
                     ok = false;
                     break;
                 }
@@ -325,7 +409,8 @@ __global__ void __maxnreg__(168)
                     break;
                 }
                 const uint64_t qd = sdesc_k128(base + OFF_Q + qs * kTileBytes);
-                for (uint32_t j = 0; j < uT; ++j, ++g) {
+                const uint32_t Ti = tiles_of(wi);
+                for (uint32_t j = 0; j < Ti; ++j, ++g) {
                     const uint32_t s = g & 1;
                     if (!mbar_wait(&b.k_full[s], (g >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA) ||
                         (g > 0 && !mbar_wait(&b.s_free, (g - 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA))) {
@@ -345,26 +430,26 @@ __global__ void __maxnreg__(168)
                     }
                     // Refill the rings: K two tiles ahead once this S is done with its slot, V
                     // one tile ahead once the PV just issued is done with its slot.
-                    if (g + 2 < NT) {
+                    if (kc.wi < nq) {  // tile g + 2 exists
                         if (!mbar_wait(&b.k_empty[s], (g >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
                             ok = false;
                             break;
                         }
-                        load_kv(true, g + 2);
+                        load_k(g + 2);
                     }
-                    if (g >= 1 && g + 1 < NT) {
+                    if (g >= 1 && vc.wi < nq) {  // tile g + 1 exists
                         if (!mbar_wait(&b.v_empty[(g + 1) & 1], ((g - 1) >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
                             ok = false;
                             break;
                         }
-                        load_kv(false, g + 1);
+                        load_v(g + 1);
                     }
                 }
             }
-            while (ok && next_pv < NT) ok = pv(next_pv++);
+            while (ok && pc.wi < nq) ok = pv(next_pv++);
             // The last item's output: staged by the softmax threads after the last PV, signalled
-            // by one more p_ready phase.
-            if (ok && NT > 0 && mbar_wait(&b.p_ready, NT & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+            // by one more p_ready phase (g = the pipeline's key tiles).
+            if (ok && g > 0 && mbar_wait(&b.p_ready, g & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA) && p.o32 == nullptr) {
                 const Item im = item_of(nq - 1);
                 tma_store_3d(&tmO, base + OFF_Q + ((nq - 1) & 1) * kTileBytes, im.h * 64, im.q0, im.g);
                 bulk_commit();
@@ -420,12 +505,25 @@ __global__ void __maxnreg__(168)
             uint8_t *row8 = nullptr;
             if (O8 && prev_im.q0 + r < n)
                 row8 = p.o8 + ((int64_t)prev_im.g * n + prev_im.q0 + r) * p.ld_o8;
+            // An FP32 output goes straight to global memory as well (no TMA store follows).
+            float *row32 = nullptr;
+            if (p.o32 != nullptr && prev_im.q0 + r < n)
+                row32 = p.o32 + ((int64_t)prev_im.g * n + prev_im.q0 + r) * p.ld_o32 + (int64_t)prev_im.h * 64;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[32];
                 tmem_ld32(t_o + 32 * h, v);
                 tmem_wait_ld();
                 if (row8 != nullptr) store_x8_32(row8, p.o8_half, (int64_t)prev_im.h * 64 + 32 * h, v, inv);
+                if (p.o32 != nullptr) {
+                    if (row32 != nullptr) {
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            *reinterpret_cast<float4 *>(row32 + 32 * h + 4 * c) =
+                                make_float4(v[4 * c] * inv, v[4 * c + 1] * inv, v[4 * c + 2] * inv, v[4 * c + 3] * inv);
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const int chunk = (4 * h + c) ^ (r & 7);
@@ -451,7 +549,23 @@ __global__ void __maxnreg__(168)
             // protocol (its P and O rows are never read back).
             const bool dead = im.q0 + quarter * 32 >= n;
             float m_run = -INFINITY, l_run = 0.0f;
-            for (int j = 0; j < T; ++j, ++cx) {
+            const int Ti = m.ntiles;
+            // Modes 1-2, this thread's row i: the visible keys of a TILE_ROWS tile are the valid keys
+            // below A plus the keys in [B, C] (encoder row: A = i + 1, or ne for a bidirectional
+            // group, and B = C = i, the diagonal; decoder row: A = l, B = ne, C = i).
+            int rA = 0, rB = 0, rC = -1;
+            if (p.mode != 0) {
+                const int i = im.q0 + r;
+                if (i < p.ne) {
+                    rA = m.bidir ? p.ne : i + 1;
+                    rB = rC = i;
+                } else {
+                    rA = min(p.l, n);
+                    rB = p.ne;
+                    rC = i;
+                }
+            }
+            for (int j = 0; j < Ti; ++j, ++cx) {
                 const bool got = mbar_wait(&b.s_full, cx & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
@@ -511,8 +625,15 @@ __global__ void __maxnreg__(168)
                     const float keep = uniform ? 0.0f : 1.0f;
 #pragma unroll
                     for (int i = 0; i < 128; ++i) s[i] = i < cnt ? s[i] * keep : -INFINITY;
-                } else if (cls == TILE_BITS) {
-                    const uint32_t wd[4] = {m.bits[4 * j], m.bits[4 * j + 1], m.bits[4 * j + 2], m.bits[4 * j + 3]};
+                } else if (cls == TILE_BITS || cls == TILE_ROWS) {
+                    uint32_t wd[4] = {m.bits[4 * j], m.bits[4 * j + 1], m.bits[4 * j + 2], m.bits[4 * j + 3]};
+                    if (cls == TILE_ROWS) {
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            const int k0 = j * kTileRows + 32 * w;
+                            wd[w] = (wd[w] & low_bits(rA - k0)) | (low_bits(rC + 1 - k0) & ~low_bits(rB - k0));
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < 128; ++i) s[i] = ((wd[i >> 5] >> (i & 31)) & 1u) ? s[i] : -INFINITY;
                 }
@@ -610,7 +731,10 @@ __global__ void __maxnreg__(168)
 
 bool attention_tc_supported(const AttentionCall &c) {
     if (c.force_path == 2) return false;
-    if (c.mask_mode != 0 || (c.rel_bias != nullptr && c.n > kMaxKeysRel)) return false;
+    if (c.mask_mode < 0 || c.mask_mode > 2) return false;
+    if (c.rel_bias != nullptr && (c.mask_mode != 0 || c.n > kMaxKeysRel)) return false;
+    if (c.mask_mode != 0 && (c.ne < 0 || c.ne > c.n || c.l < 0)) return false;
+    if (c.o32 != nullptr && (c.o8 != nullptr || (reinterpret_cast<uintptr_t>(c.o32) & 15) || (c.ld_o32 % 4))) return false;
     if (c.dtype != E_F16 && c.dtype != E_BF16) return false;
     if (c.n <= 0 || c.n > kMaxKeys || c.heads <= 0 || c.groups <= 0) return false;
     if ((int64_t)c.groups * c.n > INT32_MAX - 2 * kTileRows) return false;
@@ -629,8 +753,12 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     TSFM_TRY(make_tmap_2d(&mq, c.q, c.dtype, width, rows, c.ld_qkv, 64, kTileRows));
     TSFM_TRY(make_tmap_2d(&mk, c.k, c.dtype, width, rows, c.ld_qkv, 64, kTileRows));
     TSFM_TRY(make_tmap_2d(&mv, c.v, c.dtype, width, rows, c.ld_qkv, 64, kTileRows));
-    // Output rows per group: a query tile that runs past n is clipped at the group's end.
-    TSFM_TRY(make_tmap_grouped_rows(&mo, c.o, c.dtype, width, c.n, c.groups, c.ld_o, 64, kTileRows));
+    // Output rows per group: a query tile that runs past n is clipped at the group's end. (An FP32
+    // output is written by the softmax threads; the map is then never used.)
+    if (c.o32 == nullptr)
+        TSFM_TRY(make_tmap_grouped_rows(&mo, c.o, c.dtype, width, c.n, c.groups, c.ld_o, 64, kTileRows));
+    else
+        mo = mq;
     TcParams p;
     p.key_valid = c.key_valid;
     p.kvs = c.kv_stride > 0 ? c.kv_stride : c.n;
@@ -647,6 +775,13 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     p.o8 = static_cast<uint8_t *>(c.o8);
     p.ld_o8 = c.ld_o8;
     p.o8_half = width;
+    p.mode = c.mask_mode;
+    p.ne = c.mask_mode == 0 ? c.n : c.ne;
+    p.l = c.l;
+    p.bidir = c.group_bidir;
+    p.bidir_all = c.mask_mode == 2 ? 1 : 0;
+    p.o32 = c.o32;
+    p.ld_o32 = c.ld_o32;
     if (c.o8 && (c.dtype != E_F16 || c.ld_o8 % 16 || c.ld_o8 < 2 * width || (reinterpret_cast<uintptr_t>(c.o8) & 15)))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: an FP8 companion needs an FP16 output");
     const int64_t grid = std::min<int64_t>((p.items + 1) / 2, num_sms());

@@ -807,6 +807,47 @@ int32_t tsfm_kernel_timestral_block_inputs(const float *ctx, const uint8_t *obse
     });
 }
 
+int32_t tsfm_kernel_attention_ex(const void *q, const void *k, const void *v, int64_t ld_qkv, void *o, int64_t ld_o,
+                                 float *o32, int64_t ld_o32, const uint8_t *key_valid, int64_t kv_stride,
+                                 const uint8_t *group_bidir, int32_t groups, int32_t heads, int32_t n, float scale,
+                                 int32_t mask_mode, int32_t ne, int32_t l, int32_t dtype, int32_t force_path,
+                                 void *stream) {
+    return guarded([&]() -> Status {
+        if (!q || !k || !v || (!o && !o32)) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        if (mask_mode < 0 || mask_mode > 2) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "bad mask_mode");
+        if (force_path < 0 || force_path > 2) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "bad force_path");
+        if (mask_mode != 0 && (ne < 0 || ne > n || l < 0 || l > ne))
+            return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: need 0 <= l <= ne <= n");
+        if (dtype != TSFM_DTYPE_BF16 && dtype != TSFM_DTYPE_F16)
+            return Status::fail(TSFM_ERR_UNSUPPORTED_DTYPE, "attention: q/k/v must be BF16 or F16");
+        AttentionCall c;
+        c.q = q;
+        c.k = k;
+        c.v = v;
+        c.ld_qkv = ld_qkv;
+        c.o = o;
+        c.ld_o = ld_o;
+        c.o32 = o32;
+        c.ld_o32 = ld_o32;
+        c.key_valid = key_valid;
+        c.kv_stride = kv_stride > 0 ? kv_stride : n;
+        c.group_bidir = group_bidir;
+        c.groups = groups;
+        c.heads = heads;
+        c.n = n;
+        c.scale = scale;
+        c.mask_mode = mask_mode;
+        c.dtype = dtype == TSFM_DTYPE_F16 ? E_F16 : E_BF16;
+        c.ne = mask_mode == 0 ? n : ne;
+        c.l = mask_mode == 0 ? n : l;
+        c.force_path = force_path;
+        c.err = kernel_err_word();
+        if (force_path == 1 && !attention_tc_supported(c))
+            return Status::fail(TSFM_ERR_UNSUPPORTED, "attention: the tcgen05 path does not take this call");
+        return launch_attention(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
 int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64_t ld_qkv, void *o, int64_t ld_o,
                               const uint8_t *key_valid, const float *rel_bias, int32_t groups, int32_t heads, int32_t n,
                               float scale, int32_t mask_mode, int32_t dtype, void *stream) {

@@ -153,8 +153,8 @@ struct AttentionCall {
     // call the tcgen05 path does not take fails rather than leave it unwritten).
     void *o8 = nullptr;
     int64_t ld_o8 = 0;
-    // FP32 output instead of o (row stride ld_o32; the mma.sync path, which then runs every mask
-    // mode): for a corrected product whose input is formed after the attention (an output gate).
+    // FP32 output instead of o (row stride ld_o32, 16-byte aligned rows on the tcgen05 path): for a
+    // corrected product whose input is formed after the attention (an output gate).
     float *o32 = nullptr;
     int64_t ld_o32 = 0;
 };
