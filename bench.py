@@ -955,6 +955,7 @@ def main():
         if fast:
             line["f16_mode"] = {"value": fast["value"], "e2e": fast["e2e"], "ms_per_step": fast["ms_per_step"],
                                 "tc_peak_frac": fast["tc_peak_frac"], "gemm_tflops": fast["gemm_tflops"],
+                                "kernels": fast["kernels"],
                                 "parity": "single-pass FP16 operands: quantile tails exceed 1e-2 * sigma here"}
         if multi:
             line["library_multi_gpu"] = multi
