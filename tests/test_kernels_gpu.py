@@ -186,16 +186,19 @@ def test_attention_matches_float64_reference(n, mode, with_rel, dtype):
     assert err < (3e-2 if dtype == "bf16" else 5e-3), err
 
 
-@pytest.mark.parametrize("n,with_rel", [(1, False), (17, False), (128, False), (129, False), (256, False),
-                                        (257, False), (640, False), (1100, False), (1, True), (17, True), (130, True),
-                                        (257, True), (512, True), (513, True)])
+@pytest.mark.parametrize("n,with_rel", [(1, False), (17, False), (128, False), (129, False), (132, False),
+                                        (133, False), (256, False), (257, False), (640, False), (1100, False),
+                                        (1, True), (17, True), (129, True), (130, True), (257, True), (512, True),
+                                        (513, True)])
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 def test_attention_tcgen05_path_edges(n, with_rel, dtype):
     """The tcgen05 kernel (key-validity mask; relative-position bias up to n = 512, the mma.sync
     kernel beyond): one and two query tiles per CTA, partial key tiles, the K / V rings wrapping
     many times, a group without valid keys (uniform), a group whose first 300 keys are invalid
     (rows start with an empty max), and scores that grow by more than 2^8 per key tile so the lazy
-    O / row-sum rescale runs on every tile."""
+    O / row-sum rescale runs on every tile. n = 128 k + 1..4 (129, 132, 257) runs the key-tail
+    instance (the last keys in the softmax threads, the largest scores of the growing group among
+    them); 133 the plain one."""
     heads, G = 2, 4
     gen = torch.Generator().manual_seed(1000 + n)
     ld = 3 * heads * 64
@@ -284,7 +287,7 @@ def test_attention_timestral_masks_both_paths(n, ne, l, mode, out32, dtype):
         o32 = torch.full((G * n, heads * 64), float("nan"), device=dev(), dtype=torch.float32) if out32 else None
         tb.check(tb.lib.tsfm_kernel_attention_ex(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, None if out32 else o.data_ptr(), heads * 64,
-            o32.data_ptr() if out32 else None, heads * 64, kvd.data_ptr(), ne,
+            o32.data_ptr() if out32 else None, heads * 64, None, 0, kvd.data_ptr(), ne,
             bidird.data_ptr(), G, heads, n, scale, mode, ne, l, CODE16[TORCH16[dtype]], path, stream_ptr()))
         torch.cuda.synchronize()
         outs[path] = (o32 if out32 else o).double().cpu()
@@ -293,6 +296,40 @@ def test_attention_timestral_masks_both_paths(n, ne, l, mode, out32, dtype):
         assert err < (3e-2 if dtype == "bf16" else 5e-3), (path, err)
     if out32:
         assert (outs[1] - outs[2]).abs().max().item() < (3e-2 if dtype == "bf16" else 5e-3)
+
+
+@pytest.mark.parametrize("n", [1, 129, 577])
+def test_attention_fp8_companion(n):
+    """The tcgen05 kernel's FP8 companion of its FP16 output (corrected products), bit for bit:
+    with x the kernel's FP32 output (the same launch with an FP32 output), the FP16 output is
+    f16(x) and the companion [e4m3(f16(x) / 32) | e4m3((x - f16(x)) * 128)]."""
+    from helpers import e4m3_bits
+    heads, G = 2, 3
+    gen = torch.Generator().manual_seed(77 + n)
+    ld = 3 * heads * 64
+    qkv = (torch.randn(G * n, ld, generator=gen) * 0.7).half().to(dev())
+    q, k, v = qkv[:, :heads * 64], qkv[:, heads * 64:2 * heads * 64], qkv[:, 2 * heads * 64:]
+    kv = (torch.rand(G, n, generator=gen) > 0.2).to(torch.uint8)
+    kv[:, 0] = 1
+    kvd = kv.to(dev())
+    width = heads * 64
+    o = torch.empty(G * n, width, device=dev(), dtype=torch.float16)
+    o8 = torch.zeros(G * n, 2 * width, device=dev(), dtype=torch.uint8)
+    o32 = torch.empty(G * n, width, device=dev(), dtype=torch.float32)
+    for out, out32, out8 in ((o, None, o8), (None, o32, None)):
+        tb.check(tb.lib.tsfm_kernel_attention_ex(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, None if out is None else out.data_ptr(), width,
+            None if out32 is None else out32.data_ptr(), width, None if out8 is None else out8.data_ptr(), 2 * width,
+            kvd.data_ptr(), n, None, G, heads, n, 0.125, 0, n, n, F16, 1, stream_ptr()))
+    torch.cuda.synchronize()
+    x = o32.cpu().numpy()
+    xh = x.astype(np.float16).astype(np.float32)
+    assert np.array_equal(o.float().cpu().numpy(), xh)
+    b8 = o8.cpu().numpy()
+    assert np.array_equal(b8[:, :width], e4m3_bits(xh * np.float32(1 / 32)))
+    assert np.array_equal(b8[:, width:], e4m3_bits((x - xh) * np.float32(128)))
+    ref = attention_ref(q, k, v, kv, None, n, heads, 0.125, 0).numpy()
+    assert np.max(np.abs(x - ref)) < 5e-3
 
 
 def test_rmsnorm_matches_oracle():

@@ -59,6 +59,7 @@ constexpr int kMaxKeysRel = 512;                     // longest sequence with re
 constexpr int kRelWin = kMaxKeysRel + kTileRows;     // offsets one item's 128 query rows can see
 constexpr int kThreadsTc = 352;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kTailMax = 4;                // longest key tail folded into the softmax (mode 0)
 
 // Tile classes of a key tile. TILE_ROWS (Timestral's causal / decoder masks): the visible keys
 // depend on the query row; each softmax thread builds its row's bits from the validity bits.
@@ -118,6 +119,14 @@ struct TcParams {
     // FP32 output instead of the 16-bit one (row (g * n + i) at o32 + row * ld_o32, head h at h * 64).
     float *o32;
     int64_t ld_o32;
+    // Key tail (mode 0, n = 128 (T - 1) + tail with 1 <= tail <= kTailMax, e.g. Chronos-Bolt's 129
+    // tokens): the tensor cores cover the first T - 1 key tiles and the softmax threads the last
+    // `tail` keys (scores from the Q tile in shared memory and the key rows, their P V added to the
+    // output row when it is staged), so an item costs one key tile instead of two. tiles0: key
+    // tiles of a mode-0 item; k / v (16-bit, row stride ld): the tail keys' rows.
+    int tail, tiles0;
+    const uint16_t *kraw, *vraw;
+    int64_t ldraw;
 };
 
 // Key tiles an item reads: every tile in mode 0; in modes 1-2 the tiles up to the last key any of
@@ -127,7 +136,7 @@ __device__ __forceinline__ bool item_bidir(const TcParams &p, int g) {
     return p.mode != 0 && (p.bidir_all || (p.bidir != nullptr && p.bidir[g] != 0));
 }
 __device__ __forceinline__ int item_tiles(const TcParams &p, int g, int q0) {
-    if (p.mode == 0) return (p.n + kTileRows - 1) / kTileRows;
+    if (p.mode == 0) return p.tiles0;
     const int qhi = min(p.n, q0 + kTileRows);
     const int kv_end = item_bidir(p, g) ? max(p.ne, qhi) : qhi;
     return (kv_end + kTileRows - 1) / kTileRows;
@@ -147,6 +156,14 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
         __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
         return *reinterpret_cast<uint32_t *>(&h);
     }
+}
+
+template <bool F16>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+    if constexpr (F16)
+        return __half22float2(*reinterpret_cast<const __half2 *>(&u));
+    else
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u));
 }
 
 struct Item {
@@ -181,7 +198,8 @@ __device__ __forceinline__ void item_range(const TcParams &p, int64_t &first, in
 // 65,536. One CTA per SM (the shared memory and the 512 TMEM columns allow no second one).
 // O8: also writes the FP8 companion of the FP16 output (corrected products; a separate instance, so
 // the plain kernel keeps its registers).
-template <bool F16, bool O8 = false>
+// TAIL: the key-tail instance (TcParams::tail > 0; its extra registers stay out of the others).
+template <bool F16, bool O8 = false, bool TAIL = false>
 __global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, TcParams p) {
@@ -257,7 +275,8 @@ __global__ void __maxnreg__(168)
             // Modes 1-2: rows [i0, i1] of the item; a tile whose keys all lie below every row (or,
             // for a bidirectional group, hold no diagonal key) shows each row exactly the valid keys.
             const int i0 = im.q0, i1 = min(n, im.q0 + kTileRows) - 1;
-            for (int t = 0; t < Ti; ++t) {
+            const int Tb = p.mode == 0 ? T : Ti;  // mode 0: the tail tile's bits too
+            for (int t = 0; t < Tb; ++t) {
                 bool all_valid = true, prefix = true;
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
@@ -494,6 +513,9 @@ __global__ void __maxnreg__(168)
         // This warp's rows of the previous item still wait in TMEM (not past n).
         bool prev_live = false;
         Item prev_im{0, 0, 0};
+        float prev_pt[kTailMax];  // the previous item's tail probabilities (key tail)
+#pragma unroll
+        for (int t = 0; t < kTailMax; ++t) prev_pt[t] = 0.0f;
         // Reads this thread's row of the previous item's O, normalises it by the row sum and writes
         // it as 16-bit values into that item's Q buffer in the 128-byte-swizzled layout of a TMA
         // box (16-byte chunk c of row r at chunk c ^ (r % 8)).
@@ -514,7 +536,58 @@ __global__ void __maxnreg__(168)
                 float v[32];
                 tmem_ld32(t_o + 32 * h, v);
                 tmem_wait_ld();
-                if (row8 != nullptr) store_x8_32(row8, p.o8_half, (int64_t)prev_im.h * 64 + 32 * h, v, inv);
+                if (TAIL) {
+                    // O += P V over the key tail (rows of the previous item's group and head).
+#pragma unroll
+                    for (int t = 0; t < kTailMax; ++t) {
+                        if (t >= p.tail) break;
+                        const uint4 *vr = reinterpret_cast<const uint4 *>(
+                            p.vraw + ((int64_t)prev_im.g * n + (int64_t)(p.tiles0 * kTileRows + t)) * p.ldraw +
+                            prev_im.h * 64 + 32 * h);
+                        const float pt = prev_pt[t];
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const uint4 u = __ldg(vr + c);
+                            const float2 a = unpack2<F16>(u.x), b2 = unpack2<F16>(u.y), c2 = unpack2<F16>(u.z),
+                                         d = unpack2<F16>(u.w);
+                            v[8 * c + 0] = fmaf(pt, a.x, v[8 * c + 0]);
+                            v[8 * c + 1] = fmaf(pt, a.y, v[8 * c + 1]);
+                            v[8 * c + 2] = fmaf(pt, b2.x, v[8 * c + 2]);
+                            v[8 * c + 3] = fmaf(pt, b2.y, v[8 * c + 3]);
+                            v[8 * c + 4] = fmaf(pt, c2.x, v[8 * c + 4]);
+                            v[8 * c + 5] = fmaf(pt, c2.y, v[8 * c + 5]);
+                            v[8 * c + 6] = fmaf(pt, d.x, v[8 * c + 6]);
+                            v[8 * c + 7] = fmaf(pt, d.y, v[8 * c + 7]);
+                        }
+                    }
+                }
+                if (O8) {
+                    // The FP16 pairs serve the staged output and the companion's high parts.
+                    float x[32];
+                    uint32_t hp[16];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) x[i] = v[i] * inv;
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) hp[e] = pack_p<true>(x[2 * e], x[2 * e + 1]);
+                    if (row8 != nullptr) {
+                        uint32_t hi[8], lo[8];
+                        pack_x8_f16x2_32(x, hp, hi, lo);
+                        const int64_t col0 = (int64_t)prev_im.h * 64 + 32 * h;
+                        uint4 *ph = reinterpret_cast<uint4 *>(row8 + col0);
+                        uint4 *pl = reinterpret_cast<uint4 *>(row8 + p.o8_half + col0);
+                        ph[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        ph[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                        pl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        pl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int chunk = (4 * h + c) ^ (r & 7);
+                        *reinterpret_cast<uint4 *>(row + chunk * 16) =
+                            make_uint4(hp[4 * c], hp[4 * c + 1], hp[4 * c + 2], hp[4 * c + 3]);
+                    }
+                    continue;
+                }
                 if (p.o32 != nullptr) {
                     if (row32 != nullptr) {
 #pragma unroll
@@ -550,6 +623,9 @@ __global__ void __maxnreg__(168)
             const bool dead = im.q0 + quarter * 32 >= n;
             float m_run = -INFINITY, l_run = 0.0f;
             const int Ti = m.ntiles;
+            float pt[kTailMax];  // this item's tail probabilities (key tail)
+#pragma unroll
+            for (int t = 0; t < kTailMax; ++t) pt[t] = 0.0f;
             // Modes 1-2, this thread's row i: the visible keys of a TILE_ROWS tile are the valid keys
             // below A plus the keys in [B, C] (encoder row: A = i + 1, or ne for a bidirectional
             // group, and B = C = i, the diagonal; decoder row: A = l, B = ne, C = i).
@@ -566,6 +642,59 @@ __global__ void __maxnreg__(168)
                 }
             }
             for (int j = 0; j < Ti; ++j, ++cx) {
+                // Key tail: this row's scores of the tail keys (raw units, like S), computed from the
+                // item's Q tile in shared memory before waiting for the last S; -inf when masked.
+                float st[kTailMax];
+                const bool tail_here = TAIL && j == Ti - 1 && !dead;
+                if constexpr (TAIL) {
+                    bool q_ok = true;
+                    if (tail_here) {
+                        // The item's Q tile has landed (its load's barrier phase, observed here so the
+                        // TMA-written bytes are visible to these loads).
+                        q_ok = mbar_wait(&b.q_full[slot], (wi >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
+                    }
+                    if (!__all_sync(0xffffffffu, q_ok)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                if (tail_here) {
+#pragma unroll
+                    for (int t = 0; t < kTailMax; ++t) st[t] = 0.0f;
+                    const uint8_t *qrow = smem + q * PIPE_BYTES + OFF_Q + slot * kTileBytes + r * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + ((c ^ (r & 7)) << 4));
+                        const float2 q0 = unpack2<F16>(qa.x), q1 = unpack2<F16>(qa.y), q2 = unpack2<F16>(qa.z),
+                                     q3 = unpack2<F16>(qa.w);
+#pragma unroll
+                        for (int t = 0; t < kTailMax; ++t) {
+                            if (t >= p.tail) break;
+                            const uint4 ka = __ldg(reinterpret_cast<const uint4 *>(
+                                                       p.kraw + ((int64_t)im.g * n + (int64_t)(p.tiles0 * kTileRows + t)) * p.ldraw +
+                                                       im.h * 64) + c);
+                            const float2 k0 = unpack2<F16>(ka.x), k1 = unpack2<F16>(ka.y), k2 = unpack2<F16>(ka.z),
+                                         k3 = unpack2<F16>(ka.w);
+                            float a = st[t];
+                            a = fmaf(q0.x, k0.x, a);
+                            a = fmaf(q0.y, k0.y, a);
+                            a = fmaf(q1.x, k1.x, a);
+                            a = fmaf(q1.y, k1.y, a);
+                            a = fmaf(q2.x, k2.x, a);
+                            a = fmaf(q2.y, k2.y, a);
+                            a = fmaf(q3.x, k3.x, a);
+                            a = fmaf(q3.y, k3.y, a);
+                            st[t] = a;
+                        }
+                    }
+                    const uint32_t tb = m.bits[4 * p.tiles0];
+#pragma unroll
+                    for (int t = 0; t < kTailMax; ++t) {
+                        float x = st[t];
+                        if (p.rel) x += m.rel[p.tiles0 * kTileRows + t - r + (kTileRows - 1)];
+                        st[t] = t >= p.tail ? -INFINITY : uniform ? 0.0f : ((tb >> t) & 1u) ? x : -INFINITY;
+                    }
+                }
                 const bool got = mbar_wait(&b.s_full, cx & 1, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
@@ -641,7 +770,11 @@ __global__ void __maxnreg__(168)
                 float mxp[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
                 for (int i = 4; i + 1 < 124; i += 2) mxp[(i >> 1) & 3] = max3(mxp[(i >> 1) & 3], s[i], s[i + 1]);
-                const float mx = max3(max3(mxp[0], mxp[1], mxp[2]), max3(mxp[3], s[124], s[125]), fmaxf(s[126], s[127]));
+                float mx = max3(max3(mxp[0], mxp[1], mxp[2]), max3(mxp[3], s[124], s[125]), fmaxf(s[126], s[127]));
+                if (tail_here) {
+#pragma unroll
+                    for (int t = 0; t < kTailMax; ++t) mx = fmaxf(mx, st[t]);
+                }
                 // Lazy rescale: keep the stale max unless the new one exceeds it by 2^8.
                 const float m_new = fmaxf(m_run, mx);
                 float alpha = 1.0f;
@@ -684,6 +817,13 @@ __global__ void __maxnreg__(168)
                     }
                     tmem_st16(t_p + 16 * qc, pk);
                 }
+                if (tail_here) {
+#pragma unroll
+                    for (int t = 0; t < kTailMax; ++t) {
+                        pt[t] = ex2_approx(fmaf(st[t], sl2, -mb));
+                        sp4[t & 3] += pt[t];
+                    }
+                }
                 l_run = l_run * alpha + ((sp4[0] + sp4[1]) + (sp4[2] + sp4[3]));
                 if (j > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll
@@ -705,6 +845,8 @@ __global__ void __maxnreg__(168)
             mbar_arrive(&b.m_empty[slot]);
             prev_live = !dead;
             prev_im = im;
+#pragma unroll
+            for (int t = 0; t < kTailMax; ++t) prev_pt[t] = pt[t];
             *l_save = l_run;
         }
         // The last item's output, once its last PV is done; one more p_ready phase tells the
@@ -782,15 +924,28 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     p.bidir_all = c.mask_mode == 2 ? 1 : 0;
     p.o32 = c.o32;
     p.ld_o32 = c.ld_o32;
+    const int T = (c.n + kTileRows - 1) / kTileRows;
+    const int rem = c.n - (T - 1) * kTileRows;
+    p.tail = c.mask_mode == 0 && T >= 2 && rem <= kTailMax && c.o8 == nullptr && c.o32 == nullptr ? rem : 0;
+    p.tiles0 = T - (p.tail > 0 ? 1 : 0);
+    p.kraw = static_cast<const uint16_t *>(c.k);
+    p.vraw = static_cast<const uint16_t *>(c.v);
+    p.ldraw = c.ld_qkv;
     if (c.o8 && (c.dtype != E_F16 || c.ld_o8 % 16 || c.ld_o8 < 2 * width || (reinterpret_cast<uintptr_t>(c.o8) & 15)))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: an FP8 companion needs an FP16 output");
     const int64_t grid = std::min<int64_t>((p.items + 1) / 2, num_sms());
     if (c.dtype == E_F16 && c.o8) {
         TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<true, true>), kSmemTc));
         attn_tc_kernel<true, true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
+    } else if (c.dtype == E_F16 && p.tail > 0) {
+        TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<true, false, true>), kSmemTc));
+        attn_tc_kernel<true, false, true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
     } else if (c.dtype == E_F16) {
         TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<true>), kSmemTc));
         attn_tc_kernel<true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
+    } else if (p.tail > 0) {
+        TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<false, false, true>), kSmemTc));
+        attn_tc_kernel<false, false, true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
     } else {
         TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<false>), kSmemTc));
         attn_tc_kernel<false><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);

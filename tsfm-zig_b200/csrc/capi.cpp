@@ -808,7 +808,8 @@ int32_t tsfm_kernel_timestral_block_inputs(const float *ctx, const uint8_t *obse
 }
 
 int32_t tsfm_kernel_attention_ex(const void *q, const void *k, const void *v, int64_t ld_qkv, void *o, int64_t ld_o,
-                                 float *o32, int64_t ld_o32, const uint8_t *key_valid, int64_t kv_stride,
+                                 float *o32, int64_t ld_o32, uint8_t *o8, int64_t ld_o8, const uint8_t *key_valid,
+                                 int64_t kv_stride,
                                  const uint8_t *group_bidir, int32_t groups, int32_t heads, int32_t n, float scale,
                                  int32_t mask_mode, int32_t ne, int32_t l, int32_t dtype, int32_t force_path,
                                  void *stream) {
@@ -829,6 +830,8 @@ int32_t tsfm_kernel_attention_ex(const void *q, const void *k, const void *v, in
         c.ld_o = ld_o;
         c.o32 = o32;
         c.ld_o32 = ld_o32;
+        c.o8 = o8;
+        c.ld_o8 = ld_o8;
         c.key_valid = key_valid;
         c.kv_stride = kv_stride > 0 ? kv_stride : n;
         c.group_bidir = group_bidir;

@@ -342,6 +342,13 @@ __device__ __forceinline__ uint32_t e4m3x2(float first, float second) {
     return r;
 }
 
+// The same from a packed pair of FP16 values (the low half to the low byte).
+__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t h2) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(h2));
+    return r;
+}
+
 // Arrives on `bar` once all previously issued tcgen05 operations of this thread complete.
 // D (TMEM of both CTAs, 128 rows each) += A (128 rows from each CTA's shared memory) * B (N / 2
 // rows from each CTA's shared memory); issued by one thread of the pair's first CTA.

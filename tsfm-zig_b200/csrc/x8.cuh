@@ -28,6 +28,27 @@ __device__ __forceinline__ void pack_x8_32(const float *v, uint32_t (&hi)[8], ui
     }
 }
 
+// pack_x8_32 for values whose FP16 roundings are already packed: x[j] (FP32) and h[e] = the FP16
+// pair (x[2e], x[2e + 1]), low half first. The high parts scale the FP16 pair by 1/32 in FP16 and
+// convert it directly: exact for results in FP16's normal range, and below it (|f16(x)| < 2^-9)
+// both routes give E4M3 zero, so the bytes equal pack_x8_32's.
+__device__ __forceinline__ void pack_x8_f16x2_32(const float *x, const uint32_t *h, uint32_t (&hi)[8],
+                                                 uint32_t (&lo)[8]) {
+    const __half2 k = __float2half2_rn(kX8HiScale);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const uint32_t a = h[2 * q], b = h[2 * q + 1];
+        const __half2 sa = __hmul2(*reinterpret_cast<const __half2 *>(&a), k);
+        const __half2 sb = __hmul2(*reinterpret_cast<const __half2 *>(&b), k);
+        hi[q] = e4m3x2_f16x2(*reinterpret_cast<const uint32_t *>(&sa)) |
+                (e4m3x2_f16x2(*reinterpret_cast<const uint32_t *>(&sb)) << 16);
+        const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&a));
+        const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&b));
+        lo[q] = e4m3x2((x[4 * q] - fa.x) * kX8LoScale, (x[4 * q + 1] - fa.y) * kX8LoScale) |
+                (e4m3x2((x[4 * q + 2] - fb.x) * kX8LoScale, (x[4 * q + 3] - fb.y) * kX8LoScale) << 16);
+    }
+}
+
 // The companion of 32 values of one row written to global memory: row8[col0 + j] = hi byte j,
 // row8[half + col0 + j] = lo byte j, with 16-byte stores (row8 + col0 and row8 + half + col0
 // 16-byte aligned).
