@@ -379,12 +379,15 @@ int32_t tsfm_kernel_attention(const void *q, const void *k, const void *v, int64
  * queries i >= ne decoder rows reading the valid keys below l plus their chain [ne, i]; key_valid
  * has row stride kv_stride (0: n). o32 (row stride ld_o32 floats), when not null, receives an FP32
  * output instead of o. o8 (row stride ld_o8 bytes), when not null, receives the FP8 companion of
- * the FP16 output (tcgen05 kernel; the layout of tsfm_kernel_split_f16c's x8). force_path: 0
- * automatic, 1 the tcgen05 kernel (UNSUPPORTED if it cannot take the call), 2 the mma.sync kernel. */
+ * the FP16 output (tcgen05 kernel; the layout of tsfm_kernel_split_f16c's x8). rel_bias as in
+ * tsfm_kernel_attention (mode 0). force_path: 0 automatic, 1 the tcgen05 kernel (UNSUPPORTED if it
+ * cannot take the call), 2 the mma.sync kernel, 3 the tcgen05 kernel with two softmax threads per
+ * query row. */
 int32_t tsfm_kernel_attention_ex(const void *q, const void *k, const void *v, int64_t ld_qkv,
                                  void *o, int64_t ld_o, float *o32, int64_t ld_o32, uint8_t *o8,
                                  int64_t ld_o8, const uint8_t *key_valid, int64_t kv_stride,
-                                 const uint8_t *group_bidir, int32_t groups, int32_t heads, int32_t n,
+                                 const float *rel_bias, const uint8_t *group_bidir, int32_t groups,
+                                 int32_t heads, int32_t n,
                                  float scale, int32_t mask_mode, int32_t ne, int32_t l,
                                  int32_t dtype, int32_t force_path, void *stream);
 

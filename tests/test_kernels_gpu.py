@@ -233,6 +233,53 @@ def test_attention_tcgen05_path_edges(n, with_rel, dtype):
     assert err < (3e-2 if dtype == "bf16" else 5e-3), err
 
 
+@pytest.mark.parametrize("n,with_rel", [(1, False), (129, False), (256, False), (577, False), (1100, False),
+                                        (17, True), (129, True), (257, True)])
+@pytest.mark.parametrize("o8", [False, True])
+def test_attention_split_rows(n, with_rel, o8):
+    """The tcgen05 kernel with two softmax threads per query row (force_path 3): the groups of the
+    edge test (uniform, leading invalid keys, scores growing past the rescale threshold on every
+    tile), against float64, with and without the FP8 companion output."""
+    from helpers import e4m3_bits
+    heads, G = 2, 4
+    gen = torch.Generator().manual_seed(2000 + n)
+    ld = 3 * heads * 64
+    qkv = torch.randn(G * n, ld, generator=gen) * 0.5
+    u = torch.randn(64, generator=gen)
+    u = u / u.norm()
+    for h in range(heads):
+        rows = slice(3 * n, 4 * n)
+        qkv[rows, h * 64:(h + 1) * 64] += 2.0 * u
+        ramp = (0.05 * torch.arange(n, dtype=torch.float32))[:, None] * u[None, :]
+        qkv[rows, heads * 64 + h * 64:heads * 64 + (h + 1) * 64] += ramp
+    qkv = qkv.half().to(dev())
+    q, k, v = qkv[:, :heads * 64], qkv[:, heads * 64:2 * heads * 64], qkv[:, 2 * heads * 64:]
+    kv = (torch.rand(G, n, generator=gen) > 0.3).to(torch.uint8)
+    kv[1, :] = 0
+    kv[2, :min(n, 300)] = 0
+    if n > 300:
+        kv[2, 300] = 1
+    kv[3, :] = 1
+    rel = torch.randn(heads, 2 * n - 1, generator=gen) * 2 if with_rel else None
+    reld = rel.to(dev()) if with_rel else None
+    kvd = kv.to(dev())
+    width = heads * 64
+    o = torch.full((G * n, width), float("nan"), device=dev(), dtype=torch.float16)
+    o8b = torch.zeros(G * n, 2 * width, device=dev(), dtype=torch.uint8) if o8 else None
+    tb.check(tb.lib.tsfm_kernel_attention_ex(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, o.data_ptr(), width, None, 0,
+        o8b.data_ptr() if o8 else None, 2 * width, kvd.data_ptr(), n, None if reld is None else reld.data_ptr(),
+        None, G, heads, n, 1.0, 0, n, n, F16, 3, stream_ptr()))
+    torch.cuda.synchronize()
+    got = o.double().cpu()
+    assert torch.isfinite(got).all()
+    ref = attention_ref(q, k, v, kv, rel, n, heads, 1.0, 0)
+    assert (got - ref).abs().max().item() < 5e-3
+    if o8:
+        xh = o.float().cpu().numpy()
+        assert np.array_equal(o8b.cpu().numpy()[:, :width], e4m3_bits(xh * np.float32(1 / 32)))
+
+
 def timestral_attention_ref(q, k, v, kv, bidir, n, heads, scale, ne, l):
     """float64 restatement of Timestral's time-attention masks (timestral/model.zig:558-635):
     encoder queries i < ne see j < ne with j == i or (valid(j) and (bidirectional or j <= i));
@@ -262,9 +309,10 @@ def timestral_attention_ref(q, k, v, kv, bidir, n, heads, scale, ne, l):
 @pytest.mark.parametrize("out32", [False, True])
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 def test_attention_timestral_masks_both_paths(n, ne, l, mode, out32, dtype):
-    """Timestral's causal / bidirectional / decoder-chain masks on the tcgen05 kernel (force_path 1)
-    and the mma.sync kernel (force_path 2), 16-bit and FP32 outputs, against float64: groups with
-    per-group bidirectional rows, invalid keys everywhere but the diagonal, and decoder rows."""
+    """Timestral's causal / bidirectional / decoder-chain masks on the tcgen05 kernel (force_path 1,
+    and 3: two softmax threads per row) and the mma.sync kernel (force_path 2), 16-bit and FP32
+    outputs, against float64: groups with per-group bidirectional rows, invalid keys everywhere but
+    the diagonal, and decoder rows."""
     heads, G = 2, 5
     gen = torch.Generator().manual_seed(7 * n + ne + l + mode)
     ld = 3 * heads * 64 + 8
@@ -282,12 +330,12 @@ def test_attention_timestral_masks_both_paths(n, ne, l, mode, out32, dtype):
     ref = timestral_attention_ref(q, k, v, kv_full, bidir, n, heads, scale, ne, l)
     kvd, bidird = kv.to(dev()), bidir.to(dev())  # kept alive until the kernels have run
     outs = {}
-    for path in (1, 2):
+    for path in (1, 2, 3):
         o = torch.full((G * n, heads * 64), float("nan"), device=dev(), dtype=TORCH16[dtype])
         o32 = torch.full((G * n, heads * 64), float("nan"), device=dev(), dtype=torch.float32) if out32 else None
         tb.check(tb.lib.tsfm_kernel_attention_ex(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, None if out32 else o.data_ptr(), heads * 64,
-            o32.data_ptr() if out32 else None, heads * 64, None, 0, kvd.data_ptr(), ne,
+            o32.data_ptr() if out32 else None, heads * 64, None, 0, kvd.data_ptr(), ne, None,
             bidird.data_ptr(), G, heads, n, scale, mode, ne, l, CODE16[TORCH16[dtype]], path, stream_ptr()))
         torch.cuda.synchronize()
         outs[path] = (o32 if out32 else o).double().cpu()
@@ -320,7 +368,7 @@ def test_attention_fp8_companion(n):
         tb.check(tb.lib.tsfm_kernel_attention_ex(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, None if out is None else out.data_ptr(), width,
             None if out32 is None else out32.data_ptr(), width, None if out8 is None else out8.data_ptr(), 2 * width,
-            kvd.data_ptr(), n, None, G, heads, n, 0.125, 0, n, n, F16, 1, stream_ptr()))
+            kvd.data_ptr(), n, None, None, G, heads, n, 0.125, 0, n, n, F16, 1, stream_ptr()))
     torch.cuda.synchronize()
     x = o32.cpu().numpy()
     xh = x.astype(np.float16).astype(np.float32)

@@ -263,7 +263,7 @@ Status launch_attention(const AttentionCall &c, cudaStream_t stream) {
     // sequences (n <= 256: at Timestral's 160 tokens the mma.sync kernel is ≈ 20 % faster, the
     // tcgen05 kernel's per-item cost dominating; at 577 tokens the tcgen05 kernel is 1.8x faster).
     const bool tc_pref = c.mask_mode == 0 || c.n > 256 || c.o8 != nullptr;
-    if (c.force_path == 1 || (c.force_path == 0 && tc_pref && attention_tc_supported(c)))
+    if (c.force_path == 1 || c.force_path == 3 || (c.force_path == 0 && tc_pref && attention_tc_supported(c)))
         return launch_attention_tc(c, stream);
     if (c.o32 && (c.ld_o32 % 2 || (reinterpret_cast<uintptr_t>(c.o32) & 7)))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: FP32 output needs 8-byte alignment");

@@ -92,7 +92,12 @@ constexpr int OFF_BAR = OFF_MASK + 4 * (int)sizeof(MaskSlot);
 constexpr int kBarsPerPipe = 18;
 constexpr int OFF_LSUM = OFF_BAR + (2 * kBarsPerPipe + 2) * 8;  // [pipeline][row] row sums
 constexpr int OFF_MISC = OFF_LSUM + 2 * kTileRows * 4;
-constexpr int kSmemTc = OFF_MISC + 64 + 1024;    // + alignment slack
+// Split rows (SPLIT instances): the two threads of a row exchange partial row maxima and sums through
+// double-buffered slots [slot][pipeline][quarter][half][lane], one mbarrier per (pipeline, quarter).
+constexpr int OFF_XBAR = OFF_MISC + 64;
+constexpr int OFF_XBUF = OFF_XBAR + 8 * 8;
+constexpr int kSmemTc = OFF_XBUF + 2 * 2 * 4 * 2 * 32 * 4 + 1024;  // + alignment slack
+constexpr int kThreadsSplit = (16 + 3) * 32;
 
 // TMEM columns of pipeline p (base p * 256): S (128 FP32), P (64 columns = 128 16-bit), O (64).
 constexpr uint32_t kTmemCols = 512;
@@ -194,15 +199,21 @@ __device__ __forceinline__ void item_range(const TcParams &p, int64_t &first, in
     last = p.items * (blockIdx.x + 1) / gridDim.x;
 }
 
-// Registers are allocated for warps in groups of four; 12 warps x 32 x 168 = 64,512 of the SM's
-// 65,536. One CTA per SM (the shared memory and the 512 TMEM columns allow no second one).
-// O8: also writes the FP8 companion of the FP16 output (corrected products; a separate instance, so
-// the plain kernel keeps its registers).
-// TAIL: the key-tail instance (TcParams::tail > 0; its extra registers stay out of the others).
-template <bool F16, bool O8 = false, bool TAIL = false>
-__global__ void __maxnreg__(168)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, TcParams p) {
+// The kernel body. O8: also writes the FP8 companion of the FP16 output (corrected products; a
+// separate instance, so the plain kernel keeps its registers). TAIL: the key-tail instance
+// (TcParams::tail > 0). SPLIT: two softmax threads per query row (16 softmax warps: warp w of a
+// pipeline reads TMEM lanes 32 (w % 4) and keys 64 (w / 4) .. + 63 of each tile; the pair
+// exchanges its partial row maximum every tile and its partial row sum every item), so twice the
+// warps share the exponentials and every chain is half as long.
+template <bool F16, bool O8, bool TAIL, bool SPLIT>
+__device__ __forceinline__ void attn_tc_body(const CUtensorMap &tmQ, const CUtensorMap &tmK, const CUtensorMap &tmV,
+                                             const CUtensorMap &tmO, const TcParams &p) {
+    static_assert(!(TAIL && SPLIT), "the key tail runs on whole rows");
+    constexpr int NSW = SPLIT ? 16 : 8;       // softmax warps (warps 0 .. NSW - 1)
+    constexpr int W_MMA = NSW;                // warps NSW, NSW + 1: tensor-core threads of pipelines 0, 1
+    constexpr int W_MASK = NSW + 2;           // the mask warp
+    constexpr int PIPE_W = NSW / 2;           // softmax warps per pipeline
+    constexpr uint32_t SM_ARRIVALS = PIPE_W * 32;
     constexpr uint32_t FMT = F16 ? 0u : 1u;
     constexpr uint32_t IDESC_S = idesc_f32acc(FMT, 128, 128);
     constexpr uint32_t IDESC_PV = idesc_f32acc(FMT, 128, 64) | (1u << 16);  // B (V) is MN-major
@@ -231,13 +242,17 @@ __global__ void __maxnreg__(168)
                 mbar_init(&b.v_full[i], 1);
                 mbar_init(&b.v_empty[i], 1);
                 mbar_init(&b.m_full[i], 32);
-                mbar_init(&b.m_empty[i], 128);
+                mbar_init(&b.m_empty[i], SM_ARRIVALS);
             }
             mbar_init(&b.s_full, 1);
-            mbar_init(&b.s_free, 128);
-            mbar_init(&b.p_ready, 128);
+            mbar_init(&b.s_free, SM_ARRIVALS);
+            mbar_init(&b.p_ready, SM_ARRIVALS);
             mbar_init(&b.o_done, 1);
             mbar_init(&drain[q], 1);
+        }
+        if constexpr (SPLIT) {
+            uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + OFF_XBAR);
+            for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 64);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -246,7 +261,7 @@ __global__ void __maxnreg__(168)
         tma_prefetch_desc(&tmV);
         tma_prefetch_desc(&tmO);
     }
-    if (warp == 8) {
+    if (warp == W_MMA) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
@@ -255,7 +270,7 @@ __global__ void __maxnreg__(168)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 10) {
+    if (warp == W_MASK) {
         // ---- key masks of the coming items, in item order ----
         uint32_t wi[2] = {0, 0};
         for (int64_t it = first; it < last; ++it) {
@@ -319,10 +334,10 @@ __global__ void __maxnreg__(168)
             __syncwarp();
             mbar_arrive(&b.m_full[slot]);
         }
-    } else if (warp == 8 || warp == 9) {
-        // ---- tensor-core thread of pipeline warp - 8: MMAs and TMA transfers ----
+    } else if (warp == W_MMA || warp == W_MMA + 1) {
+        // ---- tensor-core thread of pipeline warp - W_MMA: MMAs and TMA transfers ----
         if (lane == 0) {
-            const int q = warp - 8;
+            const int q = warp - W_MMA;
             PipeBars &b = pb[q];
             uint8_t *base = smem + q * PIPE_BYTES;
             const uint32_t t_s = tmem_base + q * 256 + TM_S, t_p = tmem_base + q * 256 + TM_P;
@@ -496,18 +511,37 @@ __global__ void __maxnreg__(168)
                 }
             }
         }
-    } else if (warp < 8) {
-        // ---- softmax of pipeline warp / 4 ----
-        const int q = warp >> 2;
-        const int quarter = warp & 3;  // TMEM lane quarter
+    } else if (warp < NSW) {
+        // ---- softmax of pipeline warp / PIPE_W ----
+        constexpr int SC = SPLIT ? 64 : 128;  // keys of a tile per thread
+        constexpr int OC = SPLIT ? 32 : 64;   // output columns per thread
+        const int q = warp / PIPE_W;
+        const int wp = warp % PIPE_W;
+        const int quarter = wp & 3;  // TMEM lane quarter
+        const int half = SPLIT ? (wp >> 2) : 0;
+        const int kofs = half * SC;  // this thread's first key of a tile
         const int r = quarter * 32 + lane;
         PipeBars &b = pb[q];
         const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-        const uint32_t t_s = tmem_base + lanes + q * 256 + TM_S;
-        const uint32_t t_p = tmem_base + lanes + q * 256 + TM_P;
-        const uint32_t t_o = tmem_base + lanes + q * 256 + TM_O;
+        const uint32_t t_s = tmem_base + lanes + q * 256 + TM_S + kofs;
+        const uint32_t t_p = tmem_base + lanes + q * 256 + TM_P + kofs / 2;
+        const uint32_t t_o = tmem_base + lanes + q * 256 + TM_O + half * OC;
         const float sl2 = p.scale_log2;
         float *l_save = reinterpret_cast<float *>(smem + OFF_LSUM) + q * kTileRows + r;
+        float prev_ltot = 0.0f;  // SPLIT: the previous item's full row sum
+        // SPLIT: exchange a value with the row's other thread (bounded wait; false on abort).
+        uint32_t xph = 0;
+        float *xb = reinterpret_cast<float *>(smem + OFF_XBUF);
+        uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + OFF_XBAR) + q * 4 + quarter;
+        auto xchg = [&](float v, float &other) -> bool {
+            const int sl = (int)(xph & 1u);
+            xb[(((sl * 2 + q) * 4 + quarter) * 2 + half) * 32 + lane] = v;
+            mbar_arrive(xbar);
+            const bool got = mbar_wait(xbar, xph & 1u, abort_flag, p.err, ERR_SITE_ATTN_SOFTMAX);
+            other = xb[(((sl * 2 + q) * 4 + quarter) * 2 + (half ^ 1)) * 32 + lane];
+            ++xph;
+            return __all_sync(0xffffffffu, got);
+        };
         uint32_t cx = 0, wi = 0;  // tiles / items processed by this pipeline
         bool ok = true;
         // This warp's rows of the previous item still wait in TMEM (not past n).
@@ -520,7 +554,7 @@ __global__ void __maxnreg__(168)
         // it as 16-bit values into that item's Q buffer in the 128-byte-swizzled layout of a TMA
         // box (16-byte chunk c of row r at chunk c ^ (r % 8)).
         auto stage_prev_row = [&](uint32_t prev_slot) {
-            const float l = *l_save;
+            const float l = SPLIT ? prev_ltot : *l_save;
             const float inv = l > 0.0f ? __frcp_rn(l) : 0.0f;
             uint8_t *row = smem + q * PIPE_BYTES + OFF_Q + prev_slot * kTileBytes + r * 128;
             // The FP8 companion goes straight to global memory (rows past n are not written).
@@ -530,13 +564,14 @@ __global__ void __maxnreg__(168)
             // An FP32 output goes straight to global memory as well (no TMA store follows).
             float *row32 = nullptr;
             if (p.o32 != nullptr && prev_im.q0 + r < n)
-                row32 = p.o32 + ((int64_t)prev_im.g * n + prev_im.q0 + r) * p.ld_o32 + (int64_t)prev_im.h * 64;
+                row32 = p.o32 + ((int64_t)prev_im.g * n + prev_im.q0 + r) * p.ld_o32 + (int64_t)prev_im.h * 64 +
+                        half * OC;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < OC / 32; ++h) {
                 float v[32];
                 tmem_ld32(t_o + 32 * h, v);
                 tmem_wait_ld();
-                if (TAIL) {
+                if constexpr (TAIL) {
                     // O += P V over the key tail (rows of the previous item's group and head).
 #pragma unroll
                     for (int t = 0; t < kTailMax; ++t) {
@@ -572,7 +607,7 @@ __global__ void __maxnreg__(168)
                     if (row8 != nullptr) {
                         uint32_t hi[8], lo[8];
                         pack_x8_f16x2_32(x, hp, hi, lo);
-                        const int64_t col0 = (int64_t)prev_im.h * 64 + 32 * h;
+                        const int64_t col0 = (int64_t)prev_im.h * 64 + half * OC + 32 * h;
                         uint4 *ph = reinterpret_cast<uint4 *>(row8 + col0);
                         uint4 *pl = reinterpret_cast<uint4 *>(row8 + p.o8_half + col0);
                         ph[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
@@ -582,7 +617,7 @@ __global__ void __maxnreg__(168)
                     }
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        const int chunk = (4 * h + c) ^ (r & 7);
+                        const int chunk = (half * (OC / 8) + 4 * h + c) ^ (r & 7);
                         *reinterpret_cast<uint4 *>(row + chunk * 16) =
                             make_uint4(hp[4 * c], hp[4 * c + 1], hp[4 * c + 2], hp[4 * c + 3]);
                     }
@@ -599,7 +634,7 @@ __global__ void __maxnreg__(168)
                 }
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    const int chunk = (4 * h + c) ^ (r & 7);
+                    const int chunk = (half * (OC / 8) + 4 * h + c) ^ (r & 7);
                     *reinterpret_cast<uint4 *>(row + chunk * 16) =
                         make_uint4(pack_p<F16>(v[8 * c + 0] * inv, v[8 * c + 1] * inv),
                                    pack_p<F16>(v[8 * c + 2] * inv, v[8 * c + 3] * inv),
@@ -722,8 +757,18 @@ __global__ void __maxnreg__(168)
                     continue;
                 }
                 tc_fence_after();
-                float s[128];
-                {
+                float s[SC];
+                if constexpr (SPLIT) {
+                    float c0[32], c1[32];
+                    tmem_ld32(t_s + 0, c0);
+                    tmem_ld32(t_s + 32, c1);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        s[i] = c0[i];
+                        s[32 + i] = c1[i];
+                    }
+                } else {
                     float c0[32], c1[32], c2[32], c3[32];
                     tmem_ld32(t_s + 0, c0);
                     tmem_ld32(t_s + 32, c1);
@@ -741,39 +786,51 @@ __global__ void __maxnreg__(168)
                 tc_fence_before();
                 mbar_arrive(&b.s_free);
                 if (p.rel) {
-                    const float *rw = m.rel + j * kTileRows - r + (kTileRows - 1);
+                    const float *rw = m.rel + j * kTileRows + kofs - r + (kTileRows - 1);
 #pragma unroll
-                    for (int i = 0; i < 128; ++i) s[i] += rw[i];
+                    for (int i = 0; i < SC; ++i) s[i] += rw[i];
                 }
 
                 // Mask: valid prefix of the tile (keys below n), or per-key bits; uniform groups
                 // give every key below n the score 0.
                 const int cls = m.cls[j];
                 if (uniform || cls == TILE_PREFIX) {
-                    const int cnt = n - j * kTileRows;
+                    const int cnt = n - j * kTileRows - kofs;
                     const float keep = uniform ? 0.0f : 1.0f;
 #pragma unroll
-                    for (int i = 0; i < 128; ++i) s[i] = i < cnt ? s[i] * keep : -INFINITY;
+                    for (int i = 0; i < SC; ++i) s[i] = i < cnt ? s[i] * keep : -INFINITY;
                 } else if (cls == TILE_BITS || cls == TILE_ROWS) {
-                    uint32_t wd[4] = {m.bits[4 * j], m.bits[4 * j + 1], m.bits[4 * j + 2], m.bits[4 * j + 3]};
+                    uint32_t wd[SC / 32];
+#pragma unroll
+                    for (int w = 0; w < SC / 32; ++w) wd[w] = m.bits[4 * j + kofs / 32 + w];
                     if (cls == TILE_ROWS) {
 #pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            const int k0 = j * kTileRows + 32 * w;
+                        for (int w = 0; w < SC / 32; ++w) {
+                            const int k0 = j * kTileRows + kofs + 32 * w;
                             wd[w] = (wd[w] & low_bits(rA - k0)) | (low_bits(rC + 1 - k0) & ~low_bits(rB - k0));
                         }
                     }
 #pragma unroll
-                    for (int i = 0; i < 128; ++i) s[i] = ((wd[i >> 5] >> (i & 31)) & 1u) ? s[i] : -INFINITY;
+                    for (int i = 0; i < SC; ++i) s[i] = ((wd[i >> 5] >> (i & 31)) & 1u) ? s[i] : -INFINITY;
                 }
                 // Three-input maxima on four partial chains keep the dependency chains short.
                 float mxp[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-                for (int i = 4; i + 1 < 124; i += 2) mxp[(i >> 1) & 3] = max3(mxp[(i >> 1) & 3], s[i], s[i + 1]);
-                float mx = max3(max3(mxp[0], mxp[1], mxp[2]), max3(mxp[3], s[124], s[125]), fmaxf(s[126], s[127]));
+                for (int i = 4; i + 1 < SC - 4; i += 2) mxp[(i >> 1) & 3] = max3(mxp[(i >> 1) & 3], s[i], s[i + 1]);
+                float mx = max3(max3(mxp[0], mxp[1], mxp[2]), max3(mxp[3], s[SC - 4], s[SC - 3]),
+                                fmaxf(s[SC - 2], s[SC - 1]));
                 if (tail_here) {
 #pragma unroll
                     for (int t = 0; t < kTailMax; ++t) mx = fmaxf(mx, st[t]);
+                }
+                if constexpr (SPLIT) {
+                    // The row maximum over both halves (the pair takes the same rescale decision).
+                    float other;
+                    if (!xchg(mx, other)) {
+                        ok = false;
+                        break;
+                    }
+                    mx = fmaxf(mx, other);
                 }
                 // Lazy rescale: keep the stale max unless the new one exceeds it by 2^8.
                 const float m_new = fmaxf(m_run, mx);
@@ -800,9 +857,9 @@ __global__ void __maxnreg__(168)
                 // Quarters of a prefix tile past the last valid key hold only zeros.
                 const int live = (uniform || cls == TILE_PREFIX) ? n - j * kTileRows : kTileRows;
 #pragma unroll
-                for (int qc = 0; qc < 4; ++qc) {
+                for (int qc = 0; qc < SC / 32; ++qc) {
                     uint32_t pk[16];  // 32 keys as 16 packed 16-bit pairs
-                    if (32 * qc >= live) {
+                    if (kofs + 32 * qc >= live) {
 #pragma unroll
                         for (int e = 0; e < 16; ++e) pk[e] = 0u;
                         tmem_st16(t_p + 16 * qc, pk);
@@ -827,7 +884,7 @@ __global__ void __maxnreg__(168)
                 l_run = l_run * alpha + ((sp4[0] + sp4[1]) + (sp4[2] + sp4[3]));
                 if (j > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-                    for (int hcol = 0; hcol < 64; hcol += 32) {
+                    for (int hcol = 0; hcol < OC; hcol += 32) {
                         float ov[32];
                         tmem_ld32(t_o + hcol, ov);
                         tmem_wait_ld();
@@ -842,12 +899,23 @@ __global__ void __maxnreg__(168)
                 mbar_arrive(&b.p_ready);
             }
             if (!ok) break;
+            if constexpr (SPLIT) {
+                // The full row sum for the output staging (both halves of a live row).
+                if (!dead) {
+                    float other;
+                    if (!xchg(l_run, other)) {
+                        ok = false;
+                        break;
+                    }
+                    prev_ltot = l_run + other;
+                }
+            }
             mbar_arrive(&b.m_empty[slot]);
             prev_live = !dead;
             prev_im = im;
 #pragma unroll
             for (int t = 0; t < kTailMax; ++t) prev_pt[t] = pt[t];
-            *l_save = l_run;
+            if constexpr (!SPLIT) *l_save = l_run;
         }
         // The last item's output, once its last PV is done; one more p_ready phase tells the
         // tensor-core thread that it is staged.
@@ -863,10 +931,28 @@ __global__ void __maxnreg__(168)
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == W_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
     }
+}
+
+// Registers are allocated for warps in groups of four: 12 warps x 32 x 168 = 64,512 of the SM's
+// 65,536; the split instance, 19 warps (20 x 32 x 96 = 61,440). One CTA per SM (the shared memory
+// and the 512 TMEM columns allow no second one).
+template <bool F16, bool O8 = false, bool TAIL = false>
+__global__ void __maxnreg__(168)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, TcParams p) {
+    attn_tc_body<F16, O8, TAIL, false>(tmQ, tmK, tmV, tmO, p);
+}
+
+template <bool F16, bool O8 = false>
+__global__ void __maxnreg__(96)
+    attn_tc_split_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                         TcParams p) {
+    attn_tc_body<F16, O8, false, true>(tmQ, tmK, tmV, tmO, p);
 }
 
 }  // namespace
@@ -934,7 +1020,22 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     if (c.o8 && (c.dtype != E_F16 || c.ld_o8 % 16 || c.ld_o8 < 2 * width || (reinterpret_cast<uintptr_t>(c.o8) & 15)))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: an FP8 companion needs an FP16 output");
     const int64_t grid = std::min<int64_t>((p.items + 1) / 2, num_sms());
-    if (c.dtype == E_F16 && c.o8) {
+    // Split rows (two softmax threads per query row): the default for the key-validity mask without
+    // a key tail (Chronos-2's 577 tokens: 0.889 -> 0.814 ms per layer, with the FP8 companion
+    // 1.087 -> 0.993 ms; at Chronos-Bolt's 129 tokens the key-tail kernel is faster, 2.71 against
+    // 3.03 ms), and on request (force_path 3). force_path 1 keeps whole rows.
+    const bool split = c.force_path == 3 || (c.force_path == 0 && c.mask_mode == 0 && p.tail == 0);
+    if (split) p.tail = 0, p.tiles0 = p.mode == 0 ? (c.n + kTileRows - 1) / kTileRows : p.tiles0;
+    if (split && c.dtype == E_F16 && c.o8) {
+        TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_split_kernel<true, true>), kSmemTc));
+        attn_tc_split_kernel<true, true><<<(unsigned)grid, kThreadsSplit, kSmemTc, stream>>>(mq, mk, mv, mo, p);
+    } else if (split && c.dtype == E_F16) {
+        TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_split_kernel<true>), kSmemTc));
+        attn_tc_split_kernel<true><<<(unsigned)grid, kThreadsSplit, kSmemTc, stream>>>(mq, mk, mv, mo, p);
+    } else if (split) {
+        TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_split_kernel<false>), kSmemTc));
+        attn_tc_split_kernel<false><<<(unsigned)grid, kThreadsSplit, kSmemTc, stream>>>(mq, mk, mv, mo, p);
+    } else if (c.dtype == E_F16 && c.o8) {
         TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_kernel<true, true>), kSmemTc));
         attn_tc_kernel<true, true><<<(unsigned)grid, kThreadsTc, kSmemTc, stream>>>(mq, mk, mv, mo, p);
     } else if (c.dtype == E_F16 && p.tail > 0) {

@@ -809,14 +809,13 @@ int32_t tsfm_kernel_timestral_block_inputs(const float *ctx, const uint8_t *obse
 
 int32_t tsfm_kernel_attention_ex(const void *q, const void *k, const void *v, int64_t ld_qkv, void *o, int64_t ld_o,
                                  float *o32, int64_t ld_o32, uint8_t *o8, int64_t ld_o8, const uint8_t *key_valid,
-                                 int64_t kv_stride,
-                                 const uint8_t *group_bidir, int32_t groups, int32_t heads, int32_t n, float scale,
+                                 int64_t kv_stride, const float *rel_bias, const uint8_t *group_bidir, int32_t groups, int32_t heads, int32_t n, float scale,
                                  int32_t mask_mode, int32_t ne, int32_t l, int32_t dtype, int32_t force_path,
                                  void *stream) {
     return guarded([&]() -> Status {
         if (!q || !k || !v || (!o && !o32)) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
         if (mask_mode < 0 || mask_mode > 2) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "bad mask_mode");
-        if (force_path < 0 || force_path > 2) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "bad force_path");
+        if (force_path < 0 || force_path > 3) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "bad force_path");
         if (mask_mode != 0 && (ne < 0 || ne > n || l < 0 || l > ne))
             return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: need 0 <= l <= ne <= n");
         if (dtype != TSFM_DTYPE_BF16 && dtype != TSFM_DTYPE_F16)
@@ -834,6 +833,7 @@ int32_t tsfm_kernel_attention_ex(const void *q, const void *k, const void *v, in
         c.ld_o8 = ld_o8;
         c.key_valid = key_valid;
         c.kv_stride = kv_stride > 0 ? kv_stride : n;
+        c.rel_bias = rel_bias;
         c.group_bidir = group_bidir;
         c.groups = groups;
         c.heads = heads;
@@ -845,7 +845,7 @@ int32_t tsfm_kernel_attention_ex(const void *q, const void *k, const void *v, in
         c.l = mask_mode == 0 ? n : l;
         c.force_path = force_path;
         c.err = kernel_err_word();
-        if (force_path == 1 && !attention_tc_supported(c))
+        if ((force_path == 1 || force_path == 3) && !attention_tc_supported(c))
             return Status::fail(TSFM_ERR_UNSUPPORTED, "attention: the tcgen05 path does not take this call");
         return launch_attention(c, static_cast<cudaStream_t>(stream));
     });

@@ -148,7 +148,8 @@ struct AttentionCall {
     int ne = 0, l = 0;
     const uint8_t *group_bidir = nullptr;  // per group: 1 = bidirectional encoder rows (mode 1 only)
     int *err = nullptr;                    // device error word for the bounded waits of the tcgen05 path
-    int force_path = 0;                    // 0: automatic, 1: tcgen05 path only (error if unsupported), 2: mma.sync path
+    int force_path = 0;                    // 0: automatic, 1: tcgen05 path only (error if unsupported), 2: mma.sync path,
+                                           // 3: the tcgen05 kernel with two softmax threads per row
     // FP8 companion of the FP16 output (kernels.h layout, width heads * 64; tcgen05 path only: a
     // call the tcgen05 path does not take fails rather than leave it unwritten).
     void *o8 = nullptr;
