@@ -1020,11 +1020,11 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     if (c.o8 && (c.dtype != E_F16 || c.ld_o8 % 16 || c.ld_o8 < 2 * width || (reinterpret_cast<uintptr_t>(c.o8) & 15)))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "attention: an FP8 companion needs an FP16 output");
     const int64_t grid = std::min<int64_t>((p.items + 1) / 2, num_sms());
-    // Split rows (two softmax threads per query row): the default for the key-validity mask without
-    // a key tail (Chronos-2's 577 tokens: 0.889 -> 0.814 ms per layer, with the FP8 companion
-    // 1.087 -> 0.993 ms; at Chronos-Bolt's 129 tokens the key-tail kernel is faster, 2.71 against
-    // 3.03 ms), and on request (force_path 3). force_path 1 keeps whole rows.
-    const bool split = c.force_path == 3 || (c.force_path == 0 && c.mask_mode == 0 && p.tail == 0);
+    // Split rows (two softmax threads per query row) on request only (force_path 3): alone, with the
+    // L2 flushed and fixed clocks, it ran Chronos-2's 577 tokens 8-9 % faster (0.889 -> 0.814 ms per
+    // layer), but inside the corrected forward (power-capped clocks, operands warm in L2) the
+    // attention class took 15.9-16.4 ms against 14.5-14.8 ms for whole rows (A/B on one box).
+    const bool split = c.force_path == 3;
     if (split) p.tail = 0, p.tiles0 = p.mode == 0 ? (c.n + kTileRows - 1) / kTileRows : p.tiles0;
     if (split && c.dtype == E_F16 && c.o8) {
         TSFM_TRY(ensure_smem_attr(reinterpret_cast<const void *>(&attn_tc_split_kernel<true, true>), kSmemTc));
