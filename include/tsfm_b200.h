@@ -262,11 +262,11 @@ int tsfm_sgemm_nn(int m, int n, int k, const float *A, int lda,               /*
  * the library (held by every GPU that loads it) with room for the hi/lo splits of A and B:
  * round_up(m * round_up(k, 4), 64) + round_up(n * round_up(k, 4), 64) must not exceed 2^21 - 64
  * floats (for k a multiple of 64: m + n <= 32767), else TSFM_ERR_INVALID_ARGUMENT and nothing
- * runs. All calls share that array: calls that overlap on the GPU race. The first call on each
- * device looks up the array's address (which may load the library's device code), so make it
- * before any stream capture. Runs on `stream` (null = legacy default stream) and is synchronous:
- * it reads its device error word back and waits for `stream` before returning, so C is written
- * on return; 0 = success, else a tsfm_status. */
+ * runs. All calls share that array: calls that overlap on the GPU race. Runs on `stream` (null =
+ * legacy default stream) and is synchronous: it reads its device error word back and waits for
+ * `stream` before returning, so C is written on return; it must therefore never be called on a
+ * stream that is being captured into a CUDA graph. The first call on each device looks up the
+ * array's address (which may load the library's device code). 0 = success, else a tsfm_status. */
 int32_t tsfm_sgemm_nt_noalloc(int m, int n, int k, float alpha, const float *A, int lda,
                               const float *B, int ldb, float *C, int ldc, void *stream);
 
