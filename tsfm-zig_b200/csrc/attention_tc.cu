@@ -458,25 +458,27 @@ __device__ __forceinline__ void attn_tc_body(const CUtensorMap &tmQ, const CUten
                         mma_f16kind(t_s, qd + 2 * kk, kd + 2 * kk, IDESC_S, kk > 0 ? 1u : 0u);
                     mma_commit(&b.s_full);
                     mma_commit(&b.k_empty[s]);
+                    // V of this tile into the slot PV(g - 2) read (long done by now), a period before
+                    // PV(g) needs it; refilling here rather than after PV(g - 1) completes lets the
+                    // next S follow the softmax's s_free without waiting for that PV.
+                    if (g >= 2 && vc.wi < nq) {
+                        if (!mbar_wait(&b.v_empty[s], ((g - 2) >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
+                            ok = false;
+                            break;
+                        }
+                        load_v(g);
+                    }
                     if (next_pv < g && !pv(next_pv++)) {
                         ok = false;
                         break;
                     }
-                    // Refill the rings: K two tiles ahead once this S is done with its slot, V
-                    // one tile ahead once the PV just issued is done with its slot.
+                    // K two tiles ahead once this S is done with its slot.
                     if (kc.wi < nq) {  // tile g + 2 exists
                         if (!mbar_wait(&b.k_empty[s], (g >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
                             ok = false;
                             break;
                         }
                         load_k(g + 2);
-                    }
-                    if (g >= 1 && vc.wi < nq) {  // tile g + 1 exists
-                        if (!mbar_wait(&b.v_empty[(g + 1) & 1], ((g - 1) >> 1) & 1, abort_flag, p.err, ERR_SITE_ATTN_MMA)) {
-                            ok = false;
-                            break;
-                        }
-                        load_v(g + 1);
                     }
                 }
             }
