@@ -4,14 +4,15 @@
 // (group, head, 128-query tile). The CTA runs two independent pipelines; pipeline p takes every
 // other item of the range, so the softmax of one pipeline overlaps the other's loads, MMAs and
 // bookkeeping and the SFU (exp2) stays busy.
-// Roles (352 threads):
+// Roles (352 threads; the split-row instance doubles the softmax warps to 16, 608 threads):
 //   warps 0-3, 4-7   softmax of pipeline 0 / 1 (thread = query row; warp w reads TMEM lanes
 //                    32 (w % 4) .. + 31)
 //   warps 8, 9       lane 0: the tensor-core thread of pipeline 0 / 1. It issues the MMAs and
 //                    also every TMA transfer of its pipeline (Q, K and V loads, the output
 //                    store), each at the point of its own loop where the buffer has just been
 //                    released, so the loads run one or two key tiles ahead without a producer
-//                    that could fall behind. Warp 8 also allocates TMEM.
+//                    that could fall behind (V(j) right after S(j), K(j + 2) once S(j) is done).
+//                    Warp 8 also allocates TMEM.
 //   warp 10          key masks of the coming items (bit words per key tile, tile classes)
 // Per key tile j a pipeline issues S = Q K_j^T (M 128, N 128, K 64, FP32 in TMEM), then
 // O += P_(j-1) V_(j-1) (M 128, N 64, K 128) with P read from TMEM (16-bit, written by the
