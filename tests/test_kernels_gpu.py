@@ -196,9 +196,9 @@ def test_attention_tcgen05_path_edges(n, with_rel, dtype):
     kernel beyond): one and two query tiles per CTA, partial key tiles, the K / V rings wrapping
     many times, a group without valid keys (uniform), a group whose first 300 keys are invalid
     (rows start with an empty max), and scores that grow by more than 2^8 per key tile so the lazy
-    O / row-sum rescale runs on every tile. n = 128 k + 1..4 (129, 132, 257) runs the key-tail
-    instance (the last keys in the softmax threads, the largest scores of the growing group among
-    them); 133 the plain one."""
+    O / row-sum rescale runs on every tile. n = 128 k + 1 (129, 257) runs the key-tail instance
+    (the last key in the softmax threads, the largest score of the growing group); 132 and 133
+    the plain one."""
     heads, G = 2, 4
     gen = torch.Generator().manual_seed(1000 + n)
     ld = 3 * heads * 64

@@ -60,7 +60,8 @@ constexpr int kMaxKeysRel = 512;                     // longest sequence with re
 constexpr int kRelWin = kMaxKeysRel + kTileRows;     // offsets one item's 128 query rows can see
 constexpr int kThreadsTc = 352;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-constexpr int kTailMax = 4;                // longest key tail folded into the softmax (mode 0)
+constexpr int kTailMax = 1;                // longest key tail folded into the softmax (mode 0; one key:
+                                           // Chronos-Bolt's 129 tokens; longer tails spilled more)
 
 // Tile classes of a key tile. TILE_ROWS (Timestral's causal / decoder masks): the visible keys
 // depend on the query row; each softmax thread builds its row's bits from the validity bits.
@@ -125,7 +126,7 @@ struct TcParams {
     // FP32 output instead of the 16-bit one (row (g * n + i) at o32 + row * ld_o32, head h at h * 64).
     float *o32;
     int64_t ld_o32;
-    // Key tail (mode 0, n = 128 (T - 1) + tail with 1 <= tail <= kTailMax, e.g. Chronos-Bolt's 129
+    // Key tail (mode 0, n = 128 (T - 1) + tail with 1 <= tail <= kTailMax, i.e. Chronos-Bolt's 129
     // tokens): the tensor cores cover the first T - 1 key tiles and the softmax threads the last
     // `tail` keys (scores from the Q tile in shared memory and the key rows, their P V added to the
     // output row when it is staged), so an item costs one key tile instead of two. tiles0: key
