@@ -618,7 +618,7 @@ def run_gemm(a):
     rows): qkv (2304 x 768, FP16 out), o and the folded group projection (768 x 768, FP32
     accumulate), wi (3072 x 768, ReLU, FP16 out), wo (768 x 3072, FP32 accumulate), each with plain
     FP16 operands (tsfm_kernel_linear) and as the corrected product (tsfm_kernel_linear_f16c with the
-    FP8 companions, FP16 outputs with their companion as the forward writes them). CUDA events per
+    FP8 companions; wi's FP16 output with its companion, as the forward writes it). CUDA events per
     launch, L2 flushed between launches; TFLOP/s = 2 M N K / time (the algorithmic work; the
     corrected product executes twice the tensor-core work)."""
     import ctypes
@@ -645,7 +645,9 @@ def run_gemm(a):
                                                 sp))
         del x, w
         y = torch.zeros(M, N, device="cuda", dtype=torch.float16 if out_mode == 0 else torch.float32)
-        y8 = torch.empty(M, 2 * N, device="cuda", dtype=torch.uint8) if out_mode == 0 else None
+        # The forward writes an FP8 companion only where the output feeds a corrected product: the
+        # MLP hidden (wi -> wo); qkv feeds the attention, which reads FP16.
+        y8 = torch.empty(M, 2 * N, device="cuda", dtype=torch.uint8) if name == "wi" else None
         runs = {
             "f16": lambda: tb.check(tb.lib.tsfm_kernel_linear(x16.data_ptr(), 1, w16.data_ptr(), 1, None, y.data_ptr(),
                                                               out_mode, act, M, N, K, K, K, N, sp)),
@@ -663,7 +665,7 @@ def run_gemm(a):
                 None if y8 is None else y8.data_ptr(), out_mode, act, M, N, K, 1, sp))
             runs["f16-2k"] = lambda: tb.check(tb.lib.tsfm_kernel_linear(
                 x2.data_ptr(), 1, w2.data_ptr(), 1, None, y.data_ptr(), out_mode, act, M, N, 2 * K, 2 * K, 2 * K, N, sp))
-            if y8 is not None:  # the corrected product without writing its output's companion
+            if y8 is not None:  # wi without writing its output's companion
                 runs["f16c-no-companion"] = lambda: tb.check(tb.lib.tsfm_kernel_linear_f16c(
                     xc16.data_ptr(), x8.data_ptr(), wc16.data_ptr(), w8.data_ptr(), scale.value, None, y.data_ptr(),
                     None, out_mode, act, M, N, K, 2, sp))
