@@ -346,11 +346,13 @@ def test_attention_timestral_masks_both_paths(n, ne, l, mode, out32, dtype):
         assert (outs[1] - outs[2]).abs().max().item() < (3e-2 if dtype == "bf16" else 5e-3)
 
 
-@pytest.mark.parametrize("n", [1, 129, 577])
-def test_attention_fp8_companion(n):
+@pytest.mark.parametrize("n,pad8", [(1, 0), (129, 0), (577, 0), (129, 16)])
+def test_attention_fp8_companion(n, pad8):
     """The tcgen05 kernel's FP8 companion of its FP16 output (corrected products), bit for bit:
     with x the kernel's FP32 output (the same launch with an FP32 output), the FP16 output is
-    f16(x) and the companion [e4m3(f16(x) / 32) | e4m3((x - f16(x)) * 128)]."""
+    f16(x) and the companion [e4m3(f16(x) / 32) | e4m3((x - f16(x)) * 128)]. pad8 = 16: a
+    companion row stride that is 16- but not 32-byte aligned (16-byte stores instead of 32-byte
+    ones); the padding bytes stay untouched."""
     from helpers import e4m3_bits
     heads, G = 2, 3
     gen = torch.Generator().manual_seed(77 + n)
@@ -362,18 +364,20 @@ def test_attention_fp8_companion(n):
     kvd = kv.to(dev())
     width = heads * 64
     o = torch.empty(G * n, width, device=dev(), dtype=torch.float16)
-    o8 = torch.zeros(G * n, 2 * width, device=dev(), dtype=torch.uint8)
+    o8 = torch.full((G * n, 2 * width + pad8), 0xA5, device=dev(), dtype=torch.uint8)
     o32 = torch.empty(G * n, width, device=dev(), dtype=torch.float32)
     for out, out32, out8 in ((o, None, o8), (None, o32, None)):
         tb.check(tb.lib.tsfm_kernel_attention_ex(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), ld, None if out is None else out.data_ptr(), width,
-            None if out32 is None else out32.data_ptr(), width, None if out8 is None else out8.data_ptr(), 2 * width,
-            kvd.data_ptr(), n, None, None, G, heads, n, 0.125, 0, n, n, F16, 1, stream_ptr()))
+            None if out32 is None else out32.data_ptr(), width, None if out8 is None else out8.data_ptr(),
+            2 * width + pad8, kvd.data_ptr(), n, None, None, G, heads, n, 0.125, 0, n, n, F16, 1, stream_ptr()))
     torch.cuda.synchronize()
     x = o32.cpu().numpy()
     xh = x.astype(np.float16).astype(np.float32)
     assert np.array_equal(o.float().cpu().numpy(), xh)
     b8 = o8.cpu().numpy()
+    assert (b8[:, 2 * width:] == 0xA5).all()
+    b8 = b8[:, :2 * width]
     assert np.array_equal(b8[:, :width], e4m3_bits(xh * np.float32(1 / 32)))
     assert np.array_equal(b8[:, width:], e4m3_bits((x - xh) * np.float32(128)))
     ref = attention_ref(q, k, v, kv, None, n, heads, 0.125, 0).numpy()

@@ -116,9 +116,11 @@ struct TcParams {
     float scale_log2;
     int *err;
     // FP8 companion of the FP16 output (corrected products): row (g * n + i) at o8 + row * ld_o8,
-    // head h's 64 values at byte h * 64, their low parts o8_half bytes further.
+    // head h's 64 values at byte h * 64, their low parts o8_half bytes further. o8_v8: o8 and
+    // ld_o8 are 32-byte aligned, so each row's 32-byte runs leave in one 256-bit store.
     uint8_t *o8;
     int64_t ld_o8, o8_half;
+    int o8_v8;
     // Masks of modes 1-2 (AttentionCall): encoder queries i < ne, decoder queries i >= ne reading
     // valid keys below l and their chain [ne, i]; per-group bidirectional flags.
     int mode, ne, l, bidir_all;
@@ -612,12 +614,18 @@ __device__ __forceinline__ void attn_tc_body(const CUtensorMap &tmQ, const CUten
                         uint32_t hi[8], lo[8];
                         pack_x8_f16x2_32(x, hp, hi, lo);
                         const int64_t col0 = (int64_t)prev_im.h * 64 + half * OC + 32 * h;
-                        uint4 *ph = reinterpret_cast<uint4 *>(row8 + col0);
-                        uint4 *pl = reinterpret_cast<uint4 *>(row8 + p.o8_half + col0);
-                        ph[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        ph[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-                        pl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                        pl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                        if (p.o8_v8) {
+                            st_global_v8(row8 + col0, hi[0], hi[1], hi[2], hi[3], hi[4], hi[5], hi[6], hi[7]);
+                            st_global_v8(row8 + p.o8_half + col0, lo[0], lo[1], lo[2], lo[3], lo[4], lo[5], lo[6],
+                                         lo[7]);
+                        } else {
+                            uint4 *ph = reinterpret_cast<uint4 *>(row8 + col0);
+                            uint4 *pl = reinterpret_cast<uint4 *>(row8 + p.o8_half + col0);
+                            ph[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                            ph[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                            pl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                            pl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                        }
                     }
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
@@ -1007,6 +1015,7 @@ Status launch_attention_tc(const AttentionCall &c, cudaStream_t stream) {
     p.o8 = static_cast<uint8_t *>(c.o8);
     p.ld_o8 = c.ld_o8;
     p.o8_half = width;
+    p.o8_v8 = ((reinterpret_cast<uintptr_t>(c.o8) | (uintptr_t)c.ld_o8) & 31) == 0;
     p.mode = c.mask_mode;
     p.ne = c.mask_mode == 0 ? c.n : c.ne;
     p.l = c.l;

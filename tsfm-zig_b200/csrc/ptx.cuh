@@ -426,6 +426,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// One 32-byte global store (sm_100's 256-bit vector store); p 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t e,
+                                             uint32_t f, uint32_t g, uint32_t h) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a), "r"(b), "r"(c),
+                 "r"(d), "r"(e), "r"(f), "r"(g), "r"(h)
+                 : "memory");
+}
+
 // Makes this thread's generic-proxy shared-memory writes visible to the async proxy (the tensor
 // cores reading an operand tile through a matrix descriptor).
 __device__ __forceinline__ void fence_proxy_async_smem() {
