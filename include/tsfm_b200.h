@@ -404,6 +404,15 @@ int32_t tsfm_kernel_target_encode(const float *inputs, const uint8_t *observed, 
 int32_t tsfm_kernel_rmsnorm(const float *x, const float *scale, void *out, int32_t out_dtype,
                             int64_t rows, int64_t dim, float eps, void *stream);
 
+/* tsfm_kernel_rmsnorm_ex: tsfm_kernel_rmsnorm (out_dtype bf16, f16 or f32) plus, for an f16
+ * output, the FP8 companion the corrected mode (TSFM_COMPUTE_F16C) feeds to the next product:
+ * out8 (null for none) row r at out8 + r * ld8 bytes, byte c = e4m3(f16(y[r, c]) / 32) and byte
+ * dim + c = e4m3((y[r, c] - f16(y[r, c])) * 128), y the FP32 result. dim % 4 == 0,
+ * ld8 >= 2 * dim. The same kernels as the forecasts' norms. Replaces nn.rmsNorm
+ * (core/nn.zig:367-396); the companion has no counterpart in the reference. */
+int32_t tsfm_kernel_rmsnorm_ex(const float *x, const float *scale, void *out, int32_t out_dtype, void *out8,
+                               int64_t ld8, int64_t rows, int64_t dim, float eps, void *stream);
+
 /* ---------------------------------------------------------------------------------------------
  * CSV output of a forecast. Replaces the CLI's writeCsv (src/main.zig:181-198): a header
  * "series,variate,step" followed by ",q<level>" per quantile level, then one line per

@@ -403,6 +403,39 @@ def test_rmsnorm_matches_oracle():
     np.testing.assert_allclose(outb.float().cpu().numpy(), want, rtol=2 ** -7, atol=1e-2)
 
 
+@pytest.mark.parametrize("dim,pad8", [(256, 0), (768, 0), (768, 8), (1024, 0), (772, 0), (772, 8)])
+def test_rmsnorm_fp8_companion(dim, pad8):
+    """RMSNorm with the FP8 companion of its FP16 output (the corrected mode's norm), on both
+    kernels: rows of 256 * k values take the 256-bit-access kernel, others (772) the general one.
+    With y the same launch's FP32 output: FP16 output f16(y), companion [e4m3(f16(y) / 32) |
+    e4m3((y - f16(y)) * 128)] bit for bit, y against the oracle. pad8: companion rows longer than
+    2 * dim whose padding stays untouched."""
+    from helpers import e4m3_bits
+    rows = 1000
+    rng = np.random.default_rng(dim + pad8)
+    x = (rng.standard_normal((rows, dim)) * 3).astype(np.float32)
+    s = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    xd, sd = torch.from_numpy(x).to(dev()), torch.from_numpy(s).to(dev())
+    y = torch.zeros(rows, dim, device=dev())
+    h = torch.zeros(rows, dim, device=dev(), dtype=torch.float16)
+    b8 = torch.full((rows, 2 * dim + pad8), 0xA5, device=dev(), dtype=torch.uint8)
+    tb.check(tb.lib.tsfm_kernel_rmsnorm_ex(xd.data_ptr(), sd.data_ptr(), y.data_ptr(), F32, None, 0, rows, dim, 1e-6,
+                                           stream_ptr()))
+    tb.check(tb.lib.tsfm_kernel_rmsnorm_ex(xd.data_ptr(), sd.data_ptr(), h.data_ptr(), F16, b8.data_ptr(),
+                                           2 * dim + pad8, rows, dim, 1e-6, stream_ptr()))
+    torch.cuda.synchronize()
+    want = np.zeros_like(x)
+    ob.lib.oracle_rmsnorm(x.ctypes.data, s.ctypes.data, want.ctypes.data, rows, dim, 1e-6)
+    yv = y.cpu().numpy()
+    np.testing.assert_allclose(yv, want, rtol=1e-5, atol=1e-5)
+    yh = yv.astype(np.float16).astype(np.float32)
+    assert np.array_equal(h.float().cpu().numpy(), yh)
+    bb = b8.cpu().numpy()
+    assert (bb[:, 2 * dim:] == 0xA5).all()
+    assert np.array_equal(bb[:, :dim], e4m3_bits(yh * np.float32(1 / 32)))
+    assert np.array_equal(bb[:, dim:2 * dim], e4m3_bits((yv - yh) * np.float32(128)))
+
+
 def test_gemm_seam_padded_strides_like_reference_gpu_test():
     # core/gpu_test.zig:56-101: m, n, k = 37, 29, 23; lda, ldb, ldc = 31, 41, 47; sentinel -12345
     # must survive in the padding; tolerance 1e-4; registered-weight NT and activation NN paths.

@@ -921,4 +921,22 @@ int32_t tsfm_kernel_rmsnorm(const float *x, const float *scale, void *out, int32
     });
 }
 
+int32_t tsfm_kernel_rmsnorm_ex(const float *x, const float *scale, void *out, int32_t out_dtype, void *out8,
+                               int64_t ld8, int64_t rows, int64_t dim, float eps, void *stream) {
+    return guarded([&]() -> Status {
+        if (!x || !scale || !out) return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "null pointer");
+        RmsNormCall c;
+        c.x = x;
+        c.scale = scale;
+        c.out = out;
+        c.out_mode = out_dtype == TSFM_DTYPE_BF16 ? OUT_BF16 : out_dtype == TSFM_DTYPE_F16 ? OUT_F16 : OUT_F32;
+        c.out8 = out8;
+        c.ld8 = ld8;
+        c.rows = rows;
+        c.dim = dim;
+        c.eps = eps;
+        return launch_rmsnorm(c, static_cast<cudaStream_t>(stream));
+    });
+}
+
 }  // extern "C"

@@ -85,6 +85,79 @@ __global__ void rmsnorm_kernel(RmsNormCall c) {
     }
 }
 
+// rmsnorm_kernel for rows of NC * 256 values (NC <= 4: Chronos-2 / Bolt / Timestral widths): the
+// warp reads its row once, each lane holding 8 consecutive values per 256-value chunk in registers
+// (256-bit loads), and writes 16-byte (16-bit output), 8-byte (FP8 companion) or 32-byte (FP32)
+// runs. Same per-element arithmetic as rmsnorm_kernel; the row's sum of squares is accumulated in
+// another order, so the factor can differ from that kernel's in the last bit.
+template <int NC>
+__global__ void __launch_bounds__(256) rmsnorm_v8_kernel(RmsNormCall c) {
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= c.rows) return;
+    const int64_t in_row = c.rows_idx ? c.rows_idx[r] : c.g > 0 ? (r / c.g) * c.G + r % c.g + c.off : r;
+    const float *x = c.x + in_row * c.dim;
+    float v[NC][8];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) ld_global_v8(x + 256 * k + 8 * lane, v[k]);
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NC; ++k)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(v[k][j], v[k][j], ss);
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)c.dim + c.eps);
+    if (c.inv_out && lane == 0) c.inv_out[r] = inv;
+    const int64_t ob = r * c.dim;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int64_t i = 256 * k + 8 * lane;
+        float s[8], o[8];
+        ld_global_v8(c.scale + i, s);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = v[k][j] * inv * s[j];
+        if (c.out_mode == OUT_BF16 || c.out_mode == OUT_F16) {
+            uint32_t pk[4];
+            float2 f[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (c.out_mode == OUT_BF16) {
+                    __nv_bfloat162 a = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+                    pk[e] = *reinterpret_cast<uint32_t *>(&a);
+                } else {
+                    __half2 a = __floats2half2_rn(o[2 * e], o[2 * e + 1]);
+                    pk[e] = *reinterpret_cast<uint32_t *>(&a);
+                    f[e] = __half22float2(a);
+                }
+            }
+            *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(c.out) + ob + i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            if (c.out_mode == OUT_F16 && c.out8) {
+                uint8_t *row8 = static_cast<uint8_t *>(c.out8) + r * c.ld8;
+                uint32_t hi[2], lo[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float2 fa = f[2 * h], fb = f[2 * h + 1];
+                    const float *oo = o + 4 * h;
+                    hi[h] = e4m3x2(fa.x * kX8HiScale, fa.y * kX8HiScale) |
+                            (e4m3x2(fb.x * kX8HiScale, fb.y * kX8HiScale) << 16);
+                    lo[h] = e4m3x2((oo[0] - fa.x) * kX8LoScale, (oo[1] - fa.y) * kX8LoScale) |
+                            (e4m3x2((oo[2] - fb.x) * kX8LoScale, (oo[3] - fb.y) * kX8LoScale) << 16);
+                }
+                *reinterpret_cast<uint2 *>(row8 + i) = make_uint2(hi[0], hi[1]);
+                *reinterpret_cast<uint2 *>(row8 + c.dim + i) = make_uint2(lo[0], lo[1]);
+            }
+        } else {
+            if (c.out_mode == OUT_TF32) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[j] = to_tf32(o[j]);
+            }
+            st_global_v8(static_cast<float *>(c.out) + ob + i, __float_as_uint(o[0]), __float_as_uint(o[1]),
+                         __float_as_uint(o[2]), __float_as_uint(o[3]), __float_as_uint(o[4]), __float_as_uint(o[5]),
+                         __float_as_uint(o[6]), __float_as_uint(o[7]));
+        }
+    }
+}
+
 __device__ __forceinline__ double block_sum_d(double v, double *red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -264,6 +337,20 @@ Status launch_rmsnorm(const RmsNormCall &c, cudaStream_t stream) {
                    (reinterpret_cast<uintptr_t>(c.out8) & 3)))
         return Status::fail(TSFM_ERR_INVALID_ARGUMENT, "rmsnorm: an FP8 companion needs an FP16 output, dim % 4 == 0");
     const int64_t blocks = (c.rows + 7) / 8;
+    const auto al = [](const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+    const bool f32_out = c.out_mode != OUT_BF16 && c.out_mode != OUT_F16;
+    const bool v8 = c.dim % 256 == 0 && c.dim <= 1024 && al(c.x, 32) && al(c.scale, 32) &&
+                    al(c.out, f32_out ? 32 : 16) && (!c.out8 || (al(c.out8, 8) && c.ld8 % 8 == 0));
+    if (v8) {
+        switch (c.dim / 256) {
+        case 1: rmsnorm_v8_kernel<1><<<(unsigned)blocks, 256, 0, stream>>>(c); break;
+        case 2: rmsnorm_v8_kernel<2><<<(unsigned)blocks, 256, 0, stream>>>(c); break;
+        case 3: rmsnorm_v8_kernel<3><<<(unsigned)blocks, 256, 0, stream>>>(c); break;
+        default: rmsnorm_v8_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(c); break;
+        }
+        TSFM_CUDA(cudaGetLastError(), "rmsnorm: launch");
+        return Status::ok();
+    }
     rmsnorm_kernel<<<(unsigned)blocks, 256, 0, stream>>>(c);
     TSFM_CUDA(cudaGetLastError(), "rmsnorm: launch");
     return Status::ok();

@@ -426,6 +426,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// One 32-byte global load (sm_100's 256-bit vector load) of data no thread writes during the
+// kernel; p 32-byte aligned.
+__device__ __forceinline__ void ld_global_v8(const float *p, float (&v)[8]) {
+    asm volatile("ld.global.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+                 : "l"(p));
+}
+
 // One 32-byte global store (sm_100's 256-bit vector store); p 32-byte aligned.
 __device__ __forceinline__ void st_global_v8(void *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t e,
                                              uint32_t f, uint32_t g, uint32_t h) {

@@ -81,6 +81,7 @@ SIGNATURES = {
     "tsfm_kernel_attention_ex": (_I32, [_P, _P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I32, _I32,
                                         _I32, _F, _I32, _I32, _I32, _I32, _I32, _P]),
     "tsfm_kernel_rmsnorm": (_I32, [_P, _P, _P, _I32, _I64, _I64, _F, _P]),
+    "tsfm_kernel_rmsnorm_ex": (_I32, [_P, _P, _P, _I32, _P, _I64, _I64, _I64, _F, _P]),
     "tsfm_kernel_target_encode": (_I32, [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _I32, _P, _P]),
     "tsfm_csv_format": (_I32, [_P, _SZ, _SZ, _SZ, _P, _SZ, _I32, _P, _SZ, ctypes.POINTER(_SZ)]),
     "tsfm_csv_write": (_I32, [_P, _SZ, _SZ, _SZ, _P, _SZ, _I32, _I32, ctypes.POINTER(_SZ)]),
